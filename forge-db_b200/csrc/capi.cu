@@ -1,0 +1,678 @@
+// capi.cu -- the extern "C" entry points of include/forgegpu.h.
+//
+// Each entry point validates its arguments the way the reference's Rust
+// method does (panics become error codes), makes the context's device
+// current, runs the engine and converts any failure into a status code plus
+// a thread-local message.  The product path has no CPU fallback: if the
+// device work cannot run, the call fails.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <memory>
+#include <new>
+#include <numeric>
+
+#include "fdb_device.cuh"
+#include "fdb_internal.h"
+#include "fdb_kernels.h"
+
+namespace fdb {
+
+static thread_local std::string g_last_error;
+
+void fail(int code, const std::string& msg) { throw Error{code, msg}; }
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+uint64_t splitmix64(uint64_t& state) {
+    uint64_t z = (state += 0x9e3779b97f4a7c15ull);
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+// Partial Fisher-Yates over 0..n-1; the first `take` slots are a uniform
+// random ordered sample without replacement.
+void sample_indices(uint64_t seed, size_t n, size_t take, uint32_t* out) {
+    FDB_REQUIRE(take <= n, FDB_ERR_INVALID_ARG, "cannot take more indices than exist");
+    FDB_REQUIRE(n < (1ull << 32), FDB_ERR_UNSUPPORTED, "index space above 2^32");
+    std::vector<uint32_t> idx(n);
+    std::iota(idx.begin(), idx.end(), 0u);
+    uint64_t st = seed;
+    for (size_t i = 0; i < take; ++i) {
+        uint64_t range = n - i;
+        size_t j = i + (size_t)(((unsigned __int128)splitmix64(st) * range) >> 64);
+        std::swap(idx[i], idx[j]);
+    }
+    std::copy(idx.begin(), idx.begin() + take, out);
+}
+
+// rand's f32 sampler keeps 23 random bits: u = bits * 2^-23 in [0, 1).
+void uniform_draws(uint64_t seed, size_t count, float* out) {
+    uint64_t st = seed;
+    for (size_t i = 0; i < count; ++i)
+        out[i] = (float)(splitmix64(st) >> 41) * (1.0f / 8388608.0f);
+}
+
+}  // namespace fdb
+
+using namespace fdb;
+
+namespace {
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return FDB_OK;
+    } catch (const Error& e) {
+        set_last_error(e.msg);
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return FDB_ERR_OOM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return FDB_ERR_INVALID_ARG;
+    }
+}
+
+void check_metric(int metric) {
+    FDB_REQUIRE(metric >= FDB_METRIC_EUCLIDEAN && metric <= FDB_METRIC_MANHATTAN,
+                FDB_ERR_INVALID_ARG, "unknown metric");
+}
+
+// Pinned-or-not host <-> device staging for the host-buffer entry points.
+struct Staged {
+    DevBuf<uint64_t> ids;
+    DevBuf<float> dists;
+    DevBuf<uint32_t> counts;
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* fdb_last_error(void) { return g_last_error.c_str(); }
+
+int fdb_version(void) { return 100; }
+
+int fdb_ctx_create(int device, fdb_ctx** out) {
+    return guarded([&] {
+        FDB_REQUIRE(out, FDB_ERR_INVALID_ARG, "out is NULL");
+        int ndev = 0;
+        FDB_CUDA(cudaGetDeviceCount(&ndev));
+        FDB_REQUIRE(device >= 0 && device < ndev, FDB_ERR_INVALID_ARG, "no such CUDA device");
+        std::unique_ptr<fdb_ctx> c(new fdb_ctx());
+        c->c.device = device;
+        DeviceGuard g(device);
+        cudaDeviceProp prop;
+        FDB_CUDA(cudaGetDeviceProperties(&prop, device));
+        FDB_REQUIRE(prop.major >= 10, FDB_ERR_UNSUPPORTED,
+                    "this build targets sm_100a (B200); device is older");
+        c->c.sm_count = prop.multiProcessorCount;
+        FDB_CUDA(cudaStreamCreateWithFlags(&c->c.stream, cudaStreamNonBlocking));
+        *out = c.release();
+    });
+}
+
+int fdb_ctx_free(fdb_ctx* ctx) {
+    return guarded([&] {
+        if (!ctx) return;
+        {
+            DeviceGuard g(ctx->c.device);
+            if (ctx->c.comm) ncclCommDestroy(ctx->c.comm);
+            if (ctx->c.stream) cudaStreamDestroy(ctx->c.stream);
+        }
+        delete ctx;
+    });
+}
+
+int fdb_ctx_stream(fdb_ctx* ctx, void** stream_out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && stream_out, FDB_ERR_INVALID_ARG, "NULL argument");
+        *stream_out = (void*)ctx->c.stream;
+    });
+}
+
+int fdb_nccl_unique_id(void* id_out) {
+    return guarded([&] {
+        FDB_REQUIRE(id_out, FDB_ERR_INVALID_ARG, "NULL argument");
+        static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+        ncclUniqueId id;
+        FDB_NCCL(ncclGetUniqueId(&id));
+        std::memcpy(id_out, &id, sizeof(id));
+    });
+}
+
+int fdb_ctx_init_comm(fdb_ctx* ctx, int rank, int world, const void* nccl_id) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && nccl_id, FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_REQUIRE(world >= 1 && rank >= 0 && rank < world, FDB_ERR_INVALID_ARG,
+                    "bad rank/world");
+        DeviceGuard g(ctx->c.device);
+        if (ctx->c.comm) {
+            ncclCommDestroy(ctx->c.comm);
+            ctx->c.comm = nullptr;
+        }
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        FDB_NCCL(ncclCommInitRank(&ctx->c.comm, world, id, rank));
+        ctx->c.rank = rank;
+        ctx->c.world = world;
+    });
+}
+
+int fdb_host_alloc(size_t bytes, void** out) {
+    return guarded([&] {
+        FDB_REQUIRE(out, FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_CUDA(cudaHostAlloc(out, bytes ? bytes : 1, cudaHostAllocPortable));
+    });
+}
+
+int fdb_host_free(void* p) {
+    return guarded([&] {
+        if (p) FDB_CUDA(cudaFreeHost(p));
+    });
+}
+
+int fdb_sample_indices(uint64_t seed, size_t n, size_t take, uint32_t* out) {
+    return guarded([&] {
+        FDB_REQUIRE(out || take == 0, FDB_ERR_INVALID_ARG, "NULL argument");
+        sample_indices(seed, n, take, out);
+    });
+}
+
+int fdb_uniform_draws(uint64_t seed, size_t count, float* out) {
+    return guarded([&] {
+        FDB_REQUIRE(out || count == 0, FDB_ERR_INVALID_ARG, "NULL argument");
+        uniform_draws(seed, count, out);
+    });
+}
+
+// ---------------------------------------------------------------------------
+// distances
+// ---------------------------------------------------------------------------
+int fdb_pairwise_distance(fdb_ctx* ctx, int metric, const float* a, const float* b, size_t n,
+                          size_t dim, float* out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && (n == 0 || (a && b && out)), FDB_ERR_INVALID_ARG, "NULL argument");
+        check_metric(metric);
+        if (n == 0) return;
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> da(n * dim), db(n * dim), dout(n);
+        FDB_CUDA(cudaMemcpyAsync(da.p, a, da.bytes(), cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(db.p, b, db.bytes(), cudaMemcpyHostToDevice, s));
+        launch_pairwise(s, metric, da.p, db.p, n, (int)dim, dout.p);
+        FDB_CUDA(cudaMemcpyAsync(out, dout.p, n * 4, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+// ---------------------------------------------------------------------------
+// k-means
+// ---------------------------------------------------------------------------
+int fdb_kmeans_fit(fdb_ctx* ctx, const float* data, size_t n, size_t dim, size_t k,
+                   size_t max_iters, const uint32_t* init_idx, const float* kpp_u, uint64_t seed,
+                   float* centroids_out, uint32_t* assign_out, int* iters_run) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && centroids_out, FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_REQUIRE(n > 0 && dim > 0 && data, FDB_ERR_EMPTY_TRAINING_SET,
+                    "k-means needs at least one point");
+        FDB_REQUIRE(k > 0 && k < (1u << 31), FDB_ERR_INVALID_ARG, "bad k");
+        FDB_REQUIRE(n < (1ull << 32), FDB_ERR_UNSUPPORTED, "at most 2^32-1 points");
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> X(n * dim), C(k * dim);
+        FDB_CUDA(cudaMemcpyAsync(X.p, data, X.bytes(), cudaMemcpyHostToDevice, s));
+        int it = 0;
+        kmeans_fit_dev(ctx->c, X.p, n, (int)dim, (int)k, (int)max_iters, init_idx, kpp_u, seed,
+                       C.p, &it);
+        FDB_CUDA(cudaMemcpyAsync(centroids_out, C.p, C.bytes(), cudaMemcpyDeviceToHost, s));
+        if (assign_out) {
+            DevBuf<uint32_t> A(n);
+            launch_assign(s, X.p, n, (int)dim, (int)dim, C.p, (int)k, A.p);
+            FDB_CUDA(cudaMemcpyAsync(assign_out, A.p, n * 4, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaStreamSynchronize(s));
+        }
+        FDB_CUDA(cudaStreamSynchronize(s));
+        if (iters_run) *iters_run = it;
+    });
+}
+
+int fdb_assign(fdb_ctx* ctx, const float* x, size_t n, const float* centroids, size_t k,
+               size_t dim, uint32_t* out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && (n == 0 || (x && out)) && centroids, FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        FDB_REQUIRE(k > 0, FDB_ERR_INVALID_ARG, "no centroids");
+        if (n == 0) return;
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> X(n * dim), C(k * dim);
+        DevBuf<uint32_t> A(n);
+        FDB_CUDA(cudaMemcpyAsync(X.p, x, X.bytes(), cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(C.p, centroids, C.bytes(), cudaMemcpyHostToDevice, s));
+        launch_assign(s, X.p, n, (int)dim, (int)dim, C.p, (int)k, A.p);
+        FDB_CUDA(cudaMemcpyAsync(out, A.p, n * 4, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int fdb_find_nearest_centroids(fdb_ctx* ctx, const float* centroids, size_t kc, size_t dim,
+                               const float* query, size_t k, uint32_t* out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && centroids && query && (k == 0 || out), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        size_t take = std::min(k, kc);
+        if (take == 0) return;
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> C(kc * dim), Q(dim), D(kc);
+        DevBuf<uint32_t> P(take);
+        FDB_CUDA(cudaMemcpyAsync(C.p, centroids, C.bytes(), cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(Q.p, query, Q.bytes(), cudaMemcpyHostToDevice, s));
+        launch_coarse_dist(s, Q.p, 1, (int)dim, C.p, (int)kc, D.p);
+        launch_select(s, D.p, 1, (int)kc, (int)take, P.p);
+        FDB_CUDA(cudaMemcpyAsync(out, P.p, take * 4, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+// ---------------------------------------------------------------------------
+// product quantizer
+// ---------------------------------------------------------------------------
+int fdb_pq_train(fdb_ctx* ctx, const float* x, size_t n, size_t dim, size_t m, size_t iters,
+                 const uint32_t* init_idx, uint64_t seed, float* codebooks_out, int* iters_out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && codebooks_out, FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_REQUIRE(n > 0 && x, FDB_ERR_EMPTY_TRAINING_SET, "empty training set");
+        FDB_REQUIRE(m > 0, FDB_ERR_INVALID_ARG, "m must be positive");
+        FDB_REQUIRE(dim % m == 0, FDB_ERR_DIM_NOT_DIVISIBLE,
+                    "dimension not divisible by the number of subvectors");
+        FDB_REQUIRE(n >= (size_t)KSUB, FDB_ERR_INSUFFICIENT_VECTORS,
+                    "PQ training needs at least 256 vectors");
+        FDB_REQUIRE(n < (1ull << 32), FDB_ERR_UNSUPPORTED, "at most 2^32-1 vectors");
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        std::vector<uint32_t> idx(m * KSUB);
+        if (init_idx) std::copy(init_idx, init_idx + idx.size(), idx.begin());
+        else
+            for (size_t q = 0; q < m; ++q) sample_indices(seed + q, n, KSUB, idx.data() + q * KSUB);
+        DevBuf<float> X(n * dim), CB(m * KSUB * (dim / m));
+        FDB_CUDA(cudaMemcpyAsync(X.p, x, X.bytes(), cudaMemcpyHostToDevice, s));
+        std::vector<int> its(m);
+        pq_train_dev(ctx->c, X.p, n, (int)dim, (int)m, iters ? (int)iters : 25, idx.data(), CB.p,
+                     its.data());
+        FDB_CUDA(cudaMemcpyAsync(codebooks_out, CB.p, CB.bytes(), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+        if (iters_out) std::copy(its.begin(), its.end(), iters_out);
+    });
+}
+
+int fdb_pq_encode(fdb_ctx* ctx, const float* codebooks, size_t m, size_t dim, const float* x,
+                  size_t n, uint8_t* codes_out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && codebooks && (n == 0 || (x && codes_out)), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        FDB_REQUIRE(m > 0 && dim % m == 0, FDB_ERR_DIM_NOT_DIVISIBLE,
+                    "dimension not divisible by the number of subvectors");
+        if (n == 0) return;
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> X(n * dim), CB(m * KSUB * (dim / m));
+        DevBuf<uint8_t> codes(n * m);
+        FDB_CUDA(cudaMemcpyAsync(X.p, x, X.bytes(), cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(CB.p, codebooks, CB.bytes(), cudaMemcpyHostToDevice, s));
+        launch_pq_encode(s, X.p, n, (int)dim, nullptr, nullptr, CB.p, (int)m, nullptr, codes.p);
+        FDB_CUDA(cudaMemcpyAsync(codes_out, codes.p, n * m, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int fdb_pq_lookup_tables(fdb_ctx* ctx, const float* codebooks, size_t m, size_t dim,
+                         const float* queries, size_t nq, float* lut_out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && codebooks && (nq == 0 || (queries && lut_out)), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        FDB_REQUIRE(m > 0 && dim % m == 0, FDB_ERR_DIM_MISMATCH,
+                    "query dimension does not match the quantizer");
+        if (nq == 0) return;
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        DevBuf<float> Q(nq * dim), CB(m * KSUB * (dim / m)), L(nq * m * KSUB);
+        FDB_CUDA(cudaMemcpyAsync(Q.p, queries, Q.bytes(), cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(CB.p, codebooks, CB.bytes(), cudaMemcpyHostToDevice, s));
+        launch_lut(s, CB.p, (int)m, (int)dim, Q.p, nq, L.p);
+        FDB_CUDA(cudaMemcpyAsync(lut_out, L.p, L.bytes(), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+// ---------------------------------------------------------------------------
+// IVF-PQ
+// ---------------------------------------------------------------------------
+int fdb_ivfpq_build(fdb_ctx* ctx, const float* x, const uint64_t* ids, size_t n, size_t dim,
+                    size_t nlist, size_t m, int metric, const fdb_train_opts* opts,
+                    fdb_ivfpq** out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && out, FDB_ERR_INVALID_ARG, "NULL argument");
+        check_metric(metric);
+        FDB_REQUIRE(n > 0 && x, FDB_ERR_EMPTY_VECTOR_SET, "IVF-PQ build needs vectors");
+        FDB_REQUIRE(dim > 0 && nlist > 0 && m > 0, FDB_ERR_INVALID_ARG,
+                    "dim, nlist and m must be positive");
+        FDB_REQUIRE(dim % m == 0, FDB_ERR_DIM_NOT_DIVISIBLE,
+                    "dimension not divisible by the number of subvectors");
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        std::unique_ptr<fdb_ivfpq> h(new fdb_ivfpq());
+        h->ctx = ctx;
+        h->dim = dim;
+        h->nlist = nlist;
+        h->m = m;
+        h->metric = metric;  // stored, unused by search, as in the reference (ivf_pq.rs:353)
+        fdb_train_opts o{};
+        if (opts) o = *opts;
+        ivfpq_build(h.get(), x, ids, n, o);
+        *out = h.release();
+    });
+}
+
+int fdb_ivfpq_from_trained(fdb_ctx* ctx, const float* centroids, const float* codebooks,
+                           size_t nlist, size_t m, size_t dim, const uint64_t* offsets,
+                           const uint64_t* ids, const uint8_t* codes, int metric,
+                           fdb_ivfpq** out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && out && centroids && codebooks && offsets, FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        check_metric(metric);
+        FDB_REQUIRE(dim > 0 && nlist > 0 && m > 0, FDB_ERR_INVALID_ARG,
+                    "dim, nlist and m must be positive");
+        FDB_REQUIRE(dim % m == 0, FDB_ERR_DIM_NOT_DIVISIBLE,
+                    "dimension not divisible by the number of subvectors");
+        FDB_REQUIRE(offsets[nlist] == 0 || (ids && codes), FDB_ERR_INVALID_ARG, "NULL lists");
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        std::unique_ptr<fdb_ivfpq> h(new fdb_ivfpq());
+        h->ctx = ctx;
+        h->dim = dim;
+        h->nlist = nlist;
+        h->m = m;
+        h->metric = metric;
+        ivfpq_load(h.get(), centroids, codebooks, offsets, ids, codes);
+        *out = h.release();
+    });
+}
+
+int fdb_ivfpq_export(fdb_ivfpq* h, float* centroids, float* codebooks, uint64_t* offsets,
+                     uint64_t* ids, uint8_t* codes) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        cudaStream_t s = h->ctx->c.stream;
+        if (centroids)
+            FDB_CUDA(cudaMemcpyAsync(centroids, h->cents.p, h->cents.bytes(),
+                                     cudaMemcpyDeviceToHost, s));
+        if (codebooks)
+            FDB_CUDA(cudaMemcpyAsync(codebooks, h->cb.p, h->cb.bytes(), cudaMemcpyDeviceToHost, s));
+        if (ids && h->n_total)
+            FDB_CUDA(cudaMemcpyAsync(ids, h->ids.p, h->n_total * 8, cudaMemcpyDeviceToHost, s));
+        if (codes && h->n_total)
+            FDB_CUDA(cudaMemcpyAsync(codes, h->codes.p, h->n_total * h->m, cudaMemcpyDeviceToHost,
+                                     s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+        if (offsets) std::copy(h->h_offs_full.begin(), h->h_offs_full.end(), offsets);
+    });
+}
+
+int fdb_ivfpq_shard(fdb_ivfpq* h, int rank, int world) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        ivfpq_shard(h, rank, world);
+    });
+}
+
+int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        h->nprobe.store(std::min(nprobe, h->nlist), std::memory_order_relaxed);
+    });
+}
+
+size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h) {
+    return h ? h->nprobe.load(std::memory_order_relaxed) : 0;
+}
+size_t fdb_ivfpq_len(const fdb_ivfpq* h) { return h ? h->n_local : 0; }
+size_t fdb_ivfpq_n_partitions(const fdb_ivfpq* h) { return h ? h->nlist : 0; }
+size_t fdb_ivfpq_dim(const fdb_ivfpq* h) { return h ? h->dim : 0; }
+size_t fdb_ivfpq_n_subvectors(const fdb_ivfpq* h) { return h ? h->m : 0; }
+
+static void ivfpq_host_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k, int order,
+                              size_t take, uint64_t* ids, float* dists, uint32_t* counts,
+                              fdb_stats* stats) {
+    cudaStream_t s = h->ctx->c.stream;
+    const size_t per = nq * k;
+    h->s_q.ensure(nq * h->dim);
+    h->s_out_ids.ensure(per);
+    h->s_dists.ensure(per);
+    h->s_counts.ensure(nq);
+    FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
+    ivfpq_search_dev(h, h->s_q.p, nq, k, order, take, h->s_out_ids.p, h->s_dists.p,
+                     h->s_counts.p, stats);
+    if (k == 0) {
+        if (counts) std::fill(counts, counts + nq, 0u);
+        FDB_CUDA(cudaStreamSynchronize(s));
+        return;
+    }
+    FDB_CUDA(cudaMemcpyAsync(ids, h->s_out_ids.p, per * 8, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaMemcpyAsync(dists, h->s_dists.p, per * 4, cudaMemcpyDeviceToHost, s));
+    if (counts)
+        FDB_CUDA(cudaMemcpyAsync(counts, h->s_counts.p, nq * 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+}
+
+int fdb_ivfpq_search(fdb_ivfpq* h, const float* query, size_t k, uint64_t* ids, float* dists,
+                     size_t* n_out) {
+    return guarded([&] {
+        FDB_REQUIRE(h && query && (k == 0 || (ids && dists)), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        // search(): nprobe.min(nlist) lists; nprobe == 0 probes none.
+        size_t take = std::min(h->nprobe.load(std::memory_order_relaxed), h->nlist);
+        uint32_t cnt = 0;
+        ivfpq_host_search(h, query, 1, k, ORDER_FAST4, take, ids, dists, &cnt, nullptr);
+        if (n_out) *n_out = cnt;
+    });
+}
+
+int fdb_ivfpq_batch_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                           uint64_t* ids, float* dists, uint32_t* counts, fdb_stats* stats) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || queries) && (nq == 0 || k == 0 || (ids && dists)),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        if (nq == 0) { if (stats) std::memset(stats, 0, sizeof(*stats)); return; }
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        // batch_search(): nth = nprobe.min(nlist).saturating_sub(1), [..=nth].
+        size_t take = std::max<size_t>(1, std::min(h->nprobe.load(std::memory_order_relaxed),
+                                                   h->nlist));
+        ivfpq_host_search(h, queries, nq, k, ORDER_LANE8, take, ids, dists, counts, stats);
+    });
+}
+
+int fdb_ivfpq_batch_search_device(fdb_ivfpq* h, const float* d_queries, size_t nq, size_t k,
+                                  uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                                  fdb_stats* stats) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || d_queries) && (nq == 0 || k == 0 || (d_ids && d_dists)),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        size_t take = std::max<size_t>(1, std::min(h->nprobe.load(std::memory_order_relaxed),
+                                                   h->nlist));
+        ivfpq_search_dev(h, d_queries, nq, k, ORDER_LANE8, take, d_ids, d_dists, d_counts, stats);
+        FDB_CUDA(cudaStreamSynchronize(h->ctx->c.stream));
+    });
+}
+
+int fdb_ivfpq_free(fdb_ivfpq* h) {
+    return guarded([&] {
+        if (!h) return;
+        DeviceGuard g(h->ctx->c.device);
+        delete h;
+    });
+}
+
+int fdb_ivfpq_shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner) {
+    return guarded([&] {
+        FDB_REQUIRE(world >= 1 && (nlist == 0 || (sizes && owner)), FDB_ERR_INVALID_ARG,
+                    "bad arguments");
+        shard_plan(sizes, nlist, world, owner);
+    });
+}
+
+// ---------------------------------------------------------------------------
+// brute force
+// ---------------------------------------------------------------------------
+int fdb_bf_create(fdb_ctx* ctx, int metric, const float* x, const uint64_t* ids, size_t n,
+                  size_t dim, fdb_bf** out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && out && (n == 0 || x), FDB_ERR_INVALID_ARG, "NULL argument");
+        check_metric(metric);
+        std::unique_ptr<fdb_bf> h(new fdb_bf());
+        h->ctx = ctx;
+        h->metric = metric;
+        *out = h.release();
+        if (n) {
+            int rc = fdb_bf_add(*out, x, ids, n, dim);
+            if (rc != FDB_OK) {
+                std::string msg = g_last_error;
+                delete *out;
+                *out = nullptr;
+                fail(rc, msg);
+            }
+        }
+    });
+}
+
+int fdb_bf_add(fdb_bf* h, const float* x, const uint64_t* ids, size_t n, size_t dim) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (n == 0 || x), FDB_ERR_INVALID_ARG, "NULL argument");
+        if (n == 0) return;
+        std::lock_guard<std::mutex> lk(h->mu);
+        // add() adopts the first vector's dimension (brute_force.rs:75-80);
+        // later rows must match it.
+        if (h->dim == 0) h->dim = dim;
+        FDB_REQUIRE(dim == h->dim, FDB_ERR_DIM_MISMATCH, "vector dimension mismatch");
+        FDB_REQUIRE(h->h_ids.size() + n < (1ull << 32), FDB_ERR_UNSUPPORTED,
+                    "at most 2^32-1 rows");
+        size_t base = h->h_ids.size();
+        h->h_x.insert(h->h_x.end(), x, x + n * dim);
+        for (size_t i = 0; i < n; ++i) h->h_ids.push_back(ids ? ids[i] : (uint64_t)(base + i));
+        h->row0 = 0;
+        h->n = h->h_ids.size();
+        h->sharded = false;
+        h->shard_world = 1;
+        h->dirty = true;
+    });
+}
+
+int fdb_bf_shard(fdb_bf* h, int rank, int world) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        bf_shard(h, rank, world);
+    });
+}
+
+size_t fdb_bf_len(const fdb_bf* h) { return h ? h->n : 0; }
+size_t fdb_bf_dimension(const fdb_bf* h) { return (h && !h->h_ids.empty()) ? h->dim : 0; }
+
+static void bf_host_search(fdb_bf* h, const float* queries, size_t nq, size_t k, uint64_t* ids,
+                           float* dists, uint32_t* counts, fdb_stats* stats) {
+    cudaStream_t s = h->ctx->c.stream;
+    const size_t per = nq * k;
+    h->s_q.ensure(nq * h->dim);
+    h->s_out_ids.ensure(per);
+    h->s_dists.ensure(per);
+    h->s_counts.ensure(nq);
+    FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
+    bf_search_dev(h, h->s_q.p, nq, k, h->s_out_ids.p, h->s_dists.p, h->s_counts.p, stats);
+    FDB_CUDA(cudaMemcpyAsync(ids, h->s_out_ids.p, per * 8, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaMemcpyAsync(dists, h->s_dists.p, per * 4, cudaMemcpyDeviceToHost, s));
+    if (counts)
+        FDB_CUDA(cudaMemcpyAsync(counts, h->s_counts.p, nq * 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+}
+
+static void bf_check_k(fdb_bf* h, size_t k) {
+    // With rows present, k == 0 makes the reference peek an empty heap and
+    // panic (brute_force.rs:140-146).
+    FDB_REQUIRE(k > 0 || h->h_ids.empty(), FDB_ERR_INVALID_ARG, "k must be positive");
+}
+
+int fdb_bf_search(fdb_bf* h, const float* query, size_t k, uint64_t* ids, float* dists,
+                  size_t* n_out) {
+    return guarded([&] {
+        FDB_REQUIRE(h && query && (k == 0 || (ids && dists)), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        bf_check_k(h, k);
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        uint32_t cnt = 0;
+        if (k > 0) bf_host_search(h, query, 1, k, ids, dists, &cnt, nullptr);
+        if (n_out) *n_out = cnt;
+    });
+}
+
+int fdb_bf_batch_search(fdb_bf* h, const float* queries, size_t nq, size_t k, uint64_t* ids,
+                        float* dists, uint32_t* counts, fdb_stats* stats) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || queries) && (nq == 0 || k == 0 || (ids && dists)),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        if (stats) std::memset(stats, 0, sizeof(*stats));
+        if (nq == 0) return;
+        bf_check_k(h, k);
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        if (k == 0) { if (counts) std::fill(counts, counts + nq, 0u); return; }
+        bf_host_search(h, queries, nq, k, ids, dists, counts, stats);
+    });
+}
+
+int fdb_bf_batch_search_device(fdb_bf* h, const float* d_queries, size_t nq, size_t k,
+                               uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                               fdb_stats* stats) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || d_queries) && (nq == 0 || k == 0 || (d_ids && d_dists)),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        bf_check_k(h, k);
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        bf_search_dev(h, d_queries, nq, k, d_ids, d_dists, d_counts, stats);
+        FDB_CUDA(cudaStreamSynchronize(h->ctx->c.stream));
+    });
+}
+
+int fdb_bf_free(fdb_bf* h) {
+    return guarded([&] {
+        if (!h) return;
+        DeviceGuard g(h->ctx->c.device);
+        delete h;
+    });
+}
+
+}  // extern "C"

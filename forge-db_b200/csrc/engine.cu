@@ -1,0 +1,458 @@
+// engine.cu -- host orchestration of the IVF-PQ and brute-force indexes.
+//
+// IVF-PQ build follows IVFPQIndex::build (forge-db src/index/ivf_pq.rs:374-506):
+//   1. k-means(nlist, 25) on a training sample        (:383-400)
+//   2. assign every vector, lists keep input order     (:403-419)
+//   3. PQ trained on a sample of residuals v - c(v)    (:422-447)
+//   4. every vector's residual encoded into its list   (:450-478)
+// Search follows batch_search (:850-1047) / search (:590-677): coarse
+// quantizer, probe selection, per-(query, list) LUT + scan + top-k, and, for
+// an index whose lists are sharded over several devices, an ncclAllGather of
+// the local top-k lists followed by a merge on every device.
+#include <algorithm>
+#include <numeric>
+
+#include "fdb_device.cuh"
+#include "fdb_internal.h"
+#include "fdb_kernels.h"
+
+namespace fdb {
+
+void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
+                  const uint32_t* init_idx_host, float* cb, int* iters_out);
+
+// ---------------------------------------------------------------------------
+// small build kernels
+// ---------------------------------------------------------------------------
+__global__ void scatter_slot_kernel(const uint32_t* __restrict__ perm, size_t n,
+                                    uint32_t* __restrict__ slot) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) slot[perm[t]] = (uint32_t)t;
+}
+
+__global__ void permute_ids_kernel(const uint32_t* __restrict__ perm, size_t n,
+                                   const uint64_t* __restrict__ ids, uint64_t* __restrict__ out) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) out[t] = ids ? ids[perm[t]] : (uint64_t)perm[t];
+}
+
+// residual sample: out[i] = x[idx[i]] - cents[assign[idx[i]]]  (ivf_pq.rs:431-442)
+__global__ void residual_gather_kernel(const float* __restrict__ x, size_t dim,
+                                       const uint32_t* __restrict__ idx, size_t count,
+                                       const uint32_t* __restrict__ assign,
+                                       const float* __restrict__ cents, float* __restrict__ out) {
+    size_t total = count * dim;
+    for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (size_t)gridDim.x * blockDim.x) {
+        size_t r = t / dim, c = t - r * dim;
+        size_t v = idx[r];
+        out[t] = __fsub_rn(x[v * dim + c], cents[(size_t)assign[v] * dim + c]);
+    }
+}
+
+static unsigned blocks_for(size_t n, unsigned threads = 256) {
+    return (unsigned)((n + threads - 1) / threads);
+}
+
+// ---------------------------------------------------------------------------
+// k-means entry used by the C ABI and by the IVF build
+// ---------------------------------------------------------------------------
+// Draws for one k-means problem over n points (see fdb_train_opts).
+static void kmeans_draws(size_t n, size_t k, const uint32_t* init_idx, const float* kpp_u,
+                         uint64_t seed, std::vector<uint32_t>& idx, std::vector<float>& u) {
+    idx.resize(k);
+    u.assign(k, 0.0f);
+    if (init_idx) {
+        std::copy(init_idx, init_idx + k, idx.begin());
+    } else if (k > 64) {
+        sample_indices(seed, n, k, idx.data());
+    } else {
+        uint64_t st = seed ^ 0x6b6d65616e737070ull;  // independent stream for k-means++ picks
+        for (size_t c = 0; c < k; ++c)
+            idx[c] = (uint32_t)(((unsigned __int128)splitmix64(st) * n) >> 64);
+    }
+    if (k <= 64) {
+        if (kpp_u) std::copy(kpp_u, kpp_u + k, u.begin());
+        else uniform_draws(seed + 0x9e37ull, k, u.data());
+    }
+}
+
+// Fits k centroids on device rows x[n][dim] (KMeans::fit_raw, kmeans.rs:87-193).
+void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_iters,
+                    const uint32_t* init_idx, const float* kpp_u, uint64_t seed, float* cent,
+                    int* iters_run) {
+    FDB_REQUIRE(n > 0 && dim > 0, FDB_ERR_EMPTY_TRAINING_SET, "k-means needs at least one point");
+    FDB_REQUIRE(k > 0, FDB_ERR_INVALID_ARG, "k must be positive");
+    std::vector<uint32_t> idx;
+    std::vector<float> u;
+    if (k > 64) {
+        FDB_REQUIRE(n >= (size_t)k, FDB_ERR_INSUFFICIENT_VECTORS,
+                    "random-sample init needs at least k points");
+    }
+    kmeans_draws(n, k, init_idx, kpp_u, seed, idx, u);
+    if (k > 64) {
+        for (int c = 0; c < k; ++c)
+            FDB_REQUIRE(idx[c] < n, FDB_ERR_INVALID_ARG, "init index out of range");
+        DevBuf<uint32_t> d_idx(k);
+        FDB_CUDA(cudaMemcpyAsync(d_idx.p, idx.data(), k * sizeof(uint32_t),
+                                 cudaMemcpyHostToDevice, ctx.stream));
+        launch_gather_rows(ctx.stream, x, dim, d_idx.p, k, cent);
+        FDB_CUDA(cudaStreamSynchronize(ctx.stream));
+    } else {
+        kmeans_pp_init(ctx, x, n, dim, k, idx.data(), u.data(), cent);
+    }
+    KMeansProblem pb{x, n, dim, dim, 1, k, max_iters};
+    int it = 0;
+    kmeans_run(ctx, pb, cent, &it);
+    if (iters_run) *iters_run = it;
+}
+
+// ---------------------------------------------------------------------------
+// IVF-PQ build
+// ---------------------------------------------------------------------------
+void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, size_t n,
+                 const fdb_train_opts& o) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const int dim = (int)h->dim, nlist = (int)h->nlist, m = (int)h->m;
+    FDB_REQUIRE(n > 0, FDB_ERR_EMPTY_VECTOR_SET, "IVF-PQ build needs at least one vector");
+    FDB_REQUIRE(n < (1ull << 32), FDB_ERR_UNSUPPORTED, "at most 2^32-1 vectors per index");
+    FDB_REQUIRE(h->dim % h->m == 0, FDB_ERR_DIM_NOT_DIVISIBLE,
+                "dimension not divisible by the number of subvectors");
+    const size_t ivf_n = o.ivf_sample ? std::min(o.ivf_sample, n) : std::min<size_t>(n, 30000);
+    const size_t pq_n = o.pq_sample ? std::min(o.pq_sample, n) : std::min<size_t>(n, 100000);
+    const int ivf_iters = o.ivf_iters ? (int)o.ivf_iters : 25;
+    const int pq_iters = o.pq_iters ? (int)o.pq_iters : 25;
+    FDB_REQUIRE(pq_n >= (size_t)KSUB, FDB_ERR_INSUFFICIENT_VECTORS,
+                "PQ training needs at least 256 vectors");
+
+    DevBuf<float> X(n * dim);
+    FDB_CUDA(cudaMemcpyAsync(X.p, x_host, X.bytes(), cudaMemcpyHostToDevice, s));
+
+    // 1. IVF training sample and k-means.
+    std::vector<uint32_t> sidx(ivf_n);
+    if (o.ivf_sample_idx) std::copy(o.ivf_sample_idx, o.ivf_sample_idx + ivf_n, sidx.begin());
+    else if (ivf_n == n) std::iota(sidx.begin(), sidx.end(), 0u);  // all vectors, in order
+    else sample_indices(o.seed, n, ivf_n, sidx.data());
+    for (size_t i = 0; i < ivf_n; ++i)
+        FDB_REQUIRE(sidx[i] < n, FDB_ERR_INVALID_ARG, "IVF sample index out of range");
+    DevBuf<uint32_t> d_sidx(ivf_n);
+    DevBuf<float> S(ivf_n * dim);
+    FDB_CUDA(cudaMemcpyAsync(d_sidx.p, sidx.data(), ivf_n * 4, cudaMemcpyHostToDevice, s));
+    launch_gather_rows(s, X.p, dim, d_sidx.p, ivf_n, S.p);
+    h->cents.alloc((size_t)nlist * dim);
+    int it = 0;
+    kmeans_fit_dev(c, S.p, ivf_n, dim, nlist, ivf_iters, o.ivf_init_idx, o.ivf_kpp_u,
+                   o.seed + 1, h->cents.p, &it);
+    S.release();
+
+    // 2. Assign all vectors; stable grouping keeps input order inside lists.
+    DevBuf<uint32_t> assign(n), perm(n), slot(n);
+    launch_assign(s, X.p, n, dim, dim, h->cents.p, nlist, assign.p);
+    h->offs.alloc(nlist + 1);
+    group_by_assignment(c, assign.p, n, nlist, perm.p, h->offs.p);
+    scatter_slot_kernel<<<blocks_for(n), 256, 0, s>>>(perm.p, n, slot.p);
+    FDB_LAUNCH_CHECK();
+
+    // 3. PQ on a sample of residuals.
+    std::vector<uint32_t> pidx(pq_n);
+    if (o.pq_sample_idx) std::copy(o.pq_sample_idx, o.pq_sample_idx + pq_n, pidx.begin());
+    else sample_indices(o.seed + 2, n, pq_n, pidx.data());
+    for (size_t i = 0; i < pq_n; ++i)
+        FDB_REQUIRE(pidx[i] < n, FDB_ERR_INVALID_ARG, "PQ sample index out of range");
+    DevBuf<uint32_t> d_pidx(pq_n);
+    DevBuf<float> R(pq_n * dim);
+    FDB_CUDA(cudaMemcpyAsync(d_pidx.p, pidx.data(), pq_n * 4, cudaMemcpyHostToDevice, s));
+    residual_gather_kernel<<<std::min<unsigned>(blocks_for(pq_n * dim), 148 * 32), 256, 0, s>>>(
+        X.p, dim, d_pidx.p, pq_n, assign.p, h->cents.p, R.p);
+    FDB_LAUNCH_CHECK();
+    std::vector<uint32_t> pinit((size_t)m * KSUB);
+    if (o.pq_init_idx) {
+        std::copy(o.pq_init_idx, o.pq_init_idx + pinit.size(), pinit.begin());
+    } else {
+        for (int q = 0; q < m; ++q)
+            sample_indices(o.seed + 3 + (uint64_t)q, pq_n, KSUB, pinit.data() + (size_t)q * KSUB);
+    }
+    const int sub = dim / m;
+    h->cb.alloc((size_t)m * KSUB * sub);
+    std::vector<int> pq_its(m);
+    pq_train_dev(c, R.p, pq_n, dim, m, pq_iters, pinit.data(), h->cb.p, pq_its.data());
+    R.release();
+
+    // 4. Encode every residual into its list slot; ids in list order.
+    h->codes.alloc(n * m);
+    launch_pq_encode(s, X.p, n, dim, h->cents.p, assign.p, h->cb.p, m, slot.p, h->codes.p);
+    DevBuf<uint64_t> d_ids_in;
+    if (ids_host) {
+        d_ids_in.alloc(n);
+        FDB_CUDA(cudaMemcpyAsync(d_ids_in.p, ids_host, n * 8, cudaMemcpyHostToDevice, s));
+    }
+    h->ids.alloc(n);
+    permute_ids_kernel<<<blocks_for(n), 256, 0, s>>>(perm.p, n, d_ids_in.p, h->ids.p);
+    FDB_LAUNCH_CHECK();
+    h->h_offs_full.resize(nlist + 1);
+    FDB_CUDA(cudaMemcpyAsync(h->h_offs_full.data(), h->offs.p, (nlist + 1) * 8,
+                             cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    h->h_offs = h->h_offs_full;
+    h->n_total = h->n_local = n;
+}
+
+void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_t* offsets,
+                const uint64_t* ids, const uint8_t* codes) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const size_t nlist = h->nlist, dim = h->dim, m = h->m;
+    FDB_REQUIRE(offsets[0] == 0, FDB_ERR_INVALID_ARG, "offsets[0] must be 0");
+    for (size_t l = 0; l < nlist; ++l)
+        FDB_REQUIRE(offsets[l + 1] >= offsets[l], FDB_ERR_INVALID_ARG, "offsets must not decrease");
+    const size_t n = offsets[nlist];
+    FDB_REQUIRE(n < (1ull << 32), FDB_ERR_UNSUPPORTED, "at most 2^32-1 vectors per index");
+    h->cents.alloc(nlist * dim);
+    h->cb.alloc(m * KSUB * (dim / m));
+    h->offs.alloc(nlist + 1);
+    h->ids.alloc(n);
+    h->codes.alloc(n * m);
+    FDB_CUDA(cudaMemcpyAsync(h->cents.p, cents, h->cents.bytes(), cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(h->cb.p, cb, h->cb.bytes(), cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(h->offs.p, offsets, h->offs.bytes(), cudaMemcpyHostToDevice, s));
+    if (n) {
+        FDB_CUDA(cudaMemcpyAsync(h->ids.p, ids, n * 8, cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(h->codes.p, codes, n * m, cudaMemcpyHostToDevice, s));
+    }
+    FDB_CUDA(cudaStreamSynchronize(s));
+    h->h_offs_full.assign(offsets, offsets + nlist + 1);
+    h->h_offs = h->h_offs_full;
+    h->n_total = h->n_local = n;
+}
+
+// Greedy balance of list bytes: largest list first, onto the least-loaded
+// device (ties: lower list index first, lower rank first).
+void shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner) {
+    std::vector<size_t> order(nlist);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](size_t a, size_t b) { return sizes[a] > sizes[b]; });
+    std::vector<uint64_t> load(world, 0);
+    for (size_t l : order) {
+        int best = 0;
+        for (int r = 1; r < world; ++r)
+            if (load[r] < load[best]) best = r;
+        owner[l] = best;
+        load[best] += sizes[l];
+    }
+}
+
+void ivfpq_shard(fdb_ivfpq* h, int rank, int world) {
+    FDB_REQUIRE(world >= 1 && rank >= 0 && rank < world, FDB_ERR_INVALID_ARG, "bad rank/world");
+    const size_t nlist = h->nlist;
+    std::vector<uint64_t> sizes(nlist);
+    for (size_t l = 0; l < nlist; ++l) sizes[l] = h->h_offs_full[l + 1] - h->h_offs_full[l];
+    std::vector<int> owner(nlist);
+    shard_plan(sizes.data(), nlist, world, owner.data());
+    // Lists are scanned over [begin[l], end[l]).  A list held by another
+    // device gets end == begin.  Row positions (the tie-break tags) stay
+    // those of the unsharded index, so results do not depend on `world`.
+    std::vector<uint64_t> be(2 * nlist);
+    size_t held = 0;
+    for (size_t l = 0; l < nlist; ++l) {
+        be[l] = h->h_offs_full[l];
+        be[nlist + l] = owner[l] == rank ? h->h_offs_full[l + 1] : h->h_offs_full[l];
+        if (owner[l] == rank) held += sizes[l];
+    }
+    Ctx& c = h->ctx->c;
+    h->shard_be.alloc(2 * nlist);
+    FDB_CUDA(cudaMemcpyAsync(h->shard_be.p, be.data(), be.size() * 8, cudaMemcpyHostToDevice,
+                             c.stream));
+    FDB_CUDA(cudaStreamSynchronize(c.stream));
+    h->n_local = held;
+    h->sharded = world > 1;
+    h->shard_world = world;
+    h->shard_rank = rank;
+}
+
+void bf_shard(fdb_bf* h, int rank, int world) {
+    FDB_REQUIRE(world >= 1 && rank >= 0 && rank < world, FDB_ERR_INVALID_ARG, "bad rank/world");
+    const size_t total = h->h_ids.size();
+    const size_t r0 = total * (size_t)rank / (size_t)world;
+    const size_t r1 = total * (size_t)(rank + 1) / (size_t)world;
+    h->row0 = r0;
+    h->n = r1 - r0;
+    h->sharded = world > 1;
+    h->shard_world = world;
+    h->dirty = true;
+}
+
+// ---------------------------------------------------------------------------
+// IVF-PQ search on device buffers
+// ---------------------------------------------------------------------------
+static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_keys,
+                               const uint64_t* local_ids, DevBuf<uint64_t>& gather,
+                               DevBuf<uint64_t>& merged, DevBuf<uint64_t>& merged_ids) {
+    cudaStream_t s = c.stream;
+    const size_t per = nq * (size_t)k;
+    gather.ensure(per * 2 * (size_t)(c.world + 1));
+    uint64_t* send = gather.p + per * 2 * (size_t)c.world;
+    FDB_CUDA(cudaMemcpyAsync(send, local_keys, per * 8, cudaMemcpyDeviceToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(send + per, local_ids, per * 8, cudaMemcpyDeviceToDevice, s));
+    FDB_NCCL(ncclAllGather(send, gather.p, per * 2, ncclUint64, c.comm, s));
+    merged.ensure(per);
+    merged_ids.ensure(per);
+    launch_merge_lists(s, gather.p, c.world, per * 2, nq, k, merged.p);
+    launch_lookup_gathered(s, merged.p, gather.p, gather.p + per, c.world, per * 2, nq, k,
+                           merged_ids.p);
+}
+
+void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
+                      uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const int nlist = (int)h->nlist;
+    if (st) std::memset(st, 0, sizeof(*st));
+    if (nq == 0) return;
+    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED, "k above FDB_MAX_K");
+    FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
+                "sharded index needs a communicator of the same size");
+    const size_t per = nq * k;
+    StageTimer tm(s, st != nullptr);
+    tm.mark();
+    if (k == 0) return;
+    h->s_keys.ensure(per);
+    h->s_ids.ensure(per);
+    if (take == 0) {
+        // search() with nprobe == 0 probes nothing (ivf_pq.rs:548-552)
+        FDB_CUDA(cudaMemsetAsync(h->s_keys.p, 0xff, per * 8, s));
+    } else {
+        h->s_coarse.ensure(nq * (size_t)nlist);
+        h->s_probe.ensure(nq * take);
+        launch_coarse_dist(s, dQ, (int)nq, (int)h->dim, h->cents.p, nlist, h->s_coarse.p);
+        launch_select(s, h->s_coarse.p, (int)nq, nlist, (int)take, h->s_probe.p);
+        tm.mark();
+        h->s_stat.ensure(2);
+        FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 16, s));
+        ScanParams a{};
+        a.Q = dQ;
+        a.nq = (int)nq;
+        a.dim = (int)h->dim;
+        a.m = (int)h->m;
+        a.cents = h->cents.p;
+        a.cb = h->cb.p;
+        a.offs = h->sharded ? h->shard_be.p : h->offs.p;
+        a.ends = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
+        a.codes = h->codes.p;
+        a.probes = h->s_probe.p;
+        a.nprobe = (int)take;
+        a.k = (int)k;
+        a.out_keys = h->s_keys.p;
+        a.stat = h->s_stat.p;
+        launch_scan(s, a, order);
+    }
+    tm.mark();
+    launch_keys_to_ids(s, h->s_keys.p, per, h->ids.p, 0, h->s_ids.p);
+    const uint64_t* keys = h->s_keys.p;
+    const uint64_t* ids = h->s_ids.p;
+    if (h->sharded) {
+        exchange_and_merge(c, nq, (int)k, h->s_keys.p, h->s_ids.p, h->s_gather, h->s_merged,
+                           h->s_merged_ids);
+        keys = h->s_merged.p;
+        ids = h->s_merged_ids.p;
+    }
+    launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
+    tm.mark();
+    if (st) {
+        unsigned long long hs[2] = {0, 0};
+        if (take > 0)
+            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 16, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+        st->lists_probed = hs[0];
+        st->codes_scanned = hs[1];
+        st->bytes_scanned = hs[1] * h->m;
+        size_t last = tm.ev.size() - 1;
+        if (take > 0) {
+            st->coarse_ms = tm.ms(0, 1);
+            st->scan_ms = tm.ms(1, 2);
+            st->merge_ms = tm.ms(2, 3);
+        }
+        st->total_ms = tm.ms(0, last);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// brute force
+// ---------------------------------------------------------------------------
+void bf_upload(fdb_bf* h) {
+    if (!h->dirty) return;
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    h->x.alloc(h->n * h->dim);
+    h->ids.alloc(h->n);
+    if (h->n) {
+        FDB_CUDA(cudaMemcpyAsync(h->x.p, h->h_x.data() + h->row0 * h->dim, h->x.bytes(),
+                                 cudaMemcpyHostToDevice, s));
+        FDB_CUDA(cudaMemcpyAsync(h->ids.p, h->h_ids.data() + h->row0, h->ids.bytes(),
+                                 cudaMemcpyHostToDevice, s));
+    }
+    if (h->metric == COSINE) {
+        h->norms.alloc(h->n);
+        launch_row_norms(s, h->x.p, h->n, (int)h->dim, h->norms.p);
+    }
+    FDB_CUDA(cudaStreamSynchronize(s));
+    h->dirty = false;
+}
+
+void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
+                   float* d_dists, uint32_t* d_counts, fdb_stats* st) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    if (st) std::memset(st, 0, sizeof(*st));
+    if (nq == 0) return;
+    bf_upload(h);
+    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED, "k above FDB_MAX_K");
+    FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
+                "sharded index needs a communicator of the same size");
+    StageTimer tm(s, st != nullptr);
+    tm.mark();
+    if (k == 0) return;
+    const size_t per = nq * k;
+    h->s_keys.ensure(per);
+    h->s_ids.ensure(per);
+    if (h->n == 0) {
+        FDB_CUDA(cudaMemsetAsync(h->s_keys.p, 0xff, per * 8, s));
+    } else {
+        const float* qn = nullptr;
+        if (h->metric == COSINE) {
+            h->s_qnorm.ensure(nq);
+            launch_row_norms(s, dQ, nq, (int)h->dim, h->s_qnorm.p);
+            qn = h->s_qnorm.p;
+        }
+        size_t psz = bf_part_size(h->n, (int)nq, (int)k, c.sm_count);
+        h->s_part.ensure(psz);
+        int chunks = launch_bf_scan(s, h->metric, dQ, (int)nq, qn, h->x.p, h->n, (int)h->dim,
+                                    h->norms.p, h->row0, (int)k, c.sm_count, h->s_part.p,
+                                    h->s_part.n);
+        launch_merge_lists(s, h->s_part.p, chunks, nq * k, nq, (int)k, h->s_keys.p);
+    }
+    tm.mark();
+    launch_keys_to_ids(s, h->s_keys.p, per, h->ids.p, h->row0, h->s_ids.p);
+    const uint64_t* keys = h->s_keys.p;
+    const uint64_t* ids = h->s_ids.p;
+    if (h->sharded) {
+        exchange_and_merge(c, nq, (int)k, h->s_keys.p, h->s_ids.p, h->s_gather, h->s_merged,
+                           h->s_merged_ids);
+        keys = h->s_merged.p;
+        ids = h->s_merged_ids.p;
+    }
+    launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
+    tm.mark();
+    if (st) {
+        FDB_CUDA(cudaStreamSynchronize(s));
+        st->lists_probed = 0;
+        st->codes_scanned = (uint64_t)nq * h->n;
+        st->bytes_scanned = (uint64_t)h->n * h->dim * 4;
+        st->scan_ms = tm.ms(0, 1);
+        st->merge_ms = tm.ms(1, 2);
+        st->total_ms = tm.ms(0, 2);
+    }
+}
+
+}  // namespace fdb

@@ -1,0 +1,291 @@
+// fdb_device.cuh -- device helpers shared by every kernel.
+//
+// 1. Distances in the reference's AVX2 summation order (bit-exact):
+//    8 lane accumulators over i = j (mod 8) with fused multiply-add, a
+//    left-to-right sum of the 8 lanes, then an unfused scalar tail
+//    (forge-db src/distance/simd.rs:338-366, 427-456, 469-517).  All
+//    arithmetic goes through __f*_rn intrinsics and the translation units are
+//    built with -fmad=false, so the compiler cannot re-associate or contract.
+// 2. Orderable 64-bit keys: (monotone image of the f32 distance) << 32 | tag.
+//    Ascending key order is ascending distance with ties broken by the tag
+//    (a row position), which makes every top-k result unique and independent
+//    of how the rows are split across warps, blocks or devices.
+// 3. WarpTopK: a warp-wide sorted list of the K = 32*P smallest keys held in
+//    registers, fed through a per-warp shared-memory buffer and merged 32
+//    candidates at a time with a bitonic network.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fdb {
+
+constexpr int KSUB = 256;              // codewords per PQ subspace (constants.rs:10)
+constexpr uint64_t KEY_NONE = ~0ull;   // empty slot: sorts after every real key
+
+// ---------------------------------------------------------------------------
+// orderable keys
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t f2ord(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t o) {
+    uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+    return __uint_as_float(u);
+}
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t tag) {
+    return ((uint64_t)f2ord(d) << 32) | tag;
+}
+__device__ __forceinline__ float key_dist(uint64_t key) { return ord2f((uint32_t)(key >> 32)); }
+__device__ __forceinline__ uint32_t key_tag(uint64_t key) { return (uint32_t)key; }
+
+// ---------------------------------------------------------------------------
+// exact-order distances (generic length, any alignment)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float lane_sum(const float (&acc)[8]) {
+    float t = acc[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) t = __fadd_rn(t, acc[j]);
+    return t;
+}
+
+// euclidean_distance_squared_avx2 (simd.rs:338-366)
+__device__ __forceinline__ float l2sq_exact(const float* a, const float* b, int len) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    int i = 0;
+    for (; i + 8 <= len; i += 8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float d = __fsub_rn(a[i + j], b[i + j]);
+            acc[j] = __fmaf_rn(d, d, acc[j]);
+        }
+    }
+    float t = lane_sum(acc);
+    for (; i < len; ++i) {
+        float d = __fsub_rn(a[i], b[i]);
+        t = __fadd_rn(t, __fmul_rn(d, d));
+    }
+    return t;
+}
+
+// dot_product_avx2 (simd.rs:427-456)
+__device__ __forceinline__ float dot_exact(const float* a, const float* b, int len) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    int i = 0;
+    for (; i + 8 <= len; i += 8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fmaf_rn(a[i + j], b[i + j], acc[j]);
+    }
+    float t = lane_sum(acc);
+    for (; i < len; ++i) t = __fadd_rn(t, __fmul_rn(a[i], b[i]));
+    return t;
+}
+
+// manhattan_distance_avx2 (simd.rs:378-418)
+__device__ __forceinline__ float l1_exact(const float* a, const float* b, int len) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    int i = 0;
+    for (; i + 8 <= len; i += 8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], fabsf(__fsub_rn(a[i + j], b[i + j])));
+    }
+    float t = lane_sum(acc);
+    for (; i < len; ++i) t = __fadd_rn(t, fabsf(__fsub_rn(a[i], b[i])));
+    return t;
+}
+
+// cosine_distance_avx2 (simd.rs:469-517) from a dot product and the two
+// squared norms, each already summed in the AVX2 order.
+__device__ __forceinline__ float cosine_from(float dot, float na, float nb) {
+    float np = __fsqrt_rn(__fmul_rn(na, nb));
+    if (np == 0.0f) return 0.0f;
+    return __fsub_rn(1.0f, __fdiv_rn(dot, np));
+}
+
+enum Metric : int { EUCLIDEAN = 0, EUCLIDEAN_SQUARED = 1, COSINE = 2, DOT_PRODUCT = 3, MANHATTAN = 4 };
+
+// ---------------------------------------------------------------------------
+// PQ asymmetric distance summation orders
+// ---------------------------------------------------------------------------
+// ORDER_LANE8: asymmetric_distance_simd_avx2 / batch_asymmetric_distance_avx2
+//   (pq.rs:318-402, 435-485): lane j sums t[j], t[j+8], ... over full groups of
+//   8 subspaces; lanes summed left to right; serial tail.  Used by batch_search.
+// ORDER_FAST4: asymmetric_distance_fast (pq.rs:218-245): running sum of
+//   ((t0+t1)+t2)+t3 per group of 4, serial tail.  Used by search.
+constexpr int ORDER_LANE8 = 0;
+constexpr int ORDER_FAST4 = 1;
+
+template <int ORDER>
+__device__ __forceinline__ float adc_sum(const float* t, int m) {
+    if (ORDER == ORDER_LANE8) {
+        int full = m & ~7;
+        float total;
+        if (full > 0) {
+            float acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = t[j];
+            for (int i = 8; i < full; i += 8) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], t[i + j]);
+            }
+            total = lane_sum(acc);
+        } else {
+            total = 0.0f;
+        }
+        for (int i = full; i < m; ++i) total = __fadd_rn(total, t[i]);
+        return total;
+    } else {
+        float sum = 0.0f;
+        int i = 0;
+        for (; i + 4 <= m; i += 4) {
+            float g = __fadd_rn(__fadd_rn(__fadd_rn(t[i], t[i + 1]), t[i + 2]), t[i + 3]);
+            sum = __fadd_rn(sum, g);
+        }
+        for (; i < m; ++i) sum = __fadd_rn(sum, t[i]);
+        return sum;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// warp top-k
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t kmin(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ uint64_t kmax(uint64_t a, uint64_t b) { return a < b ? b : a; }
+
+// Sort one key per lane ascending across the warp (bitonic network).
+__device__ __forceinline__ uint64_t warp_sort32(uint64_t c, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            uint64_t o = __shfl_xor_sync(0xffffffffu, c, stride);
+            bool up = (lane & size) == 0;
+            bool lower = (lane & stride) == 0;
+            c = (lower == up) ? kmin(c, o) : kmax(c, o);
+        }
+    }
+    return c;
+}
+
+// Entry i of the sorted list lives in register i / 32 of lane i % 32.
+template <int P>
+struct WarpTopK {
+    static constexpr int K = 32 * P;
+    uint64_t L[P];
+    uint64_t thr;     // key of entry k-1: only keys below it can enter
+    int k;            // 1 <= k <= K
+    int nbuf;         // warp-uniform count of buffered candidates
+    uint64_t* buf;    // this warp's 64-entry shared buffer
+    int lane;
+
+    __device__ __forceinline__ void init(int k_, uint64_t* buf_) {
+        lane = threadIdx.x & 31;
+#pragma unroll
+        for (int e = 0; e < P; ++e) L[e] = KEY_NONE;
+        thr = KEY_NONE;
+        k = k_;
+        nbuf = 0;
+        buf = buf_;
+    }
+
+    // Merge one candidate per lane (KEY_NONE for none) into the list.
+    __device__ __forceinline__ void merge32(uint64_t c) {
+        c = warp_sort32(c, lane);
+        // Pair L[K-1-i] with candidate i: the result is bitonic and holds the
+        // K smallest of both sequences.
+        uint64_t o = __shfl_sync(0xffffffffu, c, 31 - lane);
+        L[P - 1] = kmin(L[P - 1], o);
+#pragma unroll
+        for (int t = P / 2; t >= 1; t >>= 1) {
+#pragma unroll
+            for (int e = 0; e < P; ++e) {
+                if ((e & t) == 0) {
+                    uint64_t a = L[e], b = L[e + t];
+                    L[e] = kmin(a, b);
+                    L[e + t] = kmax(a, b);
+                }
+            }
+        }
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+#pragma unroll
+            for (int e = 0; e < P; ++e) {
+                uint64_t v = __shfl_xor_sync(0xffffffffu, L[e], s);
+                L[e] = ((lane & s) == 0) ? kmin(L[e], v) : kmax(L[e], v);
+            }
+        }
+        uint64_t t = KEY_NONE;
+        const int idx = k - 1;
+#pragma unroll
+        for (int e = 0; e < P; ++e)
+            if (e == (idx >> 5)) t = L[e];
+        thr = __shfl_sync(0xffffffffu, t, idx & 31);
+    }
+
+    // Offer one key per lane (all 32 lanes must call).
+    __device__ __forceinline__ void add(uint64_t key, bool valid) {
+        bool pass = valid && key < thr;
+        unsigned mask = __ballot_sync(0xffffffffu, pass);
+        if (mask == 0) return;
+        if (pass) {
+            int pos = nbuf + __popc(mask & ((1u << lane) - 1u));
+            buf[pos] = key;
+        }
+        nbuf += __popc(mask);
+        if (nbuf >= 32) {
+            __syncwarp();
+            uint64_t c = buf[lane];
+            uint64_t rest = (lane + 32 < nbuf) ? buf[lane + 32] : KEY_NONE;
+            __syncwarp();
+            if (lane + 32 < nbuf) buf[lane] = rest;
+            nbuf -= 32;
+            __syncwarp();
+            merge32(c);
+        }
+    }
+
+    __device__ __forceinline__ void flush() {
+        if (nbuf > 0) {
+            __syncwarp();
+            uint64_t c = (lane < nbuf) ? buf[lane] : KEY_NONE;
+            __syncwarp();
+            nbuf = 0;
+            merge32(c);
+        }
+    }
+
+    // Ingest n keys from memory (shared or global) as candidates.
+    __device__ __forceinline__ void ingest(const uint64_t* keys, int n) {
+        for (int base = 0; base < n; base += 32) {
+            uint64_t c = (base + lane < n) ? keys[base + lane] : KEY_NONE;
+            bool any = __any_sync(0xffffffffu, c < thr);
+            if (any) merge32(c < thr ? c : KEY_NONE);
+        }
+    }
+
+    // Write the first k entries to out[0..k).
+    __device__ __forceinline__ void store(uint64_t* out) const {
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+            int i = e * 32 + lane;
+            if (i < k) out[i] = L[e];
+        }
+    }
+};
+
+// Block-wide merge: every warp has stored its k best to smem[w*k ...]; warp 0
+// folds them into its own list.  Caller syncs before and after.
+template <int P>
+__device__ __forceinline__ void block_merge_warp0(WarpTopK<P>& tk, const uint64_t* lists,
+                                                  int nwarps) {
+    for (int w = 1; w < nwarps; ++w) tk.ingest(lists + w * tk.k, tk.k);
+}
+
+}  // namespace fdb

@@ -1,0 +1,265 @@
+// fdb_internal.h -- host-side internals shared by the engine's translation
+// units: error propagation, device buffers, the per-device context and the
+// index handles behind the opaque C types of include/forgegpu.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "forgegpu.h"
+
+namespace fdb {
+
+// ---------------------------------------------------------------------------
+// errors: thrown inside the engine, turned into a status code at the C ABI
+// ---------------------------------------------------------------------------
+struct Error {
+    int code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(int code, const std::string& msg);
+void set_last_error(const std::string& msg);
+
+#define FDB_CUDA(x)                                                                           \
+    do {                                                                                      \
+        cudaError_t e__ = (x);                                                                \
+        if (e__ != cudaSuccess)                                                               \
+            ::fdb::fail(e__ == cudaErrorMemoryAllocation ? FDB_ERR_OOM : FDB_ERR_CUDA,         \
+                        std::string(#x) + ": " + cudaGetErrorString(e__));                    \
+    } while (0)
+
+#define FDB_LAUNCH_CHECK() FDB_CUDA(cudaGetLastError())
+
+#define FDB_NCCL(x)                                                                           \
+    do {                                                                                      \
+        ncclResult_t r__ = (x);                                                               \
+        if (r__ != ncclSuccess)                                                               \
+            ::fdb::fail(FDB_ERR_NCCL, std::string(#x) + ": " + ncclGetErrorString(r__));      \
+    } while (0)
+
+#define FDB_REQUIRE(cond, code, msg)          \
+    do {                                              \
+        if (!(cond)) ::fdb::fail((code), (msg));      \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// device memory
+// ---------------------------------------------------------------------------
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    explicit DevBuf(size_t count) { alloc(count); }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n) { o.p = nullptr; o.n = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        if (this != &o) { release(); p = o.p; n = o.n; o.p = nullptr; o.n = 0; }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void alloc(size_t count) {
+        release();
+        if (count) FDB_CUDA(cudaMalloc(&p, count * sizeof(T)));
+        n = count;
+    }
+    // Grow-only: keep the allocation if it is already large enough.
+    void ensure(size_t count) {
+        if (count > n) alloc(count);
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    size_t bytes() const { return n * sizeof(T); }
+};
+
+// ---------------------------------------------------------------------------
+// context: one device, one stream, optional communicator
+// ---------------------------------------------------------------------------
+struct Ctx {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+    std::mutex mu;  // serialises use of the context's scratch buffers
+};
+
+// Makes the context's device current for the lifetime of the guard.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) FDB_CUDA(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Times device stages on a stream with CUDA events.
+struct StageTimer {
+    cudaStream_t s;
+    bool on;
+    std::vector<cudaEvent_t> ev;
+    StageTimer(cudaStream_t s_, bool on_) : s(s_), on(on_) {}
+    ~StageTimer() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+    void mark() {
+        if (!on) return;
+        cudaEvent_t e;
+        FDB_CUDA(cudaEventCreate(&e));
+        FDB_CUDA(cudaEventRecord(e, s));
+        ev.push_back(e);
+    }
+    // Milliseconds between marks a and b (after the stream is synced).
+    double ms(size_t a, size_t b) const {
+        if (!on || b >= ev.size()) return 0.0;
+        float t = 0.f;
+        cudaEventElapsedTime(&t, ev[a], ev[b]);
+        return t;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// seeded draws (host): deterministic across processes and devices
+// ---------------------------------------------------------------------------
+uint64_t splitmix64(uint64_t& state);
+void sample_indices(uint64_t seed, size_t n, size_t take, uint32_t* out);
+void uniform_draws(uint64_t seed, size_t count, float* out);
+
+// ---------------------------------------------------------------------------
+// kernel launchers implemented in the .cu files
+// ---------------------------------------------------------------------------
+// distances.cu
+void launch_pairwise(cudaStream_t s, int metric, const float* a, const float* b, size_t n,
+                     int dim, float* out);
+void launch_gather_rows(cudaStream_t s, const float* x, size_t dim, const uint32_t* idx,
+                        size_t count, float* out);
+
+// kmeans.cu: k-means over a strided view of `n` rows; `nsub` independent
+// problems (PQ subspaces) share one launch, problem s reading columns
+// [s*dim, (s+1)*dim) of rows with stride `ld`.
+struct KMeansProblem {
+    const float* x;  // device rows
+    size_t n;
+    int dim;         // columns per problem
+    int ld;          // row stride in floats
+    int nsub;        // independent problems (1 for plain k-means)
+    int k;
+    int max_iters;
+};
+// cent: device [nsub][k][dim] initial centroids, updated in place.
+// iters_out: host [nsub].
+void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out);
+// k-means++ initialisation of one problem (nsub == 1, k <= 64).
+void kmeans_pp_init(Ctx& ctx, const float* x, size_t n, int dim, int k,
+                    const uint32_t* init_idx_host, const float* kpp_u_host, float* cent);
+void launch_assign(cudaStream_t s, const float* x, size_t n, int dim, int ld, const float* cent,
+                   int k, uint32_t* out);
+// Stable grouping of points by assignment: perm (point ids in group order)
+// and offsets[k+1].  Scratch comes from the caller's buffers.
+void group_by_assignment(Ctx& ctx, const uint32_t* assign, size_t n, int k, uint32_t* perm,
+                         uint64_t* offsets);
+
+// pq.cu
+void launch_pq_encode(cudaStream_t s, const float* x, size_t n, int dim, const float* cents,
+                      const uint32_t* assign, const float* cb, int m, const uint32_t* slot,
+                      uint8_t* codes);
+void launch_lut(cudaStream_t s, const float* cb, int m, int dim, const float* q, size_t nq,
+                float* lut);
+void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
+                  const uint32_t* init_idx_host, float* cb, int* iters_out);
+
+// engine.cu
+void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_iters,
+                    const uint32_t* init_idx, const float* kpp_u, uint64_t seed, float* cent,
+                    int* iters_run);
+void shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
+
+}  // namespace fdb
+
+struct fdb_ivfpq;
+struct fdb_bf;
+namespace fdb {
+void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, size_t n,
+                 const fdb_train_opts& o);
+void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_t* offsets,
+                const uint64_t* ids, const uint8_t* codes);
+void ivfpq_shard(fdb_ivfpq* h, int rank, int world);
+void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
+                      uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st);
+void bf_upload(fdb_bf* h);
+void bf_shard(fdb_bf* h, int rank, int world);
+void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
+                   float* d_dists, uint32_t* d_counts, fdb_stats* st);
+}  // namespace fdb
+
+// ---------------------------------------------------------------------------
+// the opaque handles
+// ---------------------------------------------------------------------------
+struct fdb_ctx {
+    fdb::Ctx c;
+};
+
+struct fdb_ivfpq {
+    fdb_ctx* ctx = nullptr;
+    size_t dim = 0, nlist = 0, m = 0;
+    int metric = 0;
+    std::atomic<size_t> nprobe{1};
+    size_t n_total = 0;  // vectors in the unsharded index
+    size_t n_local = 0;  // vectors whose lists live on this device
+    fdb::DevBuf<float> cents;     // [nlist][dim]
+    fdb::DevBuf<float> cb;        // [m][256][dim/m]
+    fdb::DevBuf<uint64_t> offs;   // [nlist+1], empty ranges for lists not held here
+    fdb::DevBuf<uint64_t> ids;    // [n_total] list-major
+    fdb::DevBuf<uint8_t> codes;   // [n_total][m] list-major
+    std::vector<uint64_t> h_offs_full;  // unsharded offsets (host)
+    std::vector<uint64_t> h_offs;       // offsets as held on this device
+    bool sharded = false;
+    int shard_world = 1, shard_rank = 0;
+    fdb::DevBuf<uint64_t> shard_be;     // [2][nlist] list begin / end when sharded
+    std::mutex mu;
+    // per-call scratch
+    fdb::DevBuf<float> s_q, s_coarse;
+    fdb::DevBuf<uint32_t> s_probe;
+    fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids;
+    fdb::DevBuf<float> s_dists;
+    fdb::DevBuf<uint32_t> s_counts;
+    fdb::DevBuf<unsigned long long> s_stat;
+};
+
+struct fdb_bf {
+    fdb_ctx* ctx = nullptr;
+    int metric = 0;
+    size_t dim = 0;
+    size_t n = 0;          // rows held on this device
+    size_t row0 = 0;       // global index of the first held row
+    std::vector<float> h_x;      // host copy kept only while rows are appended
+    std::vector<uint64_t> h_ids;
+    fdb::DevBuf<float> x;        // [n][dim]
+    fdb::DevBuf<uint64_t> ids;   // [n]
+    fdb::DevBuf<float> norms;    // [n] squared norms in AVX2 order (cosine)
+    bool dirty = true;
+    bool sharded = false;
+    int shard_world = 1;
+    std::mutex mu;
+    fdb::DevBuf<float> s_q, s_qnorm;
+    fdb::DevBuf<uint64_t> s_part, s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids;
+    fdb::DevBuf<float> s_dists;
+    fdb::DevBuf<uint32_t> s_counts;
+};

@@ -1,0 +1,53 @@
+// fdb_kernels.h -- launchers of the search kernels (host-callable).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace fdb {
+
+struct ScanParams {
+    const float* Q;
+    int nq;
+    int dim;
+    int m;
+    const float* cents;
+    const float* cb;
+    const uint64_t* offs;  // list l spans rows [offs[l], ends[l])
+    const uint64_t* ends;
+    const uint8_t* codes;
+    const uint32_t* probes;
+    int nprobe;
+    int k;
+    uint64_t* out_keys;
+    unsigned long long* stat;  // [0] lists scanned, [1] codes scanned (nullable)
+};
+
+// ivfpq_kernels.cu
+void launch_coarse_dist(cudaStream_t s, const float* Q, int nq, int dim, const float* cents,
+                        int nlist, float* D);
+void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
+                   uint32_t* probes);
+void launch_scan(cudaStream_t s, const ScanParams& a, int order);
+void launch_merge_lists(cudaStream_t s, const uint64_t* lists, int nlists, size_t list_stride,
+                        size_t nq, int k, uint64_t* out);
+void launch_lookup_gathered(cudaStream_t s, const uint64_t* keys, const uint64_t* gkeys,
+                            const uint64_t* gids, int world, size_t list_stride, size_t nq, int k,
+                            uint64_t* ids);
+void launch_keys_to_ids(cudaStream_t s, const uint64_t* keys, size_t total,
+                        const uint64_t* row_ids, uint64_t tag_base, uint64_t* ids);
+void launch_finalize(cudaStream_t s, const uint64_t* keys, const uint64_t* ids_in, size_t nq,
+                     int k, uint64_t* ids, float* dists, uint32_t* counts);
+
+// bf_kernels.cu
+void launch_row_norms(cudaStream_t s, const float* x, size_t n, int dim, float* norms);
+// Exact brute-force scan: partial top-k per (row chunk, query) into
+// part[nchunks][nq][k]; returns nchunks.
+int launch_bf_scan(cudaStream_t s, int metric, const float* Q, int nq, const float* qnorm,
+                   const float* X, size_t n, int dim, const float* xnorm, uint64_t tag_base,
+                   int k, int sm_count, uint64_t* part, size_t part_capacity);
+size_t bf_part_size(size_t n, int nq, int k, int sm_count);
+
+}  // namespace fdb

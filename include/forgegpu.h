@@ -1,0 +1,224 @@
+/*
+ * forgegpu.h -- C ABI of the B200 (sm_100a) engine for forge-db's
+ * nearest-neighbour search and training path.
+ *
+ * Every entry point replaces one method of the reference crate's Rust API
+ * (HueCodes/forge-db; file:line cited beside each declaration).  The ABI is
+ * plain C: opaque handles, caller-owned input and output buffers, sizes as
+ * size_t, and an int status (0 = OK, negative = error) whose codes map one to
+ * one onto ForgeDbError variants (src/error.rs:14-145).  Where the reference
+ * panics on bad input, the matching call returns an error code instead and
+ * fdb_last_error() holds the message.
+ *
+ * Distances keep the reference's meaning: IVF-PQ returns squared ADC sums
+ * (src/index/ivf_pq.rs:590-677, 850-1047); brute force returns the metric of
+ * src/distance/mod.rs:40-48 (Euclidean = sqrt(L2^2), DotProduct = -dot,
+ * Cosine = 1 - cos).  Result rows are sorted ascending; rows with fewer than
+ * k hits are padded with id UINT64_MAX and distance +inf, and the per-row
+ * count says how many are real.
+ *
+ * Threading: search calls on one handle are safe from several threads (a
+ * per-handle lock serialises GPU submission); fdb_ivfpq_set_nprobe is atomic
+ * and may race with searches, as in the reference (ivf_pq.rs:524-533).
+ */
+#ifndef FORGEGPU_H
+#define FORGEGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (ForgeDbError, src/error.rs:14-145) ------------------- */
+#define FDB_OK 0
+#define FDB_ERR_INVALID_ARG (-1)          /* InvalidParameter / panicking input */
+#define FDB_ERR_DIM_MISMATCH (-2)         /* DimensionMismatch */
+#define FDB_ERR_EMPTY_TRAINING_SET (-3)   /* EmptyTrainingSet */
+#define FDB_ERR_DIM_NOT_DIVISIBLE (-4)    /* DimensionNotDivisible */
+#define FDB_ERR_INSUFFICIENT_VECTORS (-5) /* InsufficientVectors */
+#define FDB_ERR_TIMEOUT (-6)              /* Timeout */
+#define FDB_ERR_CUDA (-7)                 /* device error (no reference analogue) */
+#define FDB_ERR_NCCL (-8)                 /* collective error (no reference analogue) */
+#define FDB_ERR_OOM (-9)                  /* MemoryLimitExceeded */
+#define FDB_ERR_EMPTY_VECTOR_SET (-10)    /* EmptyVectorSet */
+#define FDB_ERR_UNSUPPORTED (-11)         /* NotSupported */
+
+/* ---- DistanceMetric (src/distance/mod.rs:16-33) ------------------------- */
+#define FDB_METRIC_EUCLIDEAN 0
+#define FDB_METRIC_EUCLIDEAN_SQUARED 1
+#define FDB_METRIC_COSINE 2
+#define FDB_METRIC_DOT_PRODUCT 3
+#define FDB_METRIC_MANHATTAN 4
+
+/* Largest k (and nprobe for the warp selector) served by the search kernels. */
+#define FDB_MAX_K 256
+
+typedef struct fdb_ctx fdb_ctx;
+typedef struct fdb_ivfpq fdb_ivfpq;
+typedef struct fdb_bf fdb_bf;
+
+/* Per-call statistics (the counters of search_with_stats,
+ * src/index/ivf_pq.rs:1218-1349, plus device stage times). */
+typedef struct fdb_stats {
+    uint64_t lists_probed;   /* (query, list) pairs scanned on this device */
+    uint64_t codes_scanned;  /* PQ codes (or database rows) scored */
+    uint64_t bytes_scanned;  /* algorithmic bytes: codes_scanned * code bytes */
+    double coarse_ms;        /* coarse quantizer + probe selection */
+    double scan_ms;          /* LUT build + code scan + local top-k */
+    double merge_ms;         /* cross-device exchange + final merge */
+    double total_ms;         /* whole call, device clock */
+} fdb_stats;
+
+/* Training options for fdb_ivfpq_build.  Zero-initialise and set what you
+ * need.  The reference draws samples and initial centroids from an unseeded
+ * thread_rng (src/index/ivf_pq.rs:383-396, 422-446; src/kmeans.rs:52-64);
+ * here they are either injected (the index arrays) or drawn from `seed`. */
+typedef struct fdb_train_opts {
+    size_t ivf_sample;              /* 0 -> min(n, 30000)   (ivf_pq.rs:383) */
+    size_t pq_sample;               /* 0 -> min(n, 100000)  (ivf_pq.rs:422) */
+    size_t ivf_iters;               /* 0 -> 25              (ivf_pq.rs:398) */
+    size_t pq_iters;                /* 0 -> 25              (constants.rs:18) */
+    const uint32_t* ivf_sample_idx; /* [ivf_sample] or NULL */
+    const uint32_t* ivf_init_idx;   /* [nlist] or NULL */
+    const float* ivf_kpp_u;         /* [nlist] k-means++ draws (nlist <= 64) or NULL */
+    const uint32_t* pq_sample_idx;  /* [pq_sample] or NULL */
+    const uint32_t* pq_init_idx;    /* [m*256] or NULL */
+    uint64_t seed;                  /* used for every NULL draw above */
+} fdb_train_opts;
+
+/* ---- errors, version ---------------------------------------------------- */
+const char* fdb_last_error(void); /* thread-local message of the last failure */
+int fdb_version(void);            /* major*10000 + minor*100 + patch */
+
+/* ---- context: one device, one stream, optional NCCL communicator -------- */
+int fdb_ctx_create(int device, fdb_ctx** out);
+int fdb_ctx_free(fdb_ctx* ctx);
+/* The CUDA stream (cudaStream_t) every call of this context runs on. */
+int fdb_ctx_stream(fdb_ctx* ctx, void** stream_out);
+/* Multi-GPU: rank 0 creates the 128-byte NCCL unique id, every rank passes it
+ * to fdb_ctx_init_comm.  Searches on a sharded index then exchange local
+ * top-k lists over NVLink (ncclAllGather) and merge on every device. */
+int fdb_nccl_unique_id(void* id_out /* 128 bytes */);
+int fdb_ctx_init_comm(fdb_ctx* ctx, int rank, int world, const void* nccl_id);
+/* Host memory the device can copy from at full speed (cudaHostAlloc). */
+int fdb_host_alloc(size_t bytes, void** out);
+int fdb_host_free(void* p);
+
+/* ---- seeded draws (replacing thread_rng; deterministic across devices) -- */
+/* First `take` entries of a seeded Fisher-Yates shuffle of 0..n-1 (the
+ * `indices.shuffle(&mut rng); take(k)` idiom of src/kmeans.rs:53-61). */
+int fdb_sample_indices(uint64_t seed, size_t n, size_t take, uint32_t* out);
+/* `count` uniform draws in [0,1) on the 2^-23 grid of rand's f32 sampler. */
+int fdb_uniform_draws(uint64_t seed, size_t count, float* out);
+
+/* ---- distances (src/distance/mod.rs:40-48; simd.rs:293-517) ------------- */
+/* out[i] = metric(a[i], b[i]) for n row pairs of `dim` floats, computed on the
+ * device in the reference's AVX2 summation order (bit-exact). */
+int fdb_pairwise_distance(fdb_ctx* ctx, int metric, const float* a, const float* b, size_t n,
+                          size_t dim, float* out);
+
+/* ---- KMeans (src/kmeans.rs:18-193, 257-345) ----------------------------- */
+/* KMeans::new(k, max_iters).fit_raw(data, dim, n) (kmeans.rs:87-193; fit at
+ * :45-78 is the same algorithm).  init_idx[k]: the shuffled-prefix picks for
+ * k > 64, or for k <= 64 the first k-means++ pick (init_idx[0]) and the
+ * fallback picks; kpp_u[k]: the k-means++ uniform draws (k <= 64 only).  NULL
+ * arrays are drawn from `seed`.  assign_out[n] (nullable) receives each
+ * point's nearest final centroid (first minimum). */
+int fdb_kmeans_fit(fdb_ctx* ctx, const float* data, size_t n, size_t dim, size_t k,
+                   size_t max_iters, const uint32_t* init_idx, const float* kpp_u, uint64_t seed,
+                   float* centroids_out, uint32_t* assign_out, int* iters_run);
+/* Nearest-centroid assignment, first minimum wins (kmeans.rs:257-270;
+ * ivf_pq.rs:403-414). */
+int fdb_assign(fdb_ctx* ctx, const float* x, size_t n, const float* centroids, size_t k,
+               size_t dim, uint32_t* out);
+/* KMeans::find_nearest_centroids (kmeans.rs:334-345): the k nearest centroid
+ * ids of one query, ascending. */
+int fdb_find_nearest_centroids(fdb_ctx* ctx, const float* centroids, size_t kc, size_t dim,
+                               const float* query, size_t k, uint32_t* out);
+
+/* ---- ProductQuantizer (src/pq.rs:33-245) -------------------------------- */
+/* ProductQuantizer::try_train (pq.rs:55-95): codebooks_out[m][256][dim/m].
+ * init_idx[m*256] (NULL -> seed) are the per-subspace initial picks. */
+int fdb_pq_train(fdb_ctx* ctx, const float* x, size_t n, size_t dim, size_t m, size_t iters,
+                 const uint32_t* init_idx, uint64_t seed, float* codebooks_out, int* iters_out);
+/* ProductQuantizer::encode (pq.rs:114-139) over n vectors: codes_out[n][m]. */
+int fdb_pq_encode(fdb_ctx* ctx, const float* codebooks, size_t m, size_t dim, const float* x,
+                  size_t n, uint8_t* codes_out);
+/* build_lookup_table_flat (pq.rs:175-189) for nq queries: lut_out[nq][m*256]. */
+int fdb_pq_lookup_tables(fdb_ctx* ctx, const float* codebooks, size_t m, size_t dim,
+                         const float* queries, size_t nq, float* lut_out);
+
+/* ---- IVFPQIndex (src/index/ivf_pq.rs:343-1084) -------------------------- */
+/* IVFPQIndex::build (ivf_pq.rs:374-506).  `ids` may be NULL (ids 0..n-1).
+ * nprobe starts at 1 as in the reference. */
+int fdb_ivfpq_build(fdb_ctx* ctx, const float* x, const uint64_t* ids, size_t n, size_t dim,
+                    size_t nlist, size_t m, int metric, const fdb_train_opts* opts,
+                    fdb_ivfpq** out);
+/* An index from trained artefacts (the parity path: the same centroids,
+ * codebooks and lists as a reference-built index).  offsets[nlist+1] delimit
+ * each list's rows of ids[] and codes[][m] (list-major). */
+int fdb_ivfpq_from_trained(fdb_ctx* ctx, const float* centroids, const float* codebooks,
+                           size_t nlist, size_t m, size_t dim, const uint64_t* offsets,
+                           const uint64_t* ids, const uint8_t* codes, int metric,
+                           fdb_ivfpq** out);
+/* Copy the trained artefacts out (NULL pointers are skipped). */
+int fdb_ivfpq_export(fdb_ivfpq* h, float* centroids, float* codebooks, uint64_t* offsets,
+                     uint64_t* ids, uint8_t* codes);
+/* Keep only this rank's share of the inverted lists (greedy balance of
+ * list bytes over `world` devices); the other lists become empty here. */
+int fdb_ivfpq_shard(fdb_ivfpq* h, int rank, int world);
+/* The list -> device plan fdb_ivfpq_shard uses: owner[l] in [0, world) for
+ * each of nlist lists of the given sizes (host only; needs no device). */
+int fdb_ivfpq_shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
+/* set_nprobe (ivf_pq.rs:524-528): stores min(nprobe, nlist). */
+int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe);
+size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h);
+size_t fdb_ivfpq_len(const fdb_ivfpq* h);          /* vectors held on this device */
+size_t fdb_ivfpq_n_partitions(const fdb_ivfpq* h); /* nlist */
+size_t fdb_ivfpq_dim(const fdb_ivfpq* h);
+size_t fdb_ivfpq_n_subvectors(const fdb_ivfpq* h);  /* PQ subvectors m (pq.rs:37) */
+/* IVFPQIndex::search (ivf_pq.rs:590-677): one query, the single-query ADC
+ * order (pq.rs:218-245); n_out receives the number of results (<= k). */
+int fdb_ivfpq_search(fdb_ivfpq* h, const float* query, size_t k, uint64_t* ids, float* dists,
+                     size_t* n_out);
+/* IVFPQIndex::batch_search / batch_search_parallel (ivf_pq.rs:850-1084):
+ * host buffers; ids/dists are [nq][k], counts [nq] (nullable), stats
+ * nullable. */
+int fdb_ivfpq_batch_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                           uint64_t* ids, float* dists, uint32_t* counts, fdb_stats* stats);
+/* The same search on DEVICE buffers of this context's device, enqueued on the
+ * context stream; returns after the results are written (stream synced). */
+int fdb_ivfpq_batch_search_device(fdb_ivfpq* h, const float* d_queries, size_t nq, size_t k,
+                                  uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                                  fdb_stats* stats);
+int fdb_ivfpq_free(fdb_ivfpq* h);
+
+/* ---- BruteForceIndex (src/index/brute_force.rs:60-225) ------------------ */
+/* BruteForceIndex::new(metric) followed by add() of n rows
+ * (brute_force.rs:67-80).  `ids` may be NULL (ids 0..n-1). */
+int fdb_bf_create(fdb_ctx* ctx, int metric, const float* x, const uint64_t* ids, size_t n,
+                  size_t dim, fdb_bf** out);
+/* BruteForceIndex::add for n more rows (brute_force.rs:75-80). */
+int fdb_bf_add(fdb_bf* h, const float* x, const uint64_t* ids, size_t n, size_t dim);
+/* Keep only this rank's contiguous share of the rows. */
+int fdb_bf_shard(fdb_bf* h, int rank, int world);
+size_t fdb_bf_len(const fdb_bf* h);
+size_t fdb_bf_dimension(const fdb_bf* h); /* 0 when empty (brute_force.rs:92-99) */
+/* BruteForceIndex::search / search_parallel (brute_force.rs:162-214). */
+int fdb_bf_search(fdb_bf* h, const float* query, size_t k, uint64_t* ids, float* dists,
+                  size_t* n_out);
+/* BruteForceIndex::batch_search (brute_force.rs:220-225). */
+int fdb_bf_batch_search(fdb_bf* h, const float* queries, size_t nq, size_t k, uint64_t* ids,
+                        float* dists, uint32_t* counts, fdb_stats* stats);
+int fdb_bf_batch_search_device(fdb_bf* h, const float* d_queries, size_t nq, size_t k,
+                               uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                               fdb_stats* stats);
+int fdb_bf_free(fdb_bf* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORGEGPU_H */

@@ -1,0 +1,262 @@
+"""ctypes binding of the CPU oracle (fdb_oracle.cpp) -- TEST INFRASTRUCTURE ONLY.
+
+The oracle restates forge-db's search/training arithmetic on the CPU in the
+reference's exact summation order.  Only the tests, ``__graft_entry__.smoke``
+and the CPU-baseline leg of ``bench.py`` import this module; the CUDA engine
+never does.  See fdb_oracle.cpp for the reference file:line of each routine.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "build", "liboracle.so")
+_lib = None
+
+EUCLIDEAN, EUCLIDEAN_SQUARED, COSINE, DOT_PRODUCT, MANHATTAN = range(5)
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_sz = C.c_size_t
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (g++, AVX2+FMA, no contraction)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        sig = {
+            "orc_l2sq": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_dot": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_cosine": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_manhattan": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_metric": (C.c_float, [C.c_int, _f32p, _f32p, _sz]),
+            "orc_l2sq_scalar": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_dot_scalar": (C.c_float, [_f32p, _f32p, _sz]),
+            "orc_pairwise": (None, [C.c_int, _f32p, _f32p, _sz, _sz, _f32p]),
+            "orc_assign": (None, [_f32p, _sz, _f32p, _sz, _sz, _u32p, C.c_int]),
+            "orc_find_nearest_centroids": (None, [_f32p, _sz, _sz, _f32p, _sz, _u32p]),
+            "orc_kmeans_fit": (C.c_int, [_f32p, _sz, _sz, _sz, _sz, _u32p, _f32p, _f32p,
+                                         C.POINTER(C.c_int), C.c_int]),
+            "orc_pq_train": (C.c_int, [_f32p, _sz, _sz, _sz, _sz, _u32p, _f32p, _i32p, C.c_int]),
+            "orc_pq_encode": (None, [_f32p, _sz, _sz, _f32p, _sz, _u8p, C.c_int]),
+            "orc_lut_flat": (None, [_f32p, _sz, _sz, _f32p, _f32p]),
+            "orc_adc_fast": (C.c_float, [_f32p, _u8p, _sz]),
+            "orc_adc_lane8": (C.c_float, [_f32p, _u8p, _sz]),
+            "orc_adc_scalar": (C.c_float, [_f32p, _u8p, _sz]),
+            "orc_ivfpq_build": (C.c_int, [_f32p, _u64p, _sz, _sz, _sz, _sz, _u32p, _sz, _u32p,
+                                          _f32p, _u32p, _sz, _u32p, _sz, _sz, _f32p, _f32p,
+                                          _u32p, _u64p, _u64p, _u8p, C.c_int]),
+            "orc_ivfpq_search": (_sz, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p, _u8p, _sz,
+                                       _f32p, _sz, _u64p, _f32p]),
+            "orc_ivfpq_batch_search": (None, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p, _u8p,
+                                              _sz, _f32p, _sz, _sz, _sz, _u64p, _f32p, _u32p,
+                                              C.c_int]),
+            "orc_bf_batch_search": (None, [_f32p, _u64p, _sz, _sz, C.c_int, _f32p, _sz, _sz,
+                                           _u64p, _f32p, _u32p, C.c_int]),
+            "orc_max_threads": (C.c_int, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _threads(n):
+    return int(n) if n else lib().orc_max_threads()
+
+
+# --- distances --------------------------------------------------------------
+
+def l2sq(a, b):
+    a, b = _f32(a), _f32(b)
+    return lib().orc_l2sq(a, b, a.size)
+
+
+def dot(a, b):
+    a, b = _f32(a), _f32(b)
+    return lib().orc_dot(a, b, a.size)
+
+
+def cosine(a, b):
+    a, b = _f32(a), _f32(b)
+    return lib().orc_cosine(a, b, a.size)
+
+
+def metric(m, a, b):
+    a, b = _f32(a), _f32(b)
+    return lib().orc_metric(int(m), a, b, a.size)
+
+
+def pairwise(m, A, B):
+    A, B = _f32(A), _f32(B)
+    out = np.empty(A.shape[0], np.float32)
+    lib().orc_pairwise(int(m), A, B, A.shape[0], A.shape[1], out)
+    return out
+
+
+# --- k-means / PQ -------------------------------------------------------------
+
+def assign(X, cents, threads=0):
+    X, cents = _f32(X), _f32(cents)
+    out = np.empty(X.shape[0], np.uint32)
+    lib().orc_assign(X, X.shape[0], cents, cents.shape[0], X.shape[1], out, _threads(threads))
+    return out
+
+
+def find_nearest_centroids(cents, q, k):
+    cents, q = _f32(cents), _f32(q)
+    out = np.empty(min(k, cents.shape[0]), np.uint32)
+    lib().orc_find_nearest_centroids(cents, cents.shape[0], cents.shape[1], q, k, out)
+    return out
+
+
+def kmeans_fit(X, k, max_iters, init_idx, kpp_u=None, threads=0):
+    X = _f32(X)
+    n, dim = X.shape
+    init_idx = np.ascontiguousarray(init_idx, np.uint32)
+    kpp_u = np.zeros(k, np.float32) if kpp_u is None else _f32(kpp_u)
+    cents = np.zeros((k, dim), np.float32)
+    it = C.c_int(0)
+    rc = lib().orc_kmeans_fit(X, n, dim, k, max_iters, init_idx, kpp_u, cents, C.byref(it),
+                              _threads(threads))
+    if rc != 0:
+        raise ValueError(f"oracle kmeans_fit failed: {rc}")
+    return cents, it.value
+
+
+def pq_train(X, m, init_idx, iters=25, threads=0):
+    X = _f32(X)
+    n, dim = X.shape
+    init_idx = np.ascontiguousarray(init_idx, np.uint32)
+    cb = np.zeros((m, 256, dim // m), np.float32)
+    its = np.zeros(m, np.int32)
+    rc = lib().orc_pq_train(X, n, dim, m, iters, init_idx, cb, its, _threads(threads))
+    if rc != 0:
+        raise ValueError(f"oracle pq_train failed: {rc}")
+    return cb, its
+
+
+def pq_encode(cb, X, threads=0):
+    cb, X = _f32(cb), _f32(X)
+    m = cb.shape[0]
+    out = np.empty((X.shape[0], m), np.uint8)
+    lib().orc_pq_encode(cb, m, X.shape[1], X, X.shape[0], out, _threads(threads))
+    return out
+
+
+def lut_flat(cb, q):
+    cb, q = _f32(cb), _f32(q)
+    m = cb.shape[0]
+    out = np.empty(m * 256, np.float32)
+    lib().orc_lut_flat(cb, m, q.size, q, out)
+    return out
+
+
+def adc(order, lut, code):
+    lut = _f32(lut)
+    code = np.ascontiguousarray(code, np.uint8)
+    fn = {"fast": lib().orc_adc_fast, "lane8": lib().orc_adc_lane8,
+          "scalar": lib().orc_adc_scalar}[order]
+    return fn(lut, code, code.size)
+
+
+# --- indexes ------------------------------------------------------------------
+
+class OracleIVFPQ:
+    """Trained IVF-PQ artefacts in list-major layout plus the oracle searches."""
+
+    def __init__(self, centroids, codebooks, offsets, ids, codes):
+        self.centroids = _f32(centroids)
+        self.codebooks = _f32(codebooks)
+        self.offsets = np.ascontiguousarray(offsets, np.uint64)
+        self.ids = np.ascontiguousarray(ids, np.uint64)
+        self.codes = np.ascontiguousarray(codes, np.uint8)
+        self.nlist, self.dim = self.centroids.shape
+        self.m = self.codebooks.shape[0]
+        self.nprobe = 1
+
+    @classmethod
+    def build(cls, X, ids, nlist, m, ivf_sample_idx, ivf_init_idx, ivf_kpp_u, pq_sample_idx,
+              pq_init_idx, ivf_iters=25, pq_iters=25, threads=0):
+        X = _f32(X)
+        n, dim = X.shape
+        ids = np.ascontiguousarray(ids, np.uint64)
+        ivf_sample_idx = np.ascontiguousarray(ivf_sample_idx, np.uint32)
+        ivf_init_idx = np.ascontiguousarray(ivf_init_idx, np.uint32)
+        ivf_kpp_u = _f32(ivf_kpp_u if ivf_kpp_u is not None else np.zeros(nlist))
+        pq_sample_idx = np.ascontiguousarray(pq_sample_idx, np.uint32)
+        pq_init_idx = np.ascontiguousarray(pq_init_idx, np.uint32)
+        cents = np.zeros((nlist, dim), np.float32)
+        cb = np.zeros((m, 256, dim // m), np.float32)
+        assign = np.zeros(n, np.uint32)
+        offsets = np.zeros(nlist + 1, np.uint64)
+        lids = np.zeros(n, np.uint64)
+        codes = np.zeros((n, m), np.uint8)
+        rc = lib().orc_ivfpq_build(X, ids, n, dim, nlist, m, ivf_sample_idx, ivf_sample_idx.size,
+                                   ivf_init_idx, ivf_kpp_u, pq_sample_idx, pq_sample_idx.size,
+                                   pq_init_idx, ivf_iters, pq_iters, cents, cb, assign, offsets,
+                                   lids, codes, _threads(threads))
+        if rc != 0:
+            raise ValueError(f"oracle ivfpq_build failed: {rc}")
+        ix = cls(cents, cb, offsets, lids, codes)
+        ix.assign = assign
+        return ix
+
+    def set_nprobe(self, nprobe):
+        self.nprobe = min(int(nprobe), self.nlist)
+
+    def search(self, q, k):
+        q = _f32(q)
+        ids = np.empty(k, np.uint64)
+        d = np.empty(k, np.float32)
+        cnt = lib().orc_ivfpq_search(self.centroids, self.codebooks, self.nlist, self.m, self.dim,
+                                     self.offsets, self.ids, self.codes, self.nprobe, q, k, ids, d)
+        return ids[:cnt], d[:cnt]
+
+    def batch_search(self, Q, k, chunk=0, threads=0):
+        Q = _f32(Q)
+        nq = Q.shape[0]
+        ids = np.empty((nq, k), np.uint64)
+        d = np.empty((nq, k), np.float32)
+        counts = np.empty(nq, np.uint32)
+        lib().orc_ivfpq_batch_search(self.centroids, self.codebooks, self.nlist, self.m, self.dim,
+                                     self.offsets, self.ids, self.codes, self.nprobe, Q, nq, k,
+                                     chunk, ids, d, counts, _threads(threads))
+        return ids, d, counts
+
+
+def bf_batch_search(X, ids, metric_id, Q, k, threads=0):
+    X, Q = _f32(X), _f32(Q)
+    ids = np.ascontiguousarray(ids, np.uint64)
+    nq = Q.shape[0]
+    out_ids = np.empty((nq, k), np.uint64)
+    out_d = np.empty((nq, k), np.float32)
+    counts = np.empty(nq, np.uint32)
+    lib().orc_bf_batch_search(X, ids, X.shape[0], X.shape[1], int(metric_id), Q, nq, k, out_ids,
+                              out_d, counts, _threads(threads))
+    return out_ids, out_d, counts
+
+
+def max_threads():
+    return lib().orc_max_threads()

@@ -1,0 +1,68 @@
+"""The C ABI library loads and exports every symbol include/forgegpu.h
+declares; host-only entry points work without a GPU; device entry points
+fail cleanly (an error code, not a crash) where no GPU is visible."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "forgegpu.h")).read()
+    return sorted(set(re.findall(r"\b(fdb_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    import forgegpu as fg
+    L = fg.lib()
+    declared = header_symbols()
+    assert len(declared) >= 40
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(declared) == set(fg.exported_symbols())
+
+
+def test_version_and_error_string():
+    import forgegpu as fg
+    assert fg.lib().fdb_version() >= 100
+    assert isinstance(fg.lib().fdb_last_error(), bytes)
+
+
+def test_seeded_draws_deterministic():
+    import forgegpu as fg
+    a = fg.sample_indices(42, 1000, 100)
+    b = fg.sample_indices(42, 1000, 100)
+    assert np.array_equal(a, b)
+    assert len(set(a.tolist())) == 100 and a.max() < 1000
+    full = fg.sample_indices(7, 50, 50)
+    assert sorted(full.tolist()) == list(range(50))
+    u = fg.uniform_draws(1, 1000)
+    assert np.all((u >= 0) & (u < 1))
+    assert np.all(u * (1 << 23) == np.floor(u * (1 << 23)))  # on the 2^-23 grid
+    with pytest.raises(fg.ForgeGpuError):
+        fg.sample_indices(1, 10, 11)
+
+
+def test_shard_plan_covers_every_list_once():
+    import forgegpu as fg
+    rng = np.random.default_rng(0)
+    sizes = rng.integers(0, 5000, 1024).astype(np.uint64)
+    for world in (1, 2, 4, 8):
+        owner = fg.shard_plan(sizes, world)
+        assert owner.min() >= 0 and owner.max() < world
+        loads = np.bincount(owner, weights=sizes.astype(np.float64), minlength=world)
+        # greedy largest-first keeps every device within one list of the mean
+        assert loads.max() - loads.min() <= sizes.max()
+
+
+def test_no_gpu_fails_cleanly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    import forgegpu as fg
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.Context(0)
+    assert e.value.code in (-1, -7)

@@ -1,0 +1,243 @@
+"""Parity of the CUDA engine (through the C ABI) with the oracle.
+
+Integer and byte outputs (assignments, list layout, PQ codes) must be
+bit-exact; so must every distance the engine computes in the reference's
+summation order.  Top-k results use the port's contract (see parity.py).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from parity import assert_topk_match
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+U64MAX = np.iinfo(np.uint64).max
+
+
+@pytest.fixture(scope="module")
+def fg():
+    import forgegpu
+    return forgegpu
+
+
+@pytest.fixture(scope="module")
+def small():
+    return np.load(os.path.join(HERE, "golden", "ivfpq_small.npz"))
+
+
+# ---------------------------------------------------------------------------
+# distances
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dim", [1, 2, 7, 8, 9, 15, 16, 64, 96, 128, 256, 768])
+def test_pairwise_bit_exact(fg, ctx, orc, dim):
+    rng = np.random.default_rng(dim)
+    a = rng.standard_normal((257, dim)).astype(np.float32)
+    b = rng.standard_normal((257, dim)).astype(np.float32)
+    for metric in range(5):
+        got = fg.pairwise_distance(metric, a, b, ctx)
+        want = orc.pairwise(metric, a, b)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (metric, dim)
+
+
+def test_golden_known_values_on_gpu(fg, ctx):
+    a = np.zeros((1, 8), np.float32)
+    b = np.array([[3, 4, 0, 0, 0, 0, 0, 0]], np.float32)
+    assert fg.pairwise_distance(0, a, b, ctx)[0] == 5.0
+    assert fg.pairwise_distance(1, a, b, ctx)[0] == 25.0
+    assert fg.pairwise_distance(3, [[1, 0]], [[1, 0]], ctx)[0] == -1.0
+    assert fg.pairwise_distance(2, [[1, 0]], [[0, 1]], ctx)[0] == 1.0
+    assert fg.pairwise_distance(4, [[0, 0]], [[3, 4]], ctx)[0] == 7.0
+
+
+# ---------------------------------------------------------------------------
+# k-means, PQ
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("n,dim,k", [(5000, 128, 1024), (3000, 37, 100), (777, 8, 256)])
+def test_assign_bit_exact(fg, ctx, orc, n, dim, k):
+    rng = np.random.default_rng(n + dim)
+    X = rng.standard_normal((n, dim)).astype(np.float32)
+    C = rng.standard_normal((k, dim)).astype(np.float32)
+    C[5] = C[3]  # duplicate centroid: the first minimum must win
+    assert np.array_equal(fg.assign(X, C, ctx), orc.assign(X, C))
+
+
+@pytest.mark.parametrize("n,dim,k,iters", [(4000, 16, 100, 25), (2000, 32, 32, 25),
+                                           (3000, 8, 256, 10), (600, 5, 64, 30)])
+def test_kmeans_bit_exact(fg, ctx, orc, n, dim, k, iters):
+    rng = np.random.default_rng(k)
+    X = rng.random((n, dim), dtype=np.float32)
+    init = rng.permutation(n)[:k].astype(np.uint32)
+    u = (rng.integers(0, 1 << 23, k) / float(1 << 23)).astype(np.float32)
+    km = fg.KMeans(k, iters, ctx).fit(X, init_idx=init, kpp_u=u)
+    cents, it = orc.kmeans_fit(X, k, iters, init, u)
+    assert km.iters == it
+    assert np.array_equal(km.centroids.view(np.uint32), cents.view(np.uint32))
+    assert np.array_equal(km.assignments, orc.assign(X, cents))
+
+
+def test_kmeans_errors(fg, ctx):
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.KMeans(100, 5, ctx).fit(np.zeros((50, 4), np.float32))
+    assert e.value.kind == "InsufficientVectors"
+
+
+@pytest.mark.parametrize("n,dim,m", [(3000, 128, 16), (2000, 96, 48), (1500, 50, 10)])
+def test_pq_train_encode_lut_bit_exact(fg, ctx, orc, n, dim, m):
+    rng = np.random.default_rng(dim)
+    X = rng.standard_normal((n, dim)).astype(np.float32)
+    init = np.concatenate([rng.permutation(n)[:256] for _ in range(m)]).astype(np.uint32)
+    pq = fg.ProductQuantizer.train(X, m, init_idx=init, iters=25, ctx=ctx)
+    cb, its = orc.pq_train(X, m, init, 25)
+    assert np.array_equal(pq.iters, its)
+    assert np.array_equal(pq.codebooks.view(np.uint32), cb.view(np.uint32))
+    assert np.array_equal(pq.encode(X), orc.pq_encode(cb, X))
+    q = rng.standard_normal((3, dim)).astype(np.float32)
+    lut = pq.build_lookup_table_flat(q)
+    for i in range(3):
+        assert np.array_equal(lut[i], orc.lut_flat(cb, q[i]))
+
+
+def test_pq_errors(fg, ctx):
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.ProductQuantizer.train(np.zeros((300, 10), np.float32), 3, ctx=ctx)
+    assert e.value.kind == "DimensionNotDivisible"
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.ProductQuantizer.train(np.zeros((100, 16), np.float32), 4, ctx=ctx)
+    assert e.value.kind == "InsufficientVectors"
+
+
+# ---------------------------------------------------------------------------
+# IVF-PQ
+# ---------------------------------------------------------------------------
+def test_ivfpq_build_bit_exact(fg, ctx, small):
+    g = small
+    ix = fg.IVFPQIndex.build(g["X"], int(g["nlist"]), int(g["m"]), ids=g["ids"], ctx=ctx,
+                             ivf_sample_idx=g["ivf_sample_idx"], ivf_init_idx=g["ivf_init_idx"],
+                             ivf_kpp_u=g["ivf_kpp_u"], pq_sample_idx=g["pq_sample_idx"],
+                             pq_init_idx=g["pq_init_idx"])
+    cents, cb, offs, ids, codes = ix.export()
+    assert np.array_equal(cents.view(np.uint32), g["centroids"].view(np.uint32))
+    assert np.array_equal(cb.view(np.uint32), g["codebooks"].view(np.uint32))
+    assert np.array_equal(offs, g["offsets"])
+    assert np.array_equal(ids, g["list_ids"])
+    assert np.array_equal(codes, g["codes"])
+    assert len(ix) == g["X"].shape[0] and ix.n_partitions() == int(g["nlist"])
+
+
+def test_ivfpq_search_vs_golden(fg, ctx, small):
+    g = small
+    ix = fg.IVFPQIndex.from_trained(g["centroids"], g["codebooks"], g["offsets"], g["list_ids"],
+                                    g["codes"], ctx=ctx)
+    assert ix.nprobe() == 1
+    ix.set_nprobe(int(g["nprobe"]))
+    k = int(g["k"])
+    ids, d, cnt = ix.batch_search_arrays(g["Q"], k)
+    rate = assert_topk_match(ids, d, cnt, g["batch_ids"], g["batch_d"], g["batch_cnt"], "batch")
+    assert rate > 0.9
+    for q in range(len(g["Q"])):
+        res = ix.search(g["Q"][q], k)
+        c = int(g["single_cnt"][q])
+        si = np.array([r[0] for r in res], np.uint64)
+        sd = np.array([r[1] for r in res], np.float32)
+        assert_topk_match(si[None], sd[None], [len(res)], g["single_ids"][q:q + 1, :c],
+                          g["single_d"][q:q + 1, :c], [c], f"single {q}")
+
+
+def _oracle_index(orc, fgix):
+    cents, cb, offs, ids, codes = fgix.export()
+    return orc.OracleIVFPQ(cents, cb, offs, ids, codes)
+
+
+@pytest.mark.parametrize("nprobe,k", [(1, 10), (8, 10), (32, 1), (32, 100), (64, 256),
+                                      (300, 20), (0, 10)])
+def test_ivfpq_config_a_parity(fg, ctx, orc, nprobe, k):
+    """Config A shapes (10k x 128 U[0,1), nlist 32, M 8) at many nprobe / k."""
+    rng = np.random.default_rng(1)
+    X = rng.random((10000, 128), dtype=np.float32)
+    Q = np.random.default_rng(2).random((300, 128), dtype=np.float32)
+    ix = fg.IVFPQIndex.build(X, 32, 8, ctx=ctx, seed=123)
+    ox = _oracle_index(orc, ix)
+    ix.set_nprobe(nprobe)
+    ox.set_nprobe(nprobe)
+    assert ix.nprobe() == min(nprobe, 32)
+    ids, d, cnt = ix.batch_search_arrays(Q, k)
+    oi, od, oc = ox.batch_search(Q, k)
+    assert_topk_match(ids, d, cnt, oi, od, oc, f"batch nprobe={nprobe} k={k}")
+    for q in range(0, 300, 37):
+        res = ix.search(Q[q], k)
+        si, sd = ox.search(Q[q], k)
+        assert len(res) == len(si)
+        assert_topk_match(np.array([[r[0] for r in res]], np.uint64),
+                          np.array([[r[1] for r in res]], np.float32), [len(res)],
+                          si[None], sd[None], [len(si)], f"single q={q}")
+
+
+def test_ivfpq_ragged_lists_and_short_results(fg, ctx, orc):
+    """Lists shorter than k, empty lists and M not a multiple of 8."""
+    rng = np.random.default_rng(9)
+    X = rng.random((600, 40), dtype=np.float32)
+    ix = fg.IVFPQIndex.build(X, 64, 10, ctx=ctx, seed=5)  # M=10 -> generic code path
+    ox = _oracle_index(orc, ix)
+    ix.set_nprobe(2)
+    ox.set_nprobe(2)
+    Q = rng.random((50, 40), dtype=np.float32)
+    ids, d, cnt = ix.batch_search_arrays(Q, 50)
+    oi, od, oc = ox.batch_search(Q, 50)
+    assert_topk_match(ids, d, cnt, oi, od, oc, "ragged")
+    assert (cnt < 50).any()  # some queries see fewer than k codes
+
+
+def test_ivfpq_edge_cases(fg, ctx, small):
+    g = small
+    ix = fg.IVFPQIndex.from_trained(g["centroids"], g["codebooks"], g["offsets"], g["list_ids"],
+                                    g["codes"], ctx=ctx)
+    assert ix.batch_search(np.zeros((0, g["X"].shape[1]), np.float32), 10) == []
+    ids, d, cnt = ix.batch_search_arrays(g["Q"][:3], 0)
+    assert ids.shape == (3, 0)
+    ix.set_nprobe(100)
+    assert ix.nprobe() == int(g["nlist"])
+    with pytest.raises(fg.ForgeGpuError):
+        ix.batch_search(g["Q"][:2], 257)  # above FDB_MAX_K
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.IVFPQIndex.build(np.zeros((300, 30), np.float32), 4, 7, ctx=ctx)
+    assert e.value.kind == "DimensionNotDivisible"
+    with pytest.raises(fg.ForgeGpuError) as e:
+        fg.IVFPQIndex.build(np.zeros((100, 32), np.float32), 4, 8, ctx=ctx)
+    assert e.value.kind == "InsufficientVectors"
+
+
+# ---------------------------------------------------------------------------
+# brute force
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("metric", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("n,dim,k", [(20000, 128, 100), (5000, 13, 10), (300, 64, 256)])
+def test_bf_parity(fg, ctx, orc, metric, n, dim, k):
+    rng = np.random.default_rng(n + metric)
+    X = rng.standard_normal((n, dim)).astype(np.float32)
+    Q = rng.standard_normal((64, dim)).astype(np.float32)
+    ids = rng.permutation(n * 3)[:n].astype(np.uint64)
+    bf = fg.BruteForceIndex(metric, ctx).add(X, ids)
+    gi, gd, gc = bf.batch_search_arrays(Q, k)
+    oi, od, oc = orc.bf_batch_search(X, ids, metric, Q, k)
+    assert_topk_match(gi, gd, gc, oi, od, oc, f"bf metric={metric}")
+    res = bf.search(Q[0], k)
+    assert [r[0] for r in res][:5] == gi[0, :5].tolist()
+
+
+def test_bf_self_query_and_edges(fg, ctx):
+    rng = np.random.default_rng(4)
+    X = rng.standard_normal((1000, 32)).astype(np.float32)
+    bf = fg.BruteForceIndex(1, ctx)
+    assert bf.dimension() == 0 and bf.search(X[0], 5) == []
+    bf.add(X[:500]).add(X[500:])
+    assert len(bf) == 1000 and bf.dimension() == 32
+    ids, d, cnt = bf.batch_search_arrays(X[:50], 1)
+    assert np.array_equal(ids[:, 0], np.arange(50, dtype=np.uint64))
+    assert np.all(d[:, 0] == 0)
+    with pytest.raises(fg.ForgeGpuError):
+        bf.search(X[0], 0)  # the reference panics on k == 0 with rows present
+    with pytest.raises(fg.ForgeGpuError) as e:
+        bf.add(np.zeros((1, 31), np.float32))
+    assert e.value.kind == "DimensionMismatch"
