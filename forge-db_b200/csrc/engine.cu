@@ -10,6 +10,7 @@
 // an index whose lists are sharded over several devices, an ncclAllGather of
 // the local top-k lists followed by a merge on every device.
 #include <algorithm>
+#include <cmath>
 #include <numeric>
 
 #include "fdb_device.cuh"
@@ -18,6 +19,7 @@
 
 namespace fdb {
 
+static void ivfpq_prepare_tables(fdb_ivfpq* h);
 void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
                   const uint32_t* init_idx_host, float* cb, int* iters_out);
 
@@ -196,6 +198,53 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
     FDB_CUDA(cudaStreamSynchronize(s));
     h->h_offs = h->h_offs_full;
     h->n_total = h->n_local = n;
+    ivfpq_prepare_tables(h);
+}
+
+// Table mode needs, per index: the per-list table btab and the bound terms
+// cmax_s = max_l ||c_ls||, bmax_s = max_j ||b_sj|| (rounded up).  Built for
+// subvectors of 8+ floats, where an exact LUT entry costs 8+ FMAs.
+static void ivfpq_prepare_tables(fdb_ivfpq* h) {
+    const size_t nlist = h->nlist, dim = h->dim, m = h->m, sub = dim / m;
+    h->btab.release();
+    h->cmax.release();
+    h->bmax.release();
+    if (sub < 8) return;
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    h->btab.alloc(nlist * m * KSUB);
+    launch_ivf_tables(s, h->cents.p, h->cb.p, (int)nlist, (int)m, (int)dim, h->btab.p);
+    std::vector<float> cents(nlist * dim), cb(m * KSUB * sub);
+    FDB_CUDA(cudaMemcpyAsync(cents.data(), h->cents.p, cents.size() * 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaMemcpyAsync(cb.data(), h->cb.p, cb.size() * 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    std::vector<float> cmax(m, 0.0f), bmax(m, 0.0f);
+    for (size_t q = 0; q < m; ++q) {
+        double cm = 0.0, bm = 0.0;
+        for (size_t l = 0; l < nlist; ++l) {
+            double t = 0.0;
+            for (size_t i = 0; i < sub; ++i) {
+                double x = cents[l * dim + q * sub + i];
+                t += x * x;
+            }
+            cm = std::max(cm, std::sqrt(t));
+        }
+        for (size_t j = 0; j < (size_t)KSUB; ++j) {
+            double t = 0.0;
+            for (size_t i = 0; i < sub; ++i) {
+                double x = cb[(q * KSUB + j) * sub + i];
+                t += x * x;
+            }
+            bm = std::max(bm, std::sqrt(t));
+        }
+        cmax[q] = (float)(cm * (1.0 + 1e-6));
+        bmax[q] = (float)(bm * (1.0 + 1e-6));
+    }
+    h->cmax.alloc(m);
+    h->bmax.alloc(m);
+    FDB_CUDA(cudaMemcpyAsync(h->cmax.p, cmax.data(), m * 4, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(h->bmax.p, bmax.data(), m * 4, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
 }
 
 void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_t* offsets,
@@ -224,6 +273,7 @@ void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_
     h->h_offs_full.assign(offsets, offsets + nlist + 1);
     h->h_offs = h->h_offs_full;
     h->n_total = h->n_local = n;
+    ivfpq_prepare_tables(h);
 }
 
 // Greedy balance of list bytes: largest list first, onto the least-loaded
@@ -319,7 +369,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
     if (k == 0) return;
     h->s_keys.ensure(per);
     h->s_ids.ensure(per);
-    if (take == 0) {
+    if (take == 0) {  // marks 1..3 still taken so stage times line up
         // search() with nprobe == 0 probes nothing (ivf_pq.rs:548-552)
         FDB_CUDA(cudaMemsetAsync(h->s_keys.p, 0xff, per * 8, s));
     } else {
@@ -330,6 +380,11 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         tm.mark();
         h->s_stat.ensure(2);
         FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 16, s));
+        // Table mode: approximate scan into a shortlist of kp keys, then
+        // exact rescoring + certification; failures are re-scanned exactly.
+        const bool tables = h->btab.p && h->scan_mode != FDB_SCAN_EXACT && k <= 128;
+        const size_t kp = tables ? std::min<size_t>(FDB_MAX_K, std::max<size_t>(32, 2 * k)) : k;
+        if (tables) h->s_approx.ensure(nq * kp);
         ScanParams a{};
         a.Q = dQ;
         a.nq = (int)nq;
@@ -342,10 +397,49 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         a.codes = h->codes.p;
         a.probes = h->s_probe.p;
         a.nprobe = (int)take;
-        a.k = (int)k;
-        a.out_keys = h->s_keys.p;
+        a.k = (int)kp;
+        a.out_keys = tables ? h->s_approx.p : h->s_keys.p;
         a.stat = h->s_stat.p;
+        a.btab = tables ? h->btab.p : nullptr;
         launch_scan(s, a, order);
+        tm.mark();
+        if (tables) {
+            h->s_flags.ensure(nq + 1);
+            FDB_CUDA(cudaMemsetAsync(h->s_flags.p, 0, 4, s));
+            RescoreParams r{};
+            r.Q = dQ;
+            r.nq = (int)nq;
+            r.dim = (int)h->dim;
+            r.m = (int)h->m;
+            r.cents = h->cents.p;
+            r.cb = h->cb.p;
+            r.offs_full = h->offs.p;
+            r.nlist = nlist;
+            r.codes = h->codes.p;
+            r.approx = h->s_approx.p;
+            r.kp = (int)kp;
+            r.k = (int)k;
+            r.out_keys = h->s_keys.p;
+            r.cmax = h->cmax.p;
+            r.bmax = h->bmax.p;
+            r.flag_count = h->s_flags.p;
+            r.flag_list = h->s_flags.p + 1;
+            launch_rescore(s, r, order);
+            uint32_t nflag = 0;
+            FDB_CUDA(cudaMemcpyAsync(&nflag, h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaStreamSynchronize(s));
+            if (nflag > 0) {
+                ScanParams e = a;
+                e.nq = (int)nflag;
+                e.qidx = h->s_flags.p + 1;
+                e.k = (int)k;
+                e.out_keys = h->s_keys.p;
+                e.stat = nullptr;
+                e.btab = nullptr;
+                launch_scan(s, e, order);
+            }
+            if (st) st->exact_rescans = nflag;
+        }
     }
     tm.mark();
     launch_keys_to_ids(s, h->s_keys.p, per, h->ids.p, 0, h->s_ids.p);
@@ -371,7 +465,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         if (take > 0) {
             st->coarse_ms = tm.ms(0, 1);
             st->scan_ms = tm.ms(1, 2);
-            st->merge_ms = tm.ms(2, 3);
+            st->rescore_ms = tm.ms(2, 3);
+            st->merge_ms = tm.ms(3, 4);
         }
         st->total_ms = tm.ms(0, last);
     }

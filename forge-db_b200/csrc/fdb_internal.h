@@ -233,13 +233,17 @@ struct fdb_ivfpq {
     bool sharded = false;
     int shard_world = 1, shard_rank = 0;
     fdb::DevBuf<uint64_t> shard_be;     // [2][nlist] list begin / end when sharded
+    // table mode (subvectors of 8+ floats): per-list tables and error-bound terms
+    int scan_mode = FDB_SCAN_AUTO;
+    fdb::DevBuf<float> btab;            // [nlist][m][256]
+    fdb::DevBuf<float> cmax, bmax;      // [m]
     std::mutex mu;
     // per-call scratch
     fdb::DevBuf<float> s_q, s_coarse;
     fdb::DevBuf<uint32_t> s_probe;
-    fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids;
+    fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids, s_approx;
     fdb::DevBuf<float> s_dists;
-    fdb::DevBuf<uint32_t> s_counts;
+    fdb::DevBuf<uint32_t> s_counts, s_flags;
     fdb::DevBuf<unsigned long long> s_stat;
 };
 

@@ -23,6 +23,28 @@ struct ScanParams {
     int k;
     uint64_t* out_keys;
     unsigned long long* stat;  // [0] lists scanned, [1] codes scanned (nullable)
+    const uint32_t* qidx;      // nullable: block i scans query qidx[i] (and writes its row)
+    const float* btab;         // non-null selects table mode: [nlist][m][256]
+};
+
+struct RescoreParams {
+    const float* Q;
+    int nq;
+    int dim;
+    int m;
+    const float* cents;
+    const float* cb;
+    const uint64_t* offs_full;  // [nlist+1] offsets of the unsharded layout
+    int nlist;
+    const uint8_t* codes;
+    const uint64_t* approx;  // [nq][kp] table-mode shortlist, ascending
+    int kp;
+    int k;
+    uint64_t* out_keys;       // [nq][k] exact keys
+    const float* cmax;        // [m] max_l ||c_ls||
+    const float* bmax;        // [m] max_j ||b_sj||
+    uint32_t* flag_count;     // queries that failed certification
+    uint32_t* flag_list;
 };
 
 // ivfpq_kernels.cu
@@ -31,6 +53,9 @@ void launch_coarse_dist(cudaStream_t s, const float* Q, int nq, int dim, const f
 void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
                    uint32_t* probes);
 void launch_scan(cudaStream_t s, const ScanParams& a, int order);
+void launch_rescore(cudaStream_t s, const RescoreParams& r, int order);
+void launch_ivf_tables(cudaStream_t s, const float* cents, const float* cb, int nlist, int m,
+                       int dim, float* btab);
 void launch_merge_lists(cudaStream_t s, const uint64_t* lists, int nlists, size_t list_stride,
                         size_t nq, int k, uint64_t* out);
 void launch_lookup_gathered(cudaStream_t s, const uint64_t* keys, const uint64_t* gkeys,

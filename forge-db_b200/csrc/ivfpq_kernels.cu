@@ -266,21 +266,51 @@ __device__ __forceinline__ float adc_code(const float* __restrict__ lut,
     }
 }
 
-template <int P, int ORDER, int MB>
+// Shared memory of one scan block:
+//   lut   [m*256]  f32   the (query, list) table
+//   ctab  [m*256]  f32   table mode only: <q_s, b_sj> for this block's query
+//   resid [dim_pad] f32  exact mode: q - c_l
+//   aterm [m_pad]  f32   table mode: ||q_s - c_ls||^2
+//   wbuf  [warps*64] u64 WarpTopK candidate buffers
+//   lists [warps*k]  u64 per-warp results for the end-of-query merge
+//
+// TABLES == false: every LUT entry is L2^2(q_s - c_ls, b_sj) in the AVX2
+//   order -- the reference's value, bit for bit.
+// TABLES == true: LUT entry = ||q_s - c_ls||^2 + (||b_sj||^2 + 2<c_ls,b_sj>)
+//   - 2<q_s,b_sj>, the middle term precomputed per list at build time and the
+//   last computed once per query: the same real number with different
+//   rounding.  The block then keeps a shortlist of a.k >= 2k candidates that
+//   rescore_kernel re-ranks with exact distances and certifies.
+template <int P, int ORDER, int MB, bool TABLES>
 __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int m = MB > 0 ? MB : a.m;
-    float* lut = reinterpret_cast<float*>(smem);
-    float* resid = lut + m * KSUB;
+    const int L = m * KSUB;
     const int dim_pad = (a.dim + 3) & ~3;
-    uint64_t* wbuf = reinterpret_cast<uint64_t*>(resid + dim_pad);
+    const int m_pad = (m + 3) & ~3;
+    float* lut = reinterpret_cast<float*>(smem);
+    float* ctab = lut + L;
+    float* resid = ctab + (TABLES ? L : 0);
+    float* aterm = resid + dim_pad;
+    uint64_t* wbuf = reinterpret_cast<uint64_t*>(aterm + m_pad);
     uint64_t* lists = wbuf + SCAN_WARPS * 64;
-    const int warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = a.dim / m;
-    for (int q = blockIdx.x; q < a.nq; q += gridDim.x) {
+    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+        const int q = a.qidx ? (int)a.qidx[qi] : qi;
+        const float* qv = a.Q + (size_t)q * a.dim;
+        if (TABLES) {
+            __syncthreads();  // the previous query's ctab is no longer read
+            for (int e = threadIdx.x; e < L; e += SCAN_THREADS) {
+                const float* qs = qv + (e >> 8) * sub;
+                const float* b = a.cb + (size_t)e * sub;
+                float t = 0.0f;
+                for (int i = 0; i < sub; ++i) t = __fmaf_rn(__ldg(qs + i), __ldg(b + i), t);
+                ctab[e] = t;
+            }
+        }
         WarpTopK<P> tk;
         tk.init(a.k, wbuf + warp * 64);
-        const float* qv = a.Q + (size_t)q * a.dim;
         unsigned long long nscan = 0, nl = 0;
         for (int p = 0; p < a.nprobe; ++p) {
             const uint32_t l = a.probes[(size_t)q * a.nprobe + p];
@@ -288,23 +318,53 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
             if (beg == end) continue;  // empty, or held by another device
             __syncthreads();           // previous list's LUT no longer in use
             const float* cl = a.cents + (size_t)l * a.dim;
-            for (int d = threadIdx.x; d < a.dim; d += SCAN_THREADS)
-                resid[d] = __fsub_rn(qv[d], cl[d]);  // q - c (ivf_pq.rs:926-938)
-            __syncthreads();
-            for (int e = threadIdx.x; e < m * KSUB; e += SCAN_THREADS) {
-                const int s = e >> 8;
-                lut[e] = lut_entry(resid + s * sub, a.cb + (size_t)e * sub, sub);
+            if (TABLES) {
+                if (threadIdx.x < m) {
+                    const int s = threadIdx.x;
+                    float t = 0.0f;
+                    for (int i = 0; i < sub; ++i) {
+                        float d = __fsub_rn(__ldg(qv + s * sub + i), __ldg(cl + s * sub + i));
+                        t = __fmaf_rn(d, d, t);
+                    }
+                    aterm[s] = t;
+                }
+                __syncthreads();
+                const float4* B4 = reinterpret_cast<const float4*>(a.btab + (size_t)l * L);
+                const float4* C4 = reinterpret_cast<const float4*>(ctab);
+                float4* T4 = reinterpret_cast<float4*>(lut);
+                for (int e4 = threadIdx.x; e4 < L / 4; e4 += SCAN_THREADS) {
+                    const float A = aterm[e4 >> 6];
+                    const float4 b = __ldg(B4 + e4);
+                    const float4 c = C4[e4];
+                    float4 r;
+                    r.x = __fmaf_rn(-2.0f, c.x, __fadd_rn(A, b.x));
+                    r.y = __fmaf_rn(-2.0f, c.y, __fadd_rn(A, b.y));
+                    r.z = __fmaf_rn(-2.0f, c.z, __fadd_rn(A, b.z));
+                    r.w = __fmaf_rn(-2.0f, c.w, __fadd_rn(A, b.w));
+                    T4[e4] = r;
+                }
+            } else {
+                for (int d = threadIdx.x; d < a.dim; d += SCAN_THREADS)
+                    resid[d] = __fsub_rn(qv[d], cl[d]);  // q - c (ivf_pq.rs:926-938)
+                __syncthreads();
+                for (int e = threadIdx.x; e < L; e += SCAN_THREADS)
+                    lut[e] = lut_entry(resid + (e >> 8) * sub, a.cb + (size_t)e * sub, sub);
             }
             __syncthreads();
-            for (uint64_t base = beg + (uint64_t)warp * 32; base < end;
-                 base += (uint64_t)SCAN_WARPS * 32) {
-                const uint64_t pos = base + (threadIdx.x & 31);
-                const bool valid = pos < end;
-                float dist = 0.0f;
-                if (valid) dist = adc_code<ORDER, MB>(lut, a.codes + pos * m, m);
-                tk.add(make_key(dist, (uint32_t)pos), valid);
+            // Scan: each lane scores two codes per step; out-of-range lanes
+            // read the list's first code (always present) and are masked.
+            const uint32_t len = (uint32_t)(end - beg);
+            const uint8_t* lc = a.codes + beg * (uint64_t)m;
+            const uint32_t tag0 = (uint32_t)beg;
+            for (uint32_t b = (uint32_t)warp * 64u; b < len; b += SCAN_WARPS * 64u) {
+                const uint32_t i0 = b + lane, i1 = i0 + 32u;
+                const bool v0 = i0 < len, v1 = i1 < len;
+                const float d0 = adc_code<ORDER, MB>(lut, lc + (size_t)(v0 ? i0 : 0u) * m, m);
+                const float d1 = adc_code<ORDER, MB>(lut, lc + (size_t)(v1 ? i1 : 0u) * m, m);
+                tk.add(make_key(d0, tag0 + i0), v0);
+                tk.add(make_key(d1, tag0 + i1), v1);
             }
-            nscan += end - beg;
+            nscan += len;
             ++nl;
         }
         tk.flush();
@@ -322,14 +382,16 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
     }
 }
 
-template <int P, int ORDER, int MB>
+template <int P, int ORDER, int MB, bool TABLES>
 static void launch_scan_t(cudaStream_t s, const ScanParams& a, int grid) {
     const int m = a.m;
-    size_t smem = (size_t)m * KSUB * sizeof(float) + (size_t)((a.dim + 3) & ~3) * sizeof(float) +
+    size_t smem = (size_t)m * KSUB * sizeof(float) * (TABLES ? 2 : 1) +
+                  (size_t)((a.dim + 3) & ~3) * sizeof(float) +
+                  (size_t)((m + 3) & ~3) * sizeof(float) +
                   (size_t)SCAN_WARPS * 64 * sizeof(uint64_t) +
                   (size_t)SCAN_WARPS * a.k * sizeof(uint64_t);
     FDB_REQUIRE(smem <= 227 * 1024, FDB_ERR_UNSUPPORTED, "LUT does not fit in shared memory");
-    auto kern = scan_kernel<P, ORDER, MB>;
+    auto kern = scan_kernel<P, ORDER, MB, TABLES>;
     if (smem > 48 * 1024)
         FDB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
@@ -337,31 +399,181 @@ static void launch_scan_t(cudaStream_t s, const ScanParams& a, int grid) {
     FDB_LAUNCH_CHECK();
 }
 
-template <int P, int ORDER>
+template <int P, int ORDER, bool TABLES>
 static void launch_scan_m(cudaStream_t s, const ScanParams& a, int grid) {
     switch (a.m) {
-        case 8: launch_scan_t<P, ORDER, 8>(s, a, grid); break;
-        case 16: launch_scan_t<P, ORDER, 16>(s, a, grid); break;
-        case 32: launch_scan_t<P, ORDER, 32>(s, a, grid); break;
-        case 48: launch_scan_t<P, ORDER, 48>(s, a, grid); break;
-        default: launch_scan_t<P, ORDER, 0>(s, a, grid); break;
+        case 8: launch_scan_t<P, ORDER, 8, TABLES>(s, a, grid); break;
+        case 16: launch_scan_t<P, ORDER, 16, TABLES>(s, a, grid); break;
+        case 32: launch_scan_t<P, ORDER, 32, TABLES>(s, a, grid); break;
+        case 48: launch_scan_t<P, ORDER, 48, TABLES>(s, a, grid); break;
+        default: launch_scan_t<P, ORDER, 0, TABLES>(s, a, grid); break;
     }
 }
 
-template <int ORDER>
+template <int ORDER, bool TABLES>
 static void launch_scan_o(cudaStream_t s, const ScanParams& a, int grid) {
-    if (a.k <= 32) launch_scan_m<1, ORDER>(s, a, grid);
-    else if (a.k <= 64) launch_scan_m<2, ORDER>(s, a, grid);
-    else if (a.k <= 128) launch_scan_m<4, ORDER>(s, a, grid);
-    else launch_scan_m<8, ORDER>(s, a, grid);
+    if (a.k <= 32) launch_scan_m<1, ORDER, TABLES>(s, a, grid);
+    else if (a.k <= 64) launch_scan_m<2, ORDER, TABLES>(s, a, grid);
+    else if (a.k <= 128) launch_scan_m<4, ORDER, TABLES>(s, a, grid);
+    else launch_scan_m<8, ORDER, TABLES>(s, a, grid);
 }
 
 void launch_scan(cudaStream_t s, const ScanParams& a, int order) {
     if (a.nq == 0) return;
     FDB_REQUIRE(a.k >= 1 && a.k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED, "k out of range");
+    const bool tables = a.btab != nullptr;
     const int grid = a.nq;
-    if (order == ORDER_LANE8) launch_scan_o<ORDER_LANE8>(s, a, grid);
-    else launch_scan_o<ORDER_FAST4>(s, a, grid);
+    if (order == ORDER_LANE8) {
+        if (tables) launch_scan_o<ORDER_LANE8, true>(s, a, grid);
+        else launch_scan_o<ORDER_LANE8, false>(s, a, grid);
+    } else {
+        if (tables) launch_scan_o<ORDER_FAST4, true>(s, a, grid);
+        else launch_scan_o<ORDER_FAST4, false>(s, a, grid);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// exact rescoring and certification of a table-mode shortlist
+// ---------------------------------------------------------------------------
+// Exact ADC of one code: every LUT entry recomputed as L2^2(fl(q - c) - b)
+// in the AVX2 order and summed in the requested order -- the same
+// operations, in the same order, as the exact-mode scan.
+template <int ORDER>
+__device__ __forceinline__ float exact_adc(const float* __restrict__ q,
+                                           const float* __restrict__ c,
+                                           const float* __restrict__ cb,
+                                           const uint8_t* __restrict__ code, int m, int sub) {
+    auto entry = [&](int s) -> float {
+        const float* b = cb + ((size_t)s * KSUB + code[s]) * sub;
+        const float* qs = q + s * sub;
+        const float* cs = c + s * sub;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        int i = 0;
+        for (; i + 8 <= sub; i += 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float d = __fsub_rn(__fsub_rn(__ldg(qs + i + j), __ldg(cs + i + j)), __ldg(b + i + j));
+                acc[j] = __fmaf_rn(d, d, acc[j]);
+            }
+        }
+        float t = lane_sum(acc);
+        for (; i < sub; ++i) {
+            float d = __fsub_rn(__fsub_rn(__ldg(qs + i), __ldg(cs + i)), __ldg(b + i));
+            t = __fadd_rn(t, __fmul_rn(d, d));
+        }
+        return t;
+    };
+    return adc_order<ORDER>(entry, m);
+}
+
+constexpr int RESCORE_WARPS = 8;
+
+// One warp per query.  The shortlist (a.kp approximate keys, ascending) is
+// rescored exactly and the k best exact keys are kept.  Certification: every
+// approximate distance is within E of the exact one (E is a worst-case bound
+// of the rounding of both computations), so if (exact k-th distance) + E is
+// below the approximate distance of the last shortlisted candidate, no code
+// outside the shortlist can belong to the exact top-k.  Queries that fail the
+// test are listed for an exact re-scan.
+template <int P, int ORDER>
+__global__ void __launch_bounds__(RESCORE_WARPS * 32) rescore_kernel(RescoreParams r) {
+    __shared__ uint64_t buf[RESCORE_WARPS * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * RESCORE_WARPS + warp;
+    if (q >= r.nq) return;  // whole warp
+    const int m = r.m, sub = r.dim / m;
+    const float* qv = r.Q + (size_t)q * r.dim;
+    const uint64_t* ak = r.approx + (size_t)q * r.kp;
+    WarpTopK<P> tk;
+    tk.init(r.k, buf + warp * 64);
+    for (int base = 0; base < r.kp; base += 32) {
+        const int i = base + lane;
+        const uint64_t key = i < r.kp ? ak[i] : KEY_NONE;
+        uint64_t ek = KEY_NONE;
+        if (key != KEY_NONE) {
+            const uint32_t pos = key_tag(key);
+            int lo = 0, hi = r.nlist;  // the list l with offs[l] <= pos < offs[l+1]
+            while (lo < hi) {
+                int mid = (lo + hi) >> 1;
+                if (r.offs_full[mid + 1] <= pos) lo = mid + 1; else hi = mid;
+            }
+            const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
+                                             r.codes + (size_t)pos * m, m, sub);
+            ek = make_key(d, pos);
+        }
+        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
+    }
+    tk.store(r.out_keys + (size_t)q * r.k);
+    // error bound: E = (32 + 4m) u sum_s (|q_s| + cmax_s + bmax_s)^2, u = 2^-24
+    double part = 0.0;
+    for (int s = lane; s < m; s += 32) {
+        double qn = 0.0;
+        for (int i = 0; i < sub; ++i) {
+            double x = qv[s * sub + i];
+            qn += x * x;
+        }
+        double t = sqrt(qn) + (double)r.cmax[s] + (double)r.bmax[s];
+        part += t * t;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const double E = (32.0 + 4.0 * m) * 5.9604644775390625e-8 * part * 1.01;
+    const uint64_t last = ak[r.kp - 1];
+    bool cert = true;
+    if (last != KEY_NONE) {
+        // the shortlist is full; tk.thr is the exact k-th key
+        const double dk = (double)key_dist(tk.thr);
+        const double tau = (double)key_dist(last);
+        cert = (tk.thr != KEY_NONE) && (dk + E < tau);
+    }
+    if (!cert && lane == 0) {
+        const uint32_t idx = atomicAdd(r.flag_count, 1u);
+        r.flag_list[idx] = (uint32_t)q;
+    }
+}
+
+void launch_rescore(cudaStream_t s, const RescoreParams& r, int order) {
+    if (r.nq == 0) return;
+    unsigned grid = (unsigned)((r.nq + RESCORE_WARPS - 1) / RESCORE_WARPS);
+    const int T = RESCORE_WARPS * 32;
+#define FDB_RESCORE(PP)                                                                    \
+    do {                                                                                   \
+        if (order == ORDER_LANE8) rescore_kernel<PP, ORDER_LANE8><<<grid, T, 0, s>>>(r);   \
+        else rescore_kernel<PP, ORDER_FAST4><<<grid, T, 0, s>>>(r);                        \
+    } while (0)
+    if (r.k <= 32) FDB_RESCORE(1);
+    else if (r.k <= 64) FDB_RESCORE(2);
+    else FDB_RESCORE(4);
+#undef FDB_RESCORE
+    FDB_LAUNCH_CHECK();
+}
+
+// Per-list table of the table mode: btab[l][s][j] = ||b_sj||^2 + 2<c_ls, b_sj>.
+__global__ void ivf_tables_kernel(const float* __restrict__ cents, const float* __restrict__ cb,
+                                  int nlist, int m, int dim, float* __restrict__ btab) {
+    const size_t L = (size_t)m * KSUB;
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (size_t)nlist * L) return;
+    const size_t l = t / L;
+    const int e = (int)(t - l * L);
+    const int sub = dim / m;
+    const int s = e >> 8;
+    const float* b = cb + (size_t)e * sub;
+    const float* c = cents + l * dim + (size_t)s * sub;
+    float v = 0.0f;
+    for (int i = 0; i < sub; ++i) v = __fmaf_rn(b[i], __fmaf_rn(2.0f, c[i], b[i]), v);
+    btab[t] = v;
+}
+
+void launch_ivf_tables(cudaStream_t s, const float* cents, const float* cb, int nlist, int m,
+                       int dim, float* btab) {
+    size_t total = (size_t)nlist * m * KSUB;
+    if (total == 0) return;
+    ivf_tables_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(cents, cb, nlist, m, dim,
+                                                                      btab);
+    FDB_LAUNCH_CHECK();
 }
 
 // ---------------------------------------------------------------------------

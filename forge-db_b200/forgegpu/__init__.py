@@ -50,7 +50,8 @@ class ForgeGpuError(RuntimeError):
 class Stats(C.Structure):
     _fields_ = [("lists_probed", C.c_uint64), ("codes_scanned", C.c_uint64),
                 ("bytes_scanned", C.c_uint64), ("coarse_ms", C.c_double),
-                ("scan_ms", C.c_double), ("merge_ms", C.c_double), ("total_ms", C.c_double)]
+                ("scan_ms", C.c_double), ("rescore_ms", C.c_double), ("merge_ms", C.c_double),
+                ("total_ms", C.c_double), ("exact_rescans", C.c_uint64)]
 
 
 class TrainOpts(C.Structure):
@@ -91,6 +92,7 @@ _SIGS = {
     "fdb_ivfpq_shard": (C.c_int, [_vp, C.c_int, C.c_int]),
     "fdb_ivfpq_shard_plan": (C.c_int, [_vp, _sz, C.c_int, _vp]),
     "fdb_ivfpq_set_nprobe": (C.c_int, [_vp, _sz]),
+    "fdb_ivfpq_set_scan_mode": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_nprobe": (_sz, [_vp]),
     "fdb_ivfpq_len": (_sz, [_vp]),
     "fdb_ivfpq_n_partitions": (_sz, [_vp]),
@@ -400,8 +402,13 @@ class IVFPQIndex:
     def shard(self, rank: int, world: int):
         _check(lib().fdb_ivfpq_shard(self.h, rank, world))
 
+    SCAN_AUTO, SCAN_EXACT, SCAN_TABLES = 0, 1, 2
+
     def set_nprobe(self, nprobe: int):
         _check(lib().fdb_ivfpq_set_nprobe(self.h, nprobe))
+
+    def set_scan_mode(self, mode: int):
+        _check(lib().fdb_ivfpq_set_scan_mode(self.h, mode))
 
     def nprobe(self) -> int:
         return lib().fdb_ivfpq_nprobe(self.h)

@@ -66,10 +66,24 @@ typedef struct fdb_stats {
     uint64_t codes_scanned;  /* PQ codes (or database rows) scored */
     uint64_t bytes_scanned;  /* algorithmic bytes: codes_scanned * code bytes */
     double coarse_ms;        /* coarse quantizer + probe selection */
-    double scan_ms;          /* LUT build + code scan + local top-k */
+    double scan_ms;          /* LUT build + code scan + local top-k (scan kernel) */
+    double rescore_ms;       /* table mode: exact rescoring, certification, re-scans */
     double merge_ms;         /* cross-device exchange + final merge */
     double total_ms;         /* whole call, device clock */
+    uint64_t exact_rescans;  /* table mode: queries re-scanned exactly after
+                                failing certification */
 } fdb_stats;
+
+/* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  Both return the reference's
+ * exact distances.  EXACT builds every (query, list) table in the AVX2 order.
+ * TABLES builds it from a per-list table precomputed at build time plus a
+ * per-query table, keeps a shortlist of max(32, 2k) candidates, recomputes
+ * their distances exactly, and certifies the result with a worst-case
+ * rounding bound; a query that fails the bound is re-scanned in EXACT mode.
+ * AUTO picks TABLES for subvectors of 8+ floats and k <= 128. */
+#define FDB_SCAN_AUTO 0
+#define FDB_SCAN_EXACT 1
+#define FDB_SCAN_TABLES 2
 
 /* Training options for fdb_ivfpq_build.  Zero-initialise and set what you
  * need.  The reference draws samples and initial centroids from an unseeded
@@ -172,6 +186,9 @@ int fdb_ivfpq_shard(fdb_ivfpq* h, int rank, int world);
 /* The list -> device plan fdb_ivfpq_shard uses: owner[l] in [0, world) for
  * each of nlist lists of the given sizes (host only; needs no device). */
 int fdb_ivfpq_shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
+/* Scan mode (FDB_SCAN_*); no reference counterpart (the reference has one
+ * CPU scan).  Results are identical in every mode. */
+int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode);
 /* set_nprobe (ivf_pq.rs:524-528): stores min(nprobe, nlist). */
 int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe);
 size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h);

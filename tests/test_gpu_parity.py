@@ -241,3 +241,54 @@ def test_bf_self_query_and_edges(fg, ctx):
     with pytest.raises(fg.ForgeGpuError) as e:
         bf.add(np.zeros((1, 31), np.float32))
     assert e.value.kind == "DimensionMismatch"
+
+
+# ---------------------------------------------------------------------------
+# scan modes: exact LUT vs precomputed tables + exact rescoring
+# ---------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def gmm_index(fg, ctx):
+    from forgegpu.datasets import gmm_descriptors
+    X = gmm_descriptors(20000, components=64, seed=11)
+    Q = gmm_descriptors(400, components=64, seed=12)
+    ix = fg.IVFPQIndex.build(X, 64, 16, ctx=ctx, seed=3)
+    return ix, X, Q
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("k", [1, 10, 100])
+def test_scan_modes_match_oracle(fg, ctx, orc, gmm_index, mode, k):
+    ix, X, Q = gmm_index
+    ox = _oracle_index(orc, ix)
+    ix.set_scan_mode(mode)
+    ix.set_nprobe(8)
+    ox.set_nprobe(8)
+    ids, d, cnt, st = ix.batch_search_arrays(Q, k, stats=True)
+    oi, od, oc = ox.batch_search(Q, k)
+    rate = assert_topk_match(ids, d, cnt, oi, od, oc, f"mode={mode} k={k}")
+    assert rate > 0.95
+    if mode == 2:
+        assert st.exact_rescans <= len(Q) // 20  # nearly every query certifies
+    for q in range(0, len(Q), 97):
+        res = ix.search(Q[q], k)
+        si, sd = ox.search(Q[q], k)
+        assert np.array_equal(np.array([r[1] for r in res], np.float32), sd)
+    ix.set_scan_mode(0)
+
+
+def test_table_mode_ties_fall_back_to_exact(fg, ctx, orc):
+    """Fifty copies of each of 40 vectors: distances tie exactly, the
+    shortlist cannot be certified, and the exact re-scan must take over."""
+    rng = np.random.default_rng(21)
+    base = (rng.random((40, 64), dtype=np.float32) * 10).astype(np.float32)
+    X = np.repeat(base, 50, axis=0)
+    ix = fg.IVFPQIndex.build(X, 8, 8, ctx=ctx, seed=2)
+    ix.set_scan_mode(2)
+    ix.set_nprobe(8)
+    ox = _oracle_index(orc, ix)
+    ox.set_nprobe(8)
+    Q = base[:20] + np.float32(0.01)
+    ids, d, cnt, st = ix.batch_search_arrays(Q, 10, stats=True)
+    assert st.exact_rescans > 0
+    oi, od, oc = ox.batch_search(Q, 10)
+    assert_topk_match(ids, d, cnt, oi, od, oc, "ties")
