@@ -270,7 +270,8 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.barrier()
     torch.cuda.synchronize()
 
-    times, scan_ms, bytes_scanned, launches = [], [], [], 0
+    times, scan_ms, bytes_scanned, launches, rescans = [], [], [], 0, []
+    stage = {"coarse_ms": [], "rescore_ms": [], "merge_ms": []}
     with ClockSampler(nvml_index(local_rank)) as clk:
         for s in range(args.steps):
             flush.zero_()
@@ -283,8 +284,14 @@ def run_ours(args, rank, world, local_rank, dist):
             e1.synchronize()
             times.append(e0.elapsed_time(e1))
             scan_ms.append(st.scan_ms)
+            stage["coarse_ms"].append(st.coarse_ms)
+            stage["rescore_ms"].append(st.rescore_ms)
+            stage["merge_ms"].append(st.merge_ms)
+            rescans.append(st.exact_rescans)
             bytes_scanned.append(st.bytes_scanned)
-            launches += 5 + (2 if (world > 1 and args.mode == "lists") else 0)
+            # coarse, select, scan, [rescore (+ exact re-scan)], keys->ids, finalize
+            launches += 5 + (1 if st.rescore_ms > 0 else 0) + (1 if st.exact_rescans else 0)
+            launches += 2 if (world > 1 and args.mode == "lists") else 0
         e2e_times = []
         for s in range(args.steps):
             flush.zero_()
@@ -325,7 +332,11 @@ def run_ours(args, rank, world, local_rank, dist):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": config_dict(args, world, {"recall_at_10": recall, "build_s": round(build_s, 2)}),
+        "config": config_dict(args, world, {
+            "recall_at_10": recall, "build_s": round(build_s, 2),
+            "stage_ms": {k: round(statistics.mean(v), 4) for k, v in stage.items()},
+            "scan_kernel_ms": round(statistics.mean(scan_ms), 4),
+            "exact_rescans_per_step": statistics.mean(rescans)}),
         "e2e": {"value": e2e_value, "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4,
                 "d2h_bytes_per_step": nq * K * (8 + 4) + nq * 4},
