@@ -608,6 +608,16 @@ int fdb_bf_shard(fdb_bf* h, int rank, int world) {
     });
 }
 
+int fdb_bf_set_scan_mode(fdb_bf* h, int mode) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        FDB_REQUIRE(mode >= FDB_SCAN_AUTO && mode <= FDB_SCAN_TABLES, FDB_ERR_INVALID_ARG,
+                    "unknown scan mode");
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->scan_mode = mode;
+    });
+}
+
 size_t fdb_bf_len(const fdb_bf* h) { return h ? h->n : 0; }
 size_t fdb_bf_dimension(const fdb_bf* h) { return (h && !h->h_ids.empty()) ? h->dim : 0; }
 

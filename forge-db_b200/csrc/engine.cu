@@ -475,6 +475,40 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
 // ---------------------------------------------------------------------------
 // brute force
 // ---------------------------------------------------------------------------
+__global__ void fill_f32_kernel(float* p, size_t n, float v) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; t < n; t += (size_t)gridDim.x * blockDim.x) p[t] = v;
+}
+
+// 1/||x|| for the cosine shortlist (0 for a zero row).
+__global__ void rsqrt_kernel(const float* __restrict__ norms, size_t n, float* __restrict__ out) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) out[t] = norms[t] > 0.0f ? rsqrtf(norms[t]) : 0.0f;
+}
+
+__global__ void max_norm_kernel(const float* __restrict__ norms, size_t n, unsigned* out) {
+    unsigned best = 0;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        best = max(best, __float_as_uint(norms[i]));  // non-negative floats order as uints
+    atomicMax(out, best);
+}
+
+__global__ void scatter_rows_u64(const uint64_t* __restrict__ src, const uint32_t* __restrict__ idx,
+                                 size_t count, int k, uint64_t* __restrict__ dst) {
+    size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= count * (size_t)k) return;
+    size_t r = t / k;
+    dst[(size_t)idx[r] * k + (t - r * k)] = src[t];
+}
+
+// The tensor-core shortlist serves every metric but Manhattan, dims up to 256
+// and k up to 128 (shortlists of max(32, 2k) keys).
+static bool bf_tensor_ok(const fdb_bf* h, size_t k) {
+    return h->scan_mode != FDB_SCAN_EXACT && h->metric != MANHATTAN && h->dim <= 256 &&
+           k >= 1 && k <= 128;
+}
+
 void bf_upload(fdb_bf* h) {
     if (!h->dirty) return;
     Ctx& c = h->ctx->c;
@@ -487,12 +521,52 @@ void bf_upload(fdb_bf* h) {
         FDB_CUDA(cudaMemcpyAsync(h->ids.p, h->h_ids.data() + h->row0, h->ids.bytes(),
                                  cudaMemcpyHostToDevice, s));
     }
+    // squared norms in the AVX2 order (cosine needs them exactly; the
+    // tensor-core path uses them for every metric).  Padded by two tiles of
+    // +inf so the epilogue's whole-chunk loads stay in bounds.
+    h->norms.alloc(h->n + 256);
+    fill_f32_kernel<<<1, 256, 0, s>>>(h->norms.p + h->n, 256, INFINITY);
+    FDB_LAUNCH_CHECK();
+    launch_row_norms(s, h->x.p, h->n, (int)h->dim, h->norms.p);
+    h->rnorms.release();
     if (h->metric == COSINE) {
-        h->norms.alloc(h->n);
-        launch_row_norms(s, h->x.p, h->n, (int)h->dim, h->norms.p);
+        h->rnorms.alloc(h->n + 256);
+        FDB_CUDA(cudaMemsetAsync(h->rnorms.p, 0, (h->n + 256) * 4, s));
+        rsqrt_kernel<<<(unsigned)((h->n + 255) / 256), 256, 0, s>>>(h->norms.p, h->n,
+                                                                    h->rnorms.p);
+        FDB_LAUNCH_CHECK();
+    }
+    h->x16.release();
+    h->xmax = 0.0f;
+    if (h->metric != MANHATTAN && h->dim <= 256 && h->n > 0) {
+        h->kpad = (int)((h->dim + 63) / 64 * 64);
+        h->x16.alloc(h->n * (size_t)h->kpad);
+        launch_to_half(s, h->x.p, h->n, (int)h->dim, h->kpad, h->x16.p);
+        DevBuf<unsigned> mx(1);
+        FDB_CUDA(cudaMemsetAsync(mx.p, 0, 4, s));
+        max_norm_kernel<<<148, 256, 0, s>>>(h->norms.p, h->n, mx.p);
+        FDB_LAUNCH_CHECK();
+        unsigned bits = 0;
+        FDB_CUDA(cudaMemcpyAsync(&bits, mx.p, 4, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+        float m2;
+        std::memcpy(&m2, &bits, 4);
+        h->xmax = (float)(std::sqrt((double)m2) * (1.0 + 1e-6));
     }
     FDB_CUDA(cudaStreamSynchronize(s));
     h->dirty = false;
+}
+
+// Exact SIMT scan of nq contiguous queries into keys[nq][k].
+static void bf_exact_scan(fdb_bf* h, const float* dQ, size_t nq, size_t k, const float* qn,
+                          uint64_t* keys) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    size_t psz = bf_part_size(h->n, (int)nq, (int)k, c.sm_count);
+    h->s_part.ensure(psz);
+    int chunks = launch_bf_scan(s, h->metric, dQ, (int)nq, qn, h->x.p, h->n, (int)h->dim,
+                                h->norms.p, h->row0, (int)k, c.sm_count, h->s_part.p, h->s_part.n);
+    launch_merge_lists(s, h->s_part.p, chunks, nq * k, nq, (int)k, keys);
 }
 
 void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
@@ -511,21 +585,52 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
     const size_t per = nq * k;
     h->s_keys.ensure(per);
     h->s_ids.ensure(per);
+    uint32_t nflag = 0;
     if (h->n == 0) {
         FDB_CUDA(cudaMemsetAsync(h->s_keys.p, 0xff, per * 8, s));
+        tm.mark();
     } else {
-        const float* qn = nullptr;
-        if (h->metric == COSINE) {
-            h->s_qnorm.ensure(nq);
-            launch_row_norms(s, dQ, nq, (int)h->dim, h->s_qnorm.p);
-            qn = h->s_qnorm.p;
+        h->s_qnorm.ensure(nq);
+        launch_row_norms(s, dQ, nq, (int)h->dim, h->s_qnorm.p);
+        const float* qn = h->s_qnorm.p;
+        if (h->x16.p && bf_tensor_ok(h, k)) {
+            // tensor-core shortlist -> exact rescore -> certified, else exact re-scan
+            const size_t kp = std::min<size_t>(256, std::max<size_t>(32, 2 * k));
+            h->s_q16.ensure(nq * (size_t)h->kpad);
+            launch_to_half(s, dQ, nq, (int)h->dim, h->kpad, h->s_q16.p);
+            h->s_flags.ensure(nq + 2);
+            FDB_CUDA(cudaMemsetAsync(h->s_flags.p, 0, 8, s));
+            int* err = reinterpret_cast<int*>(h->s_flags.p + nq + 1);
+            FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
+            h->gemm.err = err;
+            gemm_shortlist(s, h->s_q16.p, (int)nq, qn, h->x16.p, h->n, h->kpad,
+                           h->metric == COSINE ? h->rnorms.p : h->norms.p, h->metric, h->row0,
+                           (int)kp, c.sm_count, h->gemm);
+            tm.mark();
+            launch_bf_rescore(s, dQ, (int)nq, h->x.p, (int)h->dim, qn, h->xmax, h->metric,
+                              h->row0, h->gemm, (int)kp, (int)k, h->s_keys.p, h->s_flags.p,
+                              h->s_flags.p + 1);
+            uint32_t hv[2] = {0, 0};
+            FDB_CUDA(cudaMemcpyAsync(&hv[0], h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaMemcpyAsync(&hv[1], err, 4, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaStreamSynchronize(s));
+            FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core scan timed out on the device");
+            nflag = hv[0];
+            if (nflag > 0) {
+                DevBuf<float> qf(nflag * h->dim), qfn(nflag);
+                DevBuf<uint64_t> kf(nflag * k);
+                launch_gather_rows(s, dQ, h->dim, h->s_flags.p + 1, nflag, qf.p);
+                launch_row_norms(s, qf.p, nflag, (int)h->dim, qfn.p);
+                bf_exact_scan(h, qf.p, nflag, k, qfn.p, kf.p);
+                scatter_rows_u64<<<(unsigned)((nflag * k + 255) / 256), 256, 0, s>>>(
+                    kf.p, h->s_flags.p + 1, nflag, (int)k, h->s_keys.p);
+                FDB_LAUNCH_CHECK();
+                FDB_CUDA(cudaStreamSynchronize(s));
+            }
+        } else {
+            bf_exact_scan(h, dQ, nq, k, qn, h->s_keys.p);
+            tm.mark();
         }
-        size_t psz = bf_part_size(h->n, (int)nq, (int)k, c.sm_count);
-        h->s_part.ensure(psz);
-        int chunks = launch_bf_scan(s, h->metric, dQ, (int)nq, qn, h->x.p, h->n, (int)h->dim,
-                                    h->norms.p, h->row0, (int)k, c.sm_count, h->s_part.p,
-                                    h->s_part.n);
-        launch_merge_lists(s, h->s_part.p, chunks, nq * k, nq, (int)k, h->s_keys.p);
     }
     tm.mark();
     launch_keys_to_ids(s, h->s_keys.p, per, h->ids.p, h->row0, h->s_ids.p);
@@ -544,9 +649,13 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
         st->lists_probed = 0;
         st->codes_scanned = (uint64_t)nq * h->n;
         st->bytes_scanned = (uint64_t)h->n * h->dim * 4;
-        st->scan_ms = tm.ms(0, 1);
-        st->merge_ms = tm.ms(1, 2);
-        st->total_ms = tm.ms(0, 2);
+        st->exact_rescans = nflag;
+        if (tm.ev.size() >= 4) {
+            st->scan_ms = tm.ms(0, 1);
+            st->rescore_ms = tm.ms(1, 2);
+            st->merge_ms = tm.ms(2, 3);
+            st->total_ms = tm.ms(0, 3);
+        }
     }
 }
 

@@ -3,6 +3,7 @@
 // index handles behind the opaque C types of include/forgegpu.h.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
 
@@ -191,6 +192,23 @@ void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_
                     int* iters_run);
 void shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
 
+// gemm_topk.cu: the tensor-core shortlist of brute force (sample pass,
+// threshold, filter pass, top-kp selection) and its exact rescoring.
+struct GemmScratch {
+    DevBuf<uint64_t> part, top32, cand, approx;
+    DevBuf<unsigned> tau_bits, cand_cnt;
+    DevBuf<float> tau;
+    int cap = 0;
+    int* err = nullptr;  // device error word (timeouts)
+};
+void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnorm,
+                    const __half* x16, size_t n, int kpad, const float* xnorm, int metric,
+                    uint64_t tag_base, int kp, int sm_count, GemmScratch& w);
+void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, int dim,
+                       const float* qnorm, float xmax, int metric, uint64_t tag_base,
+                       const GemmScratch& w, int kp, int k, uint64_t* out, uint32_t* flag_count,
+                       uint32_t* flag_list);
+
 }  // namespace fdb
 
 struct fdb_ivfpq;
@@ -257,13 +275,21 @@ struct fdb_bf {
     std::vector<uint64_t> h_ids;
     fdb::DevBuf<float> x;        // [n][dim]
     fdb::DevBuf<uint64_t> ids;   // [n]
-    fdb::DevBuf<float> norms;    // [n] squared norms in AVX2 order (cosine)
+    fdb::DevBuf<float> norms;    // [n + 256] squared norms in AVX2 order, +inf padding
+    fdb::DevBuf<float> rnorms;   // cosine: [n + 256] 1/||x|| (0 for zero rows and padding)
     bool dirty = true;
     bool sharded = false;
     int shard_world = 1;
+    // tensor-core shortlist: fp16 rows padded to a multiple of 64 columns
+    int scan_mode = FDB_SCAN_AUTO;
+    int kpad = 0;
+    float xmax = 0.0f;           // largest row norm (rounded up), for the error bound
+    fdb::DevBuf<__half> x16;     // [n][kpad]
     std::mutex mu;
     fdb::DevBuf<float> s_q, s_qnorm;
+    fdb::DevBuf<__half> s_q16;
+    fdb::GemmScratch gemm;
     fdb::DevBuf<uint64_t> s_part, s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids;
     fdb::DevBuf<float> s_dists;
-    fdb::DevBuf<uint32_t> s_counts;
+    fdb::DevBuf<uint32_t> s_counts, s_flags;
 };

@@ -1,6 +1,7 @@
 // fdb_kernels.h -- launchers of the search kernels (host-callable).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -74,5 +75,8 @@ int launch_bf_scan(cudaStream_t s, int metric, const float* Q, int nq, const flo
                    const float* X, size_t n, int dim, const float* xnorm, uint64_t tag_base,
                    int k, int sm_count, uint64_t* part, size_t part_capacity);
 size_t bf_part_size(size_t n, int nq, int k, int sm_count);
+
+// gemm_topk.cu: fp32 -> fp16 copies with zero padding to kpad columns.
+void launch_to_half(cudaStream_t s, const float* x, size_t n, int dim, int kpad, __half* out);
 
 }  // namespace fdb

@@ -1,0 +1,751 @@
+// gemm_topk.cu -- tensor-core (tcgen05) shortlist for brute-force search.
+//
+// For a block of 128 queries and a chunk of database rows, the kernel forms
+// S = Q . X^T with tcgen05.mma (fp16 operands staged in shared memory by TMA
+// with 128-byte swizzle, fp32 accumulators in TMEM) and turns every score
+// into an approximate metric value:
+//     L2^2   : ||q||^2 + ||x||^2 - 2 s
+//     dot    : -s
+//     cosine : 1 - s / sqrt(||q||^2 ||x||^2)
+// Two passes run on the same TMA -> MMA -> TMEM pipeline:
+//   SAMPLE: every S-th row tile only.  Each epilogue thread owns one query
+//     (the TMEM lane of its row); scores at or below the query's running
+//     threshold are buffered in shared memory and merged, a warp at a time,
+//     into the query's sorted top-32 in global memory.  Its 32nd distance is
+//     a per-query threshold tau that about 32*S rows of the full set pass.
+//   FILTER: every tile, eight epilogue warps (two per TMEM lane quadrant, one
+//     per half of the columns).  A score costs a shuffle, an FMA and a
+//     compare; the rare scores <= tau are appended to a per-query candidate
+//     array with an atomic counter.
+// select_candidates_kernel then takes the top-kp of each query's candidates
+// and bf_rescore_kernel recomputes them exactly in the reference's AVX2
+// summation order and certifies the result (see there), so returned
+// distances are exact and a bad tau or an overflow only costs a fallback.
+//
+// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 4-11 = epilogue.  Every wait on an mbarrier is bounded:
+// on timeout the kernel sets an error word, the other warps see it and
+// leave, in-flight copies and MMAs are waited for (bounded), TMEM is freed,
+// and the host reports FDB_ERR_TIMEOUT.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "fdb_device.cuh"
+#include "fdb_internal.h"
+#include "fdb_kernels.h"
+
+namespace fdb {
+namespace tc {
+
+constexpr int TILE_M = 128;   // queries per block (TMEM lanes)
+constexpr int TILE_N = 128;   // database rows per MMA tile
+constexpr int KATOM = 64;     // fp16 elements per 128-byte swizzle atom
+constexpr int ATOM_BYTES = TILE_M * 128;  // one [128 rows][64 fp16] swizzled atom
+constexpr int THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int SAMPLE_K = 32;  // sample-pass shortlist per query
+constexpr int EPI_SHORTLIST = 0, EPI_FILTER = 1;
+constexpr int BUF_CAP = 64;   // sample pass: buffered candidates per query
+constexpr unsigned long long WAIT_CYCLES = 4000000000ull;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait.  Returns false if the kernel is aborting (this or another
+// warp timed out).  The error word and the clock are polled every 64 tries.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = clock64();
+    for (unsigned it = 1;; ++it) {
+        if (mbar_try(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*(volatile int*)err) return false;
+            if (clock64() - t0 > WAIT_CYCLES) {
+                atomicExch(err, 1);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand tile in the 128-byte swizzle layout: 8-row groups 1024 B
+// apart (SBO), the leading offset unused, descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M=128, N=128.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(TILE_N >> 3) << 17) |
+                           ((uint32_t)(TILE_M >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+    uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmTopkParams {
+    int nq;              // queries
+    size_t n;            // database rows
+    int katoms;          // padded dim / 64
+    int metric;
+    const float* qnorm;  // [nq] exact squared norms
+    const float* colv;   // per-row column values (see column_values), padded to whole tiles
+    size_t rows_per_chunk;
+    uint64_t tag_base;   // global index of row 0
+    // SAMPLE pass
+    int tile_stride;     // process global tiles t with t % tile_stride == 0
+    uint64_t* part;      // [chunks][nq][SAMPLE_K], preset to KEY_NONE
+    unsigned* tau_g;     // [nq] best known 32nd distance (orderable bits), preset ~0
+    // FILTER pass
+    const float* tau_q;  // [nq] admission threshold
+    uint64_t* cand;      // [nq][cap] candidate keys
+    unsigned* cand_cnt;  // [nq] candidates seen (may exceed cap)
+    int cap;
+    int* err;            // error word (0 = ok)
+};
+
+// Approximate metric families (compile-time, so no per-score branching):
+//   MET_L2  : ||q||^2 + ||x||^2 - 2 s   (qv = ||q||^2, cv = ||x||^2)
+//   MET_DOT : -s
+//   MET_COS : 1 - s / (||q|| ||x||)      (qv = 1/||q||, cv = 1/||x||; a zero
+//             norm on either side gives 0, the reference's value)
+constexpr int MET_L2 = 0, MET_DOT = 1, MET_COS = 2;
+
+template <int MET>
+__device__ __forceinline__ float approx_metric(float s, float qv, float cv) {
+    if (MET == MET_DOT) return -s;
+    if (MET == MET_COS) return (qv == 0.0f || cv == 0.0f) ? 0.0f : 1.0f - s * (qv * cv);
+    return __fmaf_rn(-2.0f, s, qv + cv);
+}
+
+// The 32 per-row values of one column chunk (||x||^2 for L2, 1/||x|| for
+// cosine), read with eight warp-uniform 128-bit loads.  The arrays are padded
+// to whole tiles, so a chunk never reads past their end.
+template <int MET>
+__device__ __forceinline__ void column_values(const float* colv, size_t row0, float (&cv)[32]) {
+    if (MET == MET_DOT) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cv[j] = 0.0f;
+        return;
+    }
+    const float4* p4 = reinterpret_cast<const float4*>(colv + row0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 t = __ldg(p4 + i);
+        cv[4 * i] = t.x;
+        cv[4 * i + 1] = t.y;
+        cv[4 * i + 2] = t.z;
+        cv[4 * i + 3] = t.w;
+    }
+}
+
+// Merge lcnt (<= 32) buffered keys into a sorted top-32 list in global
+// memory (one warp); returns the list's 32nd key.
+__device__ __forceinline__ uint64_t merge_into(uint64_t* list, const uint64_t* lbuf, int lcnt,
+                                               int lane) {
+    WarpTopK<1> tk;
+    tk.init(SAMPLE_K, nullptr);
+    tk.L[0] = list[lane];
+    tk.merge32(lane < lcnt ? lbuf[lane] : KEY_NONE);
+    list[lane] = tk.L[0];
+    return tk.thr;
+}
+
+template <int EPI, int MET>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_topk_kernel(const __grid_constant__ CUtensorMap qmap,
+                     const __grid_constant__ CUtensorMap xmap, GemmTopkParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t base = smem_u32(smem_raw);
+    unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
+    const int KA = p.katoms;
+    const int NSTAGE = KA <= 3 ? 2 : 1;
+    unsigned char* a_tile = smem;                                  // KA atoms
+    unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA atoms
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(b_tile + NSTAGE * KA * ATOM_BYTES);
+    uint64_t* bars = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
+    uint64_t* a_full = bars + 0;
+    uint64_t* b_full = bars + 1;   // [2]
+    uint64_t* b_empty = bars + 3;  // [2]
+    uint64_t* t_full = bars + 5;   // [2]
+    uint64_t* t_empty = bars + 7;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qb = blockIdx.x;
+    const size_t r0 = (size_t)blockIdx.y * p.rows_per_chunk;
+    const size_t r1 = min(p.n, r0 + p.rows_per_chunk);
+    const int ntiles = r0 < r1 ? (int)((r1 - r0 + TILE_N - 1) / TILE_N) : 0;
+    // tiles this block processes: t = first + i * stride, i < count
+    const int stride = EPI == EPI_SHORTLIST ? p.tile_stride : 1;
+    const int tile0 = (int)(r0 / TILE_N);
+    const int first = (stride - tile0 % stride) % stride;
+    const int count = ntiles > first ? (ntiles - first + stride - 1) / stride : 0;
+    const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
+    const int n_epi_warps = EPI == EPI_SHORTLIST ? 4 : 8;
+
+    if (threadIdx.x == 0) {
+        mbar_init(a_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(b_full + i, 1);
+            mbar_init(b_empty + i, 1);
+            mbar_init(t_full + i, 1);
+            mbar_init(t_empty + i, n_epi_warps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(2 * TILE_N));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // Last asynchronous operation each role issued, so that an aborting
+    // block can wait for it (bounded) before it frees TMEM and exits.
+    int last_load[2] = {-1, -1};  // producer: last use issued per stage
+    int last_i = -1;              // MMA issuer: last tile committed
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0 && count > 0) {
+            mbar_expect_tx(a_full, stage_bytes);
+            for (int a = 0; a < KA; ++a)
+                tma_load_2d(a_tile + a * ATOM_BYTES, &qmap, a_full, a * KATOM, qb * TILE_M);
+            for (int i = 0; i < count; ++i) {
+                const int s = NSTAGE == 2 ? (i & 1) : 0;
+                const int use = NSTAGE == 2 ? (i >> 1) : i;
+                if (i >= NSTAGE && !mbar_wait(b_empty + s, (use - 1) & 1, p.err)) break;
+                mbar_expect_tx(b_full + s, stage_bytes);
+                const int row = (int)(r0 + (size_t)(first + i * stride) * TILE_N);
+                unsigned char* dst = b_tile + s * KA * ATOM_BYTES;
+                for (int a = 0; a < KA; ++a)
+                    tma_load_2d(dst + a * ATOM_BYTES, &xmap, b_full + s, a * KATOM, row);
+                last_load[s] = use;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0 && count > 0) {
+            bool ok = mbar_wait(a_full, 0, p.err);
+            for (int i = 0; ok && i < count; ++i) {
+                const int s = NSTAGE == 2 ? (i & 1) : 0;
+                const int use = NSTAGE == 2 ? (i >> 1) : i;
+                const int b = i & 1;  // TMEM accumulator buffer
+                if (i >= 2 && !mbar_wait(t_empty + b, ((i >> 1) - 1) & 1, p.err)) break;
+                if (!mbar_wait(b_full + s, use & 1, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(b * TILE_N);
+                const uint32_t abase = smem_u32(a_tile);
+                const uint32_t bbase = smem_u32(b_tile + s * KA * ATOM_BYTES);
+                for (int a = 0; a < KA; ++a) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {  // 4 x K16 per 64-wide atom
+                        const uint32_t off = (uint32_t)(a * ATOM_BYTES + kk * 32);
+                        umma_f16(d, smem_desc_sw128(abase + off), smem_desc_sw128(bbase + off),
+                                 (a | kk) != 0);
+                    }
+                }
+                umma_commit(b_empty + s);  // stage s may be refilled once these MMAs finish
+                umma_commit(t_full + b);   // accumulator b is ready for the epilogue
+                last_i = i;
+            }
+        }
+    } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + n_epi_warps) {
+        // ---------------- epilogue ----------------
+        const int w = warp - EPI_WARP0;
+        const int quad = w & 3;            // TMEM lane quadrant = warp % 4
+        const int half = w >> 2;           // FILTER: column half of this warp
+        const int e = quad * 32 + lane;    // query row in the block
+        const int q = qb * TILE_M + e;
+        const bool qok = q < p.nq;
+        const float qn0 = (qok && p.qnorm) ? p.qnorm[q] : 0.0f;
+        const float qn = MET == MET_COS ? (qn0 > 0.0f ? rsqrtf(qn0) : 0.0f) : qn0;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const int c0 = EPI == EPI_SHORTLIST ? 0 : 2 * half;
+        const int c1 = EPI == EPI_SHORTLIST ? TILE_N / 32 : 2 * half + 2;
+        float tau = EPI == EPI_FILTER ? (qok ? p.tau_q[q] : -__int_as_float(0x7f800000))
+                                      : __int_as_float(0x7f800000);
+        int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
+        uint64_t* mybuf = cbuf + e * BUF_CAP;
+        for (int i = 0; i < count; ++i) {
+            const int b = i & 1;
+            // one lane waits; the warp follows its verdict (tcgen05.ld is warp-wide)
+            int got = 0;
+            if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err) ? 1 : 0;
+            got = __shfl_sync(0xffffffffu, got, 0);
+            if (!got) break;
+            tc_fence_after();
+            if (EPI == EPI_SHORTLIST && qok) {
+                // Any chunk's top-32 bounds the global top-32 of the sample.
+                const unsigned g = *(volatile unsigned*)(p.tau_g + q);
+                if (g != 0xffffffffu) tau = fminf(tau, ord2f(g));
+            }
+            const size_t rb = r0 + (size_t)(first + i * stride) * TILE_N;
+#pragma unroll 1
+            for (int c = c0; c < c1; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)(b * TILE_N + c * 32), v);
+                if (c == c1 - 1) {
+                    // all of this warp's columns of buffer b are in registers
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(t_empty + b);
+                }
+                const size_t cb = rb + (size_t)c * 32;
+                const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
+                float cv[32];
+                column_values<MET>(p.colv, cb, cv);
+                const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
+                if (EPI == EPI_FILTER) {
+                    // admission test first (compare-and-accumulate, no branch);
+                    // rows past the end carry +inf in colv and never pass
+                    bool any = false;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        any |= approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]) <= tau;
+                    if (any && nvalid > 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                            if (j < nvalid && d <= tau) {
+                                const unsigned idx = atomicAdd(p.cand_cnt + q, 1u);
+                                if (idx < (unsigned)p.cap)
+                                    p.cand[(size_t)q * p.cap + idx] = make_key(d, tag0 + j);
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                        if (qok && j < nvalid && d <= tau) mybuf[cnt++] = make_key(d, tag0 + j);
+                    }
+                }
+                if (EPI == EPI_SHORTLIST) {
+                    // fold full buffers into their top-32 lists, one query at a time
+                    unsigned full;
+                    while ((full = __ballot_sync(0xffffffffu, cnt >= 32)) != 0) {
+                        const int leader = __ffs(full) - 1;
+                        const int lq = __shfl_sync(0xffffffffu, q, leader);
+                        const int lc = __shfl_sync(0xffffffffu, cnt, leader);
+                        uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
+                        uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+                        __syncwarp();
+                        const uint64_t kth = merge_into(lst, lbuf, 32, lane);
+                        __syncwarp();
+                        const uint64_t rest = (lane + 32 < lc) ? lbuf[lane + 32] : KEY_NONE;
+                        __syncwarp();
+                        if (lane + 32 < lc) lbuf[lane] = rest;
+                        __syncwarp();
+                        if (lane == leader) {
+                            cnt -= 32;
+                            if (kth != KEY_NONE) {
+                                tau = fminf(tau, key_dist(kth));
+                                atomicMin(p.tau_g + lq, (unsigned)(kth >> 32));
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (EPI == EPI_SHORTLIST) {
+            unsigned left;
+            while ((left = __ballot_sync(0xffffffffu, cnt > 0)) != 0) {
+                const int leader = __ffs(left) - 1;
+                const int lq = __shfl_sync(0xffffffffu, q, leader);
+                const int lc = __shfl_sync(0xffffffffu, cnt, leader);
+                uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
+                uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+                __syncwarp();
+                merge_into(lst, lbuf, lc, lane);
+                __syncwarp();
+                if (lane == leader) cnt = 0;
+            }
+        }
+    }
+    __syncthreads();
+    if (*(volatile int*)p.err) {
+        // aborting: let the copies and MMAs this block issued land before exit
+        // (waits on phases that already completed return at once)
+        if (warp == 0 && lane == 0) {
+            for (int s2 = 0; s2 < 2; ++s2)
+                if (last_load[s2] >= 0) {
+                    const unsigned long long t0 = clock64();
+                    while (!mbar_try(b_full + s2, last_load[s2] & 1) &&
+                           clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+        }
+        if (warp == 1 && lane == 0 && last_i >= 0) {
+            const unsigned long long t0 = clock64();
+            while (!mbar_try(t_full + (last_i & 1), (last_i >> 1) & 1) &&
+                   clock64() - t0 < WAIT_CYCLES) {
+            }
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(2 * TILE_N));
+    }
+}
+
+// Top-kp of each query's candidate keys (one warp per query).
+template <int P>
+__global__ void __launch_bounds__(256)
+    select_candidates_kernel(const uint64_t* __restrict__ cand, const unsigned* __restrict__ cnt,
+                             int cap, int nq, int kp, uint64_t* __restrict__ out) {
+    const int warp = threadIdx.x >> 5;
+    const int q = blockIdx.x * 8 + warp;
+    if (q >= nq) return;
+    WarpTopK<P> tk;
+    tk.init(kp, nullptr);
+    const int c = (int)min(cnt[q], (unsigned)cap);
+    tk.ingest(cand + (size_t)q * cap, c);
+    tk.store(out + (size_t)q * kp);
+}
+
+// tau[q] = the 32nd distance of the sample top-32 (+inf if fewer).
+__global__ void sample_tau_kernel(const uint64_t* __restrict__ top32, int nq,
+                                  float* __restrict__ tau) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    const uint64_t k = top32[(size_t)q * SAMPLE_K + SAMPLE_K - 1];
+    tau[q] = k == KEY_NONE ? __int_as_float(0x7f800000) : key_dist(k);
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        FDB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        FDB_REQUIRE(p && q == cudaDriverEntryPointSuccess, FDB_ERR_CUDA,
+                    "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// [rows][kpad] fp16, row-major; boxes of 64 (K) x 128 rows, 128-byte swizzle.
+CUtensorMap make_map(const __half* base, size_t rows, int kpad) {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {(cuuint64_t)kpad, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kpad * sizeof(__half)};
+    cuuint32_t box[2] = {(cuuint32_t)tc::KATOM, (cuuint32_t)tc::TILE_M};
+    cuuint32_t elem[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides,
+                             box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FDB_REQUIRE(r == CUDA_SUCCESS, FDB_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    return m;
+}
+
+__global__ void to_half_kernel(const float* __restrict__ x, size_t n, int dim, int kpad,
+                               __half* __restrict__ out) {
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n * (size_t)kpad) return;
+    const size_t r = t / kpad;
+    const int c = (int)(t - r * kpad);
+    out[t] = __float2half_rn(c < dim ? x[r * dim + c] : 0.0f);
+}
+
+size_t gemm_smem(int katoms, int epi) {
+    const int nstage = katoms <= 3 ? 2 : 1;
+    return 1024 + (size_t)(1 + nstage) * katoms * tc::ATOM_BYTES +
+           (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) + 16 * 8;
+}
+
+// Row chunks: enough blocks for several waves with little tail waste.
+int pick_chunks(size_t n, int nq, int sm_count, size_t* rows_per_chunk) {
+    const int nqb = (nq + tc::TILE_M - 1) / tc::TILE_M;
+    int best_r = 1;
+    double best_cost = 1e30;
+    const int rmax = (int)std::min<size_t>(
+        256, std::max<size_t>(1, (n + tc::TILE_N - 1) / tc::TILE_N / 4));
+    for (int r = 1; r <= rmax; ++r) {
+        const double ctas = (double)nqb * r;
+        const double waves = std::ceil(ctas / sm_count);
+        const double cost = waves * (1.0 / r) + 0.001 * r;
+        if (cost < best_cost - 1e-12) {
+            best_cost = cost;
+            best_r = r;
+        }
+    }
+    size_t rows = (n + best_r - 1) / best_r;
+    rows = (rows + tc::TILE_N - 1) / tc::TILE_N * tc::TILE_N;
+    *rows_per_chunk = rows;
+    return (int)((n + rows - 1) / rows);
+}
+
+template <int EPI, int MET>
+void launch_pass_m(cudaStream_t s, const CUtensorMap& qm, const CUtensorMap& xm, int nq,
+                   int chunks, const tc::GemmTopkParams& p) {
+    const size_t smem = gemm_smem(p.katoms, EPI);
+    FDB_CUDA(cudaFuncSetAttribute(tc::gemm_topk_kernel<EPI, MET>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)((nq + tc::TILE_M - 1) / tc::TILE_M), (unsigned)chunks);
+    tc::gemm_topk_kernel<EPI, MET><<<grid, tc::THREADS, smem, s>>>(qm, xm, p);
+    FDB_LAUNCH_CHECK();
+}
+
+template <int EPI>
+void launch_pass(cudaStream_t s, const CUtensorMap& qm, const CUtensorMap& xm, int nq,
+                 int chunks, const tc::GemmTopkParams& p) {
+    if (p.metric == DOT_PRODUCT) launch_pass_m<EPI, tc::MET_DOT>(s, qm, xm, nq, chunks, p);
+    else if (p.metric == COSINE) launch_pass_m<EPI, tc::MET_COS>(s, qm, xm, nq, chunks, p);
+    else launch_pass_m<EPI, tc::MET_L2>(s, qm, xm, nq, chunks, p);
+}
+
+}  // namespace
+
+void launch_to_half(cudaStream_t s, const float* x, size_t n, int dim, int kpad, __half* out) {
+    size_t total = n * (size_t)kpad;
+    if (total == 0) return;
+    to_half_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(x, n, dim, kpad, out);
+    FDB_LAUNCH_CHECK();
+}
+
+// Sample pass, threshold, filter pass and candidate selection.  Scratch is
+// carved from the caller's buffers (sizes from gemm_shortlist_scratch).
+void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnorm,
+                    const __half* x16, size_t n, int kpad, const float* colv, int metric,
+                    uint64_t tag_base, int kp, int sm_count, GemmScratch& w) {
+    FDB_REQUIRE(kpad % tc::KATOM == 0 && kpad <= 256, FDB_ERR_UNSUPPORTED, "bad padded dim");
+    FDB_REQUIRE(kp >= 1 && kp <= 256, FDB_ERR_UNSUPPORTED, "shortlist too long");
+    CUtensorMap qm = make_map(q16, (size_t)nq, kpad);
+    CUtensorMap xm = make_map(x16, n, kpad);
+    size_t rows_per_chunk = 0;
+    const int chunks = pick_chunks(n, nq, sm_count, &rows_per_chunk);
+    // about 32 * stride rows of the full set pass the sample threshold:
+    // aim for >= 2 kp of them
+    int stride = 1;
+    while (tc::SAMPLE_K * stride < 2 * kp) stride <<= 1;
+    tc::GemmTopkParams p{};
+    p.nq = nq;
+    p.n = n;
+    p.katoms = kpad / tc::KATOM;
+    p.metric = metric;
+    p.qnorm = qnorm;
+    p.colv = colv;
+    p.rows_per_chunk = rows_per_chunk;
+    p.tag_base = tag_base;
+    p.err = w.err;
+    // --- sample pass ---
+    w.part.ensure((size_t)chunks * nq * tc::SAMPLE_K);
+    w.top32.ensure((size_t)nq * tc::SAMPLE_K);
+    w.tau_bits.ensure(nq);
+    w.tau.ensure(nq);
+    FDB_CUDA(cudaMemsetAsync(w.part.p, 0xff, w.part.bytes(), s));
+    FDB_CUDA(cudaMemsetAsync(w.tau_bits.p, 0xff, (size_t)nq * 4, s));
+    p.tile_stride = stride;
+    p.part = w.part.p;
+    p.tau_g = w.tau_bits.p;
+    launch_pass<tc::EPI_SHORTLIST>(s, qm, xm, nq, chunks, p);
+    launch_merge_lists(s, w.part.p, chunks, (size_t)nq * tc::SAMPLE_K, nq, tc::SAMPLE_K,
+                       w.top32.p);
+    tc::sample_tau_kernel<<<(nq + 255) / 256, 256, 0, s>>>(w.top32.p, nq, w.tau.p);
+    FDB_LAUNCH_CHECK();
+    // --- filter pass ---
+    w.cap = std::max(1024, 16 * kp);
+    w.cand.ensure((size_t)nq * w.cap);
+    w.cand_cnt.ensure(nq);
+    FDB_CUDA(cudaMemsetAsync(w.cand_cnt.p, 0, (size_t)nq * 4, s));
+    p.tile_stride = 1;
+    p.tau_q = w.tau.p;
+    p.cand = w.cand.p;
+    p.cand_cnt = w.cand_cnt.p;
+    p.cap = w.cap;
+    launch_pass<tc::EPI_FILTER>(s, qm, xm, nq, chunks, p);
+    // --- top-kp of the candidates ---
+    w.approx.ensure((size_t)nq * kp);
+    const unsigned grid = (unsigned)((nq + 7) / 8);
+#define FDB_SEL(PP)                                                                      \
+    tc::select_candidates_kernel<PP><<<grid, 256, 0, s>>>(w.cand.p, w.cand_cnt.p, w.cap, nq, \
+                                                          kp, w.approx.p)
+    if (kp <= 32) FDB_SEL(1);
+    else if (kp <= 64) FDB_SEL(2);
+    else if (kp <= 128) FDB_SEL(4);
+    else FDB_SEL(8);
+#undef FDB_SEL
+    FDB_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------------------
+// exact rescoring of brute-force shortlists
+// ---------------------------------------------------------------------------
+constexpr int BRS_WARPS = 8;
+
+// One warp per query: exact metric of each shortlisted row (AVX2 order), k
+// best kept.  Certification: every approximate value is within E of the
+// exact one (fp16 rounding of both operands, fp32 accumulation, and the
+// rounding of the exact computation itself).  A row outside the shortlist
+// has approximate value >= B, where B is the last shortlisted value if the
+// query had at least kp candidates and tau otherwise; so if the exact k-th
+// value + E < B no such row can be in the exact top-k.  Overflowing
+// candidate arrays are never certified.
+template <int P>
+__global__ void __launch_bounds__(BRS_WARPS * 32)
+    bf_rescore_kernel(const float* __restrict__ Q, int nq, const float* __restrict__ X, int dim,
+                      const float* __restrict__ qnorm, float xmax, int metric,
+                      uint64_t tag_base, const uint64_t* __restrict__ approx, int kp, int k,
+                      const unsigned* __restrict__ cand_cnt, int cap,
+                      const float* __restrict__ tau, uint64_t* __restrict__ out,
+                      uint32_t* flag_count, uint32_t* flag_list) {
+    __shared__ uint64_t buf[BRS_WARPS * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * BRS_WARPS + warp;
+    if (q >= nq) return;
+    const float* qv = Q + (size_t)q * dim;
+    const uint64_t* ak = approx + (size_t)q * kp;
+    WarpTopK<P> tk;
+    tk.init(k, buf + warp * 64);
+    const bool l2 = metric == EUCLIDEAN || metric == EUCLIDEAN_SQUARED;  // rank by L2^2
+    for (int base = 0; base < kp; base += 32) {
+        const int i = base + lane;
+        const uint64_t key = i < kp ? ak[i] : KEY_NONE;
+        uint64_t ek = KEY_NONE;
+        if (key != KEY_NONE) {
+            const uint32_t tag = key_tag(key);
+            const float* xv = X + (size_t)(tag - tag_base) * dim;
+            float d;
+            if (l2) d = l2sq_exact(qv, xv, dim);
+            else if (metric == DOT_PRODUCT) d = -dot_exact(qv, xv, dim);
+            else d = cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
+            ek = make_key(d, tag);
+        }
+        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
+    }
+    const double qn = (double)qnorm[q];
+    const double qlen = sqrt(qn);
+    const double xm = (double)xmax;
+    double E;
+    if (l2) E = 2.5e-3 * qlen * xm + 1e-5 * (qn + xm * xm);
+    else if (metric == DOT_PRODUCT) E = 1.25e-3 * qlen * xm;
+    else E = 1.25e-3 + 1e-5;
+    const unsigned c = cand_cnt[q];
+    double B;
+    if (c >= (unsigned)kp) B = (double)key_dist(ak[kp - 1]);
+    else B = (double)tau[q];  // +inf when the sample saw fewer than 32 rows
+    bool cert = c <= (unsigned)cap;
+    if (cert && !isinf(B)) cert = tk.thr != KEY_NONE && ((double)key_dist(tk.thr) + E < B);
+    if (cert && isinf(B) && c < (unsigned)k) cert = true;  // every row was a candidate
+    if (metric == EUCLIDEAN) {
+#pragma unroll
+        for (int e = 0; e < P; ++e)
+            if (tk.L[e] != KEY_NONE)
+                tk.L[e] = make_key(__fsqrt_rn(key_dist(tk.L[e])), key_tag(tk.L[e]));
+    }
+    tk.store(out + (size_t)q * k);
+    if (!cert && lane == 0) {
+        const uint32_t idx = atomicAdd(flag_count, 1u);
+        flag_list[idx] = (uint32_t)q;
+    }
+}
+
+void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, int dim,
+                       const float* qnorm, float xmax, int metric, uint64_t tag_base,
+                       const GemmScratch& w, int kp, int k, uint64_t* out, uint32_t* flag_count,
+                       uint32_t* flag_list) {
+    if (nq == 0) return;
+    unsigned grid = (unsigned)((nq + BRS_WARPS - 1) / BRS_WARPS);
+#define FDB_BRS(PP)                                                                           \
+    bf_rescore_kernel<PP><<<grid, BRS_WARPS * 32, 0, s>>>(                                    \
+        Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, w.cap, \
+        w.tau.p, out, flag_count, flag_list)
+    if (k <= 32) FDB_BRS(1);
+    else if (k <= 64) FDB_BRS(2);
+    else if (k <= 128) FDB_BRS(4);
+    else FDB_BRS(8);
+#undef FDB_BRS
+    FDB_LAUNCH_CHECK();
+}
+
+}  // namespace fdb

@@ -106,6 +106,7 @@ _SIGS = {
     "fdb_bf_create": (C.c_int, [_vp, C.c_int, _vp, _vp, _sz, _sz, C.POINTER(_vp)]),
     "fdb_bf_add": (C.c_int, [_vp, _vp, _vp, _sz, _sz]),
     "fdb_bf_shard": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "fdb_bf_set_scan_mode": (C.c_int, [_vp, C.c_int]),
     "fdb_bf_len": (_sz, [_vp]),
     "fdb_bf_dimension": (_sz, [_vp]),
     "fdb_bf_search": (C.c_int, [_vp, _vp, _sz, _vp, _vp, C.POINTER(_sz)]),
@@ -484,6 +485,9 @@ class BruteForceIndex:
 
     def shard(self, rank: int, world: int):
         _check(lib().fdb_bf_shard(self.h, rank, world))
+
+    def set_scan_mode(self, mode: int):
+        _check(lib().fdb_bf_set_scan_mode(self.h, mode))
 
     def len(self) -> int:
         return lib().fdb_bf_len(self.h)

@@ -221,6 +221,12 @@ int fdb_bf_create(fdb_ctx* ctx, int metric, const float* x, const uint64_t* ids,
 int fdb_bf_add(fdb_bf* h, const float* x, const uint64_t* ids, size_t n, size_t dim);
 /* Keep only this rank's contiguous share of the rows. */
 int fdb_bf_shard(fdb_bf* h, int rank, int world);
+/* Scan mode (FDB_SCAN_*); no reference counterpart.  TABLES/AUTO use the
+ * tcgen05 tensor-core shortlist (fp16 operands, fp32 accumulation) for every
+ * metric but Manhattan, dims <= 256 and k <= 128, then rescore the shortlist
+ * exactly and certify it; EXACT scans every row in the AVX2 order.  Results
+ * are identical in every mode. */
+int fdb_bf_set_scan_mode(fdb_bf* h, int mode);
 size_t fdb_bf_len(const fdb_bf* h);
 size_t fdb_bf_dimension(const fdb_bf* h); /* 0 when empty (brute_force.rs:92-99) */
 /* BruteForceIndex::search / search_parallel (brute_force.rs:162-214). */

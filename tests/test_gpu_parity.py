@@ -292,3 +292,36 @@ def test_table_mode_ties_fall_back_to_exact(fg, ctx, orc):
     assert st.exact_rescans > 0
     oi, od, oc = ox.batch_search(Q, 10)
     assert_topk_match(ids, d, cnt, oi, od, oc, "ties")
+
+
+# ---------------------------------------------------------------------------
+# brute force: tcgen05 tensor-core shortlist + exact rescoring
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("metric", [0, 1, 2, 3])
+def test_bf_tensor_path_certifies_and_matches(fg, ctx, orc, metric):
+    rng = np.random.default_rng(100 + metric)
+    X = rng.standard_normal((60000, 128)).astype(np.float32)
+    Q = rng.standard_normal((300, 128)).astype(np.float32)
+    bf = fg.BruteForceIndex(metric, ctx).add(X)
+    for k in (10, 100):
+        ids, d, cnt, st = bf.batch_search_arrays(Q, k, stats=True)
+        assert st.exact_rescans <= len(Q) // 20, f"tensor path fell back {st.exact_rescans}x"
+        oi, od, oc = orc.bf_batch_search(X, np.arange(60000), metric, Q, k)
+        assert_topk_match(ids, d, cnt, oi, od, oc, f"bf tensor metric={metric} k={k}")
+    bf.set_scan_mode(1)
+    ids2, d2, c2 = bf.batch_search_arrays(Q, 10)
+    bf.set_scan_mode(0)
+    ids1, d1, c1 = bf.batch_search_arrays(Q, 10)
+    assert np.array_equal(d1, d2)
+
+
+@pytest.mark.parametrize("n,dim,nq", [(129, 64, 1), (1000, 96, 130), (5000, 200, 257)])
+def test_bf_tensor_ragged_shapes(fg, ctx, orc, n, dim, nq):
+    """Row counts and query counts off the 128 tile, dims padded to 64/256."""
+    rng = np.random.default_rng(n)
+    X = rng.standard_normal((n, dim)).astype(np.float32)
+    Q = rng.standard_normal((nq, dim)).astype(np.float32)
+    bf = fg.BruteForceIndex(1, ctx).add(X)
+    ids, d, cnt = bf.batch_search_arrays(Q, 32)
+    oi, od, oc = orc.bf_batch_search(X, np.arange(n), 1, Q, 32)
+    assert_topk_match(ids, d, cnt, oi, od, oc, f"bf ragged n={n}")
