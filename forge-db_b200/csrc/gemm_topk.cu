@@ -77,19 +77,30 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps in hardware until
+// the phase completes or about a millisecond passes, instead of spinning.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return done != 0;
+}
 // Bounded wait.  Returns false if the kernel is aborting (this or another
-// warp timed out).  The error word and the clock are polled every 64 tries.
+// warp timed out).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try(bar, parity)) return true;
     const unsigned long long t0 = clock64();
-    for (unsigned it = 1;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 63) == 0) {
-            if (*(volatile int*)err) return false;
-            if (clock64() - t0 > WAIT_CYCLES) {
-                atomicExch(err, 1);
-                return false;
-            }
+    for (;;) {
+        if (mbar_try_sleep(bar, parity)) return true;
+        if (*(volatile int*)err) return false;
+        if (clock64() - t0 > WAIT_CYCLES) {
+            atomicExch(err, 1);
+            return false;
         }
     }
 }
@@ -137,6 +148,23 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -159,6 +187,7 @@ struct GemmTopkParams {
     int metric;
     const float* qnorm;  // [nq] exact squared norms
     const float* colv;   // per-row column values (see column_values), padded to whole tiles
+    float colmax;        // L2: largest ||x||^2 (bounds the filter test's rounding)
     size_t rows_per_chunk;
     uint64_t tag_base;   // global index of row 0
     // SAMPLE pass
@@ -340,6 +369,83 @@ __global__ void __launch_bounds__(THREADS, 1)
                                       : __int_as_float(0x7f800000);
         int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
         uint64_t* mybuf = cbuf + e * BUF_CAP;
+        if constexpr (EPI == EPI_FILTER) {
+            // Per-lane admission test, one or two instructions per score:
+            //   L2 : fma(-2, s, ||x||^2) <= (tau - ||q||^2) + slack
+            //   DOT: s >= -tau                              (exact)
+            //   COS: s / ||x|| >= (1 - tau) ||q|| - slack, or a zero row
+            // The slack covers the different rounding of the rearranged test,
+            // so every row whose key distance (approx_metric) is <= tau passes;
+            // hits are re-checked with approx_metric before they are appended.
+            float tt;
+            if (!qok) {
+                tt = MET == MET_DOT ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
+            } else if (MET == MET_L2) {
+                tt = (tau - qn) + ldexpf(2.0f * fabsf(qn) + 2.0f * p.colmax + fabsf(tau), -20);
+            } else if (MET == MET_DOT) {
+                tt = -tau;
+            } else {
+                tt = qn == 0.0f ? -__int_as_float(0x7f800000)
+                                : ((1.0f - tau) - ldexpf(2.0f + fabsf(tau), -18)) / qn;
+            }
+            for (int i = 0; i < count; ++i) {
+                const int b = i & 1;
+                int got = 0;
+                if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) break;
+                tc_fence_after();
+                const size_t rb = r0 + (size_t)i * TILE_N;
+                uint32_t va[32], vb[32];
+                float ca[32], cbv[32];
+                const size_t rowa = rb + (size_t)c0 * 32, rowb = rowa + 32;
+                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + c0 * 32), va);
+                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + c0 * 32 + 32), vb);
+                column_values<MET>(p.colv, rowa, ca);
+                column_values<MET>(p.colv, rowb, cbv);
+                tmem_wait_ld();
+                // both chunks are in registers: release the accumulator now
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(t_empty + b);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t* v = h == 0 ? va : vb;
+                    const float* cv = h == 0 ? ca : cbv;
+                    const size_t cb = h == 0 ? rowa : rowb;
+                    auto fast = [&](int j) -> bool {
+                        const float s = __uint_as_float(v[j]);
+                        if (MET == MET_L2) return __fmaf_rn(-2.0f, s, cv[j]) <= tt;
+                        if (MET == MET_DOT) return s >= tt;
+                        return (s * cv[j] >= tt) || (cv[j] == 0.0f);
+                    };
+                    // A warp covers 32 queries x 32 rows per chunk, so it meets a
+                    // hit often; testing 8-row groups keeps the exact re-check
+                    // (and its divergence) to the groups that hold one.
+                    const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
+                    const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        bool any = false;
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) any |= fast(g * 8 + jj);
+                        if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+                            for (int jj = 0; jj < 8; ++jj) {
+                                const int j = g * 8 + jj;
+                                const float d =
+                                    approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                                if (qok && j < nvalid && d <= tau) {
+                                    const unsigned idx = atomicAdd(p.cand_cnt + q, 1u);
+                                    if (idx < (unsigned)p.cap)
+                                        p.cand[(size_t)q * p.cap + idx] = make_key(d, tag0 + j);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        } else
         for (int i = 0; i < count; ++i) {
             const int b = i & 1;
             // one lane waits; the warp follows its verdict (tcgen05.ld is warp-wide)
@@ -597,7 +703,7 @@ void launch_to_half(cudaStream_t s, const float* x, size_t n, int dim, int kpad,
 // carved from the caller's buffers (sizes from gemm_shortlist_scratch).
 void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnorm,
                     const __half* x16, size_t n, int kpad, const float* colv, int metric,
-                    uint64_t tag_base, int kp, int sm_count, GemmScratch& w) {
+                    uint64_t tag_base, int kp, int sm_count, float colmax, GemmScratch& w) {
     FDB_REQUIRE(kpad % tc::KATOM == 0 && kpad <= 256, FDB_ERR_UNSUPPORTED, "bad padded dim");
     FDB_REQUIRE(kp >= 1 && kp <= 256, FDB_ERR_UNSUPPORTED, "shortlist too long");
     CUtensorMap qm = make_map(q16, (size_t)nq, kpad);
@@ -615,6 +721,7 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     p.metric = metric;
     p.qnorm = qnorm;
     p.colv = colv;
+    p.colmax = colmax;
     p.rows_per_chunk = rows_per_chunk;
     p.tag_base = tag_base;
     p.err = w.err;
