@@ -24,12 +24,33 @@ HEADERS = ["fdb_device.cuh", "fdb_internal.h", "fdb_kernels.h"]
 
 NVCC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _nccl_home() -> tuple[str, str]:
+    """(include dir, lib dir) of the NCCL to build against.
+
+    PyTorch ships its own libnccl.so.2 (the nvidia-nccl wheel).  A process
+    that loads a second libnccl.so.2 first (the system one) breaks torch's
+    later import with missing symbols, so link the wheel's copy when it is
+    there: both libraries then share one NCCL."""
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec is not None and spec.submodule_search_locations:
+        for base in spec.submodule_search_locations:
+            inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+            if os.path.exists(os.path.join(inc, "nccl.h")) and os.path.exists(
+                    os.path.join(lib, "libnccl.so.2")):
+                return inc, lib
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
+NCCL_INC, NCCL_LIB = _nccl_home()
 # -fmad=false: no compiler contraction of a*b+c; every fused multiply-add in
 # the kernels is an explicit __fmaf_rn, so summation orders match the
 # reference's AVX2 arithmetic bit for bit.
 FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC,-O2",
-                "-ccbin", "g++", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
-NCCL_LIB = "/usr/lib/x86_64-linux-gnu"
+                "-ccbin", "g++", "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+                "-I", NCCL_INC]
 
 
 def _newer(target: str, deps: list[str]) -> bool:
@@ -57,7 +78,8 @@ def build(jobs: int = 8, force: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, force), SOURCES))
     if force or _newer(OUT, objs):
         cmd = [NVCC] + ARCH + ["-shared", "-o", OUT + ".tmp"] + objs + [
-            "-cudart", "static", "-L", NCCL_LIB, "-lnccl", "-Xlinker", "-rpath," + NCCL_LIB]
+            "-cudart", "static", "-L", NCCL_LIB, "-l:libnccl.so.2", "-Xlinker",
+            "-rpath," + NCCL_LIB]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

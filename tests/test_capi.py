@@ -25,6 +25,18 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(fg.exported_symbols())
 
 
+def test_torch_imports_after_the_library():
+    # the library and torch must resolve to one libnccl.so.2; loading the
+    # library first used to break torch's import with missing NCCL symbols
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); import forgegpu as fg; fg.lib(); "
+            "import torch; print('ok')" % os.path.join(ROOT, "forge-db_b200"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
 def test_version_and_error_string():
     import forgegpu as fg
     assert fg.lib().fdb_version() >= 100
