@@ -285,6 +285,65 @@ int fdb_find_nearest_centroids(fdb_ctx* ctx, const float* centroids, size_t kc, 
     });
 }
 
+}  // extern "C"
+
+// Distance matrix of fdb_find_nearest_centroids_noalloc.  It is part of the
+// library's device image (reserved when the module loads on a device), so
+// that entry point never allocates.  The distance kernel writes every entry
+// the selection reads, so nothing in it has to start at zero.
+static __device__ __align__(256) float g_noalloc_dist[FDB_NOALLOC_MAX_DISTANCES];
+
+namespace {
+
+// Address of g_noalloc_dist on `device`, looked up once per device with that
+// device current (the caller's DeviceGuard) and remembered afterwards.
+float* noalloc_scratch(int device) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static float* table[kMaxDevices] = {};
+    FDB_REQUIRE(device >= 0 && device < kMaxDevices, FDB_ERR_UNSUPPORTED,
+                "device ordinal above 63");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!table[device]) {
+        void* p = nullptr;
+        FDB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_dist));
+        FDB_REQUIRE(p != nullptr, FDB_ERR_CUDA, "scratch symbol has no device address");
+        table[device] = static_cast<float*>(p);
+    }
+    return table[device];
+}
+
+}  // namespace
+
+extern "C" {
+
+int fdb_find_nearest_centroids_noalloc(fdb_ctx* ctx, const float* d_centroids, size_t kc,
+                                       size_t dim, const float* d_queries, size_t nq, size_t k,
+                                       uint32_t* d_out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx, FDB_ERR_INVALID_ARG, "NULL context");
+        const size_t take = std::min(k, kc);
+        const bool work = nq > 0 && take > 0;
+        FDB_REQUIRE(nq <= FDB_NOALLOC_MAX_QUERIES, FDB_ERR_INVALID_ARG,
+                    "nq above FDB_NOALLOC_MAX_QUERIES (262144); split the queries into batches");
+        FDB_REQUIRE(kc <= FDB_NOALLOC_MAX_DISTANCES &&
+                        (kc == 0 || nq <= FDB_NOALLOC_MAX_DISTANCES / kc),
+                    FDB_ERR_INVALID_ARG,
+                    "nq * kc above FDB_NOALLOC_MAX_DISTANCES (4194304 distances, the fixed "
+                    "scratch); split the queries into batches");
+        FDB_REQUIRE(!work || (d_centroids && d_queries && d_out), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        DeviceGuard g(ctx->c.device);
+        float* D = noalloc_scratch(ctx->c.device);  // set-up, also on an empty call
+        if (!work) return;
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        cudaStream_t s = ctx->c.stream;
+        launch_coarse_dist(s, d_queries, (int)nq, (int)dim, d_centroids, (int)kc, D);
+        launch_select(s, D, (int)nq, (int)kc, (int)take, d_out);
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
 // ---------------------------------------------------------------------------
 // product quantizer
 // ---------------------------------------------------------------------------

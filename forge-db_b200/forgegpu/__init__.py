@@ -81,6 +81,7 @@ _SIGS = {
                                  C.POINTER(C.c_int)]),
     "fdb_assign": (C.c_int, [_vp, _vp, _sz, _vp, _sz, _sz, _vp]),
     "fdb_find_nearest_centroids": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp]),
+    "fdb_find_nearest_centroids_noalloc": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _sz, _vp]),
     "fdb_pq_train": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, C.c_uint64, _vp, _vp]),
     "fdb_pq_encode": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp]),
     "fdb_pq_lookup_tables": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp]),

@@ -152,6 +152,28 @@ int fdb_assign(fdb_ctx* ctx, const float* x, size_t n, const float* centroids, s
 int fdb_find_nearest_centroids(fdb_ctx* ctx, const float* centroids, size_t kc, size_t dim,
                                const float* query, size_t k, uint32_t* out);
 
+/* No reference counterpart.  For callers that must not allocate device
+ * memory at call time: the nearest-centroid search of
+ * fdb_find_nearest_centroids for nq queries at once, on device buffers
+ * (d_centroids[kc][dim], d_queries[nq][dim] -> d_out[nq][min(k, kc)], each
+ * row ascending, same ids as the host-buffer call).  Its only scratch, the
+ * nq x kc distance matrix, lives in a fixed array in the library's device
+ * image, so the call itself never allocates.
+ *   - nq * kc must not exceed FDB_NOALLOC_MAX_DISTANCES (16 MiB of floats)
+ *     and nq must not exceed FDB_NOALLOC_MAX_QUERIES; larger requests fail
+ *     with FDB_ERR_INVALID_ARG and nothing runs.  Split them into batches.
+ *   - The first call on a device looks up the scratch address; make it
+ *     (nq = 0 is enough) before any stream capture.  The call waits for its
+ *     own stream, so it cannot itself be captured.
+ *   - There is one scratch array per device: calls that overlap on a device
+ *     (two contexts, or two threads with separate contexts) race on it.
+ *     Calls through one context are serialised. */
+#define FDB_NOALLOC_MAX_DISTANCES (1u << 22)
+#define FDB_NOALLOC_MAX_QUERIES (1u << 18)
+int fdb_find_nearest_centroids_noalloc(fdb_ctx* ctx, const float* d_centroids, size_t kc,
+                                       size_t dim, const float* d_queries, size_t nq, size_t k,
+                                       uint32_t* d_out);
+
 /* ---- ProductQuantizer (src/pq.rs:33-245) -------------------------------- */
 /* ProductQuantizer::try_train (pq.rs:55-95): codebooks_out[m][256][dim/m].
  * init_idx[m*256] (NULL -> seed) are the per-subspace initial picks. */
