@@ -117,11 +117,15 @@ def make_data():
     return X, Q
 
 
+SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
+
+
 def config_dict(args, world, extra=None):
     d = {"workload": "ivfpq_config_c", "n_base": N_BASE, "dim": DIM, "nlist": NLIST, "m": M,
          "nprobe": args.nprobe, "global_batch": N_QUERY, "k": K,
          "data": "seeded GMM descriptor-like (1024 centres U[0,255], sigma 20, clipped, rounded)",
          "parallelism": (f"lists{world}" if args.mode == "lists" else f"replicas{world}"),
+         "scan_mode": args.scan_mode,
          "l2": "flushed between steps (256 MB write outside the timed window)"}
     if extra:
         d.update(extra)
@@ -223,6 +227,7 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
     build_s = time.time() - t0
     ix.set_nprobe(args.nprobe)
+    ix.set_scan_mode(SCAN_MODES[args.scan_mode])
     if world > 1 and args.mode == "lists":
         ix.shard(rank, world)
         Qr = Q
@@ -472,6 +477,8 @@ def main():
     ap.add_argument("--nprobe", type=int, default=32)
     ap.add_argument("--mode", default="lists", choices=["lists", "replicas"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scan-mode", default="auto", choices=list(SCAN_MODES),
+                    help="IVF-PQ scan mode (auto picks the tensor-core list scan here)")
     ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "bf"])
     ap.add_argument("--bf-metric", default="l2sq", choices=["l2sq", "dot", "cosine", "l2"])
     ap.add_argument("--bf-n", type=int, default=1_000_000, help="rows (smaller for profiling)")

@@ -513,7 +513,7 @@ int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe) {
 int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode) {
     return guarded([&] {
         FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
-        FDB_REQUIRE(mode >= FDB_SCAN_AUTO && mode <= FDB_SCAN_TABLES, FDB_ERR_INVALID_ARG,
+        FDB_REQUIRE(mode >= FDB_SCAN_AUTO && mode <= FDB_SCAN_TENSOR, FDB_ERR_INVALID_ARG,
                     "unknown scan mode");
         std::lock_guard<std::mutex> lk(h->mu);
         h->scan_mode = mode;

@@ -209,6 +209,8 @@ static void ivfpq_prepare_tables(fdb_ivfpq* h) {
     h->btab.release();
     h->cmax.release();
     h->bmax.release();
+    h->dec16.release();
+    h->dnorm.release();
     if (sub < 8) return;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -245,6 +247,7 @@ static void ivfpq_prepare_tables(fdb_ivfpq* h) {
     FDB_CUDA(cudaMemcpyAsync(h->cmax.p, cmax.data(), m * 4, cudaMemcpyHostToDevice, s));
     FDB_CUDA(cudaMemcpyAsync(h->bmax.p, bmax.data(), m * 4, cudaMemcpyHostToDevice, s));
     FDB_CUDA(cudaStreamSynchronize(s));
+    ivf_tc_prepare(h, cb, bmax);
 }
 
 void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_t* offsets,
@@ -380,9 +383,16 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         tm.mark();
         h->s_stat.ensure(2);
         FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 16, s));
+        const uint64_t* lbeg = h->sharded ? h->shard_be.p : h->offs.p;
+        const uint64_t* lend = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
+        // Tensor mode: lists scored on the tensor cores into a shortlist,
+        // exact rescoring + certification; failures are re-scanned exactly.
+        const bool tensor = ivf_tc_eligible(h, k) &&
+                            (h->scan_mode == FDB_SCAN_TENSOR ||
+                             (h->scan_mode == FDB_SCAN_AUTO && nq >= 256));
         // Table mode: approximate scan into a shortlist of kp keys, then
         // exact rescoring + certification; failures are re-scanned exactly.
-        const bool tables = h->btab.p && h->scan_mode != FDB_SCAN_EXACT && k <= 128;
+        const bool tables = !tensor && h->btab.p && h->scan_mode != FDB_SCAN_EXACT && k <= 128;
         const size_t kp = tables ? std::min<size_t>(FDB_MAX_K, std::max<size_t>(32, 2 * k)) : k;
         if (tables) h->s_approx.ensure(nq * kp);
         ScanParams a{};
@@ -392,8 +402,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         a.m = (int)h->m;
         a.cents = h->cents.p;
         a.cb = h->cb.p;
-        a.offs = h->sharded ? h->shard_be.p : h->offs.p;
-        a.ends = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
+        a.offs = lbeg;
+        a.ends = lend;
         a.codes = h->codes.p;
         a.probes = h->s_probe.p;
         a.nprobe = (int)take;
@@ -401,8 +411,26 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         a.out_keys = tables ? h->s_approx.p : h->s_keys.p;
         a.stat = h->s_stat.p;
         a.btab = tables ? h->btab.p : nullptr;
-        launch_scan(s, a, order);
-        tm.mark();
+        if (tensor) {
+            h->s_flags.ensure(nq + 1);
+            const uint32_t nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend,
+                                                 h->s_keys.p, h->s_flags.p, h->s_stat.p);
+            tm.mark();
+            if (nflag > 0) {
+                ScanParams e = a;
+                e.nq = (int)nflag;
+                e.qidx = h->s_flags.p + 1;
+                e.k = (int)k;
+                e.out_keys = h->s_keys.p;
+                e.stat = nullptr;
+                e.btab = nullptr;
+                launch_scan(s, e, order);
+            }
+            if (st) st->exact_rescans = nflag;
+        } else {
+            launch_scan(s, a, order);
+            tm.mark();
+        }
         if (tables) {
             h->s_flags.ensure(nq + 1);
             FDB_CUDA(cudaMemsetAsync(h->s_flags.p, 0, 4, s));

@@ -175,6 +175,69 @@ __device__ __forceinline__ uint64_t warp_sort32(uint64_t c, int lane) {
 }
 
 // Entry i of the sorted list lives in register i / 32 of lane i % 32.
+// ADC of one code in the requested order; `lk(i)` returns LUT[i][code[i]].
+template <int ORDER, class F>
+__device__ __forceinline__ float adc_order(F lk, int m) {
+    if (ORDER == ORDER_LANE8) {
+        const int full = m & ~7;
+        float total = 0.0f;
+        if (full > 0) {
+            float acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = lk(j);
+            for (int i = 8; i < full; i += 8) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], lk(i + j));
+            }
+            total = lane_sum(acc);
+        }
+        for (int i = full; i < m; ++i) total = __fadd_rn(total, lk(i));
+        return total;
+    } else {
+        float sum = 0.0f;
+        int i = 0;
+        for (; i + 4 <= m; i += 4) {
+            float g = __fadd_rn(__fadd_rn(__fadd_rn(lk(i), lk(i + 1)), lk(i + 2)), lk(i + 3));
+            sum = __fadd_rn(sum, g);
+        }
+        for (; i < m; ++i) sum = __fadd_rn(sum, lk(i));
+        return sum;
+    }
+}
+
+// Exact ADC of one code: every LUT entry recomputed as L2^2(fl(q - c) - b)
+// in the AVX2 order and summed in the requested order -- the same
+// operations, in the same order, as the exact-mode scan.
+template <int ORDER>
+__device__ __forceinline__ float exact_adc(const float* __restrict__ q,
+                                           const float* __restrict__ c,
+                                           const float* __restrict__ cb,
+                                           const uint8_t* __restrict__ code, int m, int sub) {
+    auto entry = [&](int s) -> float {
+        const float* b = cb + ((size_t)s * KSUB + code[s]) * sub;
+        const float* qs = q + s * sub;
+        const float* cs = c + s * sub;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        int i = 0;
+        for (; i + 8 <= sub; i += 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float d = __fsub_rn(__fsub_rn(__ldg(qs + i + j), __ldg(cs + i + j)), __ldg(b + i + j));
+                acc[j] = __fmaf_rn(d, d, acc[j]);
+            }
+        }
+        float t = lane_sum(acc);
+        for (; i < sub; ++i) {
+            float d = __fsub_rn(__fsub_rn(__ldg(qs + i), __ldg(cs + i)), __ldg(b + i));
+            t = __fadd_rn(t, __fmul_rn(d, d));
+        }
+        return t;
+    };
+    return adc_order<ORDER>(entry, m);
+}
+
 template <int P>
 struct WarpTopK {
     static constexpr int K = 32 * P;

@@ -221,6 +221,13 @@ void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_
 void ivfpq_shard(fdb_ivfpq* h, int rank, int world);
 void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
                       uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st);
+// ivf_tc.cu: tensor-core list scan (see there)
+bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k);
+void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
+                    const std::vector<float>& bmax_host);
+uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
+                       size_t take, const uint64_t* lbeg, const uint64_t* lend,
+                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat);
 void bf_upload(fdb_bf* h);
 void bf_shard(fdb_bf* h, int rank, int world);
 void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
@@ -255,6 +262,17 @@ struct fdb_ivfpq {
     int scan_mode = FDB_SCAN_AUTO;
     fdb::DevBuf<float> btab;            // [nlist][m][256]
     fdb::DevBuf<float> cmax, bmax;      // [m]
+    // tensor mode (dim <= 128 after padding): codes decoded to fp16 residual
+    // vectors scaled by 2^tc_sb, their squared norms, and lists by length
+    fdb::DevBuf<__half> dec16;          // [tc_rows][tc_dpad], lists 128-row aligned
+    fdb::DevBuf<float> dnorm;           // [tc_rows] ||rhat||^2, +inf in padding rows
+    fdb::DevBuf<uint32_t> lorder;       // [nlist] lists by decreasing length
+    fdb::DevBuf<uint32_t> tc_pstart;    // [nlist] first row of each list, 128-row aligned
+    fdb::DevBuf<float> tc_rhl;          // [nlist] upper bound of ||rhat|| per list
+    int tc_dpad = 0, tc_sb = 0;
+    size_t tc_rows = 0;                 // rows of the padded layout
+    size_t tc_maxpad = 0;               // longest padded list
+    float tc_colmax = 0.0f;             // upper bound of ||rhat||^2
     std::mutex mu;
     // per-call scratch
     fdb::DevBuf<float> s_q, s_coarse;
@@ -263,6 +281,15 @@ struct fdb_ivfpq {
     fdb::DevBuf<float> s_dists;
     fdb::DevBuf<uint32_t> s_counts, s_flags;
     fdb::DevBuf<unsigned long long> s_stat;
+    // tensor-mode scratch: pair grouping, residual rows, items, shortlists
+    fdb::DevBuf<uint32_t> t_keys, t_vals, t_cnt, t_off, t_pq, t_qbad, t_range, t_inv1, t_plen,
+        t_seg;
+    fdb::DevBuf<float> t_dump;
+    fdb::DevBuf<uint8_t> t_tmp, t_items;
+    fdb::DevBuf<__half> t_a16;
+    fdb::DevBuf<float> t_rn, t_s2, t_tau;
+    fdb::DevBuf<uint64_t> t_part, t_cand;
+    fdb::DevBuf<unsigned> t_cand_cnt;
 };
 
 struct fdb_bf {

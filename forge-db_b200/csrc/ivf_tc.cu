@@ -1,0 +1,1104 @@
+// ivf_tc.cu -- tensor-core (tcgen05) scan of IVF-PQ inverted lists.
+//
+// A batch search probes `take` lists per query.  The (query, list) pairs are
+// grouped by list.  For list l, the residual queries r = fl(q - c_l) (one
+// fp16 row per pair, scaled by a power of two) are multiplied on the tensor
+// cores with the list's decoded codes rhat = [b_{0,code_0} .. b_{m-1,code_m-1}]
+// (fp16, decoded once per index), and every score becomes
+//     d~ = ||r||^2 + ||rhat||^2 - 2 <r, rhat>
+// with ||r||^2 the exact coarse distance and ||rhat||^2 precomputed per code:
+// the reference's ADC distance (ivf_pq.rs:1005-1040, pq.rs:435-485) as a real
+// number, with different rounding.  Two passes, as in the brute-force
+// shortlist:
+//   pass 1: each query's first probed list holding 64+ codes (else its first
+//     non-empty one).  Every pair row keeps its top-64 in shared memory; the
+//     64th distance is the query's admission threshold tau.
+//   pass 2: the other probed lists.  A score costs one FMA and a compare;
+//     scores <= tau are appended to a per-query candidate array.
+// The top-64 of (pass-1 list + candidates) are rescored with the reference's
+// exact LUT sums (bit for bit, in the requested order) and certified against
+// a worst-case bound of the fp16/fp32 rounding (see certify_kernel); queries
+// that fail are re-scanned exactly by the caller.
+//
+// Decoded codes live in a padded copy of the list layout in which every list
+// starts on a 128-row boundary, so a B tile never mixes two lists and the
+// tile's ||rhat||^2 values (512 bytes, aligned) are staged into shared memory
+// by a bulk copy next to the tile itself.
+//
+// Work is split into items (one list x up to 128 pair rows).  A persistent
+// grid of one CTA per SM takes items in a fixed snake order over a list order
+// sorted by decreasing list length, so concurrent CTAs share a list's codes
+// in L2 and the long lists start first.  Warp roles as in the brute-force
+// kernel: warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner, warps
+// 4.. = epilogue; every mbarrier wait is bounded and an abort drains the
+// in-flight copies and MMAs before TMEM is freed.
+#include <cub/cub.cuh>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+
+#include "fdb_device.cuh"
+#include "fdb_internal.h"
+#include "fdb_kernels.h"
+#include "tc_ptx.cuh"
+
+namespace fdb {
+namespace ivtc {
+using namespace tc;
+
+constexpr int THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int LIST_K = 64;  // pass-1 list per query = shortlist length
+constexpr int EPI_DUMP = 0, EPI_FILTER = 1;
+constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
+constexpr float INF = __builtin_huge_valf();
+
+struct Item {
+    uint32_t a0;    // first pair row of the A tile
+    uint32_t na;    // pair rows in use (1..128)
+    uint32_t b0;    // first row of the list in the padded decoded layout
+    uint32_t nb;    // codes in the list (>= 1)
+    uint32_t tag0;  // row of the list's first code in the index (key tag)
+    uint32_t pad[3];
+};
+
+struct PassParams {
+    const Item* items;
+    const uint32_t* range;   // device-side {first item, item count} of this pass
+    int katoms;
+    const uint32_t* pair_q;  // [pairs] query of each pair row
+    const float* pair_rn;    // [pairs] ||q - c_l||^2 (the exact coarse distance)
+    const float* pair_s2;    // [pairs] -2 * 2^-(sa + sb): undoes both fp16 scalings
+    const float* colv;       // padded layout: ||rhat||^2, +inf in padding rows
+    float colmax;            // largest ||rhat||^2
+    float* dump;             // pass 1: every distance of each pair's list
+    const unsigned* seg;     // pass 1: [pairs] offset of the pair's row in dump
+    const float* tau;        // pass 2: [nq] admission threshold
+    uint64_t* cand;          // pass 2: [nq][cap] candidate keys
+    unsigned* cand_cnt;      // pass 2: [nq] candidates seen (may exceed cap)
+    int cap;
+    int* err;
+};
+
+constexpr int NSTAGE = 4;  // B tile stages
+constexpr int NEPI = 8;    // epilogue warps: 4 TMEM lane quadrants x 2 column halves
+constexpr int NCV = 4;     // ||rhat||^2 stages
+
+// Items of CTA `cta` in round r: left to right on even rounds, right to left
+// on odd ones, so each CTA's total stays close to the mean.
+__device__ __forceinline__ int snake(int r, int cta, int G) {
+    return r * G + ((r & 1) ? (G - 1 - cta) : cta);
+}
+
+// 32 consecutive floats of a shared buffer (warp-uniform address: broadcast).
+__device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 t = s4[i];
+        cv[4 * i] = t.x;
+        cv[4 * i + 1] = t.y;
+        cv[4 * i + 2] = t.z;
+        cv[4 * i + 3] = t.w;
+    }
+}
+
+// Bounded wait of one lane, verdict shared with the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int lane) {
+    int got = 0;
+    if (lane == 0) got = mbar_wait(bar, parity, err) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, got, 0) != 0;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    ivf_pass_kernel(const __grid_constant__ CUtensorMap amap,
+                    const __grid_constant__ CUtensorMap bmap, PassParams p) {
+    constexpr int NS = NSTAGE;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t base = smem_u32(smem_raw);
+    unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
+    const int KA = p.katoms;
+    const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
+    unsigned char* a_tile = smem;
+    unsigned char* b_tile = a_tile + KA * ATOM_BYTES;
+    float* cvbuf = reinterpret_cast<float*>(b_tile + NS * KA * ATOM_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(cvbuf + NCV * CV_FLOATS);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = bars + 1;
+    uint64_t* b_full = bars + 2;           // [NS]
+    uint64_t* b_empty = b_full + NS;       // [NS]
+    uint64_t* t_full = b_empty + NS;       // [2]
+    uint64_t* t_empty = t_full + 2;        // [2]
+    uint64_t* cv_full = t_empty + 2;       // [NCV]
+    uint64_t* cv_empty = cv_full + NCV;    // [NCV]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cv_empty + NCV);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const Item* items = p.items + p.range[0];
+    const int nitems = (int)p.range[1];
+
+    if (threadIdx.x == 0) {
+        mbar_init(a_full, 1);
+        mbar_init(a_empty, 1);
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(b_full + i, 1);
+            mbar_init(b_empty + i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(t_full + i, 1);
+            mbar_init(t_empty + i, NEPI);
+        }
+        for (int i = 0; i < NCV; ++i) {
+            mbar_init(cv_full + i, 1);
+            mbar_init(cv_empty + i, NEPI);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(2 * TILE_N));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // Last asynchronous operation each role issued, so that an aborting
+    // block can wait for it (bounded) before it frees TMEM and exits.
+    int last_use[NS], last_cv[NCV];
+#pragma unroll
+    for (int i = 0; i < NS; ++i) last_use[i] = -1;
+#pragma unroll
+    for (int i = 0; i < NCV; ++i) last_cv[i] = -1;
+    int last_a = -1;  // producer: last item whose A tile was requested
+    int last_g = -1;  // MMA issuer: last tile committed
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int r = 0; ok; ++r) {
+                const int idx = snake(r, cta, G);
+                if (idx >= nitems) break;
+                const Item it = items[idx];
+                if (r > 0 && !mbar_wait(a_empty, (r - 1) & 1, p.err)) break;
+                mbar_expect_tx(a_full, stage_bytes);
+                for (int a = 0; a < KA; ++a)
+                    tma_load_2d(a_tile + a * ATOM_BYTES, &amap, a_full, a * KATOM, (int)it.a0);
+                last_a = r;
+                const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int s = g % NS, use = g / NS;
+                    if (g >= NS && !mbar_wait(b_empty + s, (use - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t row = it.b0 + (uint32_t)t * TILE_N;
+                    mbar_expect_tx(b_full + s, stage_bytes);
+                    unsigned char* dst = b_tile + s * KA * ATOM_BYTES;
+                    for (int a = 0; a < KA; ++a)
+                        tma_load_2d(dst + a * ATOM_BYTES, &bmap, b_full + s, a * KATOM, (int)row);
+#pragma unroll
+                    for (int i = 0; i < NS; ++i)
+                        if (i == s) last_use[i] = use;
+                    const int c = g % NCV, cu = g / NCV;
+                    if (g >= NCV && !mbar_wait(cv_empty + c, (cu - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(cv_full + c, CV_FLOATS * 4);
+                    bulk_load(cvbuf + c * CV_FLOATS, p.colv + row, CV_FLOATS * 4, cv_full + c);
+#pragma unroll
+                    for (int i = 0; i < NCV; ++i)
+                        if (i == c) last_cv[i] = cu;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int r = 0; ok; ++r) {
+                const int idx = snake(r, cta, G);
+                if (idx >= nitems) break;
+                const Item it = items[idx];
+                const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
+                if (!mbar_wait(a_full, r & 1, p.err)) break;
+                tc_fence_after();
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int s = g % NS, use = g / NS, b = g & 1;
+                    if (g >= 2 && !mbar_wait(t_empty + b, ((g >> 1) - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    if (!mbar_wait(b_full + s, use & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)(b * TILE_N);
+                    const uint32_t abase = smem_u32(a_tile);
+                    const uint32_t bbase = smem_u32(b_tile + s * KA * ATOM_BYTES);
+                    for (int a = 0; a < KA; ++a) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {  // 4 x K16 per 64-wide atom
+                            const uint32_t off = (uint32_t)(a * ATOM_BYTES + kk * 32);
+                            umma_f16(d, smem_desc_sw128(abase + off),
+                                     smem_desc_sw128(bbase + off), (a | kk) != 0);
+                        }
+                    }
+                    umma_commit(b_empty + s);  // stage s may be refilled once these finish
+                    umma_commit(t_full + b);   // accumulator b is ready for the epilogue
+                    last_g = g;
+                }
+                if (ok) umma_commit(a_empty);  // the A tile may be replaced
+            }
+        }
+    } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + NEPI) {
+        // ---------------- epilogue ----------------
+        const int w = warp - EPI_WARP0;
+        const int quad = w & 3;  // TMEM lane quadrant = warp % 4
+        const int half = w >> 2;
+        const int e = quad * 32 + lane;  // pair row within the tile
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        int g = 0;
+        bool alive = true;
+        for (int r = 0; alive; ++r) {
+            const int idx = snake(r, cta, G);
+            if (idx >= nitems) break;
+            const Item it = items[idx];
+            const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
+            const bool rok = e < (int)it.na;
+            const uint32_t pr = it.a0 + (uint32_t)e;
+            const int q = rok ? (int)p.pair_q[pr] : 0;
+            const float rn = rok ? p.pair_rn[pr] : 0.0f;
+            const float s2 = rok ? p.pair_s2[pr] : 0.0f;
+            if constexpr (EPI == EPI_FILTER) {
+                const float tau = rok ? p.tau[q] : -INF;
+                // Admission test fma(s2, s, ||rhat||^2) <= (tau - rn) + slack: the
+                // slack covers the different rounding of the rearranged sum, so
+                // every code with d~ <= tau passes; hits are re-checked with d~.
+                const float tt =
+                    rok ? (tau - rn) + ldexpf(2.0f * fabsf(rn) + 2.0f * p.colmax + fabsf(tau), -20)
+                        : -INF;
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int b = g & 1, c = g % NCV;
+                    if (!warp_wait(t_full + b, (g >> 1) & 1, p.err, lane) ||
+                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t va[32], vb[32];
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32),
+                                     vb);
+                    float ca[32], cbv[32];
+                    load32(cvbuf + c * CV_FLOATS + half * 64, ca);
+                    load32(cvbuf + c * CV_FLOATS + half * 64 + 32, cbv);
+                    tmem_wait_ld();
+                    // both chunks are in registers: release the accumulator and values
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(t_empty + b);
+                        mbar_arrive(cv_empty + c);
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t* v = h == 0 ? va : vb;
+                        const float* cv = h == 0 ? ca : cbv;
+                        const int cidx = t * TILE_N + half * 64 + h * 32;
+                        const int nvalid = min(32, (int)it.nb - cidx);
+                        const uint32_t tag0 = it.tag0 + (uint32_t)cidx;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            bool any = false;
+#pragma unroll
+                            for (int jj = 0; jj < 8; ++jj) {
+                                const int j = g8 * 8 + jj;
+                                any |= __fmaf_rn(s2, __uint_as_float(v[j]), cv[j]) <= tt;
+                            }
+                            if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+                                for (int jj = 0; jj < 8; ++jj) {
+                                    const int j = g8 * 8 + jj;
+                                    const float d =
+                                        __fmaf_rn(s2, __uint_as_float(v[j]), __fadd_rn(rn, cv[j]));
+                                    if (rok && j < nvalid && d <= tau) {
+                                        const unsigned ix = atomicAdd(p.cand_cnt + q, 1u);
+                                        if (ix < (unsigned)p.cap)
+                                            p.cand[(size_t)q * p.cap + ix] = make_key(d, tag0 + j);
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+            } else {
+                // pass 1: every distance of the row's list goes to its dump row
+                float* drow = rok ? p.dump + p.seg[pr] : nullptr;
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int b = g & 1, c = g % NCV;
+                    if (!warp_wait(t_full + b, (g >> 1) & 1, p.err, lane) ||
+                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t va[32], vb[32];
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32),
+                                     vb);
+                    float ca[32], cbv[32];
+                    load32(cvbuf + c * CV_FLOATS + half * 64, ca);
+                    load32(cvbuf + c * CV_FLOATS + half * 64 + 32, cbv);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(t_empty + b);
+                        mbar_arrive(cv_empty + c);
+                    }
+                    if (rok) {
+                        // padding columns carry ||rhat||^2 = +inf and store +inf
+                        float4* dst = reinterpret_cast<float4*>(drow + t * TILE_N + half * 64);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t* v = h == 0 ? va : vb;
+                            const float* cv = h == 0 ? ca : cbv;
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                float4 o;
+                                o.x = __fmaf_rn(s2, __uint_as_float(v[4 * i]), __fadd_rn(rn, cv[4 * i]));
+                                o.y = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]),
+                                                __fadd_rn(rn, cv[4 * i + 1]));
+                                o.z = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]),
+                                                __fadd_rn(rn, cv[4 * i + 2]));
+                                o.w = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]),
+                                                __fadd_rn(rn, cv[4 * i + 3]));
+                                dst[h * 8 + i] = o;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (*(volatile int*)p.err) {
+        // aborting: let the copies and MMAs this block issued land before exit
+        // (waits on phases that already completed return at once)
+        if (warp == 0 && lane == 0) {
+            for (int s2 = 0; s2 < NS; ++s2)
+                if (last_use[s2] >= 0) {
+                    const unsigned long long t0 = clock64();
+                    while (!mbar_try(b_full + s2, last_use[s2] & 1) &&
+                           clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+            for (int c2 = 0; c2 < NCV; ++c2)
+                if (last_cv[c2] >= 0) {
+                    const unsigned long long t0 = clock64();
+                    while (!mbar_try(cv_full + c2, last_cv[c2] & 1) &&
+                           clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+            if (last_a >= 0) {
+                const unsigned long long t0 = clock64();
+                while (!mbar_try(a_full, last_a & 1) && clock64() - t0 < WAIT_CYCLES) {
+                }
+            }
+        }
+        if (warp == 1 && lane == 0 && last_g >= 0) {
+            const unsigned long long t0 = clock64();
+            while (!mbar_try(t_full + (last_g & 1), (last_g >> 1) & 1) &&
+                   clock64() - t0 < WAIT_CYCLES) {
+            }
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(2 * TILE_N));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// pair grouping
+// ---------------------------------------------------------------------------
+// Sort key of probe (q, p): its list for the query's pass-1 probe (the first
+// holding LIST_K+ codes, else the first non-empty one), nlist + list for the
+// query's other non-empty probes, 2 nlist for empty lists.  Also counts keys
+// and, when stat is given, lists and codes scanned.
+__global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, int take,
+                                 const uint64_t* __restrict__ lbeg,
+                                 const uint64_t* __restrict__ lend, int nlist,
+                                 uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                                 unsigned* __restrict__ counts, unsigned long long* stat) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    const uint32_t* pq = probes + (size_t)q * take;
+    int p1 = -1, pf = -1;
+    for (int j = 0; j < take && p1 < 0; ++j) {
+        const uint64_t len = lend[pq[j]] - lbeg[pq[j]];
+        if (len > 0 && pf < 0) pf = j;
+        if (len >= (uint64_t)LIST_K) p1 = j;
+    }
+    if (p1 < 0) p1 = pf;
+    unsigned long long lists = 0, codes = 0;
+    for (int j = 0; j < take; ++j) {
+        const size_t i = (size_t)q * take + j;
+        const uint32_t l = pq[j];
+        const uint64_t len = lend[l] - lbeg[l];
+        uint32_t key;
+        if (len == 0) {
+            key = 2u * (uint32_t)nlist;
+        } else {
+            key = j == p1 ? l : (uint32_t)nlist + l;
+            ++lists;
+            codes += len;
+        }
+        keys[i] = key;
+        vals[i] = (uint32_t)i;
+        atomicAdd(counts + key, 1u);
+    }
+    if (stat) {
+        atomicAdd(stat, lists);
+        atomicAdd(stat + 1, codes);
+    }
+}
+
+// One warp per sorted pair: the fp16 residual row r = fl(q - c_l) * 2^sa
+// (sa puts the largest |r_i| in [2^14, 2^15)), the coarse distance and the
+// combined scale -2 * 2^-(sa + sb).  Pairs whose scale leaves the float range
+// mark their query for the exact path.
+__global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
+                               int nlist, int take, const uint32_t* __restrict__ probes,
+                               const float* __restrict__ Q, const float* __restrict__ cents,
+                               int dim, int dpad, const float* __restrict__ coarse, int sb,
+                               __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
+                               float* __restrict__ pair_rn, float* __restrict__ pair_s2,
+                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv1) {
+    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned npairs = poff[2 * nlist];  // pairs with a non-empty list
+    if (i >= npairs) return;
+    const uint32_t v = vals[i];
+    const uint32_t q = v / (uint32_t)take;
+    const uint32_t l = probes[v];
+    const float* qv = Q + (size_t)q * dim;
+    const float* cv = cents + (size_t)l * dim;
+    float r[4];
+    float mx = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int c = lane + 32 * t;
+        r[t] = (c < dim) ? __fsub_rn(qv[c], cv[c]) : 0.0f;
+        mx = fmaxf(mx, fabsf(r[t]));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // exponent of the largest magnitude (subnormals count as 2^-127)
+    const int ex = mx > 0.0f ? (int)((__float_as_uint(mx) >> 23) & 0xff) - 127 : 0;
+    int sa = mx > 0.0f ? 14 - ex : 0;
+    sa = max(-120, min(120, sa));
+    const float scale = __uint_as_float((uint32_t)(sa + 127) << 23);  // 2^sa, exact
+    const int se = 1 - sa - sb;  // s2 = -2^se
+    const bool bad = !(mx <= 3.0e38f) || se < -125 || se > 126;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int c = lane + 32 * t;
+        if (c < dpad) a16[i * dpad + c] = __float2half_rn(bad ? 0.0f : __fmul_rn(r[t], scale));
+    }
+    if (lane == 0) {
+        pair_q[i] = q;
+        pair_rn[i] = coarse[(size_t)q * nlist + l];
+        pair_s2[i] = bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
+        if (bad) qbad[q] = 1u;
+        if (i < poff[nlist]) inv1[q] = (uint32_t)i;  // the query's pass-1 pair
+    }
+}
+
+// plen[i] = the padded length of pass-1 pair i's list (0 past the pass-1
+// pairs); an exclusive sum turns it into the pair's row offset in the dump.
+__global__ void plen_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
+                            int nlist, const uint32_t* __restrict__ probes,
+                            const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend,
+                            int n, unsigned* __restrict__ plen) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    unsigned len = 0;
+    if ((unsigned)i < poff[nlist]) {
+        const uint32_t l = probes[vals[i]];
+        len = (unsigned)((lend[l] - lbeg[l] + TILE_N - 1) / TILE_N * TILE_N);
+    }
+    plen[i] = len;
+}
+
+// Items of both passes, lists in `lorder`, one block.  items[0 .. n1) are
+// pass 1, items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
+constexpr int ITEM_THREADS = 1024;
+__global__ void __launch_bounds__(ITEM_THREADS)
+    build_items_kernel(const unsigned* __restrict__ poff, int nlist,
+                       const uint32_t* __restrict__ lorder, const uint64_t* __restrict__ lbeg,
+                       const uint64_t* __restrict__ lend, const uint32_t* __restrict__ pstart,
+                       Item* __restrict__ items, uint32_t* __restrict__ range) {
+    typedef cub::BlockScan<unsigned, ITEM_THREADS> Scan;
+    __shared__ typename Scan::TempStorage tmp;
+    __shared__ unsigned carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int pass = 0; pass < 2; ++pass) {
+        for (int base = 0; base < nlist; base += ITEM_THREADS) {
+            const int i = base + threadIdx.x;
+            unsigned cnt = 0, a0 = 0;
+            uint32_t l = 0;
+            if (i < nlist) {
+                l = lorder[i];
+                a0 = poff[pass * nlist + l];
+                cnt = poff[pass * nlist + l + 1] - a0;
+            }
+            const unsigned nit = (cnt + TILE_M - 1) / TILE_M;
+            unsigned off, tot;
+            Scan(tmp).ExclusiveSum(nit, off, tot);
+            const unsigned at = carry + off;
+            for (unsigned t = 0; t < nit; ++t) {
+                Item it;
+                it.a0 = a0 + t * TILE_M;
+                it.na = min((unsigned)TILE_M, cnt - t * TILE_M);
+                it.b0 = pstart[l];
+                it.nb = (uint32_t)(lend[l] - lbeg[l]);
+                it.tag0 = (uint32_t)lbeg[l];
+                it.pad[0] = it.pad[1] = it.pad[2] = 0;
+                items[at + t] = it;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) carry += tot;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            if (pass == 0) {
+                range[0] = 0;
+                range[1] = carry;
+                range[2] = carry;
+            } else {
+                range[3] = carry - range[2];
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// One warp per query: the top-64 keys of its pass-1 list, read from the dump,
+// into part[q]; tau[q] = their 64th distance (+inf if the list is shorter).
+__global__ void __launch_bounds__(256)
+    select1_kernel(const float* __restrict__ dump, const unsigned* __restrict__ seg,
+                   const uint32_t* __restrict__ inv1, const uint32_t* __restrict__ vals,
+                   const uint32_t* __restrict__ probes, const uint64_t* __restrict__ lbeg,
+                   const uint64_t* __restrict__ lend, int nq, uint64_t* __restrict__ part,
+                   float* __restrict__ tau) {
+    __shared__ uint64_t buf[8 * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + warp;
+    if (q >= nq) return;
+    WarpTopK<2> tk;
+    tk.init(LIST_K, buf + warp * 64);
+    const uint32_t i = inv1[q];
+    if (i != 0xffffffffu) {
+        const uint32_t l = probes[vals[i]];
+        const int nb = (int)(lend[l] - lbeg[l]);
+        const uint32_t tag0 = (uint32_t)lbeg[l];
+        const float* row = dump + seg[i];
+        for (int base = 0; base < nb; base += 32) {
+            const int j = base + lane;
+            const bool ok = j < nb;
+            const uint64_t key = ok ? make_key(row[j], tag0 + (uint32_t)j) : KEY_NONE;
+            tk.add(key, ok);
+        }
+        tk.flush();
+    }
+    tk.store(part + (size_t)q * LIST_K);
+    if (lane == 0) tau[q] = tk.thr == KEY_NONE ? INF : key_dist(tk.thr);
+}
+
+// One warp per query: the 64 best of its pass-1 list and pass-2 candidates.
+__global__ void __launch_bounds__(256)
+    select_kernel(const uint64_t* __restrict__ part, const uint64_t* __restrict__ cand,
+                  const unsigned* __restrict__ cnt, int cap, int nq,
+                  uint64_t* __restrict__ out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + warp;
+    if (q >= nq) return;
+    WarpTopK<2> tk;
+    tk.init(LIST_K, nullptr);
+    tk.L[0] = part[(size_t)q * LIST_K + lane];  // already sorted
+    tk.L[1] = part[(size_t)q * LIST_K + 32 + lane];
+    tk.thr = __shfl_sync(0xffffffffu, tk.L[1], 31);
+    tk.ingest(cand + (size_t)q * cap, (int)min(cnt[q], (unsigned)cap));
+    tk.store(out + (size_t)q * LIST_K);
+}
+
+// ---------------------------------------------------------------------------
+// exact rescoring and certification
+// ---------------------------------------------------------------------------
+struct CertParams {
+    const float* Q;
+    int nq, dim, m;
+    const float* cents;
+    const float* cb;
+    const uint64_t* offs_full;  // [nlist+1] unsharded offsets (key tags are their rows)
+    int nlist;
+    const uint8_t* codes;
+    const uint64_t* approx;     // [nq][64] tensor-core shortlist, ascending
+    int k;
+    uint64_t* out_keys;         // [nq][k]
+    const float* cmax;          // [m]
+    const float* bmax;          // [m]
+    const unsigned* cand_cnt;
+    int cap;
+    const float* tau;
+    const float* coarse;        // [nq][nlist]
+    const uint32_t* probes;     // [nq][take]
+    int take;
+    const uint64_t* lbeg;
+    const uint64_t* lend;
+    const float* rh;            // [nlist] upper bound of ||rhat|| over the list's codes
+    const uint32_t* qbad;
+    uint32_t qbase;             // global id of query 0 of this chunk
+    uint32_t* flag_count;
+    uint32_t* flag_list;
+};
+
+constexpr int CERT_WARPS = 8;
+
+// One warp per query.  The shortlist is rescored with exact_adc (the
+// reference's arithmetic) and the k best kept.  Certification: for a code of
+// list l, |d~ - D| <= E_l and |exact - D| <= E_adc, where D is the real ADC
+// distance of r = fl(q - c_l):
+//   E_l  = C1 R_l Rh_l + C2 (R_l^2 + Rh_l^2),  R_l >= ||r||, Rh_l >= ||rhat||
+//          over the list's codes, C1 = 2 (2^-10 + 2^-13) * 1.05: fp16
+//          rounding of both operands (2^-11 each, relative) and an allowance
+//          of 2^-13 for the tensor core's fp32 accumulation; C2 = 2^-16
+//          covers the fp32 roundings of ||r||^2, ||rhat||^2 and the final
+//          fused multiply-add;
+//   E_adc = (32 + 4m) 2^-24 sum_s (||q_s|| + cmax_s + bmax_s)^2 * 1.01.
+// Every code outside the shortlist has d~ >= B (B = the 64th shortlisted
+// value when the shortlist is full, tau otherwise), so it cannot enter the
+// exact top-k if, for its list, dk + E_adc + E_l < B, or if its real distance
+// is above dk anyway: (||r|| - Rh_l)^2 - E_adc > dk.  Overflowing candidate
+// arrays and queries marked bad are never certified.
+template <int ORDER>
+__global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) {
+    __shared__ uint64_t buf[CERT_WARPS * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * CERT_WARPS + warp;
+    if (q >= r.nq) return;  // whole warp
+    const int m = r.m, sub = r.dim / m;
+    const float* qv = r.Q + (size_t)q * r.dim;
+    const uint64_t* ak = r.approx + (size_t)q * LIST_K;
+    WarpTopK<1> tk;
+    tk.init(r.k, buf + warp * 64);
+    for (int base = 0; base < LIST_K; base += 32) {
+        const uint64_t key = ak[base + lane];
+        uint64_t ek = KEY_NONE;
+        if (key != KEY_NONE) {
+            const uint32_t pos = key_tag(key);
+            int lo = 0, hi = r.nlist;  // the list l with offs[l] <= pos < offs[l+1]
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (r.offs_full[mid + 1] <= pos) lo = mid + 1;
+                else hi = mid;
+            }
+            const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
+                                             r.codes + (size_t)pos * m, m, sub);
+            ek = make_key(d, pos);
+        }
+        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
+    }
+    tk.store(r.out_keys + (size_t)q * r.k);
+    double part = 0.0;
+    for (int s = lane; s < m; s += 32) {
+        double qn = 0.0;
+        for (int i = 0; i < sub; ++i) {
+            const double x = qv[s * sub + i];
+            qn += x * x;
+        }
+        const double t = sqrt(qn) + (double)r.cmax[s] + (double)r.bmax[s];
+        part += t * t;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const double Eadc = (32.0 + 4.0 * m) * 5.9604644775390625e-8 * part * 1.01;
+    const unsigned c = r.cand_cnt[q];
+    bool cert = c <= (unsigned)r.cap && r.qbad[q] == 0u;
+    const uint64_t last = ak[LIST_K - 1];
+    const double B = last != KEY_NONE ? (double)key_dist(last) : (double)r.tau[q];
+    if (cert && !isinf(B)) {
+        if (tk.thr == KEY_NONE) {
+            cert = false;
+        } else {
+            const double dk = (double)key_dist(tk.thr);
+            const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
+            const double C2 = 1.52587890625e-5;
+            bool ok = true;
+            for (int j = lane; j < r.take; j += 32) {
+                const uint32_t l = r.probes[(size_t)q * r.take + j];
+                if (r.lend[l] <= r.lbeg[l]) continue;
+                const double rh = (double)r.rh[l];
+                const double D = (double)r.coarse[(size_t)q * r.nlist + l];
+                const double R = sqrt(D) * (1.0 + 1.52587890625e-5);
+                const double El = C1 * R * rh + C2 * (R * R + rh * rh) + 1e-30;
+                const double Rl = sqrt(D) * (1.0 - 1.52587890625e-5) - rh;
+                const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - Eadc : -1.0;
+                ok = ok && ((dk + Eadc + El < B) || (dk < lower));
+            }
+            cert = __all_sync(0xffffffffu, ok);
+        }
+    }
+    if (!cert && lane == 0) {
+        const uint32_t idx = atomicAdd(r.flag_count, 1u);
+        r.flag_list[idx] = r.qbase + (uint32_t)q;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// per-index preparation: decoded codes in the padded list layout
+// ---------------------------------------------------------------------------
+// One warp per code row j: rhat scaled by 2^sb in fp16 (zero padded to dpad)
+// at row pstart[l] + (j - offs[l]) of the padded layout, and ||rhat||^2 from
+// the unscaled fp32 values.
+__global__ void decode_kernel(const uint8_t* __restrict__ codes, size_t n, int m, int sub,
+                              int dim, int dpad, const float* __restrict__ cb, float bscale,
+                              const uint64_t* __restrict__ offs, int nlist,
+                              const uint32_t* __restrict__ pstart, __half* __restrict__ dec,
+                              float* __restrict__ norm) {
+    const size_t row = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    int lo = 0, hi = nlist;  // the list l with offs[l] <= row < offs[l+1]
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (offs[mid + 1] <= row) lo = mid + 1;
+        else hi = mid;
+    }
+    const size_t prow = (size_t)pstart[lo] + (row - offs[lo]);
+    const uint8_t* code = codes + row * m;
+    float acc = 0.0f;
+    for (int c = lane; c < dpad; c += 32) {
+        float x = 0.0f;
+        if (c < dim) {
+            const int s = c / sub;
+            x = cb[((size_t)s * KSUB + code[s]) * sub + (c - s * sub)];
+        }
+        acc = __fmaf_rn(x, x, acc);
+        dec[prow * dpad + c] = __float2half_rn(__fmul_rn(x, bscale));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if (lane == 0) norm[prow] = acc;
+}
+
+__global__ void fill_inf_kernel(float* p, size_t n) {
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) p[t] = INF;
+}
+
+// rh[l] = sqrt(max ||rhat||^2 over the list's codes), rounded up (one warp per list).
+__global__ void list_rh_kernel(const float* __restrict__ norm, const uint32_t* __restrict__ pstart,
+                               const uint64_t* __restrict__ offs, int nlist,
+                               float* __restrict__ rh) {
+    const int l = (int)(((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (l >= nlist) return;
+    const size_t len = offs[l + 1] - offs[l];
+    float mx = 0.0f;
+    for (size_t i = lane; i < len; i += 32) mx = fmaxf(mx, norm[pstart[l] + i]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) rh[l] = sqrtf(mx) * (1.0f + 1e-5f);
+}
+
+size_t pass_smem(int katoms) {
+    return 1024 + (size_t)(1 + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
+           (size_t)(2 + 2 * NSTAGE + 4 + 2 * NCV) * 8 + 16;
+}
+
+template <int EPI>
+void launch_pass(cudaStream_t s, const CUtensorMap& am, const CUtensorMap& bm, int grid,
+                 const PassParams& p) {
+    const size_t smem = pass_smem(p.katoms);
+    FDB_REQUIRE(smem <= 227 * 1024, FDB_ERR_UNSUPPORTED, "list scan needs too much shared memory");
+    FDB_CUDA(cudaFuncSetAttribute(ivf_pass_kernel<EPI>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ivf_pass_kernel<EPI><<<grid, THREADS, smem, s>>>(am, bm, p);
+    FDB_LAUNCH_CHECK();
+}
+
+int bits_for(uint32_t v) {
+    int b = 1;
+    while ((1ull << b) <= v) ++b;
+    return b;
+}
+
+}  // namespace ivtc
+
+// ---------------------------------------------------------------------------
+// host entry points
+// ---------------------------------------------------------------------------
+bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k) {
+    return h->dec16.p != nullptr && k >= 1 && k <= 32;
+}
+
+// Decoded codes and their norms in the padded list layout, per-list bounds
+// of ||rhat||, and the list order.  Needs the table mode's bound terms.
+void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
+                    const std::vector<float>& bmax_host) {
+    (void)bmax_host;
+    h->dec16.release();
+    h->dnorm.release();
+    h->lorder.release();
+    h->tc_pstart.release();
+    h->tc_rhl.release();
+    const size_t n = h->n_total, dim = h->dim, m = h->m, sub = dim / m, nlist = h->nlist;
+    const int dpad = (int)((dim + 63) / 64 * 64);
+    if (dpad > 128 || n == 0) return;
+    double amax = 0.0;
+    for (float x : cb_host) amax = std::max(amax, (double)std::fabs(x));
+    if (!(amax > 0.0) || !std::isfinite(amax)) return;
+    const int sb = 13 - std::ilogb(amax);  // largest |b| * 2^sb in [2^13, 2^14)
+    if (sb < -100 || sb > 100) return;
+    // padded layout: list l starts at pstart[l], a multiple of 128 rows
+    std::vector<uint32_t> pstart(nlist);
+    size_t rows = 0;
+    for (size_t l = 0; l < nlist; ++l) {
+        pstart[l] = (uint32_t)rows;
+        const size_t len = h->h_offs_full[l + 1] - h->h_offs_full[l];
+        rows += (len + ivtc::TILE_N - 1) / ivtc::TILE_N * ivtc::TILE_N;
+        if (rows >= (1ull << 31)) return;
+    }
+    Ctx& c = h->ctx->c;
+    cudaStream_t st = c.stream;
+    h->tc_dpad = dpad;
+    h->tc_sb = sb;
+    h->tc_rows = rows;
+    h->tc_maxpad = 0;
+    for (size_t l = 0; l < nlist; ++l)
+        h->tc_maxpad = std::max<size_t>(h->tc_maxpad, (l + 1 < nlist ? pstart[l + 1] : rows) - pstart[l]);
+    double rh2 = 0.0;
+    for (size_t s = 0; s < m; ++s) rh2 += (double)bmax_host[s] * bmax_host[s];
+    h->tc_colmax = (float)(rh2 * (1.0 + 1e-5));
+    h->tc_pstart.alloc(nlist);
+    FDB_CUDA(cudaMemcpyAsync(h->tc_pstart.p, pstart.data(), nlist * 4, cudaMemcpyHostToDevice, st));
+    h->dec16.alloc(std::max<size_t>(rows, 1) * dpad);
+    h->dnorm.alloc(std::max<size_t>(rows, 1));
+    FDB_CUDA(cudaMemsetAsync(h->dec16.p, 0, h->dec16.bytes(), st));
+    ivtc::fill_inf_kernel<<<(unsigned)((h->dnorm.n + 255) / 256), 256, 0, st>>>(h->dnorm.p,
+                                                                                 h->dnorm.n);
+    FDB_LAUNCH_CHECK();
+    const unsigned blocks = (unsigned)((n * 32 + 255) / 256);
+    ivtc::decode_kernel<<<blocks, 256, 0, st>>>(h->codes.p, n, (int)m, (int)sub, (int)dim, dpad,
+                                                 h->cb.p, std::ldexp(1.0f, sb), h->offs.p,
+                                                 (int)nlist, h->tc_pstart.p, h->dec16.p,
+                                                 h->dnorm.p);
+    FDB_LAUNCH_CHECK();
+    h->tc_rhl.alloc(nlist);
+    ivtc::list_rh_kernel<<<(unsigned)((nlist * 32 + 255) / 256), 256, 0, st>>>(
+        h->dnorm.p, h->tc_pstart.p, h->offs.p, (int)nlist, h->tc_rhl.p);
+    FDB_LAUNCH_CHECK();
+    // lists by decreasing length (ties by list id)
+    std::vector<uint32_t> order(nlist);
+    std::iota(order.begin(), order.end(), 0u);
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+        return h->h_offs_full[a + 1] - h->h_offs_full[a] > h->h_offs_full[b + 1] - h->h_offs_full[b];
+    });
+    h->lorder.alloc(nlist);
+    FDB_CUDA(cudaMemcpyAsync(h->lorder.p, order.data(), nlist * 4, cudaMemcpyHostToDevice, st));
+    FDB_CUDA(cudaStreamSynchronize(st));
+}
+
+namespace {
+
+// One chunk of queries [q0, q0 + nq) through the whole tensor path.  probes
+// and coarse point at the chunk's rows; flag entries are global query ids.
+void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
+              const uint32_t* probes, const float* coarse, const uint64_t* lbeg,
+              const uint64_t* lend, uint64_t* out_keys, uint32_t* flags, uint32_t qbase,
+              unsigned long long* stat, int* err) {
+    using namespace ivtc;
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const int nlist = (int)h->nlist;
+    const size_t np = nq * take;
+    const int dpad = h->tc_dpad;
+    const int nkeys = 2 * nlist + 1;
+    // --- group the pairs by (pass, list) ---
+    h->t_keys.ensure(2 * np);
+    h->t_vals.ensure(2 * np);
+    h->t_cnt.ensure((size_t)nkeys + 1);
+    h->t_off.ensure((size_t)nkeys + 1);
+    FDB_CUDA(cudaMemsetAsync(h->t_cnt.p, 0, ((size_t)nkeys + 1) * 4, s));
+    pair_keys_kernel<<<(unsigned)((nq + 127) / 128), 128, 0, s>>>(
+        probes, (int)nq, (int)take, lbeg, lend, nlist, h->t_keys.p, h->t_vals.p, h->t_cnt.p,
+        stat);
+    FDB_LAUNCH_CHECK();
+    h->t_plen.ensure(nq + 1);
+    h->t_seg.ensure(nq + 1);
+    size_t tmp_sort = 0, tmp_scan = 0, tmp_seg = 0;
+    const int end_bit = bits_for((uint32_t)nkeys);
+    FDB_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_sort, h->t_keys.p, h->t_keys.p + np,
+                                             h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
+                                             s));
+    FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_scan, h->t_cnt.p, h->t_off.p, nkeys + 1,
+                                           s));
+    FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_seg, h->t_plen.p, h->t_seg.p,
+                                           (int)nq + 1, s));
+    h->t_tmp.ensure(std::max(tmp_sort, std::max(tmp_scan, tmp_seg)));
+    FDB_CUDA(cub::DeviceRadixSort::SortPairs(h->t_tmp.p, tmp_sort, h->t_keys.p, h->t_keys.p + np,
+                                             h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
+                                             s));
+    FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp.p, tmp_scan, h->t_cnt.p, h->t_off.p,
+                                           nkeys + 1, s));
+    const uint32_t* svals = h->t_vals.p + np;
+    // --- residual rows, dump rows and items ---
+    h->t_a16.ensure(np * dpad);
+    h->t_pq.ensure(np);
+    h->t_rn.ensure(np);
+    h->t_s2.ensure(np);
+    h->t_qbad.ensure(nq);
+    h->t_inv1.ensure(nq);
+    FDB_CUDA(cudaMemsetAsync(h->t_qbad.p, 0, nq * 4, s));
+    FDB_CUDA(cudaMemsetAsync(h->t_inv1.p, 0xff, nq * 4, s));
+    build_a_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
+        svals, h->t_off.p, nlist, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad, coarse,
+        h->tc_sb, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_qbad.p, h->t_inv1.p);
+    FDB_LAUNCH_CHECK();
+    plen_kernel<<<(unsigned)((nq + 1 + 255) / 256), 256, 0, s>>>(
+        svals, h->t_off.p, nlist, probes, lbeg, lend, (int)nq + 1, h->t_plen.p);
+    FDB_LAUNCH_CHECK();
+    FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp.p, tmp_seg, h->t_plen.p, h->t_seg.p,
+                                           (int)nq + 1, s));
+    h->t_dump.ensure(std::max<size_t>(1, nq * h->tc_maxpad));
+    const size_t max_items = np / TILE_M + 2 * std::min(np, (size_t)nlist) + 2;
+    h->t_items.ensure(max_items * sizeof(Item));
+    Item* items = reinterpret_cast<Item*>(h->t_items.p);
+    build_items_kernel<<<1, ITEM_THREADS, 0, s>>>(h->t_off.p, nlist, h->lorder.p, lbeg, lend,
+                                                  h->tc_pstart.p, items, h->t_range.p);
+    FDB_LAUNCH_CHECK();
+    // --- pass 1: distances of each query's first list; its top-64 and tau ---
+    const CUtensorMap am = make_map(h->t_a16.p, np, dpad);
+    const CUtensorMap bm = make_map(h->dec16.p, h->tc_rows, dpad);
+    const int cap = 1024;
+    h->t_part.ensure(nq * LIST_K);
+    h->t_tau.ensure(nq);
+    h->t_cand_cnt.ensure(nq);
+    h->t_cand.ensure(nq * (size_t)cap);
+    FDB_CUDA(cudaMemsetAsync(h->t_cand_cnt.p, 0, nq * 4, s));
+    PassParams p{};
+    p.items = items;
+    p.range = h->t_range.p;
+    p.katoms = dpad / KATOM;
+    p.pair_q = h->t_pq.p;
+    p.pair_rn = h->t_rn.p;
+    p.pair_s2 = h->t_s2.p;
+    p.colv = h->dnorm.p;
+    p.colmax = h->tc_colmax;
+    p.dump = h->t_dump.p;
+    p.seg = h->t_seg.p;
+    p.tau = h->t_tau.p;
+    p.cand = h->t_cand.p;
+    p.cand_cnt = h->t_cand_cnt.p;
+    p.cap = cap;
+    p.err = err;
+    const int grid = c.sm_count;
+    launch_pass<EPI_DUMP>(s, am, bm, grid, p);
+    select1_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
+        h->t_dump.p, h->t_seg.p, h->t_inv1.p, svals, probes, lbeg, lend, (int)nq, h->t_part.p,
+        h->t_tau.p);
+    FDB_LAUNCH_CHECK();
+    // --- pass 2: the other lists against tau ---
+    p.range = h->t_range.p + 2;
+    launch_pass<EPI_FILTER>(s, am, bm, grid, p);
+    // --- shortlist, exact rescoring, certification ---
+    h->s_approx.ensure(nq * LIST_K);
+    select_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(h->t_part.p, h->t_cand.p,
+                                                           h->t_cand_cnt.p, cap, (int)nq,
+                                                           h->s_approx.p);
+    FDB_LAUNCH_CHECK();
+    CertParams r{};
+    r.Q = dQ;
+    r.nq = (int)nq;
+    r.dim = (int)h->dim;
+    r.m = (int)h->m;
+    r.cents = h->cents.p;
+    r.cb = h->cb.p;
+    r.offs_full = h->offs.p;
+    r.nlist = nlist;
+    r.codes = h->codes.p;
+    r.approx = h->s_approx.p;
+    r.k = (int)k;
+    r.out_keys = out_keys;
+    r.cmax = h->cmax.p;
+    r.bmax = h->bmax.p;
+    r.cand_cnt = h->t_cand_cnt.p;
+    r.cap = cap;
+    r.tau = h->t_tau.p;
+    r.coarse = coarse;
+    r.probes = probes;
+    r.take = (int)take;
+    r.lbeg = lbeg;
+    r.lend = lend;
+    r.rh = h->tc_rhl.p;
+    r.qbad = h->t_qbad.p;
+    r.qbase = qbase;
+    r.flag_count = flags;
+    r.flag_list = flags + 1;
+    const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
+    if (order == ORDER_LANE8) certify_kernel<ORDER_LANE8><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    else certify_kernel<ORDER_FAST4><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    FDB_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+// Tensor-core shortlist + exact rescoring of nq queries whose probes and
+// coarse distances are in h->s_probe / h->s_coarse.  Writes [nq][k] exact keys
+// and lists uncertified queries in flags (flags[0] = count, then indices);
+// returns that count.  Queries run in chunks that keep the pass-1 dump
+// (one row of distances per query) within 1 GiB.
+uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
+                       size_t take, const uint64_t* lbeg, const uint64_t* lend,
+                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
+    const size_t budget = (size_t)1 << 28;  // floats
+    const size_t chunk = std::max<size_t>(1, std::min(nq, budget / std::max<size_t>(h->tc_maxpad, 1)));
+    h->t_range.ensure(8);
+    int* err = reinterpret_cast<int*>(h->t_range.p + 4);
+    FDB_CUDA(cudaMemsetAsync(flags, 0, 4, s));
+    FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
+    for (size_t q0 = 0; q0 < nq; q0 += chunk) {
+        const size_t nc = std::min(chunk, nq - q0);
+        tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,
+                 h->s_coarse.p + q0 * h->nlist, lbeg, lend, out_keys + q0 * k, flags,
+                 (uint32_t)q0, stat, err);
+    }
+    uint32_t hv[2] = {0, 0};
+    FDB_CUDA(cudaMemcpyAsync(&hv[0], flags, 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaMemcpyAsync(&hv[1], err, 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
+    return hv[0];
+}
+
+}  // namespace fdb

@@ -404,7 +404,7 @@ class IVFPQIndex:
     def shard(self, rank: int, world: int):
         _check(lib().fdb_ivfpq_shard(self.h, rank, world))
 
-    SCAN_AUTO, SCAN_EXACT, SCAN_TABLES = 0, 1, 2
+    SCAN_AUTO, SCAN_EXACT, SCAN_TABLES, SCAN_TENSOR = 0, 1, 2, 3
 
     def set_nprobe(self, nprobe: int):
         _check(lib().fdb_ivfpq_set_nprobe(self.h, nprobe))

@@ -74,16 +74,22 @@ typedef struct fdb_stats {
                                 failing certification */
 } fdb_stats;
 
-/* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  Both return the reference's
+/* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  All return the reference's
  * exact distances.  EXACT builds every (query, list) table in the AVX2 order.
  * TABLES builds it from a per-list table precomputed at build time plus a
  * per-query table, keeps a shortlist of max(32, 2k) candidates, recomputes
  * their distances exactly, and certifies the result with a worst-case
  * rounding bound; a query that fails the bound is re-scanned in EXACT mode.
- * AUTO picks TABLES for subvectors of 8+ floats and k <= 128. */
+ * TENSOR (k <= 16, dim <= 128 after padding to 64) groups the probed
+ * (query, list) pairs by list and scores them on the tcgen05 tensor cores
+ * against fp16 codes decoded at build time, keeps a shortlist of 32, and
+ * rescores and certifies it the same way.  AUTO picks TENSOR for batches of
+ * 256+ queries where it applies, else TABLES for subvectors of 8+ floats and
+ * k <= 128, else EXACT. */
 #define FDB_SCAN_AUTO 0
 #define FDB_SCAN_EXACT 1
 #define FDB_SCAN_TABLES 2
+#define FDB_SCAN_TENSOR 3
 
 /* Training options for fdb_ivfpq_build.  Zero-initialise and set what you
  * need.  The reference draws samples and initial centroids from an unseeded

@@ -255,7 +255,7 @@ def gmm_index(fg, ctx):
     return ix, X, Q
 
 
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode", [1, 2, 3])
 @pytest.mark.parametrize("k", [1, 10, 100])
 def test_scan_modes_match_oracle(fg, ctx, orc, gmm_index, mode, k):
     ix, X, Q = gmm_index
@@ -267,7 +267,7 @@ def test_scan_modes_match_oracle(fg, ctx, orc, gmm_index, mode, k):
     oi, od, oc = ox.batch_search(Q, k)
     rate = assert_topk_match(ids, d, cnt, oi, od, oc, f"mode={mode} k={k}")
     assert rate > 0.95
-    if mode == 2:
+    if mode >= 2:
         assert st.exact_rescans <= len(Q) // 20  # nearly every query certifies
     for q in range(0, len(Q), 97):
         res = ix.search(Q[q], k)
@@ -292,6 +292,76 @@ def test_table_mode_ties_fall_back_to_exact(fg, ctx, orc):
     assert st.exact_rescans > 0
     oi, od, oc = ox.batch_search(Q, 10)
     assert_topk_match(ids, d, cnt, oi, od, oc, "ties")
+
+
+# ---------------------------------------------------------------------------
+# IVF-PQ tensor mode: lists scored on tcgen05 + exact rescoring
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("nprobe,k,nq", [(1, 10, 300), (8, 1, 50), (8, 16, 300), (32, 10, 7),
+                                         (32, 16, 1000)])
+def test_ivfpq_tensor_mode_config_a(fg, ctx, orc, nprobe, k, nq):
+    rng = np.random.default_rng(1)
+    X = rng.random((10000, 128), dtype=np.float32)
+    Q = np.random.default_rng(4).random((nq, 128), dtype=np.float32)
+    ix = fg.IVFPQIndex.build(X, 32, 8, ctx=ctx, seed=123)
+    ox = _oracle_index(orc, ix)
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    ix.set_nprobe(nprobe)
+    ox.set_nprobe(nprobe)
+    ids, d, cnt, st = ix.batch_search_arrays(Q, k, stats=True)
+    oi, od, oc = ox.batch_search(Q, k)
+    assert_topk_match(ids, d, cnt, oi, od, oc, f"tensor nprobe={nprobe} k={k}")
+    assert st.lists_probed == nq * nprobe
+    for q in range(0, nq, 61):
+        res = ix.search(Q[q], k)
+        si, sd = ox.search(Q[q], k)
+        assert np.array_equal(np.array([r[1] for r in res], np.float32), sd)
+
+
+def test_ivfpq_tensor_mode_ties_and_short_lists(fg, ctx, orc):
+    """Exact ties longer than the 64-entry shortlist cannot be certified;
+    lists shorter than 64 codes leave the admission threshold at +inf.  Both
+    must end on the exact path with the oracle's answer."""
+    rng = np.random.default_rng(21)
+    base = (rng.random((40, 64), dtype=np.float32) * 10).astype(np.float32)
+    X = np.repeat(base, 100, axis=0)
+    ix = fg.IVFPQIndex.build(X, 8, 8, ctx=ctx, seed=2)
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    ix.set_nprobe(8)
+    ox = _oracle_index(orc, ix)
+    ox.set_nprobe(8)
+    Q = base[:20] + np.float32(0.01)
+    ids, d, cnt, st = ix.batch_search_arrays(Q, 10, stats=True)
+    assert st.exact_rescans > 0
+    oi, od, oc = ox.batch_search(Q, 10)
+    assert_topk_match(ids, d, cnt, oi, od, oc, "tensor ties")
+    # many tiny lists: 600 vectors in 64 lists, dim 64 -> subvectors of 8
+    X2 = rng.random((600, 64), dtype=np.float32)
+    ix2 = fg.IVFPQIndex.build(X2, 64, 8, ctx=ctx, seed=5)
+    ix2.set_scan_mode(ix2.SCAN_TENSOR)
+    ox2 = _oracle_index(orc, ix2)
+    Q2 = rng.random((300, 64), dtype=np.float32)
+    for nprobe in (1, 2, 5):
+        ix2.set_nprobe(nprobe)
+        ox2.set_nprobe(nprobe)
+        ids, d, cnt = ix2.batch_search_arrays(Q2, 16)
+        oi, od, oc = ox2.batch_search(Q2, 16)
+        assert_topk_match(ids, d, cnt, oi, od, oc, f"tensor tiny lists nprobe={nprobe}")
+
+
+def test_ivfpq_tensor_mode_gmm_certifies(fg, ctx, orc, gmm_index):
+    """Descriptor-like data: the fp16 bound certifies nearly every query."""
+    ix, X, Q = gmm_index
+    ox = _oracle_index(orc, ix)
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    for nprobe in (1, 4, 16):
+        ix.set_nprobe(nprobe)
+        ox.set_nprobe(nprobe)
+        ids, d, cnt, st = ix.batch_search_arrays(Q, 10, stats=True)
+        oi, od, oc = ox.batch_search(Q, 10)
+        assert_topk_match(ids, d, cnt, oi, od, oc, f"tensor gmm nprobe={nprobe}")
+        assert st.exact_rescans <= len(Q) // 20
+    ix.set_scan_mode(0)
 
 
 # ---------------------------------------------------------------------------
