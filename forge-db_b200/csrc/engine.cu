@@ -211,6 +211,13 @@ static void ivfpq_prepare_tables(fdb_ivfpq* h) {
     h->bmax.release();
     h->dec16.release();
     h->dnorm.release();
+    h->centsT.release();
+    if (dim <= (size_t)COARSE_TILED_MAX_DIM && nlist > 0) {
+        h->nlist_pad = (int)((nlist + 127) / 128 * 128);
+        h->centsT.alloc(dim * h->nlist_pad);
+        launch_transpose_pad(h->ctx->c.stream, h->cents.p, (int)nlist, (int)dim, h->nlist_pad,
+                             h->centsT.p);
+    }
     if (sub < 8) return;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -378,7 +385,15 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
     } else {
         h->s_coarse.ensure(nq * (size_t)nlist);
         h->s_probe.ensure(nq * take);
-        launch_coarse_dist(s, dQ, (int)nq, (int)h->dim, h->cents.p, nlist, h->s_coarse.p);
+        if (h->centsT.p) {
+            const int nq_pad = (int)((nq + 31) / 32 * 32);
+            h->s_qT.ensure(h->dim * (size_t)nq_pad);
+            launch_transpose_pad(s, dQ, (int)nq, (int)h->dim, nq_pad, h->s_qT.p);
+            launch_coarse_tiled(s, h->s_qT.p, (int)nq, nq_pad, (int)h->dim, h->centsT.p, nlist,
+                                h->nlist_pad, h->s_coarse.p);
+        } else {
+            launch_coarse_dist(s, dQ, (int)nq, (int)h->dim, h->cents.p, nlist, h->s_coarse.p);
+        }
         launch_select(s, h->s_coarse.p, (int)nq, nlist, (int)take, h->s_probe.p);
         tm.mark();
         h->s_stat.ensure(2);

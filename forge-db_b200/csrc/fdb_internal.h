@@ -260,6 +260,8 @@ struct fdb_ivfpq {
     fdb::DevBuf<uint64_t> shard_be;     // [2][nlist] list begin / end when sharded
     // table mode (subvectors of 8+ floats): per-list tables and error-bound terms
     int scan_mode = FDB_SCAN_AUTO;
+    fdb::DevBuf<float> centsT;          // [dim][nlist_pad] for the tiled coarse kernel
+    int nlist_pad = 0;
     fdb::DevBuf<float> btab;            // [nlist][m][256]
     fdb::DevBuf<float> cmax, bmax;      // [m]
     // tensor mode (dim <= 128 after padding): codes decoded to fp16 residual
@@ -275,7 +277,7 @@ struct fdb_ivfpq {
     float tc_colmax = 0.0f;             // upper bound of ||rhat||^2
     std::mutex mu;
     // per-call scratch
-    fdb::DevBuf<float> s_q, s_coarse;
+    fdb::DevBuf<float> s_q, s_coarse, s_qT;
     fdb::DevBuf<uint32_t> s_probe;
     fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids, s_approx;
     fdb::DevBuf<float> s_dists;

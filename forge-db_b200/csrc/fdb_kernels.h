@@ -53,6 +53,13 @@ void launch_coarse_dist(cudaStream_t s, const float* Q, int nq, int dim, const f
                         int nlist, float* D);
 void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
                    uint32_t* probes);
+// Register-tiled coarse distances (bit-identical to launch_coarse_dist) for
+// dim <= 256 from transposed, zero-padded operands: QT [dim][nq_pad] with
+// nq_pad a multiple of 32, CT [dim][nlist_pad] with nlist_pad a multiple of 128.
+constexpr int COARSE_TILED_MAX_DIM = 256;
+void launch_transpose_pad(cudaStream_t s, const float* x, int n, int dim, int npad, float* out);
+void launch_coarse_tiled(cudaStream_t s, const float* QT, int nq, int nq_pad, int dim,
+                         const float* CT, int nlist, int nlist_pad, float* D);
 void launch_scan(cudaStream_t s, const ScanParams& a, int order);
 void launch_rescore(cudaStream_t s, const RescoreParams& r, int order);
 void launch_ivf_tables(cudaStream_t s, const float* cents, const float* cb, int nlist, int m,

@@ -85,6 +85,129 @@ void launch_coarse_dist(cudaStream_t s, const float* Q, int nq, int dim, const f
     FDB_LAUNCH_CHECK();
 }
 
+// Register-tiled coarse distances for dim <= 256.  A block covers CT_Q queries
+// x CT_C centroids with both tiles transposed in shared memory ([dim][..]);
+// a thread owns CT_TQ x CT_TC pairs.  The AVX2 order of l2sq_exact (eight
+// lane accumulators over i = j (mod 8), then a left-to-right lane sum, then
+// the unfused scalar tail) is kept by running the lanes in the outer loop:
+// lane j's accumulator is complete before it is added to the running sum, so
+// only two registers per pair are live and every result is bit-identical.
+constexpr int CT_Q = 32, CT_C = 128, CT_TQ = 4, CT_TC = 8;
+constexpr int CT_THREADS = (CT_Q / CT_TQ) * (CT_C / CT_TC);  // 128
+constexpr int CT_MAX_DIM = 256;
+
+// out[i][q] = x[q][i] for q < n, 0 for n <= q < npad.
+__global__ void transpose_pad_kernel(const float* __restrict__ x, int n, int dim, int npad,
+                                     float* __restrict__ out) {
+    __shared__ float tile[32][33];
+    const int q0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int q = q0 + r, i = i0 + threadIdx.x;
+        tile[r][threadIdx.x] = (q < n && i < dim) ? x[(size_t)q * dim + i] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int i = i0 + r, q = q0 + threadIdx.x;
+        if (i < dim && q < npad) out[(size_t)i * npad + q] = tile[threadIdx.x][r];
+    }
+}
+
+__global__ void __launch_bounds__(CT_THREADS)
+    coarse_tiled_kernel(const float* __restrict__ QT, int nq, int nq_pad, int dim,
+                        const float* __restrict__ CT, int nlist, int nlist_pad,
+                        float* __restrict__ D) {
+    extern __shared__ __align__(16) float ct_smem[];
+    float* qs = ct_smem;              // [dim][CT_Q]
+    float* cs = qs + dim * CT_Q;      // [dim][CT_C]
+    const int q0 = blockIdx.y * CT_Q, c0 = blockIdx.x * CT_C;
+    for (int e = threadIdx.x; e < dim * (CT_Q / 4); e += CT_THREADS) {
+        const int i = e / (CT_Q / 4), v = e - i * (CT_Q / 4);
+        reinterpret_cast<float4*>(qs + i * CT_Q)[v] =
+            __ldg(reinterpret_cast<const float4*>(QT + (size_t)i * nq_pad + q0) + v);
+    }
+    for (int e = threadIdx.x; e < dim * (CT_C / 4); e += CT_THREADS) {
+        const int i = e / (CT_C / 4), v = e - i * (CT_C / 4);
+        reinterpret_cast<float4*>(cs + i * CT_C)[v] =
+            __ldg(reinterpret_cast<const float4*>(CT + (size_t)i * nlist_pad + c0) + v);
+    }
+    __syncthreads();
+    const int tq = threadIdx.x & (CT_Q / CT_TQ - 1);  // 0..7
+    const int tc = threadIdx.x / (CT_Q / CT_TQ);      // 0..15
+    const float* qb = qs + tq * CT_TQ;
+    const float* cb = cs + tc * CT_TC;
+    float t[CT_TQ][CT_TC];
+    const int full = dim & ~7;
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+        float acc[CT_TQ][CT_TC];
+#pragma unroll
+        for (int a = 0; a < CT_TQ; ++a)
+#pragma unroll
+            for (int b = 0; b < CT_TC; ++b) acc[a][b] = 0.0f;
+#pragma unroll 4
+        for (int i = j; i < full; i += 8) {
+            const float4 qv = *reinterpret_cast<const float4*>(qb + i * CT_Q);
+            const float4 c0v = *reinterpret_cast<const float4*>(cb + i * CT_C);
+            const float4 c1v = *reinterpret_cast<const float4*>(cb + i * CT_C + 4);
+            const float qa[CT_TQ] = {qv.x, qv.y, qv.z, qv.w};
+            const float ca[CT_TC] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
+#pragma unroll
+            for (int a = 0; a < CT_TQ; ++a)
+#pragma unroll
+                for (int b = 0; b < CT_TC; ++b) {
+                    const float d = __fsub_rn(qa[a], ca[b]);
+                    acc[a][b] = __fmaf_rn(d, d, acc[a][b]);
+                }
+        }
+#pragma unroll
+        for (int a = 0; a < CT_TQ; ++a)
+#pragma unroll
+            for (int b = 0; b < CT_TC; ++b) t[a][b] = j == 0 ? acc[a][b] : __fadd_rn(t[a][b], acc[a][b]);
+    }
+    for (int i = full; i < dim; ++i) {
+#pragma unroll
+        for (int a = 0; a < CT_TQ; ++a)
+#pragma unroll
+            for (int b = 0; b < CT_TC; ++b) {
+                const float d = __fsub_rn(qb[i * CT_Q + a], cb[i * CT_C + b]);
+                t[a][b] = __fadd_rn(t[a][b], __fmul_rn(d, d));
+            }
+    }
+#pragma unroll
+    for (int a = 0; a < CT_TQ; ++a) {
+        const int q = q0 + tq * CT_TQ + a;
+        if (q >= nq) continue;
+        float* row = D + (size_t)q * nlist;
+#pragma unroll
+        for (int b = 0; b < CT_TC; ++b) {
+            const int l = c0 + tc * CT_TC + b;
+            if (l < nlist) row[l] = t[a][b];
+        }
+    }
+}
+
+void launch_transpose_pad(cudaStream_t s, const float* x, int n, int dim, int npad, float* out) {
+    if (npad == 0 || dim == 0) return;
+    dim3 grid((unsigned)((npad + 31) / 32), (unsigned)((dim + 31) / 32));
+    transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, n, dim, npad, out);
+    FDB_LAUNCH_CHECK();
+}
+
+void launch_coarse_tiled(cudaStream_t s, const float* QT, int nq, int nq_pad, int dim,
+                         const float* CT, int nlist, int nlist_pad, float* D) {
+    if (nq == 0) return;
+    FDB_REQUIRE(dim <= CT_MAX_DIM && nq_pad % CT_Q == 0 && nlist_pad % CT_C == 0,
+                FDB_ERR_UNSUPPORTED, "coarse tiling: bad shape");
+    const size_t smem = (size_t)dim * (CT_Q + CT_C) * sizeof(float);
+    if (smem > 48 * 1024)
+        FDB_CUDA(cudaFuncSetAttribute(coarse_tiled_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)(nlist_pad / CT_C), (unsigned)(nq_pad / CT_Q));
+    coarse_tiled_kernel<<<grid, CT_THREADS, smem, s>>>(QT, nq, nq_pad, dim, CT, nlist, nlist_pad,
+                                                        D);
+    FDB_LAUNCH_CHECK();
+}
+
 // ---------------------------------------------------------------------------
 // probe selection
 // ---------------------------------------------------------------------------
