@@ -432,6 +432,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
                                                  h->s_keys.p, h->s_flags.p, h->s_stat.p);
             tm.mark();
             if (nflag > 0) {
+                // exact re-scan of the lists that failed, seeded with the rest
                 ScanParams e = a;
                 e.nq = (int)nflag;
                 e.qidx = h->s_flags.p + 1;
@@ -439,6 +440,9 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
                 e.out_keys = h->s_keys.p;
                 e.stat = nullptr;
                 e.btab = nullptr;
+                e.probe_list = h->t_fprobes.p;
+                e.probe_cnt = h->t_fcnt.p;
+                e.seed = true;
                 launch_scan(s, e, order);
             }
             if (st) st->exact_rescans = nflag;

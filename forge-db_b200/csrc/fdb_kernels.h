@@ -26,6 +26,12 @@ struct ScanParams {
     unsigned long long* stat;  // [0] lists scanned, [1] codes scanned (nullable)
     const uint32_t* qidx;      // nullable: block i scans query qidx[i] (and writes its row)
     const float* btab;         // non-null selects table mode: [nlist][m][256]
+    // nullable, with qidx: block i scans only the lists probe_list[i][0 .. probe_cnt[i])
+    // (row stride nprobe) and, with seed, starts from the k keys already in
+    // out_keys[qidx[i]] (which must not repeat codes of those lists)
+    const uint32_t* probe_list;
+    const uint32_t* probe_cnt;
+    bool seed;
 };
 
 struct RescoreParams {

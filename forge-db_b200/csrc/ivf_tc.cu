@@ -677,6 +677,8 @@ struct CertParams {
     uint32_t qbase;             // global id of query 0 of this chunk
     uint32_t* flag_count;
     uint32_t* flag_list;
+    uint32_t* fail_probes;      // [flag slot][take] lists to re-scan exactly
+    uint32_t* fail_cnt;         // [flag slot]
 };
 
 constexpr int CERT_WARPS = 8;
@@ -706,11 +708,14 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     const int m = r.m, sub = r.dim / m;
     const float* qv = r.Q + (size_t)q * r.dim;
     const uint64_t* ak = r.approx + (size_t)q * LIST_K;
-    WarpTopK<1> tk;
-    tk.init(r.k, buf + warp * 64);
-    for (int base = 0; base < LIST_K; base += 32) {
-        const uint64_t key = ak[base + lane];
-        uint64_t ek = KEY_NONE;
+    // exact keys of the 64 shortlisted codes (two per lane) and their lists
+    uint64_t ek[2];
+    int el[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint64_t key = ak[h * 32 + lane];
+        ek[h] = KEY_NONE;
+        el[h] = -1;
         if (key != KEY_NONE) {
             const uint32_t pos = key_tag(key);
             int lo = 0, hi = r.nlist;  // the list l with offs[l] <= pos < offs[l+1]
@@ -721,11 +726,15 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
             }
             const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
                                              r.codes + (size_t)pos * m, m, sub);
-            ek = make_key(d, pos);
+            ek[h] = make_key(d, pos);
+            el[h] = lo;
         }
-        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
     }
-    tk.store(r.out_keys + (size_t)q * r.k);
+    WarpTopK<1> tk;
+    tk.init(r.k, buf + warp * 64);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (__any_sync(0xffffffffu, ek[h] != KEY_NONE)) tk.merge32(ek[h]);
     double part = 0.0;
     for (int s = lane; s < m; s += 32) {
         double qn = 0.0;
@@ -739,36 +748,73 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     const double Eadc = (32.0 + 4.0 * m) * 5.9604644775390625e-8 * part * 1.01;
+    const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
+    const double C2 = 1.52587890625e-5;
     const unsigned c = r.cand_cnt[q];
-    bool cert = c <= (unsigned)r.cap && r.qbad[q] == 0u;
     const uint64_t last = ak[LIST_K - 1];
     const double B = last != KEY_NONE ? (double)key_dist(last) : (double)r.tau[q];
-    if (cert && !isinf(B)) {
-        if (tk.thr == KEY_NONE) {
-            cert = false;
-        } else {
-            const double dk = (double)key_dist(tk.thr);
-            const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
-            const double C2 = 1.52587890625e-5;
-            bool ok = true;
-            for (int j = lane; j < r.take; j += 32) {
-                const uint32_t l = r.probes[(size_t)q * r.take + j];
-                if (r.lend[l] <= r.lbeg[l]) continue;
-                const double rh = (double)r.rh[l];
-                const double D = (double)r.coarse[(size_t)q * r.nlist + l];
-                const double R = sqrt(D) * (1.0 + 1.52587890625e-5);
-                const double El = C1 * R * rh + C2 * (R * R + rh * rh) + 1e-30;
-                const double Rl = sqrt(D) * (1.0 - 1.52587890625e-5) - rh;
-                const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - Eadc : -1.0;
-                ok = ok && ((dk + Eadc + El < B) || (dk < lower));
-            }
-            cert = __all_sync(0xffffffffu, ok);
+    // whole-query failures: every list is re-scanned and nothing is kept
+    bool fail_all = c > (unsigned)r.cap || r.qbad[q] != 0u ||
+                    (!isinf(B) && tk.thr == KEY_NONE);
+    const double dk = tk.thr == KEY_NONE ? 0.0 : (double)key_dist(tk.thr);
+    // per-list verdict for probe j (true: no code of the list outside the
+    // shortlist can enter the exact top-k)
+    auto list_ok = [&](int j) -> bool {
+        const uint32_t l = r.probes[(size_t)q * r.take + j];
+        if (r.lend[l] <= r.lbeg[l]) return true;
+        if (isinf(B)) return true;  // every code of the list is in the shortlist
+        const double rh = (double)r.rh[l];
+        const double D = (double)r.coarse[(size_t)q * r.nlist + l];
+        const double R = sqrt(D) * (1.0 + 1.52587890625e-5);
+        const double El = C1 * R * rh + C2 * (R * R + rh * rh) + 1e-30;
+        const double Rl = sqrt(D) * (1.0 - 1.52587890625e-5) - rh;
+        const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - Eadc : -1.0;
+        return (dk + Eadc + El < B) || (dk < lower);
+    };
+    bool ok = !fail_all;
+    for (int j0 = 0; ok && j0 < r.take; j0 += 32) {
+        const int j = j0 + lane;
+        ok = __all_sync(0xffffffffu, j >= r.take || list_ok(j));
+    }
+    if (ok) {
+        tk.store(r.out_keys + (size_t)q * r.k);
+        return;
+    }
+    uint32_t slot = 0;
+    if (lane == 0) {
+        slot = atomicAdd(r.flag_count, 1u);
+        r.flag_list[slot] = r.qbase + (uint32_t)q;
+    }
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    uint32_t* fp = r.fail_probes + (size_t)slot * r.take;
+    // failed lists, compacted; shortlisted codes of those lists are dropped
+    // from the seed (the exact re-scan meets them again)
+    unsigned nf = 0;
+    bool drop0 = false, drop1 = false;
+    for (int j0 = 0; j0 < r.take; j0 += 32) {
+        const int j = j0 + lane;
+        const bool inr = j < r.take;
+        const uint32_t l = inr ? r.probes[(size_t)q * r.take + j] : 0u;
+        const bool bad = inr && (fail_all || !list_ok(j));
+        unsigned mask = __ballot_sync(0xffffffffu, bad);
+        if (bad) fp[nf + __popc(mask & ((1u << lane) - 1u))] = l;
+        nf += __popc(mask);
+        while (mask) {
+            const int b = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const int lf = (int)__shfl_sync(0xffffffffu, l, b);
+            drop0 |= el[0] == lf;
+            drop1 |= el[1] == lf;
         }
     }
-    if (!cert && lane == 0) {
-        const uint32_t idx = atomicAdd(r.flag_count, 1u);
-        r.flag_list[idx] = r.qbase + (uint32_t)q;
-    }
+    if (lane == 0) r.fail_cnt[slot] = nf;
+    WarpTopK<1> seed;
+    seed.init(r.k, buf + warp * 64);
+    __syncwarp();
+    const uint64_t s0 = drop0 ? KEY_NONE : ek[0], s1 = drop1 ? KEY_NONE : ek[1];
+    if (__any_sync(0xffffffffu, s0 != KEY_NONE)) seed.merge32(s0);
+    if (__any_sync(0xffffffffu, s1 != KEY_NONE)) seed.merge32(s1);
+    seed.store(r.out_keys + (size_t)q * r.k);
 }
 
 // ---------------------------------------------------------------------------
@@ -933,7 +979,7 @@ namespace {
 void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
               const uint32_t* probes, const float* coarse, const uint64_t* lbeg,
               const uint64_t* lend, uint64_t* out_keys, uint32_t* flags, uint32_t qbase,
-              unsigned long long* stat, int* err) {
+              unsigned long long* stat, int* err, uint32_t* fail_probes, uint32_t* fail_cnt) {
     using namespace ivtc;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -1062,6 +1108,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.qbase = qbase;
     r.flag_count = flags;
     r.flag_list = flags + 1;
+    r.fail_probes = fail_probes;
+    r.fail_cnt = fail_cnt;
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
     if (order == ORDER_LANE8) certify_kernel<ORDER_LANE8><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
     else certify_kernel<ORDER_FAST4><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
@@ -1073,7 +1121,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 // Tensor-core shortlist + exact rescoring of nq queries whose probes and
 // coarse distances are in h->s_probe / h->s_coarse.  Writes [nq][k] exact keys
 // and lists uncertified queries in flags (flags[0] = count, then indices);
-// returns that count.  Queries run in chunks that keep the pass-1 dump
+// returns that count.  For each listed query, t_fprobes / t_fcnt name the
+// lists to re-scan exactly and its out_keys row holds the seed (the exact
+// top-k of its shortlisted codes in the other lists).  Queries run in chunks that keep the pass-1 dump
 // (one row of distances per query) within 1 GiB.
 uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
                        size_t take, const uint64_t* lbeg, const uint64_t* lend,
@@ -1084,6 +1134,8 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     const size_t budget = (size_t)1 << 28;  // floats
     const size_t chunk = std::max<size_t>(1, std::min(nq, budget / std::max<size_t>(h->tc_maxpad, 1)));
     h->t_range.ensure(8);
+    h->t_fprobes.ensure(nq * take);
+    h->t_fcnt.ensure(nq);
     int* err = reinterpret_cast<int*>(h->t_range.p + 4);
     FDB_CUDA(cudaMemsetAsync(flags, 0, 4, s));
     FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
@@ -1091,7 +1143,7 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
         const size_t nc = std::min(chunk, nq - q0);
         tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,
                  h->s_coarse.p + q0 * h->nlist, lbeg, lend, out_keys + q0 * k, flags,
-                 (uint32_t)q0, stat, err);
+                 (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p);
     }
     uint32_t hv[2] = {0, 0};
     FDB_CUDA(cudaMemcpyAsync(&hv[0], flags, 4, cudaMemcpyDeviceToHost, s));

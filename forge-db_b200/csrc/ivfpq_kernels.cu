@@ -405,8 +405,11 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
         WarpTopK<P> tk;
         tk.init(a.k, wbuf + warp * 64);
         unsigned long long nscan = 0, nl = 0;
-        for (int p = 0; p < a.nprobe; ++p) {
-            const uint32_t l = a.probes[(size_t)q * a.nprobe + p];
+        const uint32_t* pl = a.probe_list ? a.probe_list + (size_t)qi * a.nprobe
+                                          : a.probes + (size_t)q * a.nprobe;
+        const int npq = a.probe_list ? (int)a.probe_cnt[qi] : a.nprobe;
+        for (int p = 0; p < npq; ++p) {
+            const uint32_t l = pl[p];
             const uint64_t beg = a.offs[l], end = a.ends[l];
             if (beg == end) continue;  // empty, or held by another device
             __syncthreads();           // previous list's LUT no longer in use
@@ -465,6 +468,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
         __syncthreads();
         if (warp == 0) {
             block_merge_warp0(tk, lists, SCAN_WARPS);
+            if (a.seed) tk.ingest(a.out_keys + (size_t)q * a.k, a.k);
             tk.store(a.out_keys + (size_t)q * a.k);
         }
         if (threadIdx.x == 0 && a.stat) {
