@@ -25,10 +25,11 @@
 // tile's ||rhat||^2 values (512 bytes, aligned) are staged into shared memory
 // by a bulk copy next to the tile itself.
 //
-// Work is split into items (one list x up to 128 pair rows).  A persistent
-// grid of one CTA per SM takes items in a fixed snake order over a list order
-// sorted by decreasing list length, so concurrent CTAs share a list's codes
-// in L2 and the long lists start first.  Warp roles as in the brute-force
+// Work is split into items (one list x up to 128 pair rows), ordered by
+// decreasing list length.  A persistent grid of one CTA per SM takes them
+// from an atomic counter (longest first, so the tail is short; concurrent
+// CTAs on one list's items share its codes in L2); the next item's A tile
+// loads while the current item finishes.  Warp roles as in the brute-force
 // kernel: warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner, warps
 // 4.. = epilogue; every mbarrier wait is bounded and an abort drains the
 // in-flight copies and MMAs before TMEM is freed.
@@ -68,6 +69,7 @@ struct Item {
 struct PassParams {
     const Item* items;
     const uint32_t* range;   // device-side {first item, item count} of this pass
+    unsigned* next;          // item counter of this pass, preset to 0
     int katoms;
     const uint32_t* pair_q;  // [pairs] query of each pair row
     const float* pair_rn;    // [pairs] ||q - c_l||^2 (the exact coarse distance)
@@ -87,11 +89,6 @@ constexpr int NSTAGE = 4;  // B tile stages
 constexpr int NEPI = 8;    // epilogue warps: 4 TMEM lane quadrants x 2 column halves
 constexpr int NCV = 4;     // ||rhat||^2 stages
 
-// Items of CTA `cta` in round r: left to right on even rounds, right to left
-// on odd ones, so each CTA's total stays close to the mean.
-__device__ __forceinline__ int snake(int r, int cta, int G) {
-    return r * G + ((r & 1) ? (G - 1 - cta) : cta);
-}
 
 // 32 consecutive floats of a shared buffer (warp-uniform address: broadcast).
 __device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
@@ -123,28 +120,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
     const int KA = p.katoms;
     const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
-    unsigned char* a_tile = smem;
-    unsigned char* b_tile = a_tile + KA * ATOM_BYTES;
+    unsigned char* a_tile = smem;                           // 2 slots of KA atoms
+    unsigned char* b_tile = a_tile + 2 * KA * ATOM_BYTES;   // NS stages of KA atoms
     float* cvbuf = reinterpret_cast<float*>(b_tile + NS * KA * ATOM_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(cvbuf + NCV * CV_FLOATS);
-    uint64_t* a_full = bars;
-    uint64_t* a_empty = bars + 1;
-    uint64_t* b_full = bars + 2;           // [NS]
+    uint64_t* a_full = bars;               // [2]
+    uint64_t* a_empty = bars + 2;          // [2]
+    uint64_t* b_full = bars + 4;           // [NS]
     uint64_t* b_empty = b_full + NS;       // [NS]
     uint64_t* t_full = b_empty + NS;       // [2]
     uint64_t* t_empty = t_full + 2;        // [2]
     uint64_t* cv_full = t_empty + 2;       // [NCV]
     uint64_t* cv_empty = cv_full + NCV;    // [NCV]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cv_empty + NCV);
+    uint64_t* it_full = cv_empty + NCV;    // [2] item ring
+    uint64_t* it_empty = it_full + 2;      // [2]
+    int* ring = reinterpret_cast<int*>(it_empty + 2);        // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, cta = blockIdx.x;
     const Item* items = p.items + p.range[0];
     const int nitems = (int)p.range[1];
 
     if (threadIdx.x == 0) {
-        mbar_init(a_full, 1);
-        mbar_init(a_empty, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(a_full + i, 1);
+            mbar_init(a_empty + i, 1);
+            mbar_init(it_full + i, 1);
+            mbar_init(it_empty + i, 1 + NEPI);
+        }
         for (int i = 0; i < NS; ++i) {
             mbar_init(b_full + i, 1);
             mbar_init(b_empty + i, 1);
@@ -176,23 +179,30 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0; i < NS; ++i) last_use[i] = -1;
 #pragma unroll
     for (int i = 0; i < NCV; ++i) last_cv[i] = -1;
-    int last_a = -1;  // producer: last item whose A tile was requested
+    int last_a[2] = {-1, -1};  // producer: last item whose A tile was requested, per slot
     int last_g = -1;  // MMA issuer: last tile committed
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            // Items are taken from the pass's counter (largest first, as they
+            // are ordered) and handed to the other roles through a 2-slot ring.
             int g = 0;
             bool ok = true;
             for (int r = 0; ok; ++r) {
-                const int idx = snake(r, cta, G);
+                const int slot = r & 1;
+                if (r >= 2 && !mbar_wait(it_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
+                const int idx = (int)atomicAdd(p.next, 1u);
+                ring[slot] = idx;
+                mbar_arrive(it_full + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
-                if (r > 0 && !mbar_wait(a_empty, (r - 1) & 1, p.err)) break;
-                mbar_expect_tx(a_full, stage_bytes);
+                if (r >= 2 && !mbar_wait(a_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
+                mbar_expect_tx(a_full + slot, stage_bytes);
                 for (int a = 0; a < KA; ++a)
-                    tma_load_2d(a_tile + a * ATOM_BYTES, &amap, a_full, a * KATOM, (int)it.a0);
-                last_a = r;
+                    tma_load_2d(a_tile + (slot * KA + a) * ATOM_BYTES, &amap, a_full + slot,
+                                a * KATOM, (int)it.a0);
+                last_a[slot] = r;
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS;
@@ -227,11 +237,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             int g = 0;
             bool ok = true;
             for (int r = 0; ok; ++r) {
-                const int idx = snake(r, cta, G);
+                const int slot = r & 1;
+                if (!mbar_wait(it_full + slot, (r >> 1) & 1, p.err)) break;
+                const int idx = *(volatile int*)(ring + slot);
+                mbar_arrive(it_empty + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
-                if (!mbar_wait(a_full, r & 1, p.err)) break;
+                if (!mbar_wait(a_full + slot, (r >> 1) & 1, p.err)) break;
                 tc_fence_after();
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS, b = g & 1;
@@ -245,7 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)(b * TILE_N);
-                    const uint32_t abase = smem_u32(a_tile);
+                    const uint32_t abase = smem_u32(a_tile + slot * KA * ATOM_BYTES);
                     const uint32_t bbase = smem_u32(b_tile + s * KA * ATOM_BYTES);
                     for (int a = 0; a < KA; ++a) {
 #pragma unroll
@@ -259,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     umma_commit(t_full + b);   // accumulator b is ready for the epilogue
                     last_g = g;
                 }
-                if (ok) umma_commit(a_empty);  // the A tile may be replaced
+                if (ok) umma_commit(a_empty + slot);  // the A slot may be refilled
             }
         }
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + NEPI) {
@@ -272,7 +285,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         int g = 0;
         bool alive = true;
         for (int r = 0; alive; ++r) {
-            const int idx = snake(r, cta, G);
+            const int slot = r & 1;
+            if (!warp_wait(it_full + slot, (r >> 1) & 1, p.err, lane)) break;
+            // lane 0 performed the acquiring wait: it reads the slot for the warp
+            int idx = 0;
+            if (lane == 0) {
+                idx = *(volatile int*)(ring + slot);
+                mbar_arrive(it_empty + slot);
+            }
+            idx = __shfl_sync(0xffffffffu, idx, 0);
             if (idx >= nitems) break;
             const Item it = items[idx];
             const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
@@ -412,11 +433,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                            clock64() - t0 < WAIT_CYCLES) {
                     }
                 }
-            if (last_a >= 0) {
-                const unsigned long long t0 = clock64();
-                while (!mbar_try(a_full, last_a & 1) && clock64() - t0 < WAIT_CYCLES) {
+            for (int sl = 0; sl < 2; ++sl)
+                if (last_a[sl] >= 0) {
+                    const unsigned long long t0 = clock64();
+                    while (!mbar_try(a_full + sl, (last_a[sl] >> 1) & 1) &&
+                           clock64() - t0 < WAIT_CYCLES) {
+                    }
                 }
-            }
         }
         if (warp == 1 && lane == 0 && last_g >= 0) {
             const unsigned long long t0 = clock64();
@@ -875,8 +898,8 @@ __global__ void list_rh_kernel(const float* __restrict__ norm, const uint32_t* _
 }
 
 size_t pass_smem(int katoms) {
-    return 1024 + (size_t)(1 + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
-           (size_t)(2 + 2 * NSTAGE + 4 + 2 * NCV) * 8 + 16;
+    return 1024 + (size_t)(2 + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
+           (size_t)(4 + 2 * NSTAGE + 4 + 2 * NCV + 4) * 8 + 2 * 4 + 16;
 }
 
 template <int EPI>
@@ -1065,6 +1088,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.cand_cnt = h->t_cand_cnt.p;
     p.cap = cap;
     p.err = err;
+    p.next = h->t_range.p + 5;
+    FDB_CUDA(cudaMemsetAsync(h->t_range.p + 5, 0, 8, s));
     const int grid = c.sm_count;
     launch_pass<EPI_DUMP>(s, am, bm, grid, p);
     select1_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
@@ -1073,6 +1098,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_LAUNCH_CHECK();
     // --- pass 2: the other lists against tau ---
     p.range = h->t_range.p + 2;
+    p.next = h->t_range.p + 6;
     launch_pass<EPI_FILTER>(s, am, bm, grid, p);
     // --- shortlist, exact rescoring, certification ---
     h->s_approx.ensure(nq * LIST_K);
