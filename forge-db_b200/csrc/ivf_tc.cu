@@ -88,6 +88,7 @@ struct PassParams {
 constexpr int NSTAGE = 4;  // B tile stages
 constexpr int NEPI = 8;    // epilogue warps: 4 TMEM lane quadrants x 2 column halves
 constexpr int NCV = 4;     // ||rhat||^2 stages
+constexpr int NACC = 4;    // TMEM accumulators (128 columns each: all 512 columns)
 
 
 // 32 consecutive floats of a shared buffer (warp-uniform address: broadcast).
@@ -128,9 +129,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* a_empty = bars + 2;          // [2]
     uint64_t* b_full = bars + 4;           // [NS]
     uint64_t* b_empty = b_full + NS;       // [NS]
-    uint64_t* t_full = b_empty + NS;       // [2]
-    uint64_t* t_empty = t_full + 2;        // [2]
-    uint64_t* cv_full = t_empty + 2;       // [NCV]
+    uint64_t* t_full = b_empty + NS;       // [NACC]
+    uint64_t* t_empty = t_full + NACC;     // [NACC]
+    uint64_t* cv_full = t_empty + NACC;    // [NCV]
     uint64_t* cv_empty = cv_full + NCV;    // [NCV]
     uint64_t* it_full = cv_empty + NCV;    // [2] item ring
     uint64_t* it_empty = it_full + 2;      // [2]
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(b_full + i, 1);
             mbar_init(b_empty + i, 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NACC; ++i) {
             mbar_init(t_full + i, 1);
             mbar_init(t_empty + i, NEPI);
         }
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(2 * TILE_N));
+                     "r"(NACC * TILE_N));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         tc_fence_before();
     }
@@ -247,8 +248,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!mbar_wait(a_full + slot, (r >> 1) & 1, p.err)) break;
                 tc_fence_after();
                 for (int t = 0; t < nt; ++t, ++g) {
-                    const int s = g % NS, use = g / NS, b = g & 1;
-                    if (g >= 2 && !mbar_wait(t_empty + b, ((g >> 1) - 1) & 1, p.err)) {
+                    const int s = g % NS, use = g / NS, b = g % NACC;
+                    if (g >= NACC && !mbar_wait(t_empty + b, ((g / NACC) - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
@@ -311,8 +312,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     rok ? (tau - rn) + ldexpf(2.0f * fabsf(rn) + 2.0f * p.colmax + fabsf(tau), -20)
                         : -INF;
                 for (int t = 0; t < nt; ++t, ++g) {
-                    const int b = g & 1, c = g % NCV;
-                    if (!warp_wait(t_full + b, (g >> 1) & 1, p.err, lane) ||
+                    const int b = g % NACC, c = g % NCV;
+                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
                         !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
                         alive = false;
                         break;
@@ -368,8 +369,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // pass 1: every distance of the row's list goes to its dump row
                 float* drow = rok ? p.dump + p.seg[pr] : nullptr;
                 for (int t = 0; t < nt; ++t, ++g) {
-                    const int b = g & 1, c = g % NCV;
-                    if (!warp_wait(t_full + b, (g >> 1) & 1, p.err, lane) ||
+                    const int b = g % NACC, c = g % NCV;
+                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
                         !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
                         alive = false;
                         break;
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (warp == 1 && lane == 0 && last_g >= 0) {
             const unsigned long long t0 = clock64();
-            while (!mbar_try(t_full + (last_g & 1), (last_g >> 1) & 1) &&
+            while (!mbar_try(t_full + (last_g % NACC), (last_g / NACC) & 1) &&
                    clock64() - t0 < WAIT_CYCLES) {
             }
         }
@@ -452,7 +453,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(2 * TILE_N));
+                     "r"(NACC * TILE_N));
     }
 }
 
@@ -899,7 +900,7 @@ __global__ void list_rh_kernel(const float* __restrict__ norm, const uint32_t* _
 
 size_t pass_smem(int katoms) {
     return 1024 + (size_t)(2 + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
-           (size_t)(4 + 2 * NSTAGE + 4 + 2 * NCV + 4) * 8 + 2 * 4 + 16;
+           (size_t)(4 + 2 * NSTAGE + 2 * NACC + 2 * NCV + 4) * 8 + 2 * 4 + 16;
 }
 
 template <int EPI>
