@@ -55,15 +55,23 @@ constexpr int EPI_WARP0 = 4;
 constexpr int LIST_K = 64;  // pass-1 list per query = shortlist length
 constexpr int EPI_DUMP = 0, EPI_FILTER = 1;
 constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
+#ifndef FDB_IVF_CHUNK_TILES
+#define FDB_IVF_CHUNK_TILES 16
+#endif
+#ifndef FDB_IVF_SPIN_WAITS
+#define FDB_IVF_SPIN_WAITS 1
+#endif
+constexpr int CHUNK_TILES = FDB_IVF_CHUNK_TILES;  // B tiles per item at most (long lists are split)
 constexpr float INF = __builtin_huge_valf();
 
 struct Item {
     uint32_t a0;    // first pair row of the A tile
     uint32_t na;    // pair rows in use (1..128)
-    uint32_t b0;    // first row of the list in the padded decoded layout
-    uint32_t nb;    // codes in the list (>= 1)
-    uint32_t tag0;  // row of the list's first code in the index (key tag)
-    uint32_t pad[3];
+    uint32_t b0;    // first row of this chunk of the list in the padded decoded layout
+    uint32_t nb;    // codes in this chunk (>= 1)
+    uint32_t tag0;  // row of the chunk's first code in the index (key tag)
+    uint32_t col0;  // index of the chunk's first code within its list
+    uint32_t pad[2];
 };
 
 struct PassParams {
@@ -85,9 +93,16 @@ struct PassParams {
     int* err;
 };
 
-constexpr int NSTAGE = 4;  // B tile stages
+#ifndef FDB_IVF_NSTAGE
+#define FDB_IVF_NSTAGE 4
+#endif
+#ifndef FDB_IVF_ASLOTS
+#define FDB_IVF_ASLOTS 2
+#endif
+constexpr int NSTAGE = FDB_IVF_NSTAGE;  // B tile stages
+constexpr int ASLOTS = FDB_IVF_ASLOTS;  // A tile slots (2: the next item's A loads early)
 constexpr int NEPI = 8;    // epilogue warps: 4 TMEM lane quadrants x 2 column halves
-constexpr int NCV = 4;     // ||rhat||^2 stages
+constexpr int NCV = NSTAGE; // ||rhat||^2 stages (one per B stage)
 constexpr int NACC = 4;    // TMEM accumulators (128 columns each: all 512 columns)
 
 
@@ -104,10 +119,27 @@ __device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
     }
 }
 
+// Waits of the single-thread roles (TMA producer, MMA issuer): polling by
+// default, since their wake-up latency is on the pipeline's critical path.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* err) {
+#if FDB_IVF_SPIN_WAITS
+    return mbar_wait_spin(bar, parity, err);
+#else
+    return mbar_wait(bar, parity, err);
+#endif
+}
+
+#ifndef FDB_IVF_EPI_SPIN
+#define FDB_IVF_EPI_SPIN 0
+#endif
 // Bounded wait of one lane, verdict shared with the warp.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int lane) {
     int got = 0;
+#if FDB_IVF_EPI_SPIN
+    if (lane == 0) got = mbar_wait_spin(bar, parity, err) ? 1 : 0;
+#else
     if (lane == 0) got = mbar_wait(bar, parity, err) ? 1 : 0;
+#endif
     return __shfl_sync(0xffffffffu, got, 0) != 0;
 }
 
@@ -121,13 +153,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
     const int KA = p.katoms;
     const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
-    unsigned char* a_tile = smem;                           // 2 slots of KA atoms
-    unsigned char* b_tile = a_tile + 2 * KA * ATOM_BYTES;   // NS stages of KA atoms
+    unsigned char* a_tile = smem;                                // ASLOTS slots of KA atoms
+    unsigned char* b_tile = a_tile + ASLOTS * KA * ATOM_BYTES;   // NS stages of KA atoms
     float* cvbuf = reinterpret_cast<float*>(b_tile + NS * KA * ATOM_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(cvbuf + NCV * CV_FLOATS);
-    uint64_t* a_full = bars;               // [2]
-    uint64_t* a_empty = bars + 2;          // [2]
-    uint64_t* b_full = bars + 4;           // [NS]
+    uint64_t* a_full = bars;               // [ASLOTS]
+    uint64_t* a_empty = bars + ASLOTS;     // [ASLOTS]
+    uint64_t* b_full = bars + 2 * ASLOTS;  // [NS]
     uint64_t* b_empty = b_full + NS;       // [NS]
     uint64_t* t_full = b_empty + NS;       // [NACC]
     uint64_t* t_empty = t_full + NACC;     // [NACC]
@@ -143,9 +175,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int nitems = (int)p.range[1];
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < ASLOTS; ++i) {
             mbar_init(a_full + i, 1);
             mbar_init(a_empty + i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(it_full + i, 1);
             mbar_init(it_empty + i, 1 + NEPI);
         }
@@ -180,7 +214,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0; i < NS; ++i) last_use[i] = -1;
 #pragma unroll
     for (int i = 0; i < NCV; ++i) last_cv[i] = -1;
-    int last_a[2] = {-1, -1};  // producer: last item whose A tile was requested, per slot
+    int last_a[2] = {-1, -1};  // producer: last item whose A tile was requested, per A slot
     int last_g = -1;  // MMA issuer: last tile committed
 
     if (warp == 0) {
@@ -192,22 +226,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int r = 0; ok; ++r) {
                 const int slot = r & 1;
-                if (r >= 2 && !mbar_wait(it_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
+                if (r >= 2 && !role_wait(it_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
                 const int idx = (int)atomicAdd(p.next, 1u);
                 ring[slot] = idx;
                 mbar_arrive(it_full + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
-                if (r >= 2 && !mbar_wait(a_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
-                mbar_expect_tx(a_full + slot, stage_bytes);
+                const int as = r % ASLOTS, au = r / ASLOTS;
+                if (r >= ASLOTS && !role_wait(a_empty + as, (au - 1) & 1, p.err)) break;
+                mbar_expect_tx(a_full + as, stage_bytes);
                 for (int a = 0; a < KA; ++a)
-                    tma_load_2d(a_tile + (slot * KA + a) * ATOM_BYTES, &amap, a_full + slot,
+                    tma_load_2d(a_tile + (as * KA + a) * ATOM_BYTES, &amap, a_full + as,
                                 a * KATOM, (int)it.a0);
-                last_a[slot] = r;
+                last_a[as] = r;
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS;
-                    if (g >= NS && !mbar_wait(b_empty + s, (use - 1) & 1, p.err)) {
+                    if (g >= NS && !role_wait(b_empty + s, (use - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
@@ -220,7 +255,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < NS; ++i)
                         if (i == s) last_use[i] = use;
                     const int c = g % NCV, cu = g / NCV;
-                    if (g >= NCV && !mbar_wait(cv_empty + c, (cu - 1) & 1, p.err)) {
+                    if (g >= NCV && !role_wait(cv_empty + c, (cu - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
@@ -239,27 +274,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int r = 0; ok; ++r) {
                 const int slot = r & 1;
-                if (!mbar_wait(it_full + slot, (r >> 1) & 1, p.err)) break;
+                if (!role_wait(it_full + slot, (r >> 1) & 1, p.err)) break;
                 const int idx = *(volatile int*)(ring + slot);
                 mbar_arrive(it_empty + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
-                if (!mbar_wait(a_full + slot, (r >> 1) & 1, p.err)) break;
+                const int as = r % ASLOTS;
+                if (!role_wait(a_full + as, (r / ASLOTS) & 1, p.err)) break;
                 tc_fence_after();
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS, b = g % NACC;
-                    if (g >= NACC && !mbar_wait(t_empty + b, ((g / NACC) - 1) & 1, p.err)) {
+                    if (g >= NACC && !role_wait(t_empty + b, ((g / NACC) - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
-                    if (!mbar_wait(b_full + s, use & 1, p.err)) {
+                    if (!role_wait(b_full + s, use & 1, p.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)(b * TILE_N);
-                    const uint32_t abase = smem_u32(a_tile + slot * KA * ATOM_BYTES);
+                    const uint32_t abase = smem_u32(a_tile + as * KA * ATOM_BYTES);
                     const uint32_t bbase = smem_u32(b_tile + s * KA * ATOM_BYTES);
                     for (int a = 0; a < KA; ++a) {
 #pragma unroll
@@ -273,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     umma_commit(t_full + b);   // accumulator b is ready for the epilogue
                     last_g = g;
                 }
-                if (ok) umma_commit(a_empty + slot);  // the A slot may be refilled
+                if (ok) umma_commit(a_empty + as);  // the A slot may be refilled
             }
         }
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + NEPI) {
@@ -303,6 +339,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int q = rok ? (int)p.pair_q[pr] : 0;
             const float rn = rok ? p.pair_rn[pr] : 0.0f;
             const float s2 = rok ? p.pair_s2[pr] : 0.0f;
+            // Chunk pipeline over the item's tiles: a warp scores 64 columns of a
+            // tile as two 32-column chunks; chunk 1 loads from TMEM while chunk 0
+            // is scored, and the next tile's chunk 0 while chunk 1 is scored.
+            // ||rhat||^2 values are read from the staged slot as they are used.
+            uint32_t va[32], vb[32];
+            auto begin_tile = [&](int gg) -> bool {
+                const int b = gg % NACC, c = gg % NCV;
+                if (!warp_wait(t_full + b, (gg / NACC) & 1, p.err, lane) ||
+                    !warp_wait(cv_full + c, (gg / NCV) & 1, p.err, lane))
+                    return false;
+                tc_fence_after();
+                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
+                return true;
+            };
             if constexpr (EPI == EPI_FILTER) {
                 const float tau = rok ? p.tau[q] : -INF;
                 // Admission test fma(s2, s, ||rhat||^2) <= (tau - rn) + slack: the
@@ -311,106 +361,107 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const float tt =
                     rok ? (tau - rn) + ldexpf(2.0f * fabsf(rn) + 2.0f * p.colmax + fabsf(tau), -20)
                         : -INF;
-                for (int t = 0; t < nt; ++t, ++g) {
-                    const int b = g % NACC, c = g % NCV;
-                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
-                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
-                        alive = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    uint32_t va[32], vb[32];
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32),
-                                     vb);
-                    float ca[32], cbv[32];
-                    load32(cvbuf + c * CV_FLOATS + half * 64, ca);
-                    load32(cvbuf + c * CV_FLOATS + half * 64 + 32, cbv);
-                    tmem_wait_ld();
-                    // both chunks are in registers: release the accumulator and values
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(t_empty + b);
-                        mbar_arrive(cv_empty + c);
+                auto score = [&](const uint32_t(&v)[32], const float* cvs, int cidx) {
+                    const int nvalid = min(32, (int)it.nb - cidx);
+                    const uint32_t tag0 = it.tag0 + (uint32_t)cidx;
+                    // The chunk's smallest test value, by a tree of minimums (short
+                    // dependency chains); one vote decides whether any lane has a hit.
+                    float x[32];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 cc = reinterpret_cast<const float4*>(cvs)[i];
+                        x[4 * i] = __fmaf_rn(s2, __uint_as_float(v[4 * i]), cc.x);
+                        x[4 * i + 1] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]), cc.y);
+                        x[4 * i + 2] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]), cc.z);
+                        x[4 * i + 3] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]), cc.w);
                     }
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint32_t* v = h == 0 ? va : vb;
-                        const float* cv = h == 0 ? ca : cbv;
-                        const int cidx = t * TILE_N + half * 64 + h * 32;
-                        const int nvalid = min(32, (int)it.nb - cidx);
-                        const uint32_t tag0 = it.tag0 + (uint32_t)cidx;
+                    for (int w2 = 16; w2 >= 1; w2 >>= 1)
 #pragma unroll
-                        for (int g8 = 0; g8 < 4; ++g8) {
-                            bool any = false;
+                        for (int i = 0; i < w2; ++i) x[i] = fminf(x[i], x[i + w2]);
+                    if (!__any_sync(0xffffffffu, x[0] <= tt)) return;
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) {
+                        const float4 c0 = reinterpret_cast<const float4*>(cvs)[2 * g8];
+                        const float4 c1 = reinterpret_cast<const float4*>(cvs)[2 * g8 + 1];
+                        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                        bool any = false;
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj)
+                            any |= __fmaf_rn(s2, __uint_as_float(v[g8 * 8 + jj]), cv[jj]) <= tt;
+                        if (__any_sync(0xffffffffu, any)) {
 #pragma unroll
                             for (int jj = 0; jj < 8; ++jj) {
                                 const int j = g8 * 8 + jj;
-                                any |= __fmaf_rn(s2, __uint_as_float(v[j]), cv[j]) <= tt;
-                            }
-                            if (__any_sync(0xffffffffu, any)) {
-#pragma unroll
-                                for (int jj = 0; jj < 8; ++jj) {
-                                    const int j = g8 * 8 + jj;
-                                    const float d =
-                                        __fmaf_rn(s2, __uint_as_float(v[j]), __fadd_rn(rn, cv[j]));
-                                    if (rok && j < nvalid && d <= tau) {
-                                        const unsigned ix = atomicAdd(p.cand_cnt + q, 1u);
-                                        if (ix < (unsigned)p.cap)
-                                            p.cand[(size_t)q * p.cap + ix] = make_key(d, tag0 + j);
-                                    }
+                                const float d =
+                                    __fmaf_rn(s2, __uint_as_float(v[j]), __fadd_rn(rn, cv[jj]));
+                                if (rok && j < nvalid && d <= tau) {
+                                    const unsigned ix = atomicAdd(p.cand_cnt + q, 1u);
+                                    if (ix < (unsigned)p.cap)
+                                        p.cand[(size_t)q * p.cap + ix] = make_key(d, tag0 + j);
                                 }
                             }
                         }
                     }
+                };
+                if (nt > 0) {
+                    if (begin_tile(g)) tmem_wait_regs(va);
+                    else alive = false;
                 }
-            } else {
-                // pass 1: every distance of the row's list goes to its dump row
-                float* drow = rok ? p.dump + p.seg[pr] : nullptr;
-                for (int t = 0; t < nt; ++t, ++g) {
+                for (int t = 0; alive && t < nt; ++t, ++g) {
                     const int b = g % NACC, c = g % NCV;
-                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
-                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
-                        alive = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    uint32_t va[32], vb[32];
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32),
-                                     vb);
-                    float ca[32], cbv[32];
-                    load32(cvbuf + c * CV_FLOATS + half * 64, ca);
-                    load32(cvbuf + c * CV_FLOATS + half * 64 + 32, cbv);
-                    tmem_wait_ld();
+                    const float* cvs = cvbuf + c * CV_FLOATS + half * 64;
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32), vb);
+                    score(va, cvs, t * TILE_N + half * 64);
+                    tmem_wait_regs(vb);
+                    // both chunks of this tile are in registers: free the accumulator
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(t_empty + b);
-                        mbar_arrive(cv_empty + c);
-                    }
-                    if (rok) {
-                        // padding columns carry ||rhat||^2 = +inf and store +inf
-                        float4* dst = reinterpret_cast<float4*>(drow + t * TILE_N + half * 64);
+                    if (lane == 0) mbar_arrive(t_empty + b);
+                    const bool more = t + 1 < nt;
+                    if (more && !begin_tile(g + 1)) alive = false;
+                    score(vb, cvs + 32, t * TILE_N + half * 64 + 32);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cv_empty + c);
+                    if (more && alive) tmem_wait_regs(va);
+                }
+            } else {
+                // pass 1: every distance of the row's list goes to its dump row;
+                // padding columns carry ||rhat||^2 = +inf and store +inf
+                float* drow = rok ? p.dump + p.seg[pr] + it.col0 : nullptr;
+                auto dump = [&](const uint32_t(&v)[32], const float* cvs, int col) {
+                    if (!rok) return;
+                    float4* dst = reinterpret_cast<float4*>(drow + col);
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint32_t* v = h == 0 ? va : vb;
-                            const float* cv = h == 0 ? ca : cbv;
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                float4 o;
-                                o.x = __fmaf_rn(s2, __uint_as_float(v[4 * i]), __fadd_rn(rn, cv[4 * i]));
-                                o.y = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]),
-                                                __fadd_rn(rn, cv[4 * i + 1]));
-                                o.z = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]),
-                                                __fadd_rn(rn, cv[4 * i + 2]));
-                                o.w = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]),
-                                                __fadd_rn(rn, cv[4 * i + 3]));
-                                dst[h * 8 + i] = o;
-                            }
-                        }
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 cc = reinterpret_cast<const float4*>(cvs)[i];
+                        float4 o;
+                        o.x = __fmaf_rn(s2, __uint_as_float(v[4 * i]), __fadd_rn(rn, cc.x));
+                        o.y = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]), __fadd_rn(rn, cc.y));
+                        o.z = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]), __fadd_rn(rn, cc.z));
+                        o.w = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]), __fadd_rn(rn, cc.w));
+                        dst[i] = o;
                     }
+                };
+                if (nt > 0) {
+                    if (begin_tile(g)) tmem_wait_regs(va);
+                    else alive = false;
+                }
+                for (int t = 0; alive && t < nt; ++t, ++g) {
+                    const int b = g % NACC, c = g % NCV;
+                    const float* cvs = cvbuf + c * CV_FLOATS + half * 64;
+                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32), vb);
+                    dump(va, cvs, t * TILE_N + half * 64);
+                    tmem_wait_regs(vb);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(t_empty + b);
+                    const bool more = t + 1 < nt;
+                    if (more && !begin_tile(g + 1)) alive = false;
+                    dump(vb, cvs + 32, t * TILE_N + half * 64 + 32);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cv_empty + c);
+                    if (more && alive) tmem_wait_regs(va);
                 }
             }
         }
@@ -434,10 +485,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                            clock64() - t0 < WAIT_CYCLES) {
                     }
                 }
-            for (int sl = 0; sl < 2; ++sl)
+            for (int sl = 0; sl < ASLOTS; ++sl)
                 if (last_a[sl] >= 0) {
                     const unsigned long long t0 = clock64();
-                    while (!mbar_try(a_full + sl, (last_a[sl] >> 1) & 1) &&
+                    while (!mbar_try(a_full + sl, (last_a[sl] / ASLOTS) & 1) &&
                            clock64() - t0 < WAIT_CYCLES) {
                     }
                 }
@@ -569,14 +620,15 @@ __global__ void plen_kernel(const uint32_t* __restrict__ vals, const unsigned* _
     plen[i] = len;
 }
 
-// Items of both passes, lists in `lorder`, one block.  items[0 .. n1) are
-// pass 1, items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
+// Items of both passes, lists in `lorder`, one block: every (list, 128 pair
+// rows, chunk of up to CHUNK_TILES tiles).  items[0 .. n1) are pass 1,
+// items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
 constexpr int ITEM_THREADS = 1024;
 __global__ void __launch_bounds__(ITEM_THREADS)
     build_items_kernel(const unsigned* __restrict__ poff, int nlist,
                        const uint32_t* __restrict__ lorder, const uint64_t* __restrict__ lbeg,
                        const uint64_t* __restrict__ lend, const uint32_t* __restrict__ pstart,
-                       Item* __restrict__ items, uint32_t* __restrict__ range) {
+                       Item* __restrict__ items, unsigned cap, uint32_t* __restrict__ range) {
     typedef cub::BlockScan<unsigned, ITEM_THREADS> Scan;
     __shared__ typename Scan::TempStorage tmp;
     __shared__ unsigned carry;
@@ -592,31 +644,38 @@ __global__ void __launch_bounds__(ITEM_THREADS)
                 a0 = poff[pass * nlist + l];
                 cnt = poff[pass * nlist + l + 1] - a0;
             }
-            const unsigned nit = (cnt + TILE_M - 1) / TILE_M;
+            const unsigned len = i < nlist ? (unsigned)(lend[l] - lbeg[l]) : 0u;
+            const unsigned nrow = (cnt + TILE_M - 1) / TILE_M;
+            const unsigned nchunk = (len + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
+            const unsigned nit = nrow * nchunk;
             unsigned off, tot;
             Scan(tmp).ExclusiveSum(nit, off, tot);
             const unsigned at = carry + off;
             for (unsigned t = 0; t < nit; ++t) {
+                const unsigned rb = t / nchunk, ch = t - rb * nchunk;
+                const unsigned c0 = ch * CHUNK_TILES * TILE_N;
                 Item it;
-                it.a0 = a0 + t * TILE_M;
-                it.na = min((unsigned)TILE_M, cnt - t * TILE_M);
-                it.b0 = pstart[l];
-                it.nb = (uint32_t)(lend[l] - lbeg[l]);
-                it.tag0 = (uint32_t)lbeg[l];
-                it.pad[0] = it.pad[1] = it.pad[2] = 0;
-                items[at + t] = it;
+                it.a0 = a0 + rb * TILE_M;
+                it.na = min((unsigned)TILE_M, cnt - rb * TILE_M);
+                it.b0 = pstart[l] + c0;
+                it.nb = min((unsigned)(CHUNK_TILES * TILE_N), len - c0);
+                it.tag0 = (uint32_t)lbeg[l] + c0;
+                it.col0 = c0;
+                it.pad[0] = it.pad[1] = 0;
+                if (at + t < cap) items[at + t] = it;
             }
             __syncthreads();
             if (threadIdx.x == 0) carry += tot;
             __syncthreads();
         }
         if (threadIdx.x == 0) {
+            // (the host sizes items[] for every case; cap only guards it)
             if (pass == 0) {
                 range[0] = 0;
-                range[1] = carry;
-                range[2] = carry;
+                range[1] = min(carry, cap);
+                range[2] = min(carry, cap);
             } else {
-                range[3] = carry - range[2];
+                range[3] = min(carry, cap) - range[2];
             }
         }
         __syncthreads();
@@ -642,12 +701,22 @@ __global__ void __launch_bounds__(256)
         const uint32_t l = probes[vals[i]];
         const int nb = (int)(lend[l] - lbeg[l]);
         const uint32_t tag0 = (uint32_t)lbeg[l];
-        const float* row = dump + seg[i];
-        for (int base = 0; base < nb; base += 32) {
-            const int j = base + lane;
-            const bool ok = j < nb;
-            const uint64_t key = ok ? make_key(row[j], tag0 + (uint32_t)j) : KEY_NONE;
-            tk.add(key, ok);
+        // the row is padded to a multiple of 128 floats: 128 per step
+        const float4* row4 = reinterpret_cast<const float4*>(dump + seg[i]);
+        for (int base = 0; base < nb; base += 128) {
+            const float4 v = row4[(base >> 2) + lane];
+            const int j = base + 4 * lane;
+            const float d[4] = {v.x, v.y, v.z, v.w};
+            uint64_t key[4];
+            bool any = false;
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                key[x] = j + x < nb ? make_key(d[x], tag0 + (uint32_t)(j + x)) : KEY_NONE;
+                any |= key[x] < tk.thr;
+            }
+            if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+            for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
         }
         tk.flush();
     }
@@ -899,8 +968,8 @@ __global__ void list_rh_kernel(const float* __restrict__ norm, const uint32_t* _
 }
 
 size_t pass_smem(int katoms) {
-    return 1024 + (size_t)(2 + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
-           (size_t)(4 + 2 * NSTAGE + 2 * NACC + 2 * NCV + 4) * 8 + 2 * 4 + 16;
+    return 1024 + (size_t)(ASLOTS + NSTAGE) * katoms * ATOM_BYTES + (size_t)NCV * CV_FLOATS * 4 +
+           (size_t)(2 * ASLOTS + 2 * NSTAGE + 2 * NACC + 2 * NCV + 4) * 8 + 2 * 4 + 16;
 }
 
 template <int EPI>
@@ -1058,11 +1127,18 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp.p, tmp_seg, h->t_plen.p, h->t_seg.p,
                                            (int)nq + 1, s));
     h->t_dump.ensure(std::max<size_t>(1, nq * h->tc_maxpad));
-    const size_t max_items = np / TILE_M + 2 * std::min(np, (size_t)nlist) + 2;
+    // items per (pass, list) = ceil(P / 128) * ceil(tiles / CHUNK_TILES) <= (a + 1)(b + 1)
+    // with a = P / 128, b = tiles / CHUNK_TILES, summed over both passes
+    const size_t max_tiles = h->tc_maxpad / TILE_N;
+    const size_t all_tiles = h->tc_rows / TILE_N;
+    const size_t max_items = np * ((max_tiles + CHUNK_TILES - 1) / CHUNK_TILES) / TILE_M +
+                             np / TILE_M + 2 * (all_tiles / CHUNK_TILES + 1) +
+                             2 * (size_t)nlist + 2;
     h->t_items.ensure(max_items * sizeof(Item));
     Item* items = reinterpret_cast<Item*>(h->t_items.p);
     build_items_kernel<<<1, ITEM_THREADS, 0, s>>>(h->t_off.p, nlist, h->lorder.p, lbeg, lend,
-                                                  h->tc_pstart.p, items, h->t_range.p);
+                                                  h->tc_pstart.p, items, (unsigned)max_items,
+                                                  h->t_range.p);
     FDB_LAUNCH_CHECK();
     // --- pass 1: distances of each query's first list; its top-64 and tau ---
     const CUtensorMap am = make_map(h->t_a16.p, np, dpad);
