@@ -221,6 +221,26 @@ __device__ __forceinline__ float exact_adc(const float* __restrict__ q,
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
         int i = 0;
+        if (((reinterpret_cast<uintptr_t>(qs) | reinterpret_cast<uintptr_t>(cs) |
+              reinterpret_cast<uintptr_t>(b)) & 15) == 0) {
+            // same operations, operands fetched with 128-bit loads
+            for (; i + 8 <= sub; i += 8) {
+                const float4 q0 = __ldg(reinterpret_cast<const float4*>(qs + i));
+                const float4 q1 = __ldg(reinterpret_cast<const float4*>(qs + i + 4));
+                const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + i));
+                const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + i + 4));
+                const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + i));
+                const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + i + 4));
+                const float qa[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                const float ca[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float ba[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float d = __fsub_rn(__fsub_rn(qa[j], ca[j]), ba[j]);
+                    acc[j] = __fmaf_rn(d, d, acc[j]);
+                }
+            }
+        }
         for (; i + 8 <= sub; i += 8) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {

@@ -513,13 +513,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ---------------------------------------------------------------------------
 // Sort key of probe (q, p): its list for the query's pass-1 probe (the first
 // holding LIST_K+ codes, else the first non-empty one), nlist + list for the
-// query's other non-empty probes, 2 nlist for empty lists.  Also counts keys
-// and, when stat is given, lists and codes scanned.
+// query's other non-empty probes, 2 nlist for empty lists.  When stat is
+// given, also counts the lists and codes scanned.
 __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, int take,
                                  const uint64_t* __restrict__ lbeg,
                                  const uint64_t* __restrict__ lend, int nlist,
                                  uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
-                                 unsigned* __restrict__ counts, unsigned long long* stat) {
+                                 unsigned long long* stat) {
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= nq) return;
     const uint32_t* pq = probes + (size_t)q * take;
@@ -545,12 +545,26 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
         }
         keys[i] = key;
         vals[i] = (uint32_t)i;
-        atomicAdd(counts + key, 1u);
     }
     if (stat) {
         atomicAdd(stat, lists);
         atomicAdd(stat + 1, codes);
     }
+}
+
+// off[k] = the first position of key >= k in the sorted keys (k <= nkeys):
+// the segment offsets of the stable sort, without a histogram.
+__global__ void seg_offsets_kernel(const uint32_t* __restrict__ keys, unsigned n, int nkeys,
+                                   unsigned* __restrict__ off) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k > nkeys) return;
+    unsigned lo = 0, hi = n;
+    while (lo < hi) {
+        const unsigned mid = (lo + hi) >> 1;
+        if (keys[mid] < (uint32_t)k) lo = mid + 1;
+        else hi = mid;
+    }
+    off[k] = lo;
 }
 
 // One warp per sorted pair: the fp16 residual row r = fl(q - c_l) * 2^sa
@@ -573,14 +587,30 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
     const uint32_t l = probes[v];
     const float* qv = Q + (size_t)q * dim;
     const float* cv = cents + (size_t)l * dim;
+    // lane holds components 4 lane .. 4 lane + 3 (dpad <= 128)
+    const bool vec = dim == dpad && ((reinterpret_cast<uintptr_t>(qv) |
+                                      reinterpret_cast<uintptr_t>(cv)) & 15) == 0;
     float r[4];
     float mx = 0.0f;
+    if (vec) {
+        r[0] = r[1] = r[2] = r[3] = 0.0f;
+        if (4 * lane < dim) {
+            const float4 a = *reinterpret_cast<const float4*>(qv + 4 * lane);
+            const float4 c4 = *reinterpret_cast<const float4*>(cv + 4 * lane);
+            r[0] = __fsub_rn(a.x, c4.x);
+            r[1] = __fsub_rn(a.y, c4.y);
+            r[2] = __fsub_rn(a.z, c4.z);
+            r[3] = __fsub_rn(a.w, c4.w);
+        }
+    } else {
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const int c = lane + 32 * t;
-        r[t] = (c < dim) ? __fsub_rn(qv[c], cv[c]) : 0.0f;
-        mx = fmaxf(mx, fabsf(r[t]));
+        for (int t = 0; t < 4; ++t) {
+            const int c = 4 * lane + t;
+            r[t] = (c < dim) ? __fsub_rn(qv[c], cv[c]) : 0.0f;
+        }
     }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) mx = fmaxf(mx, fabsf(r[t]));
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     // exponent of the largest magnitude (subnormals count as 2^-127)
@@ -590,10 +620,13 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
     const float scale = __uint_as_float((uint32_t)(sa + 127) << 23);  // 2^sa, exact
     const int se = 1 - sa - sb;  // s2 = -2^se
     const bool bad = !(mx <= 3.0e38f) || se < -125 || se > 126;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const int c = lane + 32 * t;
-        if (c < dpad) a16[i * dpad + c] = __float2half_rn(bad ? 0.0f : __fmul_rn(r[t], scale));
+    if (4 * lane < dpad) {
+        __half2 h[2];
+        h[0] = __halves2half2(__float2half_rn(bad ? 0.0f : __fmul_rn(r[0], scale)),
+                              __float2half_rn(bad ? 0.0f : __fmul_rn(r[1], scale)));
+        h[1] = __halves2half2(__float2half_rn(bad ? 0.0f : __fmul_rn(r[2], scale)),
+                              __float2half_rn(bad ? 0.0f : __fmul_rn(r[3], scale)));
+        *reinterpret_cast<uint2*>(a16 + i * dpad + 4 * lane) = *reinterpret_cast<uint2*>(h);
     }
     if (lane == 0) {
         pair_q[i] = q;
@@ -1083,30 +1116,26 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     // --- group the pairs by (pass, list) ---
     h->t_keys.ensure(2 * np);
     h->t_vals.ensure(2 * np);
-    h->t_cnt.ensure((size_t)nkeys + 1);
     h->t_off.ensure((size_t)nkeys + 1);
-    FDB_CUDA(cudaMemsetAsync(h->t_cnt.p, 0, ((size_t)nkeys + 1) * 4, s));
     pair_keys_kernel<<<(unsigned)((nq + 127) / 128), 128, 0, s>>>(
-        probes, (int)nq, (int)take, lbeg, lend, nlist, h->t_keys.p, h->t_vals.p, h->t_cnt.p,
-        stat);
+        probes, (int)nq, (int)take, lbeg, lend, nlist, h->t_keys.p, h->t_vals.p, stat);
     FDB_LAUNCH_CHECK();
     h->t_plen.ensure(nq + 1);
     h->t_seg.ensure(nq + 1);
-    size_t tmp_sort = 0, tmp_scan = 0, tmp_seg = 0;
+    size_t tmp_sort = 0, tmp_seg = 0;
     const int end_bit = bits_for((uint32_t)nkeys);
     FDB_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_sort, h->t_keys.p, h->t_keys.p + np,
                                              h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
                                              s));
-    FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_scan, h->t_cnt.p, h->t_off.p, nkeys + 1,
-                                           s));
     FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_seg, h->t_plen.p, h->t_seg.p,
                                            (int)nq + 1, s));
-    h->t_tmp.ensure(std::max(tmp_sort, std::max(tmp_scan, tmp_seg)));
+    h->t_tmp.ensure(std::max(tmp_sort, tmp_seg));
     FDB_CUDA(cub::DeviceRadixSort::SortPairs(h->t_tmp.p, tmp_sort, h->t_keys.p, h->t_keys.p + np,
                                              h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
                                              s));
-    FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp.p, tmp_scan, h->t_cnt.p, h->t_off.p,
-                                           nkeys + 1, s));
+    seg_offsets_kernel<<<(unsigned)((nkeys + 1 + 255) / 256), 256, 0, s>>>(
+        h->t_keys.p + np, (unsigned)np, nkeys, h->t_off.p);
+    FDB_LAUNCH_CHECK();
     const uint32_t* svals = h->t_vals.p + np;
     // --- residual rows, dump rows and items ---
     h->t_a16.ensure(np * dpad);
