@@ -51,6 +51,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16/fp16 tensor peak (burst: the kernel runs in short launches)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured bf16_tflops (dense fp16 has the same rate)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """Samples SM clocks and clock-event reasons through NVML while running."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -118,6 +128,13 @@ def make_data():
 
 
 SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
+
+# DRAM bytes (read + write) per launch of the dominant kernel on the default
+# workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum).
+NCU_TRAFFIC = {"ivf_pass_filter": 322.4e6, "bf_gemm_filter": None}
+# brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
+# filter pass, candidate selection, exact rescore, keys->ids, finalize
+BF_LAUNCHES = 10
 
 
 def config_dict(args, world, extra=None):
@@ -276,17 +293,22 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
 
     times, scan_ms, bytes_scanned, launches, rescans = [], [], [], 0, []
+    kern_ms, kern_scores = [], []
     stage = {"coarse_ms": [], "rescore_ms": [], "merge_ms": []}
     with ClockSampler(nvml_index(local_rank)) as clk:
         for s in range(args.steps):
             flush.zero_()
             torch.cuda.synchronize()
+            if args.profile_range and s == 0:
+                torch.cuda.profiler.start()  # for ncu --profile-from-start off
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             step_device()
             e1.record(stream)
             e1.synchronize()
+            if args.profile_range and s == 0:
+                torch.cuda.profiler.stop()
             times.append(e0.elapsed_time(e1))
             scan_ms.append(st.scan_ms)
             stage["coarse_ms"].append(st.coarse_ms)
@@ -294,8 +316,18 @@ def run_ours(args, rank, world, local_rank, dist):
             stage["merge_ms"].append(st.merge_ms)
             rescans.append(st.exact_rescans)
             bytes_scanned.append(st.bytes_scanned)
-            # coarse, select, scan, [rescore (+ exact re-scan)], keys->ids, finalize
-            launches += 5 + (1 if st.rescore_ms > 0 else 0) + (1 if st.exact_rescans else 0)
+            kern_ms.append(st.kernel_ms)
+            kern_scores.append(st.kernel_scores)
+            codes = st.bytes_scanned / M
+            if st.kernel_scores < codes:
+                # tensor mode: transpose + coarse, select, pair keys, radix sort (4),
+                # segment offsets, residual rows, dump rows, scan (2), items, pass 1,
+                # pass-1 selection, pass 2, shortlist, certify, [exact re-scan],
+                # keys->ids, finalize
+                launches += 21 + (1 if st.exact_rescans else 0)
+            else:
+                # coarse, select, scan, [rescore (+ exact re-scan)], keys->ids, finalize
+                launches += 5 + (1 if st.rescore_ms > 0 else 0) + (1 if st.exact_rescans else 0)
             launches += 2 if (world > 1 and args.mode == "lists") else 0
         e2e_times = []
         for s in range(args.steps):
@@ -331,7 +363,32 @@ def run_ours(args, rank, world, local_rank, dist):
     hbm, peak_kind = peaks()
     scan_avg_ms = statistics.mean(scan_ms)
     algo_bytes = statistics.mean(bytes_scanned)
-    achieved = algo_bytes / (scan_avg_ms / 1000.0) / 1e9
+    k_ms = statistics.mean(kern_ms)
+    k_scores = statistics.mean(kern_scores)
+    # in tensor mode the dominant kernel scores only the pass-2 pairs' codes
+    tensor_mode = st.lists_probed > 0 and k_scores < algo_bytes / M
+    dpad = (DIM + 63) // 64 * 64
+    if tensor_mode:
+        # tcgen05 list scan (pass 2): 2 * dpad flops per (query, code) score
+        tpk, tkind = tensor_peak()
+        flops = 2.0 * dpad * k_scores
+        achieved = flops / (k_ms / 1000.0) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": tpk, "unit": "TFLOP/s",
+                    "frac": achieved / tpk, "traffic": NCU_TRAFFIC.get("ivf_pass_filter"),
+                    "kernel": "ivf_pass_kernel<FILTER> (tcgen05 fp16 scores of probed lists "
+                              "1..nprobe-1 against decoded codes, fused admission test)",
+                    "peak_source": tkind, "algorithmic_flops_per_launch": flops,
+                    "scores_per_launch": k_scores, "kernel_ms": k_ms,
+                    "code_bytes_per_step": algo_bytes,
+                    "code_bytes_per_step_over_step_time_gbs":
+                        algo_bytes / (total_ms / args.steps / 1000.0) / 1e9}
+    else:
+        achieved = k_scores * M / (k_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                    "frac": achieved / hbm, "traffic": None,
+                    "kernel": "scan_kernel (LUT build + code scan + warp top-k)",
+                    "peak_source": f"{peak_kind} hbm_gbs",
+                    "algorithmic_bytes_per_launch": k_scores * M, "kernel_ms": k_ms}
     line = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -346,12 +403,7 @@ def run_ours(args, rank, world, local_rank, dist):
                 "h2d_bytes_per_step": nq * DIM * 4,
                 "d2h_bytes_per_step": nq * K * (8 + 4) + nq * 4},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None,
-                     "kernel": "scan_kernel (LUT build + code scan + warp top-k)",
-                     "peak_source": f"{peak_kind} hbm_gbs",
-                     "algorithmic_bytes_per_launch": algo_bytes,
-                     "kernel_ms": scan_avg_ms},
+        "roofline": roofline,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -414,15 +466,19 @@ def run_ours_bf(args, rank, world, local_rank, dist):
         dist.barrier()
     times, scan_ms, rescans, e2e_times = [], [], [], []
     with ClockSampler(nvml_index(local_rank)) as clk:
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            if args.profile_range and i == 0:
+                torch.cuda.profiler.start()  # for ncu --profile-from-start off
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             step()
             e1.record(stream)
             e1.synchronize()
+            if args.profile_range and i == 0:
+                torch.cuda.profiler.stop()
             times.append(e0.elapsed_time(e1))
-            scan_ms.append(st.scan_ms)
+            scan_ms.append(st.kernel_ms)
             rescans.append(st.exact_rescans)
         for _ in range(args.steps):
             e0 = torch.cuda.Event(enable_timing=True)
@@ -455,12 +511,14 @@ def run_ours_bf(args, rank, world, local_rank, dist):
         "config": {"workload": "bf_config_b", "n_base": n, "dim": DIM, "global_batch": nq, "k": k,
                    "metric": args.bf_metric, "parallelism": f"rows{world}",
                    "exact_rescans_per_step": statistics.mean(rescans),
-                   "gemm_kernel_ms": round(scan_avg, 4)},
+                   "filter_kernel_ms": round(scan_avg, 4),
+                   "l2": "not flushed: the fp16 rows (256 MB) exceed L2 every step"},
+        "gpu_launches": BF_LAUNCHES * args.steps,
         "e2e": {"value": nq * args.steps / (float(tot[1]) / 1000), "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4, "d2h_bytes_per_step": nq * k * 12 + nq * 4},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None,
-                     "kernel": "gemm_topk_kernel (tcgen05 fp16 GEMM + fused shortlist)",
+                     "kernel": "gemm_topk_kernel<FILTER> (tcgen05 fp16 GEMM + fused admission test)",
                      "peak_source": "measured bf16_tflops (dense fp16 has the same rate)",
                      "kernel_ms": scan_avg},
         "clocks": clk.summary(),
@@ -477,6 +535,9 @@ def main():
     ap.add_argument("--nprobe", type=int, default=32)
     ap.add_argument("--mode", default="lists", choices=["lists", "replicas"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the first timed step with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--scan-mode", default="auto", choices=list(SCAN_MODES),
                     help="IVF-PQ scan mode (auto picks the tensor-core list scan here)")
     ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "bf"])

@@ -396,8 +396,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         }
         launch_select(s, h->s_coarse.p, (int)nq, nlist, (int)take, h->s_probe.p);
         tm.mark();
-        h->s_stat.ensure(2);
-        FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 16, s));
+        h->s_stat.ensure(3);
+        FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 24, s));
         const uint64_t* lbeg = h->sharded ? h->shard_be.p : h->offs.p;
         const uint64_t* lend = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
         // Tensor mode: lists scored on the tensor cores into a shortlist,
@@ -428,8 +428,11 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         a.btab = tables ? h->btab.p : nullptr;
         if (tensor) {
             h->s_flags.ensure(nq + 1);
+            double pass_ms = 0.0;
             const uint32_t nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend,
-                                                 h->s_keys.p, h->s_flags.p, h->s_stat.p);
+                                                 h->s_keys.p, h->s_flags.p, h->s_stat.p,
+                                                 st ? &pass_ms : nullptr);
+            if (st) st->kernel_ms = pass_ms;
             tm.mark();
             if (nflag > 0) {
                 // exact re-scan of the lists that failed, seeded with the rest
@@ -501,9 +504,9 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
     launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
     tm.mark();
     if (st) {
-        unsigned long long hs[2] = {0, 0};
+        unsigned long long hs[3] = {0, 0, 0};
         if (take > 0)
-            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 16, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 24, cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
         st->lists_probed = hs[0];
         st->codes_scanned = hs[1];
@@ -514,6 +517,12 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
             st->scan_ms = tm.ms(1, 2);
             st->rescore_ms = tm.ms(2, 3);
             st->merge_ms = tm.ms(3, 4);
+            if (st->kernel_ms > 0.0) {
+                st->kernel_scores = hs[2];  // tensor mode: pass 2 of the list scan
+            } else {
+                st->kernel_ms = st->scan_ms;  // the scan kernel
+                st->kernel_scores = hs[1];
+            }
         }
         st->total_ms = tm.ms(0, last);
     }
@@ -650,6 +659,18 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
             int* err = reinterpret_cast<int*>(h->s_flags.p + nq + 1);
             FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
             h->gemm.err = err;
+            // device time of the filter pass, when statistics are asked for
+            cudaEvent_t fev[2] = {nullptr, nullptr};
+            if (st) {
+                FDB_CUDA(cudaEventCreate(&fev[0]));
+                FDB_CUDA(cudaEventCreate(&fev[1]));
+            }
+            struct EvPair {
+                cudaEvent_t* e;
+                ~EvPair() { for (int i = 0; i < 2; ++i) if (e[i]) cudaEventDestroy(e[i]); }
+            } fev_free{fev};
+            h->gemm.filter_ev0 = fev[0];
+            h->gemm.filter_ev1 = fev[1];
             gemm_shortlist(s, h->s_q16.p, (int)nq, qn, h->x16.p, h->n, h->kpad,
                            h->metric == COSINE ? h->rnorms.p : h->norms.p, h->metric, h->row0,
                            (int)kp, c.sm_count, h->xmax * h->xmax, h->gemm);
@@ -663,6 +684,13 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
             FDB_CUDA(cudaStreamSynchronize(s));
             FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core scan timed out on the device");
             nflag = hv[0];
+            if (st) {
+                float ms = 0.0f;
+                FDB_CUDA(cudaEventElapsedTime(&ms, fev[0], fev[1]));
+                st->kernel_ms = ms;
+                st->kernel_scores = (uint64_t)nq * h->n;
+            }
+            h->gemm.filter_ev0 = h->gemm.filter_ev1 = nullptr;
             if (nflag > 0) {
                 DevBuf<float> qf(nflag * h->dim), qfn(nflag);
                 DevBuf<uint64_t> kf(nflag * k);
@@ -695,6 +723,10 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
         FDB_CUDA(cudaStreamSynchronize(s));
         st->lists_probed = 0;
         st->codes_scanned = (uint64_t)nq * h->n;
+        if (st->kernel_ms == 0.0 && tm.ev.size() >= 4) {  // exact SIMT scan
+            st->kernel_ms = tm.ms(0, 1);
+            st->kernel_scores = (uint64_t)nq * h->n;
+        }
         st->bytes_scanned = (uint64_t)h->n * h->dim * 4;
         st->exact_rescans = nflag;
         if (tm.ev.size() >= 4) {

@@ -200,6 +200,8 @@ struct GemmScratch {
     DevBuf<float> tau;
     int cap = 0;
     int* err = nullptr;  // device error word (timeouts)
+    // optional: recorded around the filter pass (the dominant kernel)
+    cudaEvent_t filter_ev0 = nullptr, filter_ev1 = nullptr;
 };
 void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnorm,
                     const __half* x16, size_t n, int kpad, const float* xnorm, int metric,
@@ -227,7 +229,8 @@ void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
                     const std::vector<float>& bmax_host);
 uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
                        size_t take, const uint64_t* lbeg, const uint64_t* lend,
-                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat);
+                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
+                       double* pass_ms);
 void bf_upload(fdb_bf* h);
 void bf_shard(fdb_bf* h, int rank, int world);
 void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,

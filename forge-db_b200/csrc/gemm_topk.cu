@@ -584,7 +584,9 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     p.cand = w.cand.p;
     p.cand_cnt = w.cand_cnt.p;
     p.cap = w.cap;
+    if (w.filter_ev0) FDB_CUDA(cudaEventRecord(w.filter_ev0, s));
     launch_pass<tc::EPI_FILTER>(s, qm, xm, nq, chunks, p);
+    if (w.filter_ev1) FDB_CUDA(cudaEventRecord(w.filter_ev1, s));
     // --- top-kp of the candidates ---
     w.approx.ensure((size_t)nq * kp);
     const unsigned grid = (unsigned)((nq + 7) / 8);

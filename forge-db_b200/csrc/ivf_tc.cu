@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Sort key of probe (q, p): its list for the query's pass-1 probe (the first
 // holding LIST_K+ codes, else the first non-empty one), nlist + list for the
 // query's other non-empty probes, 2 nlist for empty lists.  When stat is
-// given, also counts the lists and codes scanned.
+// given, also counts the lists and codes scanned, and the codes of pass 2.
 __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, int take,
                                  const uint64_t* __restrict__ lbeg,
                                  const uint64_t* __restrict__ lend, int nlist,
@@ -530,7 +530,7 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
         if (len >= (uint64_t)LIST_K) p1 = j;
     }
     if (p1 < 0) p1 = pf;
-    unsigned long long lists = 0, codes = 0;
+    unsigned long long lists = 0, codes = 0, codes2 = 0;
     for (int j = 0; j < take; ++j) {
         const size_t i = (size_t)q * take + j;
         const uint32_t l = pq[j];
@@ -542,6 +542,7 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
             key = j == p1 ? l : (uint32_t)nlist + l;
             ++lists;
             codes += len;
+            if (j != p1) codes2 += len;
         }
         keys[i] = key;
         vals[i] = (uint32_t)i;
@@ -549,6 +550,7 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
     if (stat) {
         atomicAdd(stat, lists);
         atomicAdd(stat + 1, codes);
+        atomicAdd(stat + 2, codes2);
     }
 }
 
@@ -1105,7 +1107,8 @@ namespace {
 void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
               const uint32_t* probes, const float* coarse, const uint64_t* lbeg,
               const uint64_t* lend, uint64_t* out_keys, uint32_t* flags, uint32_t qbase,
-              unsigned long long* stat, int* err, uint32_t* fail_probes, uint32_t* fail_cnt) {
+              unsigned long long* stat, int* err, uint32_t* fail_probes, uint32_t* fail_cnt,
+              cudaEvent_t ev0, cudaEvent_t ev1) {
     using namespace ivtc;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -1205,7 +1208,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     // --- pass 2: the other lists against tau ---
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
+    if (ev0) FDB_CUDA(cudaEventRecord(ev0, s));
     launch_pass<EPI_FILTER>(s, am, bm, grid, p);
+    if (ev1) FDB_CUDA(cudaEventRecord(ev1, s));
     // --- shortlist, exact rescoring, certification ---
     h->s_approx.ensure(nq * LIST_K);
     select_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(h->t_part.p, h->t_cand.p,
@@ -1259,7 +1264,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 // (one row of distances per query) within 1 GiB.
 uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
                        size_t take, const uint64_t* lbeg, const uint64_t* lend,
-                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat) {
+                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
+                       double* pass_ms) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
@@ -1271,17 +1277,38 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     int* err = reinterpret_cast<int*>(h->t_range.p + 4);
     FDB_CUDA(cudaMemsetAsync(flags, 0, 4, s));
     FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
-    for (size_t q0 = 0; q0 < nq; q0 += chunk) {
+    // device time of pass 2, one event pair per chunk (only when asked for)
+    std::vector<cudaEvent_t> evs;
+    const size_t nchunks = (nq + chunk - 1) / chunk;
+    if (pass_ms) {
+        evs.resize(2 * nchunks, nullptr);
+        for (auto& e : evs) FDB_CUDA(cudaEventCreate(&e));
+    }
+    struct EvFree {
+        std::vector<cudaEvent_t>& v;
+        ~EvFree() { for (auto e : v) if (e) cudaEventDestroy(e); }
+    } ev_free{evs};
+    for (size_t q0 = 0, ci = 0; q0 < nq; q0 += chunk, ++ci) {
         const size_t nc = std::min(chunk, nq - q0);
         tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,
                  h->s_coarse.p + q0 * h->nlist, lbeg, lend, out_keys + q0 * k, flags,
-                 (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p);
+                 (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p,
+                 pass_ms ? evs[2 * ci] : nullptr, pass_ms ? evs[2 * ci + 1] : nullptr);
     }
     uint32_t hv[2] = {0, 0};
     FDB_CUDA(cudaMemcpyAsync(&hv[0], flags, 4, cudaMemcpyDeviceToHost, s));
     FDB_CUDA(cudaMemcpyAsync(&hv[1], err, 4, cudaMemcpyDeviceToHost, s));
     FDB_CUDA(cudaStreamSynchronize(s));
     FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
+    if (pass_ms) {
+        double tot = 0.0;
+        for (size_t ci = 0; ci < nchunks; ++ci) {
+            float ms = 0.0f;
+            FDB_CUDA(cudaEventElapsedTime(&ms, evs[2 * ci], evs[2 * ci + 1]));
+            tot += ms;
+        }
+        *pass_ms = tot;
+    }
     return hv[0];
 }
 

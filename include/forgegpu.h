@@ -70,8 +70,12 @@ typedef struct fdb_stats {
     double rescore_ms;       /* table mode: exact rescoring, certification, re-scans */
     double merge_ms;         /* cross-device exchange + final merge */
     double total_ms;         /* whole call, device clock */
-    uint64_t exact_rescans;  /* table mode: queries re-scanned exactly after
+    uint64_t exact_rescans;  /* table/tensor mode: queries re-scanned exactly after
                                 failing certification */
+    double kernel_ms;        /* device time of the dominant scan kernel: the tensor
+                                list scan's second pass (IVF-PQ tensor mode), the
+                                filter pass (brute force, tensor path), else the scan */
+    uint64_t kernel_scores;  /* (query, code/row) scores that kernel computed */
 } fdb_stats;
 
 /* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  All return the reference's
