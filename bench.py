@@ -40,6 +40,25 @@ sys.path.insert(0, os.path.join(ROOT, "forge-db_b200"))
 METRIC = "IVF-PQ QPS @ matched recall@10, 1M×128 nprobe=32, 1/2/4/8 B200"
 N_BASE, N_QUERY, DIM, NLIST, M, K = 1_000_000, 10_000, 128, 1024, 16, 10
 SEED = 2024
+WORKLOAD = "ivfpq_config_c"
+DATA_NOTE = "seeded GMM descriptor-like (1024 centres U[0,255], sigma 20, clipped, rounded)"
+DEFAULT_NPROBE = 32
+
+# IVF-PQ workloads: the headline (config C) and the embedding-scale config D
+IVF_CONFIGS = {
+    "ivfpq": dict(METRIC=METRIC, N_BASE=1_000_000, N_QUERY=10_000, DIM=128, NLIST=1024, M=16,
+                  K=10, WORKLOAD="ivfpq_config_c", DEFAULT_NPROBE=32,
+                  DATA_NOTE="seeded GMM descriptor-like (1024 centres U[0,255], sigma 20, "
+                            "clipped, rounded)"),
+    "ivfpq_d": dict(METRIC="IVF-PQ QPS, 20M×96 unit-norm (cosine), nlist 16384, M 48, nprobe=64",
+                    N_BASE=20_000_000, N_QUERY=10_000, DIM=96, NLIST=16384, M=48, K=10,
+                    WORKLOAD="ivfpq_config_d", DEFAULT_NPROBE=64,
+                    DATA_NOTE="seeded unit-norm N(0,1), 96 dims"),
+}
+
+
+def use_ivf_config(name):
+    globals().update(IVF_CONFIGS[name])
 
 
 def peaks():
@@ -123,8 +142,9 @@ def nvml_index(local_rank: int) -> int:
 
 def make_data():
     from forgegpu import datasets
-    X, Q = datasets.config_c(N_BASE, N_QUERY)
-    return X, Q
+    if WORKLOAD == "ivfpq_config_d":
+        return datasets.config_d(N_BASE, N_QUERY)
+    return datasets.config_c(N_BASE, N_QUERY)
 
 
 SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
@@ -138,9 +158,8 @@ BF_LAUNCHES = 10
 
 
 def config_dict(args, world, extra=None):
-    d = {"workload": "ivfpq_config_c", "n_base": N_BASE, "dim": DIM, "nlist": NLIST, "m": M,
-         "nprobe": args.nprobe, "global_batch": N_QUERY, "k": K,
-         "data": "seeded GMM descriptor-like (1024 centres U[0,255], sigma 20, clipped, rounded)",
+    d = {"workload": WORKLOAD, "n_base": N_BASE, "dim": DIM, "nlist": NLIST, "m": M,
+         "nprobe": args.nprobe, "global_batch": N_QUERY, "k": K, "data": DATA_NOTE,
          "parallelism": (f"lists{world}" if args.mode == "lists" else f"replicas{world}"),
          "scan_mode": args.scan_mode,
          "l2": "flushed between steps (256 MB write outside the timed window)"}
@@ -154,6 +173,11 @@ def config_dict(args, world, extra=None):
 # ---------------------------------------------------------------------------
 def run_reference(args, rank, world):
     if rank != 0:
+        return
+    if args.workload != "ivfpq":
+        print(json.dumps({"impl": "reference", "workload": args.workload,
+                          "unavailable": "the reference arm is defined for the headline "
+                                         "workload (config C) only"}), flush=True)
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -526,13 +550,101 @@ def run_ours_bf(args, rank, world, local_rank, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_ours_train(args, rank, world, local_rank, dist):
+    """Config E: k-means of 1M x 768 unit-norm rows into 4096 centroids (20 Lloyd
+    iterations from a seeded random-sample init), PQ training with M = 96 on a
+    100k-row sample, and encoding of all 1M rows, through the public API (host
+    buffers in and out).  One run per step; every rank runs the whole job
+    (training is replicated, 'replicas').  Bit-exactness at this size is
+    checked by properties on a sample (oracle assignment and encoding)."""
+    import torch
+    import forgegpu as fg
+    from forgegpu import datasets
+
+    torch.cuda.set_device(local_rank)
+    ctx = fg.Context(local_rank)
+    n, dim, k, iters, m = 1_000_000, 768, 4096, 20, 96
+    X = datasets.config_e(n)
+    init = fg.sample_indices(12, n, k)
+    pq_rows = fg.sample_indices(13, n, 100_000)
+    Xs = np.ascontiguousarray(X[pq_rows])
+    pq_init = np.concatenate([fg.sample_indices(14 + s, len(Xs), 256) for s in range(m)])
+
+    def job():
+        t = {}
+        t0 = time.perf_counter()
+        km = fg.KMeans(k, iters, ctx).fit(X, init_idx=init)
+        t["kmeans_s"] = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        pq = fg.ProductQuantizer.train(Xs, m, init_idx=pq_init, iters=25, ctx=ctx)
+        t["pq_train_s"] = time.perf_counter() - t1
+        t2 = time.perf_counter()
+        codes = pq.encode(X)
+        t["encode_s"] = time.perf_counter() - t2
+        t["total_s"] = time.perf_counter() - t0
+        return km, pq, codes, t
+
+    for _ in range(min(args.warmup, 1)):  # one untimed run (module load, allocations)
+        job()
+    if dist is not None:
+        dist.barrier()
+    runs = []
+    with ClockSampler(nvml_index(local_rank)) as clk:
+        for _ in range(max(1, min(args.steps, 3))):
+            torch.cuda.synchronize()
+            km, pq, codes, t = job()
+            runs.append(t)
+    tot = torch.tensor([max(r["total_s"] for r in runs)], dtype=torch.float64,
+                       device=torch.device("cuda", local_rank))
+    if dist is not None:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(15)
+    sample = np.sort(rng.choice(n, 2000, replace=False))
+    assign_ok = bool(np.array_equal(O.assign(X[sample], km.centroids), km.assignments[sample]))
+    codes_ok = bool(np.array_equal(O.pq_encode(pq.codebooks, X[sample]), codes[sample]))
+    # CPU baseline: the oracle's assignment step on a bounded sample, scaled to
+    # the full job's assignment work (20 iterations over 1M rows)
+    threads = O.max_threads()
+    cs = 4000
+    t0 = time.perf_counter()
+    O.assign(X[:cs], km.centroids, threads=threads)
+    dt = time.perf_counter() - t0
+    cpu_est = dt * (n / cs) * iters
+    mean = {key: statistics.mean(r[key] for r in runs) for key in runs[0]}
+    line = {
+        "metric": "Training wall time: k-means 1M×768 -> 4096 (20 iters) + PQ M 96 + encode 1M",
+        "value": float(tot[0]), "unit": "s", "n_gpus": world, "steps": len(runs),
+        "warmup": 1, "ms_per_step": 1000 * float(tot[0]), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "train_config_e", "n": n, "dim": dim, "k": k, "iters": iters,
+                   "pq_m": m, "pq_sample": len(Xs), "kmeans_iters_run": km.iters,
+                   "data": "seeded unit-norm N(0,1), 768 dims",
+                   "parallelism": f"replicas{world}", "phase_s": mean,
+                   "sample_checks": {"assignments_match_oracle": assign_ok,
+                                     "codes_match_oracle": codes_ok, "rows": len(sample)}},
+        "e2e": {"value": float(tot[0]), "unit": "s", "h2d_bytes_per_step": int(X.nbytes * 2 + Xs.nbytes),
+                "d2h_bytes_per_step": int(k * dim * 4 + n * 4 + n * m)},
+        "gpu_launches": None,
+        "cpu_baseline": {"value": cpu_est, "unit": "s", "cores": threads, "kind": "port",
+                         "sample": f"oracle assignment of {cs} rows to the 4096 centroids, "
+                                   f"scaled to {iters} iterations over {n} rows (assignment only)"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--nprobe", type=int, default=32)
+    ap.add_argument("--nprobe", type=int, default=None,
+                    help="default: 32 (config C), 64 (config D)")
     ap.add_argument("--mode", default="lists", choices=["lists", "replicas"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
@@ -540,12 +652,18 @@ def main():
                          "(for ncu --profile-from-start off)")
     ap.add_argument("--scan-mode", default="auto", choices=list(SCAN_MODES),
                     help="IVF-PQ scan mode (auto picks the tensor-core list scan here)")
-    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "bf"])
+    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "ivfpq_d", "bf", "train"],
+                    help="ivfpq: config C (the headline); ivfpq_d: config D; bf: config B; "
+                         "train: config E (k-means 1M x 768 -> 4096, PQ M 96, encode)")
     ap.add_argument("--bf-metric", default="l2sq", choices=["l2sq", "dot", "cosine", "l2"])
     ap.add_argument("--bf-n", type=int, default=1_000_000, help="rows (smaller for profiling)")
     ap.add_argument("--bf-nq", type=int, default=10_000, help="queries (smaller for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload in IVF_CONFIGS:
+        use_ivf_config(args.workload)
+    if args.nprobe is None:
+        args.nprobe = DEFAULT_NPROBE
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -565,6 +683,8 @@ def main():
     try:
         if args.workload == "bf":
             run_ours_bf(args, rank, world, local_rank, dist)
+        elif args.workload == "train":
+            run_ours_train(args, rank, world, local_rank, dist)
         else:
             run_ours(args, rank, world, local_rank, dist)
     finally:

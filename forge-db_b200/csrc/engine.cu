@@ -201,9 +201,10 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
     ivfpq_prepare_tables(h);
 }
 
-// Table mode needs, per index: the per-list table btab and the bound terms
-// cmax_s = max_l ||c_ls||, bmax_s = max_j ||b_sj|| (rounded up).  Built for
-// subvectors of 8+ floats, where an exact LUT entry costs 8+ FMAs.
+// Table and tensor modes need, per index: the bound terms cmax_s = max_l
+// ||c_ls||, bmax_s = max_j ||b_sj|| (rounded up); the table mode also the
+// per-list table btab (subvectors of 8+ floats only), the tensor mode the
+// decoded codes (ivf_tc_prepare).
 static void ivfpq_prepare_tables(fdb_ivfpq* h) {
     const size_t nlist = h->nlist, dim = h->dim, m = h->m, sub = dim / m;
     h->btab.release();
@@ -218,11 +219,15 @@ static void ivfpq_prepare_tables(fdb_ivfpq* h) {
         launch_transpose_pad(h->ctx->c.stream, h->cents.p, (int)nlist, (int)dim, h->nlist_pad,
                              h->centsT.p);
     }
-    if (sub < 8) return;
+    if (nlist == 0 || m == 0) return;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
-    h->btab.alloc(nlist * m * KSUB);
-    launch_ivf_tables(s, h->cents.p, h->cb.p, (int)nlist, (int)m, (int)dim, h->btab.p);
+    // the per-list table pays off for subvectors of 8+ floats (an exact LUT
+    // entry then costs 8+ FMAs); the bound terms serve every certified mode
+    if (sub >= 8) {
+        h->btab.alloc(nlist * m * KSUB);
+        launch_ivf_tables(s, h->cents.p, h->cb.p, (int)nlist, (int)m, (int)dim, h->btab.p);
+    }
     std::vector<float> cents(nlist * dim), cb(m * KSUB * sub);
     FDB_CUDA(cudaMemcpyAsync(cents.data(), h->cents.p, cents.size() * 4, cudaMemcpyDeviceToHost, s));
     FDB_CUDA(cudaMemcpyAsync(cb.data(), h->cb.p, cb.size() * 4, cudaMemcpyDeviceToHost, s));

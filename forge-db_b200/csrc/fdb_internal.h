@@ -289,7 +289,9 @@ struct fdb_ivfpq {
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
     fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv1, t_plen,
         t_seg, t_fprobes, t_fcnt;
-    fdb::DevBuf<float> t_dump;
+    fdb::DevBuf<float> t_dump, t_dk;
+    fdb::DevBuf<uint64_t> t_ekeys;
+    fdb::DevBuf<int> t_elist;
     fdb::DevBuf<uint8_t> t_tmp, t_items;
     fdb::DevBuf<__half> t_a16;
     fdb::DevBuf<float> t_rn, t_s2, t_tau;

@@ -512,20 +512,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 // pair grouping
 // ---------------------------------------------------------------------------
 // Sort key of probe (q, p): its list for the query's pass-1 probe (the first
-// holding LIST_K+ codes, else the first non-empty one), nlist + list for the
-// query's other non-empty probes, 2 nlist for empty lists.  When stat is
+// holding LIST_K+ codes in the unsharded index, else the first non-empty
+// one), nlist + list for the query's other probes, 2 nlist for lists that are
+// empty or held by another device.  When stat is
 // given, also counts the lists and codes scanned, and the codes of pass 2.
 __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, int take,
                                  const uint64_t* __restrict__ lbeg,
-                                 const uint64_t* __restrict__ lend, int nlist,
+                                 const uint64_t* __restrict__ lend,
+                                 const uint64_t* __restrict__ offs_full, int nlist,
                                  uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
                                  unsigned long long* stat) {
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= nq) return;
     const uint32_t* pq = probes + (size_t)q * take;
+    // the pass-1 list is chosen from the unsharded list sizes, so that on a
+    // sharded index exactly one device holds it
     int p1 = -1, pf = -1;
     for (int j = 0; j < take && p1 < 0; ++j) {
-        const uint64_t len = lend[pq[j]] - lbeg[pq[j]];
+        const uint64_t len = offs_full[pq[j] + 1] - offs_full[pq[j]];
         if (len > 0 && pf < 0) pf = j;
         if (len >= (uint64_t)LIST_K) p1 = j;
     }
@@ -790,6 +794,9 @@ struct CertParams {
     const uint64_t* approx;     // [nq][64] tensor-core shortlist, ascending
     int k;
     uint64_t* out_keys;         // [nq][k]
+    uint64_t* ekeys;            // [nq][64] exact keys of the shortlist (rescore -> certify)
+    int* elist;                 // [nq][64] their lists (-1: none)
+    float* dk;                  // [nq] exact k-th distance (+inf if fewer); min over ranks
     const float* cmax;          // [m]
     const float* bmax;          // [m]
     const unsigned* cand_cnt;
@@ -811,24 +818,11 @@ struct CertParams {
 
 constexpr int CERT_WARPS = 8;
 
-// One warp per query.  The shortlist is rescored with exact_adc (the
-// reference's arithmetic) and the k best kept.  Certification: for a code of
-// list l, |d~ - D| <= E_l and |exact - D| <= E_adc, where D is the real ADC
-// distance of r = fl(q - c_l):
-//   E_l  = C1 R_l Rh_l + C2 (R_l^2 + Rh_l^2),  R_l >= ||r||, Rh_l >= ||rhat||
-//          over the list's codes, C1 = 2 (2^-10 + 2^-13) * 1.05: fp16
-//          rounding of both operands (2^-11 each, relative) and an allowance
-//          of 2^-13 for the tensor core's fp32 accumulation; C2 = 2^-16
-//          covers the fp32 roundings of ||r||^2, ||rhat||^2 and the final
-//          fused multiply-add;
-//   E_adc = (32 + 4m) 2^-24 sum_s (||q_s|| + cmax_s + bmax_s)^2 * 1.01.
-// Every code outside the shortlist has d~ >= B (B = the 64th shortlisted
-// value when the shortlist is full, tau otherwise), so it cannot enter the
-// exact top-k if, for its list, dk + E_adc + E_l < B, or if its real distance
-// is above dk anyway: (||r|| - Rh_l)^2 - E_adc > dk.  Overflowing candidate
-// arrays and queries marked bad are never certified.
+// One warp per query: the 64 shortlisted codes rescored with exact_adc (the
+// reference's arithmetic), their exact keys and lists kept for certify_kernel,
+// the k best written out, and the exact k-th distance dk.
 template <int ORDER>
-__global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) {
+__global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) {
     __shared__ uint64_t buf[CERT_WARPS * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * CERT_WARPS + warp;
@@ -836,14 +830,13 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     const int m = r.m, sub = r.dim / m;
     const float* qv = r.Q + (size_t)q * r.dim;
     const uint64_t* ak = r.approx + (size_t)q * LIST_K;
-    // exact keys of the 64 shortlisted codes (two per lane) and their lists
-    uint64_t ek[2];
-    int el[2];
+    WarpTopK<1> tk;
+    tk.init(r.k, buf + warp * 64);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const uint64_t key = ak[h * 32 + lane];
-        ek[h] = KEY_NONE;
-        el[h] = -1;
+        uint64_t ek = KEY_NONE;
+        int el = -1;
         if (key != KEY_NONE) {
             const uint32_t pos = key_tag(key);
             int lo = 0, hi = r.nlist;  // the list l with offs[l] <= pos < offs[l+1]
@@ -854,15 +847,45 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
             }
             const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
                                              r.codes + (size_t)pos * m, m, sub);
-            ek[h] = make_key(d, pos);
-            el[h] = lo;
+            ek = make_key(d, pos);
+            el = lo;
         }
+        r.ekeys[(size_t)q * LIST_K + h * 32 + lane] = ek;
+        r.elist[(size_t)q * LIST_K + h * 32 + lane] = el;
+        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
     }
-    WarpTopK<1> tk;
-    tk.init(r.k, buf + warp * 64);
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-        if (__any_sync(0xffffffffu, ek[h] != KEY_NONE)) tk.merge32(ek[h]);
+    tk.store(r.out_keys + (size_t)q * r.k);
+    if (lane == 0) r.dk[q] = tk.thr == KEY_NONE ? INF : key_dist(tk.thr);
+}
+
+// One warp per query.  Certification: for a code of list l, |d~ - D| <= E_l
+// and |exact - D| <= E_adc, where D is the real ADC distance of r = fl(q - c_l):
+//   E_l  = C1 R_l Rh_l + C2 (R_l^2 + Rh_l^2),  R_l >= ||r||, Rh_l >= ||rhat||
+//          over the list's codes, C1 = 2 (2^-10 + 2^-13) * 1.05: fp16
+//          rounding of both operands (2^-11 each, relative) and an allowance
+//          of 2^-13 for the tensor core's fp32 accumulation; C2 = 2^-16
+//          covers the fp32 roundings of ||r||^2, ||rhat||^2 and the final
+//          fused multiply-add;
+//   E_adc = (32 + 4m) 2^-24 sum_s (||q_s|| + cmax_s + bmax_s)^2 * 1.01.
+// dk is an upper bound of the exact k-th distance of the answer: this
+// device's exact k-th over its shortlist, or on a sharded index the minimum of
+// that over all devices.  Every code outside the shortlist has d~ >= B (B =
+// the 64th shortlisted value when the shortlist is full, tau otherwise), so
+// it cannot enter the answer if, for its list, dk + E_adc + E_l < B, or if
+// its real distance is above dk anyway: (||r|| - Rh_l)^2 - E_adc > dk.  The
+// device's output (its exact top-k over the shortlist) then holds every one of
+// its codes that can be in the answer.  Overflowing candidate arrays and
+// queries marked bad are never certified.  A query with failing lists gets
+// them listed for an exact re-scan, and its output row becomes the seed: the
+// exact top-k of its shortlisted codes in the other lists.
+__global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) {
+    __shared__ uint64_t buf[CERT_WARPS * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * CERT_WARPS + warp;
+    if (q >= r.nq) return;  // whole warp
+    const int m = r.m, sub = r.dim / m;
+    const float* qv = r.Q + (size_t)q * r.dim;
+    const uint64_t* ak = r.approx + (size_t)q * LIST_K;
     double part = 0.0;
     for (int s = lane; s < m; s += 32) {
         double qn = 0.0;
@@ -881,12 +904,11 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     const unsigned c = r.cand_cnt[q];
     const uint64_t last = ak[LIST_K - 1];
     const double B = last != KEY_NONE ? (double)key_dist(last) : (double)r.tau[q];
+    const double dk = (double)r.dk[q];
     // whole-query failures: every list is re-scanned and nothing is kept
-    bool fail_all = c > (unsigned)r.cap || r.qbad[q] != 0u ||
-                    (!isinf(B) && tk.thr == KEY_NONE);
-    const double dk = tk.thr == KEY_NONE ? 0.0 : (double)key_dist(tk.thr);
+    const bool fail_all = c > (unsigned)r.cap || r.qbad[q] != 0u || (!isinf(B) && isinf(dk));
     // per-list verdict for probe j (true: no code of the list outside the
-    // shortlist can enter the exact top-k)
+    // shortlist can enter the answer)
     auto list_ok = [&](int j) -> bool {
         const uint32_t l = r.probes[(size_t)q * r.take + j];
         if (r.lend[l] <= r.lbeg[l]) return true;
@@ -904,10 +926,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
         const int j = j0 + lane;
         ok = __all_sync(0xffffffffu, j >= r.take || list_ok(j));
     }
-    if (ok) {
-        tk.store(r.out_keys + (size_t)q * r.k);
-        return;
-    }
+    if (ok) return;  // rescore_kernel's output stands
     uint32_t slot = 0;
     if (lane == 0) {
         slot = atomicAdd(r.flag_count, 1u);
@@ -915,6 +934,9 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     }
     slot = __shfl_sync(0xffffffffu, slot, 0);
     uint32_t* fp = r.fail_probes + (size_t)slot * r.take;
+    const uint64_t ek[2] = {r.ekeys[(size_t)q * LIST_K + lane],
+                            r.ekeys[(size_t)q * LIST_K + 32 + lane]};
+    const int el[2] = {r.elist[(size_t)q * LIST_K + lane], r.elist[(size_t)q * LIST_K + 32 + lane]};
     // failed lists, compacted; shortlisted codes of those lists are dropped
     // from the seed (the exact re-scan meets them again)
     unsigned nf = 0;
@@ -938,7 +960,6 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     if (lane == 0) r.fail_cnt[slot] = nf;
     WarpTopK<1> seed;
     seed.init(r.k, buf + warp * 64);
-    __syncwarp();
     const uint64_t s0 = drop0 ? KEY_NONE : ek[0], s1 = drop1 ? KEY_NONE : ek[1];
     if (__any_sync(0xffffffffu, s0 != KEY_NONE)) seed.merge32(s0);
     if (__any_sync(0xffffffffu, s1 != KEY_NONE)) seed.merge32(s1);
@@ -1121,7 +1142,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_vals.ensure(2 * np);
     h->t_off.ensure((size_t)nkeys + 1);
     pair_keys_kernel<<<(unsigned)((nq + 127) / 128), 128, 0, s>>>(
-        probes, (int)nq, (int)take, lbeg, lend, nlist, h->t_keys.p, h->t_vals.p, stat);
+        probes, (int)nq, (int)take, lbeg, lend, h->offs.p, nlist, h->t_keys.p, h->t_vals.p,
+        stat);
     FDB_LAUNCH_CHECK();
     h->t_plen.ensure(nq + 1);
     h->t_seg.ensure(nq + 1);
@@ -1205,6 +1227,10 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         h->t_dump.p, h->t_seg.p, h->t_inv1.p, svals, probes, lbeg, lend, (int)nq, h->t_part.p,
         h->t_tau.p);
     FDB_LAUNCH_CHECK();
+    if (h->sharded) {
+        // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
+        FDB_NCCL(ncclAllReduce(h->t_tau.p, h->t_tau.p, nq, ncclFloat, ncclMin, c.comm, s));
+    }
     // --- pass 2: the other lists against tau ---
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
@@ -1247,9 +1273,21 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.flag_list = flags + 1;
     r.fail_probes = fail_probes;
     r.fail_cnt = fail_cnt;
+    h->t_ekeys.ensure(nq * LIST_K);
+    h->t_elist.ensure(nq * LIST_K);
+    h->t_dk.ensure(nq);
+    r.ekeys = h->t_ekeys.p;
+    r.elist = h->t_elist.p;
+    r.dk = h->t_dk.p;
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
-    if (order == ORDER_LANE8) certify_kernel<ORDER_LANE8><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
-    else certify_kernel<ORDER_FAST4><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    if (order == ORDER_LANE8) rescore_kernel<ORDER_LANE8><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    else rescore_kernel<ORDER_FAST4><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    FDB_LAUNCH_CHECK();
+    if (h->sharded) {
+        // the answer's k-th distance is at most the smallest exact k-th of any device
+        FDB_NCCL(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s));
+    }
+    certify_kernel<<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
     FDB_LAUNCH_CHECK();
 }
 

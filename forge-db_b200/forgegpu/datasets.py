@@ -52,6 +52,16 @@ def config_c(n: int = 1_000_000, nq: int = 10_000):
     return gmm_descriptors(n, seed=6), gmm_descriptors(nq, seed=7)
 
 
+def config_d(n: int = 20_000_000, nq: int = 10_000):
+    """Unit-norm N(0,1) embeddings, 96 dimensions (seeds 9 and 10)."""
+    return normal(n, 96, seed=9, unit=True), normal(nq, 96, seed=10, unit=True)
+
+
+def config_e(n: int = 1_000_000):
+    """Unit-norm N(0,1) rows, 768 dimensions (seed 11)."""
+    return normal(n, 768, seed=11, unit=True)
+
+
 def recall_at_k(pred: np.ndarray, truth: np.ndarray, k: int) -> float:
     """dataset.rs:160-166: |pred_k n truth_k| / k, averaged over queries."""
     pred = np.atleast_2d(pred)

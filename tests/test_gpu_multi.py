@@ -32,10 +32,16 @@ def _rank_main(rank, world, q_in, q_out):
         Q = np.random.default_rng(2).random((257, 64), dtype=np.float32)
         ix = fg.IVFPQIndex.build(X, 64, 8, ctx=ctx, seed=7)
         ix.set_nprobe(16)
-        single = ix.batch_search_arrays(Q, 20)  # before sharding: the whole index
+        modes = (ix.SCAN_AUTO, ix.SCAN_TABLES, ix.SCAN_TENSOR)
+        single, sharded = [], []
+        for mode in modes:  # before sharding: the whole index
+            ix.set_scan_mode(mode)
+            single += list(ix.batch_search_arrays(Q, 20))
         ix.shard(rank, world)
         part_len = len(ix)
-        sharded = ix.batch_search_arrays(Q, 20)
+        for mode in modes:
+            ix.set_scan_mode(mode)
+            sharded += list(ix.batch_search_arrays(Q, 20))
         bf = fg.BruteForceIndex(fg.DistanceMetric.DotProduct, ctx).add(X)
         bf_single = bf.batch_search_arrays(Q, 100)
         bf.shard(rank, world)

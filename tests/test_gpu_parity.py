@@ -63,6 +63,53 @@ def test_assign_bit_exact(fg, ctx, orc, n, dim, k):
     assert np.array_equal(fg.assign(X, C, ctx), orc.assign(X, C))
 
 
+def _unit_rows(rng, n, dim):
+    X = rng.standard_normal((n, dim)).astype(np.float32)
+    return (X / np.linalg.norm(X, axis=1, keepdims=True)).astype(np.float32)
+
+
+def test_config_e_shape_training_bit_exact(fg, ctx, orc):
+    """Config E's shapes (unit-normalised 768-d rows, random-sample init for
+    k > 64, PQ with M = 96) at a size the oracle finishes in seconds:
+    centroids, assignments, codebooks and codes bit-exact."""
+    rng = np.random.default_rng(11)
+    X = _unit_rows(rng, 6000, 768)
+    k = 300
+    init = rng.permutation(len(X))[:k].astype(np.uint32)
+    km = fg.KMeans(k, 4, ctx).fit(X, init_idx=init)
+    cents, it = orc.kmeans_fit(X, k, 4, init)
+    assert km.iters == it
+    assert np.array_equal(km.centroids.view(np.uint32), cents.view(np.uint32))
+    assert np.array_equal(km.assignments, orc.assign(X, cents))
+    pinit = np.concatenate([rng.permutation(len(X))[:256] for _ in range(96)]).astype(np.uint32)
+    pq = fg.ProductQuantizer.train(X, 96, init_idx=pinit, iters=3, ctx=ctx)
+    cb, its = orc.pq_train(X, 96, pinit, 3)
+    assert np.array_equal(pq.iters, its)
+    assert np.array_equal(pq.codebooks.view(np.uint32), cb.view(np.uint32))
+    assert np.array_equal(pq.encode(X), orc.pq_encode(cb, X))
+
+
+@pytest.mark.parametrize("mode", [1, 3])
+def test_config_d_shape_search(fg, ctx, orc, mode):
+    """Config D's shapes (unit-normalised 96-d rows, M = 48: subvectors of two
+    floats, cosine metric stored and ignored) at a size the oracle finishes in
+    seconds, in the exact and the tensor scan modes."""
+    rng = np.random.default_rng(9)
+    X = _unit_rows(rng, 40000, 96)
+    Q = _unit_rows(np.random.default_rng(10), 300, 96)
+    ix = fg.IVFPQIndex.build(X, 256, 48, fg.DistanceMetric.Cosine, ctx=ctx, seed=4)
+    ox = _oracle_index(orc, ix)
+    ix.set_scan_mode(mode)
+    for nprobe in (4, 16):
+        ix.set_nprobe(nprobe)
+        ox.set_nprobe(nprobe)
+        ids, d, cnt, st = ix.batch_search_arrays(Q, 10, stats=True)
+        oi, od, oc = ox.batch_search(Q, 10)
+        assert_topk_match(ids, d, cnt, oi, od, oc, f"config D shape mode={mode} nprobe={nprobe}")
+        if mode == 3:
+            assert st.exact_rescans <= len(Q) // 10
+
+
 @pytest.mark.parametrize("n,dim,k,iters", [(4000, 16, 100, 25), (2000, 32, 32, 25),
                                            (3000, 8, 256, 10), (600, 5, 64, 30)])
 def test_kmeans_bit_exact(fg, ctx, orc, n, dim, k, iters):
