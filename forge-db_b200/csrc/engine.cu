@@ -434,25 +434,14 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         if (tensor) {
             h->s_flags.ensure(nq + 1);
             double pass_ms = 0.0;
+            std::vector<uint32_t> fail_cnt;
             const uint32_t nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend,
                                                  h->s_keys.p, h->s_flags.p, h->s_stat.p,
-                                                 st ? &pass_ms : nullptr);
+                                                 st ? &pass_ms : nullptr, &fail_cnt);
             if (st) st->kernel_ms = pass_ms;
             tm.mark();
-            if (nflag > 0) {
-                // exact re-scan of the lists that failed, seeded with the rest
-                ScanParams e = a;
-                e.nq = (int)nflag;
-                e.qidx = h->s_flags.p + 1;
-                e.k = (int)k;
-                e.out_keys = h->s_keys.p;
-                e.stat = nullptr;
-                e.btab = nullptr;
-                e.probe_list = h->t_fprobes.p;
-                e.probe_cnt = h->t_fcnt.p;
-                e.seed = true;
-                launch_scan(s, e, order);
-            }
+            // exact re-scan of the lists that failed, merged with the certified rest
+            ivf_tc_rescan(h, a, k, order, nflag, fail_cnt, h->s_keys.p);
             if (st) st->exact_rescans = nflag;
         } else {
             launch_scan(s, a, order);

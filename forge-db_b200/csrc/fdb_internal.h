@@ -230,7 +230,10 @@ void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
 uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
                        size_t take, const uint64_t* lbeg, const uint64_t* lend,
                        uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
-                       double* pass_ms);
+                       double* pass_ms, std::vector<uint32_t>* fail_cnt_host);
+struct ScanParams;
+void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, uint32_t nflag,
+                   const std::vector<uint32_t>& fail_cnt, uint64_t* out_keys);
 void bf_upload(fdb_bf* h);
 void bf_shard(fdb_bf* h, int rank, int world);
 void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
@@ -288,7 +291,8 @@ struct fdb_ivfpq {
     fdb::DevBuf<unsigned long long> s_stat;
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
     fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv1, t_plen,
-        t_seg, t_fprobes, t_fcnt;
+        t_seg, t_fprobes, t_fcnt, t_uoff, t_unit_q, t_unit_l;
+    fdb::DevBuf<uint64_t> t_unit_keys;
     fdb::DevBuf<float> t_dump, t_dk;
     fdb::DevBuf<uint64_t> t_ekeys;
     fdb::DevBuf<int> t_elist;

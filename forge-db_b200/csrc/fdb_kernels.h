@@ -27,11 +27,14 @@ struct ScanParams {
     const uint32_t* qidx;      // nullable: block i scans query qidx[i] (and writes its row)
     const float* btab;         // non-null selects table mode: [nlist][m][256]
     // nullable, with qidx: block i scans only the lists probe_list[i][0 .. probe_cnt[i])
-    // (row stride nprobe) and, with seed, starts from the k keys already in
-    // out_keys[qidx[i]] (which must not repeat codes of those lists)
+    // (row stride nprobe; probe_cnt nullable: every row holds nprobe lists) and,
+    // with seed, starts from the k keys already in its output row (which must
+    // not repeat codes of those lists)
     const uint32_t* probe_list;
     const uint32_t* probe_cnt;
     bool seed;
+    // with qidx: block i writes its k keys to out_keys[i] instead of out_keys[qidx[i]]
+    bool out_by_block;
 };
 
 struct RescoreParams {

@@ -721,8 +721,9 @@ __global__ void __launch_bounds__(ITEM_THREADS)
     }
 }
 
-// One warp per query: the top-64 keys of its pass-1 list, read from the dump,
-// into part[q]; tau[q] = their 64th distance (+inf if the list is shorter).
+// One warp per query: the top-64 keys of its pass-1 list, read from the dump
+// (128 values per step), into part[q]; tau[q] = their 64th distance (+inf if
+// the list is shorter).
 __global__ void __launch_bounds__(256)
     select1_kernel(const float* __restrict__ dump, const unsigned* __restrict__ seg,
                    const uint32_t* __restrict__ inv1, const uint32_t* __restrict__ vals,
@@ -740,7 +741,7 @@ __global__ void __launch_bounds__(256)
         const uint32_t l = probes[vals[i]];
         const int nb = (int)(lend[l] - lbeg[l]);
         const uint32_t tag0 = (uint32_t)lbeg[l];
-        // the row is padded to a multiple of 128 floats: 128 per step
+        // the row is padded to a multiple of 128 floats
         const float4* row4 = reinterpret_cast<const float4*>(dump + seg[i]);
         for (int base = 0; base < nb; base += 128) {
             const float4 v = row4[(base >> 2) + lane];
@@ -818,23 +819,23 @@ struct CertParams {
 
 constexpr int CERT_WARPS = 8;
 
-// One warp per query: the 64 shortlisted codes rescored with exact_adc (the
-// reference's arithmetic), their exact keys and lists kept for certify_kernel,
-// the k best written out, and the exact k-th distance dk.
+// Two warps per query, 32 shortlisted codes each: the codes rescored with
+// exact_adc (the reference's arithmetic), their exact keys and lists kept for
+// certify_kernel; then the query's first warp writes the k best and the exact
+// k-th distance dk.
+constexpr int RS_QUERIES = CERT_WARPS / 2;  // queries per block
 template <int ORDER>
 __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) {
-    __shared__ uint64_t buf[CERT_WARPS * 64];
+    __shared__ uint64_t keys[RS_QUERIES][LIST_K];
+    __shared__ uint64_t buf[RS_QUERIES * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.x * CERT_WARPS + warp;
-    if (q >= r.nq) return;  // whole warp
-    const int m = r.m, sub = r.dim / m;
-    const float* qv = r.Q + (size_t)q * r.dim;
-    const uint64_t* ak = r.approx + (size_t)q * LIST_K;
-    WarpTopK<1> tk;
-    tk.init(r.k, buf + warp * 64);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint64_t key = ak[h * 32 + lane];
+    const int lq = warp >> 1, h = warp & 1;
+    const int q = blockIdx.x * RS_QUERIES + lq;
+    const bool qok = q < r.nq;
+    if (qok) {
+        const int m = r.m, sub = r.dim / m;
+        const float* qv = r.Q + (size_t)q * r.dim;
+        const uint64_t key = r.approx[(size_t)q * LIST_K + h * 32 + lane];
         uint64_t ek = KEY_NONE;
         int el = -1;
         if (key != KEY_NONE) {
@@ -852,6 +853,15 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
         }
         r.ekeys[(size_t)q * LIST_K + h * 32 + lane] = ek;
         r.elist[(size_t)q * LIST_K + h * 32 + lane] = el;
+        keys[lq][h * 32 + lane] = ek;
+    }
+    __syncthreads();
+    if (!qok || h != 0) return;
+    WarpTopK<1> tk;
+    tk.init(r.k, buf + lq * 64);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const uint64_t ek = keys[lq][hh * 32 + lane];
         if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
     }
     tk.store(r.out_keys + (size_t)q * r.k);
@@ -964,6 +974,41 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     if (__any_sync(0xffffffffu, s0 != KEY_NONE)) seed.merge32(s0);
     if (__any_sync(0xffffffffu, s1 != KEY_NONE)) seed.merge32(s1);
     seed.store(r.out_keys + (size_t)q * r.k);
+}
+
+// ---------------------------------------------------------------------------
+// exact re-scan of failed lists, one block per (query, list)
+// ---------------------------------------------------------------------------
+// units uoff[f] .. uoff[f+1] of flag slot f: (query, failed list)
+__global__ void expand_units_kernel(int nflag, int take, const uint32_t* __restrict__ flag_list,
+                                    const uint32_t* __restrict__ fail_probes,
+                                    const uint32_t* __restrict__ uoff,
+                                    uint32_t* __restrict__ unit_q, uint32_t* __restrict__ unit_l) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= nflag) return;
+    const uint32_t q = flag_list[f];
+    for (uint32_t u = uoff[f], j = 0; u < uoff[f + 1]; ++u, ++j) {
+        unit_q[u] = q;
+        unit_l[u] = fail_probes[(size_t)f * take + j];
+    }
+}
+
+// One warp per flag slot: the query's seed (its out_keys row) and the exact
+// top-k of each of its re-scanned lists, merged into its out_keys row.
+__global__ void __launch_bounds__(256)
+    merge_units_kernel(int nflag, int k, const uint32_t* __restrict__ flag_list,
+                       const uint32_t* __restrict__ uoff, const uint64_t* __restrict__ unit_keys,
+                       uint64_t* __restrict__ out_keys) {
+    __shared__ uint64_t buf[8 * 64];
+    const int warp = threadIdx.x >> 5;
+    const int f = blockIdx.x * 8 + warp;
+    if (f >= nflag) return;
+    uint64_t* row = out_keys + (size_t)flag_list[f] * k;
+    WarpTopK<1> tk;
+    tk.init(k, buf + warp * 64);
+    tk.ingest(row, k);
+    for (uint32_t u = uoff[f]; u < uoff[f + 1]; ++u) tk.ingest(unit_keys + (size_t)u * k, k);
+    tk.store(row);
 }
 
 // ---------------------------------------------------------------------------
@@ -1280,8 +1325,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.elist = h->t_elist.p;
     r.dk = h->t_dk.p;
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
-    if (order == ORDER_LANE8) rescore_kernel<ORDER_LANE8><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
-    else rescore_kernel<ORDER_FAST4><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    const unsigned rgrid = (unsigned)((nq + RS_QUERIES - 1) / RS_QUERIES);
+    if (order == ORDER_LANE8) rescore_kernel<ORDER_LANE8><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+    else rescore_kernel<ORDER_FAST4><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the answer's k-th distance is at most the smallest exact k-th of any device
@@ -1303,7 +1349,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
                        size_t take, const uint64_t* lbeg, const uint64_t* lend,
                        uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
-                       double* pass_ms) {
+                       double* pass_ms, std::vector<uint32_t>* fail_cnt_host) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
@@ -1336,8 +1382,15 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     uint32_t hv[2] = {0, 0};
     FDB_CUDA(cudaMemcpyAsync(&hv[0], flags, 4, cudaMemcpyDeviceToHost, s));
     FDB_CUDA(cudaMemcpyAsync(&hv[1], err, 4, cudaMemcpyDeviceToHost, s));
+    if (fail_cnt_host) {
+        // read with the count in one synchronisation (only the first count entries matter)
+        fail_cnt_host->resize(nq);
+        FDB_CUDA(cudaMemcpyAsync(fail_cnt_host->data(), h->t_fcnt.p, nq * 4,
+                                 cudaMemcpyDeviceToHost, s));
+    }
     FDB_CUDA(cudaStreamSynchronize(s));
     FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
+    if (fail_cnt_host) fail_cnt_host->resize(hv[0]);
     if (pass_ms) {
         double tot = 0.0;
         for (size_t ci = 0; ci < nchunks; ++ci) {
@@ -1348,6 +1401,51 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
         *pass_ms = tot;
     }
     return hv[0];
+}
+
+}  // namespace fdb
+
+namespace fdb {
+
+// Exact re-scan of the lists that failed certification: one block per
+// (flagged query, failed list) computes that list's exact top-k, and each
+// flagged query's seed and lists are merged into its keys row.
+void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, uint32_t nflag,
+                   const std::vector<uint32_t>& fail_cnt, uint64_t* out_keys) {
+    if (nflag == 0) return;
+    cudaStream_t s = h->ctx->c.stream;
+    std::vector<uint32_t> uoff(nflag + 1, 0);
+    for (uint32_t f = 0; f < nflag; ++f) uoff[f + 1] = uoff[f] + fail_cnt[f];
+    const uint32_t nu = uoff[nflag];
+    h->t_uoff.ensure(nflag + 1);
+    FDB_CUDA(cudaMemcpyAsync(h->t_uoff.p, uoff.data(), (nflag + 1) * 4, cudaMemcpyHostToDevice, s));
+    if (nu > 0) {
+        h->t_unit_q.ensure(nu);
+        h->t_unit_l.ensure(nu);
+        h->t_unit_keys.ensure((size_t)nu * k);
+        ivtc::expand_units_kernel<<<(nflag + 127) / 128, 128, 0, s>>>(
+            (int)nflag, base.nprobe, h->s_flags.p + 1, h->t_fprobes.p, h->t_uoff.p, h->t_unit_q.p,
+            h->t_unit_l.p);
+        FDB_LAUNCH_CHECK();
+        ScanParams e = base;
+        e.nq = (int)nu;
+        e.qidx = h->t_unit_q.p;
+        e.probe_list = h->t_unit_l.p;
+        e.probe_cnt = nullptr;
+        e.nprobe = 1;
+        e.k = (int)k;
+        e.out_keys = h->t_unit_keys.p;
+        e.out_by_block = true;
+        e.seed = false;
+        e.stat = nullptr;
+        e.btab = nullptr;
+        launch_scan(s, e, order);
+    }
+    ivtc::merge_units_kernel<<<(nflag + 7) / 8, 256, 0, s>>>(
+        (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
+    FDB_LAUNCH_CHECK();
+    // (the offsets came from pageable memory: the copy call returned once they
+    // were staged, so the vector may go)
 }
 
 }  // namespace fdb

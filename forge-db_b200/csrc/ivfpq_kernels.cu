@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
         unsigned long long nscan = 0, nl = 0;
         const uint32_t* pl = a.probe_list ? a.probe_list + (size_t)qi * a.nprobe
                                           : a.probes + (size_t)q * a.nprobe;
-        const int npq = a.probe_list ? (int)a.probe_cnt[qi] : a.nprobe;
+        const int npq = (a.probe_list && a.probe_cnt) ? (int)a.probe_cnt[qi] : a.nprobe;
         for (int p = 0; p < npq; ++p) {
             const uint32_t l = pl[p];
             const uint64_t beg = a.offs[l], end = a.ends[l];
@@ -468,8 +468,9 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
         __syncthreads();
         if (warp == 0) {
             block_merge_warp0(tk, lists, SCAN_WARPS);
-            if (a.seed) tk.ingest(a.out_keys + (size_t)q * a.k, a.k);
-            tk.store(a.out_keys + (size_t)q * a.k);
+            uint64_t* orow = a.out_keys + (size_t)(a.out_by_block ? qi : q) * a.k;
+            if (a.seed) tk.ingest(orow, a.k);
+            tk.store(orow);
         }
         if (threadIdx.x == 0 && a.stat) {
             atomicAdd(&a.stat[0], nl);
