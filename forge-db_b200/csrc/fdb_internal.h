@@ -290,7 +290,7 @@ struct fdb_ivfpq {
     fdb::DevBuf<uint32_t> s_counts, s_flags;
     fdb::DevBuf<unsigned long long> s_stat;
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
-    fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv1, t_plen,
+    fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv, t_plen,
         t_seg, t_fprobes, t_fcnt, t_uoff, t_unit_q, t_unit_l;
     fdb::DevBuf<uint64_t> t_unit_keys;
     fdb::DevBuf<float> t_dump, t_dk;

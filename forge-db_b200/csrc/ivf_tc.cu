@@ -583,7 +583,7 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
                                int dim, int dpad, const float* __restrict__ coarse, int sb,
                                __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
                                float* __restrict__ pair_rn, float* __restrict__ pair_s2,
-                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv1) {
+                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
     const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const unsigned npairs = poff[2 * nlist];  // pairs with a non-empty list
@@ -639,12 +639,13 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
         pair_rn[i] = coarse[(size_t)q * nlist + l];
         pair_s2[i] = bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
         if (bad) qbad[q] = 1u;
-        if (i < poff[nlist]) inv1[q] = (uint32_t)i;  // the query's pass-1 pair
+        inv[v] = (uint32_t)i;  // where probe v = q * take + j sits among the sorted pairs
     }
 }
 
-// plen[i] = the padded length of pass-1 pair i's list (0 past the pass-1
-// pairs); an exclusive sum turns it into the pair's row offset in the dump.
+// plen[i] = the length of pair i's dump row: its whole list (padded to whole
+// tiles) for a pass-1 pair, the list's first tile for the others, 0 past the
+// pairs; an exclusive sum turns it into the row's offset in the dump.
 __global__ void plen_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
                             int nlist, const uint32_t* __restrict__ probes,
                             const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend,
@@ -652,16 +653,20 @@ __global__ void plen_kernel(const uint32_t* __restrict__ vals, const unsigned* _
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     unsigned len = 0;
-    if ((unsigned)i < poff[nlist]) {
+    if ((unsigned)i < poff[2 * nlist]) {
         const uint32_t l = probes[vals[i]];
-        len = (unsigned)((lend[l] - lbeg[l] + TILE_N - 1) / TILE_N * TILE_N);
+        len = (unsigned)i < poff[nlist]
+                  ? (unsigned)((lend[l] - lbeg[l] + TILE_N - 1) / TILE_N * TILE_N)
+                  : (unsigned)TILE_N;
     }
     plen[i] = len;
 }
 
-// Items of both passes, lists in `lorder`, one block: every (list, 128 pair
-// rows, chunk of up to CHUNK_TILES tiles).  items[0 .. n1) are pass 1,
-// items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
+// Items of both passes, lists in `lorder`, one block.  An item is (list, up
+// to 128 pair rows, a run of at most CHUNK_TILES tiles of the list).  Pass 1
+// (dump) holds the pass-1 segments' whole lists and the pass-2 segments' first
+// tiles; pass 2 (filter) holds the pass-2 segments' other tiles.  items[0 ..
+// n1) are pass 1, items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
 constexpr int ITEM_THREADS = 1024;
 __global__ void __launch_bounds__(ITEM_THREADS)
     build_items_kernel(const unsigned* __restrict__ poff, int nlist,
@@ -673,31 +678,38 @@ __global__ void __launch_bounds__(ITEM_THREADS)
     __shared__ unsigned carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
-    for (int pass = 0; pass < 2; ++pass) {
+    // kind 0: pass-1 segments, whole list; kind 1: pass-2 segments, first tile
+    // (both in pass 1); kind 2: pass-2 segments, tiles 1.. (pass 2)
+    for (int kind = 0; kind < 3; ++kind) {
+        const int seg = kind == 0 ? 0 : 1;
         for (int base = 0; base < nlist; base += ITEM_THREADS) {
             const int i = base + threadIdx.x;
-            unsigned cnt = 0, a0 = 0;
+            unsigned cnt = 0, a0 = 0, len = 0;
             uint32_t l = 0;
             if (i < nlist) {
                 l = lorder[i];
-                a0 = poff[pass * nlist + l];
-                cnt = poff[pass * nlist + l + 1] - a0;
+                a0 = poff[seg * nlist + l];
+                cnt = poff[seg * nlist + l + 1] - a0;
+                len = (unsigned)(lend[l] - lbeg[l]);
             }
-            const unsigned len = i < nlist ? (unsigned)(lend[l] - lbeg[l]) : 0u;
-            const unsigned nrow = (cnt + TILE_M - 1) / TILE_M;
-            const unsigned nchunk = (len + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
+            // codes [c_lo, c_hi) of the list this kind covers
+            const unsigned c_lo = kind == 2 ? (unsigned)TILE_N : 0u;
+            const unsigned c_hi = kind == 1 ? min(len, (unsigned)TILE_N) : len;
+            const unsigned span = c_hi > c_lo ? c_hi - c_lo : 0u;
+            const unsigned nrow = span > 0 ? (cnt + TILE_M - 1) / TILE_M : 0u;
+            const unsigned nchunk = (span + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
             const unsigned nit = nrow * nchunk;
             unsigned off, tot;
             Scan(tmp).ExclusiveSum(nit, off, tot);
             const unsigned at = carry + off;
             for (unsigned t = 0; t < nit; ++t) {
                 const unsigned rb = t / nchunk, ch = t - rb * nchunk;
-                const unsigned c0 = ch * CHUNK_TILES * TILE_N;
+                const unsigned c0 = c_lo + ch * CHUNK_TILES * TILE_N;
                 Item it;
                 it.a0 = a0 + rb * TILE_M;
                 it.na = min((unsigned)TILE_M, cnt - rb * TILE_M);
                 it.b0 = pstart[l] + c0;
-                it.nb = min((unsigned)(CHUNK_TILES * TILE_N), len - c0);
+                it.nb = min((unsigned)(CHUNK_TILES * TILE_N), c_hi - c0);
                 it.tag0 = (uint32_t)lbeg[l] + c0;
                 it.col0 = c0;
                 it.pad[0] = it.pad[1] = 0;
@@ -709,11 +721,11 @@ __global__ void __launch_bounds__(ITEM_THREADS)
         }
         if (threadIdx.x == 0) {
             // (the host sizes items[] for every case; cap only guards it)
-            if (pass == 0) {
+            if (kind == 1) {
                 range[0] = 0;
                 range[1] = min(carry, cap);
                 range[2] = min(carry, cap);
-            } else {
+            } else if (kind == 2) {
                 range[3] = min(carry, cap) - range[2];
             }
         }
@@ -721,32 +733,36 @@ __global__ void __launch_bounds__(ITEM_THREADS)
     }
 }
 
-// One warp per query: the top-64 keys of its pass-1 list, read from the dump
-// (128 values per step), into part[q]; tau[q] = their 64th distance (+inf if
-// the list is shorter).
+// One warp per query: the top-64 keys over its dump rows (the whole pass-1
+// list and the first tile of each other list it probes here; 128 values per
+// step) into part[q]; tau[q] = their 64th distance (+inf if fewer).
 __global__ void __launch_bounds__(256)
     select1_kernel(const float* __restrict__ dump, const unsigned* __restrict__ seg,
-                   const uint32_t* __restrict__ inv1, const uint32_t* __restrict__ vals,
-                   const uint32_t* __restrict__ probes, const uint64_t* __restrict__ lbeg,
-                   const uint64_t* __restrict__ lend, int nq, uint64_t* __restrict__ part,
-                   float* __restrict__ tau) {
+                   const uint32_t* __restrict__ inv, const unsigned* __restrict__ poff,
+                   int nlist, const uint32_t* __restrict__ probes, int take,
+                   const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend, int nq,
+                   uint64_t* __restrict__ part, float* __restrict__ tau) {
     __shared__ uint64_t buf[8 * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * 8 + warp;
     if (q >= nq) return;
     WarpTopK<2> tk;
     tk.init(LIST_K, buf + warp * 64);
-    const uint32_t i = inv1[q];
-    if (i != 0xffffffffu) {
-        const uint32_t l = probes[vals[i]];
-        const int nb = (int)(lend[l] - lbeg[l]);
+    const unsigned n1 = poff[nlist], npairs = poff[2 * nlist];
+    for (int jp = 0; jp < take; ++jp) {
+        const size_t v = (size_t)q * take + jp;
+        const uint32_t i = inv[v];
+        if (i >= npairs) continue;  // list empty or held elsewhere
+        const uint32_t l = probes[v];
+        const int len = (int)(lend[l] - lbeg[l]);
+        const int nb = i < n1 ? len : min(len, TILE_N);
         const uint32_t tag0 = (uint32_t)lbeg[l];
-        // the row is padded to a multiple of 128 floats
+        // rows are padded to a multiple of 128 floats
         const float4* row4 = reinterpret_cast<const float4*>(dump + seg[i]);
         for (int base = 0; base < nb; base += 128) {
-            const float4 v = row4[(base >> 2) + lane];
+            const float4 x4 = row4[(base >> 2) + lane];
             const int j = base + 4 * lane;
-            const float d[4] = {v.x, v.y, v.z, v.w};
+            const float d[4] = {x4.x, x4.y, x4.z, x4.w};
             uint64_t key[4];
             bool any = false;
 #pragma unroll
@@ -758,8 +774,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
         }
-        tk.flush();
     }
+    tk.flush();
     tk.store(part + (size_t)q * LIST_K);
     if (lane == 0) tau[q] = tk.thr == KEY_NONE ? INF : key_dist(tk.thr);
 }
@@ -1190,15 +1206,15 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         probes, (int)nq, (int)take, lbeg, lend, h->offs.p, nlist, h->t_keys.p, h->t_vals.p,
         stat);
     FDB_LAUNCH_CHECK();
-    h->t_plen.ensure(nq + 1);
-    h->t_seg.ensure(nq + 1);
+    h->t_plen.ensure(np + 1);
+    h->t_seg.ensure(np + 1);
     size_t tmp_sort = 0, tmp_seg = 0;
     const int end_bit = bits_for((uint32_t)nkeys);
     FDB_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_sort, h->t_keys.p, h->t_keys.p + np,
                                              h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
                                              s));
     FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_seg, h->t_plen.p, h->t_seg.p,
-                                           (int)nq + 1, s));
+                                           (int)np + 1, s));
     h->t_tmp.ensure(std::max(tmp_sort, tmp_seg));
     FDB_CUDA(cub::DeviceRadixSort::SortPairs(h->t_tmp.p, tmp_sort, h->t_keys.p, h->t_keys.p + np,
                                              h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
@@ -1213,26 +1229,28 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_rn.ensure(np);
     h->t_s2.ensure(np);
     h->t_qbad.ensure(nq);
-    h->t_inv1.ensure(nq);
+    h->t_inv.ensure(np);
     FDB_CUDA(cudaMemsetAsync(h->t_qbad.p, 0, nq * 4, s));
-    FDB_CUDA(cudaMemsetAsync(h->t_inv1.p, 0xff, nq * 4, s));
+    FDB_CUDA(cudaMemsetAsync(h->t_inv.p, 0xff, np * 4, s));
     build_a_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
         svals, h->t_off.p, nlist, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad, coarse,
-        h->tc_sb, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_qbad.p, h->t_inv1.p);
+        h->tc_sb, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_qbad.p, h->t_inv.p);
     FDB_LAUNCH_CHECK();
-    plen_kernel<<<(unsigned)((nq + 1 + 255) / 256), 256, 0, s>>>(
-        svals, h->t_off.p, nlist, probes, lbeg, lend, (int)nq + 1, h->t_plen.p);
+    plen_kernel<<<(unsigned)((np + 1 + 255) / 256), 256, 0, s>>>(
+        svals, h->t_off.p, nlist, probes, lbeg, lend, (int)np + 1, h->t_plen.p);
     FDB_LAUNCH_CHECK();
     FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp.p, tmp_seg, h->t_plen.p, h->t_seg.p,
-                                           (int)nq + 1, s));
-    h->t_dump.ensure(std::max<size_t>(1, nq * h->tc_maxpad));
-    // items per (pass, list) = ceil(P / 128) * ceil(tiles / CHUNK_TILES) <= (a + 1)(b + 1)
-    // with a = P / 128, b = tiles / CHUNK_TILES, summed over both passes
+                                           (int)np + 1, s));
+    // a whole (padded) list per pass-1 pair, one tile per other pair
+    h->t_dump.ensure(std::max<size_t>(1, nq * h->tc_maxpad + np * TILE_N));
+    // items per (kind, list) = ceil(P / 128) * ceil(tiles / CHUNK_TILES) <= (a + 1)(b + 1)
+    // with a = P / 128, b = tiles / CHUNK_TILES: the whole-list kinds (0 and 2)
+    // plus the first-tile kind (1, one chunk per row block)
     const size_t max_tiles = h->tc_maxpad / TILE_N;
     const size_t all_tiles = h->tc_rows / TILE_N;
     const size_t max_items = np * ((max_tiles + CHUNK_TILES - 1) / CHUNK_TILES) / TILE_M +
                              np / TILE_M + 2 * (all_tiles / CHUNK_TILES + 1) +
-                             2 * (size_t)nlist + 2;
+                             2 * (size_t)nlist + (np / TILE_M + nlist) + 2;
     h->t_items.ensure(max_items * sizeof(Item));
     Item* items = reinterpret_cast<Item*>(h->t_items.p);
     build_items_kernel<<<1, ITEM_THREADS, 0, s>>>(h->t_off.p, nlist, h->lorder.p, lbeg, lend,
@@ -1242,7 +1260,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     // --- pass 1: distances of each query's first list; its top-64 and tau ---
     const CUtensorMap am = make_map(h->t_a16.p, np, dpad);
     const CUtensorMap bm = make_map(h->dec16.p, h->tc_rows, dpad);
-    const int cap = 1024;
+    const int cap = 4096;  // candidates per query (uniform data can admit a few thousand)
     h->t_part.ensure(nq * LIST_K);
     h->t_tau.ensure(nq);
     h->t_cand_cnt.ensure(nq);
@@ -1269,8 +1287,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     const int grid = c.sm_count;
     launch_pass<EPI_DUMP>(s, am, bm, grid, p);
     select1_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
-        h->t_dump.p, h->t_seg.p, h->t_inv1.p, svals, probes, lbeg, lend, (int)nq, h->t_part.p,
-        h->t_tau.p);
+        h->t_dump.p, h->t_seg.p, h->t_inv.p, h->t_off.p, nlist, probes, (int)take, lbeg, lend,
+        (int)nq, h->t_part.p, h->t_tau.p);
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
@@ -1354,7 +1372,8 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     cudaStream_t s = c.stream;
     FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
     const size_t budget = (size_t)1 << 28;  // floats
-    const size_t chunk = std::max<size_t>(1, std::min(nq, budget / std::max<size_t>(h->tc_maxpad, 1)));
+    const size_t per_query = h->tc_maxpad + take * ivtc::TILE_N;  // dump floats per query
+    const size_t chunk = std::max<size_t>(1, std::min(nq, budget / per_query));
     h->t_range.ensure(8);
     h->t_fprobes.ensure(nq * take);
     h->t_fcnt.ensure(nq);
