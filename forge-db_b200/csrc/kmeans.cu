@@ -20,6 +20,7 @@
 
 #include "fdb_device.cuh"
 #include "fdb_internal.h"
+#include "fdb_kernels.h"
 
 namespace fdb {
 
@@ -116,8 +117,178 @@ static void launch_assign_multi(cudaStream_t s, const float* x, size_t n, int di
     FDB_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------
+// register-tiled assignment (one problem, large n x k)
+// ---------------------------------------------------------------------------
+// A block covers AT_Q points x AT_C centroids; a thread AT_TQ x AT_TC pairs.
+// The distance is l2sq_exact's: eight lane accumulators over i = j (mod 8),
+// summed left to right, then the unfused scalar tail.  The block runs the
+// lanes in turn, staging only dims i = j (mod 8) of both tiles (transposed) in
+// shared memory, so a pair needs two registers and the result is
+// bit-identical.  Each block reduces, per point, the first minimum of its
+// centroids into a 64-bit key (orderable distance, centroid index) and folds
+// it into best[p] with one atomicMin: smaller distance first, then the
+// smaller index -- the first minimum over all centroids, as Iterator::min_by.
+constexpr int AT_Q = 128, AT_C = 128, AT_TQ = 4, AT_TC = 8;
+constexpr int AT_THREADS = (AT_Q / AT_TQ) * (AT_C / AT_TC);  // 512
+
+__global__ void __launch_bounds__(AT_THREADS)
+    assign_tiled_kernel(const float* __restrict__ XT, size_t n, size_t n_pad, int dim,
+                        const float* __restrict__ CT, int k, int k_pad,
+                        unsigned long long* __restrict__ best) {
+    extern __shared__ __align__(16) float at_smem[];
+    const int G = dim >> 3;  // full groups of eight
+    float* qs = at_smem;                 // [G][AT_Q]
+    float* cs = qs + (size_t)G * AT_Q;   // [G][AT_C]
+    unsigned long long* red = reinterpret_cast<unsigned long long*>(cs + (size_t)G * AT_C);
+    const size_t p0 = (size_t)blockIdx.x * AT_Q;
+    const int c0 = blockIdx.y * AT_C;
+    const int tq = threadIdx.x & 31;  // point group (4 points)
+    const int tc = threadIdx.x >> 5;  // centroid group (8 centroids)
+    const float* qb = qs + tq * AT_TQ;
+    const float* cb = cs + tc * AT_TC;
+    float t[AT_TQ][AT_TC];
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < G * (AT_Q / 4); e += AT_THREADS) {
+            const int g = e / (AT_Q / 4), v = e - g * (AT_Q / 4);
+            reinterpret_cast<float4*>(qs + (size_t)g * AT_Q)[v] = __ldg(
+                reinterpret_cast<const float4*>(XT + (size_t)(8 * g + j) * n_pad + p0) + v);
+        }
+        for (int e = threadIdx.x; e < G * (AT_C / 4); e += AT_THREADS) {
+            const int g = e / (AT_C / 4), v = e - g * (AT_C / 4);
+            reinterpret_cast<float4*>(cs + (size_t)g * AT_C)[v] = __ldg(
+                reinterpret_cast<const float4*>(CT + (size_t)(8 * g + j) * k_pad + c0) + v);
+        }
+        __syncthreads();
+        float acc[AT_TQ][AT_TC];
+#pragma unroll
+        for (int a = 0; a < AT_TQ; ++a)
+#pragma unroll
+            for (int b = 0; b < AT_TC; ++b) acc[a][b] = 0.0f;
+#pragma unroll 4
+        for (int g = 0; g < G; ++g) {
+            const float4 qv = *reinterpret_cast<const float4*>(qb + (size_t)g * AT_Q);
+            const float4 c0v = *reinterpret_cast<const float4*>(cb + (size_t)g * AT_C);
+            const float4 c1v = *reinterpret_cast<const float4*>(cb + (size_t)g * AT_C + 4);
+            const float qa[AT_TQ] = {qv.x, qv.y, qv.z, qv.w};
+            const float ca[AT_TC] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
+#pragma unroll
+            for (int a = 0; a < AT_TQ; ++a)
+#pragma unroll
+                for (int b = 0; b < AT_TC; ++b) {
+                    const float d = __fsub_rn(qa[a], ca[b]);
+                    acc[a][b] = __fmaf_rn(d, d, acc[a][b]);
+                }
+        }
+#pragma unroll
+        for (int a = 0; a < AT_TQ; ++a)
+#pragma unroll
+            for (int b = 0; b < AT_TC; ++b) t[a][b] = j == 0 ? acc[a][b] : __fadd_rn(t[a][b], acc[a][b]);
+    }
+    for (int i = 8 * G; i < dim; ++i) {  // unfused scalar tail
+#pragma unroll
+        for (int a = 0; a < AT_TQ; ++a) {
+            const float xq = __ldg(XT + (size_t)i * n_pad + p0 + tq * AT_TQ + a);
+#pragma unroll
+            for (int b = 0; b < AT_TC; ++b) {
+                const float d = __fsub_rn(xq, __ldg(CT + (size_t)i * k_pad + c0 + tc * AT_TC + b));
+                t[a][b] = __fadd_rn(t[a][b], __fmul_rn(d, d));
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < AT_TQ; ++a) {
+        unsigned long long key = ~0ull;
+#pragma unroll
+        for (int b = 0; b < AT_TC; ++b) {
+            const int l = c0 + tc * AT_TC + b;
+            if (l < k) {
+                const unsigned long long kk = make_key(t[a][b], (uint32_t)l);
+                key = kk < key ? kk : key;
+            }
+        }
+        red[(size_t)tc * AT_Q + tq * AT_TQ + a] = key;
+    }
+    __syncthreads();
+    if (threadIdx.x < AT_Q) {
+        const size_t p = p0 + threadIdx.x;
+        if (p < n) {
+            unsigned long long key = ~0ull;
+            for (int r = 0; r < AT_C / AT_TC; ++r) {
+                const unsigned long long kk = red[(size_t)r * AT_Q + threadIdx.x];
+                key = kk < key ? kk : key;
+            }
+            atomicMin(best + p, key);
+        }
+    }
+}
+
+__global__ void key_index_kernel(const unsigned long long* __restrict__ best, size_t n,
+                                 uint32_t* __restrict__ out) {
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n) out[t] = (uint32_t)best[t];
+}
+
+// out[p] = first-minimum centroid of point p, from the transposed operands
+// XT [dim][n_pad] (n_pad a multiple of 128) and CT [dim][k_pad] (k_pad a
+// multiple of 128).  best: scratch of n keys.
+void launch_assign_tiled(cudaStream_t s, const float* XT, size_t n, size_t n_pad, int dim,
+                         const float* CT, int k, int k_pad, unsigned long long* best,
+                         uint32_t* out) {
+    if (n == 0) return;
+    FDB_REQUIRE(n_pad % AT_Q == 0 && k_pad % AT_C == 0, FDB_ERR_UNSUPPORTED, "bad padding");
+    const size_t smem = (size_t)(dim >> 3) * (AT_Q + AT_C) * sizeof(float) +
+                        (size_t)(AT_C / AT_TC) * AT_Q * sizeof(unsigned long long);
+    FDB_REQUIRE(smem <= 227 * 1024, FDB_ERR_UNSUPPORTED, "dimension too large for tiled assign");
+    if (smem > 48 * 1024)
+        FDB_CUDA(cudaFuncSetAttribute(assign_tiled_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FDB_CUDA(cudaMemsetAsync(best, 0xff, n * sizeof(unsigned long long), s));
+    dim3 grid((unsigned)(n_pad / AT_Q), (unsigned)(k_pad / AT_C));
+    assign_tiled_kernel<<<grid, AT_THREADS, smem, s>>>(XT, n, n_pad, dim, CT, k, k_pad, best);
+    FDB_LAUNCH_CHECK();
+    key_index_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(best, n, out);
+    FDB_LAUNCH_CHECK();
+}
+
+// The tiled kernel pays off for many points and centroids of 16+ dimensions
+// (and its dim/8 rows of both tiles must fit in shared memory).
+static bool assign_tiled_ok(size_t n, int dim, int k) {
+    return n >= 4096 && k >= 64 && dim >= 16 && (size_t)(dim >> 3) * (AT_Q + AT_C) * 4 +
+                                                       16 * AT_Q * 8 <= 200 * 1024;
+}
+
+// Transposed, zero-padded copies of the points (once) and the centroids.
+struct AssignTiled {
+    DevBuf<float> XT, CT;
+    DevBuf<unsigned long long> best;
+    size_t n_pad = 0;
+    int k_pad = 0;
+    void prepare_points(cudaStream_t s, const float* x, size_t n, int dim) {
+        n_pad = (n + AT_Q - 1) / AT_Q * AT_Q;
+        XT.alloc(n_pad * dim);
+        launch_transpose_pad(s, x, (int)n, dim, (int)n_pad, XT.p);
+        best.alloc(n);
+    }
+    void run(cudaStream_t s, size_t n, int dim, const float* cent, int k, uint32_t* out) {
+        k_pad = (k + AT_C - 1) / AT_C * AT_C;
+        CT.ensure((size_t)k_pad * dim);
+        launch_transpose_pad(s, cent, k, dim, k_pad, CT.p);
+        launch_assign_tiled(s, XT.p, n, n_pad, dim, CT.p, k, k_pad, best.p, out);
+    }
+};
+
 void launch_assign(cudaStream_t s, const float* x, size_t n, int dim, int ld, const float* cent,
                    int k, uint32_t* out) {
+    if (ld == dim && assign_tiled_ok(n, dim, k) && n < (1ull << 31)) {
+        AssignTiled at;
+        at.prepare_points(s, x, n, dim);
+        at.run(s, n, dim, cent, k, out);
+        FDB_CUDA(cudaStreamSynchronize(s));  // scratch is released on return
+        return;
+    }
     launch_assign_multi(s, x, n, dim, ld, 1, cent, k, out, nullptr);
 }
 
@@ -241,13 +412,19 @@ void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out) 
     std::vector<int> active(nsub, 1);
     std::vector<float> h_change(nsub);
     for (int q = 0; q < nsub; ++q) iters_out[q] = 0;
+    // one large problem: register-tiled assignment over a transposed copy
+    AssignTiled at;
+    const bool tiled = nsub == 1 && pb.ld == dim && assign_tiled_ok(n, dim, k) &&
+                       n < (1ull << 31);
+    if (tiled) at.prepare_points(s, pb.x, n, dim);
     for (int it = 0; it < pb.max_iters; ++it) {
         bool any = false;
         for (int q = 0; q < nsub; ++q) any |= active[q] != 0;
         if (!any) break;
         FDB_CUDA(cudaMemcpyAsync(d_active.p, active.data(), nsub * sizeof(int),
                                  cudaMemcpyHostToDevice, s));
-        launch_assign_multi(s, pb.x, n, dim, pb.ld, nsub, cent, k, assign.p, d_active.p);
+        if (tiled) at.run(s, n, dim, cent, k, assign.p);
+        else launch_assign_multi(s, pb.x, n, dim, pb.ld, nsub, cent, k, assign.p, d_active.p);
         group_multi(s, assign.p, n, nsub, k, perm.p, offs.p);
         unsigned g = (unsigned)((csz + 255) / 256);
         update_kernel<<<g, 256, 0, s>>>(pb.x, n, dim, pb.ld, nsub, k, perm.p, offs.p, cent, neu.p,
