@@ -388,18 +388,41 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         // search() with nprobe == 0 probes nothing (ivf_pq.rs:548-552)
         FDB_CUDA(cudaMemsetAsync(h->s_keys.p, 0xff, per * 8, s));
     } else {
-        h->s_coarse.ensure(nq * (size_t)nlist);
-        h->s_probe.ensure(nq * take);
-        if (h->centsT.p) {
-            const int nq_pad = (int)((nq + 31) / 32 * 32);
-            h->s_qT.ensure(h->dim * (size_t)nq_pad);
-            launch_transpose_pad(s, dQ, (int)nq, (int)h->dim, nq_pad, h->s_qT.p);
-            launch_coarse_tiled(s, h->s_qT.p, (int)nq, nq_pad, (int)h->dim, h->centsT.p, nlist,
-                                h->nlist_pad, h->s_coarse.p);
-        } else {
-            launch_coarse_dist(s, dQ, (int)nq, (int)h->dim, h->cents.p, nlist, h->s_coarse.p);
+        // Probe selection.  Every device of a sharded index holds all
+        // centroids, so each selects the probes of one slice of the queries
+        // and an all-gather gives every device all probes and their coarse
+        // distances (the slices are contiguous: rank-major = query-major).
+        const int world = h->sharded ? c.world : 1, rank = h->sharded ? c.rank : 0;
+        const size_t slice = (nq + world - 1) / world;
+        const size_t q0 = std::min(nq, slice * (size_t)rank);
+        const size_t nql = std::min(nq, q0 + slice) - q0;
+        h->s_probe.ensure(slice * world * take);
+        h->s_pdist.ensure(slice * world * take);
+        if (nql > 0) {
+            const float* Ql = dQ + q0 * h->dim;
+            h->s_coarse.ensure(nql * (size_t)nlist);
+            if (h->centsT.p) {
+                const int nq_pad = (int)((nql + 31) / 32 * 32);
+                h->s_qT.ensure(h->dim * (size_t)nq_pad);
+                launch_transpose_pad(s, Ql, (int)nql, (int)h->dim, nq_pad, h->s_qT.p);
+                launch_coarse_tiled(s, h->s_qT.p, (int)nql, nq_pad, (int)h->dim, h->centsT.p,
+                                    nlist, h->nlist_pad, h->s_coarse.p);
+            } else {
+                launch_coarse_dist(s, Ql, (int)nql, (int)h->dim, h->cents.p, nlist,
+                                   h->s_coarse.p);
+            }
+            launch_select(s, h->s_coarse.p, (int)nql, nlist, (int)take, h->s_probe.p + q0 * take,
+                          h->s_pdist.p + q0 * take);
         }
-        launch_select(s, h->s_coarse.p, (int)nq, nlist, (int)take, h->s_probe.p);
+        if (world > 1) {
+            const size_t cnt = slice * take;
+            FDB_NCCL(ncclGroupStart());
+            FDB_NCCL(ncclAllGather(h->s_probe.p + cnt * rank, h->s_probe.p, cnt, ncclUint32,
+                                   c.comm, s));
+            FDB_NCCL(ncclAllGather(h->s_pdist.p + cnt * rank, h->s_pdist.p, cnt, ncclFloat,
+                                   c.comm, s));
+            FDB_NCCL(ncclGroupEnd());
+        }
         tm.mark();
         h->s_stat.ensure(3);
         FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 24, s));

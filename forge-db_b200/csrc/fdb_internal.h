@@ -283,7 +283,7 @@ struct fdb_ivfpq {
     float tc_colmax = 0.0f;             // upper bound of ||rhat||^2
     std::mutex mu;
     // per-call scratch
-    fdb::DevBuf<float> s_q, s_coarse, s_qT;
+    fdb::DevBuf<float> s_q, s_coarse, s_qT, s_pdist;
     fdb::DevBuf<uint32_t> s_probe;
     fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids, s_approx;
     fdb::DevBuf<float> s_dists;

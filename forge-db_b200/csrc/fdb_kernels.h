@@ -60,8 +60,10 @@ struct RescoreParams {
 // ivfpq_kernels.cu
 void launch_coarse_dist(cudaStream_t s, const float* Q, int nq, int dim, const float* cents,
                         int nlist, float* D);
+// probes[q][j] = the j-th nearest list of query q (ascending (distance, list));
+// pdist (nullable) receives the distances.
 void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
-                   uint32_t* probes);
+                   uint32_t* probes, float* pdist = nullptr);
 // Register-tiled coarse distances (bit-identical to launch_coarse_dist) for
 // dim <= 256 from transposed, zero-padded operands: QT [dim][nq_pad] with
 // nq_pad a multiple of 32, CT [dim][nlist_pad] with nlist_pad a multiple of 128.

@@ -580,7 +580,7 @@ __global__ void seg_offsets_kernel(const uint32_t* __restrict__ keys, unsigned n
 __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
                                int nlist, int take, const uint32_t* __restrict__ probes,
                                const float* __restrict__ Q, const float* __restrict__ cents,
-                               int dim, int dpad, const float* __restrict__ coarse, int sb,
+                               int dim, int dpad, const float* __restrict__ pdist, int sb,
                                __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
                                float* __restrict__ pair_rn, float* __restrict__ pair_s2,
                                uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
@@ -636,7 +636,7 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
     }
     if (lane == 0) {
         pair_q[i] = q;
-        pair_rn[i] = coarse[(size_t)q * nlist + l];
+        pair_rn[i] = pdist[v];  // the exact coarse distance of this probe
         pair_s2[i] = bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
         if (bad) qbad[q] = 1u;
         inv[v] = (uint32_t)i;  // where probe v = q * take + j sits among the sorted pairs
@@ -784,14 +784,20 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     select_kernel(const uint64_t* __restrict__ part, const uint64_t* __restrict__ cand,
                   const unsigned* __restrict__ cnt, int cap, int nq,
-                  uint64_t* __restrict__ out) {
+                  const float* __restrict__ tau, uint64_t* __restrict__ out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * 8 + warp;
     if (q >= nq) return;
     WarpTopK<2> tk;
     tk.init(LIST_K, nullptr);
-    tk.L[0] = part[(size_t)q * LIST_K + lane];  // already sorted
-    tk.L[1] = part[(size_t)q * LIST_K + 32 + lane];
+    // the pass-1 list, ascending; on a sharded index entries above the
+    // exchanged threshold cannot be in the answer and are dropped
+    const float t = tau[q];
+    uint64_t a0 = part[(size_t)q * LIST_K + lane], a1 = part[(size_t)q * LIST_K + 32 + lane];
+    if (a0 != KEY_NONE && key_dist(a0) > t) a0 = KEY_NONE;
+    if (a1 != KEY_NONE && key_dist(a1) > t) a1 = KEY_NONE;
+    tk.L[0] = a0;
+    tk.L[1] = a1;
     tk.thr = __shfl_sync(0xffffffffu, tk.L[1], 31);
     tk.ingest(cand + (size_t)q * cap, (int)min(cnt[q], (unsigned)cap));
     tk.store(out + (size_t)q * LIST_K);
@@ -819,7 +825,7 @@ struct CertParams {
     const unsigned* cand_cnt;
     int cap;
     const float* tau;
-    const float* coarse;        // [nq][nlist]
+    const float* pdist;         // [nq][take] exact coarse distances of the probes
     const uint32_t* probes;     // [nq][take]
     int take;
     const uint64_t* lbeg;
@@ -940,7 +946,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
         if (r.lend[l] <= r.lbeg[l]) return true;
         if (isinf(B)) return true;  // every code of the list is in the shortlist
         const double rh = (double)r.rh[l];
-        const double D = (double)r.coarse[(size_t)q * r.nlist + l];
+        const double D = (double)r.pdist[(size_t)q * r.take + j];
         const double R = sqrt(D) * (1.0 + 1.52587890625e-5);
         const double El = C1 * R * rh + C2 * (R * R + rh * rh) + 1e-30;
         const double Rl = sqrt(D) * (1.0 - 1.52587890625e-5) - rh;
@@ -1185,9 +1191,9 @@ void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
 namespace {
 
 // One chunk of queries [q0, q0 + nq) through the whole tensor path.  probes
-// and coarse point at the chunk's rows; flag entries are global query ids.
+// and pdist point at the chunk's rows; flag entries are global query ids.
 void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
-              const uint32_t* probes, const float* coarse, const uint64_t* lbeg,
+              const uint32_t* probes, const float* pdist, const uint64_t* lbeg,
               const uint64_t* lend, uint64_t* out_keys, uint32_t* flags, uint32_t qbase,
               unsigned long long* stat, int* err, uint32_t* fail_probes, uint32_t* fail_cnt,
               cudaEvent_t ev0, cudaEvent_t ev1) {
@@ -1233,7 +1239,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_CUDA(cudaMemsetAsync(h->t_qbad.p, 0, nq * 4, s));
     FDB_CUDA(cudaMemsetAsync(h->t_inv.p, 0xff, np * 4, s));
     build_a_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
-        svals, h->t_off.p, nlist, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad, coarse,
+        svals, h->t_off.p, nlist, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad, pdist,
         h->tc_sb, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_qbad.p, h->t_inv.p);
     FDB_LAUNCH_CHECK();
     plen_kernel<<<(unsigned)((np + 1 + 255) / 256), 256, 0, s>>>(
@@ -1304,7 +1310,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->s_approx.ensure(nq * LIST_K);
     select_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(h->t_part.p, h->t_cand.p,
                                                            h->t_cand_cnt.p, cap, (int)nq,
-                                                           h->s_approx.p);
+                                                           h->t_tau.p, h->s_approx.p);
     FDB_LAUNCH_CHECK();
     CertParams r{};
     r.Q = dQ;
@@ -1324,7 +1330,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.cand_cnt = h->t_cand_cnt.p;
     r.cap = cap;
     r.tau = h->t_tau.p;
-    r.coarse = coarse;
+    r.pdist = pdist;
     r.probes = probes;
     r.take = (int)take;
     r.lbeg = lbeg;
@@ -1358,7 +1364,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 }  // namespace
 
 // Tensor-core shortlist + exact rescoring of nq queries whose probes and
-// coarse distances are in h->s_probe / h->s_coarse.  Writes [nq][k] exact keys
+// their coarse distances are in h->s_probe / h->s_pdist.  Writes [nq][k] exact keys
 // and lists uncertified queries in flags (flags[0] = count, then indices);
 // returns that count.  For each listed query, t_fprobes / t_fcnt name the
 // lists to re-scan exactly and its out_keys row holds the seed (the exact
@@ -1394,7 +1400,7 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     for (size_t q0 = 0, ci = 0; q0 < nq; q0 += chunk, ++ci) {
         const size_t nc = std::min(chunk, nq - q0);
         tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,
-                 h->s_coarse.p + q0 * h->nlist, lbeg, lend, out_keys + q0 * k, flags,
+                 h->s_pdist.p + q0 * take, lbeg, lend, out_keys + q0 * k, flags,
                  (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p,
                  pass_ms ? evs[2 * ci] : nullptr, pass_ms ? evs[2 * ci + 1] : nullptr);
     }

@@ -216,7 +216,7 @@ constexpr int SEL_WARPS = 8;
 template <int P>
 __global__ void __launch_bounds__(SEL_WARPS * 32)
     select_kernel(const float* __restrict__ D, int nq, int nlist, int take,
-                  uint32_t* __restrict__ probes) {
+                  uint32_t* __restrict__ probes, float* __restrict__ pdist) {
     __shared__ uint64_t buf[SEL_WARPS * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * SEL_WARPS + warp;
@@ -234,14 +234,18 @@ __global__ void __launch_bounds__(SEL_WARPS * 32)
 #pragma unroll
     for (int e = 0; e < P; ++e) {
         int i = e * 32 + lane;
-        if (i < take) probes[(size_t)q * take + i] = key_tag(tk.L[e]);
+        if (i < take) {
+            probes[(size_t)q * take + i] = key_tag(tk.L[e]);
+            if (pdist) pdist[(size_t)q * take + i] = key_dist(tk.L[e]);
+        }
     }
 }
 
 // More than FDB_MAX_K probes: one block per query sorts all (distance, list)
 // keys with a bitonic network in shared memory.
 __global__ void select_sort_kernel(const float* __restrict__ D, int nq, int nlist, int npow2,
-                                   int take, uint32_t* __restrict__ probes) {
+                                   int take, uint32_t* __restrict__ probes,
+                                   float* __restrict__ pdist) {
     extern __shared__ uint64_t keys[];
     const int q = blockIdx.x;
     for (int i = threadIdx.x; i < npow2; i += blockDim.x)
@@ -260,18 +264,20 @@ __global__ void select_sort_kernel(const float* __restrict__ D, int nq, int nlis
             __syncthreads();
         }
     }
-    for (int i = threadIdx.x; i < take; i += blockDim.x)
+    for (int i = threadIdx.x; i < take; i += blockDim.x) {
         probes[(size_t)q * take + i] = key_tag(keys[i]);
+        if (pdist) pdist[(size_t)q * take + i] = key_dist(keys[i]);
+    }
 }
 
 void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
-                   uint32_t* probes) {
+                   uint32_t* probes, float* pdist) {
     if (nq == 0 || take == 0) return;
     unsigned grid = (nq + SEL_WARPS - 1) / SEL_WARPS;
-    if (take <= 32) select_kernel<1><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes);
-    else if (take <= 64) select_kernel<2><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes);
-    else if (take <= 128) select_kernel<4><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes);
-    else if (take <= 256) select_kernel<8><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes);
+    if (take <= 32) select_kernel<1><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes, pdist);
+    else if (take <= 64) select_kernel<2><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes, pdist);
+    else if (take <= 128) select_kernel<4><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes, pdist);
+    else if (take <= 256) select_kernel<8><<<grid, SEL_WARPS * 32, 0, s>>>(D, nq, nlist, take, probes, pdist);
     else {
         int npow2 = 1;
         while (npow2 < nlist) npow2 <<= 1;
@@ -281,7 +287,7 @@ void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
         if (smem > 48 * 1024)
             FDB_CUDA(cudaFuncSetAttribute(select_sort_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        select_sort_kernel<<<nq, 512, smem, s>>>(D, nq, nlist, npow2, take, probes);
+        select_sort_kernel<<<nq, 512, smem, s>>>(D, nq, nlist, npow2, take, probes, pdist);
     }
     FDB_LAUNCH_CHECK();
 }
