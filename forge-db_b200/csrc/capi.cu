@@ -523,14 +523,15 @@ int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode) {
 size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h) {
     return h ? h->nprobe.load(std::memory_order_relaxed) : 0;
 }
-size_t fdb_ivfpq_len(const fdb_ivfpq* h) { return h ? h->n_local : 0; }
+size_t fdb_ivfpq_len(const fdb_ivfpq* h) { return h ? ivfpq_live_len(h) : 0; }
 size_t fdb_ivfpq_n_partitions(const fdb_ivfpq* h) { return h ? h->nlist : 0; }
 size_t fdb_ivfpq_dim(const fdb_ivfpq* h) { return h ? h->dim : 0; }
 size_t fdb_ivfpq_n_subvectors(const fdb_ivfpq* h) { return h ? h->m : 0; }
 
 static void ivfpq_host_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k, int order,
                               size_t take, uint64_t* ids, float* dists, uint32_t* counts,
-                              fdb_stats* stats) {
+                              fdb_stats* stats, const uint32_t* skip = nullptr,
+                              size_t fetch_mult = 1) {
     cudaStream_t s = h->ctx->c.stream;
     const size_t per = nq * k;
     h->s_q.ensure(nq * h->dim);
@@ -539,7 +540,7 @@ static void ivfpq_host_search(fdb_ivfpq* h, const float* queries, size_t nq, siz
     h->s_counts.ensure(nq);
     FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
     ivfpq_search_dev(h, h->s_q.p, nq, k, order, take, h->s_out_ids.p, h->s_dists.p,
-                     h->s_counts.p, stats);
+                     h->s_counts.p, stats, skip, fetch_mult);
     if (k == 0) {
         if (counts) std::fill(counts, counts + nq, 0u);
         FDB_CUDA(cudaStreamSynchronize(s));
@@ -752,6 +753,222 @@ int fdb_bf_free(fdb_bf* h) {
         DeviceGuard g(h->ctx->c.device);
         delete h;
     });
+}
+
+// ---------------------------------------------------------------------------
+// IVF-PQ: re-ranking, filters, updates
+// ---------------------------------------------------------------------------
+int fdb_ivfpq_enable_reranking(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                               size_t dim, size_t rerank_factor) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (n == 0 || (x && ids)), FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_REQUIRE(n == 0 || dim == h->dim, FDB_ERR_DIM_MISMATCH, "vector dimension mismatch");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        ivfpq_enable_reranking(h, x, ids, n, rerank_factor);
+    });
+}
+
+static void filtered_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                            const uint64_t* allowed, size_t na, uint64_t* ids, float* dists,
+                            uint32_t* counts) {
+    // search_filtered: no matching id -> no results (ivf_pq.rs:701-704)
+    if (na == 0 || k == 0) {
+        for (size_t i = 0; i < nq * k; ++i) {
+            ids[i] = ~0ull;
+            dists[i] = INFINITY;
+        }
+        if (counts) std::fill(counts, counts + nq, 0u);
+        return;
+    }
+    // nprobe.min(nlist) lists (:717-723), single-query ADC order
+    const size_t take = std::min(h->nprobe.load(std::memory_order_relaxed), h->nlist);
+    ivfpq_sync_state(h);
+    const uint32_t* skip = ivfpq_filter_bitmap(h, allowed, na);
+    ivfpq_host_search(h, queries, nq, k, ORDER_FAST4, take, ids, dists, counts, nullptr, skip,
+                      4);
+}
+
+int fdb_ivfpq_search_filtered(fdb_ivfpq* h, const float* query, size_t k,
+                              const uint64_t* allowed_ids, size_t n_allowed, uint64_t* ids,
+                              float* dists, size_t* n_out) {
+    return guarded([&] {
+        FDB_REQUIRE(h && query && (k == 0 || (ids && dists)) && (n_allowed == 0 || allowed_ids),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        uint32_t cnt = 0;
+        filtered_search(h, query, 1, k, allowed_ids, n_allowed, ids, dists, &cnt);
+        if (n_out) *n_out = cnt;
+    });
+}
+
+int fdb_ivfpq_batch_search_filtered(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                                    const uint64_t* allowed_ids, size_t n_allowed,
+                                    uint64_t* ids, float* dists, uint32_t* counts) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || queries) && (nq == 0 || k == 0 || (ids && dists)) &&
+                        (n_allowed == 0 || allowed_ids),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        if (nq == 0) return;
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        filtered_search(h, queries, nq, k, allowed_ids, n_allowed, ids, dists, counts);
+    });
+}
+
+int fdb_ivfpq_insert_batch(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                           size_t dim) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (n == 0 || (x && ids)), FDB_ERR_INVALID_ARG, "NULL argument");
+        if (n == 0) return;  // insert_batch of nothing is a no-op (:1732-1734)
+        FDB_REQUIRE(dim == h->dim, FDB_ERR_DIM_MISMATCH, "vector dimension mismatch");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lkc(h->ctx->c.mu);
+        std::lock_guard<std::mutex> lk(h->mu);
+        ivfpq_insert_batch(h, x, ids, n);
+    });
+}
+
+int fdb_ivfpq_delete(fdb_ivfpq* h, uint64_t id, int* deleted) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        const bool d = ivfpq_delete(h, id);
+        if (deleted) *deleted = d ? 1 : 0;
+    });
+}
+
+size_t fdb_ivfpq_num_tombstones(const fdb_ivfpq* h) { return h ? h->n_tomb : 0; }
+size_t fdb_ivfpq_len_with_tombstones(const fdb_ivfpq* h) { return h ? h->n_local : 0; }
+float fdb_ivfpq_fragmentation_ratio(const fdb_ivfpq* h) {
+    // tombstones / len(), 0 for an empty index (ivf_pq.rs:1815-1822)
+    if (!h) return 0.0f;
+    const size_t total = ivfpq_live_len(h);
+    return total == 0 ? 0.0f : (float)h->n_tomb / (float)total;
+}
+
+int fdb_ivfpq_compact(fdb_ivfpq* h) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lkc(h->ctx->c.mu);
+        std::lock_guard<std::mutex> lk(h->mu);
+        ivfpq_compact(h);
+    });
+}
+
+int fdb_ivfpq_rebuild(fdb_ivfpq* h, const fdb_train_opts* opts) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        FDB_REQUIRE(h->rerank, FDB_ERR_UNSUPPORTED,
+                    "operation not supported: rebuild requires original vectors (enable "
+                    "re-ranking)");
+        FDB_REQUIRE(!h->rr_ids.empty(), FDB_ERR_EMPTY_VECTOR_SET,
+                    "empty vector set: operation requires at least one vector");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lkc(h->ctx->c.mu);
+        std::lock_guard<std::mutex> lk(h->mu);
+        const std::vector<float> x = h->rr_x;
+        const std::vector<uint64_t> ids = h->rr_ids;
+        const size_t nprobe = h->nprobe.load(std::memory_order_relaxed);
+        const size_t factor = h->rerank_factor;
+        // IVFPQIndex::build(vectors, n_clusters, n_subvectors, metric) replaces
+        // the whole index; the result is unsharded
+        h->tomb.clear();
+        h->n_tomb = 0;
+        h->h_dead.clear();
+        h->dead.release();
+        h->dead_dirty = false;
+        h->id_index.clear();
+        h->id_index_ok = false;
+        h->sharded = false;
+        h->shard_world = 1;
+        h->shard_rank = 0;
+        h->owned.clear();
+        h->shard_be.release();
+        fdb_train_opts o{};
+        if (opts) o = *opts;
+        ivfpq_build(h, x.data(), ids.data(), ids.size(), o);
+        h->nprobe.store(std::min(nprobe, h->nlist), std::memory_order_relaxed);
+        ivfpq_enable_reranking(h, x.data(), ids.data(), ids.size(), factor);
+    });
+}
+
+int fdb_bf_remove(fdb_bf* h, uint64_t id, int* removed) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        // VectorStore::find_id + swap_remove (vector.rs:256-276)
+        auto it = std::find(h->h_ids.begin(), h->h_ids.end(), id);
+        if (removed) *removed = it != h->h_ids.end() ? 1 : 0;
+        if (it == h->h_ids.end()) return;
+        const size_t i = (size_t)(it - h->h_ids.begin()), last = h->h_ids.size() - 1;
+        h->h_ids[i] = h->h_ids[last];
+        h->h_ids.pop_back();
+        if (i != last)
+            std::copy(h->h_x.begin() + last * h->dim, h->h_x.begin() + (last + 1) * h->dim,
+                      h->h_x.begin() + i * h->dim);
+        h->h_x.resize(last * h->dim);
+        h->row0 = 0;
+        h->n = h->h_ids.size();
+        h->sharded = false;
+        h->shard_world = 1;
+        h->dirty = true;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// .fdb files
+// ---------------------------------------------------------------------------
+int fdb_ivfpq_save(fdb_ivfpq* h, const char* path) {
+    return guarded([&] {
+        FDB_REQUIRE(h && path, FDB_ERR_INVALID_ARG, "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        ivfpq_save(h, path);
+    });
+}
+
+int fdb_ivfpq_load(fdb_ctx* ctx, const char* path, fdb_ivfpq** out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && path && out, FDB_ERR_INVALID_ARG, "NULL argument");
+        DeviceGuard g(ctx->c.device);
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        std::unique_ptr<fdb_ivfpq> h(new fdb_ivfpq());
+        h->ctx = ctx;
+        ivfpq_load_file(h.get(), path);
+        *out = h.release();
+    });
+}
+
+int fdb_bf_save(fdb_bf* h, const char* path) {
+    return guarded([&] {
+        FDB_REQUIRE(h && path, FDB_ERR_INVALID_ARG, "NULL argument");
+        std::lock_guard<std::mutex> lk(h->mu);
+        bf_save(h, path);
+    });
+}
+
+int fdb_bf_load(fdb_ctx* ctx, const char* path, fdb_bf** out) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && path && out, FDB_ERR_INVALID_ARG, "NULL argument");
+        std::unique_ptr<fdb_bf> h(new fdb_bf());
+        h->ctx = ctx;
+        bf_load_file(h.get(), path);
+        *out = h.release();
+    });
+}
+
+int fdb_file_inspect(const char* path, fdb_file_info* info) {
+    return guarded([&] {
+        FDB_REQUIRE(path && info, FDB_ERR_INVALID_ARG, "NULL argument");
+        file_inspect(path, info);
+    });
+}
+
+uint32_t fdb_crc32(const void* data, size_t n) {
+    return crc32(static_cast<const uint8_t*>(data), n);
 }
 
 }  // extern "C"

@@ -19,7 +19,6 @@
 
 namespace fdb {
 
-static void ivfpq_prepare_tables(fdb_ivfpq* h);
 void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
                   const uint32_t* init_idx_host, float* cb, int* iters_out);
 
@@ -82,7 +81,7 @@ static void kmeans_draws(size_t n, size_t k, const uint32_t* init_idx, const flo
 // Fits k centroids on device rows x[n][dim] (KMeans::fit_raw, kmeans.rs:87-193).
 void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_iters,
                     const uint32_t* init_idx, const float* kpp_u, uint64_t seed, float* cent,
-                    int* iters_run) {
+                    int* iters_run, uint32_t* init_rows, uint8_t* ever) {
     FDB_REQUIRE(n > 0 && dim > 0, FDB_ERR_EMPTY_TRAINING_SET, "k-means needs at least one point");
     FDB_REQUIRE(k > 0, FDB_ERR_INVALID_ARG, "k must be positive");
     std::vector<uint32_t> idx;
@@ -100,12 +99,13 @@ void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_
                                  cudaMemcpyHostToDevice, ctx.stream));
         launch_gather_rows(ctx.stream, x, dim, d_idx.p, k, cent);
         FDB_CUDA(cudaStreamSynchronize(ctx.stream));
+        if (init_rows) std::copy(idx.begin(), idx.end(), init_rows);
     } else {
-        kmeans_pp_init(ctx, x, n, dim, k, idx.data(), u.data(), cent);
+        kmeans_pp_init(ctx, x, n, dim, k, idx.data(), u.data(), cent, init_rows);
     }
     KMeansProblem pb{x, n, dim, dim, 1, k, max_iters};
     int it = 0;
-    kmeans_run(ctx, pb, cent, &it);
+    kmeans_run(ctx, pb, cent, &it, ever);
     if (iters_run) *iters_run = it;
 }
 
@@ -144,9 +144,19 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
     launch_gather_rows(s, X.p, dim, d_sidx.p, ivf_n, S.p);
     h->cents.alloc((size_t)nlist * dim);
     int it = 0;
+    std::vector<uint32_t> init_rows(nlist);
+    std::vector<uint8_t> ever(std::max<size_t>((size_t)nlist, (size_t)m * KSUB));
     kmeans_fit_dev(c, S.p, ivf_n, dim, nlist, ivf_iters, o.ivf_init_idx, o.ivf_kpp_u,
-                   o.seed + 1, h->cents.p, &it);
+                   o.seed + 1, h->cents.p, &it, init_rows.data(), ever.data());
     S.release();
+    // Vector ids of the centroids as the reference stores them: a centroid
+    // starts as a clone of a training vector (its id) and becomes
+    // Vector::new(c, mean) once its cluster has members (kmeans.rs:52-61, 183).
+    h->cent_ids.resize(nlist);
+    for (int l = 0; l < nlist; ++l) {
+        const uint32_t row = sidx[init_rows[l]];
+        h->cent_ids[l] = ever[l] ? (uint64_t)l : (ids_host ? ids_host[row] : (uint64_t)row);
+    }
 
     // 2. Assign all vectors; stable grouping keeps input order inside lists.
     DevBuf<uint32_t> assign(n), perm(n), slot(n);
@@ -178,8 +188,13 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
     const int sub = dim / m;
     h->cb.alloc((size_t)m * KSUB * sub);
     std::vector<int> pq_its(m);
-    pq_train_dev(c, R.p, pq_n, dim, m, pq_iters, pinit.data(), h->cb.p, pq_its.data());
+    pq_train_dev(c, R.p, pq_n, dim, m, pq_iters, pinit.data(), h->cb.p, pq_its.data(),
+                 ever.data());
     R.release();
+    // codebook entries: fit_raw names a pick by its sample row (kmeans.rs:103)
+    h->cb_ids.resize((size_t)m * KSUB);
+    for (size_t e = 0; e < (size_t)m * KSUB; ++e)
+        h->cb_ids[e] = ever[e] ? (uint64_t)(e % KSUB) : (uint64_t)pinit[e];
 
     // 4. Encode every residual into its list slot; ids in list order.
     h->codes.alloc(n * m);
@@ -195,6 +210,8 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
     h->h_offs_full.resize(nlist + 1);
     FDB_CUDA(cudaMemcpyAsync(h->h_offs_full.data(), h->offs.p, (nlist + 1) * 8,
                              cudaMemcpyDeviceToHost, s));
+    h->h_ids.resize(n);
+    FDB_CUDA(cudaMemcpyAsync(h->h_ids.data(), h->ids.p, n * 8, cudaMemcpyDeviceToHost, s));
     FDB_CUDA(cudaStreamSynchronize(s));
     h->h_offs = h->h_offs_full;
     h->n_total = h->n_local = n;
@@ -205,7 +222,7 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
 // ||c_ls||, bmax_s = max_j ||b_sj|| (rounded up); the table mode also the
 // per-list table btab (subvectors of 8+ floats only), the tensor mode the
 // decoded codes (ivf_tc_prepare).
-static void ivfpq_prepare_tables(fdb_ivfpq* h) {
+void ivfpq_prepare_tables(fdb_ivfpq* h) {
     const size_t nlist = h->nlist, dim = h->dim, m = h->m, sub = dim / m;
     h->btab.release();
     h->cmax.release();
@@ -287,7 +304,17 @@ void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_
     FDB_CUDA(cudaStreamSynchronize(s));
     h->h_offs_full.assign(offsets, offsets + nlist + 1);
     h->h_offs = h->h_offs_full;
+    h->h_ids.assign(ids, ids + n);
     h->n_total = h->n_local = n;
+    // ids the reference's trained Vectors would carry after a full fit
+    if (h->cent_ids.size() != nlist) {
+        h->cent_ids.resize(nlist);
+        std::iota(h->cent_ids.begin(), h->cent_ids.end(), (uint64_t)0);
+    }
+    if (h->cb_ids.size() != m * KSUB) {
+        h->cb_ids.resize(m * KSUB);
+        for (size_t e = 0; e < m * KSUB; ++e) h->cb_ids[e] = e % KSUB;
+    }
     ivfpq_prepare_tables(h);
 }
 
@@ -320,10 +347,12 @@ void ivfpq_shard(fdb_ivfpq* h, int rank, int world) {
     // those of the unsharded index, so results do not depend on `world`.
     std::vector<uint64_t> be(2 * nlist);
     size_t held = 0;
+    h->owned.assign(nlist, 0);
     for (size_t l = 0; l < nlist; ++l) {
         be[l] = h->h_offs_full[l];
         be[nlist + l] = owner[l] == rank ? h->h_offs_full[l + 1] : h->h_offs_full[l];
         if (owner[l] == rank) held += sizes[l];
+        h->owned[l] = owner[l] == rank;
     }
     Ctx& c = h->ctx->c;
     h->shard_be.alloc(2 * nlist);
@@ -368,14 +397,21 @@ static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_k
                            merged_ids.p);
 }
 
-void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
-                      uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st) {
+void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, int order,
+                      size_t take, uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                      fdb_stats* st, const uint32_t* call_skip, size_t fetch_mult) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     const int nlist = (int)h->nlist;
     if (st) std::memset(st, 0, sizeof(*st));
     if (nq == 0) return;
-    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED, "k above FDB_MAX_K");
+    ivfpq_sync_state(h);
+    // fetch_k: with re-ranking, k * rerank_factor PQ candidates (ivf_pq.rs:591-596)
+    const size_t k = h->rerank ? k_out * h->rerank_factor * fetch_mult : k_out;
+    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED,
+                h->rerank ? "k * rerank_factor above FDB_MAX_K" : "k above FDB_MAX_K");
+    // rows the scan skips: this call's filter, else the tombstoned rows
+    const uint32_t* skip = call_skip ? call_skip : (h->n_tomb ? h->dead.p : nullptr);
     FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
                 "sharded index needs a communicator of the same size");
     const size_t per = nq * k;
@@ -430,7 +466,9 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         const uint64_t* lend = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
         // Tensor mode: lists scored on the tensor cores into a shortlist,
         // exact rescoring + certification; failures are re-scanned exactly.
-        const bool tensor = ivf_tc_eligible(h, k) &&
+        // (a per-call filter goes through the table or exact scan; tombstoned
+        // rows are +inf in the tensor scan's ||rhat||^2)
+        const bool tensor = ivf_tc_eligible(h, k) && !call_skip &&
                             (h->scan_mode == FDB_SCAN_TENSOR ||
                              (h->scan_mode == FDB_SCAN_AUTO && nq >= 256));
         // Table mode: approximate scan into a shortlist of kp keys, then
@@ -454,6 +492,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         a.out_keys = tables ? h->s_approx.p : h->s_keys.p;
         a.stat = h->s_stat.p;
         a.btab = tables ? h->btab.p : nullptr;
+        a.skip = skip;
         if (tensor) {
             h->s_flags.ensure(nq + 1);
             double pass_ms = 0.0;
@@ -518,7 +557,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
         keys = h->s_merged.p;
         ids = h->s_merged_ids.p;
     }
-    launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
+    if (h->rerank) launch_rerank(h, keys, ids, nq, k, dQ, k_out, d_ids, d_dists, d_counts);
+    else launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
     tm.mark();
     if (st) {
         unsigned long long hs[3] = {0, 0, 0};

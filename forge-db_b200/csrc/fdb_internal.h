@@ -12,6 +12,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "forgegpu.h"
@@ -165,11 +167,16 @@ struct KMeansProblem {
     int max_iters;
 };
 // cent: device [nsub][k][dim] initial centroids, updated in place.
-// iters_out: host [nsub].
-void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out);
-// k-means++ initialisation of one problem (nsub == 1, k <= 64).
+// iters_out: host [nsub].  ever_out (host [nsub][k], nullable): 1 where the
+// cluster had points in some iteration, i.e. where the reference's centroid
+// was rebuilt as Vector::new(k, mean) and so carries id k (kmeans.rs:183).
+void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out,
+                uint8_t* ever_out = nullptr);
+// k-means++ initialisation of one problem (nsub == 1, k <= 64); picks_out
+// (host [k], nullable) receives the row chosen for each centroid.
 void kmeans_pp_init(Ctx& ctx, const float* x, size_t n, int dim, int k,
-                    const uint32_t* init_idx_host, const float* kpp_u_host, float* cent);
+                    const uint32_t* init_idx_host, const float* kpp_u_host, float* cent,
+                    uint32_t* picks_out = nullptr);
 void launch_assign(cudaStream_t s, const float* x, size_t n, int dim, int ld, const float* cent,
                    int k, uint32_t* out);
 // Stable grouping of points by assignment: perm (point ids in group order)
@@ -184,12 +191,15 @@ void launch_pq_encode(cudaStream_t s, const float* x, size_t n, int dim, const f
 void launch_lut(cudaStream_t s, const float* cb, int m, int dim, const float* q, size_t nq,
                 float* lut);
 void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
-                  const uint32_t* init_idx_host, float* cb, int* iters_out);
+                  const uint32_t* init_idx_host, float* cb, int* iters_out,
+                  uint8_t* ever_out = nullptr);
 
 // engine.cu
+// init_rows (host [k], nullable): the point each initial centroid was
+// copied from; ever (host [k], nullable): see kmeans_run.
 void kmeans_fit_dev(Ctx& ctx, const float* x, size_t n, int dim, int k, int max_iters,
                     const uint32_t* init_idx, const float* kpp_u, uint64_t seed, float* cent,
-                    int* iters_run);
+                    int* iters_run, uint32_t* init_rows = nullptr, uint8_t* ever = nullptr);
 void shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
 
 // gemm_topk.cu: the tensor-core shortlist of brute force (sample pass,
@@ -221,8 +231,32 @@ void ivfpq_build(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, si
 void ivfpq_load(fdb_ivfpq* h, const float* cents, const float* cb, const uint64_t* offsets,
                 const uint64_t* ids, const uint8_t* codes);
 void ivfpq_shard(fdb_ivfpq* h, int rank, int world);
+void ivfpq_prepare_tables(fdb_ivfpq* h);
+// mutate.cu: tombstones, insert_batch, re-ranking, filters
+void ivfpq_sync_state(fdb_ivfpq* h);  // uploads the dead bitmap / re-ranking store if changed
+void ivfpq_enable_reranking(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                            size_t factor);
+void launch_rerank(fdb_ivfpq* h, const uint64_t* keys, const uint64_t* cand_ids, size_t nq,
+                   size_t fetch, const float* dQ, size_t k, uint64_t* d_ids, float* d_dists,
+                   uint32_t* d_counts);
+bool ivfpq_delete(fdb_ivfpq* h, uint64_t id);
+size_t ivfpq_live_len(const fdb_ivfpq* h);
+void ivfpq_compact(fdb_ivfpq* h);
+void ivfpq_insert_batch(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, size_t n);
+const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed_host, size_t na);
+// persist.cu: .fdb files
+uint32_t crc32(const uint8_t* p, size_t n);
+void ivfpq_save(fdb_ivfpq* h, const char* path);
+void ivfpq_load_file(fdb_ivfpq* h, const char* path);
+void bf_save(fdb_bf* h, const char* path);
+void bf_load_file(fdb_bf* h, const char* path);
+void file_inspect(const char* path, fdb_file_info* info);
+// call_skip (nullable): rows this call skips, dead rows included (a filter);
+// fetch_mult: candidates per result before re-ranking, on top of
+// rerank_factor (4 for search_filtered).
 void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
-                      uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st);
+                      uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st,
+                      const uint32_t* call_skip = nullptr, size_t fetch_mult = 1);
 // ivf_tc.cu: tensor-core list scan (see there)
 bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k);
 void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
@@ -264,6 +298,7 @@ struct fdb_ivfpq {
     bool sharded = false;
     int shard_world = 1, shard_rank = 0;
     fdb::DevBuf<uint64_t> shard_be;     // [2][nlist] list begin / end when sharded
+    std::vector<uint8_t> owned;         // [nlist] lists held here (sharded)
     // table mode (subvectors of 8+ floats): per-list tables and error-bound terms
     int scan_mode = FDB_SCAN_AUTO;
     fdb::DevBuf<float> centsT;          // [dim][nlist_pad] for the tiled coarse kernel
@@ -281,6 +316,32 @@ struct fdb_ivfpq {
     size_t tc_rows = 0;                 // rows of the padded layout
     size_t tc_maxpad = 0;               // longest padded list
     float tc_colmax = 0.0f;             // upper bound of ||rhat||^2
+    // Vector ids the reference keeps on centroids and codebook entries; no
+    // role in search, carried so .fdb files round-trip unchanged
+    std::vector<uint64_t> cent_ids;     // [nlist]
+    std::vector<uint64_t> cb_ids;       // [m*256]
+    // re-ranking store (enable_reranking, ivf_pq.rs:513-517): original
+    // vectors by id; host copy in slot order, device copy rebuilt when dirty
+    bool rerank = false;
+    size_t rerank_factor = 1;
+    std::vector<uint64_t> rr_ids;       // [slots]
+    std::vector<float> rr_x;            // [slots][dim]
+    std::unordered_map<uint64_t, size_t> rr_slot;
+    bool rr_dirty = false;
+    fdb::DevBuf<uint64_t> rr_sorted;    // ids ascending
+    fdb::DevBuf<uint32_t> rr_sorted_slot;
+    fdb::DevBuf<float> rr_dev;          // [slots][dim]
+    // tombstones (delete, ivf_pq.rs:1786-1805): per list, the deleted ids;
+    // `dead` marks every row of the list-major layout they hide
+    std::vector<std::unordered_set<uint64_t>> tomb;  // [nlist] (empty: none)
+    size_t n_tomb = 0;                  // sum of the per-list set sizes
+    std::vector<uint64_t> h_ids;        // host mirror of ids (list-major)
+    std::vector<uint32_t> h_dead;       // host dead bitmap (empty: no tombstones)
+    fdb::DevBuf<uint32_t> dead;         // device copy, uploaded when dead_dirty
+    bool dead_dirty = false;
+    std::vector<std::pair<uint64_t, uint32_t>> id_index;  // (id, row) ascending, lazy
+    bool id_index_ok = false;
+    fdb::DevBuf<uint32_t> f_skip;       // per-call filter bitmap (search_filtered)
     std::mutex mu;
     // per-call scratch
     fdb::DevBuf<float> s_q, s_coarse, s_qT, s_pdist;

@@ -35,6 +35,8 @@ struct ScanParams {
     bool seed;
     // with qidx: block i writes its k keys to out_keys[i] instead of out_keys[qidx[i]]
     bool out_by_block;
+    // nullable bitmap over rows: set bits are skipped (tombstones, filters)
+    const uint32_t* skip;
 };
 
 struct RescoreParams {

@@ -395,7 +395,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 const int j = g8 * 8 + jj;
                                 const float d =
                                     __fmaf_rn(s2, __uint_as_float(v[j]), __fadd_rn(rn, cv[jj]));
-                                if (rok && j < nvalid && d <= tau) {
+                                // (+inf: a tombstoned row, never admitted)
+                                if (rok && j < nvalid && d <= tau && d < INF) {
                                     const unsigned ix = atomicAdd(p.cand_cnt + q, 1u);
                                     if (ix < (unsigned)p.cap)
                                         p.cand[(size_t)q * p.cap + ix] = make_key(d, tag0 + j);
@@ -767,7 +768,9 @@ __global__ void __launch_bounds__(256)
             bool any = false;
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-                key[x] = j + x < nb ? make_key(d[x], tag0 + (uint32_t)(j + x)) : KEY_NONE;
+                // +inf marks a tombstoned row
+                key[x] = (j + x < nb && d[x] < INF) ? make_key(d[x], tag0 + (uint32_t)(j + x))
+                                                    : KEY_NONE;
                 any |= key[x] < tk.thr;
             }
             if (!__any_sync(0xffffffffu, any)) continue;

@@ -460,7 +460,12 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
             const uint32_t tag0 = (uint32_t)beg;
             for (uint32_t b = (uint32_t)warp * 64u; b < len; b += SCAN_WARPS * 64u) {
                 const uint32_t i0 = b + lane, i1 = i0 + 32u;
-                const bool v0 = i0 < len, v1 = i1 < len;
+                bool v0 = i0 < len, v1 = i1 < len;
+                if (a.skip) {
+                    const uint32_t r0 = tag0 + i0, r1 = tag0 + i1;
+                    v0 = v0 && !((__ldg(a.skip + (r0 >> 5)) >> (r0 & 31)) & 1u);
+                    v1 = v1 && !((__ldg(a.skip + (r1 >> 5)) >> (r1 & 31)) & 1u);
+                }
                 const float d0 = adc_code<ORDER, MB>(lut, lc + (size_t)(v0 ? i0 : 0u) * m, m);
                 const float d1 = adc_code<ORDER, MB>(lut, lc + (size_t)(v1 ? i1 : 0u) * m, m);
                 tk.add(make_key(d0, tag0 + i0), v0);

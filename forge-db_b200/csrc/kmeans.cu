@@ -400,7 +400,16 @@ __global__ void change_sum_kernel(const float* __restrict__ dc, int nsub, int k,
     change[s] = __fdiv_rn(total, (float)k);
 }
 
-void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out) {
+// ever[g] |= group g is non-empty, for the problems still iterating.
+__global__ void nonempty_kernel(const uint64_t* __restrict__ offs, int nsub, int k,
+                                const int* __restrict__ active, uint8_t* __restrict__ ever) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= nsub * k || !active[g / k]) return;
+    if (offs[g + 1] > offs[g]) ever[g] = 1;
+}
+
+void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out,
+                uint8_t* ever_out) {
     cudaStream_t s = ctx.stream;
     const size_t n = pb.n;
     const int nsub = pb.nsub, k = pb.k, dim = pb.dim;
@@ -409,6 +418,11 @@ void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out) 
     DevBuf<uint32_t> assign(n * nsub), perm(n * nsub);
     DevBuf<uint64_t> offs((size_t)nsub * k + 1);
     DevBuf<int> d_active(nsub);
+    DevBuf<uint8_t> ever;
+    if (ever_out) {
+        ever.alloc((size_t)nsub * k);
+        FDB_CUDA(cudaMemsetAsync(ever.p, 0, ever.bytes(), s));
+    }
     std::vector<int> active(nsub, 1);
     std::vector<float> h_change(nsub);
     for (int q = 0; q < nsub; ++q) iters_out[q] = 0;
@@ -426,6 +440,11 @@ void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out) 
         if (tiled) at.run(s, n, dim, cent, k, assign.p);
         else launch_assign_multi(s, pb.x, n, dim, pb.ld, nsub, cent, k, assign.p, d_active.p);
         group_multi(s, assign.p, n, nsub, k, perm.p, offs.p);
+        if (ever_out) {
+            nonempty_kernel<<<(nsub * k + 255) / 256, 256, 0, s>>>(offs.p, nsub, k, d_active.p,
+                                                                   ever.p);
+            FDB_LAUNCH_CHECK();
+        }
         unsigned g = (unsigned)((csz + 255) / 256);
         update_kernel<<<g, 256, 0, s>>>(pb.x, n, dim, pb.ld, nsub, k, perm.p, offs.p, cent, neu.p,
                                         d_active.p);
@@ -444,6 +463,10 @@ void kmeans_run(Ctx& ctx, const KMeansProblem& pb, float* cent, int* iters_out) 
             iters_out[q]++;
             if (h_change[q] < CONVERGENCE_THRESHOLD) active[q] = 0;
         }
+    }
+    if (ever_out) {
+        FDB_CUDA(cudaMemcpyAsync(ever_out, ever.p, ever.bytes(), cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
     }
 }
 
@@ -466,7 +489,7 @@ __global__ void kpp_update_kernel(const float* __restrict__ x, size_t n, int dim
 // Sequential total and subtract-walk, exactly as the reference: one thread.
 __global__ void kpp_pick_kernel(const float* __restrict__ mind, size_t n, float u,
                                 uint32_t fallback, const float* __restrict__ x, int dim,
-                                float* __restrict__ out_row) {
+                                float* __restrict__ out_row, uint32_t* __restrict__ pick_out) {
     __shared__ uint32_t sel;
     if (threadIdx.x == 0) {
         float total = 0.0f;
@@ -483,18 +506,21 @@ __global__ void kpp_pick_kernel(const float* __restrict__ mind, size_t n, float 
             }
         }
         sel = pick;
+        *pick_out = pick;
     }
     __syncthreads();
     for (int j = threadIdx.x; j < dim; j += blockDim.x) out_row[j] = x[(size_t)sel * dim + j];
 }
 
 void kmeans_pp_init(Ctx& ctx, const float* x, size_t n, int dim, int k,
-                    const uint32_t* init_idx, const float* kpp_u, float* cent) {
+                    const uint32_t* init_idx, const float* kpp_u, float* cent,
+                    uint32_t* picks_out) {
     cudaStream_t s = ctx.stream;
     FDB_REQUIRE(init_idx[0] < n, FDB_ERR_INVALID_ARG, "k-means++ first pick out of range");
     FDB_CUDA(cudaMemcpyAsync(cent, x + (size_t)init_idx[0] * dim, dim * sizeof(float),
                              cudaMemcpyDeviceToDevice, s));
     DevBuf<float> mind(n);
+    DevBuf<uint32_t> picks((size_t)k);
     fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mind.p, n, FLT_MAX);
     FDB_LAUNCH_CHECK();
     for (int c = 1; c < k; ++c) {
@@ -503,8 +529,14 @@ void kmeans_pp_init(Ctx& ctx, const float* x, size_t n, int dim, int k,
             x, n, dim, cent + (size_t)(c - 1) * dim, mind.p);
         FDB_LAUNCH_CHECK();
         kpp_pick_kernel<<<1, 128, 0, s>>>(mind.p, n, kpp_u[c], init_idx[c], x, dim,
-                                          cent + (size_t)c * dim);
+                                          cent + (size_t)c * dim, picks.p + c);
         FDB_LAUNCH_CHECK();
+    }
+    if (picks_out) {
+        picks_out[0] = init_idx[0];
+        if (k > 1)
+            FDB_CUDA(cudaMemcpyAsync(picks_out + 1, picks.p + 1, (size_t)(k - 1) * 4,
+                                     cudaMemcpyDeviceToHost, s));
     }
     FDB_CUDA(cudaStreamSynchronize(s));
 }

@@ -1,0 +1,456 @@
+// mutate.cu -- the IVF-PQ index's state around the scan: tombstones (delete,
+// compact), insert_batch, the re-ranking store with its device re-scoring,
+// and the per-call row filter of search_filtered.
+//
+// Layout rules kept by every change here: lists stay contiguous and in list
+// order, a list's rows keep their order (new rows go to its end, compaction
+// keeps the survivors' order), and the row position stays the tie-break tag.
+// Every change rebuilds the derived tables (ivfpq_prepare_tables) so all scan
+// modes see the same rows.
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+
+#include "fdb_device.cuh"
+#include "fdb_internal.h"
+#include "fdb_kernels.h"
+
+namespace fdb {
+
+static unsigned grid_for(size_t n, unsigned threads = 256) {
+    return (unsigned)std::max<size_t>(1, (n + threads - 1) / threads);
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+// One block per list: the tensor scan's ||rhat||^2 of every dead row becomes
+// +inf, so its score is +inf and it is never admitted or selected.
+__global__ void mask_dead_kernel(const uint32_t* __restrict__ dead,
+                                 const uint64_t* __restrict__ offs,
+                                 const uint32_t* __restrict__ pstart, float* __restrict__ dnorm) {
+    const int l = blockIdx.x;
+    const uint64_t b = offs[l], e = offs[l + 1];
+    for (uint64_t p = b + threadIdx.x; p < e; p += blockDim.x)
+        if ((dead[p >> 5] >> (p & 31)) & 1u) dnorm[pstart[l] + (p - b)] = __int_as_float(0x7f800000);
+}
+
+// One block per list: copy its rows (ids and codes, contiguous) to the list's
+// start in the new layout.
+__global__ void relayout_kernel(const uint64_t* __restrict__ old_offs,
+                                const uint64_t* __restrict__ new_offs, int m,
+                                const uint8_t* __restrict__ codes, const uint64_t* __restrict__ ids,
+                                uint8_t* __restrict__ codes2, uint64_t* __restrict__ ids2) {
+    const int l = blockIdx.x;
+    const uint64_t b = old_offs[l], e = old_offs[l + 1], nb = new_offs[l];
+    for (uint64_t p = b + threadIdx.x; p < e; p += blockDim.x) ids2[nb + (p - b)] = ids[p];
+    const uint64_t nbytes = (e - b) * (uint64_t)m;
+    const uint8_t* src = codes + b * (uint64_t)m;
+    uint8_t* dst = codes2 + nb * (uint64_t)m;
+    for (uint64_t t = threadIdx.x; t < nbytes; t += blockDim.x) dst[t] = src[t];
+}
+
+__global__ void scatter_ids_kernel(const uint64_t* __restrict__ ids, const uint32_t* __restrict__ slot,
+                                   size_t n, uint64_t* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[slot[i]] = ids[i];
+}
+
+// Kept rows (ascending) gathered into a dense layout.
+__global__ void gather_rows_kernel(const uint32_t* __restrict__ rows, size_t nkeep, int m,
+                                   const uint8_t* __restrict__ codes,
+                                   const uint64_t* __restrict__ ids, uint8_t* __restrict__ codes2,
+                                   uint64_t* __restrict__ ids2) {
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nkeep * (size_t)m) return;
+    const size_t i = t / m, j = t % m;
+    const uint32_t r = rows[i];
+    codes2[t] = codes[(size_t)r * m + j];
+    if (j == 0) ids2[i] = ids[r];
+}
+
+// One thread per 32-row word: bit p set when row p is skipped by this call
+// (dead, or its id is not in the ascending allow list).
+__global__ void filter_bitmap_kernel(const uint64_t* __restrict__ ids, size_t n,
+                                     const uint64_t* __restrict__ allow, size_t na,
+                                     const uint32_t* __restrict__ dead, uint32_t* __restrict__ out) {
+    const size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= (n + 31) / 32) return;
+    uint32_t word = dead ? dead[w] : 0u;
+    for (int j = 0; j < 32; ++j) {
+        const size_t p = w * 32 + j;
+        if (p >= n) break;
+        if ((word >> j) & 1u) continue;
+        const uint64_t id = ids[p];
+        size_t lo = 0, hi = na;
+        while (lo < hi) {
+            const size_t mid = (lo + hi) >> 1;
+            if (allow[mid] < id) lo = mid + 1;
+            else hi = mid;
+        }
+        if (lo >= na || allow[lo] != id) word |= 1u << j;
+    }
+    out[w] = word;
+}
+
+// rerank_results (ivf_pq.rs:556-582), one block per query.  Candidate i of
+// the PQ list (ascending) that has an original vector gets sqrt(L2^2(q, v))
+// (euclidean_distance_squared in the AVX2 order, correctly rounded square
+// root); candidates without one are dropped.  A stable sort by that distance
+// is a sort by (distance, i); each candidate's rank is the number of smaller
+// keys, and the first k ranks are written.
+constexpr int RERANK_MAX = FDB_MAX_K;
+__global__ void __launch_bounds__(RERANK_MAX)
+    rerank_kernel(const uint64_t* __restrict__ keys, const uint64_t* __restrict__ cand_ids,
+                  int fetch, const float* __restrict__ Q, int dim,
+                  const uint64_t* __restrict__ rr_ids, const uint32_t* __restrict__ rr_slot,
+                  size_t nrr, const float* __restrict__ rr_x, int k, uint64_t* __restrict__ out_ids,
+                  float* __restrict__ out_d, uint32_t* __restrict__ counts) {
+    __shared__ uint64_t skey[RERANK_MAX];
+    __shared__ int npresent;
+    const size_t q = blockIdx.x;
+    const int t = threadIdx.x;
+    if (t == 0) npresent = 0;
+    uint64_t key = KEY_NONE, id = 0;
+    float d = 0.0f;
+    if (t < fetch && keys[q * fetch + t] != KEY_NONE) {
+        id = cand_ids[q * fetch + t];
+        size_t lo = 0, hi = nrr;
+        while (lo < hi) {
+            const size_t mid = (lo + hi) >> 1;
+            if (rr_ids[mid] < id) lo = mid + 1;
+            else hi = mid;
+        }
+        if (lo < nrr && rr_ids[lo] == id) {
+            d = __fsqrt_rn(l2sq_exact(Q + q * dim, rr_x + (size_t)rr_slot[lo] * dim, dim));
+            key = ((uint64_t)f2ord(d) << 32) | (uint32_t)t;
+        }
+    }
+    skey[t] = key;
+    __syncthreads();
+    if (key != KEY_NONE) {
+        atomicAdd(&npresent, 1);
+        int r = 0;
+        for (int j = 0; j < (int)blockDim.x; ++j) r += skey[j] < key;
+        if (r < k) {
+            out_ids[q * k + r] = id;
+            out_d[q * k + r] = d;
+        }
+    }
+    __syncthreads();
+    const int cnt = min(npresent, k);
+    for (int r = cnt + t; r < k; r += blockDim.x) {
+        out_ids[q * k + r] = ~0ull;
+        out_d[q * k + r] = __int_as_float(0x7f800000);
+    }
+    if (t == 0 && counts) counts[q] = (uint32_t)cnt;
+}
+
+// ---------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------
+static size_t words_for(size_t n) { return (n + 31) / 32; }
+
+// Rebuilds the host dead bitmap from the per-list tombstone sets.
+static void rebuild_dead(fdb_ivfpq* h) {
+    h->h_dead.clear();
+    if (h->n_tomb == 0) return;
+    h->h_dead.assign(words_for(h->n_total), 0u);
+    for (size_t l = 0; l < h->tomb.size(); ++l) {
+        if (h->tomb[l].empty()) continue;
+        for (uint64_t p = h->h_offs_full[l]; p < h->h_offs_full[l + 1]; ++p)
+            if (h->tomb[l].count(h->h_ids[p])) h->h_dead[p >> 5] |= 1u << (p & 31);
+    }
+}
+
+void ivfpq_sync_state(fdb_ivfpq* h) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    if (h->dead_dirty) {
+        if (h->h_dead.empty()) {
+            h->dead.release();
+        } else {
+            h->dead.alloc(h->h_dead.size());
+            FDB_CUDA(cudaMemcpyAsync(h->dead.p, h->h_dead.data(), h->dead.bytes(),
+                                     cudaMemcpyHostToDevice, s));
+            if (h->dnorm.p && h->tc_pstart.p && h->nlist > 0) {
+                mask_dead_kernel<<<(unsigned)h->nlist, 256, 0, s>>>(h->dead.p, h->offs.p,
+                                                                    h->tc_pstart.p, h->dnorm.p);
+                FDB_LAUNCH_CHECK();
+            }
+        }
+        FDB_CUDA(cudaStreamSynchronize(s));
+        h->dead_dirty = false;
+    }
+    if (h->rerank && h->rr_dirty) {
+        const size_t n = h->rr_ids.size();
+        std::vector<std::pair<uint64_t, uint32_t>> order(n);
+        for (size_t i = 0; i < n; ++i) order[i] = {h->rr_ids[i], (uint32_t)i};
+        std::sort(order.begin(), order.end());
+        std::vector<uint64_t> sid(n);
+        std::vector<uint32_t> sslot(n);
+        for (size_t i = 0; i < n; ++i) {
+            sid[i] = order[i].first;
+            sslot[i] = order[i].second;
+        }
+        h->rr_sorted.alloc(std::max<size_t>(n, 1));
+        h->rr_sorted_slot.alloc(std::max<size_t>(n, 1));
+        h->rr_dev.alloc(std::max<size_t>(n * h->dim, 1));
+        if (n) {
+            FDB_CUDA(cudaMemcpyAsync(h->rr_sorted.p, sid.data(), n * 8, cudaMemcpyHostToDevice, s));
+            FDB_CUDA(cudaMemcpyAsync(h->rr_sorted_slot.p, sslot.data(), n * 4,
+                                     cudaMemcpyHostToDevice, s));
+            FDB_CUDA(cudaMemcpyAsync(h->rr_dev.p, h->rr_x.data(), n * h->dim * 4,
+                                     cudaMemcpyHostToDevice, s));
+        }
+        FDB_CUDA(cudaStreamSynchronize(s));
+        h->rr_dirty = false;
+    }
+}
+
+static void rr_put(fdb_ivfpq* h, uint64_t id, const float* v) {
+    auto it = h->rr_slot.find(id);
+    size_t slot;
+    if (it != h->rr_slot.end()) {
+        slot = it->second;
+    } else {
+        slot = h->rr_ids.size();
+        h->rr_ids.push_back(id);
+        h->rr_x.resize(h->rr_x.size() + h->dim);
+        h->rr_slot.emplace(id, slot);
+    }
+    std::copy(v, v + h->dim, h->rr_x.begin() + slot * h->dim);
+    h->rr_dirty = true;
+}
+
+static void rr_remove(fdb_ivfpq* h, uint64_t id) {
+    auto it = h->rr_slot.find(id);
+    if (it == h->rr_slot.end()) return;
+    const size_t slot = it->second, last = h->rr_ids.size() - 1;
+    h->rr_slot.erase(it);
+    if (slot != last) {
+        h->rr_ids[slot] = h->rr_ids[last];
+        std::copy(h->rr_x.begin() + last * h->dim, h->rr_x.begin() + (last + 1) * h->dim,
+                  h->rr_x.begin() + slot * h->dim);
+        h->rr_slot[h->rr_ids[slot]] = slot;
+    }
+    h->rr_ids.pop_back();
+    h->rr_x.resize(last * h->dim);
+    h->rr_dirty = true;
+}
+
+void ivfpq_enable_reranking(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                            size_t factor) {
+    h->rr_ids.clear();
+    h->rr_x.clear();
+    h->rr_slot.clear();
+    // HashMap collect: a repeated id keeps its last vector
+    for (size_t i = 0; i < n; ++i) rr_put(h, ids[i], x + i * h->dim);
+    h->rerank = true;
+    h->rerank_factor = std::max<size_t>(factor, 1);
+    h->rr_dirty = true;
+}
+
+void launch_rerank(fdb_ivfpq* h, const uint64_t* keys, const uint64_t* cand_ids, size_t nq,
+                   size_t fetch, const float* dQ, size_t k, uint64_t* d_ids, float* d_dists,
+                   uint32_t* d_counts) {
+    FDB_REQUIRE(fetch <= (size_t)RERANK_MAX, FDB_ERR_UNSUPPORTED,
+                "k * rerank_factor above FDB_MAX_K");
+    if (nq == 0 || k == 0) return;
+    const unsigned threads = (unsigned)((fetch + 31) / 32 * 32);
+    rerank_kernel<<<(unsigned)nq, threads, 0, h->ctx->c.stream>>>(
+        keys, cand_ids, (int)fetch, dQ, (int)h->dim, h->rr_sorted.p, h->rr_sorted_slot.p,
+        h->rr_ids.size(), h->rr_dev.p, (int)k, d_ids, d_dists, d_counts);
+    FDB_LAUNCH_CHECK();
+}
+
+// Lazily built (id, row) index, ascending, for delete's lookups.
+static void ensure_id_index(fdb_ivfpq* h) {
+    if (h->id_index_ok) return;
+    h->id_index.resize(h->n_total);
+    for (size_t p = 0; p < h->n_total; ++p) h->id_index[p] = {h->h_ids[p], (uint32_t)p};
+    std::sort(h->id_index.begin(), h->id_index.end());
+    h->id_index_ok = true;
+}
+
+static size_t list_of_row(const fdb_ivfpq* h, uint64_t p) {
+    return (size_t)(std::upper_bound(h->h_offs_full.begin(), h->h_offs_full.end(), p) -
+                    h->h_offs_full.begin()) - 1;
+}
+
+bool ivfpq_delete(fdb_ivfpq* h, uint64_t id) {
+    ensure_id_index(h);
+    auto lo = std::lower_bound(h->id_index.begin(), h->id_index.end(),
+                               std::make_pair(id, (uint32_t)0));
+    // rows holding the id, ascending, hence in list order
+    for (auto it = lo; it != h->id_index.end() && it->first == id;) {
+        const size_t l = list_of_row(h, it->second);
+        auto next = it;
+        while (next != h->id_index.end() && next->first == id &&
+               list_of_row(h, next->second) == l)
+            ++next;
+        const bool already = !h->tomb.empty() && h->tomb[l].count(id);
+        if (!already) {
+            if (h->tomb.empty()) h->tomb.resize(h->nlist);
+            h->tomb[l].insert(id);
+            h->n_tomb++;
+            if (h->h_dead.empty()) h->h_dead.assign(words_for(h->n_total), 0u);
+            for (auto r = it; r != next; ++r) h->h_dead[r->second >> 5] |= 1u << (r->second & 31);
+            h->dead_dirty = true;
+            if (h->rerank) rr_remove(h, id);
+            return true;
+        }
+        it = next;
+    }
+    return false;
+}
+
+size_t ivfpq_live_len(const fdb_ivfpq* h) {
+    // len(): ids.len() - tombstones.len() over the lists held here
+    if (h->n_tomb == 0) return h->n_local;
+    size_t t = 0;
+    for (size_t l = 0; l < h->tomb.size(); ++l) {
+        if (h->tomb[l].empty()) continue;
+        if (!h->sharded || h->owned[l]) t += h->tomb[l].size();
+    }
+    return h->n_local - t;
+}
+
+// After any layout change: new derived tables, dead bitmap, sharding.
+static void relayout_done(fdb_ivfpq* h) {
+    h->id_index.clear();
+    h->id_index_ok = false;
+    rebuild_dead(h);
+    h->dead_dirty = true;
+    ivfpq_prepare_tables(h);
+    if (h->shard_world > 1) ivfpq_shard(h, h->shard_rank, h->shard_world);
+    ivfpq_sync_state(h);
+}
+
+void ivfpq_compact(fdb_ivfpq* h) {
+    if (h->n_tomb == 0) return;
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const size_t nlist = h->nlist, m = h->m;
+    std::vector<uint32_t> keep;
+    keep.reserve(h->n_total);
+    std::vector<uint64_t> offs(nlist + 1, 0);
+    for (size_t l = 0; l < nlist; ++l) {
+        const bool t = !h->tomb[l].empty();
+        for (uint64_t p = h->h_offs_full[l]; p < h->h_offs_full[l + 1]; ++p)
+            if (!t || !h->tomb[l].count(h->h_ids[p])) keep.push_back((uint32_t)p);
+        offs[l + 1] = keep.size();
+    }
+    const size_t nk = keep.size();
+    DevBuf<uint32_t> d_keep(std::max<size_t>(nk, 1));
+    DevBuf<uint8_t> codes2(std::max<size_t>(nk * m, 1));
+    DevBuf<uint64_t> ids2(std::max<size_t>(nk, 1));
+    if (nk) {
+        FDB_CUDA(cudaMemcpyAsync(d_keep.p, keep.data(), nk * 4, cudaMemcpyHostToDevice, s));
+        gather_rows_kernel<<<grid_for(nk * m), 256, 0, s>>>(d_keep.p, nk, (int)m, h->codes.p,
+                                                             h->ids.p, codes2.p, ids2.p);
+        FDB_LAUNCH_CHECK();
+    }
+    FDB_CUDA(cudaMemcpyAsync(h->offs.p, offs.data(), (nlist + 1) * 8, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    h->codes = std::move(codes2);
+    h->ids = std::move(ids2);
+    std::vector<uint64_t> hid(nk);
+    for (size_t i = 0; i < nk; ++i) hid[i] = h->h_ids[keep[i]];
+    h->h_ids.swap(hid);
+    h->h_offs_full = offs;
+    h->h_offs = offs;
+    h->n_total = h->n_local = nk;
+    h->tomb.clear();
+    h->n_tomb = 0;
+    relayout_done(h);
+}
+
+void ivfpq_insert_batch(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, size_t n) {
+    if (n == 0) return;
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    const size_t nlist = h->nlist, m = h->m, dim = h->dim, n_old = h->n_total;
+    FDB_REQUIRE(n_old + n < (1ull << 32), FDB_ERR_UNSUPPORTED, "at most 2^32-1 vectors per index");
+    DevBuf<float> X(n * dim);
+    DevBuf<uint32_t> assign(n), slot(n);
+    FDB_CUDA(cudaMemcpyAsync(X.p, x_host, X.bytes(), cudaMemcpyHostToDevice, s));
+    // nearest list, first minimum (ivf_pq.rs:1737-1744)
+    launch_assign(s, X.p, n, (int)dim, (int)dim, h->cents.p, (int)nlist, assign.p);
+    std::vector<uint32_t> a(n);
+    FDB_CUDA(cudaMemcpyAsync(a.data(), assign.p, n * 4, cudaMemcpyDeviceToHost, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    std::vector<uint64_t> cnt(nlist, 0), offs(nlist + 1, 0);
+    for (size_t i = 0; i < n; ++i) cnt[a[i]]++;
+    for (size_t l = 0; l < nlist; ++l)
+        offs[l + 1] = offs[l] + (h->h_offs_full[l + 1] - h->h_offs_full[l]) + cnt[l];
+    // new rows go to the end of their list, in input order
+    std::vector<uint64_t> fill(nlist);
+    for (size_t l = 0; l < nlist; ++l) fill[l] = offs[l] + (h->h_offs_full[l + 1] - h->h_offs_full[l]);
+    std::vector<uint32_t> sl(n);
+    for (size_t i = 0; i < n; ++i) sl[i] = (uint32_t)(fill[a[i]]++);
+    const size_t n_new = n_old + n;
+    DevBuf<uint64_t> old_offs(nlist + 1), new_offs(nlist + 1), new_ids_in(n);
+    DevBuf<uint8_t> codes2(n_new * m);
+    DevBuf<uint64_t> ids2(n_new);
+    FDB_CUDA(cudaMemcpyAsync(old_offs.p, h->h_offs_full.data(), (nlist + 1) * 8,
+                             cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(new_offs.p, offs.data(), (nlist + 1) * 8, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(slot.p, sl.data(), n * 4, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaMemcpyAsync(new_ids_in.p, ids_host, n * 8, cudaMemcpyHostToDevice, s));
+    if (n_old) {
+        relayout_kernel<<<(unsigned)nlist, 256, 0, s>>>(old_offs.p, new_offs.p, (int)m,
+                                                        h->codes.p, h->ids.p, codes2.p, ids2.p);
+        FDB_LAUNCH_CHECK();
+    }
+    // residual of each new vector to its list's centroid, PQ-encoded into its slot
+    launch_pq_encode(s, X.p, n, (int)dim, h->cents.p, assign.p, h->cb.p, (int)m, slot.p, codes2.p);
+    scatter_ids_kernel<<<grid_for(n), 256, 0, s>>>(new_ids_in.p, slot.p, n, ids2.p);
+    FDB_LAUNCH_CHECK();
+    FDB_CUDA(cudaMemcpyAsync(h->offs.p, offs.data(), (nlist + 1) * 8, cudaMemcpyHostToDevice, s));
+    FDB_CUDA(cudaStreamSynchronize(s));
+    h->codes = std::move(codes2);
+    h->ids = std::move(ids2);
+    std::vector<uint64_t> hid(n_new);
+    for (size_t l = 0; l < nlist; ++l)
+        std::copy(h->h_ids.begin() + h->h_offs_full[l], h->h_ids.begin() + h->h_offs_full[l + 1],
+                  hid.begin() + offs[l]);
+    for (size_t i = 0; i < n; ++i) hid[sl[i]] = ids_host[i];
+    h->h_ids.swap(hid);
+    h->h_offs_full = offs;
+    h->h_offs = offs;
+    h->n_total = h->n_local = n_new;
+    // partition.tombstones.remove(&id) in the list the vector joined
+    if (h->n_tomb) {
+        for (size_t i = 0; i < n; ++i) h->n_tomb -= h->tomb[a[i]].erase(ids_host[i]);
+    }
+    if (h->rerank)
+        for (size_t i = 0; i < n; ++i) rr_put(h, ids_host[i], x_host + i * dim);
+    relayout_done(h);
+}
+
+// Per-call skip bitmap of search_filtered: dead rows and rows whose id is
+// not allowed.  Returns the device bitmap (in h->f_skip).
+const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed_host, size_t na) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    DevBuf<uint64_t> a(na), b(na);
+    FDB_CUDA(cudaMemcpyAsync(a.p, allowed_host, na * 8, cudaMemcpyHostToDevice, s));
+    size_t tmp = 0;
+    FDB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, a.p, b.p, (int)na, 0, 64, s));
+    DevBuf<uint8_t> t(std::max<size_t>(tmp, 1));
+    FDB_CUDA(cub::DeviceRadixSort::SortKeys(t.p, tmp, a.p, b.p, (int)na, 0, 64, s));
+    const size_t nw = words_for(h->n_total);
+    h->f_skip.ensure(std::max<size_t>(nw, 1));
+    if (nw) {
+        filter_bitmap_kernel<<<grid_for(nw), 256, 0, s>>>(h->ids.p, h->n_total, b.p, na,
+                                                           h->dead.p, h->f_skip.p);
+        FDB_LAUNCH_CHECK();
+    }
+    FDB_CUDA(cudaStreamSynchronize(s));
+    return h->f_skip.p;
+}
+
+}  // namespace fdb

@@ -102,7 +102,7 @@ __global__ void pq_init_kernel(const float* __restrict__ x, int dim, int m,
 
 // ProductQuantizer::try_train on device rows x[n][dim].
 void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
-                  const uint32_t* init_idx_host, float* cb, int* iters_out) {
+                  const uint32_t* init_idx_host, float* cb, int* iters_out, uint8_t* ever_out) {
     cudaStream_t s = ctx.stream;
     const size_t ni = (size_t)m * KSUB;
     for (size_t e = 0; e < ni; ++e)
@@ -115,7 +115,7 @@ void pq_train_dev(Ctx& ctx, const float* x, size_t n, int dim, int m, int iters,
     pq_init_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(x, dim, m, d_idx.p, cb);
     FDB_LAUNCH_CHECK();
     KMeansProblem pb{x, n, sub, dim, m, KSUB, iters};
-    kmeans_run(ctx, pb, cb, iters_out);
+    kmeans_run(ctx, pb, cb, iters_out, ever_out);
 }
 
 }  // namespace fdb

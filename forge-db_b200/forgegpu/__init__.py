@@ -28,7 +28,17 @@ ERRORS = {
     -1: "InvalidParameter", -2: "DimensionMismatch", -3: "EmptyTrainingSet",
     -4: "DimensionNotDivisible", -5: "InsufficientVectors", -6: "Timeout", -7: "Cuda",
     -8: "Nccl", -9: "MemoryLimitExceeded", -10: "EmptyVectorSet", -11: "NotSupported",
+    -12: "Io", -13: "SerializationError", -14: "ChecksumMismatch", -15: "InvalidFormat",
+    -16: "InsufficientDiskSpace",
 }
+
+
+class IndexType:
+    """src/persistence/format.rs:12-23"""
+    IvfPq = 1
+    Hnsw = 2
+    Ivf = 3
+    BruteForce = 4
 
 
 class DistanceMetric:
@@ -53,6 +63,14 @@ class Stats(C.Structure):
                 ("scan_ms", C.c_double), ("rescore_ms", C.c_double), ("merge_ms", C.c_double),
                 ("total_ms", C.c_double), ("exact_rescans", C.c_uint64),
                 ("kernel_ms", C.c_double), ("kernel_scores", C.c_uint64)]
+
+
+class FileInfo(C.Structure):
+    _fields_ = [("version", C.c_uint32), ("index_type", C.c_uint32), ("flags", C.c_uint32),
+                ("checksum", C.c_uint32), ("n", C.c_uint64), ("dim", C.c_uint64),
+                ("nlist", C.c_uint64), ("m", C.c_uint64), ("nprobe", C.c_uint64),
+                ("metric", C.c_int32), ("has_rerank", C.c_int32), ("n_rerank", C.c_uint64),
+                ("rerank_factor", C.c_uint64)]
 
 
 class TrainOpts(C.Structure):
@@ -116,6 +134,23 @@ _SIGS = {
     "fdb_bf_batch_search_device": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp,
                                              C.POINTER(Stats)]),
     "fdb_bf_free": (C.c_int, [_vp]),
+    "fdb_bf_remove": (C.c_int, [_vp, C.c_uint64, C.POINTER(C.c_int)]),
+    "fdb_ivfpq_enable_reranking": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz]),
+    "fdb_ivfpq_search_filtered": (C.c_int, [_vp, _vp, _sz, _vp, _sz, _vp, _vp, C.POINTER(_sz)]),
+    "fdb_ivfpq_batch_search_filtered": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
+    "fdb_ivfpq_insert_batch": (C.c_int, [_vp, _vp, _vp, _sz, _sz]),
+    "fdb_ivfpq_delete": (C.c_int, [_vp, C.c_uint64, C.POINTER(C.c_int)]),
+    "fdb_ivfpq_num_tombstones": (_sz, [_vp]),
+    "fdb_ivfpq_len_with_tombstones": (_sz, [_vp]),
+    "fdb_ivfpq_fragmentation_ratio": (C.c_float, [_vp]),
+    "fdb_ivfpq_compact": (C.c_int, [_vp]),
+    "fdb_ivfpq_rebuild": (C.c_int, [_vp, C.POINTER(TrainOpts)]),
+    "fdb_ivfpq_save": (C.c_int, [_vp, C.c_char_p]),
+    "fdb_ivfpq_load": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
+    "fdb_bf_save": (C.c_int, [_vp, C.c_char_p]),
+    "fdb_bf_load": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
+    "fdb_file_inspect": (C.c_int, [C.c_char_p, C.POINTER(FileInfo)]),
+    "fdb_crc32": (C.c_uint32, [_vp, _sz]),
 }
 
 _lib = None
@@ -215,6 +250,19 @@ def uniform_draws(seed: int, count: int) -> np.ndarray:
     out = np.empty(count, np.float32)
     _check(lib().fdb_uniform_draws(seed, count, _p(out)))
     return out
+
+
+def crc32(data: bytes) -> int:
+    """crc32fast::hash, the .fdb header's checksum (host only)."""
+    buf = C.create_string_buffer(bytes(data), max(len(data), 1))
+    return lib().fdb_crc32(buf, len(data))
+
+
+def inspect_file(path) -> FileInfo:
+    """Header and payload shape of a .fdb file (host only; checks what load does)."""
+    info = FileInfo()
+    _check(lib().fdb_file_inspect(os.fsencode(path), C.byref(info)))
+    return info
 
 
 def shard_plan(sizes, world: int) -> np.ndarray:
@@ -329,6 +377,28 @@ class ProductQuantizer:
 # ---------------------------------------------------------------------------
 # indexes
 # ---------------------------------------------------------------------------
+def _train_opts(seed=0, ivf_sample=0, pq_sample=0, ivf_iters=0, pq_iters=0, ivf_sample_idx=None,
+                ivf_init_idx=None, ivf_kpp_u=None, pq_sample_idx=None, pq_init_idx=None):
+    keep = []
+
+    def arr(a, dt):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dt)
+        keep.append(a)
+        return a.ctypes.data
+
+    o = TrainOpts(ivf_sample, pq_sample, ivf_iters, pq_iters,
+                  arr(ivf_sample_idx, np.uint32), arr(ivf_init_idx, np.uint32),
+                  arr(ivf_kpp_u, np.float32), arr(pq_sample_idx, np.uint32),
+                  arr(pq_init_idx, np.uint32), seed)
+    if ivf_sample_idx is not None:
+        o.ivf_sample = len(ivf_sample_idx)
+    if pq_sample_idx is not None:
+        o.pq_sample = len(pq_sample_idx)
+    return o, keep
+
+
 def _results(ids, dists, counts):
     return [list(zip(ids[i, :counts[i]].tolist(), dists[i, :counts[i]].tolist()))
             for i in range(ids.shape[0])]
@@ -350,23 +420,8 @@ class IVFPQIndex:
         ctx = ctx or default_context()
         x = _f32(vectors)
         n, dim = x.shape
-        keep = []
-
-        def arr(a, dt):
-            if a is None:
-                return None
-            a = np.ascontiguousarray(a, dt)
-            keep.append(a)
-            return a.ctypes.data
-
-        o = TrainOpts(ivf_sample, pq_sample, ivf_iters, pq_iters,
-                      arr(ivf_sample_idx, np.uint32), arr(ivf_init_idx, np.uint32),
-                      arr(ivf_kpp_u, np.float32), arr(pq_sample_idx, np.uint32),
-                      arr(pq_init_idx, np.uint32), seed)
-        if ivf_sample_idx is not None:
-            o.ivf_sample = len(ivf_sample_idx)
-        if pq_sample_idx is not None:
-            o.pq_sample = len(pq_sample_idx)
+        o, keep = _train_opts(seed, ivf_sample, pq_sample, ivf_iters, pq_iters, ivf_sample_idx,
+                              ivf_init_idx, ivf_kpp_u, pq_sample_idx, pq_init_idx)
         idv = None if ids is None else np.ascontiguousarray(ids, np.uint64)
         h = C.c_void_p()
         _check(lib().fdb_ivfpq_build(ctx.h, _p(x), _p(idv), n, dim, n_clusters, n_subvectors,
@@ -455,6 +510,82 @@ class IVFPQIndex:
 
     batch_search_parallel = batch_search
 
+    # --- re-ranking, filters, updates (ivf_pq.rs:513-831, 1731-1890) ---
+    def enable_reranking(self, vectors, ids, rerank_factor: int):
+        x = _f32(vectors)
+        idv = np.ascontiguousarray(ids, np.uint64)
+        n = x.shape[0] if x.ndim == 2 else 0
+        _check(lib().fdb_ivfpq_enable_reranking(self.h, _p(x) if n else None,
+                                                _p(idv) if n else None, n,
+                                                x.shape[1] if n else self.dim(), rerank_factor))
+
+    def search_filtered(self, query, k: int, allowed_ids):
+        """search_filtered with the matching ids of the metadata filter."""
+        q = _f32(query)
+        al = np.ascontiguousarray(allowed_ids, np.uint64)
+        ids = np.empty(max(k, 1), np.uint64)
+        d = np.empty(max(k, 1), np.float32)
+        n = C.c_size_t(0)
+        _check(lib().fdb_ivfpq_search_filtered(self.h, _p(q), k, _p(al) if al.size else None,
+                                               al.size, _p(ids), _p(d), C.byref(n)))
+        return list(zip(ids[:n.value].tolist(), d[:n.value].tolist()))
+
+    def batch_search_filtered_arrays(self, queries, k: int, allowed_ids):
+        Q = _f32(queries)
+        nq = Q.shape[0]
+        al = np.ascontiguousarray(allowed_ids, np.uint64)
+        ids = np.empty((nq, k), np.uint64)
+        d = np.empty((nq, k), np.float32)
+        cnt = np.empty(nq, np.uint32)
+        _check(lib().fdb_ivfpq_batch_search_filtered(self.h, _p(Q), nq, k,
+                                                     _p(al) if al.size else None, al.size,
+                                                     _p(ids), _p(d), _p(cnt)))
+        return ids, d, cnt
+
+    def insert_batch(self, vectors, ids):
+        x = _f32(vectors)
+        if x.ndim == 1:
+            x = x[None]
+        idv = np.ascontiguousarray(np.atleast_1d(ids), np.uint64)
+        _check(lib().fdb_ivfpq_insert_batch(self.h, _p(x), _p(idv), x.shape[0], x.shape[1]))
+
+    def delete(self, id_: int) -> bool:
+        out = C.c_int(0)
+        _check(lib().fdb_ivfpq_delete(self.h, int(id_), C.byref(out)))
+        return bool(out.value)
+
+    def num_tombstones(self) -> int:
+        return lib().fdb_ivfpq_num_tombstones(self.h)
+
+    def len_with_tombstones(self) -> int:
+        return lib().fdb_ivfpq_len_with_tombstones(self.h)
+
+    def fragmentation_ratio(self) -> float:
+        return lib().fdb_ivfpq_fragmentation_ratio(self.h)
+
+    def is_empty(self) -> bool:
+        return self.len() == 0
+
+    def compact(self):
+        _check(lib().fdb_ivfpq_compact(self.h))
+
+    def rebuild(self, seed: int = 0, **draws):
+        o, keep = _train_opts(seed, **draws)
+        _check(lib().fdb_ivfpq_rebuild(self.h, C.byref(o)))
+
+    # --- Persistable (src/persistence/mod.rs:34-73) ---
+    def save(self, path):
+        _check(lib().fdb_ivfpq_save(self.h, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, path, ctx: Context | None = None):
+        ctx = ctx or default_context()
+        h = C.c_void_p()
+        _check(lib().fdb_ivfpq_load(ctx.h, os.fsencode(path), C.byref(h)))
+        return cls(h, ctx)
+
+    load_mmap = load
+
     def close(self):
         if self.h:
             _check(lib().fdb_ivfpq_free(self.h))
@@ -523,6 +654,28 @@ class BruteForceIndex:
     def batch_search(self, queries, k: int):
         ids, d, cnt = self.batch_search_arrays(queries, k)
         return _results(ids, d, cnt)
+
+    def remove(self, id_: int) -> bool:
+        out = C.c_int(0)
+        _check(lib().fdb_bf_remove(self.h, int(id_), C.byref(out)))
+        return bool(out.value)
+
+    def is_empty(self) -> bool:
+        return self.len() == 0
+
+    def save(self, path):
+        _check(lib().fdb_bf_save(self.h, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, path, ctx: Context | None = None):
+        ctx = ctx or default_context()
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        h = C.c_void_p()
+        _check(lib().fdb_bf_load(ctx.h, os.fsencode(path), C.byref(h)))
+        self.h = h
+        self.metric = inspect_file(path).metric
+        return self
 
     def close(self):
         if self.h:

@@ -44,6 +44,11 @@ extern "C" {
 #define FDB_ERR_OOM (-9)                  /* MemoryLimitExceeded */
 #define FDB_ERR_EMPTY_VECTOR_SET (-10)    /* EmptyVectorSet */
 #define FDB_ERR_UNSUPPORTED (-11)         /* NotSupported */
+#define FDB_ERR_IO (-12)                  /* Io */
+#define FDB_ERR_SERIALIZATION (-13)       /* SerializationError (bincode) */
+#define FDB_ERR_CHECKSUM (-14)            /* ChecksumMismatch */
+#define FDB_ERR_INVALID_FORMAT (-15)      /* InvalidFormat */
+#define FDB_ERR_DISK_SPACE (-16)          /* InsufficientDiskSpace */
 
 /* ---- DistanceMetric (src/distance/mod.rs:16-33) ------------------------- */
 #define FDB_METRIC_EUCLIDEAN 0
@@ -244,6 +249,54 @@ int fdb_ivfpq_batch_search_device(fdb_ivfpq* h, const float* d_queries, size_t n
                                   fdb_stats* stats);
 int fdb_ivfpq_free(fdb_ivfpq* h);
 
+/* ---- IVFPQIndex: re-ranking, filters, updates (ivf_pq.rs:513-831, 1731-1890) */
+/* enable_reranking (ivf_pq.rs:513-517): keep the n original vectors (ids[i]
+ * names x[i]; a repeated id keeps its last vector) and from now on fetch
+ * k * max(rerank_factor, 1) PQ candidates per query, re-score those that have
+ * an original vector with sqrt(L2^2) on the device (the reference's
+ * euclidean_distance_squared order, then a correctly rounded square root),
+ * sort stably and keep k (rerank_results, ivf_pq.rs:556-582).  Results are
+ * then Euclidean distances.  k * rerank_factor must not exceed FDB_MAX_K. */
+int fdb_ivfpq_enable_reranking(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                               size_t dim, size_t rerank_factor);
+/* search_filtered (ivf_pq.rs:692-831): search() restricted to the vectors
+ * whose id is in allowed_ids[n_allowed] (the ids of the reference's
+ * MetadataStore::filter_bitmap(filter); rows with other ids are skipped during
+ * the scan).  n_allowed == 0 returns no results.  With re-ranking on, 4 *
+ * k * rerank_factor candidates are re-ranked (filter_fetch_k, :720). */
+int fdb_ivfpq_search_filtered(fdb_ivfpq* h, const float* query, size_t k,
+                              const uint64_t* allowed_ids, size_t n_allowed, uint64_t* ids,
+                              float* dists, size_t* n_out);
+/* No reference counterpart: search_filtered for nq queries sharing one
+ * filter, on host buffers (ids/dists [nq][k], counts [nq] nullable). */
+int fdb_ivfpq_batch_search_filtered(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                                    const uint64_t* allowed_ids, size_t n_allowed,
+                                    uint64_t* ids, float* dists, uint32_t* counts);
+/* insert_batch (ivf_pq.rs:1731-1773): each vector goes to its nearest list
+ * (first minimum), its residual is PQ-encoded and appended to that list, a
+ * tombstone on its id in that list is lifted, and with re-ranking on it
+ * enters the original-vector store.  ids must not be NULL. */
+int fdb_ivfpq_insert_batch(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
+                           size_t dim);
+/* delete (ivf_pq.rs:1786-1805): tombstones `id` in the first list that holds
+ * it and has not tombstoned it yet (every row of that list with the id is
+ * then skipped); *deleted = 1 if so, else 0.  Removes it from the re-ranking
+ * store. */
+int fdb_ivfpq_delete(fdb_ivfpq* h, uint64_t id, int* deleted);
+size_t fdb_ivfpq_num_tombstones(const fdb_ivfpq* h);      /* ivf_pq.rs:1807-1812 */
+size_t fdb_ivfpq_len_with_tombstones(const fdb_ivfpq* h); /* ivf_pq.rs:1098-1103 */
+float fdb_ivfpq_fragmentation_ratio(const fdb_ivfpq* h);  /* ivf_pq.rs:1815-1822 */
+/* compact (ivf_pq.rs:1828-1852): drop tombstoned rows, keeping row order. */
+int fdb_ivfpq_compact(fdb_ivfpq* h);
+/* rebuild (ivf_pq.rs:1860-1890): retrain on the re-ranking store's vectors
+ * with the same nlist, m, metric, nprobe and rerank_factor; FDB_ERR_UNSUPPORTED
+ * without re-ranking, FDB_ERR_EMPTY_VECTOR_SET when the store is empty.
+ * opts (nullable) gives the training draws as for fdb_ivfpq_build.  The
+ * vectors are taken in insertion order (the reference takes hash-map order);
+ * the rebuilt index is unsharded.  If training fails the handle is left
+ * unusable and must be freed. */
+int fdb_ivfpq_rebuild(fdb_ivfpq* h, const fdb_train_opts* opts);
+
 /* ---- BruteForceIndex (src/index/brute_force.rs:60-225) ------------------ */
 /* BruteForceIndex::new(metric) followed by add() of n rows
  * (brute_force.rs:67-80).  `ids` may be NULL (ids 0..n-1). */
@@ -271,6 +324,45 @@ int fdb_bf_batch_search_device(fdb_bf* h, const float* d_queries, size_t nq, siz
                                uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
                                fdb_stats* stats);
 int fdb_bf_free(fdb_bf* h);
+/* MutableVectorIndex::remove (brute_force.rs:267-274): swap-remove the first
+ * row with this id; *removed = 1 if one was found. */
+int fdb_bf_remove(fdb_bf* h, uint64_t id, int* removed);
+
+/* ---- .fdb files (src/persistence/mod.rs, format.rs) --------------------- */
+/* A 24-byte header (magic "FORGEDB\0", version u32 = 1, index type u32,
+ * flags u32, CRC-32 of the payload u32; format.rs:76-133) and the payload:
+ * for IVF-PQ the bincode-1.3 encoding of SerializableIVFPQ (ivf_pq.rs:197-262,
+ * 1894-1914), for brute force [metric u8][n u64][dim u64][ids][rows]
+ * (brute_force.rs:277-318).  Files are interchangeable with the reference's
+ * save()/load() (Persistable, ivf_pq.rs:1970-1994).  Saving an IVF-PQ index
+ * writes its tombstoned rows and no tombstones, as the reference does; the
+ * original-vector store is written in insertion order (the reference writes
+ * hash-map order).  A sharded index cannot be saved. */
+#define FDB_INDEX_IVFPQ 1
+#define FDB_INDEX_HNSW 2
+#define FDB_INDEX_IVF 3
+#define FDB_INDEX_BRUTE_FORCE 4
+int fdb_ivfpq_save(fdb_ivfpq* h, const char* path);
+/* load / load_mmap: checks the header (magic, version <= 1, type) and the
+ * CRC, then rebuilds the index on ctx's device. */
+int fdb_ivfpq_load(fdb_ctx* ctx, const char* path, fdb_ivfpq** out);
+int fdb_bf_save(fdb_bf* h, const char* path);
+int fdb_bf_load(fdb_ctx* ctx, const char* path, fdb_bf** out);
+/* Host only (no device): header fields and, for IVF-PQ and brute-force
+ * files, the shape of the payload.  Checks what load() checks. */
+typedef struct fdb_file_info {
+    uint32_t version, index_type, flags, checksum;
+    uint64_t n;              /* vectors (rows incl. tombstoned ones for IVF-PQ) */
+    uint64_t dim;
+    uint64_t nlist, m;       /* IVF-PQ */
+    uint64_t nprobe;         /* IVF-PQ */
+    int32_t metric;          /* FDB_METRIC_* */
+    int32_t has_rerank;      /* IVF-PQ: original vectors present */
+    uint64_t n_rerank, rerank_factor;
+} fdb_file_info;
+int fdb_file_inspect(const char* path, fdb_file_info* info);
+/* crc32fast::hash: CRC-32/ISO-HDLC of n bytes (the header's checksum). */
+uint32_t fdb_crc32(const void* data, size_t n);
 
 #ifdef __cplusplus
 }

@@ -401,6 +401,8 @@ struct IvfView {
     const uint64_t* offsets;  // nlist + 1
     const uint64_t* ids;      // list-major
     const uint8_t* codes;     // list-major, m bytes each
+    const uint8_t* skip = nullptr;  // per row, nullable: 1 = skipped (tombstone /
+                                    // filter, ivf_pq.rs:655-657 and :778-792)
 };
 
 // IVFPQIndex::search, src/index/ivf_pq.rs:590-677 (no reranking: fetch_k = k).
@@ -420,6 +422,7 @@ size_t ivf_search_one(const IvfView& ix, size_t nprobe, const float* q, size_t k
         // Threshold read once per partition (:638-642).
         float thr = (heap.size() >= k && !heap.empty()) ? heap.top().d : FLT_MAX;
         for (uint64_t p = ix.offsets[l]; p < ix.offsets[l + 1]; ++p) {
+            if (ix.skip && ix.skip[p]) continue;
             float d = adc_fast(lut.data(), ix.codes + p * ix.m, ix.m);
             if (d < thr || heap.size() < k) {
                 heap.push({d, ix.ids[p]});
@@ -458,6 +461,7 @@ void ivf_batch_chunk(const IvfView& ix, size_t nprobe, const float* Q, size_t nq
             lut_flat(ix.cb, ix.m, sub, res.data(), tables.data() + t * ix.m * KSUB);
         }
         for (uint64_t p = ix.offsets[l]; p < ix.offsets[l + 1]; ++p) {
+            if (ix.skip && ix.skip[p]) continue;
             const uint8_t* code = ix.codes + p * ix.m;
             for (size_t t = 0; t < qs.size(); ++t) {
                 float d = adc_lane8(tables.data() + t * ix.m * KSUB, code, ix.m);
@@ -622,17 +626,28 @@ size_t orc_ivfpq_search(const float* cents, const float* cb, size_t nlist, size_
     return ivf_search_one(ix, nprobe, q, k, out_ids, out_d);
 }
 
+// search() / search_filtered() with rows skipped (skip[p] != 0), k = fetch_k.
+size_t orc_ivfpq_search_skip(const float* cents, const float* cb, size_t nlist, size_t m,
+                             size_t dim, const uint64_t* offsets, const uint64_t* ids,
+                             const uint8_t* codes, const uint8_t* skip, size_t nprobe,
+                             const float* q, size_t k, uint64_t* out_ids, float* out_d) {
+    IvfView ix{cents, cb, nlist, m, dim, offsets, ids, codes, skip};
+    return ivf_search_one(ix, nprobe, q, k, out_ids, out_d);
+}
+
 // IVFPQIndex::batch_search_parallel, src/index/ivf_pq.rs:1060-1084: chunks of
 // clamp(256 KiB / (nprobe * m * 1 KiB), 4, 64) queries, each chunk through
 // batch_search, chunks spread over `nthreads` threads.  chunk == 0 selects the
 // reference's rule; chunk > 0 forces one chunk size (chunk >= nq reproduces a
 // plain batch_search call).
-void orc_ivfpq_batch_search(const float* cents, const float* cb, size_t nlist, size_t m,
-                            size_t dim, const uint64_t* offsets, const uint64_t* ids,
-                            const uint8_t* codes, size_t nprobe, const float* Q, size_t nq,
-                            size_t k, size_t chunk, uint64_t* out_ids, float* out_d,
-                            uint32_t* counts, int nthreads) {
-    IvfView ix{cents, cb, nlist, m, dim, offsets, ids, codes};
+// skip (per row, nullable): tombstoned rows (ivf_pq.rs:958-961).
+void orc_ivfpq_batch_search_skip(const float* cents, const float* cb, size_t nlist, size_t m,
+                                 size_t dim, const uint64_t* offsets, const uint64_t* ids,
+                                 const uint8_t* codes, const uint8_t* skip, size_t nprobe,
+                                 const float* Q, size_t nq, size_t k, size_t chunk,
+                                 uint64_t* out_ids, float* out_d, uint32_t* counts,
+                                 int nthreads) {
+    IvfView ix{cents, cb, nlist, m, dim, offsets, ids, codes, skip};
     if (nq == 0) return;
     if (chunk == 0) {
         size_t table_bytes = m * 256 * 4;
@@ -646,6 +661,15 @@ void orc_ivfpq_batch_search(const float* cents, const float* cb, size_t nlist, s
         ivf_batch_chunk(ix, nprobe, Q + q0 * dim, q1 - q0, k, out_ids + q0 * k, out_d + q0 * k,
                         counts ? counts + q0 : nullptr);
     }
+}
+
+void orc_ivfpq_batch_search(const float* cents, const float* cb, size_t nlist, size_t m,
+                            size_t dim, const uint64_t* offsets, const uint64_t* ids,
+                            const uint8_t* codes, size_t nprobe, const float* Q, size_t nq,
+                            size_t k, size_t chunk, uint64_t* out_ids, float* out_d,
+                            uint32_t* counts, int nthreads) {
+    orc_ivfpq_batch_search_skip(cents, cb, nlist, m, dim, offsets, ids, codes, nullptr, nprobe,
+                                Q, nq, k, chunk, out_ids, out_d, counts, nthreads);
 }
 
 // BruteForceIndex::batch_search -> search_parallel -> scan_range,

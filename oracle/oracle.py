@@ -66,6 +66,11 @@ def lib():
             "orc_ivfpq_batch_search": (None, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p, _u8p,
                                               _sz, _f32p, _sz, _sz, _sz, _u64p, _f32p, _u32p,
                                               C.c_int]),
+            "orc_ivfpq_search_skip": (_sz, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p, _u8p,
+                                            _u8p, _sz, _f32p, _sz, _u64p, _f32p]),
+            "orc_ivfpq_batch_search_skip": (None, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p,
+                                                   _u8p, _u8p, _sz, _f32p, _sz, _sz, _sz,
+                                                   _u64p, _f32p, _u32p, C.c_int]),
             "orc_bf_batch_search": (None, [_f32p, _u64p, _sz, _sz, C.c_int, _f32p, _sz, _sz,
                                            _u64p, _f32p, _u32p, C.c_int]),
             "orc_max_threads": (C.c_int, []),
@@ -260,3 +265,146 @@ def bf_batch_search(X, ids, metric_id, Q, k, threads=0):
 
 def max_threads():
     return lib().orc_max_threads()
+
+
+# --- the reference's mutable IVF-PQ state (re-ranking, tombstones, filters) ----
+
+class OracleMutableIVFPQ(OracleIVFPQ):
+    """OracleIVFPQ plus the reference's state around the scan, restated in Python:
+
+    - enable_reranking / rerank_results      src/index/ivf_pq.rs:513-517, 556-582
+    - delete / len / num_tombstones / compact                     :1786-1852, 1087-1103
+    - insert_batch                                                :1731-1773
+    - search / batch_search with fetch_k and tombstones          :590-677, 850-1047
+    - search_filtered (filter_fetch_k = 4 * fetch_k)             :692-831
+    The scan arithmetic is the C restatement (orc_ivfpq_*_skip)."""
+
+    def __init__(self, centroids, codebooks, offsets, ids, codes):
+        super().__init__(centroids, codebooks, offsets, ids, codes)
+        self.tomb = [set() for _ in range(self.nlist)]
+        self.rr = None          # dict id -> vector (HashMap<u64, Vector>)
+        self.rerank_factor = 1
+
+    # ids of list l
+    def _list_ids(self, l):
+        return self.ids[int(self.offsets[l]):int(self.offsets[l + 1])]
+
+    def skip_mask(self):
+        skip = np.zeros(self.ids.size, np.uint8)
+        for l in range(self.nlist):
+            if self.tomb[l]:
+                b = int(self.offsets[l])
+                for j, i in enumerate(self._list_ids(l).tolist()):
+                    if i in self.tomb[l]:
+                        skip[b + j] = 1
+        return skip
+
+    def enable_reranking(self, X, ids, factor):
+        X = _f32(X)
+        self.rr = {}
+        for i, v in zip(np.asarray(ids, np.uint64).tolist(), X):
+            self.rr[i] = v.copy()           # collect(): a later duplicate wins
+        self.rerank_factor = max(int(factor), 1)
+
+    def delete(self, id_):
+        for l in range(self.nlist):
+            if id_ in set(self._list_ids(l).tolist()) and id_ not in self.tomb[l]:
+                self.tomb[l].add(id_)
+                if self.rr is not None:
+                    self.rr.pop(id_, None)
+                return True
+        return False
+
+    def len(self):
+        return int(self.ids.size) - sum(len(t) for t in self.tomb)
+
+    def num_tombstones(self):
+        return sum(len(t) for t in self.tomb)
+
+    def compact(self):
+        keep = self.skip_mask() == 0
+        sizes = [int(keep[int(self.offsets[l]):int(self.offsets[l + 1])].sum())
+                 for l in range(self.nlist)]
+        self.ids = np.ascontiguousarray(self.ids[keep])
+        self.codes = np.ascontiguousarray(self.codes[keep])
+        self.offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.uint64)
+        self.tomb = [set() for _ in range(self.nlist)]
+
+    def insert_batch(self, X, ids, threads=0):
+        X = _f32(X)
+        ids = np.asarray(ids, np.uint64)
+        a = assign(X, self.centroids, threads)
+        resid = _f32(X - self.centroids[a])
+        codes = pq_encode(self.codebooks, resid, threads)
+        lists_ids = [list(self._list_ids(l)) for l in range(self.nlist)]
+        lists_codes = [list(self.codes[int(self.offsets[l]):int(self.offsets[l + 1])])
+                       for l in range(self.nlist)]
+        for i in range(X.shape[0]):
+            l = int(a[i])
+            lists_ids[l].append(ids[i])
+            lists_codes[l].append(codes[i])
+            self.tomb[l].discard(int(ids[i]))
+            if self.rr is not None:
+                self.rr[int(ids[i])] = X[i].copy()
+        sizes = [len(x) for x in lists_ids]
+        self.offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.uint64)
+        self.ids = np.array([i for x in lists_ids for i in x], np.uint64)
+        self.codes = np.ascontiguousarray(
+            np.array([c for x in lists_codes for c in x], np.uint8).reshape(-1, self.m))
+
+    def _rerank(self, q, ids, d, cnt, k):
+        """rerank_results: exact sqrt(L2^2) of the candidates with an original
+        vector, stable-sorted, first k."""
+        if self.rr is None:
+            return ids[:k][:min(cnt, k)].tolist(), d[:min(cnt, k)].tolist()
+        out = []
+        for i in ids[:cnt].tolist():
+            v = self.rr.get(i)
+            if v is not None:
+                out.append((i, np.float32(np.sqrt(np.float32(l2sq(q, v))))))
+        out.sort(key=lambda t: t[1])
+        out = out[:k]
+        return [i for i, _ in out], [float(x) for _, x in out]
+
+    def _fetch(self, k):
+        return k * self.rerank_factor if self.rr is not None else k
+
+    def search(self, q, k):
+        q = _f32(q)
+        f = self._fetch(k)
+        ids = np.empty(max(f, 1), np.uint64)
+        d = np.empty(max(f, 1), np.float32)
+        cnt = lib().orc_ivfpq_search_skip(self.centroids, self.codebooks, self.nlist, self.m,
+                                          self.dim, self.offsets, self.ids, self.codes,
+                                          self.skip_mask(), self.nprobe, q, f, ids, d)
+        return self._rerank(q, ids, d, cnt, k)
+
+    def batch_search(self, Q, k, threads=0):
+        Q = _f32(Q)
+        nq = Q.shape[0]
+        f = self._fetch(k)
+        ids = np.empty((nq, f), np.uint64)
+        d = np.empty((nq, f), np.float32)
+        counts = np.empty(nq, np.uint32)
+        lib().orc_ivfpq_batch_search_skip(self.centroids, self.codebooks, self.nlist, self.m,
+                                          self.dim, self.offsets, self.ids, self.codes,
+                                          self.skip_mask(), self.nprobe, Q, nq, f, nq, ids, d,
+                                          counts, _threads(threads))
+        return [self._rerank(Q[i], ids[i], d[i], int(counts[i]), k) for i in range(nq)]
+
+    def search_filtered(self, q, k, allowed):
+        q = _f32(q)
+        allowed = set(np.asarray(allowed, np.uint64).tolist())
+        if not allowed:
+            return [], []
+        f = self._fetch(k) * 4
+        skip = self.skip_mask()
+        for p, i in enumerate(self.ids.tolist()):
+            if i not in allowed:
+                skip[p] = 1
+        ids = np.empty(f, np.uint64)
+        d = np.empty(f, np.float32)
+        cnt = lib().orc_ivfpq_search_skip(self.centroids, self.codebooks, self.nlist, self.m,
+                                          self.dim, self.offsets, self.ids, self.codes, skip,
+                                          self.nprobe, q, f, ids, d)
+        return self._rerank(q, ids, d, cnt, k)

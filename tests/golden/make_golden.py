@@ -22,6 +22,10 @@ ivfpq_small.npz
     A small seeded IVF-PQ build (injected draws) and its batch / single
     search results from the oracle: a regression pin for the oracle and a
     fixture the GPU tests compare the engine against.
+
+ivfpq_tiny.fdb, bf_tiny.fdb
+    Index files in the reference's .fdb format (see fdb_files below);
+    `python tests/golden/make_golden.py fdb` rewrites only these two.
 """
 from __future__ import annotations
 
@@ -231,11 +235,48 @@ def ivfpq_small():
                 single_d=sd, single_cnt=sc)
 
 
+def fdb_files():
+    """ivfpq_tiny.fdb / bf_tiny.fdb: files in the reference's format, written
+    by the Python restatement of it (oracle/fdb_format.py) from seeded arrays:
+    an IVF-PQ index (4 lists of 8-d vectors, 4 subvectors, random codes and
+    ids, non-trivial centroid / codeword ids, nprobe 3, Cosine as the stored
+    metric, 12 original vectors with rerank_factor 3) and a brute-force index
+    (DotProduct, 30 rows of 6-d).  The engine must load them and write them
+    back byte for byte."""
+    sys.path.insert(0, os.path.join(HERE, "..", "..", "oracle"))
+    import fdb_format as F
+    rng = np.random.default_rng(4242)
+    nlist, dim, m, n = 4, 8, 4, 40
+    cents = rng.normal(size=(nlist, dim)).astype(np.float32)
+    cb = rng.normal(size=(m, 256, dim // m)).astype(np.float32)
+    sizes = np.array([13, 0, 19, 8])
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.uint64)
+    ids = rng.choice(10 ** 6, n, replace=False).astype(np.uint64)
+    codes = rng.integers(0, 256, (n, m)).astype(np.uint8)
+    cent_ids = np.array([0, 1, 517, 3], np.uint64)  # list 2 kept its initial pick's id
+    cb_ids = np.arange(m * 256, dtype=np.uint64) % 256
+    cb_ids[5] = 901
+    rr_ids = ids[:12].copy()
+    rr_x = rng.normal(size=(12, dim)).astype(np.float32)
+    payload = F.encode_ivfpq(cents, cent_ids, cb, cb_ids, offsets, ids, codes, nprobe=3,
+                             metric=2, rerank=(rr_ids, rr_x), rerank_factor=3)
+    with open(os.path.join(HERE, "ivfpq_tiny.fdb"), "wb") as f:
+        f.write(F.file_bytes(F.IVFPQ, payload))
+    Xb = rng.normal(size=(30, 6)).astype(np.float32)
+    idb = rng.choice(10 ** 6, 30, replace=False).astype(np.uint64)
+    with open(os.path.join(HERE, "bf_tiny.fdb"), "wb") as f:
+        f.write(F.file_bytes(F.BRUTE_FORCE, F.encode_bf(3, idb, Xb)))
+
+
 def main():
+    if sys.argv[1:] == ["fdb"]:
+        fdb_files()
+        return
     with open(os.path.join(HERE, "known_values.json"), "w") as f:
         json.dump(known_values(), f, indent=1)
     np.savez_compressed(os.path.join(HERE, "avx2_order.npz"), **avx2_order())
     np.savez_compressed(os.path.join(HERE, "ivfpq_small.npz"), **ivfpq_small())
+    fdb_files()
     print("golden fixtures written to", HERE)
 
 
