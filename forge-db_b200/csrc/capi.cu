@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <memory>
 #include <new>
 #include <numeric>
@@ -915,6 +916,114 @@ int fdb_bf_remove(fdb_bf* h, uint64_t id, int* removed) {
         h->sharded = false;
         h->shard_world = 1;
         h->dirty = true;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// IVFPQIndexBuilder (src/index/ivf_pq_builder.rs)
+// ---------------------------------------------------------------------------
+void fdb_builder_defaults(fdb_builder_opts* o) {
+    if (!o) return;
+    std::memset(o, 0, sizeof(*o));
+    o->metric = FDB_METRIC_EUCLIDEAN;
+    o->auto_tune = 1;
+    o->target_recall = -1.0f;
+    o->nprobe = 1;
+    o->rerank_factor = 1;
+}
+
+static void builder_plan(const fdb_builder_opts& o, size_t n, size_t dim, size_t* clusters_out,
+                         size_t* m_out, size_t* nprobe_out, size_t* mb_out) {
+    // auto_tune_clusters: explicit, else round(sqrt(n)), clamped to
+    // [min(256, n), min(65536, n)] when auto-tuning
+    size_t clusters = o.num_clusters;
+    if (clusters == 0) {
+        const size_t sq = (size_t)std::round(std::sqrt((double)n));
+        clusters = o.auto_tune ? std::min(std::max(sq, std::min<size_t>(256, n)),
+                                          std::min<size_t>(65536, n))
+                               : sq;
+    }
+    // auto_tune_subvectors: explicit, else dim / 4 (must divide), or with
+    // auto-tuning the largest divisor of dim not above dim / 4 (1 at least)
+    size_t m = o.num_subvectors;
+    if (m == 0) {
+        const size_t target = dim / 4;
+        if (!o.auto_tune) {
+            FDB_REQUIRE(target > 0 && dim % target == 0, FDB_ERR_INVALID_ARG,
+                        "invalid parameter: default num_subvectors " + std::to_string(target) +
+                            " does not divide dimension " + std::to_string(dim));
+            m = target;
+        } else {
+            m = 1;
+            for (size_t c = target; c >= 1; --c)
+                if (dim % c == 0) { m = c; break; }
+        }
+    }
+    // auto_tune_nprobe: an explicit nprobe > 1 (at most the clusters), else a
+    // fraction of the clusters by target recall (f32 arithmetic), else 1
+    size_t nprobe = 1;
+    if (o.nprobe > 1) {
+        nprobe = std::min(o.nprobe, clusters);
+    } else if (o.target_recall >= 0.0f) {
+        const float r = std::min(std::max(o.target_recall, 0.0f), 1.0f);
+        const float c = (float)clusters;
+        size_t p = 1;
+        if (r >= 0.95f) p = (size_t)std::ceil(c * 0.1f);
+        else if (r >= 0.9f) p = (size_t)std::ceil(c * 0.05f);
+        else if (r >= 0.8f) p = (size_t)std::ceil(c * 0.02f);
+        nprobe = std::min(std::max<size_t>(p, 1), std::max<size_t>(clusters, 1));
+    }
+    FDB_REQUIRE(clusters <= n, FDB_ERR_INSUFFICIENT_VECTORS,
+                "insufficient vectors: required " + std::to_string(clusters) + ", got " +
+                    std::to_string(n));
+    FDB_REQUIRE(m > 0 && dim % m == 0, FDB_ERR_INVALID_ARG,
+                "invalid parameter: vector dimension " + std::to_string(dim) +
+                    " must be divisible by num_subvectors " + std::to_string(m));
+    // estimate_memory_mb: codes + ids + centroids + codebooks, whole MiB
+    const size_t bytes = n * m + n * 8 + clusters * dim * 4 + m * 256 * (dim / m) * 4;
+    *clusters_out = clusters;
+    *m_out = m;
+    *nprobe_out = nprobe;
+    if (mb_out) *mb_out = bytes / (1024 * 1024);
+}
+
+int fdb_builder_plan(const fdb_builder_opts* o, size_t n, size_t dim, size_t* num_clusters,
+                     size_t* num_subvectors, size_t* nprobe, size_t* estimated_mb) {
+    return guarded([&] {
+        FDB_REQUIRE(o && num_clusters && num_subvectors && nprobe, FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        FDB_REQUIRE(n > 0, FDB_ERR_EMPTY_VECTOR_SET,
+                    "empty vector set: operation requires at least one vector");
+        builder_plan(*o, n, dim, num_clusters, num_subvectors, nprobe, estimated_mb);
+    });
+}
+
+int fdb_builder_build(fdb_ctx* ctx, const fdb_builder_opts* o, const float* x,
+                      const uint64_t* ids, size_t n, size_t dim, const fdb_train_opts* train,
+                      fdb_ivfpq** out) {
+    return guarded([&] {
+        FDB_REQUIRE(o && out, FDB_ERR_INVALID_ARG, "NULL argument");
+        FDB_REQUIRE(x, FDB_ERR_INVALID_ARG, "invalid parameter: vectors are required");
+        FDB_REQUIRE(n > 0, FDB_ERR_EMPTY_VECTOR_SET,
+                    "empty vector set: operation requires at least one vector");
+        FDB_REQUIRE(ctx, FDB_ERR_INVALID_ARG, "NULL context");
+        size_t clusters = 0, m = 0, nprobe = 1, mb = 0;
+        builder_plan(*o, n, dim, &clusters, &m, &nprobe, &mb);
+        if (o->target_memory_mb && mb > o->target_memory_mb)
+            std::fprintf(stderr, "Warning: estimated memory %zuMB exceeds target %zuMB\n", mb,
+                         o->target_memory_mb);
+        fdb_ivfpq* h = nullptr;
+        int rc = fdb_ivfpq_build(ctx, x, ids, n, dim, clusters, m, o->metric, train, &h);
+        if (rc != FDB_OK) fail(rc, g_last_error);
+        std::unique_ptr<fdb_ivfpq> hold(h);
+        hold->nprobe.store(std::min(nprobe, hold->nlist), std::memory_order_relaxed);
+        if (o->enable_reranking) {
+            std::vector<uint64_t> iv(n);
+            for (size_t i = 0; i < n; ++i) iv[i] = ids ? ids[i] : (uint64_t)i;
+            DeviceGuard g(ctx->c.device);
+            ivfpq_enable_reranking(hold.get(), x, iv.data(), n, o->rerank_factor);
+        }
+        *out = hold.release();
     });
 }
 

@@ -73,6 +73,13 @@ class FileInfo(C.Structure):
                 ("rerank_factor", C.c_uint64)]
 
 
+class BuilderOpts(C.Structure):
+    _fields_ = [("num_clusters", C.c_size_t), ("num_subvectors", C.c_size_t),
+                ("metric", C.c_int), ("auto_tune", C.c_int), ("target_memory_mb", C.c_size_t),
+                ("target_recall", C.c_float), ("nprobe", C.c_size_t),
+                ("rerank_factor", C.c_size_t), ("enable_reranking", C.c_int)]
+
+
 class TrainOpts(C.Structure):
     _fields_ = [("ivf_sample", C.c_size_t), ("pq_sample", C.c_size_t),
                 ("ivf_iters", C.c_size_t), ("pq_iters", C.c_size_t),
@@ -151,6 +158,11 @@ _SIGS = {
     "fdb_bf_load": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
     "fdb_file_inspect": (C.c_int, [C.c_char_p, C.POINTER(FileInfo)]),
     "fdb_crc32": (C.c_uint32, [_vp, _sz]),
+    "fdb_builder_defaults": (None, [C.POINTER(BuilderOpts)]),
+    "fdb_builder_plan": (C.c_int, [C.POINTER(BuilderOpts), _sz, _sz, C.POINTER(_sz),
+                                   C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)]),
+    "fdb_builder_build": (C.c_int, [_vp, C.POINTER(BuilderOpts), _vp, _vp, _sz, _sz,
+                                    C.POINTER(TrainOpts), C.POINTER(_vp)]),
 }
 
 _lib = None
@@ -596,6 +608,78 @@ class IVFPQIndex:
             self.close()
         except Exception:
             pass
+
+
+class IVFPQIndexBuilder:
+    """IVFPQIndexBuilder (src/index/ivf_pq_builder.rs:56-331): fluent setters,
+    auto-tuned parameters, build() on the GPU."""
+
+    def __init__(self):
+        self.o = BuilderOpts()
+        lib().fdb_builder_defaults(C.byref(self.o))
+        self._vectors = None
+        self._ids = None
+
+    def vectors(self, vectors, ids=None):
+        self._vectors = _f32(vectors)
+        self._ids = None if ids is None else np.ascontiguousarray(ids, np.uint64)
+        return self
+
+    def num_clusters(self, n):
+        self.o.num_clusters = n
+        return self
+
+    def num_subvectors(self, m):
+        self.o.num_subvectors = m
+        return self
+
+    def metric(self, metric):
+        self.o.metric = metric
+        return self
+
+    def auto_tune(self, enable: bool):
+        self.o.auto_tune = int(bool(enable))
+        return self
+
+    def target_memory_mb(self, mb):
+        self.o.target_memory_mb = mb
+        return self
+
+    def target_recall(self, recall):
+        self.o.target_recall = min(max(float(recall), 0.0), 1.0)
+        return self
+
+    def nprobe(self, nprobe):
+        self.o.nprobe = nprobe
+        return self
+
+    def rerank_factor(self, factor):
+        self.o.rerank_factor = max(int(factor), 1)
+        return self
+
+    def enable_reranking(self, enable: bool):
+        self.o.enable_reranking = int(bool(enable))
+        return self
+
+    def plan(self, n: int, dim: int):
+        """(num_clusters, num_subvectors, nprobe, estimated MiB) for n x dim."""
+        c, m, p, mb = C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_size_t()
+        _check(lib().fdb_builder_plan(C.byref(self.o), n, dim, C.byref(c), C.byref(m),
+                                      C.byref(p), C.byref(mb)))
+        return c.value, m.value, p.value, mb.value
+
+    def build(self, ctx: Context | None = None, seed: int = 0, **draws) -> IVFPQIndex:
+        x = self._vectors
+        n = 0 if x is None else (x.shape[0] if x.ndim == 2 else 0)
+        dim = 0 if n == 0 else x.shape[1]
+        # the argument checks come before any device work (no context needed)
+        ctx = ctx or (default_context() if n else None)
+        t, keep = _train_opts(seed, **draws)
+        h = C.c_void_p()
+        _check(lib().fdb_builder_build(ctx.h if ctx else None, C.byref(self.o),
+                                       None if x is None else (_p(x) if n else C.c_void_p(1)),
+                                       _p(self._ids), n, dim, C.byref(t), C.byref(h)))
+        return IVFPQIndex(h, ctx)
 
 
 class BruteForceIndex:

@@ -297,6 +297,35 @@ int fdb_ivfpq_compact(fdb_ivfpq* h);
  * unusable and must be freed. */
 int fdb_ivfpq_rebuild(fdb_ivfpq* h, const fdb_train_opts* opts);
 
+/* ---- IVFPQIndexBuilder (src/index/ivf_pq_builder.rs:56-331) ------------ */
+/* Zero-initialise, then fdb_builder_defaults() gives IVFPQIndexBuilder::new()
+ * (auto_tune on, nprobe 1, rerank_factor 1, Euclidean, no targets). */
+typedef struct fdb_builder_opts {
+    size_t num_clusters;      /* 0: auto_tune_clusters (:269-282) */
+    size_t num_subvectors;    /* 0: auto_tune_subvectors (:284-311) */
+    int metric;               /* FDB_METRIC_* */
+    int auto_tune;
+    size_t target_memory_mb;  /* 0: none; over budget only warns (:238-248) */
+    float target_recall;      /* < 0: none; else clamped to [0, 1] (:160-163) */
+    size_t nprobe;            /* auto_tune_nprobe (:313-337) */
+    size_t rerank_factor;     /* max(1, .) (:171-174) */
+    int enable_reranking;     /* keep the build vectors as originals */
+} fdb_builder_opts;
+void fdb_builder_defaults(fdb_builder_opts* o);
+/* Host only: the parameters build() would use for n vectors of `dim` floats
+ * (the auto-tune rules and their validation: InsufficientVectors when
+ * clusters > n, InvalidParameter when dim % m != 0) and the memory estimate
+ * of estimate_memory_mb (:340-361) in MiB. */
+int fdb_builder_plan(const fdb_builder_opts* o, size_t n, size_t dim, size_t* num_clusters,
+                     size_t* num_subvectors, size_t* nprobe, size_t* estimated_mb);
+/* IVFPQIndexBuilder::build (:188-259): plan, IVFPQIndex::build, set_nprobe,
+ * enable_reranking(vectors, rerank_factor) when asked.  x NULL -> "vectors
+ * are required" (InvalidParameter); n == 0 -> EmptyVectorSet.  train (nullable)
+ * gives the training draws as for fdb_ivfpq_build. */
+int fdb_builder_build(fdb_ctx* ctx, const fdb_builder_opts* o, const float* x,
+                      const uint64_t* ids, size_t n, size_t dim, const fdb_train_opts* train,
+                      fdb_ivfpq** out);
+
 /* ---- BruteForceIndex (src/index/brute_force.rs:60-225) ------------------ */
 /* BruteForceIndex::new(metric) followed by add() of n rows
  * (brute_force.rs:67-80).  `ids` may be NULL (ids 0..n-1). */

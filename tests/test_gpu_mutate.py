@@ -370,3 +370,29 @@ def test_rebuild_equals_a_fresh_build(fg, ctx, small):
     fresh.enable_reranking(g["X"], g["ids"], 2)
     for a, b in zip(ix.batch_search_arrays(g["Q"], 10), fresh.batch_search_arrays(g["Q"], 10)):
         assert np.array_equal(a, b)
+
+
+# ---------------------------------------------------------------------------
+# IVFPQIndexBuilder
+# ---------------------------------------------------------------------------
+def test_builder_builds_like_the_reference(fg, ctx, orc):
+    """test_builder_basic / test_builder_with_reranking (ivf_pq_builder.rs:
+    367-420) on the device, against IVFPQIndex::build and the oracle."""
+    rng = np.random.default_rng(14)
+    X = rng.random((500, 32), dtype=np.float32)
+    ix = (fg.IVFPQIndexBuilder().vectors(X).num_clusters(8).num_subvectors(4).nprobe(4)
+          .build(ctx=ctx, seed=3))
+    assert ix.n_partitions() == 8 and ix.nprobe() == 4 and len(ix) == 500
+    same = fg.IVFPQIndex.build(X, 8, 4, ctx=ctx, seed=3)
+    for a, b in zip(ix.export(), same.export()):
+        assert np.array_equal(a, b)
+    rx = (fg.IVFPQIndexBuilder().vectors(X).num_clusters(8).num_subvectors(4)
+          .enable_reranking(True).rerank_factor(10).build(ctx=ctx, seed=3))
+    ox = orc.OracleMutableIVFPQ(*rx.export())
+    ox.enable_reranking(X, np.arange(500, dtype=np.uint64), 10)
+    Q = rng.random((30, 32), dtype=np.float32)
+    for q in Q:
+        res = rx.search(q, 10)
+        assert len(res) == 10
+        assert_topk_match(*_arrays([_single(res)], 10), *_arrays([ox.search(q, 10)], 10),
+                          "builder rerank")
