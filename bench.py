@@ -163,6 +163,10 @@ def config_dict(args, world, extra=None):
          "parallelism": (f"lists{world}" if args.mode == "lists" else f"replicas{world}"),
          "scan_mode": args.scan_mode,
          "l2": "flushed between steps (256 MB write outside the timed window)"}
+    if getattr(args, "rerank", 0):
+        d["rerank_factor"] = args.rerank
+    if getattr(args, "filter_every", 0):
+        d["filter"] = f"search_filtered, ids divisible by {args.filter_every} allowed"
     if extra:
         d.update(extra)
     return d
@@ -174,7 +178,7 @@ def config_dict(args, world, extra=None):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    if args.workload != "ivfpq":
+    if args.workload != "ivfpq" or args.rerank or args.filter_every:
         print(json.dumps({"impl": "reference", "workload": args.workload,
                           "unavailable": "the reference arm is defined for the headline "
                                          "workload (config C) only"}), flush=True)
@@ -229,6 +233,49 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def cpu_baseline_rows(ix, X, Q, args):
+    """CPU baselines of the re-ranked and filtered variants: the oracle's
+    batch_search_parallel + rerank_results (all threads), or its
+    single-query search_filtered loop (one thread, as the reference)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cents, cb, offs, ids, codes = ix.export()
+    ox = O.OracleMutableIVFPQ(cents, cb, offs, ids, codes)
+    ox.set_nprobe(args.nprobe)
+    if args.rerank:
+        ox.enable_reranking(X, np.arange(X.shape[0], dtype=np.uint64), args.rerank)
+    threads = O.max_threads()
+    if args.filter_every:
+        allowed = np.arange(0, X.shape[0], args.filter_every, dtype=np.uint64)
+        skip = (ids % args.filter_every != 0).astype(np.uint8)
+        f = (K * args.rerank if args.rerank else K) * 4
+        oid = np.empty(f, np.uint64)
+        od = np.empty(f, np.float32)
+        t0 = time.perf_counter()
+        nsample = 0
+        while time.perf_counter() - t0 < 10.0 and nsample < len(Q):
+            q = Q[nsample]
+            O.lib().orc_ivfpq_search_skip(ox.centroids, ox.codebooks, ox.nlist, ox.m, ox.dim,
+                                          ox.offsets, ox.ids, ox.codes, skip, ox.nprobe, q, f,
+                                          oid, od)
+            nsample += 1
+        dt = time.perf_counter() - t0
+        del allowed
+        return {"value": nsample / dt, "unit": "queries/s", "cores": 1, "kind": "port",
+                "sample": f"first {nsample} queries through the oracle's single-query "
+                          "search_filtered (ivf_pq.rs:692-831), one thread"}
+    t0 = time.time()
+    ox.batch_search_arrays(Q[:256], K, threads=threads)
+    per_q = (time.time() - t0) / 256
+    sample = int(min(len(Q), max(256, 12.0 / max(per_q, 1e-9))))
+    t0 = time.perf_counter()
+    ox.batch_search_arrays(Q[:sample], K, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"first {sample} of the 10k queries, batch_search_parallel + "
+                      f"rerank_results x{args.rerank} (oracle restatement), {threads} threads"}
+
+
 def cpu_baseline(ix, Q, nprobe):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -269,6 +316,8 @@ def run_ours(args, rank, world, local_rank, dist):
     build_s = time.time() - t0
     ix.set_nprobe(args.nprobe)
     ix.set_scan_mode(SCAN_MODES[args.scan_mode])
+    if args.rerank:
+        ix.enable_reranking(X, np.arange(N_BASE, dtype=np.uint64), args.rerank)
     if world > 1 and args.mode == "lists":
         ix.shard(rank, world)
         Qr = Q
@@ -288,12 +337,24 @@ def run_ours(args, rank, world, local_rank, dist):
     L = fg.lib()
     st = fg.Stats()
 
+    allowed = None
+    if args.filter_every:
+        allowed = np.arange(0, N_BASE, args.filter_every, dtype=np.uint64)
+        d_allowed = torch.from_numpy(allowed.view(np.int64)).to(dev)
+        h_allowed = torch.from_numpy(allowed.view(np.int64)).pin_memory()
+
     def step_device(stats=True):
-        rc = L.fdb_ivfpq_batch_search_device(ix.h, C.c_void_p(dQ.data_ptr()), nq, K,
-                                             C.c_void_p(d_ids.data_ptr()),
-                                             C.c_void_p(d_d.data_ptr()),
-                                             C.c_void_p(d_c.data_ptr()),
-                                             C.byref(st) if stats else None)
+        if allowed is not None:
+            rc = L.fdb_ivfpq_batch_search_filtered_device(
+                ix.h, C.c_void_p(dQ.data_ptr()), nq, K, C.c_void_p(d_allowed.data_ptr()),
+                allowed.size, C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_d.data_ptr()),
+                C.c_void_p(d_c.data_ptr()), C.byref(st) if stats else None)
+        else:
+            rc = L.fdb_ivfpq_batch_search_device(ix.h, C.c_void_p(dQ.data_ptr()), nq, K,
+                                                 C.c_void_p(d_ids.data_ptr()),
+                                                 C.c_void_p(d_d.data_ptr()),
+                                                 C.c_void_p(d_c.data_ptr()),
+                                                 C.byref(st) if stats else None)
         fg._check(rc)
 
     # pinned host buffers for the end-to-end path
@@ -303,9 +364,16 @@ def run_ours(args, rank, world, local_rank, dist):
     h_c = torch.empty((nq,), dtype=torch.int32).pin_memory()
 
     def step_e2e():
-        rc = L.fdb_ivfpq_batch_search(ix.h, C.c_void_p(hQ.data_ptr()), nq, K,
-                                      C.c_void_p(h_ids.data_ptr()), C.c_void_p(h_d.data_ptr()),
-                                      C.c_void_p(h_c.data_ptr()), None)
+        if allowed is not None:
+            rc = L.fdb_ivfpq_batch_search_filtered(
+                ix.h, C.c_void_p(hQ.data_ptr()), nq, K, C.c_void_p(h_allowed.data_ptr()),
+                allowed.size, C.c_void_p(h_ids.data_ptr()), C.c_void_p(h_d.data_ptr()),
+                C.c_void_p(h_c.data_ptr()))
+        else:
+            rc = L.fdb_ivfpq_batch_search(ix.h, C.c_void_p(hQ.data_ptr()), nq, K,
+                                          C.c_void_p(h_ids.data_ptr()),
+                                          C.c_void_p(h_d.data_ptr()),
+                                          C.c_void_p(h_c.data_ptr()), None)
         fg._check(rc)
 
     for _ in range(max(3, args.warmup)):
@@ -430,9 +498,17 @@ def run_ours(args, rank, world, local_rank, dist):
         "roofline": roofline,
         "clocks": clk.summary(),
     }
+    if allowed is not None:
+        # the filter's own launches per step: radix sort of the allowed ids
+        # (10 passes over 64-bit keys) and the row bitmap
+        line["gpu_launches"] += args.steps * 11
+        line["e2e"]["h2d_bytes_per_step"] += int(allowed.nbytes)
     if world == 1 and not args.no_cpu_baseline:
-        cb, _ = cpu_baseline(ix, Q, args.nprobe)
-        line["cpu_baseline"] = cb
+        if args.rerank or args.filter_every:
+            line["cpu_baseline"] = cpu_baseline_rows(ix, X, Q, args)
+        else:
+            cb, _ = cpu_baseline(ix, Q, args.nprobe)
+            line["cpu_baseline"] = cb
     print(json.dumps(line), flush=True)
 
 
@@ -637,6 +713,85 @@ def run_ours_train(args, rank, world, local_rank, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_ours_insert(args, rank, world, local_rank, dist):
+    """insert_batch (ivf_pq.rs:1731-1773): a config C index built on the
+    first N - n vectors takes the last n in one call (assignment, residual
+    PQ encoding, list re-layout and the derived tables on the device).  One
+    step = one insert_batch of n vectors into a fresh copy of the index."""
+    import torch
+    import forgegpu as fg
+    if world > 1:
+        raise SystemExit("the insert workload runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    ctx = fg.Context(local_rank)
+    X, Q = make_data()
+    n_new = args.insert_n
+    base, new = X[:-n_new], X[-n_new:]
+    new_ids = np.arange(N_BASE - n_new, N_BASE, dtype=np.uint64)
+    path = os.path.join("/tmp", f"fdb_insert_base_{os.getpid()}.fdb")
+    ix = fg.IVFPQIndex.build(base, NLIST, M, ctx=ctx, seed=SEED)
+    ix.save(path)  # each step inserts into a fresh copy of the same index
+    t0 = time.perf_counter()
+    fg.IVFPQIndex.load(path, ctx=ctx).close()
+    load_s = time.perf_counter() - t0
+    times = []
+    with ClockSampler(nvml_index(local_rank)) as clk:
+        for s_ in range(args.warmup + args.steps):
+            cp = fg.IVFPQIndex.load(path, ctx=ctx)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            cp.insert_batch(new, new_ids)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            if s_ >= args.warmup:
+                times.append(dt)
+            if s_ == args.warmup + args.steps - 1:
+                last = cp
+            else:
+                cp.close()
+    os.remove(path)
+    # parity sample: the inserted rows' codes against the oracle's encoding
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cents, cb, offs, ids, codes = last.export()
+    pos = np.searchsorted(np.sort(ids), new_ids[:2000])
+    order = np.argsort(ids)
+    rows = order[pos]
+    a = O.assign(new[:2000], cents)
+    resid = (new[:2000] - cents[a]).astype(np.float32)
+    ok = bool(np.array_equal(O.pq_encode(cb, resid), codes[rows]))
+    # CPU baseline: the reference's insert_batch is one vector at a time on
+    # one thread: nearest centroid, residual, encode
+    cs = 3000
+    t0 = time.perf_counter()
+    a = O.assign(new[:cs], cents, threads=1)
+    O.pq_encode(cb, (new[:cs] - cents[a]).astype(np.float32), threads=1)
+    cpu = cs / (time.perf_counter() - t0)
+    mean_s = statistics.mean(times)
+    line = {
+        "metric": "insert_batch throughput into the config C index (vectors/s)",
+        "value": n_new / mean_s, "unit": "vectors/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * mean_s, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "ivfpq_insert", "n_base": N_BASE - n_new, "n_insert": n_new,
+                   "dim": DIM, "nlist": NLIST, "m": M, "data": DATA_NOTE,
+                   "timing": "wall clock around the call, device synchronised on both sides "
+                             "(the call includes host steps: list offsets, id mirror)",
+                   "load_fdb_s": round(load_s, 3),
+                   "sample_checks": {"inserted_codes_match_oracle": ok, "rows": 2000}},
+        "e2e": {"value": n_new / mean_s, "unit": "vectors/s",
+                "h2d_bytes_per_step": int(new.nbytes + new_ids.nbytes),
+                "d2h_bytes_per_step": int(n_new * 4)},
+        "gpu_launches": None,
+        "cpu_baseline": {"value": cpu, "unit": "vectors/s", "cores": 1, "kind": "port",
+                         "sample": f"oracle nearest-centroid + residual encode of {cs} "
+                                   "vectors on one thread (insert_batch's per-vector loop, "
+                                   "without the list appends)"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -652,9 +807,19 @@ def main():
                          "(for ncu --profile-from-start off)")
     ap.add_argument("--scan-mode", default="auto", choices=list(SCAN_MODES),
                     help="IVF-PQ scan mode (auto picks the tensor-core list scan here)")
-    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "ivfpq_d", "bf", "train"],
+    ap.add_argument("--workload", default="ivfpq",
+                    choices=["ivfpq", "ivfpq_d", "bf", "train", "insert"],
                     help="ivfpq: config C (the headline); ivfpq_d: config D; bf: config B; "
-                         "train: config E (k-means 1M x 768 -> 4096, PQ M 96, encode)")
+                         "train: config E (k-means 1M x 768 -> 4096, PQ M 96, encode); "
+                         "insert: insert_batch into a config C index")
+    ap.add_argument("--rerank", type=int, default=0,
+                    help="IVF-PQ: enable_reranking with this rerank_factor (fetch k*F, "
+                         "exact sqrt(L2^2) re-ranking on the device)")
+    ap.add_argument("--filter-every", type=int, default=0,
+                    help="IVF-PQ: batch search_filtered with the ids divisible by this "
+                         "number allowed")
+    ap.add_argument("--insert-n", type=int, default=100_000,
+                    help="insert workload: vectors inserted into the config C index")
     ap.add_argument("--bf-metric", default="l2sq", choices=["l2sq", "dot", "cosine", "l2"])
     ap.add_argument("--bf-n", type=int, default=1_000_000, help="rows (smaller for profiling)")
     ap.add_argument("--bf-nq", type=int, default=10_000, help="queries (smaller for profiling)")
@@ -685,6 +850,8 @@ def main():
             run_ours_bf(args, rank, world, local_rank, dist)
         elif args.workload == "train":
             run_ours_train(args, rank, world, local_rank, dist)
+        elif args.workload == "insert":
+            run_ours_insert(args, rank, world, local_rank, dist)
         else:
             run_ours(args, rank, world, local_rank, dist)
     finally:

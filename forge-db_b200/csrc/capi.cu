@@ -818,6 +818,36 @@ int fdb_ivfpq_batch_search_filtered(fdb_ivfpq* h, const float* queries, size_t n
     });
 }
 
+int fdb_ivfpq_batch_search_filtered_device(fdb_ivfpq* h, const float* d_queries, size_t nq,
+                                           size_t k, const uint64_t* d_allowed_ids,
+                                           size_t n_allowed, uint64_t* d_ids, float* d_dists,
+                                           uint32_t* d_counts, fdb_stats* stats) {
+    return guarded([&] {
+        if (stats) std::memset(stats, 0, sizeof(*stats));
+        FDB_REQUIRE(h && (nq == 0 || d_queries) && (nq == 0 || k == 0 || (d_ids && d_dists)) &&
+                        (n_allowed == 0 || d_allowed_ids),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        if (nq == 0 || k == 0) return;
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        cudaStream_t s = h->ctx->c.stream;
+        if (n_allowed == 0) {  // no results: padding only
+            const std::vector<float> inf(nq * k, INFINITY);
+            FDB_CUDA(cudaMemsetAsync(d_ids, 0xff, nq * k * 8, s));
+            FDB_CUDA(cudaMemcpyAsync(d_dists, inf.data(), nq * k * 4, cudaMemcpyHostToDevice, s));
+            if (d_counts) FDB_CUDA(cudaMemsetAsync(d_counts, 0, nq * 4, s));
+            FDB_CUDA(cudaStreamSynchronize(s));
+        } else {
+            const size_t take = std::min(h->nprobe.load(std::memory_order_relaxed), h->nlist);
+            ivfpq_sync_state(h);
+            const uint32_t* skip = ivfpq_filter_bitmap(h, d_allowed_ids, n_allowed, true);
+            ivfpq_search_dev(h, d_queries, nq, k, ORDER_FAST4, take, d_ids, d_dists, d_counts,
+                             stats, skip, 4);
+        }
+        FDB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
 int fdb_ivfpq_insert_batch(fdb_ivfpq* h, const float* x, const uint64_t* ids, size_t n,
                            size_t dim) {
     return guarded([&] {

@@ -466,9 +466,9 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         const uint64_t* lend = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
         // Tensor mode: lists scored on the tensor cores into a shortlist,
         // exact rescoring + certification; failures are re-scanned exactly.
-        // (a per-call filter goes through the table or exact scan; tombstoned
-        // rows are +inf in the tensor scan's ||rhat||^2)
-        const bool tensor = ivf_tc_eligible(h, k) && !call_skip &&
+        // (rows a call skips -- tombstones, filters -- are +inf in the
+        // tensor scan's ||rhat||^2 and never admitted)
+        const bool tensor = ivf_tc_eligible(h, k) &&
                             (h->scan_mode == FDB_SCAN_TENSOR ||
                              (h->scan_mode == FDB_SCAN_AUTO && nq >= 256));
         // Table mode: approximate scan into a shortlist of kp keys, then
@@ -497,9 +497,17 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
             h->s_flags.ensure(nq + 1);
             double pass_ms = 0.0;
             std::vector<uint32_t> fail_cnt;
-            const uint32_t nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend,
-                                                 h->s_keys.p, h->s_flags.p, h->s_stat.p,
-                                                 st ? &pass_ms : nullptr, &fail_cnt);
+            h->tc_colv = call_skip ? ivfpq_call_colv(h, call_skip) : nullptr;
+            uint32_t nflag = 0;
+            try {
+                nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend, h->s_keys.p,
+                                      h->s_flags.p, h->s_stat.p, st ? &pass_ms : nullptr,
+                                      &fail_cnt);
+            } catch (...) {
+                h->tc_colv = nullptr;
+                throw;
+            }
+            h->tc_colv = nullptr;
             if (st) st->kernel_ms = pass_ms;
             tm.mark();
             // exact re-scan of the lists that failed, merged with the certified rest

@@ -243,7 +243,10 @@ bool ivfpq_delete(fdb_ivfpq* h, uint64_t id);
 size_t ivfpq_live_len(const fdb_ivfpq* h);
 void ivfpq_compact(fdb_ivfpq* h);
 void ivfpq_insert_batch(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_host, size_t n);
-const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed_host, size_t na);
+const float* ivfpq_call_colv(fdb_ivfpq* h, const uint32_t* skip);
+// allowed: host array, or a device array when on_device
+const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed, size_t na,
+                                    bool on_device = false);
 // persist.cu: .fdb files
 uint32_t crc32(const uint8_t* p, size_t n);
 void ivfpq_save(fdb_ivfpq* h, const char* path);
@@ -342,6 +345,10 @@ struct fdb_ivfpq {
     std::vector<std::pair<uint64_t, uint32_t>> id_index;  // (id, row) ascending, lazy
     bool id_index_ok = false;
     fdb::DevBuf<uint32_t> f_skip;       // per-call filter bitmap (search_filtered)
+    fdb::DevBuf<uint64_t> f_sorted;     // allowed ids and their sorted copy
+    fdb::DevBuf<uint8_t> f_tmp;         // radix-sort scratch
+    fdb::DevBuf<float> f_colv;          // tensor scan ||rhat||^2 with a call's filter
+    const float* tc_colv = nullptr;     // set for one call: overrides dnorm
     std::mutex mu;
     // per-call scratch
     fdb::DevBuf<float> s_q, s_coarse, s_qT, s_pdist;

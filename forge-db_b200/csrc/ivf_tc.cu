@@ -847,9 +847,9 @@ constexpr int CERT_WARPS = 8;
 // Two warps per query, 32 shortlisted codes each: the codes rescored with
 // exact_adc (the reference's arithmetic), their exact keys and lists kept for
 // certify_kernel; then the query's first warp writes the k best and the exact
-// k-th distance dk.
+// k-th distance dk.  P = 1 for k <= 32, 2 for k <= 64.
 constexpr int RS_QUERIES = CERT_WARPS / 2;  // queries per block
-template <int ORDER>
+template <int ORDER, int P>
 __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) {
     __shared__ uint64_t keys[RS_QUERIES][LIST_K];
     __shared__ uint64_t buf[RS_QUERIES * 64];
@@ -882,7 +882,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
     }
     __syncthreads();
     if (!qok || h != 0) return;
-    WarpTopK<1> tk;
+    WarpTopK<P> tk;
     tk.init(r.k, buf + lq * 64);
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -913,6 +913,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
 // queries marked bad are never certified.  A query with failing lists gets
 // them listed for an exact re-scan, and its output row becomes the seed: the
 // exact top-k of its shortlisted codes in the other lists.
+template <int P>
 __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) {
     __shared__ uint64_t buf[CERT_WARPS * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -993,7 +994,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
         }
     }
     if (lane == 0) r.fail_cnt[slot] = nf;
-    WarpTopK<1> seed;
+    WarpTopK<P> seed;
     seed.init(r.k, buf + warp * 64);
     const uint64_t s0 = drop0 ? KEY_NONE : ek[0], s1 = drop1 ? KEY_NONE : ek[1];
     if (__any_sync(0xffffffffu, s0 != KEY_NONE)) seed.merge32(s0);
@@ -1020,6 +1021,7 @@ __global__ void expand_units_kernel(int nflag, int take, const uint32_t* __restr
 
 // One warp per flag slot: the query's seed (its out_keys row) and the exact
 // top-k of each of its re-scanned lists, merged into its out_keys row.
+template <int P>
 __global__ void __launch_bounds__(256)
     merge_units_kernel(int nflag, int k, const uint32_t* __restrict__ flag_list,
                        const uint32_t* __restrict__ uoff, const uint64_t* __restrict__ unit_keys,
@@ -1029,7 +1031,7 @@ __global__ void __launch_bounds__(256)
     const int f = blockIdx.x * 8 + warp;
     if (f >= nflag) return;
     uint64_t* row = out_keys + (size_t)flag_list[f] * k;
-    WarpTopK<1> tk;
+    WarpTopK<P> tk;
     tk.init(k, buf + warp * 64);
     tk.ingest(row, k);
     for (uint32_t u = uoff[f]; u < uoff[f + 1]; ++u) tk.ingest(unit_keys + (size_t)u * k, k);
@@ -1121,7 +1123,7 @@ int bits_for(uint32_t v) {
 // host entry points
 // ---------------------------------------------------------------------------
 bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k) {
-    return h->dec16.p != nullptr && k >= 1 && k <= 32;
+    return h->dec16.p != nullptr && k >= 1 && k <= (size_t)ivtc::LIST_K;
 }
 
 // Decoded codes and their norms in the padded list layout, per-list bounds
@@ -1282,7 +1284,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.pair_q = h->t_pq.p;
     p.pair_rn = h->t_rn.p;
     p.pair_s2 = h->t_s2.p;
-    p.colv = h->dnorm.p;
+    p.colv = h->tc_colv ? h->tc_colv : h->dnorm.p;
     p.colmax = h->tc_colmax;
     p.dump = h->t_dump.p;
     p.seg = h->t_seg.p;
@@ -1353,14 +1355,21 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.dk = h->t_dk.p;
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
     const unsigned rgrid = (unsigned)((nq + RS_QUERIES - 1) / RS_QUERIES);
-    if (order == ORDER_LANE8) rescore_kernel<ORDER_LANE8><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
-    else rescore_kernel<ORDER_FAST4><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+    const bool p2 = k > 32;
+    if (order == ORDER_LANE8) {
+        if (p2) rescore_kernel<ORDER_LANE8, 2><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+        else rescore_kernel<ORDER_LANE8, 1><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+    } else {
+        if (p2) rescore_kernel<ORDER_FAST4, 2><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+        else rescore_kernel<ORDER_FAST4, 1><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+    }
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the answer's k-th distance is at most the smallest exact k-th of any device
         FDB_NCCL(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s));
     }
-    certify_kernel<<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
     FDB_LAUNCH_CHECK();
 }
 
@@ -1469,8 +1478,12 @@ void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, ui
         e.btab = nullptr;
         launch_scan(s, e, order);
     }
-    ivtc::merge_units_kernel<<<(nflag + 7) / 8, 256, 0, s>>>(
-        (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
+    if (k > 32)
+        ivtc::merge_units_kernel<2><<<(nflag + 7) / 8, 256, 0, s>>>(
+            (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
+    else
+        ivtc::merge_units_kernel<1><<<(nflag + 7) / 8, 256, 0, s>>>(
+            (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
     FDB_LAUNCH_CHECK();
     // (the offsets came from pageable memory: the copy call returned once they
     // were staged, so the vector may go)

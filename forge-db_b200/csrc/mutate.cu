@@ -431,25 +431,44 @@ void ivfpq_insert_batch(fdb_ivfpq* h, const float* x_host, const uint64_t* ids_h
     relayout_done(h);
 }
 
+// The tensor scan's ||rhat||^2 for one filtered call: the index's values
+// with +inf on every row the call skips (so the filter costs one copy of
+// 4 bytes per padded row, not a change of the scan).
+const float* ivfpq_call_colv(fdb_ivfpq* h, const uint32_t* skip) {
+    cudaStream_t s = h->ctx->c.stream;
+    h->f_colv.ensure(h->dnorm.n);
+    FDB_CUDA(cudaMemcpyAsync(h->f_colv.p, h->dnorm.p, h->dnorm.bytes(), cudaMemcpyDeviceToDevice,
+                             s));
+    mask_dead_kernel<<<(unsigned)h->nlist, 256, 0, s>>>(skip, h->offs.p, h->tc_pstart.p,
+                                                        h->f_colv.p);
+    FDB_LAUNCH_CHECK();
+    return h->f_colv.p;
+}
+
 // Per-call skip bitmap of search_filtered: dead rows and rows whose id is
 // not allowed.  Returns the device bitmap (in h->f_skip).
-const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed_host, size_t na) {
+const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed, size_t na,
+                                    bool on_device) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
-    DevBuf<uint64_t> a(na), b(na);
-    FDB_CUDA(cudaMemcpyAsync(a.p, allowed_host, na * 8, cudaMemcpyHostToDevice, s));
+    FDB_REQUIRE(na < (1ull << 31), FDB_ERR_UNSUPPORTED, "at most 2^31-1 allowed ids");
+    h->f_sorted.ensure(2 * na);
+    uint64_t* a = h->f_sorted.p;
+    uint64_t* b = h->f_sorted.p + na;
+    FDB_CUDA(cudaMemcpyAsync(a, allowed, na * 8,
+                             on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
     size_t tmp = 0;
-    FDB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, a.p, b.p, (int)na, 0, 64, s));
-    DevBuf<uint8_t> t(std::max<size_t>(tmp, 1));
-    FDB_CUDA(cub::DeviceRadixSort::SortKeys(t.p, tmp, a.p, b.p, (int)na, 0, 64, s));
+    FDB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, a, b, (int)na, 0, 64, s));
+    h->f_tmp.ensure(std::max<size_t>(tmp, 1));
+    FDB_CUDA(cub::DeviceRadixSort::SortKeys(h->f_tmp.p, tmp, a, b, (int)na, 0, 64, s));
     const size_t nw = words_for(h->n_total);
     h->f_skip.ensure(std::max<size_t>(nw, 1));
     if (nw) {
-        filter_bitmap_kernel<<<grid_for(nw), 256, 0, s>>>(h->ids.p, h->n_total, b.p, na,
-                                                           h->dead.p, h->f_skip.p);
+        filter_bitmap_kernel<<<grid_for(nw), 256, 0, s>>>(h->ids.p, h->n_total, b, na,
+                                                           h->n_tomb ? h->dead.p : nullptr,
+                                                           h->f_skip.p);
         FDB_LAUNCH_CHECK();
     }
-    FDB_CUDA(cudaStreamSynchronize(s));
     return h->f_skip.p;
 }
 

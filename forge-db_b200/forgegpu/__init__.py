@@ -145,6 +145,8 @@ _SIGS = {
     "fdb_ivfpq_enable_reranking": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz]),
     "fdb_ivfpq_search_filtered": (C.c_int, [_vp, _vp, _sz, _vp, _sz, _vp, _vp, C.POINTER(_sz)]),
     "fdb_ivfpq_batch_search_filtered": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp, _vp]),
+    "fdb_ivfpq_batch_search_filtered_device": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp,
+                                                         _vp, C.POINTER(Stats)]),
     "fdb_ivfpq_insert_batch": (C.c_int, [_vp, _vp, _vp, _sz, _sz]),
     "fdb_ivfpq_delete": (C.c_int, [_vp, C.c_uint64, C.POINTER(C.c_int)]),
     "fdb_ivfpq_num_tombstones": (_sz, [_vp]),

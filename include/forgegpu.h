@@ -89,10 +89,10 @@ typedef struct fdb_stats {
  * per-query table, keeps a shortlist of max(32, 2k) candidates, recomputes
  * their distances exactly, and certifies the result with a worst-case
  * rounding bound; a query that fails the bound is re-scanned in EXACT mode.
- * TENSOR (k <= 16, dim <= 128 after padding to 64) groups the probed
- * (query, list) pairs by list and scores them on the tcgen05 tensor cores
- * against fp16 codes decoded at build time, keeps a shortlist of 32, and
- * rescores and certifies it the same way.  AUTO picks TENSOR for batches of
+ * TENSOR (k <= 64 -- with re-ranking, k * rerank_factor -- and dim <= 128
+ * after padding to 64) groups the probed (query, list) pairs by list and
+ * scores them on the tcgen05 tensor cores against fp16 codes decoded at build
+ * time, keeps a shortlist of 64, and rescores and certifies it the same way.  AUTO picks TENSOR for batches of
  * 256+ queries where it applies, else TABLES for subvectors of 8+ floats and
  * k <= 128, else EXACT. */
 #define FDB_SCAN_AUTO 0
@@ -272,6 +272,12 @@ int fdb_ivfpq_search_filtered(fdb_ivfpq* h, const float* query, size_t k,
 int fdb_ivfpq_batch_search_filtered(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
                                     const uint64_t* allowed_ids, size_t n_allowed,
                                     uint64_t* ids, float* dists, uint32_t* counts);
+/* The same on DEVICE buffers of this context's device (queries, allowed ids
+ * and outputs), enqueued on the context stream; returns when done. */
+int fdb_ivfpq_batch_search_filtered_device(fdb_ivfpq* h, const float* d_queries, size_t nq,
+                                           size_t k, const uint64_t* d_allowed_ids,
+                                           size_t n_allowed, uint64_t* d_ids, float* d_dists,
+                                           uint32_t* d_counts, fdb_stats* stats);
 /* insert_batch (ivf_pq.rs:1731-1773): each vector goes to its nearest list
  * (first minimum), its residual is PQ-encoded and appended to that list, a
  * tombstone on its id in that list is lifted, and with re-ranking on it

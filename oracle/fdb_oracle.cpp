@@ -672,6 +672,34 @@ void orc_ivfpq_batch_search(const float* cents, const float* cb, size_t nlist, s
                                 Q, nq, k, chunk, out_ids, out_d, counts, nthreads);
 }
 
+// rerank_results (src/index/ivf_pq.rs:556-582) for nq queries: candidate
+// row q holds cnt[q] PQ results (ascending); those whose id has an original
+// vector (rr_ids ascending, rr_x in that order) get sqrt(L2^2) in the
+// euclidean_distance_squared order, are stable-sorted and cut to k.
+void orc_rerank(const float* Q, size_t nq, size_t dim, const uint64_t* cand, const uint32_t* cnt,
+                size_t fetch, const uint64_t* rr_ids, const float* rr_x, size_t nrr, size_t k,
+                uint64_t* out_ids, float* out_d, uint32_t* out_cnt, int nthreads) {
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+    for (size_t q = 0; q < nq; ++q) {
+        std::vector<std::pair<float, uint64_t>> r;
+        for (size_t i = 0; i < cnt[q]; ++i) {
+            const uint64_t id = cand[q * fetch + i];
+            const uint64_t* it = std::lower_bound(rr_ids, rr_ids + nrr, id);
+            if (it == rr_ids + nrr || *it != id) continue;
+            const float d = std::sqrt(l2sq(Q + q * dim, rr_x + (size_t)(it - rr_ids) * dim, dim));
+            r.push_back({d, id});
+        }
+        std::stable_sort(r.begin(), r.end(),
+                         [](const auto& a, const auto& b) { return a.first < b.first; });
+        const size_t c = std::min(k, r.size());
+        for (size_t i = 0; i < k; ++i) {
+            out_ids[q * k + i] = i < c ? r[i].second : UINT64_MAX;
+            out_d[q * k + i] = i < c ? r[i].first : INFINITY;
+        }
+        out_cnt[q] = (uint32_t)c;
+    }
+}
+
 // BruteForceIndex::batch_search -> search_parallel -> scan_range,
 // src/index/brute_force.rs:105-225.  Admission: fill to k, then replace the
 // max on strict '<'.  The 1000-row chunk heaps of search_parallel merge under

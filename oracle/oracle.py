@@ -71,6 +71,8 @@ def lib():
             "orc_ivfpq_batch_search_skip": (None, [_f32p, _f32p, _sz, _sz, _sz, _u64p, _u64p,
                                                    _u8p, _u8p, _sz, _f32p, _sz, _sz, _sz,
                                                    _u64p, _f32p, _u32p, C.c_int]),
+            "orc_rerank": (None, [_f32p, _sz, _sz, _u64p, _u32p, _sz, _u64p, _f32p, _sz, _sz,
+                                  _u64p, _f32p, _u32p, C.c_int]),
             "orc_bf_batch_search": (None, [_f32p, _u64p, _sz, _sz, C.c_int, _f32p, _sz, _sz,
                                            _u64p, _f32p, _u32p, C.c_int]),
             "orc_max_threads": (C.c_int, []),
@@ -378,6 +380,30 @@ class OracleMutableIVFPQ(OracleIVFPQ):
                                           self.dim, self.offsets, self.ids, self.codes,
                                           self.skip_mask(), self.nprobe, q, f, ids, d)
         return self._rerank(q, ids, d, cnt, k)
+
+    def batch_search_arrays(self, Q, k, threads=0):
+        """batch_search as (ids, dists, counts) arrays; re-ranking in C++."""
+        Q = _f32(Q)
+        nq = Q.shape[0]
+        f = self._fetch(k)
+        ids = np.empty((nq, f), np.uint64)
+        d = np.empty((nq, f), np.float32)
+        counts = np.empty(nq, np.uint32)
+        lib().orc_ivfpq_batch_search_skip(self.centroids, self.codebooks, self.nlist, self.m,
+                                          self.dim, self.offsets, self.ids, self.codes,
+                                          self.skip_mask(), self.nprobe, Q, nq, f, 0, ids, d,
+                                          counts, _threads(threads))
+        if self.rr is None:
+            return ids, d, counts
+        rid = np.array(sorted(self.rr), np.uint64)
+        rx = _f32(np.stack([self.rr[i] for i in rid.tolist()])) if rid.size else \
+            np.zeros((0, self.dim), np.float32)
+        oi = np.empty((nq, k), np.uint64)
+        od = np.empty((nq, k), np.float32)
+        oc = np.empty(nq, np.uint32)
+        lib().orc_rerank(Q, nq, self.dim, ids, counts, f, rid, rx, rid.size, k, oi, od, oc,
+                         _threads(threads))
+        return oi, od, oc
 
     def batch_search(self, Q, k, threads=0):
         Q = _f32(Q)

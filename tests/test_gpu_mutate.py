@@ -295,9 +295,11 @@ def test_insert_into_reranked_index(fg, ctx, orc, small):
 # filtered search
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("rerank", [False, True])
-def test_search_filtered_matches_oracle(fg, ctx, orc, small, rerank):
+@pytest.mark.parametrize("mode", [0, 3])  # AUTO (tables / exact here), TENSOR forced
+def test_search_filtered_matches_oracle(fg, ctx, orc, small, rerank, mode):
     g = small
     ix, ox = _pair(fg, ctx, orc, g, nprobe=8)
+    ix.set_scan_mode(mode)
     if rerank:
         ix.enable_reranking(g["X"], g["ids"], 3)
         ox.enable_reranking(g["X"], g["ids"], 3)
@@ -396,3 +398,45 @@ def test_builder_builds_like_the_reference(fg, ctx, orc):
         assert len(res) == 10
         assert_topk_match(*_arrays([_single(res)], 10), *_arrays([ox.search(q, 10)], 10),
                           "builder rerank")
+
+
+def test_batch_search_filtered_device_entry(fg, ctx, orc, small):
+    """The device-buffer filtered entry returns what the host entry does."""
+    import ctypes as C
+    import torch
+    g = small
+    ix, _ = _pair(fg, ctx, orc, g, nprobe=8)
+    ix.enable_reranking(g["X"], g["ids"], 2)
+    allowed = g["ids"][g["ids"] % 4 == 1]
+    Q = np.concatenate([g["Q"]] * 8)  # 320 queries: the tensor path in AUTO mode
+    hi, hd, hc = ix.batch_search_filtered_arrays(Q, 10, allowed)
+    dev = torch.device("cuda", ctx.device)
+    dQ = torch.from_numpy(np.ascontiguousarray(Q)).to(dev)
+    da = torch.from_numpy(allowed.view(np.int64)).to(dev)
+    di = torch.empty((len(Q), 10), dtype=torch.int64, device=dev)
+    dd = torch.empty((len(Q), 10), dtype=torch.float32, device=dev)
+    dc = torch.empty(len(Q), dtype=torch.int32, device=dev)
+    st = fg.Stats()
+    fg._check(fg.lib().fdb_ivfpq_batch_search_filtered_device(
+        ix.h, C.c_void_p(dQ.data_ptr()), len(Q), 10, C.c_void_p(da.data_ptr()), allowed.size,
+        C.c_void_p(di.data_ptr()), C.c_void_p(dd.data_ptr()), C.c_void_p(dc.data_ptr()),
+        C.byref(st)))
+    assert np.array_equal(di.cpu().numpy().view(np.uint64), hi)
+    assert np.array_equal(dd.cpu().numpy(), hd) and np.array_equal(dc.cpu().numpy(), hc)
+    assert st.lists_probed > 0
+    # no allowed id: padding only
+    fg._check(fg.lib().fdb_ivfpq_batch_search_filtered_device(
+        ix.h, C.c_void_p(dQ.data_ptr()), len(Q), 10, None, 0, C.c_void_p(di.data_ptr()),
+        C.c_void_p(dd.data_ptr()), C.c_void_p(dc.data_ptr()), None))
+    assert (dc.cpu().numpy() == 0).all() and torch.isinf(dd).all()
+
+
+@pytest.mark.parametrize("k", [33, 40, 64])
+def test_tensor_mode_k_above_32(fg, ctx, orc, small, k):
+    """k in 33..64 (re-ranked fetch sizes) on the tensor path: the shortlist
+    of 64 is certified or re-scanned, results equal the oracle's."""
+    g = small
+    ix, ox = _pair(fg, ctx, orc, g, nprobe=6)
+    ix.set_scan_mode(3)
+    Q = np.concatenate([g["Q"]] * 8)
+    _check_batch(ix, ox, Q, k, f"tensor k={k}")
