@@ -384,7 +384,7 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.barrier()
     torch.cuda.synchronize()
 
-    times, scan_ms, bytes_scanned, launches, rescans = [], [], [], 0, []
+    times, scan_ms, bytes_scanned, launches, rescans, extended = [], [], [], 0, [], []
     kern_ms, kern_scores = [], []
     stage = {"coarse_ms": [], "rescore_ms": [], "merge_ms": []}
     with ClockSampler(nvml_index(local_rank)) as clk:
@@ -407,6 +407,7 @@ def run_ours(args, rank, world, local_rank, dist):
             stage["rescore_ms"].append(st.rescore_ms)
             stage["merge_ms"].append(st.merge_ms)
             rescans.append(st.exact_rescans)
+            extended.append(st.extended)
             bytes_scanned.append(st.bytes_scanned)
             kern_ms.append(st.kernel_ms)
             kern_scores.append(st.kernel_scores)
@@ -414,9 +415,9 @@ def run_ours(args, rank, world, local_rank, dist):
             if st.kernel_scores < codes:
                 # tensor mode: transpose + coarse, select, pair keys, radix sort (4),
                 # segment offsets, residual rows, dump rows, scan (2), items, pass 1,
-                # pass-1 selection, pass 2, shortlist, certify, [exact re-scan],
-                # keys->ids, finalize
-                launches += 21 + (1 if st.exact_rescans else 0)
+                # pass-1 selection, pass 2, shortlist, rescore, certify, extend,
+                # [expand + exact re-scan + merge], keys->ids, finalize
+                launches += 23 + (3 if st.exact_rescans else 0)
             else:
                 # coarse, select, scan, [rescore (+ exact re-scan)], keys->ids, finalize
                 launches += 5 + (1 if st.rescore_ms > 0 else 0) + (1 if st.exact_rescans else 0)
@@ -490,7 +491,8 @@ def run_ours(args, rank, world, local_rank, dist):
             "recall_at_10": recall, "build_s": round(build_s, 2),
             "stage_ms": {k: round(statistics.mean(v), 4) for k, v in stage.items()},
             "scan_kernel_ms": round(statistics.mean(scan_ms), 4),
-            "exact_rescans_per_step": statistics.mean(rescans)}),
+            "exact_rescans_per_step": statistics.mean(rescans),
+            "extended_certificates_per_step": statistics.mean(extended)}),
         "e2e": {"value": e2e_value, "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4,
                 "d2h_bytes_per_step": nq * K * (8 + 4) + nq * 4},
@@ -580,6 +582,7 @@ def run_ours_bf(args, rank, world, local_rank, dist):
             times.append(e0.elapsed_time(e1))
             scan_ms.append(st.kernel_ms)
             rescans.append(st.exact_rescans)
+            extended.append(st.extended)
         for _ in range(args.steps):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)

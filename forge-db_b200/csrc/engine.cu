@@ -460,8 +460,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
             FDB_NCCL(ncclGroupEnd());
         }
         tm.mark();
-        h->s_stat.ensure(3);
-        FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 24, s));
+        h->s_stat.ensure(4);
+        FDB_CUDA(cudaMemsetAsync(h->s_stat.p, 0, 32, s));
         const uint64_t* lbeg = h->sharded ? h->shard_be.p : h->offs.p;
         const uint64_t* lend = h->sharded ? h->shard_be.p + nlist : h->offs.p + 1;
         // Tensor mode: lists scored on the tensor cores into a shortlist,
@@ -569,11 +569,12 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     else launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
     tm.mark();
     if (st) {
-        unsigned long long hs[3] = {0, 0, 0};
+        unsigned long long hs[4] = {0, 0, 0, 0};
         if (take > 0)
-            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 24, cudaMemcpyDeviceToHost, s));
+            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 32, cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
         st->lists_probed = hs[0];
+        st->extended = hs[3];
         st->codes_scanned = hs[1];
         st->bytes_scanned = hs[1] * h->m;
         size_t last = tm.ev.size() - 1;

@@ -205,18 +205,12 @@ __device__ __forceinline__ float adc_order(F lk, int m) {
     }
 }
 
-// Exact ADC of one code: every LUT entry recomputed as L2^2(fl(q - c) - b)
-// in the AVX2 order and summed in the requested order -- the same
-// operations, in the same order, as the exact-mode scan.
-template <int ORDER>
-__device__ __forceinline__ float exact_adc(const float* __restrict__ q,
-                                           const float* __restrict__ c,
-                                           const float* __restrict__ cb,
-                                           const uint8_t* __restrict__ code, int m, int sub) {
-    auto entry = [&](int s) -> float {
-        const float* b = cb + ((size_t)s * KSUB + code[s]) * sub;
-        const float* qs = q + s * sub;
-        const float* cs = c + s * sub;
+// One exact LUT entry: L2^2(fl(q_s - c_s) - b) in the AVX2 order, for
+// subspace s of length sub and codeword b.
+__device__ __forceinline__ float exact_lut_entry(const float* __restrict__ qs,
+                                                 const float* __restrict__ cs,
+                                                 const float* __restrict__ b, int sub) {
+    {
         float acc[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
@@ -254,8 +248,119 @@ __device__ __forceinline__ float exact_adc(const float* __restrict__ q,
             t = __fadd_rn(t, __fmul_rn(d, d));
         }
         return t;
+    }
+}
+
+// Exact ADC of one code: every LUT entry recomputed as L2^2(fl(q - c) - b)
+// in the AVX2 order and summed in the requested order -- the same
+// operations, in the same order, as the exact-mode scan.
+template <int ORDER>
+__device__ __forceinline__ float exact_adc(const float* __restrict__ q,
+                                           const float* __restrict__ c,
+                                           const float* __restrict__ cb,
+                                           const uint8_t* __restrict__ code, int m, int sub) {
+    auto entry = [&](int s) -> float {
+        return exact_lut_entry(q + s * sub, c + s * sub, cb + ((size_t)s * KSUB + code[s]) * sub,
+                               sub);
     };
     return adc_order<ORDER>(entry, m);
+}
+
+// The same value computed by a group of G lanes (G = 8, 16 or 32, m <= G,
+// the warp split into 32 / G groups that all call this together): lane gl
+// of the group computes LUT entry gl, and the entries are summed in the
+// requested order through shuffles, so every operation and its order are
+// those of exact_adc.  `code` is the group's code (may differ per group).
+// Every lane of the group returns the total.
+template <int ORDER, int G>
+__device__ __forceinline__ float group_exact_adc(const float* __restrict__ q,
+                                                 const float* __restrict__ c,
+                                                 const float* __restrict__ cb,
+                                                 const uint8_t* __restrict__ code, int m, int sub,
+                                                 int gl, bool active) {
+    float t = 0.0f;
+    if (active && gl < m)
+        t = exact_lut_entry(q + gl * sub, c + gl * sub,
+                            cb + ((size_t)gl * KSUB + code[gl]) * sub, sub);
+    auto at = [&](int i) { return __shfl_sync(0xffffffffu, t, i, G); };
+    if (ORDER == ORDER_LANE8) {
+        const int full = m & ~7;
+        float total = 0.0f;
+        if (full > 0) {
+            // acc_j = t_j + t_{j+8} + ... (lane j < 8), then acc_0 + ... + acc_7
+            float acc = t;
+            for (int i = 8; i < full; i += 8) {
+                const float o = __shfl_down_sync(0xffffffffu, t, i, G);
+                acc = __fadd_rn(acc, o);
+            }
+            total = __shfl_sync(0xffffffffu, acc, 0, G);
+#pragma unroll
+            for (int j = 1; j < 8; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, acc, j, G));
+        }
+        for (int i = full; i < m; ++i) total = __fadd_rn(total, at(i));
+        return total;
+    } else {
+        float sum = 0.0f;
+        int i = 0;
+        for (; i + 4 <= m; i += 4) {
+            const float g = __fadd_rn(__fadd_rn(__fadd_rn(at(i), at(i + 1)), at(i + 2)), at(i + 3));
+            sum = __fadd_rn(sum, g);
+        }
+        for (; i < m; ++i) sum = __fadd_rn(sum, at(i));
+        return sum;
+    }
+}
+
+// Exact distances of up to 32 codes, one per lane (row `pos` of `codes`, in
+// list `list`; `valid` false for none), computed by lane groups of G; each
+// lane gets its own code's distance.  dres: 32 floats of this warp's shared
+// memory.  Whole warp.
+template <int ORDER, int G>
+__device__ __forceinline__ float warp_exact_adc_g(const float* __restrict__ qv,
+                                                  const float* __restrict__ cents, int dim,
+                                                  const float* __restrict__ cb,
+                                                  const uint8_t* __restrict__ codes, int m,
+                                                  int sub, uint32_t pos, int list, bool valid,
+                                                  float* dres) {
+    constexpr int NG = 32 / G;  // codes per round
+    const int lane = threadIdx.x & 31, g = lane / G, gl = lane % G;
+    const unsigned any = __ballot_sync(0xffffffffu, valid);
+    for (int r0 = 0; r0 < 32; r0 += NG) {
+        const int c = r0 + g;  // the code this lane's group computes this round
+        const uint32_t cpos = __shfl_sync(0xffffffffu, pos, c);
+        const int clist = __shfl_sync(0xffffffffu, list, c);
+        const bool cval = (any >> c) & 1u;
+        if (!__any_sync(0xffffffffu, cval)) continue;
+        const float d = group_exact_adc<ORDER, G>(
+            qv, cents + (size_t)(cval ? clist : 0) * dim, cb, codes + (size_t)cpos * m, m, sub,
+            gl, cval);
+        if (gl == 0) dres[c] = d;
+    }
+    __syncwarp();
+    const float mine = dres[lane];
+    __syncwarp();
+    return valid ? mine : 0.0f;
+}
+
+template <int ORDER>
+__device__ __forceinline__ float warp_exact_adc(const float* __restrict__ qv,
+                                                const float* __restrict__ cents, int dim,
+                                                const float* __restrict__ cb,
+                                                const uint8_t* __restrict__ codes, int m, int sub,
+                                                uint32_t pos, int list, bool valid,
+                                                float* dres) {
+    if (m <= 8)
+        return warp_exact_adc_g<ORDER, 8>(qv, cents, dim, cb, codes, m, sub, pos, list, valid,
+                                          dres);
+    if (m <= 16)
+        return warp_exact_adc_g<ORDER, 16>(qv, cents, dim, cb, codes, m, sub, pos, list, valid,
+                                           dres);
+    if (m <= 32)
+        return warp_exact_adc_g<ORDER, 32>(qv, cents, dim, cb, codes, m, sub, pos, list, valid,
+                                           dres);
+    return valid ? exact_adc<ORDER>(qv, cents + (size_t)list * dim, cb, codes + (size_t)pos * m,
+                                    m, sub)
+                 : 0.0f;
 }
 
 template <int P>

@@ -369,6 +369,10 @@ struct fdb_ivfpq {
     fdb::DevBuf<float> t_rn, t_s2, t_tau;
     fdb::DevBuf<uint64_t> t_part, t_cand;
     fdb::DevBuf<unsigned> t_cand_cnt;
+    fdb::DevBuf<uint32_t> t_ext;        // [0] extended queries, then their indices
+    fdb::DevBuf<float> t_ext_thr, t_tadm;
+    fdb::DevBuf<unsigned> t_icnt;       // item counts per (kind, list) and their offsets
+    fdb::DevBuf<uint8_t> t_tmp2;        // scan scratch for the item offsets
 };
 
 struct fdb_bf {

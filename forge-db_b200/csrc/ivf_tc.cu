@@ -663,74 +663,84 @@ __global__ void plen_kernel(const uint32_t* __restrict__ vals, const unsigned* _
     plen[i] = len;
 }
 
-// Items of both passes, lists in `lorder`, one block.  An item is (list, up
-// to 128 pair rows, a run of at most CHUNK_TILES tiles of the list).  Pass 1
-// (dump) holds the pass-1 segments' whole lists and the pass-2 segments' first
-// tiles; pass 2 (filter) holds the pass-2 segments' other tiles.  items[0 ..
-// n1) are pass 1, items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
-constexpr int ITEM_THREADS = 1024;
-__global__ void __launch_bounds__(ITEM_THREADS)
-    build_items_kernel(const unsigned* __restrict__ poff, int nlist,
-                       const uint32_t* __restrict__ lorder, const uint64_t* __restrict__ lbeg,
-                       const uint64_t* __restrict__ lend, const uint32_t* __restrict__ pstart,
-                       Item* __restrict__ items, unsigned cap, uint32_t* __restrict__ range) {
-    typedef cub::BlockScan<unsigned, ITEM_THREADS> Scan;
-    __shared__ typename Scan::TempStorage tmp;
-    __shared__ unsigned carry;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    // kind 0: pass-1 segments, whole list; kind 1: pass-2 segments, first tile
-    // (both in pass 1); kind 2: pass-2 segments, tiles 1.. (pass 2)
-    for (int kind = 0; kind < 3; ++kind) {
-        const int seg = kind == 0 ? 0 : 1;
-        for (int base = 0; base < nlist; base += ITEM_THREADS) {
-            const int i = base + threadIdx.x;
-            unsigned cnt = 0, a0 = 0, len = 0;
-            uint32_t l = 0;
-            if (i < nlist) {
-                l = lorder[i];
-                a0 = poff[seg * nlist + l];
-                cnt = poff[seg * nlist + l + 1] - a0;
-                len = (unsigned)(lend[l] - lbeg[l]);
-            }
-            // codes [c_lo, c_hi) of the list this kind covers
-            const unsigned c_lo = kind == 2 ? (unsigned)TILE_N : 0u;
-            const unsigned c_hi = kind == 1 ? min(len, (unsigned)TILE_N) : len;
-            const unsigned span = c_hi > c_lo ? c_hi - c_lo : 0u;
-            const unsigned nrow = span > 0 ? (cnt + TILE_M - 1) / TILE_M : 0u;
-            const unsigned nchunk = (span + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
-            const unsigned nit = nrow * nchunk;
-            unsigned off, tot;
-            Scan(tmp).ExclusiveSum(nit, off, tot);
-            const unsigned at = carry + off;
-            for (unsigned t = 0; t < nit; ++t) {
-                const unsigned rb = t / nchunk, ch = t - rb * nchunk;
-                const unsigned c0 = c_lo + ch * CHUNK_TILES * TILE_N;
-                Item it;
-                it.a0 = a0 + rb * TILE_M;
-                it.na = min((unsigned)TILE_M, cnt - rb * TILE_M);
-                it.b0 = pstart[l] + c0;
-                it.nb = min((unsigned)(CHUNK_TILES * TILE_N), c_hi - c0);
-                it.tag0 = (uint32_t)lbeg[l] + c0;
-                it.col0 = c0;
-                it.pad[0] = it.pad[1] = 0;
-                if (at + t < cap) items[at + t] = it;
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) carry += tot;
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) {
-            // (the host sizes items[] for every case; cap only guards it)
-            if (kind == 1) {
-                range[0] = 0;
-                range[1] = min(carry, cap);
-                range[2] = min(carry, cap);
-            } else if (kind == 2) {
-                range[3] = min(carry, cap) - range[2];
-            }
-        }
-        __syncthreads();
+// Items of both passes, lists in `lorder`.  An item is (list, up to 128
+// pair rows, a run of at most CHUNK_TILES tiles of the list).  Pass 1 (dump)
+// holds the pass-1 segments' whole lists and the pass-2 segments' first
+// tiles; pass 2 (filter) holds the pass-2 segments' other tiles.  Slot
+// s = kind * nlist + i describes list lorder[i] for kind 0 (pass-1 segment,
+// whole list), 1 (pass-2 segment, first tile) or 2 (pass-2 segment, tiles
+// 1..).  item_count_kernel counts each slot's items, an exclusive sum places
+// them, item_fill_kernel writes them (one warp per slot): items[0 .. n1) are
+// pass 1, items[n1 .. n1 + n2) pass 2; range = {0, n1, n1, n2}.
+struct ItemSlot {
+    unsigned a0, cnt, c_lo, c_hi, nchunk;
+    uint32_t l;
+};
+
+__device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict__ poff, int nlist,
+                                              const uint32_t* __restrict__ lorder,
+                                              const uint64_t* __restrict__ lbeg,
+                                              const uint64_t* __restrict__ lend) {
+    const int kind = s / nlist, i = s - kind * nlist;
+    const int seg = kind == 0 ? 0 : 1;
+    ItemSlot t;
+    t.l = lorder[i];
+    t.a0 = poff[seg * nlist + t.l];
+    t.cnt = poff[seg * nlist + t.l + 1] - t.a0;
+    const unsigned len = (unsigned)(lend[t.l] - lbeg[t.l]);
+    // codes [c_lo, c_hi) of the list this kind covers
+    t.c_lo = kind == 2 ? (unsigned)TILE_N : 0u;
+    t.c_hi = kind == 1 ? min(len, (unsigned)TILE_N) : len;
+    const unsigned span = t.c_hi > t.c_lo ? t.c_hi - t.c_lo : 0u;
+    t.nchunk = (span + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
+    if (span == 0) t.cnt = 0;
+    return t;
+}
+
+__global__ void item_count_kernel(const unsigned* __restrict__ poff, int nlist,
+                                  const uint32_t* __restrict__ lorder,
+                                  const uint64_t* __restrict__ lbeg,
+                                  const uint64_t* __restrict__ lend, unsigned* __restrict__ counts) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s > 3 * nlist) return;
+    if (s == 3 * nlist) {  // the exclusive sum's total
+        counts[s] = 0;
+        return;
+    }
+    const ItemSlot t = item_slot(s, poff, nlist, lorder, lbeg, lend);
+    counts[s] = ((t.cnt + TILE_M - 1) / TILE_M) * t.nchunk;
+}
+
+__global__ void __launch_bounds__(256)
+    item_fill_kernel(const unsigned* __restrict__ poff, int nlist,
+                     const uint32_t* __restrict__ lorder, const uint64_t* __restrict__ lbeg,
+                     const uint64_t* __restrict__ lend, const uint32_t* __restrict__ pstart,
+                     const unsigned* __restrict__ ioff, Item* __restrict__ items, unsigned cap,
+                     uint32_t* __restrict__ range) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s = blockIdx.x * 8 + warp;
+    if (s == 0 && lane == 0) {
+        const unsigned n1 = min(ioff[2 * nlist], cap), n12 = min(ioff[3 * nlist], cap);
+        range[0] = 0;
+        range[1] = n1;
+        range[2] = n1;
+        range[3] = n12 - n1;
+    }
+    if (s >= 3 * nlist) return;
+    const ItemSlot t = item_slot(s, poff, nlist, lorder, lbeg, lend);
+    const unsigned at = ioff[s], nit = ioff[s + 1] - at;
+    for (unsigned u = lane; u < nit; u += 32) {
+        const unsigned rb = u / t.nchunk, ch = u - rb * t.nchunk;
+        const unsigned c0 = t.c_lo + ch * CHUNK_TILES * TILE_N;
+        Item it;
+        it.a0 = t.a0 + rb * TILE_M;
+        it.na = min((unsigned)TILE_M, t.cnt - rb * TILE_M);
+        it.b0 = pstart[t.l] + c0;
+        it.nb = min((unsigned)(CHUNK_TILES * TILE_N), t.c_hi - c0);
+        it.tag0 = (uint32_t)lbeg[t.l] + c0;
+        it.col0 = c0;
+        it.pad[0] = it.pad[1] = 0;
+        if (at + u < cap) items[at + u] = it;
     }
 }
 
@@ -806,6 +816,58 @@ __global__ void __launch_bounds__(256)
     tk.store(out + (size_t)q * LIST_K);
 }
 
+// One warp per query: tadm = tau + 2 (E_adc + max_l E_l), the pass-2
+// admission threshold (the bounds of certify_kernel; rounded up).  With the
+// factor 2 the certificate extension always applies (dk <= tau + E); a
+// smaller factor admits fewer candidates and extends when dk is below
+// tau + (factor - 1) E.
+#ifndef FDB_IVF_MARGIN
+#define FDB_IVF_MARGIN 2.0
+#endif
+__global__ void __launch_bounds__(256)
+    margin_kernel(const float* __restrict__ Q, int nq, int dim, int m,
+                  const float* __restrict__ cmax, const float* __restrict__ bmax,
+                  const uint32_t* __restrict__ probes, const float* __restrict__ pdist, int take,
+                  const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend,
+                  const float* __restrict__ rh, const float* __restrict__ tau,
+                  float* __restrict__ tadm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + warp;
+    if (q >= nq) return;
+    const int sub = dim / m;
+    const float* qv = Q + (size_t)q * dim;
+    double part = 0.0;
+    for (int s = lane; s < m; s += 32) {
+        double qn = 0.0;
+        for (int i = 0; i < sub; ++i) {
+            const double x = qv[s * sub + i];
+            qn += x * x;
+        }
+        const double t = sqrt(qn) + (double)cmax[s] + (double)bmax[s];
+        part += t * t;
+    }
+    double emax = 0.0;
+    const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
+    const double C2 = 1.52587890625e-5;
+    for (int j = lane; j < take; j += 32) {
+        const uint32_t l = probes[(size_t)q * take + j];
+        if (lend[l] <= lbeg[l]) continue;
+        const double r = (double)rh[l];
+        const double R = sqrt((double)pdist[(size_t)q * take + j]) * (1.0 + 1.52587890625e-5);
+        emax = fmax(emax, C1 * R * r + C2 * (R * R + r * r) + 1e-30);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        part += __shfl_xor_sync(0xffffffffu, part, o);
+        emax = fmax(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+    }
+    if (lane == 0) {
+        const double eadc = (32.0 + 4.0 * m) * 5.9604644775390625e-8 * part * 1.01;
+        const float delta = __double2float_ru(FDB_IVF_MARGIN * (eadc + emax) * (1.0 + 1e-6));
+        tadm[q] = __fadd_ru(tau[q], delta);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // exact rescoring and certification
 // ---------------------------------------------------------------------------
@@ -840,9 +902,29 @@ struct CertParams {
     uint32_t* flag_list;
     uint32_t* fail_probes;      // [flag slot][take] lists to re-scan exactly
     uint32_t* fail_cnt;         // [flag slot]
+    const uint64_t* part;       // [nq][64] pass-1 keys (the extension's first source)
+    const uint64_t* cand;       // [nq][cap] pass-2 candidates (its second source)
+    uint32_t* ext_count;        // queries certified by extension
+    uint32_t* ext_list;         // their local indices
+    float* ext_thr;             // their extension thresholds
+    unsigned long long* stat;   // [3] counts extended queries (nullable)
+    uint32_t* over_count;       // extensions that held too many entries
+    uint32_t* over_list;
+    const float* tadm;          // [nq] pass-2 admission threshold tau + delta
+    const float* dump;          // pass-1 distances, their rows and pair lookups
+    const unsigned* seg;
+    const uint32_t* inv;
+    const unsigned* poff;
 };
 
 constexpr int CERT_WARPS = 8;
+#ifndef FDB_IVF_EXT_MAX
+#define FDB_IVF_EXT_MAX 256
+#endif
+constexpr unsigned EXT_MAX = FDB_IVF_EXT_MAX;  // entries an extension may rescore
+constexpr int EXT_THREADS = 256;
+constexpr int EXT_MAX_TAKE = 256;  // probes per query an extension handles
+static_assert(EXT_MAX <= (unsigned)EXT_THREADS, "one thread rescores one collected entry");
 
 // Two warps per query, 32 shortlisted codes each: the codes rescored with
 // exact_adc (the reference's arithmetic), their exact keys and lists kept for
@@ -857,7 +939,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
     const int lq = warp >> 1, h = warp & 1;
     const int q = blockIdx.x * RS_QUERIES + lq;
     const bool qok = q < r.nq;
-    if (qok) {
+    if (qok) {  // warp-uniform
         const int m = r.m, sub = r.dim / m;
         const float* qv = r.Q + (size_t)q * r.dim;
         const uint64_t key = r.approx[(size_t)q * LIST_K + h * 32 + lane];
@@ -871,6 +953,7 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
                 if (r.offs_full[mid + 1] <= pos) lo = mid + 1;
                 else hi = mid;
             }
+            // one code per lane: 32 independent chains keep many loads in flight
             const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
                                              r.codes + (size_t)pos * m, m, sub);
             ek = make_key(d, pos);
@@ -914,11 +997,20 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
 // them listed for an exact re-scan, and its output row becomes the seed: the
 // exact top-k of its shortlisted codes in the other lists.
 template <int P>
-__global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) {
+__global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r, int forced) {
     __shared__ uint64_t buf[CERT_WARPS * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.x * CERT_WARPS + warp;
-    if (q >= r.nq) return;  // whole warp
+    // forced: the queries whose extension held too many entries, sent to
+    // the re-scan path
+    int q;
+    if (forced) {
+        const uint32_t sl = blockIdx.x * CERT_WARPS + warp;
+        if (sl >= *r.over_count) return;  // whole warp
+        q = (int)r.over_list[sl];
+    } else {
+        q = blockIdx.x * CERT_WARPS + warp;
+        if (q >= r.nq) return;  // whole warp
+    }
     const int m = r.m, sub = r.dim / m;
     const float* qv = r.Q + (size_t)q * r.dim;
     const uint64_t* ak = r.approx + (size_t)q * LIST_K;
@@ -939,7 +1031,9 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     const double C2 = 1.52587890625e-5;
     const unsigned c = r.cand_cnt[q];
     const uint64_t last = ak[LIST_K - 1];
-    const double B = last != KEY_NONE ? (double)key_dist(last) : (double)r.tau[q];
+    // (stored entries are the shortlist when it is not full; anything else
+    // has d~ above the admission threshold)
+    const double B = last != KEY_NONE ? (double)key_dist(last) : (double)r.tadm[q];
     const double dk = (double)r.dk[q];
     // whole-query failures: every list is re-scanned and nothing is kept
     const bool fail_all = c > (unsigned)r.cap || r.qbad[q] != 0u || (!isinf(B) && isinf(dk));
@@ -957,12 +1051,44 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
         const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - Eadc : -1.0;
         return (dk + Eadc + El < B) || (dk < lower);
     };
-    bool ok = !fail_all;
+    bool ok = !fail_all && !forced;
     for (int j0 = 0; ok && j0 < r.take; j0 += 32) {
         const int j = j0 + lane;
         ok = __all_sync(0xffffffffu, j >= r.take || list_ok(j));
     }
     if (ok) return;  // rescore_kernel's output stands
+    // Extension.  Every pass-1 distance is in the dump and pass 2 stores
+    // every code with d~ <= tadm = tau + 2 (E_adc + max_l E_l), so if
+    //   T = dk + E_adc + max_l E_l  <  tadm
+    // (always, as dk <= tau + E_adc + max_l E_l) rescoring every stored
+    // entry outside the shortlist with d~ <= T leaves only codes with
+    // d~ > T >= (new dk) + E_adc + E_l unscored: the merged exact top-k is
+    // certified without re-scanning any list.
+    if (!fail_all && !forced && c <= (unsigned)r.cap && r.take <= EXT_MAX_TAKE) {
+        double emax = 0.0;
+        for (int j = lane; j < r.take; j += 32) {
+            const uint32_t l = r.probes[(size_t)q * r.take + j];
+            if (r.lend[l] <= r.lbeg[l]) continue;
+            const double rh = (double)r.rh[l];
+            const double R = sqrt((double)r.pdist[(size_t)q * r.take + j]) * (1.0 + 1.52587890625e-5);
+            emax = fmax(emax, C1 * R * rh + C2 * (R * R + rh * rh) + 1e-30);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) emax = fmax(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+        const double T = (dk + Eadc + emax) * (1.0 + 1e-9);
+        if (T < (double)r.tadm[q]) {
+            if (lane == 0) {
+                // the largest float not above T: entries with d~ up to it are
+                // rescored, the rest have d~ > T
+                float tf = (float)T;
+                if ((double)tf > T) tf = nextafterf(tf, 0.0f);
+                const uint32_t slot = atomicAdd(r.ext_count, 1u);
+                r.ext_list[slot] = (uint32_t)q;
+                r.ext_thr[slot] = tf;
+            }
+            return;  // extend_kernel merges into rescore_kernel's output
+        }
+    }
     uint32_t slot = 0;
     if (lane == 0) {
         slot = atomicAdd(r.flag_count, 1u);
@@ -1000,6 +1126,100 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r) 
     if (__any_sync(0xffffffffu, s0 != KEY_NONE)) seed.merge32(s0);
     if (__any_sync(0xffffffffu, s1 != KEY_NONE)) seed.merge32(s1);
     seed.store(r.out_keys + (size_t)q * r.k);
+}
+
+// One block per extended query (see certify_kernel): every pass-1 distance
+// (dump) and pass-2 candidate that lies outside the shortlist (key above its
+// 64th) with d~ <= the query's threshold is collected, rescored exactly (one
+// entry per thread) and merged into its exact top-k row.  A query with more
+// than EXT_MAX such entries goes to the re-scan path instead.
+template <int ORDER, int P>
+__global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
+    __shared__ uint64_t keys[EXT_MAX];
+    __shared__ uint64_t buf[64];
+    __shared__ unsigned pstart[EXT_MAX_TAKE], plen[EXT_MAX_TAKE], ptag[EXT_MAX_TAKE];
+    __shared__ unsigned cnt;
+    __shared__ float dres[EXT_THREADS / 32][32];
+    typedef cub::BlockScan<unsigned, EXT_THREADS> Scan;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    const uint32_t slot = blockIdx.x;
+    if (slot >= *r.ext_count) return;  // whole block
+    const int t = threadIdx.x;
+    const int q = (int)r.ext_list[slot];
+    const float thr = r.ext_thr[slot];
+    const uint64_t last = r.approx[(size_t)q * LIST_K + LIST_K - 1];
+    if (t == 0) cnt = 0;
+    // the query's pass-1 dump rows (as select1_kernel) and their prefix
+    const unsigned n1 = r.poff[r.nlist], npairs = r.poff[2 * r.nlist];
+    unsigned nb = 0;
+    if (t < r.take) {
+        const size_t v = (size_t)q * r.take + t;
+        const uint32_t i = r.inv[v];
+        if (i < npairs) {
+            const uint32_t l = r.probes[v];
+            const unsigned len = (unsigned)(r.lend[l] - r.lbeg[l]);
+            nb = i < n1 ? len : min(len, (unsigned)TILE_N);
+            pstart[t] = r.seg[i];
+            ptag[t] = (uint32_t)r.lbeg[l];
+        }
+    }
+    unsigned off, total;
+    Scan(scan_tmp).ExclusiveSum(nb, off, total);
+    if (t < r.take) plen[t] = off;  // prefix
+    __syncthreads();
+    const int take = r.take;
+    auto keep = [&](uint64_t key) {
+        if (key == KEY_NONE || key <= last || key_dist(key) > thr) return;
+        const unsigned ix = atomicAdd(&cnt, 1u);
+        if (ix < EXT_MAX) keys[ix] = key;
+    };
+    for (unsigned f = t; f < total; f += EXT_THREADS) {
+        int lo = 0, hi = take - 1;  // the last pair whose prefix is <= f
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (plen[mid] <= f) lo = mid;
+            else hi = mid - 1;
+        }
+        const unsigned j = f - plen[lo];
+        const float d = r.dump[pstart[lo] + j];
+        if (d <= thr) keep(make_key(d, ptag[lo] + j));
+    }
+    const unsigned nc = min(r.cand_cnt[q], (unsigned)r.cap);
+    for (unsigned e = t; e < nc; e += EXT_THREADS) keep(r.cand[(size_t)q * r.cap + e]);
+    __syncthreads();
+    const unsigned n = cnt;
+    if (n > EXT_MAX) {
+        if (t == 0) r.over_list[atomicAdd(r.over_count, 1u)] = (uint32_t)q;
+        return;  // whole block
+    }
+    {
+        // warp w rescores entries [32 w, 32 w + 32) by lane groups
+        const bool valid = t < (int)n;
+        uint32_t pos = 0;
+        int lo = 0;
+        if (valid) {
+            pos = key_tag(keys[t]);
+            int hi = r.nlist;  // the list l with offs[l] <= pos < offs[l+1]
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (r.offs_full[mid + 1] <= pos) lo = mid + 1;
+                else hi = mid;
+            }
+        }
+        const int m = r.m, sub = r.dim / m;
+        const float d = warp_exact_adc<ORDER>(r.Q + (size_t)q * r.dim, r.cents, r.dim, r.cb,
+                                              r.codes, m, sub, pos, lo, valid, dres[t >> 5]);
+        if (valid) keys[t] = make_key(d, pos);
+    }
+    __syncthreads();
+    if (t >= 32) return;
+    WarpTopK<P> tk;
+    tk.init(r.k, buf);
+    tk.ingest(keys, (int)n);
+    uint64_t* row = r.out_keys + (size_t)q * r.k;
+    tk.ingest(row, r.k);
+    tk.store(row);
+    if (t == 0 && r.stat) atomicAdd(r.stat + 3, 1ull);
 }
 
 // ---------------------------------------------------------------------------
@@ -1264,10 +1484,23 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
                              2 * (size_t)nlist + (np / TILE_M + nlist) + 2;
     h->t_items.ensure(max_items * sizeof(Item));
     Item* items = reinterpret_cast<Item*>(h->t_items.p);
-    build_items_kernel<<<1, ITEM_THREADS, 0, s>>>(h->t_off.p, nlist, h->lorder.p, lbeg, lend,
-                                                  h->tc_pstart.p, items, (unsigned)max_items,
-                                                  h->t_range.p);
-    FDB_LAUNCH_CHECK();
+    {
+        const int nslot = 3 * nlist;
+        h->t_icnt.ensure(2 * ((size_t)nslot + 1));
+        unsigned* icnt = h->t_icnt.p;
+        unsigned* ioff = h->t_icnt.p + nslot + 1;
+        item_count_kernel<<<(unsigned)((nslot + 1 + 255) / 256), 256, 0, s>>>(
+            h->t_off.p, nlist, h->lorder.p, lbeg, lend, icnt);
+        FDB_LAUNCH_CHECK();
+        size_t tmp_items = 0;
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_items, icnt, ioff, nslot + 1, s));
+        h->t_tmp2.ensure(std::max<size_t>(tmp_items, 1));
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp2.p, tmp_items, icnt, ioff, nslot + 1, s));
+        item_fill_kernel<<<(unsigned)((nslot + 7) / 8), 256, 0, s>>>(
+            h->t_off.p, nlist, h->lorder.p, lbeg, lend, h->tc_pstart.p, ioff, items,
+            (unsigned)max_items, h->t_range.p);
+        FDB_LAUNCH_CHECK();
+    }
     // --- pass 1: distances of each query's first list; its top-64 and tau ---
     const CUtensorMap am = make_map(h->t_a16.p, np, dpad);
     const CUtensorMap bm = make_map(h->dec16.p, h->tc_rows, dpad);
@@ -1305,7 +1538,13 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
         FDB_NCCL(ncclAllReduce(h->t_tau.p, h->t_tau.p, nq, ncclFloat, ncclMin, c.comm, s));
     }
-    // --- pass 2: the other lists against tau ---
+    // --- pass 2: the other lists against tau + the certification margin ---
+    h->t_tadm.ensure(nq);
+    margin_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
+        dQ, (int)nq, (int)h->dim, (int)h->m, h->cmax.p, h->bmax.p, probes, pdist, (int)take,
+        lbeg, lend, h->tc_rhl.p, h->t_tau.p, h->t_tadm.p);
+    FDB_LAUNCH_CHECK();
+    p.tau = h->t_tadm.p;
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
     if (ev0) FDB_CUDA(cudaEventRecord(ev0, s));
@@ -1353,6 +1592,23 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.ekeys = h->t_ekeys.p;
     r.elist = h->t_elist.p;
     r.dk = h->t_dk.p;
+    h->t_ext.ensure(2 * nq + 2);
+    h->t_ext_thr.ensure(nq);
+    FDB_CUDA(cudaMemsetAsync(h->t_ext.p, 0, 4, s));
+    FDB_CUDA(cudaMemsetAsync(h->t_ext.p + nq + 1, 0, 4, s));
+    r.over_count = h->t_ext.p + nq + 1;
+    r.over_list = h->t_ext.p + nq + 2;
+    r.part = h->t_part.p;
+    r.cand = h->t_cand.p;
+    r.ext_count = h->t_ext.p;
+    r.ext_list = h->t_ext.p + 1;
+    r.ext_thr = h->t_ext_thr.p;
+    r.stat = stat;
+    r.tadm = h->t_tadm.p;
+    r.dump = h->t_dump.p;
+    r.seg = h->t_seg.p;
+    r.inv = h->t_inv.p;
+    r.poff = h->t_off.p;
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
     const unsigned rgrid = (unsigned)((nq + RS_QUERIES - 1) / RS_QUERIES);
     const bool p2 = k > 32;
@@ -1368,8 +1624,22 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         // the answer's k-th distance is at most the smallest exact k-th of any device
         FDB_NCCL(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s));
     }
-    if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
-    else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r);
+    if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
+    else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
+    FDB_LAUNCH_CHECK();
+    // extended queries: one block each (grid sized for all of them); those
+    // with too many entries then take the re-scan path
+    const unsigned egrid = (unsigned)nq;
+    if (order == ORDER_LANE8) {
+        if (p2) extend_kernel<ORDER_LANE8, 2><<<egrid, EXT_THREADS, 0, s>>>(r);
+        else extend_kernel<ORDER_LANE8, 1><<<egrid, EXT_THREADS, 0, s>>>(r);
+    } else {
+        if (p2) extend_kernel<ORDER_FAST4, 2><<<egrid, EXT_THREADS, 0, s>>>(r);
+        else extend_kernel<ORDER_FAST4, 1><<<egrid, EXT_THREADS, 0, s>>>(r);
+    }
+    FDB_LAUNCH_CHECK();
+    if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 1);
+    else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 1);
     FDB_LAUNCH_CHECK();
 }
 

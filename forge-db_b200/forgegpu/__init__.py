@@ -62,7 +62,8 @@ class Stats(C.Structure):
                 ("bytes_scanned", C.c_uint64), ("coarse_ms", C.c_double),
                 ("scan_ms", C.c_double), ("rescore_ms", C.c_double), ("merge_ms", C.c_double),
                 ("total_ms", C.c_double), ("exact_rescans", C.c_uint64),
-                ("kernel_ms", C.c_double), ("kernel_scores", C.c_uint64)]
+                ("kernel_ms", C.c_double), ("kernel_scores", C.c_uint64),
+                ("extended", C.c_uint64)]
 
 
 class FileInfo(C.Structure):

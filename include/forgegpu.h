@@ -81,6 +81,8 @@ typedef struct fdb_stats {
                                 list scan's second pass (IVF-PQ tensor mode), the
                                 filter pass (brute force, tensor path), else the scan */
     uint64_t kernel_scores;  /* (query, code/row) scores that kernel computed */
+    uint64_t extended;       /* tensor mode: queries certified by rescoring every stored
+                                candidate below a widened threshold instead of a re-scan */
 } fdb_stats;
 
 /* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  All return the reference's

@@ -366,9 +366,10 @@ def test_ivfpq_tensor_mode_config_a(fg, ctx, orc, nprobe, k, nq):
 
 
 def test_ivfpq_tensor_mode_ties_and_short_lists(fg, ctx, orc):
-    """Exact ties longer than the 64-entry shortlist cannot be certified;
-    lists shorter than 64 codes leave the admission threshold at +inf.  Both
-    must end on the exact path with the oracle's answer."""
+    """Exact ties longer than the 64-entry shortlist cannot be certified from
+    the shortlist alone; lists shorter than 64 codes leave the admission
+    threshold at +inf.  Both must end on the exact re-scan or the extended
+    certificate with the oracle's answer."""
     rng = np.random.default_rng(21)
     base = (rng.random((40, 64), dtype=np.float32) * 10).astype(np.float32)
     X = np.repeat(base, 100, axis=0)
@@ -379,7 +380,6 @@ def test_ivfpq_tensor_mode_ties_and_short_lists(fg, ctx, orc):
     ox.set_nprobe(8)
     Q = base[:20] + np.float32(0.01)
     ids, d, cnt, st = ix.batch_search_arrays(Q, 10, stats=True)
-    assert st.exact_rescans > 0
     oi, od, oc = ox.batch_search(Q, 10)
     assert_topk_match(ids, d, cnt, oi, od, oc, "tensor ties")
     # many tiny lists: 600 vectors in 64 lists, dim 64 -> subvectors of 8
