@@ -224,11 +224,20 @@ __global__ void __launch_bounds__(SEL_WARPS * 32)
     WarpTopK<P> tk;
     tk.init(take, buf + warp * 64);
     const float* row = D + (size_t)q * nlist;
-    for (int base = 0; base < nlist; base += 32) {
-        int l = base + lane;
-        bool valid = l < nlist;
-        uint64_t key = valid ? make_key(row[l], (uint32_t)l) : KEY_NONE;
-        tk.add(key, valid);
+    // eight loads in flight per lane, then their keys
+    for (int base = 0; base < nlist; base += 32 * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int l = base + u * 32 + lane;
+            v[u] = l < nlist ? row[l] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int l = base + u * 32 + lane;
+            const bool valid = l < nlist;
+            tk.add(valid ? make_key(v[u], (uint32_t)l) : KEY_NONE, valid);
+        }
     }
     tk.flush();
 #pragma unroll
