@@ -913,6 +913,7 @@ int fdb_ivfpq_rebuild(fdb_ivfpq* h, const fdb_train_opts* opts) {
         h->dead_dirty = false;
         h->id_index.clear();
         h->id_index_ok = false;
+        h->d_idx_ok = false;
         h->sharded = false;
         h->shard_world = 1;
         h->shard_rank = 0;

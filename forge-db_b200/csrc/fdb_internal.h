@@ -345,8 +345,10 @@ struct fdb_ivfpq {
     std::vector<std::pair<uint64_t, uint32_t>> id_index;  // (id, row) ascending, lazy
     bool id_index_ok = false;
     fdb::DevBuf<uint32_t> f_skip;       // per-call filter bitmap (search_filtered)
-    fdb::DevBuf<uint64_t> f_sorted;     // allowed ids and their sorted copy
-    fdb::DevBuf<uint8_t> f_tmp;         // radix-sort scratch
+    fdb::DevBuf<uint64_t> f_sorted;     // allowed ids copied from the host
+    fdb::DevBuf<uint64_t> d_idx_ids;    // ids sorted, with their rows (filters)
+    fdb::DevBuf<uint32_t> d_idx_rows;
+    bool d_idx_ok = false;
     fdb::DevBuf<float> f_colv;          // tensor scan ||rhat||^2 with a call's filter
     const float* tc_colv = nullptr;     // set for one call: overrides dnorm
     std::mutex mu;

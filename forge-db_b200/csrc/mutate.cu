@@ -71,77 +71,124 @@ __global__ void gather_rows_kernel(const uint32_t* __restrict__ rows, size_t nke
     if (j == 0) ids2[i] = ids[r];
 }
 
-// One thread per 32-row word: bit p set when row p is skipped by this call
-// (dead, or its id is not in the ascending allow list).
-__global__ void filter_bitmap_kernel(const uint64_t* __restrict__ ids, size_t n,
-                                     const uint64_t* __restrict__ allow, size_t na,
-                                     const uint32_t* __restrict__ dead, uint32_t* __restrict__ out) {
+// One thread per allowed id: every row holding it (a range of the
+// (id, row) index sorted by id) gets its bit set in `allow`.
+__global__ void allow_rows_kernel(const uint64_t* __restrict__ allowed, size_t na,
+                                  const uint64_t* __restrict__ sorted_ids,
+                                  const uint32_t* __restrict__ sorted_rows, size_t n,
+                                  uint32_t* __restrict__ allow) {
+    const size_t a = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= na) return;
+    const uint64_t id = allowed[a];
+    size_t lo = 0, hi = n;
+    while (lo < hi) {
+        const size_t mid = (lo + hi) >> 1;
+        if (sorted_ids[mid] < id) lo = mid + 1;
+        else hi = mid;
+    }
+    for (size_t p = lo; p < n && sorted_ids[p] == id; ++p) {
+        const uint32_t r = sorted_rows[p];
+        atomicOr(allow + (r >> 5), 1u << (r & 31));
+    }
+}
+
+// skip = not allowed, or dead; rows past n stay allowed (never scanned).
+__global__ void skip_words_kernel(const uint32_t* __restrict__ allow,
+                                  const uint32_t* __restrict__ dead, size_t n,
+                                  uint32_t* __restrict__ skip) {
     const size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (w >= (n + 31) / 32) return;
-    uint32_t word = dead ? dead[w] : 0u;
-    for (int j = 0; j < 32; ++j) {
-        const size_t p = w * 32 + j;
-        if (p >= n) break;
-        if ((word >> j) & 1u) continue;
-        const uint64_t id = ids[p];
-        size_t lo = 0, hi = na;
-        while (lo < hi) {
-            const size_t mid = (lo + hi) >> 1;
-            if (allow[mid] < id) lo = mid + 1;
-            else hi = mid;
-        }
-        if (lo >= na || allow[lo] != id) word |= 1u << j;
-    }
-    out[w] = word;
+    const size_t rem = n - w * 32;
+    const uint32_t valid = rem >= 32 ? 0xffffffffu : ((1u << rem) - 1u);
+    skip[w] = ((~allow[w]) & valid) | (dead ? dead[w] : 0u);
 }
 
 // rerank_results (ivf_pq.rs:556-582), one block per query.  Candidate i of
 // the PQ list (ascending) that has an original vector gets sqrt(L2^2(q, v))
 // (euclidean_distance_squared in the AVX2 order, correctly rounded square
-// root); candidates without one are dropped.  A stable sort by that distance
-// is a sort by (distance, i); each candidate's rank is the number of smaller
-// keys, and the first k ranks are written.
+// root); candidates without one are dropped.  Eight threads score one
+// candidate: thread j runs the order's accumulator j (elements i = j mod 8)
+// and the eight are summed left to right through shuffles, then the tail --
+// the same operations in the same order as l2sq_exact.  A stable sort by
+// distance is a sort by (distance, i); each candidate's rank is the number
+// of smaller keys, and the first k ranks are written.
 constexpr int RERANK_MAX = FDB_MAX_K;
-__global__ void __launch_bounds__(RERANK_MAX)
+constexpr int RERANK_THREADS = 256;  // 32 candidates scored at a time
+__global__ void __launch_bounds__(RERANK_THREADS)
     rerank_kernel(const uint64_t* __restrict__ keys, const uint64_t* __restrict__ cand_ids,
                   int fetch, const float* __restrict__ Q, int dim,
                   const uint64_t* __restrict__ rr_ids, const uint32_t* __restrict__ rr_slot,
                   size_t nrr, const float* __restrict__ rr_x, int k, uint64_t* __restrict__ out_ids,
                   float* __restrict__ out_d, uint32_t* __restrict__ counts) {
     __shared__ uint64_t skey[RERANK_MAX];
-    __shared__ int npresent;
+    __shared__ uint64_t sid[RERANK_MAX];
+    __shared__ int sslot[RERANK_MAX];
     const size_t q = blockIdx.x;
     const int t = threadIdx.x;
-    if (t == 0) npresent = 0;
-    uint64_t key = KEY_NONE, id = 0;
-    float d = 0.0f;
-    if (t < fetch && keys[q * fetch + t] != KEY_NONE) {
-        id = cand_ids[q * fetch + t];
-        size_t lo = 0, hi = nrr;
-        while (lo < hi) {
-            const size_t mid = (lo + hi) >> 1;
-            if (rr_ids[mid] < id) lo = mid + 1;
-            else hi = mid;
+    const float* qv = Q + q * dim;
+    // look up each candidate's original vector
+    for (int c = t; c < RERANK_MAX; c += RERANK_THREADS) {
+        int slot = -1;
+        uint64_t id = 0;
+        if (c < fetch && keys[q * fetch + c] != KEY_NONE) {
+            id = cand_ids[q * fetch + c];
+            size_t lo = 0, hi = nrr;
+            while (lo < hi) {
+                const size_t mid = (lo + hi) >> 1;
+                if (rr_ids[mid] < id) lo = mid + 1;
+                else hi = mid;
+            }
+            if (lo < nrr && rr_ids[lo] == id) slot = (int)rr_slot[lo];
         }
-        if (lo < nrr && rr_ids[lo] == id) {
-            d = __fsqrt_rn(l2sq_exact(Q + q * dim, rr_x + (size_t)rr_slot[lo] * dim, dim));
-            key = ((uint64_t)f2ord(d) << 32) | (uint32_t)t;
+        sslot[c] = slot;
+        sid[c] = id;
+        skey[c] = KEY_NONE;
+    }
+    __syncthreads();
+    // score: 32 candidates per pass, 8 lanes each
+    const int g = t >> 3, j = t & 7;
+    const int full = dim & ~7;
+    for (int c0 = 0; c0 < fetch; c0 += RERANK_THREADS / 8) {
+        const int c = c0 + g;
+        const int slot = c < fetch ? sslot[c] : -1;
+        float acc = 0.0f;
+        if (slot >= 0) {
+            const float* x = rr_x + (size_t)slot * dim;
+            for (int i = j; i < full; i += 8) {
+                const float d = __fsub_rn(qv[i], x[i]);
+                acc = __fmaf_rn(d, d, acc);
+            }
+        }
+        // acc_0 + acc_1 + ... + acc_7, then the unfused tail
+        float tot = __shfl_sync(0xffffffffu, acc, 0, 8);
+#pragma unroll
+        for (int u = 1; u < 8; ++u) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, acc, u, 8));
+        if (slot >= 0 && j == 0) {
+            const float* x = rr_x + (size_t)slot * dim;
+            for (int i = full; i < dim; ++i) {
+                const float d = __fsub_rn(qv[i], x[i]);
+                tot = __fadd_rn(tot, __fmul_rn(d, d));
+            }
+            const float dd = __fsqrt_rn(tot);
+            skey[c] = ((uint64_t)f2ord(dd) << 32) | (uint32_t)c;
         }
     }
-    skey[t] = key;
     __syncthreads();
-    if (key != KEY_NONE) {
-        atomicAdd(&npresent, 1);
+    // rank among present keys
+    int present = 0;
+    for (int c = 0; c < fetch; ++c) present += skey[c] != KEY_NONE;
+    for (int c = t; c < fetch; c += RERANK_THREADS) {
+        const uint64_t key = skey[c];
+        if (key == KEY_NONE) continue;
         int r = 0;
-        for (int j = 0; j < (int)blockDim.x; ++j) r += skey[j] < key;
+        for (int u = 0; u < fetch; ++u) r += skey[u] < key;
         if (r < k) {
-            out_ids[q * k + r] = id;
-            out_d[q * k + r] = d;
+            out_ids[q * k + r] = sid[c];
+            out_d[q * k + r] = key_dist(key);
         }
     }
-    __syncthreads();
-    const int cnt = min(npresent, k);
-    for (int r = cnt + t; r < k; r += blockDim.x) {
+    const int cnt = min(present, k);
+    for (int r = cnt + t; r < k; r += RERANK_THREADS) {
         out_ids[q * k + r] = ~0ull;
         out_d[q * k + r] = __int_as_float(0x7f800000);
     }
@@ -259,8 +306,7 @@ void launch_rerank(fdb_ivfpq* h, const uint64_t* keys, const uint64_t* cand_ids,
     FDB_REQUIRE(fetch <= (size_t)RERANK_MAX, FDB_ERR_UNSUPPORTED,
                 "k * rerank_factor above FDB_MAX_K");
     if (nq == 0 || k == 0) return;
-    const unsigned threads = (unsigned)((fetch + 31) / 32 * 32);
-    rerank_kernel<<<(unsigned)nq, threads, 0, h->ctx->c.stream>>>(
+    rerank_kernel<<<(unsigned)nq, RERANK_THREADS, 0, h->ctx->c.stream>>>(
         keys, cand_ids, (int)fetch, dQ, (int)h->dim, h->rr_sorted.p, h->rr_sorted_slot.p,
         h->rr_ids.size(), h->rr_dev.p, (int)k, d_ids, d_dists, d_counts);
     FDB_LAUNCH_CHECK();
@@ -322,6 +368,7 @@ size_t ivfpq_live_len(const fdb_ivfpq* h) {
 static void relayout_done(fdb_ivfpq* h) {
     h->id_index.clear();
     h->id_index_ok = false;
+    h->d_idx_ok = false;
     rebuild_dead(h);
     h->dead_dirty = true;
     ivfpq_prepare_tables(h);
@@ -445,6 +492,30 @@ const float* ivfpq_call_colv(fdb_ivfpq* h, const uint32_t* skip) {
     return h->f_colv.p;
 }
 
+// The (id, row) index sorted by id on the device, built on first use after
+// a layout change.
+static void ensure_dev_id_index(fdb_ivfpq* h) {
+    if (h->d_idx_ok) return;
+    cudaStream_t s = h->ctx->c.stream;
+    const size_t n = h->n_total;
+    h->d_idx_ids.alloc(std::max<size_t>(n, 1));
+    h->d_idx_rows.alloc(std::max<size_t>(n, 1));
+    if (n) {
+        DevBuf<uint32_t> rows(n);
+        std::vector<uint32_t> iota(n);
+        std::iota(iota.begin(), iota.end(), 0u);
+        FDB_CUDA(cudaMemcpyAsync(rows.p, iota.data(), n * 4, cudaMemcpyHostToDevice, s));
+        size_t tmp = 0;
+        FDB_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, h->ids.p, h->d_idx_ids.p, rows.p,
+                                                 h->d_idx_rows.p, (int)n, 0, 64, s));
+        DevBuf<uint8_t> t(std::max<size_t>(tmp, 1));
+        FDB_CUDA(cub::DeviceRadixSort::SortPairs(t.p, tmp, h->ids.p, h->d_idx_ids.p, rows.p,
+                                                 h->d_idx_rows.p, (int)n, 0, 64, s));
+        FDB_CUDA(cudaStreamSynchronize(s));
+    }
+    h->d_idx_ok = true;
+}
+
 // Per-call skip bitmap of search_filtered: dead rows and rows whose id is
 // not allowed.  Returns the device bitmap (in h->f_skip).
 const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed, size_t na,
@@ -452,21 +523,24 @@ const uint32_t* ivfpq_filter_bitmap(fdb_ivfpq* h, const uint64_t* allowed, size_
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     FDB_REQUIRE(na < (1ull << 31), FDB_ERR_UNSUPPORTED, "at most 2^31-1 allowed ids");
-    h->f_sorted.ensure(2 * na);
-    uint64_t* a = h->f_sorted.p;
-    uint64_t* b = h->f_sorted.p + na;
-    FDB_CUDA(cudaMemcpyAsync(a, allowed, na * 8,
-                             on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
-    size_t tmp = 0;
-    FDB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, a, b, (int)na, 0, 64, s));
-    h->f_tmp.ensure(std::max<size_t>(tmp, 1));
-    FDB_CUDA(cub::DeviceRadixSort::SortKeys(h->f_tmp.p, tmp, a, b, (int)na, 0, 64, s));
+    FDB_REQUIRE(h->n_total < (1ull << 31), FDB_ERR_UNSUPPORTED, "at most 2^31-1 rows");
+    ensure_dev_id_index(h);
+    const uint64_t* a = allowed;
+    if (!on_device) {
+        h->f_sorted.ensure(na);
+        FDB_CUDA(cudaMemcpyAsync(h->f_sorted.p, allowed, na * 8, cudaMemcpyHostToDevice, s));
+        a = h->f_sorted.p;
+    }
     const size_t nw = words_for(h->n_total);
-    h->f_skip.ensure(std::max<size_t>(nw, 1));
+    h->f_skip.ensure(2 * std::max<size_t>(nw, 1));
+    uint32_t* allow = h->f_skip.p + std::max<size_t>(nw, 1);
     if (nw) {
-        filter_bitmap_kernel<<<grid_for(nw), 256, 0, s>>>(h->ids.p, h->n_total, b, na,
-                                                           h->n_tomb ? h->dead.p : nullptr,
-                                                           h->f_skip.p);
+        FDB_CUDA(cudaMemsetAsync(allow, 0, nw * 4, s));
+        allow_rows_kernel<<<grid_for(na), 256, 0, s>>>(a, na, h->d_idx_ids.p, h->d_idx_rows.p,
+                                                       h->n_total, allow);
+        FDB_LAUNCH_CHECK();
+        skip_words_kernel<<<grid_for(nw), 256, 0, s>>>(allow, h->n_tomb ? h->dead.p : nullptr,
+                                                       h->n_total, h->f_skip.p);
         FDB_LAUNCH_CHECK();
     }
     return h->f_skip.p;
