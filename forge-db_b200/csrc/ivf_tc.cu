@@ -760,32 +760,50 @@ __global__ void __launch_bounds__(256)
     WarpTopK<2> tk;
     tk.init(LIST_K, buf + warp * 64);
     const unsigned n1 = poff[nlist], npairs = poff[2 * nlist];
-    for (int jp = 0; jp < take; ++jp) {
-        const size_t v = (size_t)q * take + jp;
-        const uint32_t i = inv[v];
-        if (i >= npairs) continue;  // list empty or held elsewhere
-        const uint32_t l = probes[v];
-        const int len = (int)(lend[l] - lbeg[l]);
-        const int nb = i < n1 ? len : min(len, TILE_N);
-        const uint32_t tag0 = (uint32_t)lbeg[l];
-        // rows are padded to a multiple of 128 floats
-        const float4* row4 = reinterpret_cast<const float4*>(dump + seg[i]);
-        for (int base = 0; base < nb; base += 128) {
-            const float4 x4 = row4[(base >> 2) + lane];
-            const int j = base + 4 * lane;
-            const float d[4] = {x4.x, x4.y, x4.z, x4.w};
-            uint64_t key[4];
-            bool any = false;
-#pragma unroll
-            for (int x = 0; x < 4; ++x) {
-                // +inf marks a tombstoned row
-                key[x] = (j + x < nb && d[x] < INF) ? make_key(d[x], tag0 + (uint32_t)(j + x))
-                                                    : KEY_NONE;
-                any |= key[x] < tk.thr;
+    // Probes in batches of 32: each lane looks up one probe's dump row (the
+    // index chain inv -> list -> bounds runs in parallel across lanes), then
+    // the rows are streamed one probe at a time.
+    for (int jp0 = 0; jp0 < take; jp0 += 32) {
+        const int jp = jp0 + lane;
+        unsigned start = 0, nbl = 0, tagl = 0;
+        if (jp < take) {
+            const size_t v = (size_t)q * take + jp;
+            const uint32_t i = inv[v];
+            if (i < npairs) {  // else: list empty or held elsewhere
+                const uint32_t l = probes[v];
+                const unsigned len = (unsigned)(lend[l] - lbeg[l]);
+                nbl = i < n1 ? len : min(len, (unsigned)TILE_N);
+                start = seg[i];
+                tagl = (uint32_t)lbeg[l];
             }
-            if (!__any_sync(0xffffffffu, any)) continue;
+        }
+        unsigned live = __ballot_sync(0xffffffffu, nbl > 0);
+        while (live) {
+            const int p = __ffs(live) - 1;
+            live &= live - 1;
+            const int nb = (int)__shfl_sync(0xffffffffu, nbl, p);
+            const uint32_t tag0 = __shfl_sync(0xffffffffu, tagl, p);
+            // rows are padded to a multiple of 128 floats
+            const float4* row4 =
+                reinterpret_cast<const float4*>(dump + __shfl_sync(0xffffffffu, start, p));
+            for (int base = 0; base < nb; base += 128) {
+                const float4 x4 = row4[(base >> 2) + lane];
+                const int j = base + 4 * lane;
+                const float d[4] = {x4.x, x4.y, x4.z, x4.w};
+                uint64_t key[4];
+                bool any = false;
 #pragma unroll
-            for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
+                for (int x = 0; x < 4; ++x) {
+                    // +inf marks a tombstoned row
+                    key[x] = (j + x < nb && d[x] < INF)
+                                 ? make_key(d[x], tag0 + (uint32_t)(j + x))
+                                 : KEY_NONE;
+                    any |= key[x] < tk.thr;
+                }
+                if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+                for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
+            }
         }
     }
     tk.flush();

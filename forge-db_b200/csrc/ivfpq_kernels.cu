@@ -112,31 +112,39 @@ __global__ void transpose_pad_kernel(const float* __restrict__ x, int n, int dim
     }
 }
 
+// Shared memory holds one lane's rows at a time: for lane j the rows
+// i = j, j + 8, ... (< full) of both tiles (then the tail rows), so a block
+// needs (full / 8) x (CT_Q + CT_C) floats and many blocks fit on an SM.
 __global__ void __launch_bounds__(CT_THREADS)
     coarse_tiled_kernel(const float* __restrict__ QT, int nq, int nq_pad, int dim,
                         const float* __restrict__ CT, int nlist, int nlist_pad,
                         float* __restrict__ D) {
     extern __shared__ __align__(16) float ct_smem[];
-    float* qs = ct_smem;              // [dim][CT_Q]
-    float* cs = qs + dim * CT_Q;      // [dim][CT_C]
+    const int full = dim & ~7, rows = max(full / 8, dim - full);
+    float* qs = ct_smem;              // [rows][CT_Q]
+    float* cs = qs + rows * CT_Q;     // [rows][CT_C]
     const int q0 = blockIdx.y * CT_Q, c0 = blockIdx.x * CT_C;
-    for (int e = threadIdx.x; e < dim * (CT_Q / 4); e += CT_THREADS) {
-        const int i = e / (CT_Q / 4), v = e - i * (CT_Q / 4);
-        reinterpret_cast<float4*>(qs + i * CT_Q)[v] =
-            __ldg(reinterpret_cast<const float4*>(QT + (size_t)i * nq_pad + q0) + v);
-    }
-    for (int e = threadIdx.x; e < dim * (CT_C / 4); e += CT_THREADS) {
-        const int i = e / (CT_C / 4), v = e - i * (CT_C / 4);
-        reinterpret_cast<float4*>(cs + i * CT_C)[v] =
-            __ldg(reinterpret_cast<const float4*>(CT + (size_t)i * nlist_pad + c0) + v);
-    }
-    __syncthreads();
     const int tq = threadIdx.x & (CT_Q / CT_TQ - 1);  // 0..7
     const int tc = threadIdx.x / (CT_Q / CT_TQ);      // 0..15
     const float* qb = qs + tq * CT_TQ;
     const float* cb = cs + tc * CT_TC;
+    // rows i0, i0 + step, ... (nr of them) of both tiles into shared memory
+    auto stage = [&](int i0, int step, int nr) {
+        __syncthreads();  // the previous stage is no longer read
+        for (int e = threadIdx.x; e < nr * (CT_Q / 4); e += CT_THREADS) {
+            const int r = e / (CT_Q / 4), v = e - r * (CT_Q / 4);
+            reinterpret_cast<float4*>(qs + r * CT_Q)[v] = __ldg(
+                reinterpret_cast<const float4*>(QT + (size_t)(i0 + r * step) * nq_pad + q0) + v);
+        }
+        for (int e = threadIdx.x; e < nr * (CT_C / 4); e += CT_THREADS) {
+            const int r = e / (CT_C / 4), v = e - r * (CT_C / 4);
+            reinterpret_cast<float4*>(cs + r * CT_C)[v] = __ldg(
+                reinterpret_cast<const float4*>(CT + (size_t)(i0 + r * step) * nlist_pad + c0) + v);
+        }
+        __syncthreads();
+    };
     float t[CT_TQ][CT_TC];
-    const int full = dim & ~7;
+    const int nr = full / 8;
 #pragma unroll 1
     for (int j = 0; j < 8; ++j) {
         float acc[CT_TQ][CT_TC];
@@ -144,11 +152,12 @@ __global__ void __launch_bounds__(CT_THREADS)
         for (int a = 0; a < CT_TQ; ++a)
 #pragma unroll
             for (int b = 0; b < CT_TC; ++b) acc[a][b] = 0.0f;
+        if (nr > 0) stage(j, 8, nr);
 #pragma unroll 4
-        for (int i = j; i < full; i += 8) {
-            const float4 qv = *reinterpret_cast<const float4*>(qb + i * CT_Q);
-            const float4 c0v = *reinterpret_cast<const float4*>(cb + i * CT_C);
-            const float4 c1v = *reinterpret_cast<const float4*>(cb + i * CT_C + 4);
+        for (int r = 0; r < nr; ++r) {  // element i = j + 8 r
+            const float4 qv = *reinterpret_cast<const float4*>(qb + r * CT_Q);
+            const float4 c0v = *reinterpret_cast<const float4*>(cb + r * CT_C);
+            const float4 c1v = *reinterpret_cast<const float4*>(cb + r * CT_C + 4);
             const float qa[CT_TQ] = {qv.x, qv.y, qv.z, qv.w};
             const float ca[CT_TC] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
 #pragma unroll
@@ -164,14 +173,17 @@ __global__ void __launch_bounds__(CT_THREADS)
 #pragma unroll
             for (int b = 0; b < CT_TC; ++b) t[a][b] = j == 0 ? acc[a][b] : __fadd_rn(t[a][b], acc[a][b]);
     }
-    for (int i = full; i < dim; ++i) {
+    if (dim > full) {
+        stage(full, 1, dim - full);
+        for (int r = 0; r < dim - full; ++r) {
 #pragma unroll
-        for (int a = 0; a < CT_TQ; ++a)
+            for (int a = 0; a < CT_TQ; ++a)
 #pragma unroll
-            for (int b = 0; b < CT_TC; ++b) {
-                const float d = __fsub_rn(qb[i * CT_Q + a], cb[i * CT_C + b]);
-                t[a][b] = __fadd_rn(t[a][b], __fmul_rn(d, d));
-            }
+                for (int b = 0; b < CT_TC; ++b) {
+                    const float d = __fsub_rn(qb[r * CT_Q + a], cb[r * CT_C + b]);
+                    t[a][b] = __fadd_rn(t[a][b], __fmul_rn(d, d));
+                }
+        }
     }
 #pragma unroll
     for (int a = 0; a < CT_TQ; ++a) {
@@ -198,7 +210,8 @@ void launch_coarse_tiled(cudaStream_t s, const float* QT, int nq, int nq_pad, in
     if (nq == 0) return;
     FDB_REQUIRE(dim <= CT_MAX_DIM && nq_pad % CT_Q == 0 && nlist_pad % CT_C == 0,
                 FDB_ERR_UNSUPPORTED, "coarse tiling: bad shape");
-    const size_t smem = (size_t)dim * (CT_Q + CT_C) * sizeof(float);
+    const int full = dim & ~7, rows = std::max(full / 8, dim - full);
+    const size_t smem = (size_t)std::max(rows, 1) * (CT_Q + CT_C) * sizeof(float);
     if (smem > 48 * 1024)
         FDB_CUDA(cudaFuncSetAttribute(coarse_tiled_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
