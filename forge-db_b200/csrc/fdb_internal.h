@@ -375,6 +375,13 @@ struct fdb_ivfpq {
     fdb::DevBuf<float> t_ext_thr, t_tadm;
     fdb::DevBuf<unsigned> t_icnt;       // item counts per (kind, list) and their offsets
     fdb::DevBuf<uint8_t> t_tmp2;        // scan scratch for the item offsets
+    // pass-2 pruning: kept pairs per list and their offsets, flags, the kept
+    // pair ids (count first) and their compacted rows
+    fdb::DevBuf<unsigned> t_live, t_sel;
+    fdb::DevBuf<uint8_t> t_pflag, t_tmp3;
+    fdb::DevBuf<__half> t_a2;
+    fdb::DevBuf<uint32_t> t_q2;
+    fdb::DevBuf<float> t_rn2, t_s22;
 };
 
 struct fdb_bf {

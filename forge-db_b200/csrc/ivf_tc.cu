@@ -555,8 +555,8 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
     if (stat) {
         atomicAdd(stat, lists);
         atomicAdd(stat + 1, codes);
-        atomicAdd(stat + 2, codes2);
     }
+    (void)codes2;
 }
 
 // off[k] = the first position of key >= k in the sorted keys (k <= nkeys):
@@ -677,7 +677,10 @@ struct ItemSlot {
     uint32_t l;
 };
 
-__device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict__ poff, int nlist,
+// poff2 (nullable): for kind 2, the live pass-2 pairs' offsets per list
+// ([nlist + 1], rows of the compacted pass-2 matrix) instead of poff's.
+__device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict__ poff,
+                                              const unsigned* __restrict__ poff2, int nlist,
                                               const uint32_t* __restrict__ lorder,
                                               const uint64_t* __restrict__ lbeg,
                                               const uint64_t* __restrict__ lend) {
@@ -685,8 +688,13 @@ __device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict_
     const int seg = kind == 0 ? 0 : 1;
     ItemSlot t;
     t.l = lorder[i];
-    t.a0 = poff[seg * nlist + t.l];
-    t.cnt = poff[seg * nlist + t.l + 1] - t.a0;
+    if (kind == 2 && poff2) {
+        t.a0 = poff2[t.l];
+        t.cnt = poff2[t.l + 1] - t.a0;
+    } else {
+        t.a0 = poff[seg * nlist + t.l];
+        t.cnt = poff[seg * nlist + t.l + 1] - t.a0;
+    }
     const unsigned len = (unsigned)(lend[t.l] - lbeg[t.l]);
     // codes [c_lo, c_hi) of the list this kind covers
     t.c_lo = kind == 2 ? (unsigned)TILE_N : 0u;
@@ -697,38 +705,47 @@ __device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict_
     return t;
 }
 
-__global__ void item_count_kernel(const unsigned* __restrict__ poff, int nlist,
+// Slots [s0, s0 + nslot): counts[s - s0] = the slot's items, counts[nslot] = 0.
+__global__ void item_count_kernel(const unsigned* __restrict__ poff,
+                                  const unsigned* __restrict__ poff2, int nlist, int s0, int nslot,
                                   const uint32_t* __restrict__ lorder,
                                   const uint64_t* __restrict__ lbeg,
                                   const uint64_t* __restrict__ lend, unsigned* __restrict__ counts) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s > 3 * nlist) return;
-    if (s == 3 * nlist) {  // the exclusive sum's total
-        counts[s] = 0;
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u > nslot) return;
+    if (u == nslot) {  // the exclusive sum's total
+        counts[u] = 0;
         return;
     }
-    const ItemSlot t = item_slot(s, poff, nlist, lorder, lbeg, lend);
-    counts[s] = ((t.cnt + TILE_M - 1) / TILE_M) * t.nchunk;
+    const ItemSlot t = item_slot(s0 + u, poff, poff2, nlist, lorder, lbeg, lend);
+    counts[u] = ((t.cnt + TILE_M - 1) / TILE_M) * t.nchunk;
 }
 
+// Items of slots [s0, s0 + nslot) at items[base + ioff[u]], base = 0 for
+// the pass-1 slots (kinds 0, 1: range[0..1] = {0, n1}) and range[1] for the
+// pass-2 slots (kind 2: range[2..3] = {n1, n2}).
 __global__ void __launch_bounds__(256)
-    item_fill_kernel(const unsigned* __restrict__ poff, int nlist,
-                     const uint32_t* __restrict__ lorder, const uint64_t* __restrict__ lbeg,
-                     const uint64_t* __restrict__ lend, const uint32_t* __restrict__ pstart,
-                     const unsigned* __restrict__ ioff, Item* __restrict__ items, unsigned cap,
-                     uint32_t* __restrict__ range) {
+    item_fill_kernel(const unsigned* __restrict__ poff, const unsigned* __restrict__ poff2,
+                     int nlist, int s0, int nslot, const uint32_t* __restrict__ lorder,
+                     const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend,
+                     const uint32_t* __restrict__ pstart, const unsigned* __restrict__ ioff,
+                     Item* __restrict__ items, unsigned cap, uint32_t* __restrict__ range) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int s = blockIdx.x * 8 + warp;
-    if (s == 0 && lane == 0) {
-        const unsigned n1 = min(ioff[2 * nlist], cap), n12 = min(ioff[3 * nlist], cap);
-        range[0] = 0;
-        range[1] = n1;
-        range[2] = n1;
-        range[3] = n12 - n1;
+    const int u = blockIdx.x * 8 + warp;
+    const unsigned base = s0 == 0 ? 0u : range[1];
+    if (u == 0 && lane == 0) {
+        const unsigned end = min(base + ioff[nslot], cap);
+        if (s0 == 0) {
+            range[0] = 0;
+            range[1] = end;
+        } else {
+            range[2] = base;
+            range[3] = end - base;
+        }
     }
-    if (s >= 3 * nlist) return;
-    const ItemSlot t = item_slot(s, poff, nlist, lorder, lbeg, lend);
-    const unsigned at = ioff[s], nit = ioff[s + 1] - at;
+    if (u >= nslot) return;
+    const ItemSlot t = item_slot(s0 + u, poff, poff2, nlist, lorder, lbeg, lend);
+    const unsigned at = base + ioff[u], nit = ioff[u + 1] - ioff[u];
     for (unsigned u = lane; u < nit; u += 32) {
         const unsigned rb = u / t.nchunk, ch = u - rb * t.nchunk;
         const unsigned c0 = t.c_lo + ch * CHUNK_TILES * TILE_N;
@@ -741,6 +758,73 @@ __global__ void __launch_bounds__(256)
         it.col0 = c0;
         it.pad[0] = it.pad[1] = 0;
         if (at + u < cap) items[at + u] = it;
+    }
+}
+
+// Pass-2 pairs whose list cannot hold a code with d~ <= tadm are dropped:
+// every code of list l has real distance D >= (||r|| - Rh_l)^2 and
+// d~ >= D - E_l, so a pair with (||r|| - Rh_l)^2 - E_l > tadm[q] admits
+// nothing (the bounds of certify_kernel).  flags[i] = 1 for the pass-2 pairs
+// kept (lists longer than one tile: pass 2 covers tiles 1..); live[l] counts
+// them per list, stat[2] their pass-2 scores.
+__global__ void prune_kernel(const uint32_t* __restrict__ skeys, const unsigned* __restrict__ poff,
+                             int nlist, unsigned np, const uint32_t* __restrict__ pair_q,
+                             const float* __restrict__ pair_rn, const float* __restrict__ rh,
+                             const float* __restrict__ tadm, const uint64_t* __restrict__ lbeg,
+                             const uint64_t* __restrict__ lend, uint8_t* __restrict__ flags,
+                             unsigned* __restrict__ live, unsigned long long* stat) {
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned n1 = poff[nlist], npairs = poff[2 * nlist];
+    uint8_t keep = 0;
+    unsigned long long scores = 0;
+    if (i < np && i >= n1 && i < npairs) {
+        const uint32_t l = skeys[i] - (uint32_t)nlist;
+        const uint64_t len = lend[l] - lbeg[l];
+        if (len > (uint64_t)TILE_N) {
+            const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
+            const double C2 = 1.52587890625e-5;
+            const double r = (double)rh[l];
+            const double D = (double)pair_rn[i];
+            const double R = sqrt(D) * (1.0 + 1.52587890625e-5);
+            const double El = C1 * R * r + C2 * (R * R + r * r) + 1e-30;
+            const double Rl = sqrt(D) * (1.0 - 1.52587890625e-5) - r;
+            const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - El : -1.0;
+            if (!(lower > (double)tadm[pair_q[i]])) {
+                keep = 1;
+                atomicAdd(live + l, 1u);
+                scores = len - TILE_N;
+            }
+        }
+    }
+    if (i < np) flags[i] = keep;
+    if (stat) {
+        // one atomic per warp (every lane of the warp is still here)
+        for (int o = 16; o >= 1; o >>= 1) scores += __shfl_xor_sync(0xffffffffu, scores, o);
+        if ((threadIdx.x & 31) == 0 && scores) atomicAdd(stat + 2, scores);
+    }
+}
+
+// The kept pass-2 pairs (sel[0 .. *nsel), ascending) gathered into a compact
+// matrix of A rows and their per-pair values, one warp per row.
+__global__ void gather_pairs_kernel(const unsigned* __restrict__ sel,
+                                    const unsigned* __restrict__ nsel, int dpad,
+                                    const __half* __restrict__ a16,
+                                    const uint32_t* __restrict__ pair_q,
+                                    const float* __restrict__ pair_rn,
+                                    const float* __restrict__ pair_s2, __half* __restrict__ a2,
+                                    uint32_t* __restrict__ q2, float* __restrict__ rn2,
+                                    float* __restrict__ s22) {
+    const unsigned j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (j >= *nsel) return;
+    const unsigned i = sel[j];
+    const uint4* src = reinterpret_cast<const uint4*>(a16 + (size_t)i * dpad);
+    uint4* dst = reinterpret_cast<uint4*>(a2 + (size_t)j * dpad);
+    for (int v = lane; v < dpad / 8; v += 32) dst[v] = src[v];
+    if (lane == 0) {
+        q2[j] = pair_q[i];
+        rn2[j] = pair_rn[i];
+        s22[j] = pair_s2[i];
     }
 }
 
@@ -1502,23 +1586,24 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
                              2 * (size_t)nlist + (np / TILE_M + nlist) + 2;
     h->t_items.ensure(max_items * sizeof(Item));
     Item* items = reinterpret_cast<Item*>(h->t_items.p);
-    {
-        const int nslot = 3 * nlist;
-        h->t_icnt.ensure(2 * ((size_t)nslot + 1));
+    // items of slots [s0, s0 + nslot): count, exclusive sum, fill
+    h->t_icnt.ensure(2 * (3 * (size_t)nlist + 1));
+    auto make_items = [&](int s0, int nslot, const unsigned* poff2) {
         unsigned* icnt = h->t_icnt.p;
         unsigned* ioff = h->t_icnt.p + nslot + 1;
         item_count_kernel<<<(unsigned)((nslot + 1 + 255) / 256), 256, 0, s>>>(
-            h->t_off.p, nlist, h->lorder.p, lbeg, lend, icnt);
+            h->t_off.p, poff2, nlist, s0, nslot, h->lorder.p, lbeg, lend, icnt);
         FDB_LAUNCH_CHECK();
         size_t tmp_items = 0;
         FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp_items, icnt, ioff, nslot + 1, s));
         h->t_tmp2.ensure(std::max<size_t>(tmp_items, 1));
         FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp2.p, tmp_items, icnt, ioff, nslot + 1, s));
         item_fill_kernel<<<(unsigned)((nslot + 7) / 8), 256, 0, s>>>(
-            h->t_off.p, nlist, h->lorder.p, lbeg, lend, h->tc_pstart.p, ioff, items,
-            (unsigned)max_items, h->t_range.p);
+            h->t_off.p, poff2, nlist, s0, nslot, h->lorder.p, lbeg, lend, h->tc_pstart.p, ioff,
+            items, (unsigned)max_items, h->t_range.p);
         FDB_LAUNCH_CHECK();
-    }
+    };
+    make_items(0, 2 * nlist, nullptr);  // pass 1: whole pass-1 lists, first tiles
     // --- pass 1: distances of each query's first list; its top-64 and tau ---
     const CUtensorMap am = make_map(h->t_a16.p, np, dpad);
     const CUtensorMap bm = make_map(h->dec16.p, h->tc_rows, dpad);
@@ -1562,11 +1647,46 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         dQ, (int)nq, (int)h->dim, (int)h->m, h->cmax.p, h->bmax.p, probes, pdist, (int)take,
         lbeg, lend, h->tc_rhl.p, h->t_tau.p, h->t_tadm.p);
     FDB_LAUNCH_CHECK();
+    // --- drop the pass-2 pairs whose list cannot admit a code; compact the rest ---
+    h->t_live.ensure(2 * ((size_t)nlist + 1));
+    h->t_pflag.ensure(np);
+    h->t_sel.ensure(np + 1);
+    unsigned* live = h->t_live.p;
+    unsigned* live_off = h->t_live.p + nlist + 1;
+    FDB_CUDA(cudaMemsetAsync(live, 0, ((size_t)nlist + 1) * 4, s));
+    prune_kernel<<<(unsigned)((np + 255) / 256), 256, 0, s>>>(
+        h->t_keys.p + np, h->t_off.p, nlist, (unsigned)np, h->t_pq.p, h->t_rn.p, h->tc_rhl.p,
+        h->t_tadm.p, lbeg, lend, h->t_pflag.p, live, stat);
+    FDB_LAUNCH_CHECK();
+    {
+        size_t t1 = 0, t2 = 0;
+        cub::CountingInputIterator<unsigned> ids(0u);
+        FDB_CUDA(cub::DeviceSelect::Flagged(nullptr, t1, ids, h->t_pflag.p, h->t_sel.p + 1,
+                                            h->t_sel.p, (int)np, s));
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t2, live, live_off, nlist + 1, s));
+        h->t_tmp3.ensure(std::max<size_t>(std::max(t1, t2), 1));
+        FDB_CUDA(cub::DeviceSelect::Flagged(h->t_tmp3.p, t1, ids, h->t_pflag.p, h->t_sel.p + 1,
+                                            h->t_sel.p, (int)np, s));
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp3.p, t2, live, live_off, nlist + 1, s));
+    }
+    h->t_a2.ensure(np * dpad);
+    h->t_q2.ensure(np);
+    h->t_rn2.ensure(np);
+    h->t_s22.ensure(np);
+    gather_pairs_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
+        h->t_sel.p + 1, h->t_sel.p, dpad, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_a2.p,
+        h->t_q2.p, h->t_rn2.p, h->t_s22.p);
+    FDB_LAUNCH_CHECK();
+    make_items(2 * nlist, nlist, live_off);  // pass 2: tiles 1.. of the kept pairs' lists
+    const CUtensorMap am2 = make_map(h->t_a2.p, np, dpad);
+    p.pair_q = h->t_q2.p;
+    p.pair_rn = h->t_rn2.p;
+    p.pair_s2 = h->t_s22.p;
     p.tau = h->t_tadm.p;
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
     if (ev0) FDB_CUDA(cudaEventRecord(ev0, s));
-    launch_pass<EPI_FILTER>(s, am, bm, grid, p);
+    launch_pass<EPI_FILTER>(s, am2, bm, grid, p);
     if (ev1) FDB_CUDA(cudaEventRecord(ev1, s));
     // --- shortlist, exact rescoring, certification ---
     h->s_approx.ensure(nq * LIST_K);
