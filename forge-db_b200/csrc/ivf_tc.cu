@@ -62,6 +62,11 @@ constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
 #define FDB_IVF_SPIN_WAITS 1
 #endif
 constexpr int CHUNK_TILES = FDB_IVF_CHUNK_TILES;  // B tiles per item at most (long lists are split)
+#ifndef FDB_IVF_SAMPLE_DIV
+#define FDB_IVF_SAMPLE_DIV 16
+#endif
+// pass 1 samples at least 1/SAMPLE_DIV of each query's probed codes
+constexpr uint64_t SAMPLE_DIV = FDB_IVF_SAMPLE_DIV;
 constexpr float INF = __builtin_huge_valf();
 
 struct Item {
@@ -535,19 +540,35 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
         if (len >= (uint64_t)LIST_K) p1 = j;
     }
     if (p1 < 0) p1 = pf;
-    unsigned long long lists = 0, codes = 0, codes2 = 0;
+    unsigned long long lists = 0, codes = 0;
+    // pass 1 scores the pass-1 list and the first tiles of the nearest other
+    // probes until it has seen 1/SAMPLE_DIV of the query's codes (the
+    // admission threshold is the 64th of what it saw, so pass 2 admits about
+    // 64 * SAMPLE_DIV codes)
+    uint64_t total = 0, seen = 0;
+    for (int j = 0; j < take; ++j) total += lend[pq[j]] - lbeg[pq[j]];
+    if (p1 >= 0) seen = lend[pq[p1]] - lbeg[pq[p1]];
     for (int j = 0; j < take; ++j) {
         const size_t i = (size_t)q * take + j;
         const uint32_t l = pq[j];
         const uint64_t len = lend[l] - lbeg[l];
         uint32_t key;
         if (len == 0) {
-            key = 2u * (uint32_t)nlist;
+            key = 3u * (uint32_t)nlist;
         } else {
-            key = j == p1 ? l : (uint32_t)nlist + l;
+            // the pass-1 list; the first tiles of the nearest other probes
+            // (probes are in ascending coarse distance) also go to pass 1;
+            // the other probes' lists are left to pass 2 whole
+            if (j == p1) {
+                key = l;
+            } else if (seen * SAMPLE_DIV < total) {
+                key = (uint32_t)nlist + l;
+                seen += len < (uint64_t)TILE_N ? len : (uint64_t)TILE_N;
+            } else {
+                key = 2u * (uint32_t)nlist + l;
+            }
             ++lists;
             codes += len;
-            if (j != p1) codes2 += len;
         }
         keys[i] = key;
         vals[i] = (uint32_t)i;
@@ -556,7 +577,6 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
         atomicAdd(stat, lists);
         atomicAdd(stat + 1, codes);
     }
-    (void)codes2;
 }
 
 // off[k] = the first position of key >= k in the sorted keys (k <= nkeys):
@@ -587,7 +607,7 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
                                uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
     const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const unsigned npairs = poff[2 * nlist];  // pairs with a non-empty list
+    const unsigned npairs = poff[3 * nlist];  // pairs with a non-empty list
     if (i >= npairs) return;
     const uint32_t v = vals[i];
     const uint32_t q = v / (uint32_t)take;
@@ -688,16 +708,18 @@ __device__ __forceinline__ ItemSlot item_slot(int s, const unsigned* __restrict_
     const int seg = kind == 0 ? 0 : 1;
     ItemSlot t;
     t.l = lorder[i];
-    if (kind == 2 && poff2) {
-        t.a0 = poff2[t.l];
-        t.cnt = poff2[t.l + 1] - t.a0;
+    if (kind >= 2) {
+        // kept pass-2 pairs: sampled (kind 2) then unsampled (kind 3) rows
+        const unsigned* o = poff2 + (kind - 2) * nlist;
+        t.a0 = o[t.l];
+        t.cnt = o[t.l + 1] - t.a0;
     } else {
         t.a0 = poff[seg * nlist + t.l];
         t.cnt = poff[seg * nlist + t.l + 1] - t.a0;
     }
     const unsigned len = (unsigned)(lend[t.l] - lbeg[t.l]);
     // codes [c_lo, c_hi) of the list this kind covers
-    t.c_lo = kind == 2 ? (unsigned)TILE_N : 0u;
+    t.c_lo = kind == 2 ? (unsigned)TILE_N : 0u;  // kind 2's first tile was in pass 1
     t.c_hi = kind == 1 ? min(len, (unsigned)TILE_N) : len;
     const unsigned span = t.c_hi > t.c_lo ? t.c_hi - t.c_lo : 0u;
     t.nchunk = (span + CHUNK_TILES * TILE_N - 1) / (CHUNK_TILES * TILE_N);
@@ -765,8 +787,8 @@ __global__ void __launch_bounds__(256)
 // every code of list l has real distance D >= (||r|| - Rh_l)^2 and
 // d~ >= D - E_l, so a pair with (||r|| - Rh_l)^2 - E_l > tadm[q] admits
 // nothing (the bounds of certify_kernel).  flags[i] = 1 for the pass-2 pairs
-// kept (lists longer than one tile: pass 2 covers tiles 1..); live[l] counts
-// them per list, stat[2] their pass-2 scores.
+// kept; live[l] (sampled) and live[nlist + l] (unsampled) count them per
+// list, stat[2] their pass-2 scores.
 __global__ void prune_kernel(const uint32_t* __restrict__ skeys, const unsigned* __restrict__ poff,
                              int nlist, unsigned np, const uint32_t* __restrict__ pair_q,
                              const float* __restrict__ pair_rn, const float* __restrict__ rh,
@@ -774,13 +796,17 @@ __global__ void prune_kernel(const uint32_t* __restrict__ skeys, const unsigned*
                              const uint64_t* __restrict__ lend, uint8_t* __restrict__ flags,
                              unsigned* __restrict__ live, unsigned long long* stat) {
     const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
-    const unsigned n1 = poff[nlist], npairs = poff[2 * nlist];
+    const unsigned n1 = poff[nlist], npairs = poff[3 * nlist];
     uint8_t keep = 0;
     unsigned long long scores = 0;
     if (i < np && i >= n1 && i < npairs) {
-        const uint32_t l = skeys[i] - (uint32_t)nlist;
+        // sampled pairs (keys nlist + l) cover tiles 1.., the others (keys
+        // 2 nlist + l) the whole list
+        const bool smp = skeys[i] < 2u * (uint32_t)nlist;
+        const uint32_t l = skeys[i] - (smp ? 1u : 2u) * (uint32_t)nlist;
         const uint64_t len = lend[l] - lbeg[l];
-        if (len > (uint64_t)TILE_N) {
+        const uint64_t skip = smp ? (uint64_t)TILE_N : 0;
+        if (len > skip) {
             const double C1 = 2.0 * (9.765625e-4 + 1.220703125e-4) * 1.05;
             const double C2 = 1.52587890625e-5;
             const double r = (double)rh[l];
@@ -791,8 +817,8 @@ __global__ void prune_kernel(const uint32_t* __restrict__ skeys, const unsigned*
             const double lower = Rl > 0.0 ? Rl * Rl * (1.0 - 1e-6) - El : -1.0;
             if (!(lower > (double)tadm[pair_q[i]])) {
                 keep = 1;
-                atomicAdd(live + l, 1u);
-                scores = len - TILE_N;
+                atomicAdd(live + (smp ? 0 : nlist) + l, 1u);
+                scores = len - skip;
             }
         }
     }
@@ -1530,7 +1556,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     const int nlist = (int)h->nlist;
     const size_t np = nq * take;
     const int dpad = h->tc_dpad;
-    const int nkeys = 2 * nlist + 1;
+    const int nkeys = 3 * nlist + 1;
     // --- group the pairs by (pass, list) ---
     h->t_keys.ensure(2 * np);
     h->t_vals.ensure(2 * np);
@@ -1583,7 +1609,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     const size_t all_tiles = h->tc_rows / TILE_N;
     const size_t max_items = np * ((max_tiles + CHUNK_TILES - 1) / CHUNK_TILES) / TILE_M +
                              np / TILE_M + 2 * (all_tiles / CHUNK_TILES + 1) +
-                             2 * (size_t)nlist + (np / TILE_M + nlist) + 2;
+                             2 * (size_t)nlist + (np / TILE_M + nlist) + 2 +
+                             (all_tiles / CHUNK_TILES + 1) + 2 * (size_t)nlist;
     h->t_items.ensure(max_items * sizeof(Item));
     Item* items = reinterpret_cast<Item*>(h->t_items.p);
     // items of slots [s0, s0 + nslot): count, exclusive sum, fill
@@ -1648,12 +1675,12 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         lbeg, lend, h->tc_rhl.p, h->t_tau.p, h->t_tadm.p);
     FDB_LAUNCH_CHECK();
     // --- drop the pass-2 pairs whose list cannot admit a code; compact the rest ---
-    h->t_live.ensure(2 * ((size_t)nlist + 1));
+    h->t_live.ensure(2 * (2 * (size_t)nlist + 1));
     h->t_pflag.ensure(np);
     h->t_sel.ensure(np + 1);
     unsigned* live = h->t_live.p;
-    unsigned* live_off = h->t_live.p + nlist + 1;
-    FDB_CUDA(cudaMemsetAsync(live, 0, ((size_t)nlist + 1) * 4, s));
+    unsigned* live_off = h->t_live.p + 2 * nlist + 1;
+    FDB_CUDA(cudaMemsetAsync(live, 0, (2 * (size_t)nlist + 1) * 4, s));
     prune_kernel<<<(unsigned)((np + 255) / 256), 256, 0, s>>>(
         h->t_keys.p + np, h->t_off.p, nlist, (unsigned)np, h->t_pq.p, h->t_rn.p, h->tc_rhl.p,
         h->t_tadm.p, lbeg, lend, h->t_pflag.p, live, stat);
@@ -1663,11 +1690,12 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         cub::CountingInputIterator<unsigned> ids(0u);
         FDB_CUDA(cub::DeviceSelect::Flagged(nullptr, t1, ids, h->t_pflag.p, h->t_sel.p + 1,
                                             h->t_sel.p, (int)np, s));
-        FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t2, live, live_off, nlist + 1, s));
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t2, live, live_off, 2 * nlist + 1, s));
         h->t_tmp3.ensure(std::max<size_t>(std::max(t1, t2), 1));
         FDB_CUDA(cub::DeviceSelect::Flagged(h->t_tmp3.p, t1, ids, h->t_pflag.p, h->t_sel.p + 1,
                                             h->t_sel.p, (int)np, s));
-        FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp3.p, t2, live, live_off, nlist + 1, s));
+        FDB_CUDA(cub::DeviceScan::ExclusiveSum(h->t_tmp3.p, t2, live, live_off, 2 * nlist + 1,
+                                               s));
     }
     h->t_a2.ensure(np * dpad);
     h->t_q2.ensure(np);
@@ -1677,7 +1705,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
         h->t_sel.p + 1, h->t_sel.p, dpad, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_a2.p,
         h->t_q2.p, h->t_rn2.p, h->t_s22.p);
     FDB_LAUNCH_CHECK();
-    make_items(2 * nlist, nlist, live_off);  // pass 2: tiles 1.. of the kept pairs' lists
+    make_items(2 * nlist, 2 * nlist, live_off);  // pass 2: the kept pairs' lists
     const CUtensorMap am2 = make_map(h->t_a2.p, np, dpad);
     p.pair_q = h->t_q2.p;
     p.pair_rn = h->t_rn2.p;
