@@ -63,7 +63,7 @@ constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
 #endif
 constexpr int CHUNK_TILES = FDB_IVF_CHUNK_TILES;  // B tiles per item at most (long lists are split)
 #ifndef FDB_IVF_SAMPLE_DIV
-#define FDB_IVF_SAMPLE_DIV 16
+#define FDB_IVF_SAMPLE_DIV 32
 #endif
 // pass 1 samples at least 1/SAMPLE_DIV of each query's probed codes
 constexpr uint64_t SAMPLE_DIV = FDB_IVF_SAMPLE_DIV;
@@ -339,6 +339,25 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (idx >= nitems) break;
             const Item it = items[idx];
             const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
+            if (quad * 32 >= (int)it.na) {
+                // no pair row in this warp's TMEM quadrant: keep the barrier
+                // phases in step (wait for each tile, release it) and skip
+                // the loads and the scoring
+                for (int t = 0; t < nt; ++t, ++g) {
+                    const int b = g % NACC, c = g % NCV;
+                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
+                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
+                        alive = false;
+                        break;
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(t_empty + b);
+                        mbar_arrive(cv_empty + c);
+                    }
+                }
+                continue;
+            }
             const bool rok = e < (int)it.na;
             const uint32_t pr = it.a0 + (uint32_t)e;
             const int q = rok ? (int)p.pair_q[pr] : 0;
