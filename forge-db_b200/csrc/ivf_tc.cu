@@ -111,6 +111,22 @@ constexpr int NCV = NSTAGE; // ||rhat||^2 stages (one per B stage)
 constexpr int NACC = 4;    // TMEM accumulators (128 columns each: all 512 columns)
 
 
+// Packed pairs of f32 (element 0 in the low half): sm_100's f32x2
+// instructions round each element exactly as the scalar _rn operation does.
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // 32 consecutive floats of a shared buffer (warp-uniform address: broadcast).
 __device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
@@ -385,6 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const float tt =
                     rok ? (tau - rn) + ldexpf(2.0f * fabsf(rn) + 2.0f * p.colmax + fabsf(tau), -20)
                         : -INF;
+                const uint64_t s22 = pack2(__float_as_uint(s2), __float_as_uint(s2));
                 auto score = [&](const uint32_t(&v)[32], const float* cvs, int cidx) {
                     const int nvalid = min(32, (int)it.nb - cidx);
                     const uint32_t tag0 = it.tag0 + (uint32_t)cidx;
@@ -393,11 +410,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     float x[32];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 cc = reinterpret_cast<const float4*>(cvs)[i];
-                        x[4 * i] = __fmaf_rn(s2, __uint_as_float(v[4 * i]), cc.x);
-                        x[4 * i + 1] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]), cc.y);
-                        x[4 * i + 2] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]), cc.z);
-                        x[4 * i + 3] = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]), cc.w);
+                        // fma.rn.f32x2: two independent fmaf_rn per instruction
+                        const ulonglong2 cc = reinterpret_cast<const ulonglong2*>(cvs)[i];
+                        const uint64_t x01 = fma2(s22, pack2(v[4 * i], v[4 * i + 1]), cc.x);
+                        const uint64_t x23 = fma2(s22, pack2(v[4 * i + 2], v[4 * i + 3]), cc.y);
+                        x[4 * i] = __uint_as_float((uint32_t)x01);
+                        x[4 * i + 1] = __uint_as_float((uint32_t)(x01 >> 32));
+                        x[4 * i + 2] = __uint_as_float((uint32_t)x23);
+                        x[4 * i + 3] = __uint_as_float((uint32_t)(x23 >> 32));
                     }
 #pragma unroll
                     for (int w2 = 16; w2 >= 1; w2 >>= 1)
@@ -454,17 +474,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // pass 1: every distance of the row's list goes to its dump row;
                 // padding columns carry ||rhat||^2 = +inf and store +inf
                 float* drow = rok ? p.dump + p.seg[pr] + it.col0 : nullptr;
+                const uint64_t s22 = pack2(__float_as_uint(s2), __float_as_uint(s2));
+                const uint64_t rn2 = pack2(__float_as_uint(rn), __float_as_uint(rn));
                 auto dump = [&](const uint32_t(&v)[32], const float* cvs, int col) {
                     if (!rok) return;
-                    float4* dst = reinterpret_cast<float4*>(drow + col);
+                    ulonglong2* dst = reinterpret_cast<ulonglong2*>(drow + col);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 cc = reinterpret_cast<const float4*>(cvs)[i];
-                        float4 o;
-                        o.x = __fmaf_rn(s2, __uint_as_float(v[4 * i]), __fadd_rn(rn, cc.x));
-                        o.y = __fmaf_rn(s2, __uint_as_float(v[4 * i + 1]), __fadd_rn(rn, cc.y));
-                        o.z = __fmaf_rn(s2, __uint_as_float(v[4 * i + 2]), __fadd_rn(rn, cc.z));
-                        o.w = __fmaf_rn(s2, __uint_as_float(v[4 * i + 3]), __fadd_rn(rn, cc.w));
+                        // fmaf_rn(s2, v, rn + ||rhat||^2), two per instruction
+                        const ulonglong2 cc = reinterpret_cast<const ulonglong2*>(cvs)[i];
+                        ulonglong2 o;
+                        o.x = fma2(s22, pack2(v[4 * i], v[4 * i + 1]), add2(rn2, cc.x));
+                        o.y = fma2(s22, pack2(v[4 * i + 2], v[4 * i + 3]), add2(rn2, cc.y));
                         dst[i] = o;
                     }
                 };

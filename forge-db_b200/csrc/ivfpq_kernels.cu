@@ -153,20 +153,29 @@ __global__ void __launch_bounds__(CT_THREADS)
 #pragma unroll
             for (int b = 0; b < CT_TC; ++b) acc[a][b] = 0.0f;
         if (nr > 0) stage(j, 8, nr);
+        // packed pairs of centroids: sub.rn.f32x2 / fma.rn.f32x2 perform two
+        // independent round-to-nearest operations, the same results as the
+        // scalar __fsub_rn / __fmaf_rn, in half the instructions
+        uint64_t* acc2 = reinterpret_cast<uint64_t*>(&acc[0][0]);
 #pragma unroll 4
         for (int r = 0; r < nr; ++r) {  // element i = j + 8 r
             const float4 qv = *reinterpret_cast<const float4*>(qb + r * CT_Q);
-            const float4 c0v = *reinterpret_cast<const float4*>(cb + r * CT_C);
-            const float4 c1v = *reinterpret_cast<const float4*>(cb + r * CT_C + 4);
+            const ulonglong2 c01 = *reinterpret_cast<const ulonglong2*>(cb + r * CT_C);
+            const ulonglong2 c23 = *reinterpret_cast<const ulonglong2*>(cb + r * CT_C + 4);
+            const uint64_t cpair[CT_TC / 2] = {c01.x, c01.y, c23.x, c23.y};
             const float qa[CT_TQ] = {qv.x, qv.y, qv.z, qv.w};
-            const float ca[CT_TC] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
 #pragma unroll
-            for (int a = 0; a < CT_TQ; ++a)
+            for (int a = 0; a < CT_TQ; ++a) {
+                const uint32_t qb32 = __float_as_uint(qa[a]);
+                const uint64_t qq = ((uint64_t)qb32 << 32) | qb32;
 #pragma unroll
-                for (int b = 0; b < CT_TC; ++b) {
-                    const float d = __fsub_rn(qa[a], ca[b]);
-                    acc[a][b] = __fmaf_rn(d, d, acc[a][b]);
+                for (int b2 = 0; b2 < CT_TC / 2; ++b2) {
+                    uint64_t d;
+                    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(qq), "l"(cpair[b2]));
+                    uint64_t& ac = acc2[a * (CT_TC / 2) + b2];
+                    asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(ac) : "l"(d));
                 }
+            }
         }
 #pragma unroll
         for (int a = 0; a < CT_TQ; ++a)
