@@ -568,54 +568,91 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
                                  const uint64_t* __restrict__ offs_full, int nlist,
                                  uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
                                  unsigned long long* stat) {
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= nq) return;
+    // one warp per query, lanes over its probes (32 at a time, in order)
+    const int q = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q >= nq) return;  // whole warp
     const uint32_t* pq = probes + (size_t)q * take;
-    // the pass-1 list is chosen from the unsharded list sizes, so that on a
-    // sharded index exactly one device holds it
+    // the pass-1 list: the first probe whose list holds >= 64 codes in the
+    // unsharded index (so that on a sharded index exactly one device holds
+    // it), else the first non-empty one
     int p1 = -1, pf = -1;
-    for (int j = 0; j < take && p1 < 0; ++j) {
-        const uint64_t len = offs_full[pq[j] + 1] - offs_full[pq[j]];
-        if (len > 0 && pf < 0) pf = j;
-        if (len >= (uint64_t)LIST_K) p1 = j;
-    }
-    if (p1 < 0) p1 = pf;
-    unsigned long long lists = 0, codes = 0;
-    // pass 1 scores the pass-1 list and the first tiles of the nearest other
-    // probes until it has seen 1/SAMPLE_DIV of the query's codes (the
-    // admission threshold is the 64th of what it saw, so pass 2 admits about
-    // 64 * SAMPLE_DIV codes)
-    uint64_t total = 0, seen = 0;
-    for (int j = 0; j < take; ++j) total += lend[pq[j]] - lbeg[pq[j]];
-    if (p1 >= 0) seen = lend[pq[p1]] - lbeg[pq[p1]];
-    for (int j = 0; j < take; ++j) {
-        const size_t i = (size_t)q * take + j;
-        const uint32_t l = pq[j];
-        const uint64_t len = lend[l] - lbeg[l];
-        uint32_t key;
-        if (len == 0) {
-            key = 3u * (uint32_t)nlist;
-        } else {
-            // the pass-1 list; the first tiles of the nearest other probes
-            // (probes are in ascending coarse distance) also go to pass 1;
-            // the other probes' lists are left to pass 2 whole
-            if (j == p1) {
-                key = l;
-            } else if (seen * SAMPLE_DIV < total) {
-                key = (uint32_t)nlist + l;
-                seen += len < (uint64_t)TILE_N ? len : (uint64_t)TILE_N;
-            } else {
-                key = 2u * (uint32_t)nlist + l;
-            }
-            ++lists;
-            codes += len;
+    uint64_t total = 0;
+    for (int j0 = 0; j0 < take; j0 += 32) {
+        const int j = j0 + lane;
+        uint64_t full = 0, len = 0;
+        if (j < take) {
+            const uint32_t l = pq[j];
+            full = offs_full[l + 1] - offs_full[l];
+            len = lend[l] - lbeg[l];
         }
-        keys[i] = key;
-        vals[i] = (uint32_t)i;
+        total += len;
+        const unsigned big = __ballot_sync(0xffffffffu, full >= (uint64_t)LIST_K);
+        const unsigned nz = __ballot_sync(0xffffffffu, full > 0);
+        if (p1 < 0 && big) p1 = j0 + __ffs(big) - 1;
+        if (pf < 0 && nz) pf = j0 + __ffs(nz) - 1;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (p1 < 0) p1 = pf;
+    // pass 1 scores the pass-1 list and the first tiles of the nearest other
+    // probes (probes are in ascending coarse distance) until it has seen
+    // 1/SAMPLE_DIV of the query's codes (the admission threshold is the 64th
+    // of what it saw, so pass 2 admits about 64 * SAMPLE_DIV codes); the
+    // other probes' lists are left to pass 2 whole
+    uint64_t seen = p1 >= 0 ? lend[pq[p1]] - lbeg[pq[p1]] : 0;
+    unsigned long long lists = 0, codes = 0;
+    for (int j0 = 0; j0 < take; j0 += 32) {
+        const int j = j0 + lane;
+        uint32_t l = 0;
+        uint64_t len = 0;
+        if (j < take) {
+            l = pq[j];
+            len = lend[l] - lbeg[l];
+        }
+        const bool other = j < take && len > 0 && j != p1;
+        // seen before this probe: the carry plus the earlier lanes' tiles
+        uint64_t c = other ? (len < (uint64_t)TILE_N ? len : (uint64_t)TILE_N) : 0;
+        uint64_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint64_t before = seen + incl - c;
+        // (sampling stops at the first probe that finds the quota met, so a
+        // probe is sampled exactly when the quota was not met before it)
+        const bool smp = other && before * SAMPLE_DIV < total;
+        if (j < take) {
+            uint32_t key;
+            if (len == 0) key = 3u * (uint32_t)nlist;
+            else if (j == p1) key = l;
+            else if (smp) key = (uint32_t)nlist + l;
+            else key = 2u * (uint32_t)nlist + l;
+            const size_t i = (size_t)q * take + j;
+            keys[i] = key;
+            vals[i] = (uint32_t)i;
+            if (len > 0) {
+                ++lists;
+                codes += len;
+            }
+        }
+        // carry: only sampled probes add to `seen` (as the serial rule)
+        uint64_t add = smp ? c : 0;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) add += __shfl_xor_sync(0xffffffffu, add, o);
+        seen += add;
     }
     if (stat) {
-        atomicAdd(stat, lists);
-        atomicAdd(stat + 1, codes);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            lists += __shfl_xor_sync(0xffffffffu, lists, o);
+            codes += __shfl_xor_sync(0xffffffffu, codes, o);
+        }
+        if (lane == 0) {
+            atomicAdd(stat, lists);
+            atomicAdd(stat + 1, codes);
+        }
     }
 }
 
@@ -638,20 +675,15 @@ __global__ void seg_offsets_kernel(const uint32_t* __restrict__ keys, unsigned n
 // (sa puts the largest |r_i| in [2^14, 2^15)), the coarse distance and the
 // combined scale -2 * 2^-(sa + sb).  Pairs whose scale leaves the float range
 // mark their query for the exact path.
-__global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
-                               int nlist, int take, const uint32_t* __restrict__ probes,
-                               const float* __restrict__ Q, const float* __restrict__ cents,
-                               int dim, int dpad, const float* __restrict__ pdist, int sb,
-                               __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
-                               float* __restrict__ pair_rn, float* __restrict__ pair_s2,
-                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
-    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// One warp writes the fp16 residual row of probe v (query q, list l) at
+// `row`: r = fl(q - c_l) scaled by 2^sa (largest |r_i| in [2^14, 2^15));
+// returns the combined scale s2 = -2^(1 - sa - sb), or 0 with *bad set when
+// the row cannot be represented (the query then takes the exact path).
+__device__ __forceinline__ float write_a_row(const float* __restrict__ Q,
+                                             const float* __restrict__ cents, int dim, int dpad,
+                                             uint32_t q, uint32_t l, int sb,
+                                             __half* __restrict__ row, bool* bad_out) {
     const int lane = threadIdx.x & 31;
-    const unsigned npairs = poff[3 * nlist];  // pairs with a non-empty list
-    if (i >= npairs) return;
-    const uint32_t v = vals[i];
-    const uint32_t q = v / (uint32_t)take;
-    const uint32_t l = probes[v];
     const float* qv = Q + (size_t)q * dim;
     const float* cv = cents + (size_t)l * dim;
     // lane holds components 4 lane .. 4 lane + 3 (dpad <= 128)
@@ -693,14 +725,65 @@ __global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned
                               __float2half_rn(bad ? 0.0f : __fmul_rn(r[1], scale)));
         h[1] = __halves2half2(__float2half_rn(bad ? 0.0f : __fmul_rn(r[2], scale)),
                               __float2half_rn(bad ? 0.0f : __fmul_rn(r[3], scale)));
-        *reinterpret_cast<uint2*>(a16 + i * dpad + 4 * lane) = *reinterpret_cast<uint2*>(h);
+        *reinterpret_cast<uint2*>(row + 4 * lane) = *reinterpret_cast<uint2*>(h);
+    }
+    *bad_out = bad;
+    return bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
+}
+
+// One warp per sorted pair i < poff[3 nlist]: pair_q, pair_rn and inv for
+// every pair; the A row and pair_s2 only for the pairs pass 1 scores
+// (i < poff[2 nlist]: pass-1 lists and sampled first tiles).  Pass-2 rows
+// are written later for the pairs pruning keeps (build_a2_kernel).
+__global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
+                               int nlist, int take, const uint32_t* __restrict__ probes,
+                               const float* __restrict__ Q, const float* __restrict__ cents,
+                               int dim, int dpad, const float* __restrict__ pdist, int sb,
+                               __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
+                               float* __restrict__ pair_rn, float* __restrict__ pair_s2,
+                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
+    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned npairs = poff[3 * nlist];  // pairs with a non-empty list
+    if (i >= npairs) return;
+    const uint32_t v = vals[i];
+    const uint32_t q = v / (uint32_t)take;
+    if (i < poff[2 * nlist]) {
+        bool bad = false;
+        const float s2 = write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a16 + i * dpad, &bad);
+        if (lane == 0) {
+            pair_s2[i] = s2;
+            if (bad) qbad[q] = 1u;
+        }
     }
     if (lane == 0) {
         pair_q[i] = q;
         pair_rn[i] = pdist[v];  // the exact coarse distance of this probe
-        pair_s2[i] = bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
+        inv[v] = (uint32_t)i;   // where probe v = q * take + j sits among the sorted pairs
+    }
+}
+
+// One warp per kept pass-2 pair j (sel[j] = its sorted index): its row of
+// the compact pass-2 matrix and per-pair values.
+__global__ void build_a2_kernel(const unsigned* __restrict__ sel, const unsigned* __restrict__ nsel,
+                                const uint32_t* __restrict__ vals, int take,
+                                const uint32_t* __restrict__ probes, const float* __restrict__ Q,
+                                const float* __restrict__ cents, int dim, int dpad,
+                                const float* __restrict__ pdist, int sb, __half* __restrict__ a2,
+                                uint32_t* __restrict__ q2, float* __restrict__ rn2,
+                                float* __restrict__ s22, uint32_t* __restrict__ qbad) {
+    const size_t j = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (j >= *nsel) return;
+    const uint32_t v = vals[sel[j]];
+    const uint32_t q = v / (uint32_t)take;
+    bool bad = false;
+    const float s2 = write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a2 + j * dpad, &bad);
+    if (lane == 0) {
+        q2[j] = q;
+        rn2[j] = pdist[v];
+        s22[j] = s2;
         if (bad) qbad[q] = 1u;
-        inv[v] = (uint32_t)i;  // where probe v = q * take + j sits among the sorted pairs
     }
 }
 
@@ -867,30 +950,6 @@ __global__ void prune_kernel(const uint32_t* __restrict__ skeys, const unsigned*
         // one atomic per warp (every lane of the warp is still here)
         for (int o = 16; o >= 1; o >>= 1) scores += __shfl_xor_sync(0xffffffffu, scores, o);
         if ((threadIdx.x & 31) == 0 && scores) atomicAdd(stat + 2, scores);
-    }
-}
-
-// The kept pass-2 pairs (sel[0 .. *nsel), ascending) gathered into a compact
-// matrix of A rows and their per-pair values, one warp per row.
-__global__ void gather_pairs_kernel(const unsigned* __restrict__ sel,
-                                    const unsigned* __restrict__ nsel, int dpad,
-                                    const __half* __restrict__ a16,
-                                    const uint32_t* __restrict__ pair_q,
-                                    const float* __restrict__ pair_rn,
-                                    const float* __restrict__ pair_s2, __half* __restrict__ a2,
-                                    uint32_t* __restrict__ q2, float* __restrict__ rn2,
-                                    float* __restrict__ s22) {
-    const unsigned j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (j >= *nsel) return;
-    const unsigned i = sel[j];
-    const uint4* src = reinterpret_cast<const uint4*>(a16 + (size_t)i * dpad);
-    uint4* dst = reinterpret_cast<uint4*>(a2 + (size_t)j * dpad);
-    for (int v = lane; v < dpad / 8; v += 32) dst[v] = src[v];
-    if (lane == 0) {
-        q2[j] = pair_q[i];
-        rn2[j] = pair_rn[i];
-        s22[j] = pair_s2[i];
     }
 }
 
@@ -1601,7 +1660,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_keys.ensure(2 * np);
     h->t_vals.ensure(2 * np);
     h->t_off.ensure((size_t)nkeys + 1);
-    pair_keys_kernel<<<(unsigned)((nq + 127) / 128), 128, 0, s>>>(
+    pair_keys_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, s>>>(
         probes, (int)nq, (int)take, lbeg, lend, h->offs.p, nlist, h->t_keys.p, h->t_vals.p,
         stat);
     FDB_LAUNCH_CHECK();
@@ -1741,9 +1800,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_q2.ensure(np);
     h->t_rn2.ensure(np);
     h->t_s22.ensure(np);
-    gather_pairs_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
-        h->t_sel.p + 1, h->t_sel.p, dpad, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_a2.p,
-        h->t_q2.p, h->t_rn2.p, h->t_s22.p);
+    build_a2_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
+        h->t_sel.p + 1, h->t_sel.p, svals, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad,
+        pdist, h->tc_sb, h->t_a2.p, h->t_q2.p, h->t_rn2.p, h->t_s22.p, h->t_qbad.p);
     FDB_LAUNCH_CHECK();
     make_items(2 * nlist, 2 * nlist, live_off);  // pass 2: the kept pairs' lists
     const CUtensorMap am2 = make_map(h->t_a2.p, np, dpad);
