@@ -416,6 +416,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
                 "sharded index needs a communicator of the same size");
     const size_t per = nq * k;
     StageTimer tm(s, st != nullptr);
+    StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
+    bool tensor_ran = false;
     tm.mark();
     if (k == 0) return;
     h->s_keys.ensure(per);
@@ -495,24 +497,20 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         a.skip = skip;
         if (tensor) {
             h->s_flags.ensure(nq + 1);
-            double pass_ms = 0.0;
-            std::vector<uint32_t> fail_cnt;
             h->tc_colv = call_skip ? ivfpq_call_colv(h, call_skip) : nullptr;
-            uint32_t nflag = 0;
             try {
-                nflag = ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend, h->s_keys.p,
-                                      h->s_flags.p, h->s_stat.p, st ? &pass_ms : nullptr,
-                                      &fail_cnt);
+                ivf_tc_search(h, dQ, nq, k, order, take, lbeg, lend, h->s_keys.p,
+                              h->s_flags.p, h->s_stat.p, st ? &pass_tm : nullptr);
             } catch (...) {
                 h->tc_colv = nullptr;
                 throw;
             }
             h->tc_colv = nullptr;
-            if (st) st->kernel_ms = pass_ms;
+            tensor_ran = true;
             tm.mark();
-            // exact re-scan of the lists that failed, merged with the certified rest
-            ivf_tc_rescan(h, a, k, order, nflag, fail_cnt, h->s_keys.p);
-            if (st) st->exact_rescans = nflag;
+            // exact re-scan of the lists that failed, merged with the certified
+            // rest (counts stay on the device: no synchronisation here)
+            ivf_tc_rescan(h, a, nq, k, order, h->s_keys.p);
         } else {
             launch_scan(s, a, order);
             tm.mark();
@@ -568,11 +566,31 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     if (h->rerank) launch_rerank(h, keys, ids, nq, k, dQ, k_out, d_ids, d_dists, d_counts);
     else launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
     tm.mark();
-    if (st) {
-        unsigned long long hs[4] = {0, 0, 0, 0};
-        if (take > 0)
-            FDB_CUDA(cudaMemcpyAsync(hs, h->s_stat.p, 32, cudaMemcpyDeviceToHost, s));
+    // The tensor path's error word (a bounded wait in the list scan that ran
+    // out) and the statistics are read into pinned words after one
+    // synchronisation: pin[0..3] statistics, pin[4] error word, pin[5] the
+    // number of re-scanned queries.
+    int tc_err = 0;
+    if (tensor_ran || st) {
+        uint64_t* pin = h->s_pin.get();
+        for (int i = 0; i < 6; ++i) pin[i] = 0;
+        if (tensor_ran) {
+            FDB_CUDA(cudaMemcpyAsync(pin + 4, ivf_tc_error_word(h), 4, cudaMemcpyDeviceToHost, s));
+            if (st) FDB_CUDA(cudaMemcpyAsync(pin + 5, h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
+        }
+        if (st && take > 0)
+            FDB_CUDA(cudaMemcpyAsync(pin, h->s_stat.p, 32, cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
+        tc_err = (int)(uint32_t)pin[4];
+    }
+    if (st) {
+        const uint64_t* hs = h->s_pin.get();
+        if (tensor_ran) {
+            double pass_ms = 0.0;
+            for (size_t i = 0; i + 1 < pass_tm.ev.size(); i += 2) pass_ms += pass_tm.ms(i, i + 1);
+            st->kernel_ms = pass_ms;
+            st->exact_rescans = (uint32_t)hs[5];
+        }
         st->lists_probed = hs[0];
         st->extended = hs[3];
         st->codes_scanned = hs[1];
@@ -592,6 +610,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         }
         st->total_ms = tm.ms(0, last);
     }
+    FDB_REQUIRE(tc_err == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
 }
 
 // ---------------------------------------------------------------------------

@@ -468,6 +468,90 @@ struct WarpTopK {
     }
 };
 
+// Threshold pre-pass for a warp's top-k over a stream of keys.  Offering
+// every key to WarpTopK admits, for keys in arbitrary order, about
+// k (1 + ln(n / k)) of them, each through a 64-bit bitonic merge; binning the
+// keys first lets only the bins that hold the k smallest be offered.
+// visit(f) must make the same warp-uniform sequence of f(key, valid) calls
+// on every lane each time it runs (it runs twice here, and the caller's
+// collecting pass is the third).  Bins split [min, max] of the keys' distance
+// bits (the high 32 bits) into 256 ranges; the bin of a key never decreases
+// as the key grows, so the keys in bins <= bstar are a prefix of the sorted
+// keys holding at least k of them (all keys if there are fewer) and contain
+// the k smallest.  hist: 256 words of this warp's shared memory.
+struct KeyBins {
+    uint32_t umin;
+    float scale;
+    int bstar;
+    __device__ __forceinline__ bool keep(uint64_t key) const {
+        const float b = (float)((uint32_t)(key >> 32) - umin) * scale;
+        return min(255, (int)b) <= bstar;
+    }
+};
+
+template <class Visit>
+__device__ __forceinline__ KeyBins warp_key_bins(Visit&& visit, int k, unsigned* hist) {
+    const int lane = threadIdx.x & 31;
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    visit([&](uint64_t key, bool valid) {
+        if (valid) {
+            const uint32_t u = (uint32_t)(key >> 32);
+            lo = min(lo, u);
+            hi = max(hi, u);
+        }
+    });
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    KeyBins b;
+    b.umin = lo;
+    b.bstar = 255;
+    b.scale = 0.0f;
+    if (lo > hi) return b;  // no valid key
+    b.scale = 256.0f / ((float)(hi - lo) + 1.0f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[j * 32 + lane] = 0u;
+    __syncwarp();
+    visit([&](uint64_t key, bool valid) {
+        if (valid) {
+            const float f = (float)((uint32_t)(key >> 32) - lo) * b.scale;
+            atomicAdd(&hist[min(255, (int)f)], 1u);
+        }
+    });
+    __syncwarp();
+    // lane owns bins 8 lane .. 8 lane + 7; the first bin where the running
+    // count reaches k is bstar
+    unsigned c[8], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        c[j] = hist[8 * lane + j];
+        sum += c[j];
+    }
+    unsigned incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const unsigned reach = __ballot_sync(0xffffffffu, incl >= (unsigned)k);
+    if (reach) {
+        const int owner = __ffs(reach) - 1;
+        int bs = 255;
+        unsigned run = incl - sum;
+        bool found = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            run += c[j];
+            if (!found && run >= (unsigned)k) {
+                bs = 8 * lane + j;
+                found = true;
+            }
+        }
+        b.bstar = __shfl_sync(0xffffffffu, bs, owner);
+    }
+    __syncwarp();  // hist may be reused
+    return b;
+}
+
 // Block-wide merge: every warp has stored its k best to smem[w*k ...]; warp 0
 // folds them into its own list.  Caller syncs before and after.
 template <int P>

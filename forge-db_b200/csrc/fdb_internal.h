@@ -113,6 +113,23 @@ struct DeviceGuard {
     }
 };
 
+// A few words of pinned host memory for small device-to-host readbacks: an
+// asynchronous copy into pageable memory waits for the stream and costs a
+// round trip each, into pinned memory it is queued like a kernel.
+struct PinnedWords {
+    uint64_t* p = nullptr;
+    PinnedWords() = default;
+    PinnedWords(const PinnedWords&) = delete;
+    PinnedWords& operator=(const PinnedWords&) = delete;
+    ~PinnedWords() {
+        if (p) cudaFreeHost(p);
+    }
+    uint64_t* get() {  // 8 words
+        if (!p) FDB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p), 64, cudaHostAllocPortable));
+        return p;
+    }
+};
+
 // Times device stages on a stream with CUDA events.
 struct StageTimer {
     cudaStream_t s;
@@ -264,13 +281,13 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int or
 bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k);
 void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,
                     const std::vector<float>& bmax_host);
-uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
-                       size_t take, const uint64_t* lbeg, const uint64_t* lend,
-                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
-                       double* pass_ms, std::vector<uint32_t>* fail_cnt_host);
+void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
+                   const uint64_t* lbeg, const uint64_t* lend, uint64_t* out_keys,
+                   uint32_t* flags, unsigned long long* stat, StageTimer* pass_tm);
+int* ivf_tc_error_word(fdb_ivfpq* h);
 struct ScanParams;
-void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, uint32_t nflag,
-                   const std::vector<uint32_t>& fail_cnt, uint64_t* out_keys);
+void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t nq, size_t k, int order,
+                   uint64_t* out_keys);
 void bf_upload(fdb_bf* h);
 void bf_shard(fdb_bf* h, int rank, int world);
 void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_ids,
@@ -359,6 +376,7 @@ struct fdb_ivfpq {
     fdb::DevBuf<float> s_dists;
     fdb::DevBuf<uint32_t> s_counts, s_flags;
     fdb::DevBuf<unsigned long long> s_stat;
+    fdb::PinnedWords s_pin;  // end-of-call readbacks (statistics, error word, counts)
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
     fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv, t_plen,
         t_seg, t_fprobes, t_fcnt, t_uoff, t_unit_q, t_unit_l;

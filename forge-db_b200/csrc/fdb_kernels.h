@@ -37,6 +37,11 @@ struct ScanParams {
     bool out_by_block;
     // nullable bitmap over rows: set bits are skipped (tombstones, filters)
     const uint32_t* skip;
+    // nullable: the number of queries (blocks of work) is *nq_dev - nq_dev_base,
+    // read on the device (clamped to [0, nq]); grid_cap > 0 caps the grid
+    const uint32_t* nq_dev;
+    uint32_t nq_dev_base;
+    int grid_cap;
 };
 
 struct RescoreParams {

@@ -1360,17 +1360,24 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) certify_kernel(CertParams r, 
 // 64th) with d~ <= the query's threshold is collected, rescored exactly (one
 // entry per thread) and merged into its exact top-k row.  A query with more
 // than EXT_MAX such entries goes to the re-scan path instead.
+typedef cub::BlockScan<unsigned, EXT_THREADS> ExtScan;
+struct ExtShared {
+    uint64_t keys[EXT_MAX];
+    uint64_t buf[64];
+    unsigned pstart[EXT_MAX_TAKE], plen[EXT_MAX_TAKE], ptag[EXT_MAX_TAKE];
+    unsigned cnt;
+    float dres[EXT_THREADS / 32][32];
+    typename ExtScan::TempStorage scan_tmp;
+};
+
+// One extended query (flag slot `slot`), the whole block.
 template <int ORDER, int P>
-__global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
-    __shared__ uint64_t keys[EXT_MAX];
-    __shared__ uint64_t buf[64];
-    __shared__ unsigned pstart[EXT_MAX_TAKE], plen[EXT_MAX_TAKE], ptag[EXT_MAX_TAKE];
-    __shared__ unsigned cnt;
-    __shared__ float dres[EXT_THREADS / 32][32];
-    typedef cub::BlockScan<unsigned, EXT_THREADS> Scan;
-    __shared__ typename Scan::TempStorage scan_tmp;
-    const uint32_t slot = blockIdx.x;
-    if (slot >= *r.ext_count) return;  // whole block
+__device__ __forceinline__ void extend_slot(const CertParams& r, uint32_t slot, ExtShared& sh) {
+    uint64_t* keys = sh.keys;
+    unsigned* pstart = sh.pstart;
+    unsigned* plen = sh.plen;
+    unsigned* ptag = sh.ptag;
+    unsigned& cnt = sh.cnt;
     const int t = threadIdx.x;
     const int q = (int)r.ext_list[slot];
     const float thr = r.ext_thr[slot];
@@ -1391,7 +1398,7 @@ __global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
         }
     }
     unsigned off, total;
-    Scan(scan_tmp).ExclusiveSum(nb, off, total);
+    ExtScan(sh.scan_tmp).ExclusiveSum(nb, off, total);
     if (t < r.take) plen[t] = off;  // prefix
     __syncthreads();
     const int take = r.take;
@@ -1435,13 +1442,13 @@ __global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
         }
         const int m = r.m, sub = r.dim / m;
         const float d = warp_exact_adc<ORDER>(r.Q + (size_t)q * r.dim, r.cents, r.dim, r.cb,
-                                              r.codes, m, sub, pos, lo, valid, dres[t >> 5]);
+                                              r.codes, m, sub, pos, lo, valid, sh.dres[t >> 5]);
         if (valid) keys[t] = make_key(d, pos);
     }
     __syncthreads();
     if (t >= 32) return;
     WarpTopK<P> tk;
-    tk.init(r.k, buf);
+    tk.init(r.k, sh.buf);
     tk.ingest(keys, (int)n);
     uint64_t* row = r.out_keys + (size_t)q * r.k;
     tk.ingest(row, r.k);
@@ -1449,40 +1456,87 @@ __global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
     if (t == 0 && r.stat) atomicAdd(r.stat + 3, 1ull);
 }
 
-// ---------------------------------------------------------------------------
-// exact re-scan of failed lists, one block per (query, list)
-// ---------------------------------------------------------------------------
-// units uoff[f] .. uoff[f+1] of flag slot f: (query, failed list)
-__global__ void expand_units_kernel(int nflag, int take, const uint32_t* __restrict__ flag_list,
-                                    const uint32_t* __restrict__ fail_probes,
-                                    const uint32_t* __restrict__ uoff,
-                                    uint32_t* __restrict__ unit_q, uint32_t* __restrict__ unit_l) {
-    const int f = blockIdx.x * blockDim.x + threadIdx.x;
-    if (f >= nflag) return;
-    const uint32_t q = flag_list[f];
-    for (uint32_t u = uoff[f], j = 0; u < uoff[f + 1]; ++u, ++j) {
-        unit_q[u] = q;
-        unit_l[u] = fail_probes[(size_t)f * take + j];
+// A grid of a few blocks per SM walks the extended queries (their count is
+// only known on the device).
+template <int ORDER, int P>
+__global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
+    __shared__ ExtShared sh;
+    const uint32_t count = *r.ext_count;
+    for (uint32_t slot = blockIdx.x; slot < count; slot += gridDim.x) {
+        __syncthreads();  // the previous slot's shared state is no longer read
+        extend_slot<ORDER, P>(r, slot, sh);
     }
 }
 
-// One warp per flag slot: the query's seed (its out_keys row) and the exact
-// top-k of each of its re-scanned lists, merged into its out_keys row.
+// ---------------------------------------------------------------------------
+// exact re-scan of failed lists, one block per (query, list)
+// ---------------------------------------------------------------------------
+// Unit offsets: uoff[f] = the failed lists of flag slots 0 .. f-1 (flags[0]
+// slots, fail_cnt[f] lists each); *nunits = their total.  One block.
+__global__ void __launch_bounds__(1024)
+    unit_offsets_kernel(const uint32_t* __restrict__ flags, const uint32_t* __restrict__ fail_cnt,
+                        uint32_t* __restrict__ uoff, uint32_t* __restrict__ nunits) {
+    typedef cub::BlockScan<unsigned, 1024> Scan;
+    __shared__ typename Scan::TempStorage tmp;
+    __shared__ unsigned carry;
+    const unsigned nflag = flags[0];
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (unsigned b = 0; b < nflag; b += 1024) {
+        const unsigned f = b + threadIdx.x;
+        const unsigned v = f < nflag ? fail_cnt[f] : 0u;
+        unsigned ex, tot;
+        Scan(tmp).ExclusiveSum(v, ex, tot);
+        const unsigned c0 = carry;
+        if (f < nflag) uoff[f] = c0 + ex;
+        __syncthreads();  // every thread has read carry (and tmp is free)
+        if (threadIdx.x == 0) carry = c0 + tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        uoff[nflag] = carry;
+        *nunits = carry;
+    }
+}
+
+// The units u in [r0, r0 + ucap) of flag slot f (units uoff[f] .. uoff[f+1]:
+// its query and its failed lists in order), written at u - r0.
+__global__ void expand_units_kernel(const uint32_t* __restrict__ flags, int take,
+                                    const uint32_t* __restrict__ fail_probes,
+                                    const uint32_t* __restrict__ uoff, uint32_t r0, uint32_t ucap,
+                                    uint32_t* __restrict__ unit_q, uint32_t* __restrict__ unit_l) {
+    const uint32_t f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= flags[0]) return;
+    const uint32_t q = flags[1 + f];
+    const uint32_t u0 = uoff[f], u1 = uoff[f + 1];
+    const uint32_t lo = max(u0, r0), hi = min(u1, r0 + ucap);
+    for (uint32_t u = lo; u < hi; ++u) {
+        unit_q[u - r0] = q;
+        unit_l[u - r0] = fail_probes[(size_t)f * take + (u - u0)];
+    }
+}
+
+// One warp per flag slot (grid-stride over flags[0] slots): the query's row
+// (its seed, or the merge of earlier rounds) and the exact top-k of each of
+// its units in [r0, r0 + ucap), merged into its out_keys row.
 template <int P>
 __global__ void __launch_bounds__(256)
-    merge_units_kernel(int nflag, int k, const uint32_t* __restrict__ flag_list,
-                       const uint32_t* __restrict__ uoff, const uint64_t* __restrict__ unit_keys,
-                       uint64_t* __restrict__ out_keys) {
+    merge_units_kernel(int k, const uint32_t* __restrict__ flags,
+                       const uint32_t* __restrict__ uoff, uint32_t r0, uint32_t ucap,
+                       const uint64_t* __restrict__ unit_keys, uint64_t* __restrict__ out_keys) {
     __shared__ uint64_t buf[8 * 64];
     const int warp = threadIdx.x >> 5;
-    const int f = blockIdx.x * 8 + warp;
-    if (f >= nflag) return;
-    uint64_t* row = out_keys + (size_t)flag_list[f] * k;
-    WarpTopK<P> tk;
-    tk.init(k, buf + warp * 64);
-    tk.ingest(row, k);
-    for (uint32_t u = uoff[f]; u < uoff[f + 1]; ++u) tk.ingest(unit_keys + (size_t)u * k, k);
-    tk.store(row);
+    const uint32_t nflag = flags[0];
+    for (uint32_t f = blockIdx.x * 8 + warp; f < nflag; f += gridDim.x * 8) {
+        const uint32_t lo = max(uoff[f], r0), hi = min(uoff[f + 1], r0 + ucap);
+        if (lo >= hi) continue;  // warp-uniform
+        uint64_t* row = out_keys + (size_t)flags[1 + f] * k;
+        WarpTopK<P> tk;
+        tk.init(k, buf + warp * 64);
+        tk.ingest(row, k);
+        for (uint32_t u = lo; u < hi; ++u) tk.ingest(unit_keys + (size_t)(u - r0) * k, k);
+        tk.store(row);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1648,7 +1702,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
               const uint32_t* probes, const float* pdist, const uint64_t* lbeg,
               const uint64_t* lend, uint64_t* out_keys, uint32_t* flags, uint32_t qbase,
               unsigned long long* stat, int* err, uint32_t* fail_probes, uint32_t* fail_cnt,
-              cudaEvent_t ev0, cudaEvent_t ev1) {
+              StageTimer* pass_tm) {
     using namespace ivtc;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -1812,9 +1866,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.tau = h->t_tadm.p;
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
-    if (ev0) FDB_CUDA(cudaEventRecord(ev0, s));
+    if (pass_tm) pass_tm->mark();
     launch_pass<EPI_FILTER>(s, am2, bm, grid, p);
-    if (ev1) FDB_CUDA(cudaEventRecord(ev1, s));
+    if (pass_tm) pass_tm->mark();
     // --- shortlist, exact rescoring, certification ---
     h->s_approx.ensure(nq * LIST_K);
     select_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(h->t_part.p, h->t_cand.p,
@@ -1892,9 +1946,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
     else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
     FDB_LAUNCH_CHECK();
-    // extended queries: one block each (grid sized for all of them); those
-    // with too many entries then take the re-scan path
-    const unsigned egrid = (unsigned)nq;
+    // extended queries (a block each, in turn); those with too many entries
+    // then take the re-scan path
+    const unsigned egrid = (unsigned)std::min<size_t>(nq, (size_t)c.sm_count * 8);
     if (order == ORDER_LANE8) {
         if (p2) extend_kernel<ORDER_LANE8, 2><<<egrid, EXT_THREADS, 0, s>>>(r);
         else extend_kernel<ORDER_LANE8, 1><<<egrid, EXT_THREADS, 0, s>>>(r);
@@ -1911,16 +1965,18 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 }  // namespace
 
 // Tensor-core shortlist + exact rescoring of nq queries whose probes and
-// their coarse distances are in h->s_probe / h->s_pdist.  Writes [nq][k] exact keys
-// and lists uncertified queries in flags (flags[0] = count, then indices);
-// returns that count.  For each listed query, t_fprobes / t_fcnt name the
-// lists to re-scan exactly and its out_keys row holds the seed (the exact
-// top-k of its shortlisted codes in the other lists).  Queries run in chunks that keep the pass-1 dump
-// (one row of distances per query) within 1 GiB.
-uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order,
-                       size_t take, const uint64_t* lbeg, const uint64_t* lend,
-                       uint64_t* out_keys, uint32_t* flags, unsigned long long* stat,
-                       double* pass_ms, std::vector<uint32_t>* fail_cnt_host) {
+// their coarse distances are in h->s_probe / h->s_pdist, enqueued without a
+// host synchronisation.  Writes [nq][k] exact keys and lists uncertified
+// queries in flags (flags[0] = count, then indices); for each listed query,
+// t_fprobes / t_fcnt name the lists to re-scan exactly (ivf_tc_rescan) and its
+// out_keys row holds the seed (the exact top-k of its shortlisted codes in
+// the other lists).  A bounded wait that ran out sets the word that
+// ivf_tc_error_word names.  Queries run in chunks that keep the pass-1 dump
+// (one row of distances per query) within 1 GiB.  pass_tm (nullable) gets a
+// mark before and after each pass-2 launch.
+void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
+                   const uint64_t* lbeg, const uint64_t* lend, uint64_t* out_keys,
+                   uint32_t* flags, unsigned long long* stat, StageTimer* pass_tm) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
@@ -1930,77 +1986,61 @@ uint32_t ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int o
     h->t_range.ensure(8);
     h->t_fprobes.ensure(nq * take);
     h->t_fcnt.ensure(nq);
-    int* err = reinterpret_cast<int*>(h->t_range.p + 4);
+    int* err = ivf_tc_error_word(h);
     FDB_CUDA(cudaMemsetAsync(flags, 0, 4, s));
     FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
-    // device time of pass 2, one event pair per chunk (only when asked for)
-    std::vector<cudaEvent_t> evs;
-    const size_t nchunks = (nq + chunk - 1) / chunk;
-    if (pass_ms) {
-        evs.resize(2 * nchunks, nullptr);
-        for (auto& e : evs) FDB_CUDA(cudaEventCreate(&e));
-    }
-    struct EvFree {
-        std::vector<cudaEvent_t>& v;
-        ~EvFree() { for (auto e : v) if (e) cudaEventDestroy(e); }
-    } ev_free{evs};
-    for (size_t q0 = 0, ci = 0; q0 < nq; q0 += chunk, ++ci) {
+    for (size_t q0 = 0; q0 < nq; q0 += chunk) {
         const size_t nc = std::min(chunk, nq - q0);
         tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,
                  h->s_pdist.p + q0 * take, lbeg, lend, out_keys + q0 * k, flags,
-                 (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p,
-                 pass_ms ? evs[2 * ci] : nullptr, pass_ms ? evs[2 * ci + 1] : nullptr);
+                 (uint32_t)q0, stat, err, h->t_fprobes.p, h->t_fcnt.p, pass_tm);
     }
-    uint32_t hv[2] = {0, 0};
-    FDB_CUDA(cudaMemcpyAsync(&hv[0], flags, 4, cudaMemcpyDeviceToHost, s));
-    FDB_CUDA(cudaMemcpyAsync(&hv[1], err, 4, cudaMemcpyDeviceToHost, s));
-    if (fail_cnt_host) {
-        // read with the count in one synchronisation (only the first count entries matter)
-        fail_cnt_host->resize(nq);
-        FDB_CUDA(cudaMemcpyAsync(fail_cnt_host->data(), h->t_fcnt.p, nq * 4,
-                                 cudaMemcpyDeviceToHost, s));
-    }
-    FDB_CUDA(cudaStreamSynchronize(s));
-    FDB_REQUIRE(hv[1] == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
-    if (fail_cnt_host) fail_cnt_host->resize(hv[0]);
-    if (pass_ms) {
-        double tot = 0.0;
-        for (size_t ci = 0; ci < nchunks; ++ci) {
-            float ms = 0.0f;
-            FDB_CUDA(cudaEventElapsedTime(&ms, evs[2 * ci], evs[2 * ci + 1]));
-            tot += ms;
-        }
-        *pass_ms = tot;
-    }
-    return hv[0];
+}
+
+int* ivf_tc_error_word(fdb_ivfpq* h) {
+    h->t_range.ensure(8);
+    return reinterpret_cast<int*>(h->t_range.p + 4);
 }
 
 }  // namespace fdb
 
 namespace fdb {
 
-// Exact re-scan of the lists that failed certification: one block per
-// (flagged query, failed list) computes that list's exact top-k, and each
-// flagged query's seed and lists are merged into its keys row.
-void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, uint32_t nflag,
-                   const std::vector<uint32_t>& fail_cnt, uint64_t* out_keys) {
-    if (nflag == 0) return;
+// Exact re-scan of the lists that failed certification, driven by the
+// counts on the device (no host synchronisation): one block per (flagged
+// query, failed list) unit computes that list's exact top-k, and each flagged
+// query's seed and lists are merged into its out_keys row.  Units run in
+// rounds of at most ucap, which bounds the per-unit key buffer; one round
+// covers every unit the batch can produce unless nq * take * k is large.
+void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t nq, size_t k, int order,
+                   uint64_t* out_keys) {
+    if (nq == 0) return;
     cudaStream_t s = h->ctx->c.stream;
-    std::vector<uint32_t> uoff(nflag + 1, 0);
-    for (uint32_t f = 0; f < nflag; ++f) uoff[f + 1] = uoff[f] + fail_cnt[f];
-    const uint32_t nu = uoff[nflag];
-    h->t_uoff.ensure(nflag + 1);
-    FDB_CUDA(cudaMemcpyAsync(h->t_uoff.p, uoff.data(), (nflag + 1) * 4, cudaMemcpyHostToDevice, s));
-    if (nu > 0) {
-        h->t_unit_q.ensure(nu);
-        h->t_unit_l.ensure(nu);
-        h->t_unit_keys.ensure((size_t)nu * k);
-        ivtc::expand_units_kernel<<<(nflag + 127) / 128, 128, 0, s>>>(
-            (int)nflag, base.nprobe, h->s_flags.p + 1, h->t_fprobes.p, h->t_uoff.p, h->t_unit_q.p,
-            h->t_unit_l.p);
+    const size_t take = (size_t)base.nprobe;
+    const size_t worst = nq * take;
+    const size_t key_budget = (size_t)64 << 20;  // bytes of per-unit keys
+    const size_t ucap = std::max<size_t>(1, std::min(worst, key_budget / (k * sizeof(uint64_t))));
+    FDB_REQUIRE(worst < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) units");
+    h->t_uoff.ensure(nq + 2);  // offsets per flag slot, then the unit count
+    h->t_unit_q.ensure(ucap);
+    h->t_unit_l.ensure(ucap);
+    h->t_unit_keys.ensure(ucap * k);
+    uint32_t* nunits = h->t_uoff.p + nq + 1;
+    const uint32_t* flags = h->s_flags.p;
+    ivtc::unit_offsets_kernel<<<1, 1024, 0, s>>>(flags, h->t_fcnt.p, h->t_uoff.p, nunits);
+    FDB_LAUNCH_CHECK();
+    const int sms = h->ctx->c.sm_count;
+    const unsigned mgrid = (unsigned)std::min<size_t>((nq + 7) / 8, (size_t)sms * 8);
+    for (size_t r0 = 0; r0 < worst; r0 += ucap) {
+        ivtc::expand_units_kernel<<<(unsigned)((nq + 127) / 128), 128, 0, s>>>(
+            flags, (int)take, h->t_fprobes.p, h->t_uoff.p, (uint32_t)r0, (uint32_t)ucap,
+            h->t_unit_q.p, h->t_unit_l.p);
         FDB_LAUNCH_CHECK();
         ScanParams e = base;
-        e.nq = (int)nu;
+        e.nq = (int)ucap;
+        e.nq_dev = nunits;
+        e.nq_dev_base = (uint32_t)r0;
+        e.grid_cap = sms * 8;
         e.qidx = h->t_unit_q.p;
         e.probe_list = h->t_unit_l.p;
         e.probe_cnt = nullptr;
@@ -2012,16 +2052,16 @@ void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t k, int order, ui
         e.stat = nullptr;
         e.btab = nullptr;
         launch_scan(s, e, order);
+        if (k > 32)
+            ivtc::merge_units_kernel<2><<<mgrid, 256, 0, s>>>(
+                (int)k, flags, h->t_uoff.p, (uint32_t)r0, (uint32_t)ucap, h->t_unit_keys.p,
+                out_keys);
+        else
+            ivtc::merge_units_kernel<1><<<mgrid, 256, 0, s>>>(
+                (int)k, flags, h->t_uoff.p, (uint32_t)r0, (uint32_t)ucap, h->t_unit_keys.p,
+                out_keys);
+        FDB_LAUNCH_CHECK();
     }
-    if (k > 32)
-        ivtc::merge_units_kernel<2><<<(nflag + 7) / 8, 256, 0, s>>>(
-            (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
-    else
-        ivtc::merge_units_kernel<1><<<(nflag + 7) / 8, 256, 0, s>>>(
-            (int)nflag, (int)k, h->s_flags.p + 1, h->t_uoff.p, h->t_unit_keys.p, out_keys);
-    FDB_LAUNCH_CHECK();
-    // (the offsets came from pageable memory: the copy call returned once they
-    // were staged, so the vector may go)
 }
 
 }  // namespace fdb

@@ -240,27 +240,33 @@ __global__ void __launch_bounds__(SEL_WARPS * 32)
     select_kernel(const float* __restrict__ D, int nq, int nlist, int take,
                   uint32_t* __restrict__ probes, float* __restrict__ pdist) {
     __shared__ uint64_t buf[SEL_WARPS * 64];
+    __shared__ unsigned hist[SEL_WARPS * 256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * SEL_WARPS + warp;
     if (q >= nq) return;  // whole warp leaves together
     WarpTopK<P> tk;
     tk.init(take, buf + warp * 64);
     const float* row = D + (size_t)q * nlist;
-    // eight loads in flight per lane, then their keys
-    for (int base = 0; base < nlist; base += 32 * 8) {
-        float v[8];
+    // the row's keys, eight loads in flight per lane
+    auto visit = [&](auto&& f) {
+        for (int base = 0; base < nlist; base += 32 * 8) {
+            float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int l = base + u * 32 + lane;
-            v[u] = l < nlist ? row[l] : 0.0f;
-        }
+            for (int u = 0; u < 8; ++u) {
+                const int l = base + u * 32 + lane;
+                v[u] = l < nlist ? row[l] : 0.0f;
+            }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int l = base + u * 32 + lane;
-            const bool valid = l < nlist;
-            tk.add(valid ? make_key(v[u], (uint32_t)l) : KEY_NONE, valid);
+            for (int u = 0; u < 8; ++u) {
+                const int l = base + u * 32 + lane;
+                const bool valid = l < nlist;
+                f(valid ? make_key(v[u], (uint32_t)l) : KEY_NONE, valid);
+            }
         }
-    }
+    };
+    // only the bins that hold the take smallest keys are offered
+    const KeyBins kb = warp_key_bins(visit, take, hist + warp * 256);
+    visit([&](uint64_t key, bool valid) { tk.add(key, valid && kb.keep(key)); });
     tk.flush();
 #pragma unroll
     for (int e = 0; e < P; ++e) {
@@ -426,7 +432,12 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(ScanParams a) {
     uint64_t* lists = wbuf + SCAN_WARPS * 64;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = a.dim / m;
-    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+    int nq = a.nq;
+    if (a.nq_dev) {
+        const uint32_t total = *a.nq_dev;
+        nq = total > a.nq_dev_base ? (int)min((uint32_t)a.nq, total - a.nq_dev_base) : 0;
+    }
+    for (int qi = blockIdx.x; qi < nq; qi += gridDim.x) {
         const int q = a.qidx ? (int)a.qidx[qi] : qi;
         const float* qv = a.Q + (size_t)q * a.dim;
         if (TABLES) {
@@ -562,7 +573,7 @@ void launch_scan(cudaStream_t s, const ScanParams& a, int order) {
     if (a.nq == 0) return;
     FDB_REQUIRE(a.k >= 1 && a.k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED, "k out of range");
     const bool tables = a.btab != nullptr;
-    const int grid = a.nq;
+    const int grid = a.grid_cap > 0 ? std::min(a.nq, a.grid_cap) : a.nq;
     if (order == ORDER_LANE8) {
         if (tables) launch_scan_o<ORDER_LANE8, true>(s, a, grid);
         else launch_scan_o<ORDER_LANE8, false>(s, a, grid);

@@ -396,6 +396,26 @@ def test_ivfpq_tensor_mode_ties_and_short_lists(fg, ctx, orc):
         assert_topk_match(ids, d, cnt, oi, od, oc, f"tensor tiny lists nprobe={nprobe}")
 
 
+def test_ivfpq_tensor_mode_rescan_rounds(fg, ctx, orc):
+    """The exact re-scan runs from counts kept on the device, in rounds of at
+    most 64 MiB of per-unit keys (131072 units at k = 64).  8200 queries x 16
+    probes can produce more units than one round holds; runs of 400 identical
+    codes exceed both the shortlist and the extension, so queries re-scan."""
+    rng = np.random.default_rng(33)
+    base = (rng.random((25, 64), dtype=np.float32) * 10).astype(np.float32)
+    X = np.repeat(base, 400, axis=0)
+    ix = fg.IVFPQIndex.build(X, 16, 8, ctx=ctx, seed=3)
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    ix.set_nprobe(16)
+    ox = _oracle_index(orc, ix)
+    ox.set_nprobe(16)
+    Q = base[rng.integers(0, 25, 8200)] + rng.random((8200, 64), dtype=np.float32) * 0.05
+    ids, d, cnt, st = ix.batch_search_arrays(Q, 64, stats=True)
+    oi, od, oc = ox.batch_search(Q, 64)
+    assert_topk_match(ids, d, cnt, oi, od, oc, "tensor re-scan rounds")
+    assert st.exact_rescans > 0
+
+
 def test_ivfpq_tensor_mode_gmm_certifies(fg, ctx, orc, gmm_index):
     """Descriptor-like data: the fp16 bound certifies nearly every query."""
     ix, X, Q = gmm_index
