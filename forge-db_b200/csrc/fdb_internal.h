@@ -390,7 +390,7 @@ struct fdb_ivfpq {
     fdb::DevBuf<uint64_t> t_part, t_cand;
     fdb::DevBuf<unsigned> t_cand_cnt;
     fdb::DevBuf<uint32_t> t_ext;        // [0] extended queries, then their indices
-    fdb::DevBuf<float> t_ext_thr, t_tadm;
+    fdb::DevBuf<float> t_ext_thr, t_tadm, t_eb;
     fdb::DevBuf<unsigned> t_icnt;       // item counts per (kind, list) and their offsets
     fdb::DevBuf<uint8_t> t_tmp2;        // scan scratch for the item offsets
     // pass-2 pruning: kept pairs per list and their offsets, flags, the kept

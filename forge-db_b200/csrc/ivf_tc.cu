@@ -731,59 +731,70 @@ __device__ __forceinline__ float write_a_row(const float* __restrict__ Q,
     return bad ? 0.0f : -__uint_as_float((uint32_t)(se + 127) << 23);
 }
 
-// One warp per sorted pair i < poff[3 nlist]: pair_q, pair_rn and inv for
-// every pair; the A row and pair_s2 only for the pairs pass 1 scores
-// (i < poff[2 nlist]: pass-1 lists and sampled first tiles).  Pass-2 rows
-// are written later for the pairs pruning keeps (build_a2_kernel).
-__global__ void build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
-                               int nlist, int take, const uint32_t* __restrict__ probes,
-                               const float* __restrict__ Q, const float* __restrict__ cents,
-                               int dim, int dpad, const float* __restrict__ pdist, int sb,
-                               __half* __restrict__ a16, uint32_t* __restrict__ pair_q,
-                               float* __restrict__ pair_rn, float* __restrict__ pair_s2,
-                               uint32_t* __restrict__ qbad, uint32_t* __restrict__ inv) {
-    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+// Every sorted pair i < poff[3 nlist] gets pair_q, pair_rn and inv (a thread
+// each); the pairs pass 1 scores (i < poff[2 nlist]: pass-1 lists and sampled
+// first tiles) also get their A row and pair_s2 (a warp each).  A grid of a
+// few blocks per SM strides over both (the counts are known on the device
+// only).  Pass-2 rows are written later for the pairs pruning keeps
+// (build_a2_kernel).
+__global__ void __launch_bounds__(256)
+    build_a_kernel(const uint32_t* __restrict__ vals, const unsigned* __restrict__ poff,
+                   int nlist, int take, const uint32_t* __restrict__ probes,
+                   const float* __restrict__ Q, const float* __restrict__ cents, int dim,
+                   int dpad, const float* __restrict__ pdist, int sb, __half* __restrict__ a16,
+                   uint32_t* __restrict__ pair_q, float* __restrict__ pair_rn,
+                   float* __restrict__ pair_s2, uint32_t* __restrict__ qbad,
+                   uint32_t* __restrict__ inv) {
     const unsigned npairs = poff[3 * nlist];  // pairs with a non-empty list
-    if (i >= npairs) return;
-    const uint32_t v = vals[i];
-    const uint32_t q = v / (uint32_t)take;
-    if (i < poff[2 * nlist]) {
+    const unsigned n1 = poff[2 * nlist];      // pairs pass 1 scores
+    const unsigned nthreads = gridDim.x * blockDim.x;
+    const unsigned gt = blockIdx.x * blockDim.x + threadIdx.x;
+    for (unsigned i = gt; i < npairs; i += nthreads) {
+        const uint32_t v = vals[i];
+        pair_q[i] = v / (uint32_t)take;
+        pair_rn[i] = pdist[v];  // the exact coarse distance of this probe
+        inv[v] = i;             // where probe v = q * take + j sits among the sorted pairs
+    }
+    const int lane = threadIdx.x & 31;
+    for (unsigned i = gt >> 5; i < n1; i += nthreads >> 5) {  // warp-uniform
+        const uint32_t v = vals[i];
+        const uint32_t q = v / (uint32_t)take;
         bool bad = false;
-        const float s2 = write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a16 + i * dpad, &bad);
+        const float s2 = write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a16 + (size_t)i * dpad,
+                                     &bad);
         if (lane == 0) {
             pair_s2[i] = s2;
             if (bad) qbad[q] = 1u;
         }
     }
-    if (lane == 0) {
-        pair_q[i] = q;
-        pair_rn[i] = pdist[v];  // the exact coarse distance of this probe
-        inv[v] = (uint32_t)i;   // where probe v = q * take + j sits among the sorted pairs
-    }
 }
 
 // One warp per kept pass-2 pair j (sel[j] = its sorted index): its row of
 // the compact pass-2 matrix and per-pair values.
-__global__ void build_a2_kernel(const unsigned* __restrict__ sel, const unsigned* __restrict__ nsel,
-                                const uint32_t* __restrict__ vals, int take,
-                                const uint32_t* __restrict__ probes, const float* __restrict__ Q,
-                                const float* __restrict__ cents, int dim, int dpad,
-                                const float* __restrict__ pdist, int sb, __half* __restrict__ a2,
-                                uint32_t* __restrict__ q2, float* __restrict__ rn2,
-                                float* __restrict__ s22, uint32_t* __restrict__ qbad) {
-    const size_t j = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// (a grid of a few blocks per SM strides over the kept pairs)
+__global__ void __launch_bounds__(256)
+    build_a2_kernel(const unsigned* __restrict__ sel, const unsigned* __restrict__ nsel,
+                    const uint32_t* __restrict__ vals, int take,
+                    const uint32_t* __restrict__ probes, const float* __restrict__ Q,
+                    const float* __restrict__ cents, int dim, int dpad,
+                    const float* __restrict__ pdist, int sb, __half* __restrict__ a2,
+                    uint32_t* __restrict__ q2, float* __restrict__ rn2,
+                    float* __restrict__ s22, uint32_t* __restrict__ qbad) {
     const int lane = threadIdx.x & 31;
-    if (j >= *nsel) return;
-    const uint32_t v = vals[sel[j]];
-    const uint32_t q = v / (uint32_t)take;
-    bool bad = false;
-    const float s2 = write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a2 + j * dpad, &bad);
-    if (lane == 0) {
-        q2[j] = q;
-        rn2[j] = pdist[v];
-        s22[j] = s2;
-        if (bad) qbad[q] = 1u;
+    const unsigned n = *nsel;
+    const unsigned nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (unsigned j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < n; j += nwarps) {
+        const uint32_t v = vals[sel[j]];
+        const uint32_t q = v / (uint32_t)take;
+        bool bad = false;
+        const float s2 =
+            write_a_row(Q, cents, dim, dpad, q, probes[v], sb, a2 + (size_t)j * dpad, &bad);
+        if (lane == 0) {
+            q2[j] = q;
+            rn2[j] = pdist[v];
+            s22[j] = s2;
+            if (bad) qbad[q] = 1u;
+        }
     }
 }
 
@@ -1057,7 +1068,7 @@ __global__ void __launch_bounds__(256)
                   const uint32_t* __restrict__ probes, const float* __restrict__ pdist, int take,
                   const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend,
                   const float* __restrict__ rh, const float* __restrict__ tau,
-                  float* __restrict__ tadm) {
+                  float* __restrict__ tadm, float* __restrict__ ebound) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * 8 + warp;
     if (q >= nq) return;
@@ -1092,6 +1103,7 @@ __global__ void __launch_bounds__(256)
         const double eadc = (32.0 + 4.0 * m) * 5.9604644775390625e-8 * part * 1.01;
         const float delta = __double2float_ru(FDB_IVF_MARGIN * (eadc + emax) * (1.0 + 1e-6));
         tadm[q] = __fadd_ru(tau[q], delta);
+        ebound[q] = __double2float_ru((eadc + emax) * (1.0 + 1e-6));
     }
 }
 
@@ -1138,6 +1150,7 @@ struct CertParams {
     uint32_t* over_count;       // extensions that held too many entries
     uint32_t* over_list;
     const float* tadm;          // [nq] pass-2 admission threshold tau + delta
+    const float* ebound;        // [nq] E_adc + max_l E_l over the query's lists (rounded up)
     const float* dump;          // pass-1 distances, their rows and pair lookups
     const unsigned* seg;
     const uint32_t* inv;
@@ -1156,7 +1169,12 @@ static_assert(EXT_MAX <= (unsigned)EXT_THREADS, "one thread rescores one collect
 // Two warps per query, 32 shortlisted codes each: the codes rescored with
 // exact_adc (the reference's arithmetic), their exact keys and lists kept for
 // certify_kernel; then the query's first warp writes the k best and the exact
-// k-th distance dk.  P = 1 for k <= 32, 2 for k <= 64.
+// k-th distance dk.  P = 1 for k <= 32, 2 for k <= 64.  For k <= 32 the
+// second warp's codes (shortlist entries 32..63) are skipped when they cannot
+// matter: each has d~ >= d~_32 and so an exact distance >= d~_32 - E, while the
+// exact k-th is at most d~_(k-1) + E (E = E_adc + max_l E_l, the bounds of
+// certify_kernel); when d~_32 - E > d~_(k-1) + E none of them can enter the
+// answer or a seed, and their keys stay empty.
 constexpr int RS_QUERIES = CERT_WARPS / 2;  // queries per block
 template <int ORDER, int P>
 __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) {
@@ -1169,7 +1187,16 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
     if (qok) {  // warp-uniform
         const int m = r.m, sub = r.dim / m;
         const float* qv = r.Q + (size_t)q * r.dim;
-        const uint64_t key = r.approx[(size_t)q * LIST_K + h * 32 + lane];
+        const size_t row = (size_t)q * LIST_K;
+        bool skip = false;
+        if (P == 1 && h == 1) {
+            const uint64_t a32 = r.approx[row + 32], akm1 = r.approx[row + r.k - 1];
+            const float e = r.ebound[q];
+            skip = a32 == KEY_NONE ||
+                   (akm1 != KEY_NONE &&
+                    __fsub_rd(key_dist(a32), e) > __fadd_ru(key_dist(akm1), e));
+        }
+        const uint64_t key = skip ? KEY_NONE : r.approx[row + h * 32 + lane];
         uint64_t ek = KEY_NONE;
         int el = -1;
         if (key != KEY_NONE) {
@@ -1186,8 +1213,8 @@ __global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) 
             ek = make_key(d, pos);
             el = lo;
         }
-        r.ekeys[(size_t)q * LIST_K + h * 32 + lane] = ek;
-        r.elist[(size_t)q * LIST_K + h * 32 + lane] = el;
+        r.ekeys[row + h * 32 + lane] = ek;
+        r.elist[row + h * 32 + lane] = el;
         keys[lq][h * 32 + lane] = ek;
     }
     __syncthreads();
@@ -1744,7 +1771,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_inv.ensure(np);
     FDB_CUDA(cudaMemsetAsync(h->t_qbad.p, 0, nq * 4, s));
     FDB_CUDA(cudaMemsetAsync(h->t_inv.p, 0xff, np * 4, s));
-    build_a_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
+    const unsigned rows_grid =
+        (unsigned)std::min<size_t>((np * 32 + 255) / 256, (size_t)c.sm_count * 8);
+    build_a_kernel<<<rows_grid, 256, 0, s>>>(
         svals, h->t_off.p, nlist, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad, pdist,
         h->tc_sb, h->t_a16.p, h->t_pq.p, h->t_rn.p, h->t_s2.p, h->t_qbad.p, h->t_inv.p);
     FDB_LAUNCH_CHECK();
@@ -1823,9 +1852,10 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     }
     // --- pass 2: the other lists against tau + the certification margin ---
     h->t_tadm.ensure(nq);
+    h->t_eb.ensure(nq);
     margin_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
         dQ, (int)nq, (int)h->dim, (int)h->m, h->cmax.p, h->bmax.p, probes, pdist, (int)take,
-        lbeg, lend, h->tc_rhl.p, h->t_tau.p, h->t_tadm.p);
+        lbeg, lend, h->tc_rhl.p, h->t_tau.p, h->t_tadm.p, h->t_eb.p);
     FDB_LAUNCH_CHECK();
     // --- drop the pass-2 pairs whose list cannot admit a code; compact the rest ---
     h->t_live.ensure(2 * (2 * (size_t)nlist + 1));
@@ -1854,7 +1884,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_q2.ensure(np);
     h->t_rn2.ensure(np);
     h->t_s22.ensure(np);
-    build_a2_kernel<<<(unsigned)((np * 32 + 255) / 256), 256, 0, s>>>(
+    build_a2_kernel<<<rows_grid, 256, 0, s>>>(
         h->t_sel.p + 1, h->t_sel.p, svals, (int)take, probes, dQ, h->cents.p, (int)h->dim, dpad,
         pdist, h->tc_sb, h->t_a2.p, h->t_q2.p, h->t_rn2.p, h->t_s22.p, h->t_qbad.p);
     FDB_LAUNCH_CHECK();
@@ -1924,6 +1954,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     r.ext_thr = h->t_ext_thr.p;
     r.stat = stat;
     r.tadm = h->t_tadm.p;
+    r.ebound = h->t_eb.p;
     r.dump = h->t_dump.p;
     r.seg = h->t_seg.p;
     r.inv = h->t_inv.p;
