@@ -539,19 +539,27 @@ static void ivfpq_host_search(fdb_ivfpq* h, const float* queries, size_t nq, siz
     h->s_out_ids.ensure(per);
     h->s_dists.ensure(per);
     h->s_counts.ensure(nq);
-    FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
-    ivfpq_search_dev(h, h->s_q.p, nq, k, order, take, h->s_out_ids.p, h->s_dists.p,
-                     h->s_counts.p, stats, skip, fetch_mult);
     if (k == 0) {
+        FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
+        ivfpq_search_dev(h, h->s_q.p, nq, k, order, take, h->s_out_ids.p, h->s_dists.p,
+                         h->s_counts.p, stats, skip, fetch_mult);
         if (counts) std::fill(counts, counts + nq, 0u);
         FDB_CUDA(cudaStreamSynchronize(s));
         return;
     }
-    FDB_CUDA(cudaMemcpyAsync(ids, h->s_out_ids.p, per * 8, cudaMemcpyDeviceToHost, s));
-    FDB_CUDA(cudaMemcpyAsync(dists, h->s_dists.p, per * 4, cudaMemcpyDeviceToHost, s));
-    if (counts)
-        FDB_CUDA(cudaMemcpyAsync(counts, h->s_counts.p, nq * 4, cudaMemcpyDeviceToHost, s));
-    FDB_CUDA(cudaStreamSynchronize(s));
+    FDB_CUDA(cudaMemcpyAsync(h->s_q.p, queries, nq * h->dim * 4, cudaMemcpyHostToDevice, s));
+    // the engine copies the results back before its one synchronisation
+    HostIO io;
+    io.ids = ids;
+    io.dists = dists;
+    io.counts = counts;
+    try {
+        ivfpq_search_dev(h, h->s_q.p, nq, k, order, take, h->s_out_ids.p, h->s_dists.p,
+                         h->s_counts.p, stats, skip, fetch_mult, &io);
+    } catch (...) {
+        cudaStreamSynchronize(s);  // the caller's buffers may go once this returns
+        throw;
+    }
 }
 
 int fdb_ivfpq_search(fdb_ivfpq* h, const float* query, size_t k, uint64_t* ids, float* dists,

@@ -399,7 +399,8 @@ static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_k
 
 void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, int order,
                       size_t take, uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
-                      fdb_stats* st, const uint32_t* call_skip, size_t fetch_mult) {
+                      fdb_stats* st, const uint32_t* call_skip, size_t fetch_mult,
+                      const HostIO* io) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     const int nlist = (int)h->nlist;
@@ -566,12 +567,18 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     if (h->rerank) launch_rerank(h, keys, ids, nq, k, dQ, k_out, d_ids, d_dists, d_counts);
     else launch_finalize(s, keys, ids, nq, (int)k, d_ids, d_dists, d_counts);
     tm.mark();
+    if (io && io->ids && k_out > 0) {  // results to the host before the one synchronisation
+        FDB_CUDA(cudaMemcpyAsync(io->ids, d_ids, nq * k_out * 8, cudaMemcpyDeviceToHost, s));
+        FDB_CUDA(cudaMemcpyAsync(io->dists, d_dists, nq * k_out * 4, cudaMemcpyDeviceToHost, s));
+        if (io->counts)
+            FDB_CUDA(cudaMemcpyAsync(io->counts, d_counts, nq * 4, cudaMemcpyDeviceToHost, s));
+    }
     // The tensor path's error word (a bounded wait in the list scan that ran
     // out) and the statistics are read into pinned words after one
     // synchronisation: pin[0..3] statistics, pin[4] error word, pin[5] the
     // number of re-scanned queries.
     int tc_err = 0;
-    if (tensor_ran || st) {
+    if (tensor_ran || st || io) {
         uint64_t* pin = h->s_pin.get();
         for (int i = 0; i < 6; ++i) pin[i] = 0;
         if (tensor_ran) {

@@ -130,6 +130,14 @@ struct PinnedWords {
     }
 };
 
+// Host result buffers of one search (ivfpq_search_dev): the results are
+// copied to them before the call's one synchronisation.
+struct HostIO {
+    uint64_t* ids = nullptr;      // host [nq][k] (nullable: no copies)
+    float* dists = nullptr;
+    uint32_t* counts = nullptr;   // nullable
+};
+
 // Times device stages on a stream with CUDA events.
 struct StageTimer {
     cudaStream_t s;
@@ -274,9 +282,11 @@ void file_inspect(const char* path, fdb_file_info* info);
 // call_skip (nullable): rows this call skips, dead rows included (a filter);
 // fetch_mult: candidates per result before re-ranking, on top of
 // rerank_factor (4 for search_filtered).
+// io (nullable): host result buffers; with io the call ends synchronised.
 void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
                       uint64_t* d_ids, float* d_dists, uint32_t* d_counts, fdb_stats* st,
-                      const uint32_t* call_skip = nullptr, size_t fetch_mult = 1);
+                      const uint32_t* call_skip = nullptr, size_t fetch_mult = 1,
+                      const HostIO* io = nullptr);
 // ivf_tc.cu: tensor-core list scan (see there)
 bool ivf_tc_eligible(const fdb_ivfpq* h, size_t k);
 void ivf_tc_prepare(fdb_ivfpq* h, const std::vector<float>& cb_host,

@@ -416,6 +416,45 @@ def test_ivfpq_tensor_mode_rescan_rounds(fg, ctx, orc):
     assert st.exact_rescans > 0
 
 
+def test_ivfpq_pinned_host_batch_matches_device_entry(fg, ctx, orc, gmm_index):
+    """The host-buffer batch search (pinned buffers, results copied back
+    before the call's one synchronisation) returns what the device-buffer
+    entry point and the oracle return, on repeated calls."""
+    import ctypes as C
+    import torch
+    ix, X, _ = gmm_index
+    from forgegpu.datasets import gmm_descriptors
+    Q = gmm_descriptors(3001, components=64, seed=13)
+    ix.set_nprobe(8)
+    L = fg.lib()
+    nq, k = Q.shape[0], 10
+    hQ = torch.from_numpy(Q).pin_memory()
+    h_ids = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    h_d = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    h_c = torch.empty((nq,), dtype=torch.int32).pin_memory()
+    for _ in range(2):
+        fg._check(L.fdb_ivfpq_batch_search(ix.h, C.c_void_p(hQ.data_ptr()), nq, k,
+                                           C.c_void_p(h_ids.data_ptr()),
+                                           C.c_void_p(h_d.data_ptr()),
+                                           C.c_void_p(h_c.data_ptr()), None))
+        dQ = torch.from_numpy(Q).cuda()
+        d_ids = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+        d_d = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+        d_c = torch.empty((nq,), dtype=torch.int32, device="cuda")
+        fg._check(L.fdb_ivfpq_batch_search_device(ix.h, C.c_void_p(dQ.data_ptr()), nq, k,
+                                                  C.c_void_p(d_ids.data_ptr()),
+                                                  C.c_void_p(d_d.data_ptr()),
+                                                  C.c_void_p(d_c.data_ptr()), None))
+        assert torch.equal(h_ids, d_ids.cpu()) and torch.equal(h_d, d_d.cpu())
+        assert torch.equal(h_c, d_c.cpu())
+    ox = _oracle_index(orc, ix)
+    ox.set_nprobe(8)
+    oi, od, oc = ox.batch_search(Q, k)
+    assert_topk_match(h_ids.numpy().view(np.uint64), h_d.numpy(), h_c.numpy().view(np.uint32),
+                      oi, od, oc, "pinned host batch")
+    ix.set_nprobe(1)
+
+
 def test_ivfpq_tensor_mode_gmm_certifies(fg, ctx, orc, gmm_index):
     """Descriptor-like data: the fp16 bound certifies nearly every query."""
     ix, X, Q = gmm_index
