@@ -582,7 +582,6 @@ def run_ours_bf(args, rank, world, local_rank, dist):
             times.append(e0.elapsed_time(e1))
             scan_ms.append(st.kernel_ms)
             rescans.append(st.exact_rescans)
-            extended.append(st.extended)
         for _ in range(args.steps):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
