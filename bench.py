@@ -387,6 +387,13 @@ def run_ours(args, rank, world, local_rank, dist):
     times, scan_ms, bytes_scanned, launches, rescans, extended = [], [], [], 0, [], []
     kern_ms, kern_scores = [], []
     stage = {"coarse_ms": [], "rescore_ms": [], "merge_ms": []}
+    # rounds of the exact re-scan: units (query, failed list) at most nq * nprobe,
+    # per-unit keys of the fetched k (k x rerank factor, x4 when filtered with
+    # re-ranking) within 64 MiB a round
+    k_fetch = K * max(1, args.rerank) * (4 if (args.filter_every and args.rerank) else 1)
+    units = N_QUERY * args.nprobe
+    ucap = max(1, min(units, (64 << 20) // (k_fetch * 8)))
+    rescan_rounds = (units + ucap - 1) // ucap
     with ClockSampler(nvml_index(local_rank)) as clk:
         for s in range(args.steps):
             flush.zero_()
@@ -413,11 +420,15 @@ def run_ours(args, rank, world, local_rank, dist):
             kern_scores.append(st.kernel_scores)
             codes = st.bytes_scanned / M
             if st.kernel_scores < codes:
-                # tensor mode: transpose + coarse, select, pair keys, radix sort (4),
-                # segment offsets, residual rows, dump rows, scan (2), items, pass 1,
-                # pass-1 selection, pass 2, shortlist, rescore, certify, extend,
-                # [expand + exact re-scan + merge], keys->ids, finalize
-                launches += 23 + (3 if st.exact_rescans else 0)
+                # tensor mode (own kernels; the CUB sort, scans and selection are
+                # library kernels): transpose, coarse, probe selection, pair keys,
+                # segment offsets, residual rows, dump-row lengths, item counts and
+                # fills (2 + 2), pass 1, pass-1 selection, margin, pruning, pass-2
+                # rows, pass 2, shortlist, rescore, certify (2), extend, keys->ids,
+                # finalize = 24; the device-driven re-scan: unit offsets, then
+                # expand + scan + merge per round of units (launched whether or
+                # not any query failed certification)
+                launches += 24 + 1 + 3 * rescan_rounds
             else:
                 # coarse, select, scan, [rescore (+ exact re-scan)], keys->ids, finalize
                 launches += 5 + (1 if st.rescore_ms > 0 else 0) + (1 if st.exact_rescans else 0)
