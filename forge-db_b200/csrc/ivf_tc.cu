@@ -657,18 +657,17 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
 }
 
 // off[k] = the first position of key >= k in the sorted keys (k <= nkeys):
-// the segment offsets of the stable sort, without a histogram.
+// the segment offsets of the stable sort, without a histogram.  Position i
+// (0 <= i <= n) is that first position for every k in (keys[i-1], keys[i]]
+// (keys[-1] = -1, keys[n] = nkeys), so a thread per position writes each
+// offset exactly once.
 __global__ void seg_offsets_kernel(const uint32_t* __restrict__ keys, unsigned n, int nkeys,
                                    unsigned* __restrict__ off) {
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
-    if (k > nkeys) return;
-    unsigned lo = 0, hi = n;
-    while (lo < hi) {
-        const unsigned mid = (lo + hi) >> 1;
-        if (keys[mid] < (uint32_t)k) lo = mid + 1;
-        else hi = mid;
-    }
-    off[k] = lo;
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i > n) return;
+    const uint32_t lo = i == 0 ? 0u : keys[i - 1] + 1u;
+    const uint32_t hi = i == n ? (uint32_t)nkeys : keys[i];
+    for (uint32_t k = lo; k <= hi; ++k) off[k] = i;
 }
 
 // One warp per sorted pair: the fp16 residual row r = fl(q - c_l) * 2^sa
@@ -1474,11 +1473,13 @@ __device__ __forceinline__ void extend_slot(const CertParams& r, uint32_t slot, 
     }
     __syncthreads();
     if (t >= 32) return;
+    // the current exact top-k first: its k-th then skips most batches of the
+    // collected entries (the result is the top-k of the union either way)
     WarpTopK<P> tk;
     tk.init(r.k, sh.buf);
-    tk.ingest(keys, (int)n);
     uint64_t* row = r.out_keys + (size_t)q * r.k;
     tk.ingest(row, r.k);
+    tk.ingest(keys, (int)n);
     tk.store(row);
     if (t == 0 && r.stat) atomicAdd(r.stat + 3, 1ull);
 }
@@ -1758,7 +1759,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_CUDA(cub::DeviceRadixSort::SortPairs(h->t_tmp.p, tmp_sort, h->t_keys.p, h->t_keys.p + np,
                                              h->t_vals.p, h->t_vals.p + np, (int)np, 0, end_bit,
                                              s));
-    seg_offsets_kernel<<<(unsigned)((nkeys + 1 + 255) / 256), 256, 0, s>>>(
+    seg_offsets_kernel<<<(unsigned)((np + 1 + 255) / 256), 256, 0, s>>>(
         h->t_keys.p + np, (unsigned)np, nkeys, h->t_off.p);
     FDB_LAUNCH_CHECK();
     const uint32_t* svals = h->t_vals.p + np;
