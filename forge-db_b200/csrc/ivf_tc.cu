@@ -1176,7 +1176,7 @@ static_assert(EXT_MAX <= (unsigned)EXT_THREADS, "one thread rescores one collect
 // answer or a seed, and their keys stay empty.
 constexpr int RS_QUERIES = CERT_WARPS / 2;  // queries per block
 template <int ORDER, int P>
-__global__ void __launch_bounds__(CERT_WARPS * 32) rescore_kernel(CertParams r) {
+__global__ void __launch_bounds__(CERT_WARPS * 32, 4) rescore_kernel(CertParams r) {
     __shared__ uint64_t keys[RS_QUERIES][LIST_K];
     __shared__ uint64_t buf[RS_QUERIES * 64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
