@@ -71,8 +71,11 @@ typedef struct fdb_stats {
     uint64_t codes_scanned;  /* PQ codes (or database rows) scored */
     uint64_t bytes_scanned;  /* algorithmic bytes: codes_scanned * code bytes */
     double coarse_ms;        /* coarse quantizer + probe selection */
-    double scan_ms;          /* LUT build + code scan + local top-k (scan kernel) */
-    double rescore_ms;       /* table mode: exact rescoring, certification, re-scans */
+    double scan_ms;          /* LUT build + code scan + local top-k (scan kernel); tensor
+                                mode: both list-scan passes with the shortlist, exact
+                                rescoring, certification and its extension */
+    double rescore_ms;       /* table mode: exact rescoring, certification, re-scans;
+                                tensor mode: the exact re-scan of failed lists */
     double merge_ms;         /* cross-device exchange + final merge */
     double total_ms;         /* whole call, device clock */
     uint64_t exact_rescans;  /* table/tensor mode: queries re-scanned exactly after
