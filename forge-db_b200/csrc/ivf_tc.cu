@@ -63,7 +63,7 @@ constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
 #endif
 constexpr int CHUNK_TILES = FDB_IVF_CHUNK_TILES;  // B tiles per item at most (long lists are split)
 #ifndef FDB_IVF_SAMPLE_DIV
-#define FDB_IVF_SAMPLE_DIV 32
+#define FDB_IVF_SAMPLE_DIV 64
 #endif
 // pass 1 samples at least 1/SAMPLE_DIV of each query's probed codes
 constexpr uint64_t SAMPLE_DIV = FDB_IVF_SAMPLE_DIV;
