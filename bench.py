@@ -151,7 +151,7 @@ SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
 
 # DRAM bytes (read + write) per launch of the dominant kernel on the default
 # workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC = {"ivf_pass_filter": 90.6e6, "bf_gemm_filter": None}
+NCU_TRAFFIC = {"ivf_pass_filter": 88.4e6, "bf_gemm_filter": None}
 # brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
 # filter pass, candidate selection, exact rescore, keys->ids, finalize
 BF_LAUNCHES = 10
