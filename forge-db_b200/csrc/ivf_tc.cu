@@ -56,7 +56,7 @@ constexpr int LIST_K = 64;  // pass-1 list per query = shortlist length
 constexpr int EPI_DUMP = 0, EPI_FILTER = 1;
 constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
 #ifndef FDB_IVF_CHUNK_TILES
-#define FDB_IVF_CHUNK_TILES 16
+#define FDB_IVF_CHUNK_TILES 8
 #endif
 #ifndef FDB_IVF_SPIN_WAITS
 #define FDB_IVF_SPIN_WAITS 1
