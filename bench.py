@@ -148,6 +148,8 @@ def make_data():
 
 
 SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
+RECALL_QUERIES = 2000  # queries whose recall@10 both arms report
+SCALING = "strong"     # the batch and the index are fixed as N grows
 
 # DRAM bytes (read + write) per launch of the dominant kernel on the default
 # workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum).
@@ -155,6 +157,63 @@ NCU_TRAFFIC = {"ivf_pass_filter": 88.4e6, "bf_gemm_filter": None}
 # brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
 # filter pass, candidate selection, exact rescore, keys->ids, finalize
 BF_LAUNCHES = 10
+
+
+DIST_RTOL, TIE_RTOL = 1e-4, 1e-5  # north_star: distances 1e-4 rel, near-ties 1e-5 rel
+
+
+def parity_summary(g_ids, g_d, g_cnt, o_ids, o_d, o_cnt):
+    """The port's parity contract over a batch, vectorised: result counts
+    equal, rows ascending, distances within 1e-4 relative, and every id in
+    one answer but not the other within 1e-5 relative of the k-th distance
+    (a near-tie).  Reports the share of rows that are identical outright."""
+    g_ids = np.asarray(g_ids).astype(np.uint64)
+    o_ids = np.asarray(o_ids).astype(np.uint64)
+    g_d = np.asarray(g_d, np.float32)
+    o_d = np.asarray(o_d, np.float32)
+    g_cnt = np.asarray(g_cnt).astype(np.int64)
+    o_cnt = np.asarray(o_cnt).astype(np.int64)
+    nq, k = o_ids.shape
+    count_bad = int((g_cnt != o_cnt).sum())
+    valid = np.arange(k)[None, :] < o_cnt[:, None]
+    od = np.where(valid, o_d, 0).astype(np.float64)
+    gd = np.where(valid, g_d, 0).astype(np.float64)
+    rel = np.abs(gd - od) / np.maximum(np.abs(od), 1e-30)
+    max_rel = float(rel[valid].max()) if valid.any() else 0.0
+    dist_bad = int(((rel > DIST_RTOL) & valid).any(axis=1).sum())
+    unsorted = int((np.diff(np.where(valid, g_d, np.inf), axis=1) < 0).any(axis=1).sum())
+    exact = (np.where(valid, g_ids == o_ids, True).all(axis=1) &
+             np.where(valid, g_d.view(np.uint32) == o_d.view(np.uint32), True).all(axis=1))
+    beyond = 0
+    near_tie_rows = 0
+    for q in np.nonzero(~exact)[0]:
+        c = int(o_cnt[q])
+        gs, os_ = set(g_ids[q, :c].tolist()), set(o_ids[q, :c].tolist())
+        if gs == os_:
+            continue
+        near_tie_rows += 1
+        dk = float(o_d[q, c - 1])
+        tol = TIE_RTOL * max(abs(dk), 1e-30)
+        dmap = dict(zip(o_ids[q, :c].tolist(), o_d[q, :c].tolist()))
+        dmap.update(zip(g_ids[q, :c].tolist(), g_d[q, :c].tolist()))
+        beyond += sum(1 for i in gs ^ os_ if abs(dmap[i] - dk) > tol)
+    ok = count_bad == 0 and dist_bad == 0 and unsorted == 0 and beyond == 0
+    return {"queries": int(nq), "exact_rate": float(exact.mean()) if nq else 1.0,
+            "max_rel_dist": max_rel, "rows_dist_beyond_1e-4": dist_bad,
+            "rows_count_mismatch": count_bad, "rows_unsorted": unsorted,
+            "rows_with_near_tie_swaps": near_tie_rows, "id_mismatch_beyond_ties": beyond,
+            "ok": bool(ok)}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def config_dict(args, world, extra=None):
@@ -176,29 +235,31 @@ def config_dict(args, world, extra=None):
 # reference arm: the CPU path of the reference (oracle restatement)
 # ---------------------------------------------------------------------------
 def run_reference(args, rank, world):
+    """The reference's CPU path: the oracle's restatement of
+    IVFPQIndex::batch_search_parallel (ivf_pq.rs:1060-1084) on every host
+    core, over the index the GPU arm builds (the oracle trains it from the
+    same seeded draws, so both arms search identical centroids, codebooks and
+    lists; the printed index checksum shows it)."""
     if rank != 0:
         return
-    if args.workload != "ivfpq" or args.rerank or args.filter_every:
+    if args.workload not in IVF_CONFIGS or args.rerank or args.filter_every:
         print(json.dumps({"impl": "reference", "workload": args.workload,
-                          "unavailable": "the reference arm is defined for the headline "
-                                         "workload (config C) only"}), flush=True)
+                          "unavailable": "the reference arm is defined for the IVF-PQ "
+                                         "workloads (configs C and D) without re-ranking "
+                                         "or filters"}), flush=True)
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     X, Q = make_data()
-    rng = np.random.default_rng(SEED)
     n = X.shape[0]
+    threads = O.host_threads()
     t0 = time.time()
-    threads = O.max_threads()
-    ix = O.OracleIVFPQ.build(
-        X, np.arange(n), NLIST, M, rng.permutation(n)[:30000].astype(np.uint32),
-        rng.permutation(30000)[:NLIST].astype(np.uint32), None,
-        rng.permutation(n)[:100000].astype(np.uint32),
-        np.concatenate([rng.permutation(100000)[:256] for _ in range(M)]).astype(np.uint32),
-        threads=threads)
+    sidx, init, kpp_u, pidx, pinit = O.engine_build_draws(SEED, n, NLIST, M)
+    ix = O.OracleIVFPQ.build(X, np.arange(n), NLIST, M, sidx, init, kpp_u, pidx, pinit,
+                             threads=threads)
     build_s = time.time() - t0
     ix.set_nprobe(args.nprobe)
-    # size the per-step sample to ~8 s of work
+    # size the per-step sample to about 8 s of work
     probe = Q[:256]
     t0 = time.time()
     ix.batch_search(probe, K, threads=threads)
@@ -213,21 +274,44 @@ def run_reference(args, rank, world):
         ix.batch_search(Q[off:off + sample], K, threads=threads)
         times.append(time.perf_counter() - t0)
     qps = sample * len(times) / sum(times)
+    # recall@10 of the same queries the GPU arm scores, against exact L2
+    # ground truth (compute_ground_truth, dataset.rs:39-59: brute force)
+    from forgegpu.datasets import recall_at_k
+    nr = min(N_QUERY, RECALL_QUERIES)
+    oi, _, _ = ix.batch_search(Q[:nr], K, threads=threads)
+    gt, _, _ = O.bf_batch_search(X, np.arange(n), O.EUCLIDEAN_SQUARED, Q[:nr], K,
+                                 threads=threads)
+    recall = recall_at_k(oi, gt, K)
     line = {
         "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * statistics.mean(times), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args, world, {"sample_queries_per_step": sample,
-                                            "cpu_build_s": round(build_s, 1)}),
+        "scaling": SCALING, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, world),
+        "details": {"recall_at_10": recall, "recall_queries": nr,
+                    "sample_queries_per_step": sample, "cpu_build_s": round(build_s, 1),
+                    "index_crc32": index_checksum(ix.centroids, ix.codebooks, ix.offsets,
+                                                  ix.ids, ix.codes)},
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} of the 10k queries per step, oracle restatement "
-                                   "of batch_search_parallel (ivf_pq.rs:1060-1084), "
-                                   f"{threads} OpenMP threads; index trained by the oracle"},
+                         "cpu_model": cpu_model(),
+                         "sample": f"{sample} of the {N_QUERY} queries per step, oracle "
+                                   "restatement of batch_search_parallel "
+                                   "(ivf_pq.rs:1060-1084), "
+                                   f"{threads} OpenMP threads ({cpu_model()}); index trained "
+                                   "by the oracle from the GPU arm's seeded draws"},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def index_checksum(cents, cb, offs, ids, codes):
+    """CRC-32 over the trained artefacts (equal checksums: the same index)."""
+    import zlib
+    c = 0
+    for a in (cents, cb, offs, ids, codes):
+        c = zlib.crc32(np.ascontiguousarray(a).tobytes(), c)
+    return c
 
 
 # ---------------------------------------------------------------------------
@@ -276,24 +360,41 @@ def cpu_baseline_rows(ix, X, Q, args):
                       f"rerank_results x{args.rerank} (oracle restatement), {threads} threads"}
 
 
-def cpu_baseline(ix, Q, nprobe):
+def oracle_answer(exported, Q, nprobe, timed):
+    """The oracle's batch_search over the GPU-built index (its exported
+    artefacts) for every query of Q: the parity checker, and, when `timed`,
+    the CPU baseline -- a pass over a bounded sample (about 12 s of CPU work)
+    timed on every host core; the remaining queries run untimed."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    cents, cb, offs, ids, codes = ix.export()
+    cents, cb, offs, ids, codes = exported
     ox = O.OracleIVFPQ(cents, cb, offs, ids, codes)
     ox.set_nprobe(nprobe)
-    threads = O.max_threads()
-    t0 = time.time()
-    ox.batch_search(Q[:256], K, threads=threads)
-    per_q = (time.time() - t0) / 256
-    sample = int(min(len(Q), max(256, 12.0 / max(per_q, 1e-9))))
-    t0 = time.perf_counter()
-    oi, od, oc = ox.batch_search(Q[:sample], K, threads=threads)
-    dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"first {sample} of the 10k queries, one batch_search_parallel pass "
-                      "(oracle restatement, ivf_pq.rs:1060-1084) over the GPU-built index"}, \
-        (oi, od, oc, sample)
+    threads = O.host_threads()
+    nq = len(Q)
+    cb_line = None
+    if timed:
+        t0 = time.time()
+        ox.batch_search(Q[:256], K, threads=threads)
+        per_q = (time.time() - t0) / 256
+        sample = int(min(nq, max(256, 12.0 / max(per_q, 1e-9))))
+        t0 = time.perf_counter()
+        oi, od, oc = ox.batch_search(Q[:sample], K, threads=threads)
+        dt = time.perf_counter() - t0
+        cb_line = {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+                   "cpu_model": cpu_model(),
+                   "sample": f"first {sample} of the {nq} queries, one batch_search_parallel "
+                             "pass (oracle restatement, ivf_pq.rs:1060-1084) over the "
+                             f"GPU-built index, {threads} threads ({cpu_model()})"}
+    else:
+        sample = 0
+        oi = np.empty((0, K), np.uint64)
+        od = np.empty((0, K), np.float32)
+        oc = np.empty(0, np.uint32)
+    if sample < nq:
+        ri, rd, rc = ox.batch_search(Q[sample:], K, threads=threads)
+        oi, od, oc = np.concatenate([oi, ri]), np.concatenate([od, rd]), np.concatenate([oc, rc])
+    return cb_line, (oi, od, oc)
 
 
 def run_ours(args, rank, world, local_rank, dist):
@@ -318,7 +419,14 @@ def run_ours(args, rank, world, local_rank, dist):
     ix.set_scan_mode(SCAN_MODES[args.scan_mode])
     if args.rerank:
         ix.enable_reranking(X, np.arange(N_BASE, dtype=np.uint64), args.rerank)
+    # the trained artefacts, for the oracle's parity check on rank 0
+    exported = ix.export() if rank == 0 else None
+    unsharded = None
     if world > 1 and args.mode == "lists":
+        # the single-device answer of this rank's index before sharding: the
+        # sharded answer must equal it bit for bit (shard_parity)
+        if rank == 0 and not (args.rerank or args.filter_every):
+            unsharded = ix.batch_search_arrays(Q, K)
         ix.shard(rank, world)
         Qr = Q
     elif world > 1:
@@ -455,14 +563,17 @@ def run_ours(args, rank, world, local_rank, dist):
 
     if rank != 0:
         return
+    g_ids = d_ids.cpu().numpy().astype(np.uint64)
+    g_d = d_d.cpu().numpy()
+    g_c = d_c.cpu().numpy()
     # recall@10 against exact L2 ground truth (BF on the GPU) for the batch
-    ids_h = d_ids.cpu().numpy().astype(np.uint64)
     recall = None
+    nr = min(nq, RECALL_QUERIES)
     if world == 1 or args.mode == "lists":
         bf = fg.BruteForceIndex(fg.DistanceMetric.EuclideanSquared, ctx).add(X)
-        gt, _, _ = bf.batch_search_arrays(Q[:2000], K)
+        gt, _, _ = bf.batch_search_arrays(Q[:nr], K)
         from forgegpu.datasets import recall_at_k
-        recall = recall_at_k(ids_h[:2000], gt, K)
+        recall = recall_at_k(g_ids[:nr], gt, K)
         bf.close()
     hbm, peak_kind = peaks()
     scan_avg_ms = statistics.mean(scan_ms)
@@ -496,14 +607,16 @@ def run_ours(args, rank, world, local_rank, dist):
     line = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": SCALING, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": config_dict(args, world, {
-            "recall_at_10": recall, "build_s": round(build_s, 2),
+        "config": config_dict(args, world),
+        "details": {
+            "recall_at_10": recall, "recall_queries": nr, "build_s": round(build_s, 2),
             "stage_ms": {k: round(statistics.mean(v), 4) for k, v in stage.items()},
             "scan_kernel_ms": round(statistics.mean(scan_ms), 4),
             "exact_rescans_per_step": statistics.mean(rescans),
-            "extended_certificates_per_step": statistics.mean(extended)}),
+            "extended_certificates_per_step": statistics.mean(extended),
+            "index_crc32": index_checksum(*exported)},
         "e2e": {"value": e2e_value, "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4,
                 "d2h_bytes_per_step": nq * K * (8 + 4) + nq * 4},
@@ -516,13 +629,38 @@ def run_ours(args, rank, world, local_rank, dist):
         # (10 passes over 64-bit keys) and the row bitmap
         line["gpu_launches"] += args.steps * 11
         line["e2e"]["h2d_bytes_per_step"] += int(allowed.nbytes)
-    if world == 1 and not args.no_cpu_baseline:
-        if args.rerank or args.filter_every:
+    # the end-to-end entry point returned the device entry point's answer
+    e2e_same = bool(np.array_equal(h_ids.numpy().astype(np.uint64), g_ids) and
+                    np.array_equal(h_d.numpy().view(np.uint32), g_d.view(np.uint32)) and
+                    np.array_equal(h_c.numpy(), g_c))
+    ok = e2e_same
+    if args.rerank or args.filter_every:
+        if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_rows(ix, X, Q, args)
-        else:
-            cb, _ = cpu_baseline(ix, Q, args.nprobe)
-            line["cpu_baseline"] = cb
+    else:
+        # parity of every query of the batch with the oracle over the same index
+        t0 = time.time()
+        cb_line, (oi, od, oc) = oracle_answer(exported, Qr, args.nprobe,
+                                              timed=(world == 1 and not args.no_cpu_baseline))
+        par = parity_summary(g_ids, g_d, g_c, oi, od, oc)
+        par["e2e_answer_identical"] = e2e_same
+        par["oracle_s"] = round(time.time() - t0, 1)
+        line["parity"] = par
+        ok = ok and par["ok"]
+        if cb_line is not None:
+            line["cpu_baseline"] = cb_line
+    if unsharded is not None:
+        ui, ud, uc = unsharded
+        same = bool(np.array_equal(ui, g_ids) and np.array_equal(ud.view(np.uint32),
+                                                                  g_d.view(np.uint32)) and
+                    np.array_equal(uc.astype(np.int64), g_c.astype(np.int64)))
+        line["shard_parity"] = {"queries": int(nq), "identical_to_unsharded": same}
+        ok = ok and same
     print(json.dumps(line), flush=True)
+    if not ok:
+        print("PARITY FAILURE: the GPU answer differs from the oracle's (see 'parity')",
+              file=sys.stderr, flush=True)
+        raise SystemExit(3)
 
 
 def run_ours_bf(args, rank, world, local_rank, dist):
@@ -636,7 +774,35 @@ def run_ours_bf(args, rank, world, local_rank, dist):
                      "kernel_ms": scan_avg},
         "clocks": clk.summary(),
     }
+    # parity with the oracle's brute force (brute_force.rs:180-225) on a
+    # bounded sample of the batch (about 15 s of CPU work on every host core)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = O.host_threads()
+    g_ids = d_ids.cpu().numpy().astype(np.uint64)
+    g_d = d_d.cpu().numpy()
+    g_c = d_c.cpu().numpy()
+    ids_all = np.arange(n, dtype=np.uint64)
+    t0 = time.time()
+    O.bf_batch_search(X, ids_all, metric, Q[:32], k, threads=threads)
+    per_q = (time.time() - t0) / 32
+    ns = int(min(nq, max(200, 15.0 / max(per_q, 1e-9))))
+    t0 = time.perf_counter()
+    oi, od, oc = O.bf_batch_search(X, ids_all, metric, Q[:ns], k, threads=threads)
+    cpu_s = time.perf_counter() - t0
+    par = parity_summary(g_ids[:ns], g_d[:ns], g_c[:ns], oi, od, oc)
+    par["sample"] = f"first {ns} of the {nq} queries"
+    line["parity"] = par
+    line["cpu_baseline"] = {"value": ns / cpu_s,
+                            "unit": "queries/s", "cores": threads, "kind": "port",
+                            "cpu_model": cpu_model(),
+                            "sample": f"first {ns} queries through the oracle's batch_search "
+                                      f"(brute_force.rs:180-225), {threads} threads"}
     print(json.dumps(line), flush=True)
+    if not par["ok"]:
+        print("PARITY FAILURE: brute-force answer differs from the oracle's", file=sys.stderr,
+              flush=True)
+        raise SystemExit(3)
 
 
 def run_ours_train(args, rank, world, local_rank, dist):

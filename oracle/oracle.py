@@ -269,6 +269,81 @@ def max_threads():
     return lib().orc_max_threads()
 
 
+def host_threads():
+    """Every core this process may run on (OMP_NUM_THREADS, which torchrun
+    sets to 1, does not limit the count passed explicitly to the oracle)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# --- the engine's default draws, restated ---------------------------------------
+# The reference draws its training samples and initial centroids from
+# rand::thread_rng (src/index/ivf_pq.rs:388, 426; src/kmeans.rs:54, 97, 107),
+# which no run can reproduce.  The engine replaces it with a documented
+# splitmix64 stream; restating that stream here lets the oracle build the very
+# index a GPU run builds from the same seed (the draws are inputs to both).
+
+_M64 = (1 << 64) - 1
+
+
+def _splitmix64(state):
+    state = (state + 0x9E3779B97F4A7C15) & _M64
+    z = state
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return state, z ^ (z >> 31)
+
+
+def splitmix_sample_indices(seed, n, take):
+    """Partial Fisher-Yates over 0..n-1 driven by splitmix64: slot i swaps with
+    i + floor(r * (n - i) / 2^64).  The first `take` slots are the sample."""
+    idx = np.arange(n, dtype=np.uint32)
+    st = int(seed) & _M64
+    for i in range(int(take)):
+        st, r = _splitmix64(st)
+        j = i + ((r * (n - i)) >> 64)
+        idx[i], idx[j] = idx[j], idx[i]
+    return idx[:take].copy()
+
+
+def splitmix_uniform(seed, count):
+    """23 random bits per draw: u = (r >> 41) * 2^-23 in [0, 1)."""
+    st = int(seed) & _M64
+    out = np.empty(int(count), np.float32)
+    for i in range(int(count)):
+        st, r = _splitmix64(st)
+        out[i] = np.float32(r >> 41) * np.float32(1.0 / 8388608.0)
+    return out
+
+
+def engine_build_draws(seed, n, nlist, m, ivf_sample=30000, pq_sample=100000):
+    """The draws an engine build with `seed` and default options takes:
+    (ivf_sample_idx, ivf_init_idx, ivf_kpp_u, pq_sample_idx, pq_init_idx).
+    Random-sample init for nlist > 64, k-means++ picks and draws otherwise."""
+    seed = int(seed)
+    ivf_n = min(ivf_sample, n)
+    pq_n = min(pq_sample, n)
+    sidx = (np.arange(n, dtype=np.uint32) if ivf_n == n
+            else splitmix_sample_indices(seed, n, ivf_n))
+    kseed = (seed + 1) & _M64
+    if nlist > 64:
+        init = splitmix_sample_indices(kseed, ivf_n, nlist)
+        kpp_u = None
+    else:
+        st = kseed ^ 0x6B6D65616E737070
+        init = np.empty(nlist, np.uint32)
+        for c in range(nlist):
+            st, r = _splitmix64(st)
+            init[c] = (r * ivf_n) >> 64
+        kpp_u = splitmix_uniform((kseed + 0x9E37) & _M64, nlist)
+    pidx = splitmix_sample_indices((seed + 2) & _M64, n, pq_n)
+    pinit = np.concatenate([splitmix_sample_indices((seed + 3 + q) & _M64, pq_n, 256)
+                            for q in range(m)]).astype(np.uint32)
+    return sidx, init, kpp_u, pidx, pinit
+
+
 # --- the reference's mutable IVF-PQ state (re-ranking, tombstones, filters) ----
 
 class OracleMutableIVFPQ(OracleIVFPQ):

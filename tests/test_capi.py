@@ -58,6 +58,23 @@ def test_seeded_draws_deterministic():
         fg.sample_indices(1, 10, 11)
 
 
+def test_oracle_restates_the_engine_draws(orc):
+    """The oracle's splitmix64 restatement gives the engine's default build
+    draws, so the reference arm can train the index the GPU arm trains."""
+    import forgegpu as fg
+    for seed, n, take in [(2024, 1_000_000, 3000), (0, 50, 50), ((1 << 64) - 2, 977, 13)]:
+        assert np.array_equal(orc.splitmix_sample_indices(seed, n, take),
+                              fg.sample_indices(seed, n, take))
+    assert np.array_equal(orc.splitmix_uniform(99, 257).view(np.uint32),
+                          fg.uniform_draws(99, 257).view(np.uint32))
+    sidx, init, kpp, pidx, pinit = orc.engine_build_draws(5, 40000, 32, 4, ivf_sample=3000,
+                                                          pq_sample=2000)
+    assert np.array_equal(sidx, fg.sample_indices(5, 40000, 3000))
+    assert kpp is not None and kpp.size == 32 and init.max() < 3000
+    assert np.array_equal(pidx, fg.sample_indices(7, 40000, 2000))
+    assert np.array_equal(pinit[256:512], fg.sample_indices(9, 2000, 256))
+
+
 def test_shard_plan_covers_every_list_once():
     import forgegpu as fg
     rng = np.random.default_rng(0)
