@@ -9,14 +9,17 @@ QPS with queries already in HBM (device clock, max over ranks); `e2e` is the
 same through the C ABI entry point with pinned host buffers, the query
 upload and the result download inside the timed region.  L2 (126 MB) is
 flushed between steps by writing a 256 MB buffer outside the timed window,
-because the index (16 MB of codes) would otherwise stay L2-resident.
+because the index (16 MB of codes) would otherwise stay L2-resident.  Every
+run checks the answer for the whole batch against the oracle (`parity`).
 
-Multi-GPU (torchrun, one rank per GPU): `--mode lists` (default) gives each
-rank a share of the inverted lists; every rank runs the full query batch on
-its lists, the local top-k lists are exchanged with ncclAllGather inside the
-engine and merged on every device (strong scaling: the index and batch are
-fixed).  `--mode replicas` holds the whole index on every rank and splits
-the queries (no collective).
+Multi-GPU (torchrun, one rank per GPU): `--mode replicas` (default) holds the
+whole index on every rank and gives each rank its own 10k-query batch (weak
+scaling; queries are independent, so there is no collective on the data
+path).  `--mode lists` gives each rank a share of the inverted lists; every
+rank runs the full 10k batch on its lists, the local top-k lists are
+exchanged with ncclAllGather inside the engine and merged on every device
+(strong scaling: the index and batch are fixed; `shard_parity` checks the
+sharded answer against the unsharded one).
 
 `--impl reference` times the reference's CPU path (the oracle's restatement
 of IVFPQIndex::batch_search_parallel, all host threads) on a bounded sample.
@@ -147,6 +150,15 @@ def make_data():
     return datasets.config_c(N_BASE, N_QUERY)
 
 
+def rank_queries(rank):
+    """The query batch of one replica rank: rank 0 takes the N=1 batch, the
+    others draw their own from the same distribution (other seeds)."""
+    from forgegpu import datasets
+    if WORKLOAD == "ivfpq_config_d":
+        return datasets.normal(N_QUERY, DIM, seed=10 + 1000 * rank, unit=True)
+    return datasets.gmm_descriptors(N_QUERY, seed=7 + 1000 * rank)
+
+
 SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
 RECALL_QUERIES = 2000  # queries whose recall@10 both arms report
 SCALING = "strong"     # the batch and the index are fixed as N grows
@@ -218,7 +230,10 @@ def cpu_model():
 
 def config_dict(args, world, extra=None):
     d = {"workload": WORKLOAD, "n_base": N_BASE, "dim": DIM, "nlist": NLIST, "m": M,
-         "nprobe": args.nprobe, "global_batch": N_QUERY, "k": K, "data": DATA_NOTE,
+         "nprobe": args.nprobe,
+         "global_batch": N_QUERY * (world if args.mode == "replicas" else 1),
+         "queries_per_gpu": N_QUERY, "k": K,
+         "data": DATA_NOTE,
          "parallelism": (f"lists{world}" if args.mode == "lists" else f"replicas{world}"),
          "scan_mode": args.scan_mode,
          "l2": "flushed between steps (256 MB write outside the timed window)"}
@@ -430,8 +445,8 @@ def run_ours(args, rank, world, local_rank, dist):
         ix.shard(rank, world)
         Qr = Q
     elif world > 1:
-        lo, hi = N_QUERY * rank // world, N_QUERY * (rank + 1) // world
-        Qr = Q[lo:hi]
+        # replicas: the whole index on every rank, a batch of queries per rank
+        Qr = Q if rank == 0 else rank_queries(rank)
     else:
         Qr = Q
     nq = Qr.shape[0]
@@ -558,8 +573,10 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.barrier()
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     total_ms, total_e2e_ms = float(tot[0]), float(tot[1])
-    value = N_QUERY * args.steps / (total_ms / 1000.0)
-    e2e_value = N_QUERY * args.steps / (total_e2e_ms / 1000.0)
+    # queries answered by the whole job per step (replicas: one batch per rank)
+    job_queries = N_QUERY * (world if args.mode == "replicas" else 1)
+    value = job_queries * args.steps / (total_ms / 1000.0)
+    e2e_value = job_queries * args.steps / (total_e2e_ms / 1000.0)
 
     if rank != 0:
         return
@@ -569,9 +586,9 @@ def run_ours(args, rank, world, local_rank, dist):
     # recall@10 against exact L2 ground truth (BF on the GPU) for the batch
     recall = None
     nr = min(nq, RECALL_QUERIES)
-    if world == 1 or args.mode == "lists":
+    if True:
         bf = fg.BruteForceIndex(fg.DistanceMetric.EuclideanSquared, ctx).add(X)
-        gt, _, _ = bf.batch_search_arrays(Q[:nr], K)
+        gt, _, _ = bf.batch_search_arrays(Qr[:nr], K)
         from forgegpu.datasets import recall_at_k
         recall = recall_at_k(g_ids[:nr], gt, K)
         bf.close()
@@ -979,7 +996,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--nprobe", type=int, default=None,
                     help="default: 32 (config C), 64 (config D)")
-    ap.add_argument("--mode", default="lists", choices=["lists", "replicas"])
+    ap.add_argument("--mode", default="replicas", choices=["lists", "replicas"],
+                    help="multi-GPU: replicas (default; the index on every rank, a batch "
+                         "of queries per rank, weak scaling, no collective) or lists (the "
+                         "inverted lists sharded, the batch broadcast, local top-k lists "
+                         "exchanged by ncclAllGather and merged; strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the first timed step with cudaProfilerStart/Stop "
@@ -1008,6 +1029,8 @@ def main():
         use_ivf_config(args.workload)
     if args.nprobe is None:
         args.nprobe = DEFAULT_NPROBE
+    global SCALING
+    SCALING = "weak" if args.mode == "replicas" else "strong"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -9,11 +9,13 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <memory>
 #include <new>
 #include <numeric>
+#include <thread>
 
 #include "fdb_device.cuh"
 #include "fdb_internal.h"
@@ -25,6 +27,42 @@ static thread_local std::string g_last_error;
 
 void fail(int code, const std::string& msg) { throw Error{code, msg}; }
 void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+static double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+// Polls a non-blocking communicator until its pending operation leaves
+// ncclInProgress or `limit_s` passes.  Returns the final state, or
+// ncclInProgress if the limit ran out.
+static ncclResult_t nccl_settle(ncclComm_t comm, double limit_s) {
+    const double t0 = now_s();
+    ncclResult_t st = ncclInProgress;
+    for (;;) {
+        if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) return ncclInternalError;
+        if (st != ncclInProgress) return st;
+        if (now_s() - t0 > limit_s) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+void nccl_complete(ncclResult_t r, ncclComm_t comm, const char* what) {
+    if (r == ncclInProgress && comm) r = nccl_settle(comm, 300.0);
+    if (r == ncclInProgress)
+        fail(FDB_ERR_TIMEOUT, std::string(what) + ": did not complete within 300 s");
+    if (r != ncclSuccess) fail(FDB_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+// Releases a communicator: finalize (flushes its operations; bounded), then
+// destroy, or abort when the finalize does not complete.
+static void release_comm(ncclComm_t comm) {
+    if (!comm) return;
+    ncclResult_t r = ncclCommFinalize(comm);
+    if (r == ncclInProgress) r = nccl_settle(comm, 10.0);
+    if (r == ncclSuccess) ncclCommDestroy(comm);
+    else ncclCommAbort(comm);
+}
 
 uint64_t splitmix64(uint64_t& state) {
     uint64_t z = (state += 0x9e3779b97f4a7c15ull);
@@ -113,6 +151,10 @@ int fdb_ctx_create(int device, fdb_ctx** out) {
         FDB_REQUIRE(prop.major >= 10, FDB_ERR_UNSUPPORTED,
                     "this build targets sm_100a (B200); device is older");
         c->c.sm_count = prop.multiProcessorCount;
+        int khz = 0;
+        if (cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device) == cudaSuccess && khz > 0)
+            c->c.clock_khz = khz;
+        c->c.wait_cycles = seconds_to_cycles(c->c, c->c.wait_s.load());
         FDB_CUDA(cudaStreamCreateWithFlags(&c->c.stream, cudaStreamNonBlocking));
         *out = c.release();
     });
@@ -123,7 +165,7 @@ int fdb_ctx_free(fdb_ctx* ctx) {
         if (!ctx) return;
         {
             DeviceGuard g(ctx->c.device);
-            if (ctx->c.comm) ncclCommDestroy(ctx->c.comm);
+            release_comm(ctx->c.comm);
             if (ctx->c.stream) cudaStreamDestroy(ctx->c.stream);
         }
         delete ctx;
@@ -147,21 +189,58 @@ int fdb_nccl_unique_id(void* id_out) {
     });
 }
 
-int fdb_ctx_init_comm(fdb_ctx* ctx, int rank, int world, const void* nccl_id) {
+int fdb_ctx_init_comm_timeout(fdb_ctx* ctx, int rank, int world, const void* nccl_id,
+                              double timeout_s) {
     return guarded([&] {
         FDB_REQUIRE(ctx && nccl_id, FDB_ERR_INVALID_ARG, "NULL argument");
         FDB_REQUIRE(world >= 1 && rank >= 0 && rank < world, FDB_ERR_INVALID_ARG,
                     "bad rank/world");
+        FDB_REQUIRE(timeout_s > 0.0, FDB_ERR_INVALID_ARG, "timeout must be positive");
         DeviceGuard g(ctx->c.device);
-        if (ctx->c.comm) {
-            ncclCommDestroy(ctx->c.comm);
-            ctx->c.comm = nullptr;
-        }
+        std::lock_guard<std::mutex> lk(ctx->c.mu);
+        release_comm(ctx->c.comm);
+        ctx->c.comm = nullptr;
+        ctx->c.rank = 0;
+        ctx->c.world = 1;
         ncclUniqueId id;
         std::memcpy(&id, nccl_id, sizeof(id));
-        FDB_NCCL(ncclCommInitRank(&ctx->c.comm, world, id, rank));
+        // non-blocking: the join of all ranks can be given up on a deadline
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        ncclComm_t comm = nullptr;
+        ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+        if (r == ncclInProgress) r = nccl_settle(comm, timeout_s);
+        if (r != ncclSuccess) {
+            if (comm) ncclCommAbort(comm);
+            if (r == ncclInProgress)
+                fail(FDB_ERR_TIMEOUT, "NCCL communicator: not every rank joined within the "
+                                      "timeout; initialisation aborted");
+            fail(FDB_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+        }
+        ctx->c.comm = comm;
         ctx->c.rank = rank;
         ctx->c.world = world;
+    });
+}
+
+int fdb_ctx_init_comm(fdb_ctx* ctx, int rank, int world, const void* nccl_id) {
+    return fdb_ctx_init_comm_timeout(ctx, rank, world, nccl_id, 300.0);
+}
+
+int fdb_ctx_set_wait_limit(fdb_ctx* ctx, double seconds) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx, FDB_ERR_INVALID_ARG, "NULL context");
+        FDB_REQUIRE(seconds > 0.0 && seconds <= 3600.0, FDB_ERR_INVALID_ARG,
+                    "wait limit must be in (0, 3600] seconds");
+        ctx->c.wait_s = seconds;
+        ctx->c.wait_cycles = seconds_to_cycles(ctx->c, seconds);
+    });
+}
+
+int fdb_ctx_test_stall_scans(fdb_ctx* ctx, int count) {
+    return guarded([&] {
+        FDB_REQUIRE(ctx && count >= 0, FDB_ERR_INVALID_ARG, "bad arguments");
+        ctx->c.test_stalls = count;
     });
 }
 
@@ -297,7 +376,10 @@ static __device__ __align__(256) float g_noalloc_dist[FDB_NOALLOC_MAX_DISTANCES]
 namespace {
 
 // Address of g_noalloc_dist on `device`, looked up once per device with that
-// device current (the caller's DeviceGuard) and remembered afterwards.
+// device current (the caller's DeviceGuard) and remembered for the life of
+// the process.  A cudaDeviceReset of that device unloads the module and
+// leaves the remembered address stale; like every other handle of this
+// library on that device, it must not be used after a reset.
 float* noalloc_scratch(int device) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
@@ -332,6 +414,11 @@ int fdb_find_nearest_centroids_noalloc(fdb_ctx* ctx, const float* d_centroids, s
                     FDB_ERR_INVALID_ARG,
                     "nq * kc above FDB_NOALLOC_MAX_DISTANCES (4194304 distances, the fixed "
                     "scratch); split the queries into batches");
+        // more than 256 nearest ids are selected by a sort of each whole row in
+        // shared memory (the row padded to a power of two), which holds at most
+        // 16384 centroids
+        FDB_REQUIRE(take <= 256 || kc <= FDB_NOALLOC_MAX_SORTED_CENTROIDS, FDB_ERR_INVALID_ARG,
+                    "min(k, kc) above 256 needs kc <= FDB_NOALLOC_MAX_SORTED_CENTROIDS (16384)");
         FDB_REQUIRE(!work || (d_centroids && d_queries && d_out), FDB_ERR_INVALID_ARG,
                     "NULL argument");
         DeviceGuard g(ctx->c.device);
@@ -589,6 +676,69 @@ int fdb_ivfpq_batch_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t
         size_t take = std::max<size_t>(1, std::min(h->nprobe.load(std::memory_order_relaxed),
                                                    h->nlist));
         ivfpq_host_search(h, queries, nq, k, ORDER_LANE8, take, ids, dists, counts, stats);
+    });
+}
+
+}  // extern "C"
+
+namespace {
+
+// Runs `search` under a deadline `timeout_s` from now (IVFPQIndex::
+// search_with_timeout, ivf_pq.rs:1369-1455): the bounded waits inside the
+// tensor-core kernels give up at the deadline, and a call whose results come
+// back after it reports FDB_ERR_TIMEOUT, as the reference's checks between
+// its stages do.  elapsed_out (nullable) gets the call's duration in seconds.
+template <class F>
+void with_deadline(fdb_ivfpq* h, double timeout_s, double* elapsed_out, F&& search) {
+    FDB_REQUIRE(timeout_s >= 0.0, FDB_ERR_INVALID_ARG, "timeout must not be negative");
+    const double t0 = now_s();
+    struct Reset {
+        fdb_ivfpq* h;
+        ~Reset() { h->call_wait_cycles = 0; }
+    } reset{h};
+    h->call_wait_cycles = seconds_to_cycles(h->ctx->c, timeout_s);
+    search();
+    const double dt = now_s() - t0;
+    if (elapsed_out) *elapsed_out = dt;
+    FDB_REQUIRE(dt <= timeout_s, FDB_ERR_TIMEOUT, "search did not complete within the timeout");
+}
+
+}  // namespace
+
+extern "C" {
+
+int fdb_ivfpq_search_with_timeout(fdb_ivfpq* h, const float* query, size_t k, double timeout_s,
+                                  uint64_t* ids, float* dists, size_t* n_out,
+                                  double* elapsed_s) {
+    return guarded([&] {
+        FDB_REQUIRE(h && query && (k == 0 || (ids && dists)), FDB_ERR_INVALID_ARG,
+                    "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        size_t take = std::min(h->nprobe.load(std::memory_order_relaxed), h->nlist);
+        uint32_t cnt = 0;
+        with_deadline(h, timeout_s, elapsed_s, [&] {
+            ivfpq_host_search(h, query, 1, k, ORDER_FAST4, take, ids, dists, &cnt, nullptr);
+        });
+        if (n_out) *n_out = cnt;
+    });
+}
+
+int fdb_ivfpq_batch_search_with_timeout(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                                        double timeout_s, uint64_t* ids, float* dists,
+                                        uint32_t* counts, double* elapsed_s) {
+    return guarded([&] {
+        FDB_REQUIRE(h && (nq == 0 || queries) && (nq == 0 || k == 0 || (ids && dists)),
+                    FDB_ERR_INVALID_ARG, "NULL argument");
+        DeviceGuard g(h->ctx->c.device);
+        std::lock_guard<std::mutex> lk(h->mu);
+        size_t take = std::max<size_t>(1, std::min(h->nprobe.load(std::memory_order_relaxed),
+                                                   h->nlist));
+        with_deadline(h, timeout_s, elapsed_s, [&] {
+            if (nq > 0)
+                ivfpq_host_search(h, queries, nq, k, ORDER_LANE8, take, ids, dists, counts,
+                                  nullptr);
+        });
     });
 }
 

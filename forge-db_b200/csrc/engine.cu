@@ -389,7 +389,7 @@ static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_k
     uint64_t* send = gather.p + per * 2 * (size_t)c.world;
     FDB_CUDA(cudaMemcpyAsync(send, local_keys, per * 8, cudaMemcpyDeviceToDevice, s));
     FDB_CUDA(cudaMemcpyAsync(send + per, local_ids, per * 8, cudaMemcpyDeviceToDevice, s));
-    FDB_NCCL(ncclAllGather(send, gather.p, per * 2, ncclUint64, c.comm, s));
+    FDB_NCCL_C(ncclAllGather(send, gather.p, per * 2, ncclUint64, c.comm, s), c.comm);
     merged.ensure(per);
     merged_ids.ensure(per);
     launch_merge_lists(s, gather.p, c.world, per * 2, nq, k, merged.p);
@@ -455,12 +455,12 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         }
         if (world > 1) {
             const size_t cnt = slice * take;
-            FDB_NCCL(ncclGroupStart());
-            FDB_NCCL(ncclAllGather(h->s_probe.p + cnt * rank, h->s_probe.p, cnt, ncclUint32,
-                                   c.comm, s));
-            FDB_NCCL(ncclAllGather(h->s_pdist.p + cnt * rank, h->s_pdist.p, cnt, ncclFloat,
-                                   c.comm, s));
-            FDB_NCCL(ncclGroupEnd());
+            FDB_NCCL_C(ncclGroupStart(), c.comm);
+            FDB_NCCL_C(ncclAllGather(h->s_probe.p + cnt * rank, h->s_probe.p, cnt, ncclUint32,
+                                   c.comm, s), c.comm);
+            FDB_NCCL_C(ncclAllGather(h->s_pdist.p + cnt * rank, h->s_pdist.p, cnt, ncclFloat,
+                                   c.comm, s), c.comm);
+            FDB_NCCL_C(ncclGroupEnd(), c.comm);
         }
         tm.mark();
         h->s_stat.ensure(4);
@@ -751,6 +751,7 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
             int* err = reinterpret_cast<int*>(h->s_flags.p + nq + 1);
             FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
             h->gemm.err = err;
+            h->gemm.wait_cycles = wait_limit_cycles(c);
             // device time of the filter pass, when statistics are asked for
             cudaEvent_t fev[2] = {nullptr, nullptr};
             if (st) {

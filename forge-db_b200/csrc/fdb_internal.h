@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -47,6 +48,12 @@ void set_last_error(const std::string& msg);
         if (r__ != ncclSuccess)                                                               \
             ::fdb::fail(FDB_ERR_NCCL, std::string(#x) + ": " + ncclGetErrorString(r__));      \
     } while (0)
+
+// An NCCL call on the context's communicator, which is non-blocking (so that
+// initialisation can have a deadline): a call that returns ncclInProgress is
+// complete once the communicator's asynchronous state leaves that value.
+void nccl_complete(ncclResult_t r, ncclComm_t comm, const char* what);
+#define FDB_NCCL_C(x, comm) ::fdb::nccl_complete((x), (comm), #x)
 
 #define FDB_REQUIRE(cond, code, msg)          \
     do {                                              \
@@ -93,11 +100,37 @@ struct DevBuf {
 struct Ctx {
     int device = 0;
     int sm_count = 0;
+    int clock_khz = 1965000;  // SM clock (cycles per ms): converts wait limits
     cudaStream_t stream = nullptr;
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     std::mutex mu;  // serialises use of the context's scratch buffers
+    // Limit of every bounded wait inside the tensor-core kernels, in SM clock
+    // cycles and in seconds (fdb_ctx_set_wait_limit); a call with its own
+    // deadline lowers it for its duration.
+    std::atomic<unsigned long long> wait_cycles{4000000000ull};
+    std::atomic<double> wait_s{2.0};
+    std::atomic<int> test_stalls{0};  // test hook: list-scan launches left to stall
 };
+
+// The wait limit in force for a call (call_cycles: the call's own limit, 0 =
+// none), in SM clock cycles.
+inline unsigned long long wait_limit_cycles(const Ctx& c, unsigned long long call_cycles = 0) {
+    const unsigned long long w = c.wait_cycles.load(std::memory_order_relaxed);
+    return call_cycles ? std::min(call_cycles, w) : w;
+}
+inline unsigned long long seconds_to_cycles(const Ctx& c, double s) {
+    const double cyc = s * (double)c.clock_khz * 1000.0;
+    return cyc < 1.0 ? 1ull : (cyc > 1.8e19 ? 18000000000000000000ull : (unsigned long long)cyc);
+}
+// Test hook: true (once per requested stall) if this list-scan launch is to
+// issue no work, so that its bounded waits run out.
+inline bool take_test_stall(Ctx& c) {
+    int n = c.test_stalls.load();
+    while (n > 0)
+        if (c.test_stalls.compare_exchange_weak(n, n - 1)) return true;
+    return false;
+}
 
 // Makes the context's device current for the lifetime of the guard.
 struct DeviceGuard {
@@ -235,6 +268,7 @@ struct GemmScratch {
     DevBuf<float> tau;
     int cap = 0;
     int* err = nullptr;  // device error word (timeouts)
+    unsigned long long wait_cycles = 4000000000ull;  // limit of each bounded wait
     // optional: recorded around the filter pass (the dominant kernel)
     cudaEvent_t filter_ev0 = nullptr, filter_ev1 = nullptr;
 };
@@ -316,6 +350,7 @@ struct fdb_ivfpq {
     size_t dim = 0, nlist = 0, m = 0;
     int metric = 0;
     std::atomic<size_t> nprobe{1};
+    unsigned long long call_wait_cycles = 0;  // a call's own wait limit (0: none)
     size_t n_total = 0;  // vectors in the unsharded index
     size_t n_local = 0;  // vectors whose lists live on this device
     fdb::DevBuf<float> cents;     // [nlist][dim]

@@ -67,6 +67,7 @@ struct GemmTopkParams {
     unsigned* cand_cnt;  // [nq] candidates seen (may exceed cap)
     int cap;
     int* err;            // error word (0 = ok)
+    unsigned long long wait;  // limit of each bounded wait, SM clock cycles
 };
 
 // Approximate metric families (compile-time, so no per-score branching):
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int i = 0; i < count; ++i) {
                 const int s = NSTAGE == 2 ? (i & 1) : 0;
                 const int use = NSTAGE == 2 ? (i >> 1) : i;
-                if (i >= NSTAGE && !mbar_wait(b_empty + s, (use - 1) & 1, p.err)) break;
+                if (i >= NSTAGE && !mbar_wait(b_empty + s, (use - 1) & 1, p.err, p.wait)) break;
                 mbar_expect_tx(b_full + s, stage_bytes);
                 const int row = (int)(r0 + (size_t)(first + i * stride) * TILE_N);
                 unsigned char* dst = b_tile + s * KA * ATOM_BYTES;
@@ -195,13 +196,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0 && count > 0) {
-            bool ok = mbar_wait(a_full, 0, p.err);
+            bool ok = mbar_wait(a_full, 0, p.err, p.wait);
             for (int i = 0; ok && i < count; ++i) {
                 const int s = NSTAGE == 2 ? (i & 1) : 0;
                 const int use = NSTAGE == 2 ? (i >> 1) : i;
                 const int b = i & 1;  // TMEM accumulator buffer
-                if (i >= 2 && !mbar_wait(t_empty + b, ((i >> 1) - 1) & 1, p.err)) break;
-                if (!mbar_wait(b_full + s, use & 1, p.err)) break;
+                if (i >= 2 && !mbar_wait(t_empty + b, ((i >> 1) - 1) & 1, p.err, p.wait)) break;
+                if (!mbar_wait(b_full + s, use & 1, p.err, p.wait)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * TILE_N);
                 const uint32_t abase = smem_u32(a_tile);
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int i = 0; i < count; ++i) {
                 const int b = i & 1;
                 int got = 0;
-                if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err) ? 1 : 0;
+                if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err, p.wait) ? 1 : 0;
                 got = __shfl_sync(0xffffffffu, got, 0);
                 if (!got) break;
                 tc_fence_after();
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int b = i & 1;
             // one lane waits; the warp follows its verdict (tcgen05.ld is warp-wide)
             int got = 0;
-            if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err) ? 1 : 0;
+            if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err, p.wait) ? 1 : 0;
             got = __shfl_sync(0xffffffffu, got, 0);
             if (!got) break;
             tc_fence_after();
@@ -409,8 +410,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     }
-    __syncthreads();
-    if (*(volatile int*)p.err) {
+    // One verdict for the whole block (another block may set the word while
+    // this block's threads read it; the barrier inside must not diverge).
+    if (__syncthreads_or(*(volatile int*)p.err != 0)) {
         // aborting: let the copies and MMAs this block issued land before exit
         // (waits on phases that already completed return at once)
         if (warp == 0 && lane == 0) {
@@ -559,6 +561,7 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     p.rows_per_chunk = rows_per_chunk;
     p.tag_base = tag_base;
     p.err = w.err;
+    p.wait = w.wait_cycles;
     // --- sample pass ---
     w.part.ensure((size_t)chunks * nq * tc::SAMPLE_K);
     w.top32.ensure((size_t)nq * tc::SAMPLE_K);

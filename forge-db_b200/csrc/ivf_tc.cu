@@ -96,6 +96,8 @@ struct PassParams {
     unsigned* cand_cnt;      // pass 2: [nq] candidates seen (may exceed cap)
     int cap;
     int* err;
+    unsigned long long wait;  // limit of each bounded wait, SM clock cycles
+    int stall;                // test hook: issue nothing (the waits run out)
 };
 
 #ifndef FDB_IVF_NSTAGE
@@ -142,11 +144,12 @@ __device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
 
 // Waits of the single-thread roles (TMA producer, MMA issuer): polling by
 // default, since their wake-up latency is on the pipeline's critical path.
-__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          unsigned long long limit) {
 #if FDB_IVF_SPIN_WAITS
-    return mbar_wait_spin(bar, parity, err);
+    return mbar_wait_spin(bar, parity, err, limit);
 #else
-    return mbar_wait(bar, parity, err);
+    return mbar_wait(bar, parity, err, limit);
 #endif
 }
 
@@ -154,12 +157,13 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* e
 #define FDB_IVF_EPI_SPIN 0
 #endif
 // Bounded wait of one lane, verdict shared with the warp.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int lane) {
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          unsigned long long limit, int lane) {
     int got = 0;
 #if FDB_IVF_EPI_SPIN
-    if (lane == 0) got = mbar_wait_spin(bar, parity, err) ? 1 : 0;
+    if (lane == 0) got = mbar_wait_spin(bar, parity, err, limit) ? 1 : 0;
 #else
-    if (lane == 0) got = mbar_wait(bar, parity, err) ? 1 : 0;
+    if (lane == 0) got = mbar_wait(bar, parity, err, limit) ? 1 : 0;
 #endif
     return __shfl_sync(0xffffffffu, got, 0) != 0;
 }
@@ -240,21 +244,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
+        // (p.stall, a test hook: the ring stays empty and nothing is copied,
+        // so the other roles wait on it_full until their limit runs out)
+        if (lane == 0 && !p.stall) {
             // Items are taken from the pass's counter (largest first, as they
             // are ordered) and handed to the other roles through a 2-slot ring.
             int g = 0;
             bool ok = true;
             for (int r = 0; ok; ++r) {
                 const int slot = r & 1;
-                if (r >= 2 && !role_wait(it_empty + slot, ((r >> 1) - 1) & 1, p.err)) break;
+                if (r >= 2 && !role_wait(it_empty + slot, ((r >> 1) - 1) & 1, p.err, p.wait))
+                    break;
                 const int idx = (int)atomicAdd(p.next, 1u);
                 ring[slot] = idx;
                 mbar_arrive(it_full + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
                 const int as = r % ASLOTS, au = r / ASLOTS;
-                if (r >= ASLOTS && !role_wait(a_empty + as, (au - 1) & 1, p.err)) break;
+                if (r >= ASLOTS && !role_wait(a_empty + as, (au - 1) & 1, p.err, p.wait)) break;
                 mbar_expect_tx(a_full + as, stage_bytes);
                 for (int a = 0; a < KA; ++a)
                     tma_load_2d(a_tile + (as * KA + a) * ATOM_BYTES, &amap, a_full + as,
@@ -263,7 +270,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS;
-                    if (g >= NS && !role_wait(b_empty + s, (use - 1) & 1, p.err)) {
+                    if (g >= NS && !role_wait(b_empty + s, (use - 1) & 1, p.err, p.wait)) {
                         ok = false;
                         break;
                     }
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < NS; ++i)
                         if (i == s) last_use[i] = use;
                     const int c = g % NCV, cu = g / NCV;
-                    if (g >= NCV && !role_wait(cv_empty + c, (cu - 1) & 1, p.err)) {
+                    if (g >= NCV && !role_wait(cv_empty + c, (cu - 1) & 1, p.err, p.wait)) {
                         ok = false;
                         break;
                     }
@@ -295,22 +302,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int r = 0; ok; ++r) {
                 const int slot = r & 1;
-                if (!role_wait(it_full + slot, (r >> 1) & 1, p.err)) break;
+                if (!role_wait(it_full + slot, (r >> 1) & 1, p.err, p.wait)) break;
                 const int idx = *(volatile int*)(ring + slot);
                 mbar_arrive(it_empty + slot);
                 if (idx >= nitems) break;
                 const Item it = items[idx];
                 const int nt = (int)((it.nb + TILE_N - 1) / TILE_N);
                 const int as = r % ASLOTS;
-                if (!role_wait(a_full + as, (r / ASLOTS) & 1, p.err)) break;
+                if (!role_wait(a_full + as, (r / ASLOTS) & 1, p.err, p.wait)) break;
                 tc_fence_after();
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int s = g % NS, use = g / NS, b = g % NACC;
-                    if (g >= NACC && !role_wait(t_empty + b, ((g / NACC) - 1) & 1, p.err)) {
+                    if (g >= NACC &&
+                        !role_wait(t_empty + b, ((g / NACC) - 1) & 1, p.err, p.wait)) {
                         ok = false;
                         break;
                     }
-                    if (!role_wait(b_full + s, use & 1, p.err)) {
+                    if (!role_wait(b_full + s, use & 1, p.err, p.wait)) {
                         ok = false;
                         break;
                     }
@@ -344,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool alive = true;
         for (int r = 0; alive; ++r) {
             const int slot = r & 1;
-            if (!warp_wait(it_full + slot, (r >> 1) & 1, p.err, lane)) break;
+            if (!warp_wait(it_full + slot, (r >> 1) & 1, p.err, p.wait, lane)) break;
             // lane 0 performed the acquiring wait: it reads the slot for the warp
             int idx = 0;
             if (lane == 0) {
@@ -361,8 +369,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // the loads and the scoring
                 for (int t = 0; t < nt; ++t, ++g) {
                     const int b = g % NACC, c = g % NCV;
-                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, lane) ||
-                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, lane)) {
+                    if (!warp_wait(t_full + b, (g / NACC) & 1, p.err, p.wait, lane) ||
+                        !warp_wait(cv_full + c, (g / NCV) & 1, p.err, p.wait, lane)) {
                         alive = false;
                         break;
                     }
@@ -386,8 +394,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t va[32], vb[32];
             auto begin_tile = [&](int gg) -> bool {
                 const int b = gg % NACC, c = gg % NCV;
-                if (!warp_wait(t_full + b, (gg / NACC) & 1, p.err, lane) ||
-                    !warp_wait(cv_full + c, (gg / NCV) & 1, p.err, lane))
+                if (!warp_wait(t_full + b, (gg / NACC) & 1, p.err, p.wait, lane) ||
+                    !warp_wait(cv_full + c, (gg / NCV) & 1, p.err, p.wait, lane))
                     return false;
                 tc_fence_after();
                 tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
@@ -512,8 +520,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     }
-    __syncthreads();
-    if (*(volatile int*)p.err) {
+    // One verdict for the whole block (another block may set the word while
+    // this block's threads read it; the barrier inside must not diverge).
+    if (__syncthreads_or(*(volatile int*)p.err != 0)) {
         // aborting: let the copies and MMAs this block issued land before exit
         // (waits on phases that already completed return at once)
         if (warp == 0 && lane == 0) {
@@ -1839,6 +1848,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.cand_cnt = h->t_cand_cnt.p;
     p.cap = cap;
     p.err = err;
+    p.wait = wait_limit_cycles(c, h->call_wait_cycles);
+    p.stall = take_test_stall(c) ? 1 : 0;
     p.next = h->t_range.p + 5;
     FDB_CUDA(cudaMemsetAsync(h->t_range.p + 5, 0, 8, s));
     const int grid = c.sm_count;
@@ -1849,7 +1860,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
-        FDB_NCCL(ncclAllReduce(h->t_tau.p, h->t_tau.p, nq, ncclFloat, ncclMin, c.comm, s));
+        FDB_NCCL_C(ncclAllReduce(h->t_tau.p, h->t_tau.p, nq, ncclFloat, ncclMin, c.comm, s), c.comm);
     }
     // --- pass 2: the other lists against tau + the certification margin ---
     h->t_tadm.ensure(nq);
@@ -1897,6 +1908,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.tau = h->t_tadm.p;
     p.range = h->t_range.p + 2;
     p.next = h->t_range.p + 6;
+    p.stall = take_test_stall(c) ? 1 : 0;
     if (pass_tm) pass_tm->mark();
     launch_pass<EPI_FILTER>(s, am2, bm, grid, p);
     if (pass_tm) pass_tm->mark();
@@ -1973,7 +1985,7 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the answer's k-th distance is at most the smallest exact k-th of any device
-        FDB_NCCL(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s));
+        FDB_NCCL_C(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s), c.comm);
     }
     if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
     else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);

@@ -320,7 +320,7 @@ void launch_select(cudaStream_t s, const float* D, int nq, int nlist, int take,
         while (npow2 < nlist) npow2 <<= 1;
         size_t smem = (size_t)npow2 * sizeof(uint64_t);
         FDB_REQUIRE(smem <= 200 * 1024, FDB_ERR_UNSUPPORTED,
-                    "nprobe > 256 supported up to 25600 lists");
+                    "more than 256 probes supported up to 16384 lists");
         if (smem > 48 * 1024)
             FDB_CUDA(cudaFuncSetAttribute(select_sort_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -22,7 +22,10 @@ constexpr int TILE_M = 128;   // rows of the A operand per tile (TMEM lanes)
 constexpr int TILE_N = 128;   // rows of the B operand per MMA tile
 constexpr int KATOM = 64;     // fp16 elements per 128-byte swizzle atom
 constexpr int ATOM_BYTES = TILE_M * 128;  // one [128 rows][64 fp16] swizzled atom
-constexpr unsigned long long WAIT_CYCLES = 4000000000ull;  // ~2 s at 1.9 GHz
+// Default limit of a bounded wait (about 2 s at 1.9 GHz).  Kernels take the
+// limit as a parameter (the context's setting); the drain of an aborting
+// block, which only waits for copies and MMAs it issued, always uses this.
+constexpr unsigned long long WAIT_CYCLES = 4000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -63,15 +66,16 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
-// Bounded wait.  Returns false if the kernel is aborting (this or another
-// warp timed out).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait: gives up after `limit` SM clock cycles.  Returns false if
+// the kernel is aborting (this or another warp timed out).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          unsigned long long limit) {
     if (mbar_try(bar, parity)) return true;
     const unsigned long long t0 = clock64();
     for (;;) {
         if (mbar_try_sleep(bar, parity)) return true;
         if (*(volatile int*)err) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             atomicExch(err, 1);
             return false;
         }
@@ -93,14 +97,15 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // Bounded wait that polls instead of suspending, for the single threads
 // (TMA producer, MMA issuer) whose wake-up latency is on the critical path.
 // Returns false if the kernel is aborting.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err,
+                                               unsigned long long limit) {
     if (mbar_test(bar, parity)) return true;
     const unsigned long long t0 = clock64();
     for (uint32_t n = 1;; ++n) {
         if (mbar_test(bar, parity)) return true;
         if ((n & 255) == 0) {
             if (*(volatile int*)err) return false;
-            if (clock64() - t0 > WAIT_CYCLES) {
+            if (clock64() - t0 > limit) {
                 atomicExch(err, 1);
                 return false;
             }

@@ -99,6 +99,9 @@ _SIGS = {
     "fdb_ctx_stream": (C.c_int, [_vp, C.POINTER(_vp)]),
     "fdb_nccl_unique_id": (C.c_int, [_vp]),
     "fdb_ctx_init_comm": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
+    "fdb_ctx_init_comm_timeout": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_double]),
+    "fdb_ctx_set_wait_limit": (C.c_int, [_vp, C.c_double]),
+    "fdb_ctx_test_stall_scans": (C.c_int, [_vp, C.c_int]),
     "fdb_host_alloc": (C.c_int, [_sz, C.POINTER(_vp)]),
     "fdb_host_free": (C.c_int, [_vp]),
     "fdb_sample_indices": (C.c_int, [C.c_uint64, _sz, _sz, _vp]),
@@ -130,6 +133,10 @@ _SIGS = {
     "fdb_ivfpq_batch_search": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, C.POINTER(Stats)]),
     "fdb_ivfpq_batch_search_device": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp,
                                                 C.POINTER(Stats)]),
+    "fdb_ivfpq_search_with_timeout": (C.c_int, [_vp, _vp, _sz, C.c_double, _vp, _vp,
+                                                C.POINTER(_sz), C.POINTER(C.c_double)]),
+    "fdb_ivfpq_batch_search_with_timeout": (C.c_int, [_vp, _vp, _sz, _sz, C.c_double, _vp, _vp,
+                                                      _vp, C.POINTER(C.c_double)]),
     "fdb_ivfpq_free": (C.c_int, [_vp]),
     "fdb_bf_create": (C.c_int, [_vp, C.c_int, _vp, _vp, _sz, _sz, C.POINTER(_vp)]),
     "fdb_bf_add": (C.c_int, [_vp, _vp, _vp, _sz, _sz]),
@@ -223,9 +230,20 @@ class Context:
         _check(lib().fdb_ctx_stream(self.h, C.byref(s)))
         return s.value or 0
 
-    def init_comm(self, rank: int, world: int, nccl_id: bytes):
+    def init_comm(self, rank: int, world: int, nccl_id: bytes, timeout_s: float = 300.0):
+        """The NCCL communicator of a sharded index; FDB_ERR_TIMEOUT (and no
+        communicator) if not every rank joins within timeout_s."""
         buf = C.create_string_buffer(bytes(nccl_id), 128)
-        _check(lib().fdb_ctx_init_comm(self.h, rank, world, buf))
+        _check(lib().fdb_ctx_init_comm_timeout(self.h, rank, world, buf, float(timeout_s)))
+
+    def set_wait_limit(self, seconds: float):
+        """Limit of each bounded wait inside the tensor-core kernels."""
+        _check(lib().fdb_ctx_set_wait_limit(self.h, float(seconds)))
+
+    def test_stall_scans(self, count: int):
+        """Test hook: the next `count` list-scan launches issue no work, so
+        their bounded waits run out (the call returns FDB_ERR_TIMEOUT)."""
+        _check(lib().fdb_ctx_test_stall_scans(self.h, int(count)))
 
     def close(self):
         if self.h:
@@ -524,6 +542,31 @@ class IVFPQIndex:
         return _results(ids, d, cnt)
 
     batch_search_parallel = batch_search
+
+    def search_with_timeout(self, query, k: int, timeout_s: float):
+        """search_with_timeout (ivf_pq.rs:1369-1455): (results, elapsed
+        seconds), or ForgeGpuError kind "Timeout" past the deadline."""
+        q = _f32(query)
+        ids = np.empty(max(k, 1), np.uint64)
+        d = np.empty(max(k, 1), np.float32)
+        n = C.c_size_t(0)
+        el = C.c_double(0.0)
+        _check(lib().fdb_ivfpq_search_with_timeout(self.h, _p(q), k, float(timeout_s), _p(ids),
+                                                   _p(d), C.byref(n), C.byref(el)))
+        return list(zip(ids[:n.value].tolist(), d[:n.value].tolist())), el.value
+
+    def batch_search_with_timeout_arrays(self, queries, k: int, timeout_s: float):
+        """batch_search under one deadline: (ids, dists, counts, elapsed)."""
+        Q = _f32(queries)
+        nq = Q.shape[0]
+        ids = np.empty((nq, k), np.uint64)
+        d = np.empty((nq, k), np.float32)
+        cnt = np.empty(nq, np.uint32)
+        el = C.c_double(0.0)
+        _check(lib().fdb_ivfpq_batch_search_with_timeout(self.h, _p(Q), nq, k, float(timeout_s),
+                                                         _p(ids), _p(d), _p(cnt),
+                                                         C.byref(el)))
+        return ids, d, cnt, el.value
 
     # --- re-ranking, filters, updates (ivf_pq.rs:513-831, 1731-1890) ---
     def enable_reranking(self, vectors, ids, rerank_factor: int):

@@ -133,9 +133,27 @@ int fdb_ctx_free(fdb_ctx* ctx);
 int fdb_ctx_stream(fdb_ctx* ctx, void** stream_out);
 /* Multi-GPU: rank 0 creates the 128-byte NCCL unique id, every rank passes it
  * to fdb_ctx_init_comm.  Searches on a sharded index then exchange local
- * top-k lists over NVLink (ncclAllGather) and merge on every device. */
+ * top-k lists over NVLink (ncclAllGather) and merge on every device.  The
+ * communicator is non-blocking: if not every rank joins within timeout_s
+ * (300 s for fdb_ctx_init_comm) the initialisation is aborted and the call
+ * returns FDB_ERR_TIMEOUT; the context stays usable without a communicator.
+ * (No reference counterpart: the reference runs on one host's cores.) */
 int fdb_nccl_unique_id(void* id_out /* 128 bytes */);
 int fdb_ctx_init_comm(fdb_ctx* ctx, int rank, int world, const void* nccl_id);
+int fdb_ctx_init_comm_timeout(fdb_ctx* ctx, int rank, int world, const void* nccl_id,
+                              double timeout_s);
+/* Limit of every bounded wait inside the tensor-core kernels (default 2 s).
+ * A wait that runs out makes the kernel stop, drain the copies it issued and
+ * return; the call then fails with FDB_ERR_TIMEOUT and the context stays
+ * usable (the next call starts clean).  Counterpart of the deadline checks of
+ * search_with_timeout (ivf_pq.rs:1369-1455). */
+int fdb_ctx_set_wait_limit(fdb_ctx* ctx, double seconds);
+/* Test hook for the timeout path: the next `count` list-scan launches of the
+ * tensor path on this context issue no work, so the waits inside them find a
+ * flag that nothing sets and run out after the wait limit (no fault, no hang:
+ * nothing is in flight).  The call that contains them returns
+ * FDB_ERR_TIMEOUT. */
+int fdb_ctx_test_stall_scans(fdb_ctx* ctx, int count);
 /* Host memory the device can copy from at full speed (cudaHostAlloc). */
 int fdb_host_alloc(size_t bytes, void** out);
 int fdb_host_free(void* p);
@@ -172,24 +190,37 @@ int fdb_assign(fdb_ctx* ctx, const float* x, size_t n, const float* centroids, s
 int fdb_find_nearest_centroids(fdb_ctx* ctx, const float* centroids, size_t kc, size_t dim,
                                const float* query, size_t k, uint32_t* out);
 
-/* No reference counterpart.  For callers that must not allocate device
- * memory at call time: the nearest-centroid search of
- * fdb_find_nearest_centroids for nq queries at once, on device buffers
+/* No reference counterpart.  An allocation-free form of
+ * fdb_find_nearest_centroids for callers that cannot call cudaMalloc at
+ * search time: a serving process that reserved all of its device memory in
+ * a pool at start-up (another allocation would fail or evict its pool), or a
+ * latency-bound loop where cudaMalloc's implicit device synchronisation is
+ * not allowed.  It serves nq queries at once on device buffers
  * (d_centroids[kc][dim], d_queries[nq][dim] -> d_out[nq][min(k, kc)], each
- * row ascending, same ids as the host-buffer call).  Its only scratch, the
- * nq x kc distance matrix, lives in a fixed array in the library's device
- * image, so the call itself never allocates.
- *   - nq * kc must not exceed FDB_NOALLOC_MAX_DISTANCES (16 MiB of floats)
- *     and nq must not exceed FDB_NOALLOC_MAX_QUERIES; larger requests fail
- *     with FDB_ERR_INVALID_ARG and nothing runs.  Split them into batches.
- *   - The first call on a device looks up the scratch address; make it
- *     (nq = 0 is enough) before any stream capture.  The call waits for its
- *     own stream, so it cannot itself be captured.
- *   - There is one scratch array per device: calls that overlap on a device
- *     (two contexts, or two threads with separate contexts) race on it.
- *     Calls through one context are serialised. */
+ * row ascending, the same ids as the host-buffer call).  Its only scratch,
+ * the nq x kc distance matrix, lives in a fixed array in the library's
+ * device image (16 MiB on every device that loads the library, held until
+ * the process exits), so the call itself never allocates.
+ *   - nq * kc must not exceed FDB_NOALLOC_MAX_DISTANCES (4 Mi floats) and nq
+ *     must not exceed FDB_NOALLOC_MAX_QUERIES; when min(k, kc) is above 256,
+ *     kc must not exceed FDB_NOALLOC_MAX_SORTED_CENTROIDS.  Larger requests
+ *     fail with FDB_ERR_INVALID_ARG before any device work.  Split them into
+ *     batches.
+ *   - The first call on a device does the set-up: it looks up the scratch
+ *     array's device address (with that device current) and keeps it for the
+ *     life of the process.  Make that first call (nq = 0 is enough) before
+ *     any stream capture.  A call with min(k, kc) above 256 and kc above
+ *     4096 also raises the selection kernel's shared-memory limit
+ *     (cudaFuncSetAttribute, no allocation) on each such call.
+ *   - After cudaDeviceReset of a device the kept address is stale, like every
+ *     other handle of this library on that device: do not call it again.
+ *   - There is one scratch array per device and each call reuses it: calls
+ *     that overlap on a device (two contexts, or two threads with separate
+ *     contexts) race on it.  Calls through one context are serialised, and
+ *     the call returns after its work on the device is complete. */
 #define FDB_NOALLOC_MAX_DISTANCES (1u << 22)
 #define FDB_NOALLOC_MAX_QUERIES (1u << 18)
+#define FDB_NOALLOC_MAX_SORTED_CENTROIDS (1u << 14)
 int fdb_find_nearest_centroids_noalloc(fdb_ctx* ctx, const float* d_centroids, size_t kc,
                                        size_t dim, const float* d_queries, size_t nq, size_t k,
                                        uint32_t* d_out);
@@ -247,6 +278,18 @@ int fdb_ivfpq_search(fdb_ivfpq* h, const float* query, size_t k, uint64_t* ids, 
  * nullable. */
 int fdb_ivfpq_batch_search(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
                            uint64_t* ids, float* dists, uint32_t* counts, fdb_stats* stats);
+/* IVFPQIndex::search_with_timeout (ivf_pq.rs:1369-1455): search() under a
+ * deadline timeout_s from the call.  Returns FDB_ERR_TIMEOUT (results not
+ * valid) when the deadline passes -- the kernels' bounded waits give up at it
+ * and results that come back after it are refused; elapsed_s (nullable)
+ * receives the call's duration, the reference's Ok((results, elapsed)).
+ * The batch form applies one deadline to batch_search() of nq queries. */
+int fdb_ivfpq_search_with_timeout(fdb_ivfpq* h, const float* query, size_t k, double timeout_s,
+                                  uint64_t* ids, float* dists, size_t* n_out,
+                                  double* elapsed_s);
+int fdb_ivfpq_batch_search_with_timeout(fdb_ivfpq* h, const float* queries, size_t nq, size_t k,
+                                        double timeout_s, uint64_t* ids, float* dists,
+                                        uint32_t* counts, double* elapsed_s);
 /* The same search on DEVICE buffers of this context's device, enqueued on the
  * context stream; returns after the results are written (stream synced). */
 int fdb_ivfpq_batch_search_device(fdb_ivfpq* h, const float* d_queries, size_t nq, size_t k,

@@ -31,10 +31,11 @@ def fg():
 def long_lists(fg, ctx, orc):
     from forgegpu.datasets import gmm_descriptors
     X = gmm_descriptors(200_000, components=128, seed=21)
-    # crowds: 300 copies each of 10 rows (more identical codes than the
-    # extension rescores), placed among the others
+    # crowds: 600 copies each of 10 rows (more identical codes than the
+    # 64-entry shortlist and the 256 entries an extension rescores), placed
+    # among the others
     crowd = gmm_descriptors(10, components=128, seed=23)
-    X = np.concatenate([X[:100_000], np.repeat(crowd, 300, axis=0), X[100_000:]])
+    X = np.concatenate([X[:100_000], np.repeat(crowd, 600, axis=0), X[100_000:]])
     Q = gmm_descriptors(2000, components=128, seed=22)
     ix = fg.IVFPQIndex.build(X, 128, 16, ctx=ctx, seed=7)
     cents, cb, offs, ids, codes = ix.export()
@@ -51,8 +52,10 @@ def test_tensor_path_long_lists(fg, orc, long_lists, nprobe, k):
     ox.set_nprobe(nprobe)
     ids, d, cnt, st = ix.batch_search_arrays(Q, k, stats=True)
     oi, od, oc = ox.batch_search(Q, k)
+    # the contract holds row by row; rows equal outright (ids and distances)
+    # are most of them (near-ties at the k-th distance may order differently)
     rate = assert_topk_match(ids, d, cnt, oi, od, oc, f"long lists nprobe={nprobe} k={k}")
-    assert rate > 0.9
+    assert rate > 0.8
     assert 0 < st.lists_probed <= len(Q) * nprobe  # empty lists are not counted
     # the tensor path ran and pruned part of the probed codes
     assert 0 < st.kernel_scores < st.codes_scanned
@@ -61,7 +64,7 @@ def test_tensor_path_long_lists(fg, orc, long_lists, nprobe, k):
 
 def test_tensor_path_long_lists_take_every_fallback(fg, orc, long_lists):
     """Over the whole batch the certificate extension and the exact re-scan
-    both run: queries next to a crowd of 300 identical codes cannot be
+    both run: queries next to a crowd of 600 identical codes cannot be
     certified from 64 shortlisted entries nor by extending over 256."""
     ix, ox, X, Q, _, crowd = long_lists
     ix.set_scan_mode(ix.SCAN_TENSOR)

@@ -1,11 +1,16 @@
 """The allocation-free nearest-centroid search, called through the C ABI.
 
-fdb_find_nearest_centroids_noalloc keeps its distance matrix in a fixed
-device array instead of allocating one per call.  These tests compare it,
-on device buffers the test owns, with the host-buffer entry point
-fdb_find_nearest_centroids (one query per call), twice in a row so that a
-second call over the reused scratch is checked too.  The file name sorts
-last so the tests also run after everything else in the suite.
+fdb_find_nearest_centroids_noalloc serves callers that cannot allocate
+device memory at search time (a process whose device memory is all reserved
+in a pool at start-up, or a loop that must not take cudaMalloc's implicit
+synchronisation): it keeps its distance matrix in a fixed device array
+instead of allocating one per call.  These tests compare it, on device
+buffers the test owns, with the host-buffer entry point
+fdb_find_nearest_centroids (one query per call) and with the oracle's
+restatement of KMeans::find_nearest_centroids (src/kmeans.rs:334-345), twice
+in a row so that a second call over the reused scratch is checked too.  The
+file name sorts last so the tests also run after everything else in the
+suite.
 """
 import ctypes as C
 
@@ -34,7 +39,7 @@ def _noalloc(lib, ctx, d_cents, kc, dim, d_q, nq, k, d_out):
 
 
 @pytest.mark.parametrize("k", [1, 16, 40, 300])
-def test_noalloc_matches_host_entry_point_twice(ctx, k):
+def test_noalloc_matches_host_entry_point_twice(ctx, orc, k):
     import torch
     import forgegpu as fg
     lib = fg.lib()
@@ -57,6 +62,7 @@ def test_noalloc_matches_host_entry_point_twice(ctx, k):
         for i in range(nq):
             want = _host_nearest(lib, ctx, cents, np.ascontiguousarray(q[i]), k)
             assert np.array_equal(got[i], want), (call, i)
+            assert np.array_equal(got[i], orc.find_nearest_centroids(cents, q[i], k)), (call, i)
 
 
 def test_noalloc_rejects_sizes_above_the_scratch(ctx):
@@ -69,6 +75,14 @@ def test_noalloc_rejects_sizes_above_the_scratch(ctx):
     rc = lib.fdb_find_nearest_centroids_noalloc(ctx.h, None, 4, 8, None, (1 << 18) + 1, 4, None)
     assert rc == -1
     assert b"FDB_NOALLOC_MAX_QUERIES" in lib.fdb_last_error()
+    # more than 256 ids per query are sorted in shared memory: at most 16384
+    # centroids then
+    rc = lib.fdb_find_nearest_centroids_noalloc(ctx.h, None, (1 << 14) + 1, 8, None, 5, 300,
+                                                None)
+    assert rc == -1
+    assert b"FDB_NOALLOC_MAX_SORTED_CENTROIDS" in lib.fdb_last_error()
+    rc = lib.fdb_find_nearest_centroids_noalloc(ctx.h, None, 1 << 14, 8, None, 5, 300, None)
+    assert rc == -1 and b"NULL" in lib.fdb_last_error()
     # exactly at the limit passes the size checks and then needs buffers
     rc = lib.fdb_find_nearest_centroids_noalloc(ctx.h, None, 1 << 12, 8, None, 1 << 10, 4, None)
     assert rc == -1 and b"NULL" in lib.fdb_last_error()
