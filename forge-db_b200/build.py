@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "forgegpu", "libforgegpu.so")
 SOURCES = ["capi.cu", "engine.cu", "distances.cu", "kmeans.cu", "pq.cu", "ivfpq_kernels.cu",
-           "bf_kernels.cu", "gemm_topk.cu", "ivf_tc.cu", "mutate.cu", "persist.cu"]
+           "bf_kernels.cu", "gemm_topk.cu", "ivf_tc.cu", "coarse_tc.cu", "mutate.cu", "persist.cu"]
 HEADERS = ["fdb_device.cuh", "fdb_internal.h", "fdb_kernels.h", "tc_ptx.cuh"]
 
 NVCC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")

@@ -236,6 +236,7 @@ void ivfpq_prepare_tables(fdb_ivfpq* h) {
         launch_transpose_pad(h->ctx->c.stream, h->cents.p, (int)nlist, (int)dim, h->nlist_pad,
                              h->centsT.p);
     }
+    coarse_tc_prepare(h);
     if (nlist == 0 || m == 0) return;
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
@@ -418,7 +419,8 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     const size_t per = nq * k;
     StageTimer tm(s, st != nullptr);
     StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
-    bool tensor_ran = false;
+    bool tensor_ran = false;  // the tensor-core list scan ran
+    bool waits_ran = false;   // some kernel with bounded waits ran (error word)
     tm.mark();
     if (k == 0) return;
     h->s_keys.ensure(per);
@@ -437,7 +439,13 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         const size_t nql = std::min(nq, q0 + slice) - q0;
         h->s_probe.ensure(slice * world * take);
         h->s_pdist.ensure(slice * world * take);
-        if (nql > 0) {
+        // the error word of the bounded waits in the tensor-core kernels
+        FDB_CUDA(cudaMemsetAsync(ivf_tc_error_word(h), 0, 4, s));
+        if (nql > 0 && coarse_tc_eligible(h, nql, take)) {
+            coarse_tc(h, dQ + q0 * h->dim, nql, take, h->s_probe.p + q0 * take,
+                      h->s_pdist.p + q0 * take);
+            waits_ran = true;
+        } else if (nql > 0) {
             const float* Ql = dQ + q0 * h->dim;
             h->s_coarse.ensure(nql * (size_t)nlist);
             if (h->centsT.p) {
@@ -578,13 +586,14 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     // synchronisation: pin[0..3] statistics, pin[4] error word, pin[5] the
     // number of re-scanned queries.
     int tc_err = 0;
-    if (tensor_ran || st || io) {
+    waits_ran = waits_ran || tensor_ran;
+    if (waits_ran || st || io) {
         uint64_t* pin = h->s_pin.get();
         for (int i = 0; i < 6; ++i) pin[i] = 0;
-        if (tensor_ran) {
+        if (waits_ran)
             FDB_CUDA(cudaMemcpyAsync(pin + 4, ivf_tc_error_word(h), 4, cudaMemcpyDeviceToHost, s));
-            if (st) FDB_CUDA(cudaMemcpyAsync(pin + 5, h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
-        }
+        if (tensor_ran && st)
+            FDB_CUDA(cudaMemcpyAsync(pin + 5, h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
         if (st && take > 0)
             FDB_CUDA(cudaMemcpyAsync(pin, h->s_stat.p, 32, cudaMemcpyDeviceToHost, s));
         FDB_CUDA(cudaStreamSynchronize(s));
@@ -617,7 +626,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         }
         st->total_ms = tm.ms(0, last);
     }
-    FDB_REQUIRE(tc_err == 0, FDB_ERR_TIMEOUT, "tensor-core list scan timed out on the device");
+    FDB_REQUIRE(tc_err == 0, FDB_ERR_TIMEOUT, "a tensor-core kernel timed out on the device");
 }
 
 // ---------------------------------------------------------------------------

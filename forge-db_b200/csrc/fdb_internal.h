@@ -329,6 +329,11 @@ void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order
                    const uint64_t* lbeg, const uint64_t* lend, uint64_t* out_keys,
                    uint32_t* flags, unsigned long long* stat, StageTimer* pass_tm);
 int* ivf_tc_error_word(fdb_ivfpq* h);
+// coarse_tc.cu: the coarse quantizer on the tensor cores
+void coarse_tc_prepare(fdb_ivfpq* h);
+bool coarse_tc_eligible(const fdb_ivfpq* h, size_t nq, size_t take);
+void coarse_tc(fdb_ivfpq* h, const float* dQ, size_t nq, size_t take, uint32_t* probes,
+               float* pdist);
 struct ScanParams;
 void ivf_tc_rescan(fdb_ivfpq* h, const ScanParams& base, size_t nq, size_t k, int order,
                    uint64_t* out_keys);
@@ -368,6 +373,12 @@ struct fdb_ivfpq {
     int scan_mode = FDB_SCAN_AUTO;
     fdb::DevBuf<float> centsT;          // [dim][nlist_pad] for the tiled coarse kernel
     int nlist_pad = 0;
+    // tensor-core coarse quantizer: centroids as fp16 rows scaled by 2^c16_sb,
+    // zero-padded to [c16_npad][c16_dpad], their squared norms, max norm
+    fdb::DevBuf<__half> c16;
+    fdb::DevBuf<float> c16_norm;
+    int c16_dpad = 0, c16_sb = 0, c16_npad = 0;
+    float c16_cmax = 0.0f;
     fdb::DevBuf<float> btab;            // [nlist][m][256]
     fdb::DevBuf<float> cmax, bmax;      // [m]
     // tensor mode (dim <= 128 after padding): codes decoded to fp16 residual
@@ -416,6 +427,9 @@ struct fdb_ivfpq {
     std::mutex mu;
     // per-call scratch
     fdb::DevBuf<float> s_q, s_coarse, s_qT, s_pdist;
+    fdb::DevBuf<__half> s_cq16;         // tensor coarse: fp16 query rows
+    fdb::DevBuf<float> s_cqn, s_cqs2, s_cqerr, s_cdapprox;
+    fdb::DevBuf<uint32_t> s_crange;     // tensor coarse: per-row min / max of d~
     fdb::DevBuf<uint32_t> s_probe;
     fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids, s_approx;
     fdb::DevBuf<float> s_dists;

@@ -2030,9 +2030,8 @@ void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order
     h->t_range.ensure(8);
     h->t_fprobes.ensure(nq * take);
     h->t_fcnt.ensure(nq);
-    int* err = ivf_tc_error_word(h);
+    int* err = ivf_tc_error_word(h);  // cleared by the caller at the start of the call
     FDB_CUDA(cudaMemsetAsync(flags, 0, 4, s));
-    FDB_CUDA(cudaMemsetAsync(err, 0, 4, s));
     for (size_t q0 = 0; q0 < nq; q0 += chunk) {
         const size_t nc = std::min(chunk, nq - q0);
         tc_chunk(h, dQ + q0 * h->dim, nc, k, order, take, h->s_probe.p + q0 * take,

@@ -127,3 +127,35 @@ def test_oracle_build_from_engine_draws_is_the_gpu_index(fg, ctx, orc, n, nlist,
     assert np.array_equal(offs, ox.offsets)
     assert np.array_equal(ids, ox.ids)
     assert np.array_equal(codes, ox.codes)
+
+
+@pytest.mark.parametrize("dim,nlist", [(8, 50), (37, 300), (64, 1024), (100, 130), (256, 257),
+                                       (128, 2048)])
+@pytest.mark.parametrize("nprobe", [1, 7, 64, 200])
+def test_tensor_coarse_quantizer_probes_match_oracle(fg, ctx, orc, dim, nlist, nprobe):
+    """Batches of 64+ queries pick their probes with the tcgen05 coarse
+    quantizer (fp16 GEMM, certified band, exact rescoring).  In the exact
+    scan mode that is the only approximate step, so any probe that differs
+    from find_nearest_partitions (ivf_pq.rs:865-888) shows in the results."""
+    if nprobe > nlist:
+        pytest.skip("nprobe above nlist")
+    rng = np.random.default_rng(dim * 1000 + nlist)
+    n = max(4 * nlist, 3000)
+    X = (rng.standard_normal((n, dim)) * rng.uniform(0.1, 50)).astype(np.float32)
+    Q = X[rng.integers(0, n, 300)] + rng.standard_normal((300, dim)).astype(np.float32)
+    m = 1 if dim % 2 else 2
+    ix = fg.IVFPQIndex.build(X, nlist, m, ctx=ctx, seed=dim, ivf_sample=min(n, 6000),
+                             pq_sample=min(n, 4000), ivf_iters=4, pq_iters=2)
+    ox = _oracle(orc, ix)
+    ix.set_scan_mode(1)
+    ix.set_nprobe(nprobe)
+    ox.set_nprobe(nprobe)
+    ids, d, cnt = ix.batch_search_arrays(Q, 10)
+    oi, od, oc = ox.batch_search(Q, 10)
+    assert_topk_match(ids, d, cnt, oi, od, oc, f"coarse dim={dim} nlist={nlist} p={nprobe}")
+    ix.set_scan_mode(0)
+
+
+def _oracle(orc, ix):
+    cents, cb, offs, ids, codes = ix.export()
+    return orc.OracleIVFPQ(cents, cb, offs, ids, codes)
