@@ -608,6 +608,14 @@ int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode) {
     });
 }
 
+int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->graphs = enable != 0;
+    });
+}
+
 size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h) {
     return h ? h->nprobe.load(std::memory_order_relaxed) : 0;
 }

@@ -398,31 +398,27 @@ static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_k
                            merged_ids.p);
 }
 
-void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, int order,
-                      size_t take, uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
-                      fdb_stats* st, const uint32_t* call_skip, size_t fetch_mult,
-                      const HostIO* io) {
+namespace {
+
+using SearchRun = GraphSlot::Run;
+
+// Every piece of device work of one search, enqueued on the context stream
+// without a host synchronisation: probe selection, the scan, rescoring, the
+// exchange of a sharded index, the results (and, with io, their copies to
+// the host) and the end-of-call readbacks into pinned words.  The timers
+// get their marks here.
+SearchRun ivfpq_enqueue(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, size_t k,
+                        int order, size_t take, uint64_t* d_ids, float* d_dists,
+                        uint32_t* d_counts, fdb_stats* st, const uint32_t* call_skip,
+                        const uint32_t* skip, const HostIO* io, StageTimer& tm,
+                        StageTimer& pass_tm) {
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     const int nlist = (int)h->nlist;
-    if (st) std::memset(st, 0, sizeof(*st));
-    if (nq == 0) return;
-    ivfpq_sync_state(h);
-    // fetch_k: with re-ranking, k * rerank_factor PQ candidates (ivf_pq.rs:591-596)
-    const size_t k = h->rerank ? k_out * h->rerank_factor * fetch_mult : k_out;
-    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED,
-                h->rerank ? "k * rerank_factor above FDB_MAX_K" : "k above FDB_MAX_K");
-    // rows the scan skips: this call's filter, else the tombstoned rows
-    const uint32_t* skip = call_skip ? call_skip : (h->n_tomb ? h->dead.p : nullptr);
-    FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
-                "sharded index needs a communicator of the same size");
     const size_t per = nq * k;
-    StageTimer tm(s, st != nullptr);
-    StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
     bool tensor_ran = false;  // the tensor-core list scan ran
     bool waits_ran = false;   // some kernel with bounded waits ran (error word)
     tm.mark();
-    if (k == 0) return;
     h->s_keys.ensure(per);
     h->s_ids.ensure(per);
     if (take == 0) {  // marks 1..3 still taken so stage times line up
@@ -581,21 +577,148 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
         if (io->counts)
             FDB_CUDA(cudaMemcpyAsync(io->counts, d_counts, nq * 4, cudaMemcpyDeviceToHost, s));
     }
-    // The tensor path's error word (a bounded wait in the list scan that ran
-    // out) and the statistics are read into pinned words after one
-    // synchronisation: pin[0..3] statistics, pin[4] error word, pin[5] the
-    // number of re-scanned queries.
-    int tc_err = 0;
+    // The error word of the bounded waits and the statistics are read into
+    // pinned words (after the caller's one synchronisation): pin[0..3]
+    // statistics, pin[4] error word, pin[5] the number of re-scanned queries.
     waits_ran = waits_ran || tensor_ran;
     if (waits_ran || st || io) {
         uint64_t* pin = h->s_pin.get();
-        for (int i = 0; i < 6; ++i) pin[i] = 0;
         if (waits_ran)
             FDB_CUDA(cudaMemcpyAsync(pin + 4, ivf_tc_error_word(h), 4, cudaMemcpyDeviceToHost, s));
         if (tensor_ran && st)
             FDB_CUDA(cudaMemcpyAsync(pin + 5, h->s_flags.p, 4, cudaMemcpyDeviceToHost, s));
         if (st && take > 0)
             FDB_CUDA(cudaMemcpyAsync(pin, h->s_stat.p, 32, cudaMemcpyDeviceToHost, s));
+    }
+    SearchRun r;
+    r.tensor_ran = tensor_ran;
+    r.waits_ran = waits_ran;
+    return r;
+}
+
+// The search key of a captured graph: every value the enqueued work bakes
+// into its launches (pointers, sizes, modes) besides the scratch buffers,
+// whose addresses stay put while the allocation epoch is unchanged.
+GraphKey search_key(const fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, size_t k,
+                    int order, size_t take, const uint64_t* d_ids, const float* d_dists,
+                    const uint32_t* d_counts, const fdb_stats* st, const uint32_t* call_skip,
+                    const uint32_t* skip, const HostIO* io) {
+    GraphKey g{};
+    g[0] = (uint64_t)dQ;
+    g[1] = nq;
+    g[2] = k_out;
+    g[3] = k;
+    g[4] = (uint64_t)order;
+    g[5] = take;
+    g[6] = (uint64_t)d_ids;
+    g[7] = (uint64_t)d_dists;
+    g[8] = (uint64_t)d_counts;
+    g[9] = st != nullptr;
+    g[10] = (uint64_t)call_skip;
+    g[11] = (uint64_t)skip;
+    g[12] = io ? (uint64_t)io->ids : 0;
+    g[13] = io ? (uint64_t)io->dists : 0;
+    g[14] = io ? (uint64_t)io->counts : 0;
+    g[15] = ((uint64_t)h->scan_mode << 32) | (uint64_t)h->rerank;
+    g[16] = h->rerank_factor;
+    g[17] = 1;  // a valid key
+    return g;
+}
+
+}  // namespace
+
+void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, int order,
+                      size_t take, uint64_t* d_ids, float* d_dists, uint32_t* d_counts,
+                      fdb_stats* st, const uint32_t* call_skip, size_t fetch_mult,
+                      const HostIO* io) {
+    Ctx& c = h->ctx->c;
+    cudaStream_t s = c.stream;
+    if (st) std::memset(st, 0, sizeof(*st));
+    if (nq == 0) return;
+    ivfpq_sync_state(h);
+    // fetch_k: with re-ranking, k * rerank_factor PQ candidates (ivf_pq.rs:591-596)
+    const size_t k = h->rerank ? k_out * h->rerank_factor * fetch_mult : k_out;
+    FDB_REQUIRE(k <= FDB_MAX_K, FDB_ERR_UNSUPPORTED,
+                h->rerank ? "k * rerank_factor above FDB_MAX_K" : "k above FDB_MAX_K");
+    // rows the scan skips: this call's filter, else the tombstoned rows
+    const uint32_t* skip = call_skip ? call_skip : (h->n_tomb ? h->dead.p : nullptr);
+    FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
+                "sharded index needs a communicator of the same size");
+    if (k == 0) return;
+    StageTimer tm(s, st != nullptr);
+    StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
+    uint64_t* pin = h->s_pin.get();
+    for (int i = 0; i < 6; ++i) pin[i] = 0;
+    // A search of one device whose work has no host synchronisation (it has
+    // none unless the table mode's count readback) runs as a CUDA graph from
+    // its second call with the same key: the first call runs eagerly (and
+    // sizes every scratch buffer), the second is captured, later ones replay
+    // it -- one launch instead of ~40.  The test hooks and a call's own
+    // deadline keep a call eager.
+    GraphCache& gc = h->graphs_cache;
+    const bool graphable = h->graphs && !h->sharded && take > 0 &&
+                           c.test_stalls.load() == 0 && h->call_wait_cycles == 0 &&
+                           !(h->btab.p && h->scan_mode != FDB_SCAN_EXACT &&
+                             !(ivf_tc_eligible(h, k) &&
+                               (h->scan_mode == FDB_SCAN_TENSOR ||
+                                (h->scan_mode == FDB_SCAN_AUTO && nq >= 256))) &&
+                             k <= 128);
+    const GraphKey key = search_key(h, dQ, nq, k_out, k, order, take, d_ids, d_dists, d_counts,
+                                    st, call_skip, skip, io);
+    const uint64_t epoch = devbuf_epoch().load();
+    SearchRun r;
+    GraphSlot* hit = graphable ? gc.find(key, epoch) : nullptr;
+    if (hit) {
+        FDB_CUDA(cudaGraphLaunch(hit->exec, s));
+        r = hit->run;
+        tm.borrow(hit->tm_ev);
+        pass_tm.borrow(hit->pass_ev);
+    } else if (graphable && gc.was_seen(key, epoch) && !gc.is_refused(key)) {
+        GraphSlot* g = gc.take();
+        g->ensure_events(32);
+        tm.use_pool(&g->pool, 0);
+        pass_tm.use_pool(&g->pool, 16);
+        FDB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        bool ok = true;
+        try {
+            r = ivfpq_enqueue(h, dQ, nq, k_out, k, order, take, d_ids, d_dists, d_counts, st,
+                              call_skip, skip, io, tm, pass_tm);
+        } catch (...) {
+            ok = false;
+        }
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+        cudaGraphExec_t exec = nullptr;
+        ok = ok && ec == cudaSuccess && graph && devbuf_epoch().load() == epoch &&
+             cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+        if (graph) cudaGraphDestroy(graph);
+        if (ok) {
+            g->exec = exec;
+            g->key = key;
+            g->epoch = epoch;
+            g->used = ++gc.clock;
+            g->run = r;
+            g->tm_ev = tm.ev;
+            g->pass_ev = pass_tm.ev;
+            FDB_CUDA(cudaGraphLaunch(exec, s));
+        } else {
+            // not capturable: this key stays eager
+            if (exec) cudaGraphExecDestroy(exec);
+            cudaGetLastError();
+            gc.refused.push_back(key);
+            tm.reset();
+            pass_tm.reset();
+            r = ivfpq_enqueue(h, dQ, nq, k_out, k, order, take, d_ids, d_dists, d_counts, st,
+                              call_skip, skip, io, tm, pass_tm);
+        }
+    } else {
+        r = ivfpq_enqueue(h, dQ, nq, k_out, k, order, take, d_ids, d_dists, d_counts, st,
+                          call_skip, skip, io, tm, pass_tm);
+        if (graphable) gc.note_seen(key, devbuf_epoch().load());  // after this call's allocations
+    }
+    const bool tensor_ran = r.tensor_ran;
+    int tc_err = 0;
+    if (r.waits_ran || st || io) {
         FDB_CUDA(cudaStreamSynchronize(s));
         tc_err = (int)(uint32_t)pin[4];
     }

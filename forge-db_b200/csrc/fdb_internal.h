@@ -8,9 +8,11 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -63,6 +65,13 @@ void nccl_complete(ncclResult_t r, ncclComm_t comm, const char* what);
 // ---------------------------------------------------------------------------
 // device memory
 // ---------------------------------------------------------------------------
+// Counts every device allocation and release made through DevBuf: a captured
+// CUDA graph bakes in buffer addresses, and stays valid while this is unchanged.
+inline std::atomic<uint64_t>& devbuf_epoch() {
+    static std::atomic<uint64_t> e{0};
+    return e;
+}
+
 template <typename T>
 struct DevBuf {
     T* p = nullptr;
@@ -79,7 +88,10 @@ struct DevBuf {
     ~DevBuf() { release(); }
     void alloc(size_t count) {
         release();
-        if (count) FDB_CUDA(cudaMalloc(&p, count * sizeof(T)));
+        if (count) {
+            FDB_CUDA(cudaMalloc(&p, count * sizeof(T)));
+            devbuf_epoch().fetch_add(1);
+        }
         n = count;
     }
     // Grow-only: keep the allocation if it is already large enough.
@@ -87,7 +99,10 @@ struct DevBuf {
         if (count > n) alloc(count);
     }
     void release() {
-        if (p) cudaFree(p);
+        if (p) {
+            cudaFree(p);
+            devbuf_epoch().fetch_add(1);
+        }
         p = nullptr;
         n = 0;
     }
@@ -171,20 +186,48 @@ struct HostIO {
     uint32_t* counts = nullptr;   // nullable
 };
 
-// Times device stages on a stream with CUDA events.
+// Times device stages on a stream with CUDA events.  Inside a stream
+// capture it records into events of a pool that outlives the call (external
+// records: graph nodes that record the event at each replay).
 struct StageTimer {
     cudaStream_t s;
     bool on;
     std::vector<cudaEvent_t> ev;
+    std::vector<cudaEvent_t>* pool = nullptr;  // owner of the events (capture, replay)
+    size_t next = 0;                           // next pool event
+    bool owned = true;
     StageTimer(cudaStream_t s_, bool on_) : s(s_), on(on_) {}
-    ~StageTimer() {
-        for (auto e : ev) cudaEventDestroy(e);
+    ~StageTimer() { reset(); }
+    void reset() {
+        if (owned)
+            for (auto e : ev) cudaEventDestroy(e);
+        ev.clear();
+        pool = nullptr;
+        owned = true;
+    }
+    void use_pool(std::vector<cudaEvent_t>* p, size_t first) {
+        reset();
+        pool = p;
+        next = first;
+        owned = false;
+    }
+    // the events a replayed graph records (owned by the graph's pool)
+    void borrow(const std::vector<cudaEvent_t>& e) {
+        reset();
+        ev = e;
+        owned = false;
     }
     void mark() {
         if (!on) return;
         cudaEvent_t e;
-        FDB_CUDA(cudaEventCreate(&e));
-        FDB_CUDA(cudaEventRecord(e, s));
+        if (pool) {
+            FDB_REQUIRE(next < pool->size(), FDB_ERR_UNSUPPORTED, "stage timer pool exhausted");
+            e = (*pool)[next++];
+            FDB_CUDA(cudaEventRecordWithFlags(e, s, cudaEventRecordExternal));
+        } else {
+            FDB_CUDA(cudaEventCreate(&e));
+            FDB_CUDA(cudaEventRecord(e, s));
+        }
         ev.push_back(e);
     }
     // Milliseconds between marks a and b (after the stream is synced).
@@ -282,6 +325,88 @@ void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, i
 
 }  // namespace fdb
 
+// A captured search (see ivfpq_search_dev): the key of the call it replays,
+// the allocation epoch its buffer addresses belong to, and its timing events.
+namespace fdb {
+using GraphKey = std::array<uint64_t, 18>;
+struct GraphSlot {
+    GraphKey key{};
+    uint64_t epoch = 0;
+    uint64_t used = 0;  // last use (LRU)
+    cudaGraphExec_t exec = nullptr;
+    struct Run {
+        bool tensor_ran = false, waits_ran = false;
+    } run;
+    std::vector<cudaEvent_t> pool, tm_ev, pass_ev;
+    void drop() {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        key = GraphKey{};
+        tm_ev.clear();
+        pass_ev.clear();
+    }
+    void ensure_events(size_t n) {
+        while (pool.size() < n) {
+            cudaEvent_t e;
+            FDB_CUDA(cudaEventCreate(&e));
+            pool.push_back(e);
+        }
+    }
+    ~GraphSlot() {
+        drop();
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+// Captured searches of one index (a few keys: a caller typically alternates
+// between a couple of call shapes) and the keys seen once, eagerly.
+struct GraphCache {
+    static constexpr size_t kSlots = 4, kSeen = 8;
+    std::vector<std::unique_ptr<GraphSlot>> slots;
+    std::vector<std::pair<GraphKey, uint64_t>> seen;  // (key, epoch after the call)
+    std::vector<GraphKey> refused;                    // keys that could not be captured
+    uint64_t clock = 0;
+    GraphSlot* find(const GraphKey& k, uint64_t epoch) {
+        for (auto& g : slots)
+            if (g->exec && g->key == k && g->epoch == epoch) {
+                g->used = ++clock;
+                return g.get();
+            }
+        return nullptr;
+    }
+    bool was_seen(const GraphKey& k, uint64_t epoch) const {
+        for (auto& e : seen)
+            if (e.first == k && e.second == epoch) return true;
+        return false;
+    }
+    bool is_refused(const GraphKey& k) const {
+        for (auto& r : refused)
+            if (r == k) return true;
+        return false;
+    }
+    void note_seen(const GraphKey& k, uint64_t epoch) {
+        for (auto& e : seen)
+            if (e.first == k) {
+                e.second = epoch;
+                return;
+            }
+        if (seen.size() == kSeen) seen.erase(seen.begin());
+        seen.emplace_back(k, epoch);
+    }
+    // a slot for a new capture: a free one, else the least recently used
+    GraphSlot* take() {
+        if (slots.size() < kSlots) {
+            slots.emplace_back(new GraphSlot());
+            return slots.back().get();
+        }
+        GraphSlot* lru = slots[0].get();
+        for (auto& g : slots)
+            if (g->used < lru->used) lru = g.get();
+        lru->drop();
+        return lru;
+    }
+};
+}  // namespace fdb
+
 struct fdb_ivfpq;
 struct fdb_bf;
 namespace fdb {
@@ -356,6 +481,8 @@ struct fdb_ivfpq {
     int metric = 0;
     std::atomic<size_t> nprobe{1};
     unsigned long long call_wait_cycles = 0;  // a call's own wait limit (0: none)
+    bool graphs = true;                       // replay repeated searches as CUDA graphs
+    fdb::GraphCache graphs_cache;
     size_t n_total = 0;  // vectors in the unsharded index
     size_t n_local = 0;  // vectors whose lists live on this device
     fdb::DevBuf<float> cents;     // [nlist][dim]

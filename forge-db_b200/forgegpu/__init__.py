@@ -124,6 +124,7 @@ _SIGS = {
     "fdb_ivfpq_shard_plan": (C.c_int, [_vp, _sz, C.c_int, _vp]),
     "fdb_ivfpq_set_nprobe": (C.c_int, [_vp, _sz]),
     "fdb_ivfpq_set_scan_mode": (C.c_int, [_vp, C.c_int]),
+    "fdb_ivfpq_set_graphs": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_nprobe": (_sz, [_vp]),
     "fdb_ivfpq_len": (_sz, [_vp]),
     "fdb_ivfpq_n_partitions": (_sz, [_vp]),
@@ -500,6 +501,10 @@ class IVFPQIndex:
 
     def set_scan_mode(self, mode: int):
         _check(lib().fdb_ivfpq_set_scan_mode(self.h, mode))
+
+    def set_graphs(self, enable: bool):
+        """Replay repeated same-shape batch searches as CUDA graphs."""
+        _check(lib().fdb_ivfpq_set_graphs(self.h, int(bool(enable))))
 
     def nprobe(self) -> int:
         return lib().fdb_ivfpq_nprobe(self.h)

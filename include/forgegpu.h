@@ -262,6 +262,11 @@ int fdb_ivfpq_shard_plan(const uint64_t* sizes, size_t nlist, int world, int* ow
 /* Scan mode (FDB_SCAN_*); no reference counterpart (the reference has one
  * CPU scan).  Results are identical in every mode. */
 int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode);
+/* Repeated batch searches of one shape (the same buffers, sizes and modes)
+ * replay a CUDA graph of the whole device step from their second call
+ * instead of launching ~40 kernels (default: on).  No reference counterpart
+ * (a launch-overhead choice of this engine); results are identical. */
+int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable);
 /* set_nprobe (ivf_pq.rs:524-528): stores min(nprobe, nlist). */
 int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe);
 size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h);
