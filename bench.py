@@ -165,7 +165,7 @@ SCALING = "strong"     # the batch and the index are fixed as N grows
 
 # DRAM bytes (read + write) per launch of the dominant kernel on the default
 # workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC = {"ivf_pass_filter": 88.4e6, "bf_gemm_filter": None}
+NCU_TRAFFIC = {"ivf_pass_filter": 91.8e6, "bf_gemm_filter": None}
 # brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
 # filter pass, candidate selection, exact rescore, keys->ids, finalize
 BF_LAUNCHES = 10

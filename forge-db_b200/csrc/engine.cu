@@ -705,6 +705,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
             // not capturable: this key stays eager
             if (exec) cudaGraphExecDestroy(exec);
             cudaGetLastError();
+            if (gc.refused.size() == GraphCache::kSeen) gc.refused.erase(gc.refused.begin());
             gc.refused.push_back(key);
             tm.reset();
             pass_tm.reset();

@@ -982,58 +982,128 @@ __global__ void __launch_bounds__(256)
                    const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend, int nq,
                    uint64_t* __restrict__ part, float* __restrict__ tau) {
     __shared__ uint64_t buf[8 * 64];
+    __shared__ unsigned hist[8 * 256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * 8 + warp;
     if (q >= nq) return;
-    WarpTopK<2> tk;
-    tk.init(LIST_K, buf + warp * 64);
     const unsigned n1 = poff[nlist], npairs = poff[2 * nlist];
-    // Probes in batches of 32: each lane looks up one probe's dump row (the
-    // index chain inv -> list -> bounds runs in parallel across lanes), then
-    // the rows are streamed one probe at a time.
-    for (int jp0 = 0; jp0 < take; jp0 += 32) {
-        const int jp = jp0 + lane;
-        unsigned start = 0, nbl = 0, tagl = 0;
-        if (jp < take) {
-            const size_t v = (size_t)q * take + jp;
-            const uint32_t i = inv[v];
-            if (i < npairs) {  // else: list empty or held elsewhere
-                const uint32_t l = probes[v];
-                const unsigned len = (unsigned)(lend[l] - lbeg[l]);
-                nbl = i < n1 ? len : min(len, (unsigned)TILE_N);
-                start = seg[i];
-                tagl = (uint32_t)lbeg[l];
+    // Visits the query's dump rows: probes in batches of 32 (each lane looks
+    // up one probe's row: the index chain inv -> list -> bounds runs in
+    // parallel across lanes), then the rows one probe at a time, 128 entries
+    // per step, f(d[4], tag of entry 0, entries valid) per lane.
+    auto visit = [&](auto&& f) {
+        for (int jp0 = 0; jp0 < take; jp0 += 32) {
+            const int jp = jp0 + lane;
+            unsigned start = 0, nbl = 0, tagl = 0;
+            if (jp < take) {
+                const size_t v = (size_t)q * take + jp;
+                const uint32_t i = inv[v];
+                if (i < npairs) {  // else: list empty or held elsewhere
+                    const uint32_t l = probes[v];
+                    const unsigned len = (unsigned)(lend[l] - lbeg[l]);
+                    nbl = i < n1 ? len : min(len, (unsigned)TILE_N);
+                    start = seg[i];
+                    tagl = (uint32_t)lbeg[l];
+                }
+            }
+            unsigned live = __ballot_sync(0xffffffffu, nbl > 0);
+            while (live) {
+                const int p = __ffs(live) - 1;
+                live &= live - 1;
+                const int nb = (int)__shfl_sync(0xffffffffu, nbl, p);
+                const uint32_t tag0 = __shfl_sync(0xffffffffu, tagl, p);
+                // rows are padded to a multiple of 128 floats
+                const float4* row4 =
+                    reinterpret_cast<const float4*>(dump + __shfl_sync(0xffffffffu, start, p));
+                for (int base = 0; base < nb; base += 128) {
+                    const float4 x4 = row4[(base >> 2) + lane];
+                    const int j = base + 4 * lane;
+                    const float d[4] = {x4.x, x4.y, x4.z, x4.w};
+                    f(d, tag0 + (uint32_t)j, nb - j);
+                }
             }
         }
-        unsigned live = __ballot_sync(0xffffffffu, nbl > 0);
-        while (live) {
-            const int p = __ffs(live) - 1;
-            live &= live - 1;
-            const int nb = (int)__shfl_sync(0xffffffffu, nbl, p);
-            const uint32_t tag0 = __shfl_sync(0xffffffffu, tagl, p);
-            // rows are padded to a multiple of 128 floats
-            const float4* row4 =
-                reinterpret_cast<const float4*>(dump + __shfl_sync(0xffffffffu, start, p));
-            for (int base = 0; base < nb; base += 128) {
-                const float4 x4 = row4[(base >> 2) + lane];
-                const int j = base + 4 * lane;
-                const float d[4] = {x4.x, x4.y, x4.z, x4.w};
-                uint64_t key[4];
-                bool any = false;
+    };
+    // 1. the range of the query's finite distances (+inf marks a tombstoned row)
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    visit([&](const float(&d)[4], uint32_t, int nv) {
 #pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    // +inf marks a tombstoned row
-                    key[x] = (j + x < nb && d[x] < INF)
-                                 ? make_key(d[x], tag0 + (uint32_t)(j + x))
-                                 : KEY_NONE;
-                    any |= key[x] < tk.thr;
+        for (int x = 0; x < 4; ++x)
+            if (x < nv && d[x] < INF) {
+                lo = min(lo, f2ord(d[x]));
+                hi = max(hi, f2ord(d[x]));
+            }
+    });
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    // 2. a threshold t with at least LIST_K entries d <= t: the rounded-up
+    //    upper edge of the first of 256 bins (between lo and hi) whose running
+    //    count reaches LIST_K (all entries when there are fewer)
+    float t = INF;
+    if (lo <= hi) {
+        unsigned* hs = hist + warp * 256;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hs[j * 32 + lane] = 0u;
+        __syncwarp();
+        const float scale = 256.0f / ((float)(hi - lo) + 1.0f);
+        visit([&](const float(&d)[4], uint32_t, int nv) {
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+                if (x < nv && d[x] < INF)
+                    atomicAdd(&hs[min(255, (int)((float)(f2ord(d[x]) - lo) * scale))], 1u);
+        });
+        __syncwarp();
+        unsigned c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            c[j] = hs[8 * lane + j];
+            sum += c[j];
+        }
+        unsigned incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const unsigned reach = __ballot_sync(0xffffffffu, incl >= (unsigned)LIST_K);
+        if (reach) {
+            const int owner = __ffs(reach) - 1;
+            int bs = 255;
+            unsigned run = incl - sum;
+            bool found = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                run += c[j];
+                if (!found && run >= (unsigned)LIST_K) {
+                    bs = 8 * lane + j;
+                    found = true;
                 }
-                if (!__any_sync(0xffffffffu, any)) continue;
-#pragma unroll
-                for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
+            }
+            const int bstar = __shfl_sync(0xffffffffu, bs, owner);
+            if (bstar < 255) {
+                // every entry in bins <= bstar has (bits - lo) * scale < bstar + 1
+                // in float arithmetic; the bound is widened for both roundings
+                const double w = ((double)bstar + 1.0) / (double)scale * (1.0 + 1e-6) + 2.0;
+                t = ord2f((uint32_t)min((double)hi, (double)lo + ceil(w)));
             }
         }
     }
+    // 3. the top-LIST_K keys among the entries d <= t
+    WarpTopK<2> tk;
+    tk.init(LIST_K, buf + warp * 64);
+    visit([&](const float(&d)[4], uint32_t tag, int nv) {
+        uint64_t key[4];
+        bool any = false;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            key[x] = (x < nv && d[x] < INF && d[x] <= t) ? make_key(d[x], tag + (uint32_t)x)
+                                                          : KEY_NONE;
+            any |= key[x] < tk.thr;
+        }
+        if (!__any_sync(0xffffffffu, any)) return;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) tk.add(key[x], key[x] != KEY_NONE);
+    });
     tk.flush();
     tk.store(part + (size_t)q * LIST_K);
     if (lane == 0) tau[q] = tk.thr == KEY_NONE ? INF : key_dist(tk.thr);
