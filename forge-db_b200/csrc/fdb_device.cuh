@@ -266,6 +266,67 @@ __device__ __forceinline__ float exact_adc(const float* __restrict__ q,
     return adc_order<ORDER>(entry, m);
 }
 
+// exact_adc for a compile-time shape (M subvectors of SUB floats, SUB a
+// multiple of 4, the rows 16-byte aligned): every loop is unrolled, so the
+// loads of all M entries can be in flight together instead of one entry's
+// after another's.  Same operations in the same order as exact_adc.
+template <int ORDER, int M, int SUB>
+__device__ __forceinline__ float exact_adc_fixed(const float* __restrict__ q,
+                                                 const float* __restrict__ c,
+                                                 const float* __restrict__ cb,
+                                                 const uint8_t* __restrict__ code) {
+    static_assert(SUB % 4 == 0 || SUB == 2, "row segments of whole 128- or 64-bit loads");
+    uint8_t cd[M];
+#pragma unroll
+    for (int s = 0; s < M; ++s) cd[s] = __ldg(code + s);
+    float lut[M];
+#pragma unroll
+    for (int s = 0; s < M; ++s) {
+        const float* qs = q + s * SUB;
+        const float* cs = c + s * SUB;
+        const float* b = cb + ((size_t)s * KSUB + cd[s]) * SUB;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        float t;
+        if constexpr (SUB >= 8) {
+#pragma unroll
+            for (int i = 0; i + 8 <= SUB; i += 8) {
+                const float4 q0 = __ldg(reinterpret_cast<const float4*>(qs + i));
+                const float4 q1 = __ldg(reinterpret_cast<const float4*>(qs + i + 4));
+                const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + i));
+                const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + i + 4));
+                const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + i));
+                const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + i + 4));
+                const float qa[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                const float ca[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float ba[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float d = __fsub_rn(__fsub_rn(qa[j], ca[j]), ba[j]);
+                    acc[j] = __fmaf_rn(d, d, acc[j]);
+                }
+            }
+            t = lane_sum(acc);
+#pragma unroll
+            for (int i = SUB & ~7; i < SUB; ++i) {
+                const float d = __fsub_rn(__fsub_rn(__ldg(qs + i), __ldg(cs + i)), __ldg(b + i));
+                t = __fadd_rn(t, __fmul_rn(d, d));
+            }
+        } else {
+            // fewer than 8 floats: no full lane group, the unfused tail only
+            t = lane_sum(acc);
+#pragma unroll
+            for (int i = 0; i < SUB; ++i) {
+                const float d = __fsub_rn(__fsub_rn(__ldg(qs + i), __ldg(cs + i)), __ldg(b + i));
+                t = __fadd_rn(t, __fmul_rn(d, d));
+            }
+        }
+        lut[s] = t;
+    }
+    return adc_order<ORDER>([&](int i) { return lut[i]; }, M);
+}
+
 // The same value computed by a group of G lanes (G = 8, 16 or 32, m <= G,
 // the warp split into 32 / G groups that all call this together): lane gl
 // of the group computes LUT entry gl, and the entries are summed in the

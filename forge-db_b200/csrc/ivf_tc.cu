@@ -1254,7 +1254,9 @@ static_assert(EXT_MAX <= (unsigned)EXT_THREADS, "one thread rescores one collect
 // certify_kernel); when d~_32 - E > d~_(k-1) + E none of them can enter the
 // answer or a seed, and their keys stay empty.
 constexpr int RS_QUERIES = CERT_WARPS / 2;  // queries per block
-template <int ORDER, int P>
+// MS selects a compile-time ADC shape (1: m = 16 x 8 floats, 2: m = 48 x 2
+// floats; 0: any shape, loops with run-time bounds).
+template <int ORDER, int P, int MS>
 __global__ void __launch_bounds__(CERT_WARPS * 32, 4) rescore_kernel(CertParams r) {
     __shared__ uint64_t keys[RS_QUERIES][LIST_K];
     __shared__ uint64_t buf[RS_QUERIES * 64];
@@ -1286,8 +1288,12 @@ __global__ void __launch_bounds__(CERT_WARPS * 32, 4) rescore_kernel(CertParams 
                 else hi = mid;
             }
             // one code per lane: 32 independent chains keep many loads in flight
-            const float d = exact_adc<ORDER>(qv, r.cents + (size_t)lo * r.dim, r.cb,
-                                             r.codes + (size_t)pos * m, m, sub);
+            const float* cl = r.cents + (size_t)lo * r.dim;
+            const uint8_t* cd = r.codes + (size_t)pos * m;
+            float d;
+            if constexpr (MS == 1) d = exact_adc_fixed<ORDER, 16, 8>(qv, cl, r.cb, cd);
+            else if constexpr (MS == 2) d = exact_adc_fixed<ORDER, 48, 2>(qv, cl, r.cb, cd);
+            else d = exact_adc<ORDER>(qv, cl, r.cb, cd, m, sub);
             ek = make_key(d, pos);
             el = lo;
         }
@@ -1475,8 +1481,9 @@ struct ExtShared {
     typename ExtScan::TempStorage scan_tmp;
 };
 
-// One extended query (flag slot `slot`), the whole block.
-template <int ORDER, int P>
+// One extended query (flag slot `slot`), the whole block.  MS: a
+// compile-time ADC shape as in rescore_kernel (0: any shape).
+template <int ORDER, int P, int MS>
 __device__ __forceinline__ void extend_slot(const CertParams& r, uint32_t slot, ExtShared& sh) {
     uint64_t* keys = sh.keys;
     unsigned* pstart = sh.pstart;
@@ -1546,8 +1553,21 @@ __device__ __forceinline__ void extend_slot(const CertParams& r, uint32_t slot, 
             }
         }
         const int m = r.m, sub = r.dim / m;
-        const float d = warp_exact_adc<ORDER>(r.Q + (size_t)q * r.dim, r.cents, r.dim, r.cb,
-                                              r.codes, m, sub, pos, lo, valid, sh.dres[t >> 5]);
+        float d;
+        if constexpr (MS != 0) {
+            // one entry per thread, every load of its code in flight together
+            d = 0.0f;
+            if (valid) {
+                const float* qv = r.Q + (size_t)q * r.dim;
+                const float* cl = r.cents + (size_t)lo * r.dim;
+                const uint8_t* cd = r.codes + (size_t)pos * m;
+                if constexpr (MS == 1) d = exact_adc_fixed<ORDER, 16, 8>(qv, cl, r.cb, cd);
+                else d = exact_adc_fixed<ORDER, 48, 2>(qv, cl, r.cb, cd);
+            }
+        } else {
+            d = warp_exact_adc<ORDER>(r.Q + (size_t)q * r.dim, r.cents, r.dim, r.cb, r.codes,
+                                      m, sub, pos, lo, valid, sh.dres[t >> 5]);
+        }
         if (valid) keys[t] = make_key(d, pos);
     }
     __syncthreads();
@@ -1565,13 +1585,13 @@ __device__ __forceinline__ void extend_slot(const CertParams& r, uint32_t slot, 
 
 // A grid of a few blocks per SM walks the extended queries (their count is
 // only known on the device).
-template <int ORDER, int P>
+template <int ORDER, int P, int MS>
 __global__ void __launch_bounds__(EXT_THREADS) extend_kernel(CertParams r) {
     __shared__ ExtShared sh;
     const uint32_t count = *r.ext_count;
     for (uint32_t slot = blockIdx.x; slot < count; slot += gridDim.x) {
         __syncthreads();  // the previous slot's shared state is no longer read
-        extend_slot<ORDER, P>(r, slot, sh);
+        extend_slot<ORDER, P, MS>(r, slot, sh);
     }
 }
 
@@ -2045,13 +2065,23 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     const unsigned cgrid = (unsigned)((nq + CERT_WARPS - 1) / CERT_WARPS);
     const unsigned rgrid = (unsigned)((nq + RS_QUERIES - 1) / RS_QUERIES);
     const bool p2 = k > 32;
+    // compile-time ADC shapes for the common layouts (rows 16-byte aligned)
+    const int sub = (int)(h->dim / h->m);
+    const int ms = (h->m == 16 && sub == 8) ? 1 : (h->m == 48 && sub == 2) ? 2 : 0;
+#define FDB_RESCORE(O, PP, MM) rescore_kernel<O, PP, MM><<<rgrid, CERT_WARPS * 32, 0, s>>>(r)
+#define FDB_RESCORE_MS(O, PP)                  \
+    if (ms == 1) { FDB_RESCORE(O, PP, 1); }    \
+    else if (ms == 2) { FDB_RESCORE(O, PP, 2); } \
+    else { FDB_RESCORE(O, PP, 0); }
     if (order == ORDER_LANE8) {
-        if (p2) rescore_kernel<ORDER_LANE8, 2><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
-        else rescore_kernel<ORDER_LANE8, 1><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+        if (p2) { FDB_RESCORE_MS(ORDER_LANE8, 2) }
+        else { FDB_RESCORE_MS(ORDER_LANE8, 1) }
     } else {
-        if (p2) rescore_kernel<ORDER_FAST4, 2><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
-        else rescore_kernel<ORDER_FAST4, 1><<<rgrid, CERT_WARPS * 32, 0, s>>>(r);
+        if (p2) { FDB_RESCORE_MS(ORDER_FAST4, 2) }
+        else { FDB_RESCORE_MS(ORDER_FAST4, 1) }
     }
+#undef FDB_RESCORE_MS
+#undef FDB_RESCORE
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the answer's k-th distance is at most the smallest exact k-th of any device
@@ -2063,13 +2093,20 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     // extended queries (a block each, in turn); those with too many entries
     // then take the re-scan path
     const unsigned egrid = (unsigned)std::min<size_t>(nq, (size_t)c.sm_count * 8);
+#define FDB_EXTEND(O, PP, MM) extend_kernel<O, PP, MM><<<egrid, EXT_THREADS, 0, s>>>(r)
+#define FDB_EXTEND_MS(O, PP)                   \
+    if (ms == 1) { FDB_EXTEND(O, PP, 1); }     \
+    else if (ms == 2) { FDB_EXTEND(O, PP, 2); } \
+    else { FDB_EXTEND(O, PP, 0); }
     if (order == ORDER_LANE8) {
-        if (p2) extend_kernel<ORDER_LANE8, 2><<<egrid, EXT_THREADS, 0, s>>>(r);
-        else extend_kernel<ORDER_LANE8, 1><<<egrid, EXT_THREADS, 0, s>>>(r);
+        if (p2) { FDB_EXTEND_MS(ORDER_LANE8, 2) }
+        else { FDB_EXTEND_MS(ORDER_LANE8, 1) }
     } else {
-        if (p2) extend_kernel<ORDER_FAST4, 2><<<egrid, EXT_THREADS, 0, s>>>(r);
-        else extend_kernel<ORDER_FAST4, 1><<<egrid, EXT_THREADS, 0, s>>>(r);
+        if (p2) { FDB_EXTEND_MS(ORDER_FAST4, 2) }
+        else { FDB_EXTEND_MS(ORDER_FAST4, 1) }
     }
+#undef FDB_EXTEND_MS
+#undef FDB_EXTEND
     FDB_LAUNCH_CHECK();
     if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 1);
     else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 1);
