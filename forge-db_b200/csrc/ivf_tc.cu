@@ -123,6 +123,12 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
 }
+// min of three floats in one instruction
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -427,11 +433,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                         x[4 * i + 2] = __uint_as_float((uint32_t)x23);
                         x[4 * i + 3] = __uint_as_float((uint32_t)(x23 >> 32));
                     }
+                    // three-input minimums: 32 -> 11 -> 4 -> 1 in 16 instructions
+                    float t[11];
 #pragma unroll
-                    for (int w2 = 16; w2 >= 1; w2 >>= 1)
-#pragma unroll
-                        for (int i = 0; i < w2; ++i) x[i] = fminf(x[i], x[i + w2]);
-                    if (!__any_sync(0xffffffffu, x[0] <= tt)) return;
+                    for (int k = 0; k < 10; ++k) t[k] = min3f(x[3 * k], x[3 * k + 1], x[3 * k + 2]);
+                    t[10] = fminf(x[30], x[31]);
+                    const float mn = fminf(min3f(min3f(t[0], t[1], t[2]), min3f(t[3], t[4], t[5]),
+                                                 min3f(t[6], t[7], t[8])),
+                                           fminf(t[9], t[10]));
+                    if (!__any_sync(0xffffffffu, mn <= tt)) return;
 #pragma unroll
                     for (int g8 = 0; g8 < 4; ++g8) {
                         const float4 c0 = reinterpret_cast<const float4*>(cvs)[2 * g8];
