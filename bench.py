@@ -510,6 +510,10 @@ def run_ours(args, rank, world, local_rank, dist):
     times, scan_ms, bytes_scanned, launches, rescans, extended = [], [], [], 0, [], []
     kern_ms, kern_scores = [], []
     stage = {"coarse_ms": [], "rescore_ms": [], "merge_ms": []}
+    # sharded lists: device time inside each collective (waits for the
+    # slowest rank included)
+    comm_names = ("allgather_probes", "allreduce_tau", "allreduce_dk", "allgather_results")
+    comm = {n: [] for n in comm_names}
     # rounds of the exact re-scan: units (query, failed list) at most nq * nprobe,
     # per-unit keys of the fetched k (k x rerank factor, x4 when filtered with
     # re-ranking) within 64 MiB a round
@@ -536,6 +540,8 @@ def run_ours(args, rank, world, local_rank, dist):
             stage["coarse_ms"].append(st.coarse_ms)
             stage["rescore_ms"].append(st.rescore_ms)
             stage["merge_ms"].append(st.merge_ms)
+            for i, n in enumerate(comm_names):
+                comm[n].append(st.comm_ms[i])
             rescans.append(st.exact_rescans)
             extended.append(st.extended)
             bytes_scanned.append(st.bytes_scanned)
@@ -630,9 +636,13 @@ def run_ours(args, rank, world, local_rank, dist):
         "details": {
             "recall_at_10": recall, "recall_queries": nr, "build_s": round(build_s, 2),
             "stage_ms": {k: round(statistics.mean(v), 4) for k, v in stage.items()},
+            "pass2_kernel_ms": round(statistics.mean(kern_ms), 4),
+            "collective_ms": ({k: round(statistics.mean(v), 4) for k, v in comm.items()}
+                              if args.mode == "lists" and world > 1 else None),
             "scan_kernel_ms": round(statistics.mean(scan_ms), 4),
             "exact_rescans_per_step": statistics.mean(rescans),
             "extended_certificates_per_step": statistics.mean(extended),
+            "pass1_quota": ix.pass1_quota(args.nprobe) if tensor_mode else None,
             "index_crc32": index_checksum(*exported)},
         "e2e": {"value": e2e_value, "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4,

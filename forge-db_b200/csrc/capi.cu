@@ -608,6 +608,31 @@ int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode) {
     });
 }
 
+int fdb_ivfpq_set_pass1_quota(fdb_ivfpq* h, size_t nprobe, uint64_t div) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        const size_t take = std::max<size_t>(1, std::min(nprobe, h->nlist));
+        for (auto& e : h->tc_quota)
+            if (e.first == take) {
+                e.second = div;
+                return;
+            }
+        h->tc_quota.emplace_back(take, div);
+    });
+}
+
+int fdb_ivfpq_get_pass1_quota(fdb_ivfpq* h, size_t nprobe, int64_t* div) {
+    return guarded([&] {
+        FDB_REQUIRE(h && div, FDB_ERR_INVALID_ARG, "NULL argument");
+        std::lock_guard<std::mutex> lk(h->mu);
+        const size_t take = std::max<size_t>(1, std::min(nprobe, h->nlist));
+        *div = -1;
+        for (const auto& e : h->tc_quota)
+            if (e.first == take) *div = (int64_t)e.second;
+    });
+}
+
 int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable) {
     return guarded([&] {
         FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");

@@ -305,7 +305,10 @@ __global__ void __launch_bounds__(THREADS, 2)
 // centroid rows in global memory, in the order of l2sq_exact, the NC rows
 // interleaved for memory-level parallelism; 128-bit loads when the rows are
 // 16-byte aligned.
-template <int NC>
+// DIM > 0: a compile-time length (a multiple of 8, the rows 16-byte
+// aligned), every loop unrolled so that all loads of a row are in flight
+// together; DIM == 0: the run-time length dim.
+template <int NC, int DIM = 0>
 __device__ __forceinline__ void l2sq_rows(const float* __restrict__ qs,
                                           const float* const (&c)[NC], int dim, bool vec,
                                           float (&out)[NC]) {
@@ -314,6 +317,29 @@ __device__ __forceinline__ void l2sq_rows(const float* __restrict__ qs,
     for (int r = 0; r < NC; ++r)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[r][j] = 0.0f;
+    if constexpr (DIM > 0) {
+        static_assert(DIM % 8 == 0, "whole lane groups");
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+#pragma unroll
+        for (int i = 0; i < DIM; i += 8) {
+            const float4 qa = q4[i >> 2], qb = q4[(i >> 2) + 1];
+            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int r = 0; r < NC; ++r) {
+                const float4* c4 = reinterpret_cast<const float4*>(c[r]);
+                const float4 u = __ldg(c4 + (i >> 2)), w = __ldg(c4 + (i >> 2) + 1);
+                const float cv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float d = __fsub_rn(qv[j], cv[j]);
+                    acc[r][j] = __fmaf_rn(d, d, acc[r][j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NC; ++r) out[r] = lane_sum(acc[r]);
+        return;
+    }
     const int full = dim & ~7;
     if (vec) {
         const float4* q4 = reinterpret_cast<const float4*>(qs);
@@ -383,7 +409,7 @@ __device__ __forceinline__ void warp_sort64(uint64_t& a, uint64_t& b, int lane) 
 // t comes from a 256-bin histogram of the row's distance bits between the
 // row's minimum and maximum (from the GEMM): the upper edge of the first bin
 // where the running count reaches `take`, rounded up.
-template <int R, int P>
+template <int R, int P, int DIM>
 __global__ void __launch_bounds__(REF_WARPS * 32, 3)
     coarse_refine_kernel(const float* __restrict__ D, int ldd, int nq, int nlist, int take,
                          const float* __restrict__ Q, int dim, const float* __restrict__ cents,
@@ -490,14 +516,14 @@ __global__ void __launch_bounds__(REF_WARPS * 32, 3)
         if (nc <= 32) {
             const float* rows[1] = {cents + (size_t)l0 * dim};
             float d[1];
-            l2sq_rows<1>(qs, rows, dim, vec, d);
+            l2sq_rows<1, DIM>(qs, rows, dim, vec, d);
             if (lane < n0) ka = make_key(d[0], l0);
         } else {
             const bool has1 = lane + 32 < nc;
             const uint32_t l1 = cb[has1 ? lane + 32 : 0];
             const float* rows[2] = {cents + (size_t)l0 * dim, cents + (size_t)l1 * dim};
             float d[2];
-            l2sq_rows<2>(qs, rows, dim, vec, d);
+            l2sq_rows<2, DIM>(qs, rows, dim, vec, d);
             ka = make_key(d[0], l0);
             if (has1) kb = make_key(d[1], l1);
         }
@@ -519,7 +545,7 @@ __global__ void __launch_bounds__(REF_WARPS * 32, 3)
         const uint32_t l = has ? (list ? list[b0 + lane] : (uint32_t)(b0 + lane)) : 0u;
         const float* rows[1] = {cents + (size_t)l * dim};
         float d[1];
-        l2sq_rows<1>(qs, rows, dim, vec, d);
+        l2sq_rows<1, DIM>(qs, rows, dim, vec, d);
         tk.add(has ? make_key(d[0], l) : KEY_NONE, has);
     };
     if (nc <= CAND_CAP) {
@@ -663,7 +689,13 @@ void coarse_tc(fdb_ivfpq* h, const float* dQ, size_t nq, size_t take, uint32_t* 
         uint32_t* pr = probes + q0 * take;
         float* pd = pdist ? pdist + q0 * take : nullptr;
 #define FDB_REFINE(RR, PP)                                                                   \
-    coarse_refine_kernel<RR, PP><<<rgrid, REF_WARPS * 32, 0, s>>>(                           \
+    do {                                                                                     \
+        if (h->dim == 128) FDB_REFINE_D(RR, PP, 128);                                        \
+        else if (h->dim == 96) FDB_REFINE_D(RR, PP, 96);                                     \
+        else FDB_REFINE_D(RR, PP, 0);                                                        \
+    } while (0)
+#define FDB_REFINE_D(RR, PP, DD)                                                             \
+    coarse_refine_kernel<RR, PP, DD><<<rgrid, REF_WARPS * 32, 0, s>>>(                       \
         h->s_cdapprox.p, npad, (int)nc, (int)h->nlist, (int)take, Qc, (int)h->dim, h->cents.p, \
         h->s_cqerr.p, p.rmin, p.rmax, pr, pd)
 #define FDB_REFINE_P(RR)                  \
@@ -678,6 +710,7 @@ void coarse_tc(fdb_ivfpq* h, const float* dQ, size_t nq, size_t take, uint32_t* 
         else { FDB_REFINE_P(64); }
 #undef FDB_REFINE_P
 #undef FDB_REFINE
+#undef FDB_REFINE_D
         FDB_LAUNCH_CHECK();
     }
 }

@@ -390,7 +390,9 @@ static void exchange_and_merge(Ctx& c, size_t nq, int k, const uint64_t* local_k
     uint64_t* send = gather.p + per * 2 * (size_t)c.world;
     FDB_CUDA(cudaMemcpyAsync(send, local_keys, per * 8, cudaMemcpyDeviceToDevice, s));
     FDB_CUDA(cudaMemcpyAsync(send + per, local_ids, per * 8, cudaMemcpyDeviceToDevice, s));
+    comm_mark(c, COMM_RESULTS);
     FDB_NCCL_C(ncclAllGather(send, gather.p, per * 2, ncclUint64, c.comm, s), c.comm);
+    comm_mark(c, COMM_RESULTS);
     merged.ensure(per);
     merged_ids.ensure(per);
     launch_merge_lists(s, gather.p, c.world, per * 2, nq, k, merged.p);
@@ -459,12 +461,14 @@ SearchRun ivfpq_enqueue(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, 
         }
         if (world > 1) {
             const size_t cnt = slice * take;
+            comm_mark(c, COMM_PROBES);
             FDB_NCCL_C(ncclGroupStart(), c.comm);
             FDB_NCCL_C(ncclAllGather(h->s_probe.p + cnt * rank, h->s_probe.p, cnt, ncclUint32,
                                    c.comm, s), c.comm);
             FDB_NCCL_C(ncclAllGather(h->s_pdist.p + cnt * rank, h->s_pdist.p, cnt, ncclFloat,
                                    c.comm, s), c.comm);
             FDB_NCCL_C(ncclGroupEnd(), c.comm);
+            comm_mark(c, COMM_PROBES);
         }
         tm.mark();
         h->s_stat.ensure(4);
@@ -596,6 +600,54 @@ SearchRun ivfpq_enqueue(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, 
     return r;
 }
 
+// The pass-1 sampling quota for `take` probes on the tensor path: the one
+// set or calibrated for this nprobe, else calibrated now on the first ns
+// queries of this batch (up to 16384: the item structure of a small sample
+// differs from a full batch's) -- each candidate quota runs the whole search
+// on that sample twice (the first sizes the scratch) and the fastest second
+// run (device time) wins.  The quota changes only how the work is split between
+// the two list-scan passes; every quota returns the same (exact) answer.
+uint64_t pass1_quota(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, size_t k,
+                     int order, size_t take, const uint32_t* skip) {
+    for (const auto& e : h->tc_quota)
+        if (e.first == take) return e.second;
+    constexpr uint64_t kDefault = 64;
+    if (h->sharded || nq < 1024) return kDefault;  // ranks must agree; too small to time
+    cudaStream_t s = h->ctx->c.stream;
+    const size_t ns = std::min<size_t>(nq, 16384);
+    h->s_cal_ids.ensure(ns * k_out);
+    h->s_cal_d.ensure(ns * k_out);
+    h->s_cal_c.ensure(ns);
+    cudaEvent_t e0, e1;
+    FDB_CUDA(cudaEventCreate(&e0));
+    FDB_CUDA(cudaEventCreate(&e1));
+    struct Ev {
+        cudaEvent_t a, b;
+        ~Ev() { cudaEventDestroy(a); cudaEventDestroy(b); }
+    } ev{e0, e1};
+    uint64_t best = kDefault;
+    float best_ms = 0.0f;
+    for (const uint64_t div : {128ull, 64ull, 16ull, 4ull, 0ull}) {
+        h->tc_sample_div = div;
+        float ms = 0.0f;
+        for (int rep = 0; rep < 2; ++rep) {
+            StageTimer off0(s, false), off1(s, false);
+            FDB_CUDA(cudaEventRecord(e0, s));
+            ivfpq_enqueue(h, dQ, ns, k_out, k, order, take, h->s_cal_ids.p, h->s_cal_d.p,
+                          h->s_cal_c.p, nullptr, nullptr, skip, nullptr, off0, off1);
+            FDB_CUDA(cudaEventRecord(e1, s));
+            FDB_CUDA(cudaEventSynchronize(e1));
+            FDB_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+        }
+        if (best_ms == 0.0f || ms < best_ms) {
+            best_ms = ms;
+            best = div;
+        }
+    }
+    h->tc_quota.emplace_back(take, best);
+    return best;
+}
+
 // The search key of a captured graph: every value the enqueued work bakes
 // into its launches (pointers, sizes, modes) besides the scratch buffers,
 // whose addresses stay put while the allocation epoch is unchanged.
@@ -622,6 +674,7 @@ GraphKey search_key(const fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out
     g[15] = ((uint64_t)h->scan_mode << 32) | (uint64_t)h->rerank;
     g[16] = h->rerank_factor;
     g[17] = 1;  // a valid key
+    g[18] = h->tc_sample_div;
     return g;
 }
 
@@ -645,8 +698,16 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
     FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
                 "sharded index needs a communicator of the same size");
     if (k == 0) return;
+    // the tensor path's pass-1 quota for this nprobe (calibrated on first use)
+    const bool tensor_path = ivf_tc_eligible(h, k) &&
+                             (h->scan_mode == FDB_SCAN_TENSOR ||
+                              (h->scan_mode == FDB_SCAN_AUTO && nq >= 256));
+    if (tensor_path && take > 0)
+        h->tc_sample_div = call_skip ? 64 : pass1_quota(h, dQ, nq, k_out, k, order, take, skip);
     StageTimer tm(s, st != nullptr);
     StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
+    StageTimer comm_tm(s, st != nullptr && h->sharded);  // around each collective
+    CommTimerScope comm_scope(c, comm_tm);
     uint64_t* pin = h->s_pin.get();
     for (int i = 0; i < 6; ++i) pin[i] = 0;
     // A search of one device whose work has no host synchronisation (it has
@@ -731,6 +792,7 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
             st->kernel_ms = pass_ms;
             st->exact_rescans = (uint32_t)hs[5];
         }
+        comm_scope.read(st);
         st->lists_probed = hs[0];
         st->extended = hs[3];
         st->codes_scanned = hs[1];
@@ -861,6 +923,8 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
     FDB_REQUIRE(!h->sharded || (c.comm && c.world == h->shard_world), FDB_ERR_INVALID_ARG,
                 "sharded index needs a communicator of the same size");
     StageTimer tm(s, st != nullptr);
+    StageTimer comm_tm(s, st != nullptr && h->sharded);  // around the exchange
+    CommTimerScope comm_scope(c, comm_tm);
     tm.mark();
     if (k == 0) return;
     const size_t per = nq * k;
@@ -961,6 +1025,7 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
             st->merge_ms = tm.ms(2, 3);
             st->total_ms = tm.ms(0, 3);
         }
+        comm_scope.read(st);
     }
 }
 

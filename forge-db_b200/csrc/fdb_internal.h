@@ -112,6 +112,7 @@ struct DevBuf {
 // ---------------------------------------------------------------------------
 // context: one device, one stream, optional communicator
 // ---------------------------------------------------------------------------
+struct StageTimer;
 struct Ctx {
     int device = 0;
     int sm_count = 0;
@@ -126,7 +127,13 @@ struct Ctx {
     std::atomic<unsigned long long> wait_cycles{4000000000ull};
     std::atomic<double> wait_s{2.0};
     std::atomic<int> test_stalls{0};  // test hook: list-scan launches left to stall
+    // A timed call on a sharded index: event marks before and after each
+    // collective (comm_ids: which one, FDB_COMM_*), read into fdb_stats.comm_ms.
+    StageTimer* comm_tm = nullptr;
+    std::vector<int> comm_ids;
 };
+// the collectives of a sharded search, in fdb_stats.comm_ms order
+constexpr int COMM_PROBES = 0, COMM_TAU = 1, COMM_DK = 2, COMM_RESULTS = 3;
 
 // The wait limit in force for a call (call_cycles: the call's own limit, 0 =
 // none), in SM clock cycles.
@@ -239,6 +246,31 @@ struct StageTimer {
     }
 };
 
+// A mark before (and, called again, after) collective `id` of a timed call.
+inline void comm_mark(Ctx& c, int id) {
+    if (!c.comm_tm) return;
+    c.comm_tm->mark();
+    c.comm_ids.push_back(id);
+}
+
+// Times the collectives of one call on a sharded index (timer on) and
+// detaches the timer from the context when the call ends.
+struct CommTimerScope {
+    Ctx& c;
+    StageTimer& tm;
+    CommTimerScope(Ctx& c_, StageTimer& tm_) : c(c_), tm(tm_) {
+        c.comm_ids.clear();
+        c.comm_tm = tm.on ? &tm : nullptr;
+    }
+    ~CommTimerScope() { c.comm_tm = nullptr; }
+    // after the stream is synchronised
+    void read(fdb_stats* st) const {
+        if (!c.comm_tm) return;
+        for (size_t i = 0; i + 1 < c.comm_ids.size(); i += 2)
+            st->comm_ms[c.comm_ids[i]] += tm.ms(i, i + 1);
+    }
+};
+
 // ---------------------------------------------------------------------------
 // seeded draws (host): deterministic across processes and devices
 // ---------------------------------------------------------------------------
@@ -328,7 +360,7 @@ void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, i
 // A captured search (see ivfpq_search_dev): the key of the call it replays,
 // the allocation epoch its buffer addresses belong to, and its timing events.
 namespace fdb {
-using GraphKey = std::array<uint64_t, 18>;
+using GraphKey = std::array<uint64_t, 19>;
 struct GraphSlot {
     GraphKey key{};
     uint64_t epoch = 0;
@@ -519,6 +551,10 @@ struct fdb_ivfpq {
     size_t tc_rows = 0;                 // rows of the padded layout
     size_t tc_maxpad = 0;               // longest padded list
     float tc_colmax = 0.0f;             // upper bound of ||rhat||^2
+    // pass-1 sampling quota: 1/div of a query's probed codes (0: every probe's
+    // first tile); chosen per nprobe by timing a sample batch (calibrated)
+    uint64_t tc_sample_div = 64;
+    std::vector<std::pair<size_t, uint64_t>> tc_quota;  // (nprobe, div) calibrated
     // Vector ids the reference keeps on centroids and codebook entries; no
     // role in search, carried so .fdb files round-trip unchanged
     std::vector<uint64_t> cent_ids;     // [nlist]
@@ -561,6 +597,9 @@ struct fdb_ivfpq {
     fdb::DevBuf<uint64_t> s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids, s_approx;
     fdb::DevBuf<float> s_dists;
     fdb::DevBuf<uint32_t> s_counts, s_flags;
+    fdb::DevBuf<uint64_t> s_cal_ids;    // pass-1 quota calibration outputs
+    fdb::DevBuf<float> s_cal_d;
+    fdb::DevBuf<uint32_t> s_cal_c;
     fdb::DevBuf<unsigned long long> s_stat;
     fdb::PinnedWords s_pin;  // end-of-call readbacks (statistics, error word, counts)
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
@@ -615,4 +654,7 @@ struct fdb_bf {
     fdb::DevBuf<uint64_t> s_part, s_keys, s_ids, s_gather, s_merged, s_merged_ids, s_out_ids;
     fdb::DevBuf<float> s_dists;
     fdb::DevBuf<uint32_t> s_counts, s_flags;
+    fdb::DevBuf<uint64_t> s_cal_ids;    // pass-1 quota calibration outputs
+    fdb::DevBuf<float> s_cal_d;
+    fdb::DevBuf<uint32_t> s_cal_c;
 };

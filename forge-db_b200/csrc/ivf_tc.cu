@@ -62,11 +62,7 @@ constexpr int CV_FLOATS = TILE_N;  // ||rhat||^2 values per B tile
 #define FDB_IVF_SPIN_WAITS 1
 #endif
 constexpr int CHUNK_TILES = FDB_IVF_CHUNK_TILES;  // B tiles per item at most (long lists are split)
-#ifndef FDB_IVF_SAMPLE_DIV
-#define FDB_IVF_SAMPLE_DIV 64
-#endif
-// pass 1 samples at least 1/SAMPLE_DIV of each query's probed codes
-constexpr uint64_t SAMPLE_DIV = FDB_IVF_SAMPLE_DIV;
+
 constexpr float INF = __builtin_huge_valf();
 
 struct Item {
@@ -416,11 +412,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     rok ? (tau - rn) + ldexpf(2.0f * fabsf(rn) + 2.0f * p.colmax + fabsf(tau), -20)
                         : -INF;
                 const uint64_t s22 = pack2(__float_as_uint(s2), __float_as_uint(s2));
-                auto score = [&](const uint32_t(&v)[32], const float* cvs, int cidx) {
-                    const int nvalid = min(32, (int)it.nb - cidx);
-                    const uint32_t tag0 = it.tag0 + (uint32_t)cidx;
-                    // The chunk's smallest test value, by a tree of minimums (short
-                    // dependency chains); one vote decides whether any lane has a hit.
+                // The test of a 32-column chunk: bit g is set when some row of the
+                // warp may admit a code among the chunk's columns 8g..8g+7.  Each
+                // group's smallest test value comes from a short tree of minimums;
+                // one vote skips the chunk when no lane can have a hit.
+                auto test = [&](const uint32_t(&v)[32], const float* cvs) -> unsigned {
                     float x[32];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -433,38 +429,53 @@ __global__ void __launch_bounds__(THREADS, 1)
                         x[4 * i + 2] = __uint_as_float((uint32_t)x23);
                         x[4 * i + 3] = __uint_as_float((uint32_t)(x23 >> 32));
                     }
-                    // three-input minimums: 32 -> 11 -> 4 -> 1 in 16 instructions
-                    float t[11];
-#pragma unroll
-                    for (int k = 0; k < 10; ++k) t[k] = min3f(x[3 * k], x[3 * k + 1], x[3 * k + 2]);
-                    t[10] = fminf(x[30], x[31]);
-                    const float mn = fminf(min3f(min3f(t[0], t[1], t[2]), min3f(t[3], t[4], t[5]),
-                                                 min3f(t[6], t[7], t[8])),
-                                           fminf(t[9], t[10]));
-                    if (!__any_sync(0xffffffffu, mn <= tt)) return;
+                    float m[4];
 #pragma unroll
                     for (int g8 = 0; g8 < 4; ++g8) {
-                        const float4 c0 = reinterpret_cast<const float4*>(cvs)[2 * g8];
-                        const float4 c1 = reinterpret_cast<const float4*>(cvs)[2 * g8 + 1];
-                        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                        bool any = false;
+                        const float* y = x + 8 * g8;
+                        m[g8] = min3f(min3f(y[0], y[1], y[2]), min3f(y[3], y[4], y[5]),
+                                      fminf(y[6], y[7]));
+                    }
+                    const float mn = fminf(fminf(m[0], m[1]), fminf(m[2], m[3]));
+                    if (!__any_sync(0xffffffffu, mn <= tt)) return 0u;
+                    unsigned gm = 0;
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8)
+                        gm |= __any_sync(0xffffffffu, m[g8] <= tt) ? 1u << g8 : 0u;
+                    return gm;
+                };
+                // The groups of gm (bits 0-3: this warp's first 32 columns of the
+                // tile, 4-7: the next 32) reloaded from the accumulator, which is
+                // still held: every code with d~ <= tau (+inf: a tombstoned row,
+                // never admitted) is appended to its query's candidates.  One copy
+                // of this code serves both chunks, which keeps the loop small.
+                auto admit = [&](unsigned gm, uint32_t tcol, const float* cvs, int cbase) {
+                    const uint32_t tag = it.tag0 + (uint32_t)cbase;
+                    const int nvalid = (int)it.nb - cbase;
+                    uint64_t* crow = p.cand + (size_t)q * p.cap;
+                    while (gm) {
+                        const int gi = __ffs(gm) - 1;
+                        gm &= gm - 1;
+                        uint32_t w[8];
+                        tmem_ld8(tmem + lane_base + tcol + (uint32_t)(gi * 8), w);
+                        // the row's hits in the group, reserved with one atomic
+                        float d[8];
+                        unsigned hm = 0;
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int j = gi * 8 + jj;
+                            d[jj] = __fmaf_rn(s2, __uint_as_float(w[jj]), __fadd_rn(rn, cvs[j]));
+                            if (rok && j < nvalid && d[jj] <= tau && d[jj] < INF) hm |= 1u << jj;
+                        }
+                        if (hm == 0) continue;
+                        unsigned ix = atomicAdd(p.cand_cnt + q, (unsigned)__popc(hm));
 #pragma unroll
                         for (int jj = 0; jj < 8; ++jj)
-                            any |= __fmaf_rn(s2, __uint_as_float(v[g8 * 8 + jj]), cv[jj]) <= tt;
-                        if (__any_sync(0xffffffffu, any)) {
-#pragma unroll
-                            for (int jj = 0; jj < 8; ++jj) {
-                                const int j = g8 * 8 + jj;
-                                const float d =
-                                    __fmaf_rn(s2, __uint_as_float(v[j]), __fadd_rn(rn, cv[jj]));
-                                // (+inf: a tombstoned row, never admitted)
-                                if (rok && j < nvalid && d <= tau && d < INF) {
-                                    const unsigned ix = atomicAdd(p.cand_cnt + q, 1u);
-                                    if (ix < (unsigned)p.cap)
-                                        p.cand[(size_t)q * p.cap + ix] = make_key(d, tag0 + j);
-                                }
+                            if (hm >> jj & 1u) {
+                                if (ix < (unsigned)p.cap)
+                                    crow[ix] = make_key(d[jj], tag + (uint32_t)(gi * 8 + jj));
+                                ++ix;
                             }
-                        }
                     }
                 };
                 if (nt > 0) {
@@ -474,18 +485,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int t = 0; alive && t < nt; ++t, ++g) {
                     const int b = g % NACC, c = g % NCV;
                     const float* cvs = cvbuf + c * CV_FLOATS + half * 64;
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32), vb);
-                    score(va, cvs, t * TILE_N + half * 64);
+                    const uint32_t tcol = (uint32_t)(b * TILE_N + half * 64);
+                    tmem_ld32_nowait(tmem + lane_base + tcol + 32u, vb);
+                    unsigned gm = test(va, cvs);
                     tmem_wait_regs(vb);
-                    // both chunks of this tile are in registers: free the accumulator
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(t_empty + b);
+                    // the next tile's first chunk loads while this one is tested
                     const bool more = t + 1 < nt;
                     if (more && !begin_tile(g + 1)) alive = false;
-                    score(vb, cvs + 32, t * TILE_N + half * 64 + 32);
+                    gm |= test(vb, cvs + 32) << 4;
+                    if (gm) admit(gm, tcol, cvs, t * TILE_N + half * 64);
+                    // done with the accumulator and the staged norms
+                    tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(cv_empty + c);
+                    if (lane == 0) {
+                        mbar_arrive(t_empty + b);
+                        mbar_arrive(cv_empty + c);
+                    }
                     if (more && alive) tmem_wait_regs(va);
                 }
             } else {
@@ -581,12 +596,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 // one), nlist + list for the query's other probes, 2 nlist for lists that are
 // empty or held by another device.  When stat is
 // given, also counts the lists and codes scanned, and the codes of pass 2.
+// sample_div: pass 1 samples the nearest other probes' first tiles until it
+// has seen 1/sample_div of the query's probed codes (0: every probe's first
+// tile).
 __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, int take,
                                  const uint64_t* __restrict__ lbeg,
                                  const uint64_t* __restrict__ lend,
                                  const uint64_t* __restrict__ offs_full, int nlist,
-                                 uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
-                                 unsigned long long* stat) {
+                                 uint64_t sample_div, uint32_t* __restrict__ keys,
+                                 uint32_t* __restrict__ vals, unsigned long long* stat) {
     // one warp per query, lanes over its probes (32 at a time, in order)
     const int q = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
@@ -616,8 +634,8 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
     if (p1 < 0) p1 = pf;
     // pass 1 scores the pass-1 list and the first tiles of the nearest other
     // probes (probes are in ascending coarse distance) until it has seen
-    // 1/SAMPLE_DIV of the query's codes (the admission threshold is the 64th
-    // of what it saw, so pass 2 admits about 64 * SAMPLE_DIV codes); the
+    // 1/sample_div of the query's codes (the admission threshold is the 64th
+    // of what it saw, so pass 2 admits about 64 * sample_div codes); the
     // other probes' lists are left to pass 2 whole
     uint64_t seen = p1 >= 0 ? lend[pq[p1]] - lbeg[pq[p1]] : 0;
     unsigned long long lists = 0, codes = 0;
@@ -641,7 +659,7 @@ __global__ void pair_keys_kernel(const uint32_t* __restrict__ probes, int nq, in
         const uint64_t before = seen + incl - c;
         // (sampling stops at the first probe that finds the quota met, so a
         // probe is sampled exactly when the quota was not met before it)
-        const bool smp = other && before * SAMPLE_DIV < total;
+        const bool smp = other && (sample_div == 0 || before * sample_div < total);
         if (j < take) {
             uint32_t key;
             if (len == 0) key = 3u * (uint32_t)nlist;
@@ -1852,8 +1870,8 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     h->t_vals.ensure(2 * np);
     h->t_off.ensure((size_t)nkeys + 1);
     pair_keys_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, s>>>(
-        probes, (int)nq, (int)take, lbeg, lend, h->offs.p, nlist, h->t_keys.p, h->t_vals.p,
-        stat);
+        probes, (int)nq, (int)take, lbeg, lend, h->offs.p, nlist, h->tc_sample_div,
+        h->t_keys.p, h->t_vals.p, stat);
     FDB_LAUNCH_CHECK();
     h->t_plen.ensure(np + 1);
     h->t_seg.ensure(np + 1);
@@ -1960,7 +1978,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
+        comm_mark(c, COMM_TAU);
         FDB_NCCL_C(ncclAllReduce(h->t_tau.p, h->t_tau.p, nq, ncclFloat, ncclMin, c.comm, s), c.comm);
+        comm_mark(c, COMM_TAU);
     }
     // --- pass 2: the other lists against tau + the certification margin ---
     h->t_tadm.ensure(nq);
@@ -2095,7 +2115,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the answer's k-th distance is at most the smallest exact k-th of any device
+        comm_mark(c, COMM_DK);
         FDB_NCCL_C(ncclAllReduce(h->t_dk.p, h->t_dk.p, nq, ncclFloat, ncclMin, c.comm, s), c.comm);
+        comm_mark(c, COMM_DK);
     }
     if (p2) certify_kernel<2><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);
     else certify_kernel<1><<<cgrid, CERT_WARPS * 32, 0, s>>>(r, 0);

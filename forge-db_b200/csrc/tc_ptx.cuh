@@ -180,6 +180,17 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[3
           "=r"(v[31])
         : "r"(taddr));
 }
+// Eight consecutive 32-bit columns of the warp's TMEM lane quadrant, waited
+// for (the wait also covers every earlier tcgen05.ld of the thread).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7])
+        : "r"(taddr)
+        : "memory");
+}
 // Wait for this thread's outstanding tcgen05.ld and tie the wait to the
 // destination registers, so no use of them can be scheduled before it.
 __device__ __forceinline__ void tmem_wait_regs(uint32_t (&v)[32]) {

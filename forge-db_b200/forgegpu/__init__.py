@@ -63,7 +63,7 @@ class Stats(C.Structure):
                 ("scan_ms", C.c_double), ("rescore_ms", C.c_double), ("merge_ms", C.c_double),
                 ("total_ms", C.c_double), ("exact_rescans", C.c_uint64),
                 ("kernel_ms", C.c_double), ("kernel_scores", C.c_uint64),
-                ("extended", C.c_uint64)]
+                ("extended", C.c_uint64), ("comm_ms", C.c_double * 4)]
 
 
 class FileInfo(C.Structure):
@@ -125,6 +125,8 @@ _SIGS = {
     "fdb_ivfpq_set_nprobe": (C.c_int, [_vp, _sz]),
     "fdb_ivfpq_set_scan_mode": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_set_graphs": (C.c_int, [_vp, C.c_int]),
+    "fdb_ivfpq_set_pass1_quota": (C.c_int, [_vp, _sz, C.c_uint64]),
+    "fdb_ivfpq_get_pass1_quota": (C.c_int, [_vp, _sz, C.POINTER(C.c_int64)]),
     "fdb_ivfpq_nprobe": (_sz, [_vp]),
     "fdb_ivfpq_len": (_sz, [_vp]),
     "fdb_ivfpq_n_partitions": (_sz, [_vp]),
@@ -501,6 +503,18 @@ class IVFPQIndex:
 
     def set_scan_mode(self, mode: int):
         _check(lib().fdb_ivfpq_set_scan_mode(self.h, mode))
+
+    def set_pass1_quota(self, nprobe: int, div: int):
+        """The tensor path's pass-1 sampling quota (1/div of the probed codes,
+        0: every probe's first tile) for batches with `nprobe` probes."""
+        _check(lib().fdb_ivfpq_set_pass1_quota(self.h, int(nprobe), int(div)))
+
+    def pass1_quota(self, nprobe: int):
+        """The pass-1 quota in use for `nprobe` probes, None before the first
+        large tensor-path batch calibrates it."""
+        v = C.c_int64()
+        _check(lib().fdb_ivfpq_get_pass1_quota(self.h, int(nprobe), C.byref(v)))
+        return None if v.value < 0 else v.value
 
     def set_graphs(self, enable: bool):
         """Replay repeated same-shape batch searches as CUDA graphs."""

@@ -86,6 +86,12 @@ typedef struct fdb_stats {
     uint64_t kernel_scores;  /* (query, code/row) scores that kernel computed */
     uint64_t extended;       /* tensor mode: queries certified by rescoring every stored
                                 candidate below a widened threshold instead of a re-scan */
+    double comm_ms[4];       /* sharded index: device time inside each collective, its wait
+                                for the slowest device included: [0] all-gather of the
+                                probes, [1] all-reduce of the pass-1 thresholds, [2]
+                                all-reduce of the exact k-th distances, [3] all-gather of
+                                the local top-k lists (within coarse_ms, scan_ms, scan_ms
+                                and merge_ms) */
 } fdb_stats;
 
 /* IVF-PQ scan modes (fdb_ivfpq_set_scan_mode).  All return the reference's
@@ -267,6 +273,17 @@ int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode);
  * instead of launching ~40 kernels (default: on).  No reference counterpart
  * (a launch-overhead choice of this engine); results are identical. */
 int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable);
+/* The tensor path's pass-1 sampling quota for batch searches with `nprobe`
+ * probes: pass 1 scores each query's first list plus the first tile of its
+ * nearest other probes until it has seen 1/div of the query's probed codes
+ * (div 0: every probe's first tile).  Unset, it is calibrated on the first
+ * batch of 1024+ queries with that nprobe (up to 16384 of its queries timed under
+ * div 128, 64, 16, 4, 0; the fastest is kept).  It splits the work between
+ * the two passes only: results are identical for every div.  No reference
+ * counterpart. */
+int fdb_ivfpq_set_pass1_quota(fdb_ivfpq* h, size_t nprobe, uint64_t div);
+/* The quota in use for `nprobe` probes (set or calibrated), -1 if none yet. */
+int fdb_ivfpq_get_pass1_quota(fdb_ivfpq* h, size_t nprobe, int64_t* div);
 /* set_nprobe (ivf_pq.rs:524-528): stores min(nprobe, nlist). */
 int fdb_ivfpq_set_nprobe(fdb_ivfpq* h, size_t nprobe);
 size_t fdb_ivfpq_nprobe(const fdb_ivfpq* h);

@@ -159,3 +159,37 @@ def test_tensor_coarse_quantizer_probes_match_oracle(fg, ctx, orc, dim, nlist, n
 def _oracle(orc, ix):
     cents, cb, offs, ids, codes = ix.export()
     return orc.OracleIVFPQ(cents, cb, offs, ids, codes)
+
+
+@pytest.mark.parametrize("div", [0, 4, 64, 128])
+def test_pass1_quota_does_not_change_the_answer(fg, orc, long_lists, div):
+    """Every pass-1 sampling quota (every probe's first tile, 1/4 .. 1/128 of
+    the probed codes) returns the oracle's answer; it only moves work between
+    the two list-scan passes."""
+    ix, ox, X, Q, _, _ = long_lists
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    ix.set_nprobe(32)
+    ox.set_nprobe(32)
+    ix.set_pass1_quota(32, div)
+    ids, d, cnt = ix.batch_search_arrays(Q, 10)
+    oi, od, oc = ox.batch_search(Q, 10)
+    assert_topk_match(ids, d, cnt, oi, od, oc, f"pass-1 quota 1/{div}")
+    ix.set_scan_mode(0)
+
+
+def test_pass1_quota_calibrates_on_a_large_batch(fg, ctx, orc):
+    """A first batch of 1024+ queries calibrates the quota (timing a sample
+    under several quotas) and still returns the oracle's answer."""
+    from forgegpu.datasets import gmm_descriptors
+    X = gmm_descriptors(60000, components=64, seed=61)
+    Q = gmm_descriptors(1500, components=64, seed=62)
+    ix = fg.IVFPQIndex.build(X, 64, 16, ctx=ctx, seed=11)
+    ix.set_nprobe(16)
+    ox = _oracle(orc, ix)
+    ox.set_nprobe(16)
+    assert ix.pass1_quota(16) is None
+    for _ in range(2):
+        ids, d, cnt = ix.batch_search_arrays(Q, 10)
+        oi, od, oc = ox.batch_search(Q, 10)
+        assert_topk_match(ids, d, cnt, oi, od, oc, "calibrated quota")
+    assert ix.pass1_quota(16) in (0, 4, 16, 64, 128)
