@@ -237,6 +237,8 @@ def config_dict(args, world, extra=None):
          "parallelism": (f"lists{world}" if args.mode == "lists" else f"replicas{world}"),
          "scan_mode": args.scan_mode,
          "l2": "flushed between steps (256 MB write outside the timed window)"}
+    if getattr(args, "ivf_sample", 0):
+        d["ivf_sample"] = args.ivf_sample
     if getattr(args, "rerank", 0):
         d["rerank_factor"] = args.rerank
     if getattr(args, "filter_every", 0):
@@ -269,7 +271,8 @@ def run_reference(args, rank, world):
     n = X.shape[0]
     threads = O.host_threads()
     t0 = time.time()
-    sidx, init, kpp_u, pidx, pinit = O.engine_build_draws(SEED, n, NLIST, M)
+    sidx, init, kpp_u, pidx, pinit = O.engine_build_draws(SEED, n, NLIST, M,
+                                                          ivf_sample=args.ivf_sample or 30000)
     ix = O.OracleIVFPQ.build(X, np.arange(n), NLIST, M, sidx, init, kpp_u, pidx, pinit,
                              threads=threads)
     build_s = time.time() - t0
@@ -427,7 +430,7 @@ def run_ours(args, rank, world, local_rank, dist):
 
     X, Q = make_data()
     t0 = time.time()
-    ix = fg.IVFPQIndex.build(X, NLIST, M, ctx=ctx, seed=SEED)
+    ix = fg.IVFPQIndex.build(X, NLIST, M, ctx=ctx, seed=SEED, ivf_sample=args.ivf_sample)
     torch.cuda.synchronize()
     build_s = time.time() - t0
     ix.set_nprobe(args.nprobe)
@@ -1033,10 +1036,19 @@ def main():
     ap.add_argument("--bf-metric", default="l2sq", choices=["l2sq", "dot", "cosine", "l2"])
     ap.add_argument("--bf-n", type=int, default=1_000_000, help="rows (smaller for profiling)")
     ap.add_argument("--bf-nq", type=int, default=10_000, help="queries (smaller for profiling)")
+    ap.add_argument("--n-base", type=int, default=None,
+                    help="IVF-PQ: database rows (a smaller case of the workload, for profiling)")
+    ap.add_argument("--nlist", type=int, default=None, help="IVF-PQ: lists (with --n-base)")
+    ap.add_argument("--ivf-sample", type=int, default=0,
+                    help="IVF-PQ: k-means training sample (default: the reference's)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload in IVF_CONFIGS:
         use_ivf_config(args.workload)
+        if args.n_base:
+            globals()["N_BASE"] = args.n_base
+        if args.nlist:
+            globals()["NLIST"] = args.nlist
     if args.nprobe is None:
         args.nprobe = DEFAULT_NPROBE
     global SCALING

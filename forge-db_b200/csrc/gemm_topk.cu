@@ -13,17 +13,21 @@
 //     threshold are buffered in shared memory and merged, a warp at a time,
 //     into the query's sorted top-32 in global memory.  Its 32nd distance is
 //     a per-query threshold tau that about 32*S rows of the full set pass.
-//   FILTER: every tile, eight epilogue warps (two per TMEM lane quadrant, one
-//     per half of the columns).  A score costs a shuffle, an FMA and a
-//     compare; the rare scores <= tau are appended to a per-query candidate
-//     array with an atomic counter.
+//   FILTER: every tile, sixteen epilogue warps (four per TMEM lane quadrant,
+//     one 32-column chunk each; the tile's column values staged in shared
+//     memory by the producer, four TMEM accumulators so the MMA runs ahead).
+//     A score costs half a packed FMA and a third of a three-input minimum;
+//     the 8-column groups that may hold a score <= tau are reloaded from
+//     TMEM and their hits appended to a per-query candidate array, one
+//     atomic per row and group.
 // select_candidates_kernel then takes the top-kp of each query's candidates
 // and bf_rescore_kernel recomputes them exactly in the reference's AVX2
 // summation order and certifies the result (see there), so returned
 // distances are exact and a bad tau or an overflow only costs a fallback.
 //
-// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
-// TMEM owner, warps 4-11 = epilogue.  Every wait on an mbarrier is bounded:
+// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner,
+// warps 4-7 (sample pass, 384 threads) or 4-19 (filter pass, 640 threads) =
+// epilogue.  Every wait on an mbarrier is bounded:
 // on timeout the kernel sets an error word, the other warps see it and
 // leave, in-flight copies and MMAs are waited for (bounded), TMEM is freed,
 // and the host reports FDB_ERR_TIMEOUT.
@@ -41,11 +45,25 @@
 namespace fdb {
 namespace tc {
 
+// Threads per block: the filter pass runs sixteen epilogue warps (four per
+// TMEM lane quadrant, one 32-column chunk of each tile apiece) so that the
+// latency of each warp's loads and candidate appends is hidden by the others.
 constexpr int THREADS = 384;
+constexpr int THREADS_FILTER = 640;
 constexpr int EPI_WARP0 = 4;
 constexpr int SAMPLE_K = 32;  // sample-pass shortlist per query
 constexpr int EPI_SHORTLIST = 0, EPI_FILTER = 1;
 constexpr int BUF_CAP = 64;   // sample pass: buffered candidates per query
+constexpr int NCV = 4;        // filter pass: staged column-value slots (one per tile)
+constexpr int MAX_STAGES = 6; // B pipeline stages at most
+// mbarriers: a_full, b_full/b_empty [MAX_STAGES], t_full/t_empty [4], cv_full/cv_empty [NCV]
+constexpr int NBARS = 1 + 2 * MAX_STAGES + 8 + 2 * NCV;
+
+// B pipeline stages: the filter pass keeps more tiles in flight (its shared
+// memory holds no candidate buffers); at most ~200 KB in every case.
+__host__ __device__ constexpr int b_stages(int katoms, int epi) {
+    return epi == EPI_FILTER ? (katoms <= 2 ? 4 : (katoms == 3 ? 3 : 2)) : (katoms <= 3 ? 2 : 1);
+}
 
 struct GemmTopkParams {
     int nq;              // queries
@@ -118,24 +136,33 @@ __device__ __forceinline__ uint64_t merge_into(uint64_t* list, const uint64_t* l
 }
 
 template <int EPI, int MET>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 1)
     gemm_topk_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, GemmTopkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
     const int KA = p.katoms;
-    const int NSTAGE = KA <= 3 ? 2 : 1;
+    const int NSTAGE = b_stages(KA, EPI);
+    // TMEM accumulators (128 columns each): the filter pass lets the MMA run
+    // up to three tiles ahead of its epilogue
+    constexpr int NACC = EPI == EPI_FILTER ? 4 : 2;
+    // the filter pass stages each tile's column values (||x||^2 or 1/||x||)
+    // in shared memory by a bulk copy that the producer issues with the tile
+    constexpr bool STAGE_CV = EPI == EPI_FILTER && MET != MET_DOT;
     unsigned char* a_tile = smem;                                  // KA atoms
     unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA atoms
-    uint64_t* cbuf = reinterpret_cast<uint64_t*>(b_tile + NSTAGE * KA * ATOM_BYTES);
+    float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * ATOM_BYTES);  // [NCV][TILE_N]
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + (EPI == EPI_FILTER ? NCV * TILE_N : 0));
     uint64_t* bars = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
     uint64_t* a_full = bars + 0;
-    uint64_t* b_full = bars + 1;   // [2]
-    uint64_t* b_empty = bars + 3;  // [2]
-    uint64_t* t_full = bars + 5;   // [2]
-    uint64_t* t_empty = bars + 7;  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    uint64_t* b_full = a_full + 1;              // [MAX_STAGES]
+    uint64_t* b_empty = b_full + MAX_STAGES;    // [MAX_STAGES]
+    uint64_t* t_full = b_empty + MAX_STAGES;    // [4]
+    uint64_t* t_empty = t_full + 4;             // [4]
+    uint64_t* cv_full = t_empty + 4;            // [NCV]
+    uint64_t* cv_empty = cv_full + NCV;         // [NCV]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qb = blockIdx.x;
@@ -148,22 +175,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int first = (stride - tile0 % stride) % stride;
     const int count = ntiles > first ? (ntiles - first + stride - 1) / stride : 0;
     const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
-    const int n_epi_warps = EPI == EPI_SHORTLIST ? 4 : 8;
+    const int n_epi_warps = EPI == EPI_SHORTLIST ? 4 : 16;
 
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < MAX_STAGES; ++i) {
             mbar_init(b_full + i, 1);
             mbar_init(b_empty + i, 1);
+        }
+        for (int i = 0; i < 4; ++i) {
             mbar_init(t_full + i, 1);
             mbar_init(t_empty + i, n_epi_warps);
+        }
+        for (int i = 0; i < NCV; ++i) {
+            mbar_init(cv_full + i, 1);
+            mbar_init(cv_empty + i, n_epi_warps);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(2 * TILE_N));
+                     "r"(NACC * TILE_N));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         tc_fence_before();
     }
@@ -172,8 +205,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = *tmem_slot;
     // Last asynchronous operation each role issued, so that an aborting
     // block can wait for it (bounded) before it frees TMEM and exits.
-    int last_load[2] = {-1, -1};  // producer: last use issued per stage
-    int last_i = -1;              // MMA issuer: last tile committed
+    int last_load[MAX_STAGES];  // producer: last use issued per B stage
+    int last_cv[NCV];           // producer: last use issued per column-value slot
+    for (int i = 0; i < MAX_STAGES; ++i) last_load[i] = -1;
+    for (int i = 0; i < NCV; ++i) last_cv[i] = -1;
+    int last_i = -1;                      // MMA issuer: last tile committed
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -182,8 +218,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int a = 0; a < KA; ++a)
                 tma_load_2d(a_tile + a * ATOM_BYTES, &qmap, a_full, a * KATOM, qb * TILE_M);
             for (int i = 0; i < count; ++i) {
-                const int s = NSTAGE == 2 ? (i & 1) : 0;
-                const int use = NSTAGE == 2 ? (i >> 1) : i;
+                const int s = i % NSTAGE;
+                const int use = i / NSTAGE;
                 if (i >= NSTAGE && !mbar_wait(b_empty + s, (use - 1) & 1, p.err, p.wait)) break;
                 mbar_expect_tx(b_full + s, stage_bytes);
                 const int row = (int)(r0 + (size_t)(first + i * stride) * TILE_N);
@@ -191,6 +227,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int a = 0; a < KA; ++a)
                     tma_load_2d(dst + a * ATOM_BYTES, &xmap, b_full + s, a * KATOM, row);
                 last_load[s] = use;
+                if (STAGE_CV) {
+                    // the tile's 128 column values (colv is padded to whole tiles;
+                    // row is a multiple of 128, so the copy is 512-byte aligned)
+                    const int c = i % NCV, cu = i / NCV;
+                    if (i >= NCV && !mbar_wait(cv_empty + c, (cu - 1) & 1, p.err, p.wait)) break;
+                    mbar_expect_tx(cv_full + c, TILE_N * 4);
+                    bulk_load(cvbuf + c * TILE_N, p.colv + row, TILE_N * 4, cv_full + c);
+                    last_cv[c] = cu;
+                }
             }
         }
     } else if (warp == 1) {
@@ -198,10 +243,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && count > 0) {
             bool ok = mbar_wait(a_full, 0, p.err, p.wait);
             for (int i = 0; ok && i < count; ++i) {
-                const int s = NSTAGE == 2 ? (i & 1) : 0;
-                const int use = NSTAGE == 2 ? (i >> 1) : i;
-                const int b = i & 1;  // TMEM accumulator buffer
-                if (i >= 2 && !mbar_wait(t_empty + b, ((i >> 1) - 1) & 1, p.err, p.wait)) break;
+                const int s = i % NSTAGE;
+                const int use = i / NSTAGE;
+                const int b = i % NACC;  // TMEM accumulator buffer
+                if (i >= NACC && !mbar_wait(t_empty + b, ((i / NACC) - 1) & 1, p.err, p.wait))
+                    break;
                 if (!mbar_wait(b_full + s, use & 1, p.err, p.wait)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * TILE_N);
@@ -224,15 +270,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue ----------------
         const int w = warp - EPI_WARP0;
         const int quad = w & 3;            // TMEM lane quadrant = warp % 4
-        const int half = w >> 2;           // FILTER: column half of this warp
+        const int part = w >> 2;           // FILTER: 32-column chunk of this warp
         const int e = quad * 32 + lane;    // query row in the block
         const int q = qb * TILE_M + e;
         const bool qok = q < p.nq;
         const float qn0 = (qok && p.qnorm) ? p.qnorm[q] : 0.0f;
         const float qn = MET == MET_COS ? (qn0 > 0.0f ? rsqrtf(qn0) : 0.0f) : qn0;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const int c0 = EPI == EPI_SHORTLIST ? 0 : 2 * half;
-        const int c1 = EPI == EPI_SHORTLIST ? TILE_N / 32 : 2 * half + 2;
+        const int c0 = EPI == EPI_SHORTLIST ? 0 : part;
+        const int c1 = EPI == EPI_SHORTLIST ? TILE_N / 32 : part + 1;
         float tau = EPI == EPI_FILTER ? (qok ? p.tau_q[q] : -__int_as_float(0x7f800000))
                                       : __int_as_float(0x7f800000);
         int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
@@ -256,61 +302,115 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tt = qn == 0.0f ? -__int_as_float(0x7f800000)
                                 : ((1.0f - tau) - ldexpf(2.0f + fabsf(tau), -18)) / qn;
             }
+            // The test of a 32-column chunk: bit g is set when some row of the
+            // warp may admit a row among the chunk's columns 8g..8g+7.  Each
+            // group's best test value comes from a short tree (L2: the smallest
+            // fma(-2, s, ||x||^2), two per f32x2 instruction; dot and cosine:
+            // the negated largest s or s/||x||, zero rows counted as hits) and
+            // one vote skips the chunk when no lane can have a hit.
+            const float T = MET == MET_L2 ? tt : -tt;
+            auto test = [&](const uint32_t(&v)[32], const float* cvs) -> unsigned {
+                float m[4];
+                if constexpr (MET == MET_L2) {
+                    const uint64_t m2 = pack2(__float_as_uint(-2.0f), __float_as_uint(-2.0f));
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) {  // one group at a time: few live values
+                        float y[8];
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; ++h2) {
+                            const int i2 = 2 * g8 + h2;
+                            const ulonglong2 cc = reinterpret_cast<const ulonglong2*>(cvs)[i2];
+                            const uint64_t x01 = fma2(m2, pack2(v[4 * i2], v[4 * i2 + 1]), cc.x);
+                            const uint64_t x23 =
+                                fma2(m2, pack2(v[4 * i2 + 2], v[4 * i2 + 3]), cc.y);
+                            y[4 * h2] = __uint_as_float((uint32_t)x01);
+                            y[4 * h2 + 1] = __uint_as_float((uint32_t)(x01 >> 32));
+                            y[4 * h2 + 2] = __uint_as_float((uint32_t)x23);
+                            y[4 * h2 + 3] = __uint_as_float((uint32_t)(x23 >> 32));
+                        }
+                        m[g8] = min3f(min3f(y[0], y[1], y[2]), min3f(y[3], y[4], y[5]),
+                                      fminf(y[6], y[7]));
+                    }
+                } else {
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) {
+                        float y[8];
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int j = 8 * g8 + jj;
+                            const float sj = __uint_as_float(v[j]);
+                            if (MET == MET_DOT) y[jj] = -sj;
+                            else
+                                y[jj] = cvs[j] == 0.0f ? -__int_as_float(0x7f800000)
+                                                       : -(sj * cvs[j]);
+                        }
+                        m[g8] = min3f(min3f(y[0], y[1], y[2]), min3f(y[3], y[4], y[5]),
+                                      fminf(y[6], y[7]));
+                    }
+                }
+                const float mn = fminf(fminf(m[0], m[1]), fminf(m[2], m[3]));
+                if (!__any_sync(0xffffffffu, mn <= T)) return 0u;
+                unsigned gm = 0;
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8)
+                    gm |= __any_sync(0xffffffffu, m[g8] <= T) ? 1u << g8 : 0u;
+                return gm;
+            };
+            // The groups of gm (bit g: columns 8g..8g+7 of this warp's chunk),
+            // reloaded from the accumulator, which is still held: every row
+            // whose key distance (approx_metric) is <= tau is appended to the
+            // query's candidates, one atomic per group.
+            auto admit = [&](unsigned gm, uint32_t tcol, const float* cvs, size_t cbase) {
+                const int nvalid = cbase < r1 ? (int)min((size_t)32, r1 - cbase) : 0;
+                const uint32_t tag = (uint32_t)(p.tag_base + cbase);
+                uint64_t* crow = p.cand + (size_t)q * p.cap;
+                while (gm) {
+                    const int gi = __ffs(gm) - 1;
+                    gm &= gm - 1;
+                    uint32_t w8[8];
+                    tmem_ld8(tmem + lane_base + tcol + (uint32_t)(gi * 8), w8);
+                    float d[8];
+                    unsigned hm = 0;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int j = gi * 8 + jj;
+                        d[jj] = approx_metric<MET>(__uint_as_float(w8[jj]), qn,
+                                                   MET == MET_DOT ? 0.0f : cvs[j]);
+                        if (qok && j < nvalid && d[jj] <= tau) hm |= 1u << jj;
+                    }
+                    if (hm == 0) continue;
+                    unsigned ix = atomicAdd(p.cand_cnt + q, (unsigned)__popc(hm));
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+                        if (hm >> jj & 1u) {
+                            if (ix < (unsigned)p.cap)
+                                crow[ix] = make_key(d[jj], tag + (uint32_t)(gi * 8 + jj));
+                            ++ix;
+                        }
+                }
+            };
             for (int i = 0; i < count; ++i) {
-                const int b = i & 1;
+                const int b = i % NACC, c = i % NCV;
                 int got = 0;
-                if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err, p.wait) ? 1 : 0;
+                if (lane == 0)
+                    got = mbar_wait(t_full + b, (i / NACC) & 1, p.err, p.wait) &&
+                          (!STAGE_CV || mbar_wait(cv_full + c, (i / NCV) & 1, p.err, p.wait));
                 got = __shfl_sync(0xffffffffu, got, 0);
                 if (!got) break;
                 tc_fence_after();
-                const size_t rb = r0 + (size_t)i * TILE_N;
-                uint32_t va[32], vb[32];
-                float ca[32], cbv[32];
-                const size_t rowa = rb + (size_t)c0 * 32, rowb = rowa + 32;
-                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + c0 * 32), va);
-                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + c0 * 32 + 32), vb);
-                column_values<MET>(p.colv, rowa, ca);
-                column_values<MET>(p.colv, rowb, cbv);
-                tmem_wait_ld();
-                // both chunks are in registers: release the accumulator now
+                const uint32_t tcol = (uint32_t)(b * TILE_N + part * 32);
+                uint32_t va[32];
+                tmem_ld32_nowait(tmem + lane_base + tcol, va);
+                tmem_wait_regs(va);
+                const float* cvs = cvbuf + c * TILE_N + part * 32;
+                const unsigned gm = test(va, cvs);
+                if (gm) admit(gm, tcol, cvs, r0 + (size_t)i * TILE_N + (size_t)part * 32);
+                // done with the accumulator and the staged column values
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(t_empty + b);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t* v = h == 0 ? va : vb;
-                    const float* cv = h == 0 ? ca : cbv;
-                    const size_t cb = h == 0 ? rowa : rowb;
-                    auto fast = [&](int j) -> bool {
-                        const float s = __uint_as_float(v[j]);
-                        if (MET == MET_L2) return __fmaf_rn(-2.0f, s, cv[j]) <= tt;
-                        if (MET == MET_DOT) return s >= tt;
-                        return (s * cv[j] >= tt) || (cv[j] == 0.0f);
-                    };
-                    // A warp covers 32 queries x 32 rows per chunk, so it meets a
-                    // hit often; testing 8-row groups keeps the exact re-check
-                    // (and its divergence) to the groups that hold one.
-                    const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
-                    const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        bool any = false;
-#pragma unroll
-                        for (int jj = 0; jj < 8; ++jj) any |= fast(g * 8 + jj);
-                        if (__any_sync(0xffffffffu, any)) {
-#pragma unroll
-                            for (int jj = 0; jj < 8; ++jj) {
-                                const int j = g * 8 + jj;
-                                const float d =
-                                    approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
-                                if (qok && j < nvalid && d <= tau) {
-                                    const unsigned idx = atomicAdd(p.cand_cnt + q, 1u);
-                                    if (idx < (unsigned)p.cap)
-                                        p.cand[(size_t)q * p.cap + idx] = make_key(d, tag0 + j);
-                                }
-                            }
-                        }
-                    }
+                if (lane == 0) {
+                    mbar_arrive(t_empty + b);
+                    if (STAGE_CV) mbar_arrive(cv_empty + c);
                 }
             }
         } else
@@ -416,17 +516,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         // aborting: let the copies and MMAs this block issued land before exit
         // (waits on phases that already completed return at once)
         if (warp == 0 && lane == 0) {
-            for (int s2 = 0; s2 < 2; ++s2)
+            for (int s2 = 0; s2 < NSTAGE; ++s2)
                 if (last_load[s2] >= 0) {
                     const unsigned long long t0 = clock64();
                     while (!mbar_try(b_full + s2, last_load[s2] & 1) &&
                            clock64() - t0 < WAIT_CYCLES) {
                     }
                 }
+            for (int c2 = 0; c2 < NCV; ++c2)
+                if (last_cv[c2] >= 0) {
+                    const unsigned long long t0 = clock64();
+                    while (!mbar_try(cv_full + c2, last_cv[c2] & 1) &&
+                           clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
         }
         if (warp == 1 && lane == 0 && last_i >= 0) {
             const unsigned long long t0 = clock64();
-            while (!mbar_try(t_full + (last_i & 1), (last_i >> 1) & 1) &&
+            while (!mbar_try(t_full + (last_i % NACC), (last_i / NACC) & 1) &&
                    clock64() - t0 < WAIT_CYCLES) {
             }
         }
@@ -435,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(2 * TILE_N));
+                     "r"(NACC * TILE_N));
     }
 }
 
@@ -480,9 +587,11 @@ __global__ void to_half_kernel(const float* __restrict__ x, size_t n, int dim, i
 }
 
 size_t gemm_smem(int katoms, int epi) {
-    const int nstage = katoms <= 3 ? 2 : 1;
+    const int nstage = tc::b_stages(katoms, epi);
     return 1024 + (size_t)(1 + nstage) * katoms * tc::ATOM_BYTES +
-           (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) + 16 * 8;
+           (epi == tc::EPI_FILTER ? (size_t)tc::NCV * tc::TILE_N * 4 : 0) +
+           (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) +
+           (tc::NBARS + 1) * 8;
 }
 
 // Row chunks: enough blocks for several waves with little tail waste.
@@ -514,7 +623,8 @@ void launch_pass_m(cudaStream_t s, const CUtensorMap& qm, const CUtensorMap& xm,
     FDB_CUDA(cudaFuncSetAttribute(tc::gemm_topk_kernel<EPI, MET>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((unsigned)((nq + tc::TILE_M - 1) / tc::TILE_M), (unsigned)chunks);
-    tc::gemm_topk_kernel<EPI, MET><<<grid, tc::THREADS, smem, s>>>(qm, xm, p);
+    tc::gemm_topk_kernel<EPI, MET>
+        <<<grid, EPI == tc::EPI_FILTER ? tc::THREADS_FILTER : tc::THREADS, smem, s>>>(qm, xm, p);
     FDB_LAUNCH_CHECK();
 }
 

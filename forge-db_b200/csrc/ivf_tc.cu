@@ -109,28 +109,6 @@ constexpr int NCV = NSTAGE; // ||rhat||^2 stages (one per B stage)
 constexpr int NACC = 4;    // TMEM accumulators (128 columns each: all 512 columns)
 
 
-// Packed pairs of f32 (element 0 in the low half): sm_100's f32x2
-// instructions round each element exactly as the scalar _rn operation does.
-__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
-    return ((uint64_t)hi << 32) | lo;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-// min of three floats in one instruction
-__device__ __forceinline__ float min3f(float a, float b, float c) {
-    float d;
-    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
 // 32 consecutive floats of a shared buffer (warp-uniform address: broadcast).
 __device__ __forceinline__ void load32(const float* src, float (&cv)[32]) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
@@ -2155,7 +2133,9 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
 // out_keys row holds the seed (the exact top-k of its shortlisted codes in
 // the other lists).  A bounded wait that ran out sets the word that
 // ivf_tc_error_word names.  Queries run in chunks that keep the pass-1 dump
-// (one row of distances per query) within 1 GiB.  pass_tm (nullable) gets a
+// (one row of distances per query, sized for the longest list) within 4 GiB:
+// every chunk re-reads the lists it probes and fills its list-scan items with
+// fewer pair rows, so one chunk per batch is best.  pass_tm (nullable) gets a
 // mark before and after each pass-2 launch.
 void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, size_t take,
                    const uint64_t* lbeg, const uint64_t* lend, uint64_t* out_keys,
@@ -2163,7 +2143,7 @@ void ivf_tc_search(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order
     Ctx& c = h->ctx->c;
     cudaStream_t s = c.stream;
     FDB_REQUIRE(nq * take < (1ull << 31), FDB_ERR_UNSUPPORTED, "too many (query, list) pairs");
-    const size_t budget = (size_t)1 << 28;  // floats
+    const size_t budget = (size_t)1 << 30;  // floats
     const size_t per_query = h->tc_maxpad + take * ivtc::TILE_N;  // dump floats per query
     const size_t chunk = std::max<size_t>(1, std::min(nq, budget / per_query));
     h->t_range.ensure(8);
