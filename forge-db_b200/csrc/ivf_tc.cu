@@ -50,7 +50,7 @@ namespace fdb {
 namespace ivtc {
 using namespace tc;
 
-constexpr int THREADS = 384;
+constexpr int THREADS = 640;
 constexpr int EPI_WARP0 = 4;
 constexpr int LIST_K = 64;  // pass-1 list per query = shortlist length
 constexpr int EPI_DUMP = 0, EPI_FILTER = 1;
@@ -104,7 +104,7 @@ struct PassParams {
 #endif
 constexpr int NSTAGE = FDB_IVF_NSTAGE;  // B tile stages
 constexpr int ASLOTS = FDB_IVF_ASLOTS;  // A tile slots (2: the next item's A loads early)
-constexpr int NEPI = 8;    // epilogue warps: 4 TMEM lane quadrants x 2 column halves
+constexpr int NEPI = 16;   // epilogue warps: 4 TMEM lane quadrants x 4 column chunks
 constexpr int NCV = NSTAGE; // ||rhat||^2 stages (one per B stage)
 constexpr int NACC = 4;    // TMEM accumulators (128 columns each: all 512 columns)
 
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- epilogue ----------------
         const int w = warp - EPI_WARP0;
         const int quad = w & 3;  // TMEM lane quadrant = warp % 4
-        const int half = w >> 2;
+        const int part = w >> 2;  // 32-column chunk of each tile
         const int e = quad * 32 + lane;  // pair row within the tile
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         int g = 0;
@@ -367,18 +367,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int q = rok ? (int)p.pair_q[pr] : 0;
             const float rn = rok ? p.pair_rn[pr] : 0.0f;
             const float s2 = rok ? p.pair_s2[pr] : 0.0f;
-            // Chunk pipeline over the item's tiles: a warp scores 64 columns of a
-            // tile as two 32-column chunks; chunk 1 loads from TMEM while chunk 0
-            // is scored, and the next tile's chunk 0 while chunk 1 is scored.
-            // ||rhat||^2 values are read from the staged slot as they are used.
-            uint32_t va[32], vb[32];
+            // Each of the item's tiles: this warp's 32-column chunk is loaded from
+            // TMEM and scored against the staged ||rhat||^2 values.  Sixteen
+            // epilogue warps (four per lane quadrant) hide one another's load
+            // and append latencies; a warp pipelining two chunks itself with
+            // half as many warps ran pass 2 of config D 1.6x slower.
+            uint32_t va[32];
             auto begin_tile = [&](int gg) -> bool {
                 const int b = gg % NACC, c = gg % NCV;
                 if (!warp_wait(t_full + b, (gg / NACC) & 1, p.err, p.wait, lane) ||
                     !warp_wait(cv_full + c, (gg / NCV) & 1, p.err, p.wait, lane))
                     return false;
                 tc_fence_after();
-                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64), va);
+                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + part * 32), va);
                 return true;
             };
             if constexpr (EPI == EPI_FILTER) {
@@ -428,6 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // never admitted) is appended to its query's candidates.  One copy
                 // of this code serves both chunks, which keeps the loop small.
                 auto admit = [&](unsigned gm, uint32_t tcol, const float* cvs, int cbase) {
+                    // (bit g: columns 8g..8g+7 of this warp's chunk)
                     const uint32_t tag = it.tag0 + (uint32_t)cbase;
                     const int nvalid = (int)it.nb - cbase;
                     uint64_t* crow = p.cand + (size_t)q * p.cap;
@@ -456,22 +458,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                     }
                 };
-                if (nt > 0) {
-                    if (begin_tile(g)) tmem_wait_regs(va);
-                    else alive = false;
-                }
-                for (int t = 0; alive && t < nt; ++t, ++g) {
+                for (int t = 0; t < nt; ++t, ++g) {
+                    if (!begin_tile(g)) {
+                        alive = false;
+                        break;
+                    }
                     const int b = g % NACC, c = g % NCV;
-                    const float* cvs = cvbuf + c * CV_FLOATS + half * 64;
-                    const uint32_t tcol = (uint32_t)(b * TILE_N + half * 64);
-                    tmem_ld32_nowait(tmem + lane_base + tcol + 32u, vb);
-                    unsigned gm = test(va, cvs);
-                    tmem_wait_regs(vb);
-                    // the next tile's first chunk loads while this one is tested
-                    const bool more = t + 1 < nt;
-                    if (more && !begin_tile(g + 1)) alive = false;
-                    gm |= test(vb, cvs + 32) << 4;
-                    if (gm) admit(gm, tcol, cvs, t * TILE_N + half * 64);
+                    const float* cvs = cvbuf + c * CV_FLOATS + part * 32;
+                    const uint32_t tcol = (uint32_t)(b * TILE_N + part * 32);
+                    tmem_wait_regs(va);
+                    const unsigned gm = test(va, cvs);
+                    if (gm) admit(gm, tcol, cvs, t * TILE_N + part * 32);
                     // done with the accumulator and the staged norms
                     tc_fence_before();
                     __syncwarp();
@@ -479,7 +476,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                         mbar_arrive(t_empty + b);
                         mbar_arrive(cv_empty + c);
                     }
-                    if (more && alive) tmem_wait_regs(va);
                 }
             } else {
                 // pass 1: every distance of the row's list goes to its dump row;
@@ -500,25 +496,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                         dst[i] = o;
                     }
                 };
-                if (nt > 0) {
-                    if (begin_tile(g)) tmem_wait_regs(va);
-                    else alive = false;
-                }
-                for (int t = 0; alive && t < nt; ++t, ++g) {
+                for (int t = 0; t < nt; ++t, ++g) {
+                    if (!begin_tile(g)) {
+                        alive = false;
+                        break;
+                    }
                     const int b = g % NACC, c = g % NCV;
-                    const float* cvs = cvbuf + c * CV_FLOATS + half * 64;
-                    tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * TILE_N + half * 64 + 32), vb);
-                    dump(va, cvs, t * TILE_N + half * 64);
-                    tmem_wait_regs(vb);
+                    const float* cvs = cvbuf + c * CV_FLOATS + part * 32;
+                    tmem_wait_regs(va);
+                    dump(va, cvs, t * TILE_N + part * 32);
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(t_empty + b);
-                    const bool more = t + 1 < nt;
-                    if (more && !begin_tile(g + 1)) alive = false;
-                    dump(vb, cvs + 32, t * TILE_N + half * 64 + 32);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(cv_empty + c);
-                    if (more && alive) tmem_wait_regs(va);
+                    if (lane == 0) {
+                        mbar_arrive(t_empty + b);
+                        mbar_arrive(cv_empty + c);
+                    }
                 }
             }
         }
