@@ -50,6 +50,9 @@ constexpr int REF_WARPS = 8;      // refine: queries per block
 constexpr int MAX_DPAD = 256;
 constexpr int CAND_CAP = 128;     // refine: candidates rescored from the compact list
 constexpr int REG_NLIST = 2048;   // refine: rows held in registers (64 per lane) at most
+constexpr int BIG_THREADS = 256;  // refine of longer rows: one block per query
+constexpr int BIG_CAND = 1024;    // its compact candidate list
+constexpr int MAX_NLIST = 1 << 16;  // the tensor coarse path's largest nlist
 
 struct GemmParams {
     int nq;
@@ -565,6 +568,134 @@ __global__ void __launch_bounds__(REF_WARPS * 32, 3)
     }
 }
 
+// Rows longer than REG_NLIST (nlist up to MAX_NLIST): one block per query
+// reads its row of approximate distances from D (L2-resident: the GEMM wrote
+// the chunk just before) twice -- once into the same 256-bin histogram, once
+// to collect the band d~ <= t + 2 E_q -- and rescores the band exactly.  The
+// rules are those of coarse_refine_kernel (same threshold arithmetic, same
+// keys), so the probes are the same; only the memory the row lives in and
+// the number of threads per query differ.
+template <int P, int DIM>
+__global__ void __launch_bounds__(BIG_THREADS)
+    coarse_refine_big_kernel(const float* __restrict__ D, int ldd, int nq, int nlist, int take,
+                             const float* __restrict__ Q, int dim,
+                             const float* __restrict__ cents, const float* __restrict__ qerr,
+                             const uint32_t* __restrict__ rmin, const uint32_t* __restrict__ rmax,
+                             uint32_t* __restrict__ probes, float* __restrict__ pdist) {
+    __shared__ unsigned hist[256];
+    __shared__ uint32_t cand[BIG_CAND];
+    __shared__ uint64_t ckey[BIG_CAND];
+    __shared__ uint64_t tkbuf[64];
+    __shared__ __align__(16) float qs[MAX_DPAD];
+    __shared__ unsigned ncand;
+    __shared__ int s_bstar;
+    const int q = blockIdx.x;
+    if (q >= nq) return;  // whole block leaves together
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* row = D + (size_t)q * ldd;
+    for (int i = tid; i < dim; i += BIG_THREADS) qs[i] = Q[(size_t)q * dim + i];
+    hist[tid] = 0u;
+    if (tid == 0) ncand = 0u;
+    __syncthreads();
+    const float E = qerr[q];
+    const uint32_t lo = rmin[q], hi = rmax[q];
+    float thr = __int_as_float(0x7f800000);
+    if (isfinite(E) && lo <= hi) {  // block-uniform
+        const float scale = 256.0f / ((float)(hi - lo) + 1.0f);
+        for (int l = tid; l < nlist; l += BIG_THREADS) {
+            const float f = (float)(f2ord(row[l]) - lo) * scale;
+            atomicAdd(&hist[min(255, (int)f)], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lane owns bins 8 lane .. 8 lane + 7; the first bin where the
+            // running count reaches take is bstar
+            unsigned c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = hist[8 * lane + j];
+                sum += c[j];
+            }
+            unsigned incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const unsigned reach = __ballot_sync(0xffffffffu, incl >= (unsigned)take);
+            int bstar = 255;
+            if (reach) {
+                const int owner = __ffs(reach) - 1;
+                int bs = 255;
+                unsigned run = incl - sum;
+                bool found = false;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    run += c[j];
+                    if (!found && run >= (unsigned)take) {
+                        bs = 8 * lane + j;
+                        found = true;
+                    }
+                }
+                bstar = __shfl_sync(0xffffffffu, bs, owner);
+            }
+            if (lane == 0) s_bstar = bstar;
+        }
+        __syncthreads();
+        const int bstar = s_bstar;
+        uint32_t tb = hi;
+        if (bstar < 255) {
+            const double w = ((double)bstar + 1.0) / (double)scale * (1.0 + 1e-6) + 2.0;
+            tb = (uint32_t)min((double)hi, (double)lo + ceil(w));
+        }
+        const float t = ord2f(tb);
+        thr = t + 2.0f * E;
+        thr = thr + fabsf(thr) * ldexpf(1.0f, -22);  // the sum's own rounding
+    }
+    // candidates d~ <= t + 2 E_q (a NaN distance stays a candidate), compacted
+    for (int l = tid; l < nlist; l += BIG_THREADS)
+        if (!(row[l] > thr)) {
+            const unsigned pos = atomicAdd(&ncand, 1u);
+            if (pos < (unsigned)BIG_CAND) cand[pos] = (uint32_t)l;
+        }
+    __syncthreads();
+    const unsigned nc = ncand;
+    // a band too wide for the list (or no usable bound): every centroid
+    const bool all = nc > (unsigned)BIG_CAND;
+    const int n = all ? nlist : (int)nc;
+    const bool vec = (dim & 3) == 0;
+    WarpTopK<P> tk;
+    if (warp == 0) tk.init(take, tkbuf);
+    for (int b0 = 0; b0 < n; b0 += BIG_CAND) {
+        const int cnt = min(BIG_CAND, n - b0);
+        for (int i = tid; i < cnt; i += BIG_THREADS) {
+            const uint32_t l = all ? (uint32_t)(b0 + i) : cand[i];
+            const float* rows[1] = {cents + (size_t)l * dim};
+            float d[1];
+            l2sq_rows<1, DIM>(qs, rows, dim, vec, d);
+            ckey[i] = make_key(d[0], l);
+        }
+        __syncthreads();
+        if (warp == 0)
+            for (int i0 = 0; i0 < cnt; i0 += 32) {
+                const bool has = i0 + lane < cnt;
+                tk.add(has ? ckey[i0 + lane] : KEY_NONE, has);
+            }
+        __syncthreads();
+    }
+    if (warp == 0) {
+        tk.flush();
+#pragma unroll
+        for (int e = 0; e < P; ++e) {
+            const int i = e * 32 + lane;
+            if (i < take) {
+                probes[(size_t)q * take + i] = key_tag(tk.L[e]);
+                if (pdist) pdist[(size_t)q * take + i] = key_dist(tk.L[e]);
+            }
+        }
+    }
+}
+
 }  // namespace ctc
 
 // Centroids for the tensor-core coarse quantizer: fp16 rows scaled by 2^sb
@@ -621,7 +752,7 @@ void coarse_tc_prepare(fdb_ivfpq* h) {
 
 bool coarse_tc_eligible(const fdb_ivfpq* h, size_t nq, size_t take) {
     return h->c16.p != nullptr && nq >= 64 && take >= 1 && take <= 256 &&
-           take <= h->nlist && h->nlist <= (size_t)ctc::REG_NLIST;
+           take <= h->nlist && h->nlist <= (size_t)ctc::MAX_NLIST;
 }
 
 // Probes (ascending (distance, list) keys) and their exact distances for nq
@@ -703,11 +834,24 @@ void coarse_tc(fdb_ivfpq* h, const float* dQ, size_t nq, size_t take, uint32_t* 
     else if (take <= 64) FDB_REFINE(RR, 2); \
     else if (take <= 128) FDB_REFINE(RR, 4); \
     else FDB_REFINE(RR, 8)
+#define FDB_BIG_D(PP, DD)                                                                    \
+    coarse_refine_big_kernel<PP, DD><<<(unsigned)nc, BIG_THREADS, 0, s>>>(                   \
+        h->s_cdapprox.p, npad, (int)nc, (int)h->nlist, (int)take, Qc, (int)h->dim, h->cents.p, \
+        h->s_cqerr.p, p.rmin, p.rmax, pr, pd)
+// (run-time dim: the unrolled fixed-dim rescoring needs ~170 registers, which
+// would leave one block per SM for the two passes over the row)
+#define FDB_BIG(PP) FDB_BIG_D(PP, 0)
         const size_t nl = h->nlist;
         if (nl <= 256) { FDB_REFINE_P(8); }
         else if (nl <= 512) { FDB_REFINE_P(16); }
         else if (nl <= 1024) { FDB_REFINE_P(32); }
-        else { FDB_REFINE_P(64); }
+        else if (nl <= (size_t)REG_NLIST) { FDB_REFINE_P(64); }
+        else if (take <= 32) { FDB_BIG(1); }
+        else if (take <= 64) { FDB_BIG(2); }
+        else if (take <= 128) { FDB_BIG(4); }
+        else { FDB_BIG(8); }
+#undef FDB_BIG
+#undef FDB_BIG_D
 #undef FDB_REFINE_P
 #undef FDB_REFINE
 #undef FDB_REFINE_D

@@ -130,11 +130,12 @@ def test_oracle_build_from_engine_draws_is_the_gpu_index(fg, ctx, orc, n, nlist,
 
 
 @pytest.mark.parametrize("dim,nlist", [(8, 50), (37, 300), (64, 1024), (100, 130), (256, 257),
-                                       (128, 2048)])
+                                       (128, 2048), (96, 3000), (33, 5000), (128, 16384)])
 @pytest.mark.parametrize("nprobe", [1, 7, 64, 200])
 def test_tensor_coarse_quantizer_probes_match_oracle(fg, ctx, orc, dim, nlist, nprobe):
     """Batches of 64+ queries pick their probes with the tcgen05 coarse
-    quantizer (fp16 GEMM, certified band, exact rescoring).  In the exact
+    quantizer (fp16 GEMM, certified band, exact rescoring; above 2048 lists
+    the band is taken by a block per query from memory).  In the exact
     scan mode that is the only approximate step, so any probe that differs
     from find_nearest_partitions (ivf_pq.rs:865-888) shows in the results."""
     if nprobe > nlist:
@@ -144,7 +145,7 @@ def test_tensor_coarse_quantizer_probes_match_oracle(fg, ctx, orc, dim, nlist, n
     X = (rng.standard_normal((n, dim)) * rng.uniform(0.1, 50)).astype(np.float32)
     Q = X[rng.integers(0, n, 300)] + rng.standard_normal((300, dim)).astype(np.float32)
     m = 1 if dim % 2 else 2
-    ix = fg.IVFPQIndex.build(X, nlist, m, ctx=ctx, seed=dim, ivf_sample=min(n, 6000),
+    ix = fg.IVFPQIndex.build(X, nlist, m, ctx=ctx, seed=dim, ivf_sample=min(n, max(6000, 2 * nlist)),
                              pq_sample=min(n, 4000), ivf_iters=4, pq_iters=2)
     ox = _oracle(orc, ix)
     ix.set_scan_mode(1)
