@@ -604,7 +604,7 @@ struct fdb_ivfpq {
     fdb::PinnedWords s_pin;  // end-of-call readbacks (statistics, error word, counts)
     // tensor-mode scratch: pair grouping, residual rows, items, shortlists
     fdb::DevBuf<uint32_t> t_keys, t_vals, t_off, t_pq, t_qbad, t_range, t_inv, t_plen,
-        t_seg, t_fprobes, t_fcnt, t_uoff, t_unit_q, t_unit_l;
+        t_seg, t_fprobes, t_fcnt, t_uoff, t_unit_q, t_unit_l, t_qrange;
     fdb::DevBuf<uint64_t> t_unit_keys;
     fdb::DevBuf<float> t_dump, t_dk;
     fdb::DevBuf<uint64_t> t_ekeys;

@@ -86,6 +86,8 @@ struct PassParams {
     const float* colv;       // padded layout: ||rhat||^2, +inf in padding rows
     float colmax;            // largest ||rhat||^2
     float* dump;             // pass 1: every distance of each pair's list
+    uint32_t* lo;            // pass 1: [nq] smallest finite distance (orderable bits), preset ~0
+    uint32_t* hi;            // pass 1: [nq] ~(largest finite distance, orderable bits), preset ~0
     const unsigned* seg;     // pass 1: [pairs] offset of the pair's row in dump
     const float* tau;        // pass 2: [nq] admission threshold
     uint64_t* cand;          // pass 2: [nq][cap] candidate keys
@@ -483,9 +485,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float* drow = rok ? p.dump + p.seg[pr] + it.col0 : nullptr;
                 const uint64_t s22 = pack2(__float_as_uint(s2), __float_as_uint(s2));
                 const uint64_t rn2 = pack2(__float_as_uint(rn), __float_as_uint(rn));
+                // The chunk's finite distances also update the query's range
+                // (select1_kernel's histogram bounds), so that kernel need not
+                // read the dump a third time; +inf (padding, tombstones) and
+                // NaN are left out, as there.
                 auto dump = [&](const uint32_t(&v)[32], const float* cvs, int col) {
                     if (!rok) return;
                     ulonglong2* dst = reinterpret_cast<ulonglong2*>(drow + col);
+                    float mn = INF, mx = -INF;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         // fmaf_rn(s2, v, rn + ||rhat||^2), two per instruction
@@ -494,6 +501,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                         o.x = fma2(s22, pack2(v[4 * i], v[4 * i + 1]), add2(rn2, cc.x));
                         o.y = fma2(s22, pack2(v[4 * i + 2], v[4 * i + 3]), add2(rn2, cc.y));
                         dst[i] = o;
+                        const float y[4] = {__uint_as_float((uint32_t)o.x),
+                                            __uint_as_float((uint32_t)(o.x >> 32)),
+                                            __uint_as_float((uint32_t)o.y),
+                                            __uint_as_float((uint32_t)(o.y >> 32))};
+#pragma unroll
+                        for (int x = 0; x < 4; ++x)
+                            if (y[x] < INF) {  // finite (NaN compares false)
+                                mn = fminf(mn, y[x]);
+                                mx = fmaxf(mx, y[x]);
+                            }
+                    }
+                    if (mn < INF) {
+                        atomicMin(p.lo + q, f2ord(mn));
+                        atomicMin(p.hi + q, ~f2ord(mx));
                     }
                 };
                 for (int t = 0; t < nt; ++t, ++g) {
@@ -978,6 +999,7 @@ __global__ void __launch_bounds__(256)
                    const uint32_t* __restrict__ inv, const unsigned* __restrict__ poff,
                    int nlist, const uint32_t* __restrict__ probes, int take,
                    const uint64_t* __restrict__ lbeg, const uint64_t* __restrict__ lend, int nq,
+                   const uint32_t* __restrict__ qlo, const uint32_t* __restrict__ qhi,
                    uint64_t* __restrict__ part, float* __restrict__ tau) {
     __shared__ uint64_t buf[8 * 64];
     __shared__ unsigned hist[8 * 256];
@@ -1022,18 +1044,9 @@ __global__ void __launch_bounds__(256)
             }
         }
     };
-    // 1. the range of the query's finite distances (+inf marks a tombstoned row)
-    uint32_t lo = 0xffffffffu, hi = 0u;
-    visit([&](const float(&d)[4], uint32_t, int nv) {
-#pragma unroll
-        for (int x = 0; x < 4; ++x)
-            if (x < nv && d[x] < INF) {
-                lo = min(lo, f2ord(d[x]));
-                hi = max(hi, f2ord(d[x]));
-            }
-    });
-    lo = __reduce_min_sync(0xffffffffu, lo);
-    hi = __reduce_max_sync(0xffffffffu, hi);
+    // 1. the range of the query's finite distances (+inf marks a tombstoned
+    //    row), gathered by pass 1's epilogue as it wrote the dump rows
+    const uint32_t lo = qlo[q], hi = ~qhi[q];
     // 2. a threshold t with at least LIST_K entries d <= t: the rounded-up
     //    upper edge of the first of 256 bins (between lo and hi) whose running
     //    count reaches LIST_K (all entries when there are fewer)
@@ -1940,11 +1953,15 @@ void tc_chunk(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k, int order, siz
     p.stall = take_test_stall(c) ? 1 : 0;
     p.next = h->t_range.p + 5;
     FDB_CUDA(cudaMemsetAsync(h->t_range.p + 5, 0, 8, s));
+    h->t_qrange.ensure(2 * nq);
+    FDB_CUDA(cudaMemsetAsync(h->t_qrange.p, 0xff, 2 * nq * 4, s));
+    p.lo = h->t_qrange.p;
+    p.hi = h->t_qrange.p + nq;
     const int grid = c.sm_count;
     launch_pass<EPI_DUMP>(s, am, bm, grid, p);
     select1_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
         h->t_dump.p, h->t_seg.p, h->t_inv.p, h->t_off.p, nlist, probes, (int)take, lbeg, lend,
-        (int)nq, h->t_part.p, h->t_tau.p);
+        (int)nq, h->t_qrange.p, h->t_qrange.p + nq, h->t_part.p, h->t_tau.p);
     FDB_LAUNCH_CHECK();
     if (h->sharded) {
         // the device holding a query's pass-1 list sets its threshold (+inf elsewhere)
