@@ -633,6 +633,14 @@ int fdb_ivfpq_get_pass1_quota(fdb_ivfpq* h, size_t nprobe, int64_t* div) {
     });
 }
 
+int fdb_ivfpq_set_stage_timers(fdb_ivfpq* h, int enable) {
+    return guarded([&] {
+        FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->stage_timers = enable != 0;
+    });
+}
+
 int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable) {
     return guarded([&] {
         FDB_REQUIRE(h, FDB_ERR_INVALID_ARG, "NULL handle");

@@ -673,7 +673,8 @@ GraphKey search_key(const fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out
     g[14] = io ? (uint64_t)io->counts : 0;
     g[15] = ((uint64_t)h->scan_mode << 32) | (uint64_t)h->rerank;
     g[16] = h->rerank_factor;
-    g[17] = 1;  // a valid key
+    // a valid key; which marks are recorded (only a call with statistics has any)
+    g[17] = 1 | ((st != nullptr && h->stage_timers) ? 2u : 0u);
     g[18] = h->tc_sample_div;
     return g;
 }
@@ -704,9 +705,12 @@ void ivfpq_search_dev(fdb_ivfpq* h, const float* dQ, size_t nq, size_t k_out, in
                               (h->scan_mode == FDB_SCAN_AUTO && nq >= 256));
     if (tensor_path && take > 0)
         h->tc_sample_div = call_skip ? 64 : pass1_quota(h, dQ, nq, k_out, k, order, take, skip);
-    StageTimer tm(s, st != nullptr);
+    // (the stage and collective marks are event records inside the step,
+    // each a dependency point of its own; with stage_timers off a call with
+    // statistics records only the two around the list scan's pass 2)
+    StageTimer tm(s, st != nullptr && h->stage_timers);
     StageTimer pass_tm(s, st != nullptr);  // around each pass-2 launch (tensor mode)
-    StageTimer comm_tm(s, st != nullptr && h->sharded);  // around each collective
+    StageTimer comm_tm(s, st != nullptr && h->sharded && h->stage_timers);  // around collectives
     CommTimerScope comm_scope(c, comm_tm);
     uint64_t* pin = h->s_pin.get();
     for (int i = 0; i < 6; ++i) pin[i] = 0;

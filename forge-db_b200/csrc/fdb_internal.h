@@ -514,6 +514,7 @@ struct fdb_ivfpq {
     std::atomic<size_t> nprobe{1};
     unsigned long long call_wait_cycles = 0;  // a call's own wait limit (0: none)
     bool graphs = true;                       // replay repeated searches as CUDA graphs
+    bool stage_timers = true;                 // fill the stage times of fdb_stats
     fdb::GraphCache graphs_cache;
     size_t n_total = 0;  // vectors in the unsharded index
     size_t n_local = 0;  // vectors whose lists live on this device

@@ -126,6 +126,7 @@ _SIGS = {
     "fdb_ivfpq_set_scan_mode": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_set_graphs": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_set_pass1_quota": (C.c_int, [_vp, _sz, C.c_uint64]),
+    "fdb_ivfpq_set_stage_timers": (C.c_int, [_vp, C.c_int]),
     "fdb_ivfpq_get_pass1_quota": (C.c_int, [_vp, _sz, C.POINTER(C.c_int64)]),
     "fdb_ivfpq_nprobe": (_sz, [_vp]),
     "fdb_ivfpq_len": (_sz, [_vp]),
@@ -515,6 +516,11 @@ class IVFPQIndex:
         v = C.c_int64()
         _check(lib().fdb_ivfpq_get_pass1_quota(self.h, int(nprobe), C.byref(v)))
         return None if v.value < 0 else v.value
+
+    def set_stage_timers(self, enable: bool):
+        """Fill fdb_stats' stage times (on by default); off, statistics keep
+        the counters and the list scan's pass-2 time only."""
+        _check(lib().fdb_ivfpq_set_stage_timers(self.h, 1 if enable else 0))
 
     def set_graphs(self, enable: bool):
         """Replay repeated same-shape batch searches as CUDA graphs."""

@@ -273,6 +273,12 @@ int fdb_ivfpq_set_scan_mode(fdb_ivfpq* h, int mode);
  * instead of launching ~40 kernels (default: on).  No reference counterpart
  * (a launch-overhead choice of this engine); results are identical. */
 int fdb_ivfpq_set_graphs(fdb_ivfpq* h, int enable);
+/* Whether a search given an fdb_stats fills its stage times (coarse_ms,
+ * scan_ms, rescore_ms, merge_ms, total_ms, comm_ms; default: on).  Each stage
+ * mark is an event record inside the step; off, a call with statistics
+ * records only the two events around the list scan's pass 2 (kernel_ms) and
+ * the counters.  No reference counterpart. */
+int fdb_ivfpq_set_stage_timers(fdb_ivfpq* h, int enable);
 /* The tensor path's pass-1 sampling quota for batch searches with `nprobe`
  * probes: pass 1 scores each query's first list plus the first tile of its
  * nearest other probes until it has seen 1/div of the query's probed codes

@@ -98,3 +98,27 @@ def test_replayed_searches_match_eager_and_oracle(fg, ctx, orc):
     again = device_call()
     assert np.array_equal(eager[0], again[0])
     assert np.array_equal(eager[1].view(np.uint32), again[1].view(np.uint32))
+
+
+def test_stage_timers_off_keeps_pass2_time_and_answer(fg, ctx, orc):
+    """With the stage timers off a call with statistics still reports the
+    counters and the list scan's pass-2 time, not the stage times, and the
+    answer (replayed or eager) does not change."""
+    from forgegpu.datasets import gmm_descriptors
+    X = gmm_descriptors(30000, components=64, seed=54)
+    Q = gmm_descriptors(600, components=64, seed=55)
+    ix = fg.IVFPQIndex.build(X, 64, 16, ctx=ctx, seed=12)
+    ix.set_nprobe(8)
+    ix.set_scan_mode(ix.SCAN_TENSOR)
+    on = ix.batch_search_arrays(Q, 10, stats=True)
+    assert on[3].coarse_ms > 0.0 and on[3].kernel_ms > 0.0
+    ix.set_stage_timers(False)
+    for _ in range(3):  # eager, capture, replay
+        off = ix.batch_search_arrays(Q, 10, stats=True)
+        assert np.array_equal(off[0], on[0])
+        assert np.array_equal(off[1].view(np.uint32), on[1].view(np.uint32))
+        assert off[3].coarse_ms == 0.0 and off[3].total_ms == 0.0
+        assert off[3].kernel_ms > 0.0 and off[3].kernel_scores == on[3].kernel_scores
+    ix.set_stage_timers(True)
+    again = ix.batch_search_arrays(Q, 10, stats=True)
+    assert again[3].coarse_ms > 0.0
