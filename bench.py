@@ -163,9 +163,11 @@ SCAN_MODES = {"auto": 0, "exact": 1, "tables": 2, "tensor": 3}
 RECALL_QUERIES = 2000  # queries whose recall@10 both arms report
 SCALING = "strong"     # the batch and the index are fixed as N grows
 
-# DRAM bytes (read + write) per launch of the dominant kernel on the default
-# workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC = {"ivf_pass_filter": 91.8e6, "bf_gemm_filter": None}
+# DRAM bytes (read + write) per launch of the dominant kernel, per workload,
+# from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of that
+# workload at its bench size; None where only a smaller case was captured
+# (config D: its traffic does not scale by a known factor).
+NCU_TRAFFIC = {"ivfpq_config_c": 87.5e6, "ivfpq_config_d": None, "bf_config_b": None}
 # brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
 # filter pass, candidate selection, exact rescore, keys->ids, finalize
 BF_LAUNCHES = 10
@@ -636,7 +638,11 @@ def run_ours(args, rank, world, local_rank, dist):
         flops = 2.0 * dpad * k_scores
         achieved = flops / (k_ms / 1000.0) / 1e12
         roofline = {"bound": "tensor", "achieved": achieved, "peak": tpk, "unit": "TFLOP/s",
-                    "frac": achieved / tpk, "traffic": NCU_TRAFFIC.get("ivf_pass_filter"),
+                    "frac": achieved / tpk,
+                    "traffic": (NCU_TRAFFIC.get(WORKLOAD)
+                                if (N_BASE, NLIST) == (IVF_CONFIGS[args.workload]["N_BASE"],
+                                                       IVF_CONFIGS[args.workload]["NLIST"])
+                                else None),
                     "kernel": "ivf_pass_kernel<FILTER> (tcgen05 fp16 scores of probed lists "
                               "1..nprobe-1 against decoded codes, fused admission test)",
                     "peak_source": tkind, "algorithmic_flops_per_launch": flops,
@@ -822,7 +828,9 @@ def run_ours_bf(args, rank, world, local_rank, dist):
         "e2e": {"value": nq * args.steps / (float(tot[1]) / 1000), "unit": "queries/s",
                 "h2d_bytes_per_step": nq * DIM * 4, "d2h_bytes_per_step": nq * k * 12 + nq * 4},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": (NCU_TRAFFIC.get("bf_config_b")
+                                 if (n, nq, args.bf_metric) == (1_000_000, 10_000, "l2sq") else None),
                      "kernel": "gemm_topk_kernel<FILTER> (tcgen05 fp16 GEMM + fused admission test)",
                      "peak_source": "measured bf16_tflops (dense fp16 has the same rate)",
                      "kernel_ms": scan_avg},
