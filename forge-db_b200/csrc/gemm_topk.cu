@@ -147,13 +147,13 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     // TMEM accumulators (128 columns each): the filter pass lets the MMA run
     // up to three tiles ahead of its epilogue
     constexpr int NACC = EPI == EPI_FILTER ? 4 : 2;
-    // the filter pass stages each tile's column values (||x||^2 or 1/||x||)
-    // in shared memory by a bulk copy that the producer issues with the tile
-    constexpr bool STAGE_CV = EPI == EPI_FILTER && MET != MET_DOT;
+    // each tile's column values (||x||^2 or 1/||x||) are staged in shared
+    // memory by a bulk copy that the producer issues with the tile
+    constexpr bool STAGE_CV = MET != MET_DOT;
     unsigned char* a_tile = smem;                                  // KA atoms
     unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA atoms
     float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * ATOM_BYTES);  // [NCV][TILE_N]
-    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + (EPI == EPI_FILTER ? NCV * TILE_N : 0));
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + NCV * TILE_N);
     uint64_t* bars = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
     uint64_t* a_full = bars + 0;
     uint64_t* b_full = a_full + 1;              // [MAX_STAGES]
@@ -415,14 +415,16 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
             }
         } else
         for (int i = 0; i < count; ++i) {
-            const int b = i & 1;
+            const int b = i % NACC, cs = i % NCV;
             // one lane waits; the warp follows its verdict (tcgen05.ld is warp-wide)
             int got = 0;
-            if (lane == 0) got = mbar_wait(t_full + b, (i >> 1) & 1, p.err, p.wait) ? 1 : 0;
+            if (lane == 0)
+                got = mbar_wait(t_full + b, (i / NACC) & 1, p.err, p.wait) &&
+                      (!STAGE_CV || mbar_wait(cv_full + cs, (i / NCV) & 1, p.err, p.wait));
             got = __shfl_sync(0xffffffffu, got, 0);
             if (!got) break;
             tc_fence_after();
-            if (EPI == EPI_SHORTLIST && qok) {
+            if (qok) {
                 // Any chunk's top-32 bounds the global top-32 of the sample.
                 const unsigned g = *(volatile unsigned*)(p.tau_g + q);
                 if (g != 0xffffffffu) tau = fminf(tau, ord2f(g));
@@ -440,60 +442,52 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                 }
                 const size_t cb = rb + (size_t)c * 32;
                 const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
+                // the chunk's staged column values, eight 16-byte shared loads
                 float cv[32];
-                column_values<MET>(p.colv, cb, cv);
-                const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
-                if (EPI == EPI_FILTER) {
-                    // admission test first (compare-and-accumulate, no branch);
-                    // rows past the end carry +inf in colv and never pass
-                    bool any = false;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        any |= approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]) <= tau;
-                    if (any && nvalid > 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
-                            if (j < nvalid && d <= tau) {
-                                const unsigned idx = atomicAdd(p.cand_cnt + q, 1u);
-                                if (idx < (unsigned)p.cap)
-                                    p.cand[(size_t)q * p.cap + idx] = make_key(d, tag0 + j);
-                            }
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
-                        if (qok && j < nvalid && d <= tau) mybuf[cnt++] = make_key(d, tag0 + j);
-                    }
+                for (int i4 = 0; i4 < 8; ++i4) {
+                    const float4 t4 = MET == MET_DOT
+                                          ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                                          : reinterpret_cast<const float4*>(
+                                                cvbuf + cs * TILE_N + c * 32)[i4];
+                    cv[4 * i4] = t4.x;
+                    cv[4 * i4 + 1] = t4.y;
+                    cv[4 * i4 + 2] = t4.z;
+                    cv[4 * i4 + 3] = t4.w;
                 }
-                if (EPI == EPI_SHORTLIST) {
-                    // fold full buffers into their top-32 lists, one query at a time
-                    unsigned full;
-                    while ((full = __ballot_sync(0xffffffffu, cnt >= 32)) != 0) {
-                        const int leader = __ffs(full) - 1;
-                        const int lq = __shfl_sync(0xffffffffu, q, leader);
-                        const int lc = __shfl_sync(0xffffffffu, cnt, leader);
-                        uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
-                        uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
-                        __syncwarp();
-                        const uint64_t kth = merge_into(lst, lbuf, 32, lane);
-                        __syncwarp();
-                        const uint64_t rest = (lane + 32 < lc) ? lbuf[lane + 32] : KEY_NONE;
-                        __syncwarp();
-                        if (lane + 32 < lc) lbuf[lane] = rest;
-                        __syncwarp();
-                        if (lane == leader) {
-                            cnt -= 32;
-                            if (kth != KEY_NONE) {
-                                tau = fminf(tau, key_dist(kth));
-                                atomicMin(p.tau_g + lq, (unsigned)(kth >> 32));
-                            }
+                const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                    if (qok && j < nvalid && d <= tau) mybuf[cnt++] = make_key(d, tag0 + j);
+                }
+                // fold full buffers into their top-32 lists, one query at a time
+                unsigned full;
+                while ((full = __ballot_sync(0xffffffffu, cnt >= 32)) != 0) {
+                    const int leader = __ffs(full) - 1;
+                    const int lq = __shfl_sync(0xffffffffu, q, leader);
+                    const int lc = __shfl_sync(0xffffffffu, cnt, leader);
+                    uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
+                    uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+                    __syncwarp();
+                    const uint64_t kth = merge_into(lst, lbuf, 32, lane);
+                    __syncwarp();
+                    const uint64_t rest = (lane + 32 < lc) ? lbuf[lane + 32] : KEY_NONE;
+                    __syncwarp();
+                    if (lane + 32 < lc) lbuf[lane] = rest;
+                    __syncwarp();
+                    if (lane == leader) {
+                        cnt -= 32;
+                        if (kth != KEY_NONE) {
+                            tau = fminf(tau, key_dist(kth));
+                            atomicMin(p.tau_g + lq, (unsigned)(kth >> 32));
                         }
                     }
                 }
             }
+            // done with the staged column values of this tile
+            __syncwarp();
+            if (STAGE_CV && lane == 0) mbar_arrive(cv_empty + cs);
         }
         if (EPI == EPI_SHORTLIST) {
             unsigned left;
@@ -589,7 +583,7 @@ __global__ void to_half_kernel(const float* __restrict__ x, size_t n, int dim, i
 size_t gemm_smem(int katoms, int epi) {
     const int nstage = tc::b_stages(katoms, epi);
     return 1024 + (size_t)(1 + nstage) * katoms * tc::ATOM_BYTES +
-           (epi == tc::EPI_FILTER ? (size_t)tc::NCV * tc::TILE_N * 4 : 0) +
+           (size_t)tc::NCV * tc::TILE_N * 4 +
            (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) +
            (tc::NBARS + 1) * 8;
 }
