@@ -154,7 +154,12 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA atoms
     float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * ATOM_BYTES);  // [NCV][TILE_N]
     uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + NCV * TILE_N);
-    uint64_t* bars = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
+    // sample pass: each query row's top-32 list of this block's chunk is kept
+    // in shared memory while the block runs (one global write at the end)
+    // when it fits beside the operand tiles (padded dim <= 192)
+    const bool use_sl = EPI == EPI_SHORTLIST && KA <= 3;
+    uint64_t* slists = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
+    uint64_t* bars = slists + (use_sl ? TILE_M * SAMPLE_K : 0);
     uint64_t* a_full = bars + 0;
     uint64_t* b_full = a_full + 1;              // [MAX_STAGES]
     uint64_t* b_empty = b_full + MAX_STAGES;    // [MAX_STAGES]
@@ -283,6 +288,16 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                                       : __int_as_float(0x7f800000);
         int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
         uint64_t* mybuf = cbuf + e * BUF_CAP;
+        // the top-32 list of a row of this warp (leader: its lane)
+        auto row_list = [&](int leader, int lq) -> uint64_t* {
+            return use_sl ? slists + (size_t)(e - lane + leader) * SAMPLE_K
+                          : p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+        };
+        if (use_sl) {
+#pragma unroll 4
+            for (int i2 = 0; i2 < SAMPLE_K; ++i2) slists[(size_t)e * SAMPLE_K + i2] = KEY_NONE;
+            __syncwarp();
+        }
         if constexpr (EPI == EPI_FILTER) {
             // Per-lane admission test, one or two instructions per score:
             //   L2 : fma(-2, s, ||x||^2) <= (tau - ||q||^2) + slack
@@ -456,10 +471,25 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                     cv[4 * i4 + 3] = t4.w;
                 }
                 const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
+                // once tau is tight most chunks hold no value <= tau for any lane:
+                // one vote on the chunk's smallest value skips the appends
+                float x[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float d = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
-                    if (qok && j < nvalid && d <= tau) mybuf[cnt++] = make_key(d, tag0 + j);
+                for (int j = 0; j < 32; ++j) x[j] = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                float t11[11];
+#pragma unroll
+                for (int k3 = 0; k3 < 10; ++k3)
+                    t11[k3] = min3f(x[3 * k3], x[3 * k3 + 1], x[3 * k3 + 2]);
+                t11[10] = fminf(x[30], x[31]);
+                const float mn = fminf(min3f(min3f(t11[0], t11[1], t11[2]),
+                                             min3f(t11[3], t11[4], t11[5]),
+                                             min3f(t11[6], t11[7], t11[8])),
+                                       fminf(t11[9], t11[10]));
+                // (NaN never passes d <= tau, as in the appends below)
+                if (__any_sync(0xffffffffu, qok && mn <= tau)) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (qok && j < nvalid && x[j] <= tau) mybuf[cnt++] = make_key(x[j], tag0 + j);
                 }
                 // fold full buffers into their top-32 lists, one query at a time
                 unsigned full;
@@ -468,7 +498,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                     const int lq = __shfl_sync(0xffffffffu, q, leader);
                     const int lc = __shfl_sync(0xffffffffu, cnt, leader);
                     uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
-                    uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+                    uint64_t* lst = row_list(leader, lq);
                     __syncwarp();
                     const uint64_t kth = merge_into(lst, lbuf, 32, lane);
                     __syncwarp();
@@ -496,11 +526,21 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                 const int lq = __shfl_sync(0xffffffffu, q, leader);
                 const int lc = __shfl_sync(0xffffffffu, cnt, leader);
                 uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
-                uint64_t* lst = p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
+                uint64_t* lst = row_list(leader, lq);
                 __syncwarp();
                 merge_into(lst, lbuf, lc, lane);
                 __syncwarp();
                 if (lane == leader) cnt = 0;
+            }
+            if (use_sl) {
+                // the warp's 32 lists to global memory, one row per step
+                __syncwarp();
+                for (int r2 = 0; r2 < 32; ++r2) {
+                    const int qr = qb * TILE_M + (e - lane + r2);
+                    if (qr < p.nq)
+                        p.part[((size_t)blockIdx.y * p.nq + qr) * SAMPLE_K + lane] =
+                            slists[(size_t)(e - lane + r2) * SAMPLE_K + lane];
+                }
             }
         }
     }
@@ -585,6 +625,7 @@ size_t gemm_smem(int katoms, int epi) {
     return 1024 + (size_t)(1 + nstage) * katoms * tc::ATOM_BYTES +
            (size_t)tc::NCV * tc::TILE_N * 4 +
            (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) +
+           (epi == tc::EPI_SHORTLIST && katoms <= 3 ? (size_t)tc::TILE_M * tc::SAMPLE_K * 8 : 0) +
            (tc::NBARS + 1) * 8;
 }
 
