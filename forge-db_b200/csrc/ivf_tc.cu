@@ -1248,10 +1248,10 @@ struct CertParams {
 
 constexpr int CERT_WARPS = 8;
 #ifndef FDB_IVF_EXT_MAX
-#define FDB_IVF_EXT_MAX 256
+#define FDB_IVF_EXT_MAX 1024
 #endif
 constexpr unsigned EXT_MAX = FDB_IVF_EXT_MAX;  // entries an extension may rescore
-constexpr int EXT_THREADS = 256;
+constexpr int EXT_THREADS = 1024;
 constexpr int EXT_MAX_TAKE = 256;  // probes per query an extension handles
 static_assert(EXT_MAX <= (unsigned)EXT_THREADS, "one thread rescores one collected entry");
 

@@ -399,11 +399,12 @@ def test_ivfpq_tensor_mode_ties_and_short_lists(fg, ctx, orc):
 def test_ivfpq_tensor_mode_rescan_rounds(fg, ctx, orc):
     """The exact re-scan runs from counts kept on the device, in rounds of at
     most 64 MiB of per-unit keys (131072 units at k = 64).  8200 queries x 16
-    probes can produce more units than one round holds; runs of 400 identical
-    codes exceed both the shortlist and the extension, so queries re-scan."""
+    probes can produce more units than one round holds; runs of 1200 identical
+    codes exceed both the shortlist and the extension (1024 entries), so
+    queries re-scan."""
     rng = np.random.default_rng(33)
     base = (rng.random((25, 64), dtype=np.float32) * 10).astype(np.float32)
-    X = np.repeat(base, 400, axis=0)
+    X = np.repeat(base, 1200, axis=0)
     ix = fg.IVFPQIndex.build(X, 16, 8, ctx=ctx, seed=3)
     ix.set_scan_mode(ix.SCAN_TENSOR)
     ix.set_nprobe(16)

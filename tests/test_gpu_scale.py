@@ -31,11 +31,11 @@ def fg():
 def long_lists(fg, ctx, orc):
     from forgegpu.datasets import gmm_descriptors
     X = gmm_descriptors(200_000, components=128, seed=21)
-    # crowds: 600 copies each of 10 rows (more identical codes than the
-    # 64-entry shortlist and the 256 entries an extension rescores), placed
+    # crowds: 1200 copies each of 10 rows (more identical codes than the
+    # 64-entry shortlist and the 1024 entries an extension rescores), placed
     # among the others
     crowd = gmm_descriptors(10, components=128, seed=23)
-    X = np.concatenate([X[:100_000], np.repeat(crowd, 600, axis=0), X[100_000:]])
+    X = np.concatenate([X[:100_000], np.repeat(crowd, 1200, axis=0), X[100_000:]])
     Q = gmm_descriptors(2000, components=128, seed=22)
     ix = fg.IVFPQIndex.build(X, 128, 16, ctx=ctx, seed=7)
     cents, cb, offs, ids, codes = ix.export()
@@ -64,8 +64,8 @@ def test_tensor_path_long_lists(fg, orc, long_lists, nprobe, k):
 
 def test_tensor_path_long_lists_take_every_fallback(fg, orc, long_lists):
     """Over the whole batch the certificate extension and the exact re-scan
-    both run: queries next to a crowd of 600 identical codes cannot be
-    certified from 64 shortlisted entries nor by extending over 256."""
+    both run: queries next to a crowd of 1200 identical codes cannot be
+    certified from 64 shortlisted entries nor by extending over 1024."""
     ix, ox, X, Q, _, crowd = long_lists
     ix.set_scan_mode(ix.SCAN_TENSOR)
     ix.set_nprobe(32)
