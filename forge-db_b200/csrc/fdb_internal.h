@@ -339,7 +339,7 @@ void shard_plan(const uint64_t* sizes, size_t nlist, int world, int* owner);
 // threshold, filter pass, top-kp selection) and its exact rescoring.
 struct GemmScratch {
     DevBuf<uint64_t> part, top32, cand, approx;
-    DevBuf<unsigned> tau_bits, cand_cnt;
+    DevBuf<unsigned> tau_bits, cand_cnt, seg_cnt;
     DevBuf<float> tau;
     int cap = 0;
     int* err = nullptr;  // device error word (timeouts)

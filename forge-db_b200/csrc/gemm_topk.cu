@@ -61,9 +61,16 @@ constexpr int NBARS = 1 + 2 * MAX_STAGES + 8 + 2 * NCV;
 
 // B pipeline stages: the filter pass keeps more tiles in flight (its shared
 // memory holds no candidate buffers); at most ~200 KB in every case.
-__host__ __device__ constexpr int b_stages(int katoms, int epi) {
-    return epi == EPI_FILTER ? (katoms <= 2 ? 4 : (katoms == 3 ? 3 : 2)) : (katoms <= 3 ? 2 : 1);
+__host__ __device__ constexpr int b_stages(int katoms, int epi, int bn) {
+    return epi == EPI_FILTER
+               ? (bn == 256 ? (katoms == 1 ? 4 : 2) : (katoms <= 2 ? 4 : (katoms == 3 ? 3 : 2)))
+               : (katoms <= 3 ? 2 : 1);
 }
+// The filter pass's B tile height: 256 rows (one N = 256 MMA per K step:
+// the A tile is read from shared memory once per 256 rows instead of once
+// per 128, which with the TMA writes is what bounds the MMA rate) where the
+// stages fit, i.e. padded dim <= 128; else 128.
+__host__ __device__ constexpr int filter_bn(int katoms) { return katoms <= 2 ? 256 : 128; }
 
 struct GemmTopkParams {
     int nq;              // queries
@@ -83,6 +90,8 @@ struct GemmTopkParams {
     const float* tau_q;  // [nq] admission threshold
     uint64_t* cand;      // [nq][cap] candidate keys
     unsigned* cand_cnt;  // [nq] candidates seen (may exceed cap)
+    int seg;             // FILTER: entries of a (query, row chunk) segment of the candidate row
+    unsigned* seg_cnt;   // FILTER: [nq][chunks] entries each block found (may exceed seg)
     int cap;
     int* err;            // error word (0 = ok)
     unsigned long long wait;  // limit of each bounded wait, SM clock cycles
@@ -135,29 +144,34 @@ __device__ __forceinline__ uint64_t merge_into(uint64_t* list, const uint64_t* l
     return tk.thr;
 }
 
-template <int EPI, int MET>
+// BN: rows of the B tile per MMA (128, or 256 for the filter pass).
+template <int EPI, int MET, int BN>
 __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 1)
     gemm_topk_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, GemmTopkParams p) {
+    static_assert(BN == 128 || (BN == 256 && EPI == EPI_FILTER), "tile height");
+    constexpr int BATOM = BN * 128;  // bytes of one 64-wide K atom of the B tile
+    constexpr uint32_t IDESC_BN = (1u << 4) | ((uint32_t)(BN >> 3) << 17) |
+                                  ((uint32_t)(TILE_M >> 4) << 24);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
     unsigned char* smem = smem_raw + ((1024 - (base & 1023)) & 1023);  // 1024-byte aligned
     const int KA = p.katoms;
-    const int NSTAGE = b_stages(KA, EPI);
-    // TMEM accumulators (128 columns each): the filter pass lets the MMA run
-    // up to three tiles ahead of its epilogue
-    constexpr int NACC = EPI == EPI_FILTER ? 4 : 2;
+    const int NSTAGE = b_stages(KA, EPI, BN);
+    // TMEM accumulators (BN columns each, 512 columns in all for the filter
+    // pass): the MMA runs ahead of the epilogue by NACC - 1 tiles
+    constexpr int NACC = EPI == EPI_FILTER ? 512 / BN : 2;
     // each tile's column values (||x||^2 or 1/||x||) are staged in shared
     // memory by a bulk copy that the producer issues with the tile
     constexpr bool STAGE_CV = MET != MET_DOT;
     unsigned char* a_tile = smem;                                  // KA atoms
-    unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA atoms
-    float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * ATOM_BYTES);  // [NCV][TILE_N]
-    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + NCV * TILE_N);
+    unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA B atoms
+    float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * BATOM);  // [NCV][BN]
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + NCV * BN);
     // sample pass: each query row's top-32 list of this block's chunk is kept
     // in shared memory while the block runs (one global write at the end)
-    // when it fits beside the operand tiles (padded dim <= 192)
-    const bool use_sl = EPI == EPI_SHORTLIST && KA <= 3;
+    // when it fits beside the operand tiles (padded dim <= 128)
+    const bool use_sl = EPI == EPI_SHORTLIST && KA <= 2;
     uint64_t* slists = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
     uint64_t* bars = slists + (use_sl ? TILE_M * SAMPLE_K : 0);
     uint64_t* a_full = bars + 0;
@@ -169,17 +183,23 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     uint64_t* cv_empty = cv_full + NCV;         // [NCV]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
 
+    // filter pass: the hits of each query row of this block go to the block's
+    // own segment of the query's candidate row, counted here (shared-memory
+    // atomics instead of one global atomic per row and group)
+    __shared__ unsigned qcnt[TILE_M];
+    if (EPI == EPI_FILTER && threadIdx.x < TILE_M) qcnt[threadIdx.x] = 0u;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qb = blockIdx.x;
     const size_t r0 = (size_t)blockIdx.y * p.rows_per_chunk;
     const size_t r1 = min(p.n, r0 + p.rows_per_chunk);
-    const int ntiles = r0 < r1 ? (int)((r1 - r0 + TILE_N - 1) / TILE_N) : 0;
+    const int ntiles = r0 < r1 ? (int)((r1 - r0 + BN - 1) / BN) : 0;
     // tiles this block processes: t = first + i * stride, i < count
     const int stride = EPI == EPI_SHORTLIST ? p.tile_stride : 1;
-    const int tile0 = (int)(r0 / TILE_N);
+    const int tile0 = (int)(r0 / BN);
     const int first = (stride - tile0 % stride) % stride;
     const int count = ntiles > first ? (ntiles - first + stride - 1) / stride : 0;
-    const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);
+    const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);  // the A tile
+    const uint32_t bstage_bytes = (uint32_t)(KA * BATOM);
     const int n_epi_warps = EPI == EPI_SHORTLIST ? 4 : 16;
 
     if (threadIdx.x == 0) {
@@ -201,7 +221,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(NACC * TILE_N));
+                     "r"(NACC * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         tc_fence_before();
     }
@@ -226,19 +246,25 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                 const int s = i % NSTAGE;
                 const int use = i / NSTAGE;
                 if (i >= NSTAGE && !mbar_wait(b_empty + s, (use - 1) & 1, p.err, p.wait)) break;
-                mbar_expect_tx(b_full + s, stage_bytes);
-                const int row = (int)(r0 + (size_t)(first + i * stride) * TILE_N);
-                unsigned char* dst = b_tile + s * KA * ATOM_BYTES;
+                mbar_expect_tx(b_full + s, bstage_bytes);
+                const int row = (int)(r0 + (size_t)(first + i * stride) * BN);
+                unsigned char* dst = b_tile + s * KA * BATOM;
+                // a 256-row atom is two stacked 128-row boxes (the swizzle
+                // repeats every 8 rows, so the halves join seamlessly); rows
+                // past the end of the rows read as zeros
                 for (int a = 0; a < KA; ++a)
-                    tma_load_2d(dst + a * ATOM_BYTES, &xmap, b_full + s, a * KATOM, row);
+#pragma unroll
+                    for (int hb = 0; hb < BN / TILE_N; ++hb)
+                        tma_load_2d(dst + a * BATOM + hb * ATOM_BYTES, &xmap, b_full + s,
+                                    a * KATOM, row + hb * TILE_N);
                 last_load[s] = use;
                 if (STAGE_CV) {
-                    // the tile's 128 column values (colv is padded to whole tiles;
-                    // row is a multiple of 128, so the copy is 512-byte aligned)
+                    // the tile's BN column values (colv is padded by 256 beyond
+                    // its rows; row is a multiple of BN, so the copy is aligned)
                     const int c = i % NCV, cu = i / NCV;
                     if (i >= NCV && !mbar_wait(cv_empty + c, (cu - 1) & 1, p.err, p.wait)) break;
-                    mbar_expect_tx(cv_full + c, TILE_N * 4);
-                    bulk_load(cvbuf + c * TILE_N, p.colv + row, TILE_N * 4, cv_full + c);
+                    mbar_expect_tx(cv_full + c, BN * 4);
+                    bulk_load(cvbuf + c * BN, p.colv + row, BN * 4, cv_full + c);
                     last_cv[c] = cu;
                 }
             }
@@ -255,15 +281,15 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                     break;
                 if (!mbar_wait(b_full + s, use & 1, p.err, p.wait)) break;
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(b * TILE_N);
+                const uint32_t d = tmem + (uint32_t)(b * BN);
                 const uint32_t abase = smem_u32(a_tile);
-                const uint32_t bbase = smem_u32(b_tile + s * KA * ATOM_BYTES);
+                const uint32_t bbase = smem_u32(b_tile + s * KA * BATOM);
                 for (int a = 0; a < KA; ++a) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {  // 4 x K16 per 64-wide atom
-                        const uint32_t off = (uint32_t)(a * ATOM_BYTES + kk * 32);
-                        umma_f16(d, smem_desc_sw128(abase + off), smem_desc_sw128(bbase + off),
-                                 (a | kk) != 0);
+                        umma_f16_n(d, smem_desc_sw128(abase + (uint32_t)(a * ATOM_BYTES + kk * 32)),
+                                   smem_desc_sw128(bbase + (uint32_t)(a * BATOM + kk * 32)),
+                                   IDESC_BN, (a | kk) != 0);
                     }
                 }
                 umma_commit(b_empty + s);  // stage s may be refilled once these MMAs finish
@@ -275,7 +301,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
         // ---------------- epilogue ----------------
         const int w = warp - EPI_WARP0;
         const int quad = w & 3;            // TMEM lane quadrant = warp % 4
-        const int part = w >> 2;           // FILTER: 32-column chunk of this warp
+        const int part = w >> 2;           // FILTER: BN/4-column part of each tile
         const int e = quad * 32 + lane;    // query row in the block
         const int q = qb * TILE_M + e;
         const bool qok = q < p.nq;
@@ -283,7 +309,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
         const float qn = MET == MET_COS ? (qn0 > 0.0f ? rsqrtf(qn0) : 0.0f) : qn0;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const int c0 = EPI == EPI_SHORTLIST ? 0 : part;
-        const int c1 = EPI == EPI_SHORTLIST ? TILE_N / 32 : part + 1;
+        const int c1 = EPI == EPI_SHORTLIST ? BN / 32 : part + 1;
         float tau = EPI == EPI_FILTER ? (qok ? p.tau_q[q] : -__int_as_float(0x7f800000))
                                       : __int_as_float(0x7f800000);
         int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
@@ -378,7 +404,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
             auto admit = [&](unsigned gm, uint32_t tcol, const float* cvs, size_t cbase) {
                 const int nvalid = cbase < r1 ? (int)min((size_t)32, r1 - cbase) : 0;
                 const uint32_t tag = (uint32_t)(p.tag_base + cbase);
-                uint64_t* crow = p.cand + (size_t)q * p.cap;
+                uint64_t* crow = p.cand + (size_t)q * p.cap + (size_t)blockIdx.y * p.seg;
                 while (gm) {
                     const int gi = __ffs(gm) - 1;
                     gm &= gm - 1;
@@ -394,11 +420,11 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                         if (qok && j < nvalid && d[jj] <= tau) hm |= 1u << jj;
                     }
                     if (hm == 0) continue;
-                    unsigned ix = atomicAdd(p.cand_cnt + q, (unsigned)__popc(hm));
+                    unsigned ix = atomicAdd(qcnt + e, (unsigned)__popc(hm));
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj)
                         if (hm >> jj & 1u) {
-                            if (ix < (unsigned)p.cap)
+                            if (ix < (unsigned)p.seg)
                                 crow[ix] = make_key(d[jj], tag + (uint32_t)(gi * 8 + jj));
                             ++ix;
                         }
@@ -413,13 +439,19 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                 got = __shfl_sync(0xffffffffu, got, 0);
                 if (!got) break;
                 tc_fence_after();
-                const uint32_t tcol = (uint32_t)(b * TILE_N + part * 32);
-                uint32_t va[32];
-                tmem_ld32_nowait(tmem + lane_base + tcol, va);
-                tmem_wait_regs(va);
-                const float* cvs = cvbuf + c * TILE_N + part * 32;
-                const unsigned gm = test(va, cvs);
-                if (gm) admit(gm, tcol, cvs, r0 + (size_t)i * TILE_N + (size_t)part * 32);
+                // this warp's BN/4 columns of the tile, 32 at a time (one copy
+                // of the test and slow path: the loop is not unrolled)
+#pragma unroll 1
+                for (int hc = 0; hc < BN / 128; ++hc) {
+                    const int col = part * (BN / 4) + hc * 32;
+                    const uint32_t tcol = (uint32_t)(b * BN + col);
+                    uint32_t va[32];
+                    tmem_ld32_nowait(tmem + lane_base + tcol, va);
+                    tmem_wait_regs(va);
+                    const float* cvs = cvbuf + c * BN + col;
+                    const unsigned gm = test(va, cvs);
+                    if (gm) admit(gm, tcol, cvs, r0 + (size_t)i * BN + (size_t)col);
+                }
                 // done with the accumulator and the staged column values
                 tc_fence_before();
                 __syncwarp();
@@ -444,11 +476,11 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                 const unsigned g = *(volatile unsigned*)(p.tau_g + q);
                 if (g != 0xffffffffu) tau = fminf(tau, ord2f(g));
             }
-            const size_t rb = r0 + (size_t)(first + i * stride) * TILE_N;
+            const size_t rb = r0 + (size_t)(first + i * stride) * BN;
 #pragma unroll 1
             for (int c = c0; c < c1; ++c) {
                 uint32_t v[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)(b * TILE_N + c * 32), v);
+                tmem_ld32(tmem + lane_base + (uint32_t)(b * BN + c * 32), v);
                 if (c == c1 - 1) {
                     // all of this warp's columns of buffer b are in registers
                     tc_fence_before();
@@ -464,7 +496,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                     const float4 t4 = MET == MET_DOT
                                           ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
                                           : reinterpret_cast<const float4*>(
-                                                cvbuf + cs * TILE_N + c * 32)[i4];
+                                                cvbuf + cs * BN + c * 32)[i4];
                     cv[4 * i4] = t4.x;
                     cv[4 * i4 + 1] = t4.y;
                     cv[4 * i4 + 2] = t4.z;
@@ -576,8 +608,43 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(NACC * TILE_N));
+                     "r"(NACC * BN));
     }
+    if (EPI == EPI_FILTER && threadIdx.x < TILE_M) {
+        // (every epilogue warp is past the block-wide barrier above)
+        const int qq = qb * TILE_M + (int)threadIdx.x;
+        if (qq < p.nq) p.seg_cnt[(size_t)qq * gridDim.y + blockIdx.y] = qcnt[threadIdx.x];
+    }
+}
+
+// One warp per query: the filter pass's per-block segments of its candidate
+// row moved to the row's front (in block order, a forward copy: a segment's
+// destination never passes its source), and the count; a segment that
+// overflowed marks the row as overflowing (count cap + 1: never certified).
+__global__ void __launch_bounds__(256)
+    compact_segments_kernel(uint64_t* __restrict__ cand, const unsigned* __restrict__ seg_cnt,
+                            int chunks, int seg, int cap, int nq, unsigned* __restrict__ cnt) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + warp;
+    if (q >= nq) return;
+    uint64_t* row = cand + (size_t)q * cap;
+    unsigned total = 0;
+    bool over = false;
+    for (int y = 0; y < chunks; ++y) {
+        const unsigned c = seg_cnt[(size_t)q * chunks + y];
+        over = over || c > (unsigned)seg;
+        const unsigned n = min(c, (unsigned)seg);
+        const size_t src = (size_t)y * seg;
+        if (src != total)
+            for (unsigned i = 0; i < n; i += 32) {
+                const uint64_t v = i + lane < n ? row[src + i + lane] : 0;
+                __syncwarp();
+                if (i + lane < n) row[total + i + lane] = v;
+                __syncwarp();
+            }
+        total += n;
+    }
+    if (lane == 0) cnt[q] = over ? (unsigned)cap + 1u : total;
 }
 
 // Top-kp of each query's candidate keys (one warp per query).
@@ -620,12 +687,12 @@ __global__ void to_half_kernel(const float* __restrict__ x, size_t n, int dim, i
     out[t] = __float2half_rn(c < dim ? x[r * dim + c] : 0.0f);
 }
 
-size_t gemm_smem(int katoms, int epi) {
-    const int nstage = tc::b_stages(katoms, epi);
-    return 1024 + (size_t)(1 + nstage) * katoms * tc::ATOM_BYTES +
-           (size_t)tc::NCV * tc::TILE_N * 4 +
+size_t gemm_smem(int katoms, int epi, int bn) {
+    const int nstage = tc::b_stages(katoms, epi, bn);
+    return 1024 + (size_t)katoms * tc::ATOM_BYTES + (size_t)nstage * katoms * bn * 128 +
+           (size_t)tc::NCV * bn * 4 +
            (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) +
-           (epi == tc::EPI_SHORTLIST && katoms <= 3 ? (size_t)tc::TILE_M * tc::SAMPLE_K * 8 : 0) +
+           (epi == tc::EPI_SHORTLIST && katoms <= 2 ? (size_t)tc::TILE_M * tc::SAMPLE_K * 8 : 0) +
            (tc::NBARS + 1) * 8;
 }
 
@@ -646,7 +713,8 @@ int pick_chunks(size_t n, int nq, int sm_count, size_t* rows_per_chunk) {
         }
     }
     size_t rows = (n + best_r - 1) / best_r;
-    rows = (rows + tc::TILE_N - 1) / tc::TILE_N * tc::TILE_N;
+    // a multiple of 256 rows: whole filter-pass tiles (and sample-pass tiles)
+    rows = (rows + 255) / 256 * 256;
     *rows_per_chunk = rows;
     return (int)((n + rows - 1) / rows);
 }
@@ -654,12 +722,18 @@ int pick_chunks(size_t n, int nq, int sm_count, size_t* rows_per_chunk) {
 template <int EPI, int MET>
 void launch_pass_m(cudaStream_t s, const CUtensorMap& qm, const CUtensorMap& xm, int nq,
                    int chunks, const tc::GemmTopkParams& p) {
-    const size_t smem = gemm_smem(p.katoms, EPI);
-    FDB_CUDA(cudaFuncSetAttribute(tc::gemm_topk_kernel<EPI, MET>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((unsigned)((nq + tc::TILE_M - 1) / tc::TILE_M), (unsigned)chunks);
-    tc::gemm_topk_kernel<EPI, MET>
-        <<<grid, EPI == tc::EPI_FILTER ? tc::THREADS_FILTER : tc::THREADS, smem, s>>>(qm, xm, p);
+    const unsigned threads = EPI == tc::EPI_FILTER ? tc::THREADS_FILTER : tc::THREADS;
+    auto go = [&](auto kernel, int bn) {
+        const size_t smem = gemm_smem(p.katoms, EPI, bn);
+        FDB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+        kernel<<<grid, threads, smem, s>>>(qm, xm, p);
+    };
+    if (EPI == tc::EPI_FILTER && tc::filter_bn(p.katoms) == 256)
+        go(tc::gemm_topk_kernel<EPI, MET, (EPI == tc::EPI_FILTER ? 256 : 128)>, 256);
+    else
+        go(tc::gemm_topk_kernel<EPI, MET, 128>, 128);
     FDB_LAUNCH_CHECK();
 }
 
@@ -723,10 +797,14 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     tc::sample_tau_kernel<<<(nq + 255) / 256, 256, 0, s>>>(w.top32.p, nq, w.tau.p);
     FDB_LAUNCH_CHECK();
     // --- filter pass ---
-    w.cap = std::max(1024, 16 * kp);
+    // each row chunk's block owns a segment of every candidate row
+    const int seg = std::max(32, std::max(1024, 16 * kp) / chunks);
+    w.cap = seg * chunks;
     w.cand.ensure((size_t)nq * w.cap);
     w.cand_cnt.ensure(nq);
-    FDB_CUDA(cudaMemsetAsync(w.cand_cnt.p, 0, (size_t)nq * 4, s));
+    w.seg_cnt.ensure((size_t)nq * chunks);
+    p.seg = seg;
+    p.seg_cnt = w.seg_cnt.p;
     p.tile_stride = 1;
     p.tau_q = w.tau.p;
     p.cand = w.cand.p;
@@ -735,6 +813,9 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     if (w.filter_ev0) FDB_CUDA(cudaEventRecord(w.filter_ev0, s));
     launch_pass<tc::EPI_FILTER>(s, qm, xm, nq, chunks, p);
     if (w.filter_ev1) FDB_CUDA(cudaEventRecord(w.filter_ev1, s));
+    tc::compact_segments_kernel<<<(unsigned)((nq + 7) / 8), 256, 0, s>>>(
+        w.cand.p, w.seg_cnt.p, chunks, seg, w.cap, nq, w.cand_cnt.p);
+    FDB_LAUNCH_CHECK();
     // --- top-kp of the candidates ---
     w.approx.ensure((size_t)nq * kp);
     const unsigned grid = (unsigned)((nq + 7) / 8);

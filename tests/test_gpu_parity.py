@@ -492,7 +492,8 @@ def test_bf_tensor_path_certifies_and_matches(fg, ctx, orc, metric):
     assert np.array_equal(d1, d2)
 
 
-@pytest.mark.parametrize("n,dim,nq", [(129, 64, 1), (1000, 96, 130), (5000, 200, 257)])
+@pytest.mark.parametrize("n,dim,nq", [(129, 64, 1), (1000, 96, 130), (3000, 160, 200),
+                                      (5000, 200, 257)])
 def test_bf_tensor_ragged_shapes(fg, ctx, orc, n, dim, nq):
     """Row counts and query counts off the 128 tile, dims padded to 64/256."""
     rng = np.random.default_rng(n)
