@@ -95,3 +95,22 @@ def test_no_gpu_fails_cleanly():
     with pytest.raises(fg.ForgeGpuError) as e:
         fg.Context(0)
     assert e.value.code in (-1, -7)
+
+
+def test_tuning_switches_reject_null_handles():
+    """The switches and deadlines of the C ABI fail with FDB_ERR_INVALID_ARG
+    on a NULL handle (no device needed)."""
+    import ctypes as C
+    import forgegpu as fg
+    L = fg.lib()
+    div = C.c_int64()
+    calls = [
+        lambda: L.fdb_ivfpq_set_stage_timers(None, 0),
+        lambda: L.fdb_ivfpq_set_graphs(None, 1),
+        lambda: L.fdb_ivfpq_set_pass1_quota(None, 32, 64),
+        lambda: L.fdb_ivfpq_get_pass1_quota(None, 32, C.byref(div)),
+        lambda: L.fdb_ctx_set_wait_limit(None, 1.0),
+        lambda: L.fdb_ctx_test_stall_scans(None, 1),
+    ]
+    for call in calls:
+        assert call() == -1
