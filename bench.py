@@ -169,8 +169,9 @@ SCALING = "strong"     # the batch and the index are fixed as N grows
 # (config D: its traffic does not scale by a known factor).
 NCU_TRAFFIC = {"ivfpq_config_c": 87.5e6, "ivfpq_config_d": None, "bf_config_b": None}
 # brute force, tensor path: row norms, query to fp16, sample pass, merge, tau,
-# filter pass, candidate selection, exact rescore, keys->ids, finalize
-BF_LAUNCHES = 10
+# filter pass, segment compaction, candidate selection, exact rescore,
+# keys->ids, finalize
+BF_LAUNCHES = 11
 
 
 DIST_RTOL, TIE_RTOL = 1e-4, 1e-5  # north_star: distances 1e-4 rel, near-ties 1e-5 rel
