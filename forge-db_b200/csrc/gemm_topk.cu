@@ -7,27 +7,28 @@
 //     L2^2   : ||q||^2 + ||x||^2 - 2 s
 //     dot    : -s
 //     cosine : 1 - s / sqrt(||q||^2 ||x||^2)
-// Two passes run on the same TMA -> MMA -> TMEM pipeline:
-//   SAMPLE: every S-th row tile only.  Each epilogue thread owns one query
-//     (the TMEM lane of its row); scores at or below the query's running
-//     threshold are buffered in shared memory and merged, a warp at a time,
-//     into the query's sorted top-32 in global memory.  Its 32nd distance is
-//     a per-query threshold tau that about 32*S rows of the full set pass.
-//   FILTER: every tile, sixteen epilogue warps (four per TMEM lane quadrant,
-//     one 32-column chunk each; the tile's column values staged in shared
-//     memory by the producer, four TMEM accumulators so the MMA runs ahead).
-//     A score costs half a packed FMA and a third of a three-input minimum;
-//     the 8-column groups that may hold a score <= tau are reloaded from
-//     TMEM and their hits appended to a per-query candidate array, one
-//     atomic per row and group.
+// Two passes run on the same TMA -> MMA -> TMEM pipeline, with sixteen
+// epilogue warps (four per TMEM lane quadrant, each a part of every tile's
+// columns) and the tile's column values staged in shared memory by the
+// producer:
+//   SAMPLE: every S-th 128-row tile only.  Each epilogue thread keeps the 8
+//     smallest keys of its row over its 32-column part, sorted in registers
+//     (a chunk whose smallest value cannot enter is skipped by one vote); the
+//     four parts' lists are the row's 32 entries for the block's row chunk,
+//     and the 32nd of their merge over all chunks is a per-query threshold
+//     tau that about 32*S rows of the full set pass.
+//   FILTER: every tile (256 rows for padded dims <= 128, one N = 256 MMA per
+//     K step, else 128).  A score costs half a packed FMA and a third of a
+//     three-input minimum; the 8-column groups that may hold a score <= tau
+//     are reloaded from TMEM and their hits appended to the block's segment
+//     of the query's candidate row, counted with shared-memory atomics.
 // select_candidates_kernel then takes the top-kp of each query's candidates
 // and bf_rescore_kernel recomputes them exactly in the reference's AVX2
 // summation order and certifies the result (see there), so returned
 // distances are exact and a bad tau or an overflow only costs a fallback.
 //
-// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner,
-// warps 4-7 (sample pass, 384 threads) or 4-19 (filter pass, 640 threads) =
-// epilogue.  Every wait on an mbarrier is bounded:
+// Warp roles (640 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 4-19 = epilogue.  Every wait on an mbarrier is bounded:
 // on timeout the kernel sets an error word, the other warps see it and
 // leave, in-flight copies and MMAs are waited for (bounded), TMEM is freed,
 // and the host reports FDB_ERR_TIMEOUT.
@@ -45,15 +46,13 @@
 namespace fdb {
 namespace tc {
 
-// Threads per block: the filter pass runs sixteen epilogue warps (four per
-// TMEM lane quadrant, one 32-column chunk of each tile apiece) so that the
-// latency of each warp's loads and candidate appends is hidden by the others.
-constexpr int THREADS = 384;
+// Threads per block: both passes run sixteen epilogue warps (four per TMEM
+// lane quadrant, one part of each tile's columns apiece) so that the latency
+// of each warp's loads and appends is hidden by the others.
 constexpr int THREADS_FILTER = 640;
 constexpr int EPI_WARP0 = 4;
 constexpr int SAMPLE_K = 32;  // sample-pass shortlist per query
 constexpr int EPI_SHORTLIST = 0, EPI_FILTER = 1;
-constexpr int BUF_CAP = 64;   // sample pass: buffered candidates per query
 constexpr int NCV = 4;        // filter pass: staged column-value slots (one per tile)
 constexpr int MAX_STAGES = 6; // B pipeline stages at most
 // mbarriers: a_full, b_full/b_empty [MAX_STAGES], t_full/t_empty [4], cv_full/cv_empty [NCV]
@@ -62,9 +61,7 @@ constexpr int NBARS = 1 + 2 * MAX_STAGES + 8 + 2 * NCV;
 // B pipeline stages: the filter pass keeps more tiles in flight (its shared
 // memory holds no candidate buffers); at most ~200 KB in every case.
 __host__ __device__ constexpr int b_stages(int katoms, int epi, int bn) {
-    return epi == EPI_FILTER
-               ? (bn == 256 ? (katoms == 1 ? 4 : 2) : (katoms <= 2 ? 4 : (katoms == 3 ? 3 : 2)))
-               : (katoms <= 3 ? 2 : 1);
+    return bn == 256 ? (katoms == 1 ? 4 : 2) : (katoms <= 2 ? 4 : (katoms == 3 ? 3 : 2));
 }
 // The filter pass's B tile height: 256 rows (one N = 256 MMA per K step:
 // the A tile is read from shared memory once per 256 rows instead of once
@@ -85,7 +82,6 @@ struct GemmTopkParams {
     // SAMPLE pass
     int tile_stride;     // process global tiles t with t % tile_stride == 0
     uint64_t* part;      // [chunks][nq][SAMPLE_K], preset to KEY_NONE
-    unsigned* tau_g;     // [nq] best known 32nd distance (orderable bits), preset ~0
     // FILTER pass
     const float* tau_q;  // [nq] admission threshold
     uint64_t* cand;      // [nq][cap] candidate keys
@@ -132,21 +128,9 @@ __device__ __forceinline__ void column_values(const float* colv, size_t row0, fl
     }
 }
 
-// Merge lcnt (<= 32) buffered keys into a sorted top-32 list in global
-// memory (one warp); returns the list's 32nd key.
-__device__ __forceinline__ uint64_t merge_into(uint64_t* list, const uint64_t* lbuf, int lcnt,
-                                               int lane) {
-    WarpTopK<1> tk;
-    tk.init(SAMPLE_K, nullptr);
-    tk.L[0] = list[lane];
-    tk.merge32(lane < lcnt ? lbuf[lane] : KEY_NONE);
-    list[lane] = tk.L[0];
-    return tk.thr;
-}
-
 // BN: rows of the B tile per MMA (128, or 256 for the filter pass).
 template <int EPI, int MET, int BN>
-__global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 1)
+__global__ void __launch_bounds__(THREADS_FILTER, 1)
     gemm_topk_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap xmap, GemmTopkParams p) {
     static_assert(BN == 128 || (BN == 256 && EPI == EPI_FILTER), "tile height");
@@ -160,20 +144,14 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     const int NSTAGE = b_stages(KA, EPI, BN);
     // TMEM accumulators (BN columns each, 512 columns in all for the filter
     // pass): the MMA runs ahead of the epilogue by NACC - 1 tiles
-    constexpr int NACC = EPI == EPI_FILTER ? 512 / BN : 2;
+    constexpr int NACC = 512 / BN;
     // each tile's column values (||x||^2 or 1/||x||) are staged in shared
     // memory by a bulk copy that the producer issues with the tile
     constexpr bool STAGE_CV = MET != MET_DOT;
     unsigned char* a_tile = smem;                                  // KA atoms
     unsigned char* b_tile = a_tile + KA * ATOM_BYTES;              // NSTAGE x KA B atoms
     float* cvbuf = reinterpret_cast<float*>(b_tile + NSTAGE * KA * BATOM);  // [NCV][BN]
-    uint64_t* cbuf = reinterpret_cast<uint64_t*>(cvbuf + NCV * BN);
-    // sample pass: each query row's top-32 list of this block's chunk is kept
-    // in shared memory while the block runs (one global write at the end)
-    // when it fits beside the operand tiles (padded dim <= 128)
-    const bool use_sl = EPI == EPI_SHORTLIST && KA <= 2;
-    uint64_t* slists = cbuf + (EPI == EPI_SHORTLIST ? TILE_M * BUF_CAP : 0);
-    uint64_t* bars = slists + (use_sl ? TILE_M * SAMPLE_K : 0);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(cvbuf + NCV * BN);
     uint64_t* a_full = bars + 0;
     uint64_t* b_full = a_full + 1;              // [MAX_STAGES]
     uint64_t* b_empty = b_full + MAX_STAGES;    // [MAX_STAGES]
@@ -200,7 +178,7 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
     const int count = ntiles > first ? (ntiles - first + stride - 1) / stride : 0;
     const uint32_t stage_bytes = (uint32_t)(KA * ATOM_BYTES);  // the A tile
     const uint32_t bstage_bytes = (uint32_t)(KA * BATOM);
-    const int n_epi_warps = EPI == EPI_SHORTLIST ? 4 : 16;
+    const int n_epi_warps = 16;
 
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
@@ -301,29 +279,15 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
         // ---------------- epilogue ----------------
         const int w = warp - EPI_WARP0;
         const int quad = w & 3;            // TMEM lane quadrant = warp % 4
-        const int part = w >> 2;           // FILTER: BN/4-column part of each tile
+        const int part = w >> 2;           // BN/4-column part of each tile
         const int e = quad * 32 + lane;    // query row in the block
         const int q = qb * TILE_M + e;
         const bool qok = q < p.nq;
         const float qn0 = (qok && p.qnorm) ? p.qnorm[q] : 0.0f;
         const float qn = MET == MET_COS ? (qn0 > 0.0f ? rsqrtf(qn0) : 0.0f) : qn0;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const int c0 = EPI == EPI_SHORTLIST ? 0 : part;
-        const int c1 = EPI == EPI_SHORTLIST ? BN / 32 : part + 1;
-        float tau = EPI == EPI_FILTER ? (qok ? p.tau_q[q] : -__int_as_float(0x7f800000))
-                                      : __int_as_float(0x7f800000);
-        int cnt = 0;  // SAMPLE: buffered candidates of this thread's query
-        uint64_t* mybuf = cbuf + e * BUF_CAP;
-        // the top-32 list of a row of this warp (leader: its lane)
-        auto row_list = [&](int leader, int lq) -> uint64_t* {
-            return use_sl ? slists + (size_t)(e - lane + leader) * SAMPLE_K
-                          : p.part + ((size_t)blockIdx.y * p.nq + lq) * SAMPLE_K;
-        };
-        if (use_sl) {
-#pragma unroll 4
-            for (int i2 = 0; i2 < SAMPLE_K; ++i2) slists[(size_t)e * SAMPLE_K + i2] = KEY_NONE;
-            __syncwarp();
-        }
+        const float tau = EPI == EPI_FILTER ? (qok ? p.tau_q[q] : -__int_as_float(0x7f800000))
+                                            : __int_as_float(0x7f800000);
         if constexpr (EPI == EPI_FILTER) {
             // Per-lane admission test, one or two instructions per score:
             //   L2 : fma(-2, s, ||x||^2) <= (tau - ||q||^2) + slack
@@ -460,54 +424,45 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                     if (STAGE_CV) mbar_arrive(cv_empty + c);
                 }
             }
-        } else
-        for (int i = 0; i < count; ++i) {
-            const int b = i % NACC, cs = i % NCV;
-            // one lane waits; the warp follows its verdict (tcgen05.ld is warp-wide)
-            int got = 0;
-            if (lane == 0)
-                got = mbar_wait(t_full + b, (i / NACC) & 1, p.err, p.wait) &&
-                      (!STAGE_CV || mbar_wait(cv_full + cs, (i / NCV) & 1, p.err, p.wait));
-            got = __shfl_sync(0xffffffffu, got, 0);
-            if (!got) break;
-            tc_fence_after();
-            if (qok) {
-                // Any chunk's top-32 bounds the global top-32 of the sample.
-                const unsigned g = *(volatile unsigned*)(p.tau_g + q);
-                if (g != 0xffffffffu) tau = fminf(tau, ord2f(g));
-            }
-            const size_t rb = r0 + (size_t)(first + i * stride) * BN;
-#pragma unroll 1
-            for (int c = c0; c < c1; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)(b * BN + c * 32), v);
-                if (c == c1 - 1) {
-                    // all of this warp's columns of buffer b are in registers
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(t_empty + b);
-                }
-                const size_t cb = rb + (size_t)c * 32;
-                const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
-                // the chunk's staged column values, eight 16-byte shared loads
-                float cv[32];
+        } else {
+            // Sample pass: each thread keeps the 8 smallest keys of its row over
+            // its 32-column part of the sampled tiles, sorted in registers.  The
+            // four parts' lists form the chunk's 32 entries for the row; the
+            // merged 32nd over all chunks is tau.  That is at least the 32nd of
+            // every sampled row (a part may hold more than 8 of the best 32), so
+            // at least 32 sampled rows lie at or below it.
+            uint64_t top[8];
 #pragma unroll
-                for (int i4 = 0; i4 < 8; ++i4) {
-                    const float4 t4 = MET == MET_DOT
-                                          ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
-                                          : reinterpret_cast<const float4*>(
-                                                cvbuf + cs * BN + c * 32)[i4];
-                    cv[4 * i4] = t4.x;
-                    cv[4 * i4 + 1] = t4.y;
-                    cv[4 * i4 + 2] = t4.z;
-                    cv[4 * i4 + 3] = t4.w;
-                }
-                const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
-                // once tau is tight most chunks hold no value <= tau for any lane:
-                // one vote on the chunk's smallest value skips the appends
+            for (int i2 = 0; i2 < 8; ++i2) top[i2] = KEY_NONE;
+            for (int i = 0; i < count; ++i) {
+                const int b = i % NACC, cs = i % NCV;
+                int got = 0;
+                if (lane == 0)
+                    got = mbar_wait(t_full + b, (i / NACC) & 1, p.err, p.wait) &&
+                          (!STAGE_CV || mbar_wait(cv_full + cs, (i / NCV) & 1, p.err, p.wait));
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) break;
+                tc_fence_after();
+                uint32_t v[32];
+                tmem_ld32_nowait(tmem + lane_base + (uint32_t)(b * BN + part * 32), v);
+                tmem_wait_regs(v);
+                const float* cvs = cvbuf + cs * BN + part * 32;
                 float x[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) x[j] = approx_metric<MET>(__uint_as_float(v[j]), qn, cv[j]);
+                for (int j = 0; j < 32; ++j)
+                    x[j] = approx_metric<MET>(__uint_as_float(v[j]), qn,
+                                              MET == MET_DOT ? 0.0f : cvs[j]);
+                // the scores and column values are in registers: release both
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(t_empty + b);
+                    if (STAGE_CV) mbar_arrive(cv_empty + cs);
+                }
+                const size_t cb = r0 + (size_t)(first + i * stride) * BN + (size_t)part * 32;
+                const int nvalid = cb < r1 ? (int)min((size_t)32, r1 - cb) : 0;
+                const uint32_t tag0 = (uint32_t)(p.tag_base + cb);
+                const float thr = top[7] == KEY_NONE ? __int_as_float(0x7f800000) : key_dist(top[7]);
                 float t11[11];
 #pragma unroll
                 for (int k3 = 0; k3 < 10; ++k3)
@@ -517,62 +472,27 @@ __global__ void __launch_bounds__(EPI == EPI_FILTER ? THREADS_FILTER : THREADS, 
                                              min3f(t11[3], t11[4], t11[5]),
                                              min3f(t11[6], t11[7], t11[8])),
                                        fminf(t11[9], t11[10]));
-                // (NaN never passes d <= tau, as in the appends below)
-                if (__any_sync(0xffffffffu, qok && mn <= tau)) {
+                if (!__any_sync(0xffffffffu, qok && nvalid > 0 && mn <= thr)) continue;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (qok && j < nvalid && x[j] <= tau) mybuf[cnt++] = make_key(x[j], tag0 + j);
-                }
-                // fold full buffers into their top-32 lists, one query at a time
-                unsigned full;
-                while ((full = __ballot_sync(0xffffffffu, cnt >= 32)) != 0) {
-                    const int leader = __ffs(full) - 1;
-                    const int lq = __shfl_sync(0xffffffffu, q, leader);
-                    const int lc = __shfl_sync(0xffffffffu, cnt, leader);
-                    uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
-                    uint64_t* lst = row_list(leader, lq);
-                    __syncwarp();
-                    const uint64_t kth = merge_into(lst, lbuf, 32, lane);
-                    __syncwarp();
-                    const uint64_t rest = (lane + 32 < lc) ? lbuf[lane + 32] : KEY_NONE;
-                    __syncwarp();
-                    if (lane + 32 < lc) lbuf[lane] = rest;
-                    __syncwarp();
-                    if (lane == leader) {
-                        cnt -= 32;
-                        if (kth != KEY_NONE) {
-                            tau = fminf(tau, key_dist(kth));
-                            atomicMin(p.tau_g + lq, (unsigned)(kth >> 32));
-                        }
+                for (int j = 0; j < 32; ++j) {
+                    // (NaN fails x <= thr and is never kept)
+                    if (!(qok && j < nvalid && x[j] <= thr)) continue;
+                    const uint64_t k = make_key(x[j], tag0 + (uint32_t)j);
+                    if (k >= top[7]) continue;
+                    top[7] = k;
+#pragma unroll
+                    for (int i2 = 7; i2 > 0; --i2) {
+                        const uint64_t lo2 = kmin(top[i2 - 1], top[i2]);
+                        const uint64_t hi2 = kmax(top[i2 - 1], top[i2]);
+                        top[i2 - 1] = lo2;
+                        top[i2] = hi2;
                     }
                 }
             }
-            // done with the staged column values of this tile
-            __syncwarp();
-            if (STAGE_CV && lane == 0) mbar_arrive(cv_empty + cs);
-        }
-        if (EPI == EPI_SHORTLIST) {
-            unsigned left;
-            while ((left = __ballot_sync(0xffffffffu, cnt > 0)) != 0) {
-                const int leader = __ffs(left) - 1;
-                const int lq = __shfl_sync(0xffffffffu, q, leader);
-                const int lc = __shfl_sync(0xffffffffu, cnt, leader);
-                uint64_t* lbuf = cbuf + (size_t)(e - lane + leader) * BUF_CAP;
-                uint64_t* lst = row_list(leader, lq);
-                __syncwarp();
-                merge_into(lst, lbuf, lc, lane);
-                __syncwarp();
-                if (lane == leader) cnt = 0;
-            }
-            if (use_sl) {
-                // the warp's 32 lists to global memory, one row per step
-                __syncwarp();
-                for (int r2 = 0; r2 < 32; ++r2) {
-                    const int qr = qb * TILE_M + (e - lane + r2);
-                    if (qr < p.nq)
-                        p.part[((size_t)blockIdx.y * p.nq + qr) * SAMPLE_K + lane] =
-                            slists[(size_t)(e - lane + r2) * SAMPLE_K + lane];
-                }
+            if (qok) {
+                uint64_t* dst = p.part + ((size_t)blockIdx.y * p.nq + q) * SAMPLE_K + part * 8;
+#pragma unroll
+                for (int i2 = 0; i2 < 8; ++i2) dst[i2] = top[i2];
             }
         }
     }
@@ -690,10 +610,7 @@ __global__ void to_half_kernel(const float* __restrict__ x, size_t n, int dim, i
 size_t gemm_smem(int katoms, int epi, int bn) {
     const int nstage = tc::b_stages(katoms, epi, bn);
     return 1024 + (size_t)katoms * tc::ATOM_BYTES + (size_t)nstage * katoms * bn * 128 +
-           (size_t)tc::NCV * bn * 4 +
-           (epi == tc::EPI_SHORTLIST ? (size_t)tc::TILE_M * tc::BUF_CAP * 8 : 0) +
-           (epi == tc::EPI_SHORTLIST && katoms <= 2 ? (size_t)tc::TILE_M * tc::SAMPLE_K * 8 : 0) +
-           (tc::NBARS + 1) * 8;
+           (size_t)tc::NCV * bn * 4 + (tc::NBARS + 1) * 8;
 }
 
 // Row chunks: enough blocks for several waves with little tail waste.
@@ -723,7 +640,7 @@ template <int EPI, int MET>
 void launch_pass_m(cudaStream_t s, const CUtensorMap& qm, const CUtensorMap& xm, int nq,
                    int chunks, const tc::GemmTopkParams& p) {
     dim3 grid((unsigned)((nq + tc::TILE_M - 1) / tc::TILE_M), (unsigned)chunks);
-    const unsigned threads = EPI == tc::EPI_FILTER ? tc::THREADS_FILTER : tc::THREADS;
+    const unsigned threads = tc::THREADS_FILTER;
     auto go = [&](auto kernel, int bn) {
         const size_t smem = gemm_smem(p.katoms, EPI, bn);
         FDB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -784,13 +701,10 @@ void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnor
     // --- sample pass ---
     w.part.ensure((size_t)chunks * nq * tc::SAMPLE_K);
     w.top32.ensure((size_t)nq * tc::SAMPLE_K);
-    w.tau_bits.ensure(nq);
     w.tau.ensure(nq);
     FDB_CUDA(cudaMemsetAsync(w.part.p, 0xff, w.part.bytes(), s));
-    FDB_CUDA(cudaMemsetAsync(w.tau_bits.p, 0xff, (size_t)nq * 4, s));
     p.tile_stride = stride;
     p.part = w.part.p;
-    p.tau_g = w.tau_bits.p;
     launch_pass<tc::EPI_SHORTLIST>(s, qm, xm, nq, chunks, p);
     launch_merge_lists(s, w.part.p, chunks, (size_t)nq * tc::SAMPLE_K, nq, tc::SAMPLE_K,
                        w.top32.p);
