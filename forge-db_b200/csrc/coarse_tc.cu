@@ -304,89 +304,6 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
 }
 
-// Exact L2^2 of the query row in shared memory (broadcast reads) and NC
-// centroid rows in global memory, in the order of l2sq_exact, the NC rows
-// interleaved for memory-level parallelism; 128-bit loads when the rows are
-// 16-byte aligned.
-// DIM > 0: a compile-time length (a multiple of 8, the rows 16-byte
-// aligned), every loop unrolled so that all loads of a row are in flight
-// together; DIM == 0: the run-time length dim.
-template <int NC, int DIM = 0>
-__device__ __forceinline__ void l2sq_rows(const float* __restrict__ qs,
-                                          const float* const (&c)[NC], int dim, bool vec,
-                                          float (&out)[NC]) {
-    float acc[NC][8];
-#pragma unroll
-    for (int r = 0; r < NC; ++r)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[r][j] = 0.0f;
-    if constexpr (DIM > 0) {
-        static_assert(DIM % 8 == 0, "whole lane groups");
-        const float4* q4 = reinterpret_cast<const float4*>(qs);
-#pragma unroll
-        for (int i = 0; i < DIM; i += 8) {
-            const float4 qa = q4[i >> 2], qb = q4[(i >> 2) + 1];
-            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-            for (int r = 0; r < NC; ++r) {
-                const float4* c4 = reinterpret_cast<const float4*>(c[r]);
-                const float4 u = __ldg(c4 + (i >> 2)), w = __ldg(c4 + (i >> 2) + 1);
-                const float cv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float d = __fsub_rn(qv[j], cv[j]);
-                    acc[r][j] = __fmaf_rn(d, d, acc[r][j]);
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < NC; ++r) out[r] = lane_sum(acc[r]);
-        return;
-    }
-    const int full = dim & ~7;
-    if (vec) {
-        const float4* q4 = reinterpret_cast<const float4*>(qs);
-#pragma unroll 2
-        for (int i = 0; i < full; i += 8) {
-            const float4 qa = q4[i >> 2], qb = q4[(i >> 2) + 1];
-            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            float cv[NC][8];
-#pragma unroll
-            for (int r = 0; r < NC; ++r) {
-                const float4* c4 = reinterpret_cast<const float4*>(c[r]);
-                const float4 u = __ldg(c4 + (i >> 2)), w = __ldg(c4 + (i >> 2) + 1);
-                cv[r][0] = u.x; cv[r][1] = u.y; cv[r][2] = u.z; cv[r][3] = u.w;
-                cv[r][4] = w.x; cv[r][5] = w.y; cv[r][6] = w.z; cv[r][7] = w.w;
-            }
-#pragma unroll
-            for (int r = 0; r < NC; ++r)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float d = __fsub_rn(qv[j], cv[r][j]);
-                    acc[r][j] = __fmaf_rn(d, d, acc[r][j]);
-                }
-        }
-    } else {
-        for (int i = 0; i < full; i += 8) {
-#pragma unroll
-            for (int r = 0; r < NC; ++r)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float d = __fsub_rn(qs[i + j], __ldg(c[r] + i + j));
-                    acc[r][j] = __fmaf_rn(d, d, acc[r][j]);
-                }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < NC; ++r) {
-        float t = lane_sum(acc[r]);
-        for (int i = full; i < dim; ++i) {
-            const float d = __fsub_rn(qs[i], __ldg(c[r] + i));
-            t = __fadd_rn(t, __fmul_rn(d, d));
-        }
-        out[r] = t;
-    }
-}
 
 // Sorts 64 keys held two per lane (a: entries 0..31, b: 32..63 on input):
 // on return a holds the 32 smallest ascending by lane, b the 32 largest.

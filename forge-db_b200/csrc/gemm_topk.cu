@@ -757,7 +757,9 @@ constexpr int BRS_WARPS = 8;
 // query had at least kp candidates and tau otherwise; so if the exact k-th
 // value + E < B no such row can be in the exact top-k.  Overflowing
 // candidate arrays are never certified.
-template <int P>
+// DIM: 128 (the row length known at compile time, every load of a row in
+// flight together) or 0 (run time).
+template <int P, int DIM>
 __global__ void __launch_bounds__(BRS_WARPS * 32)
     bf_rescore_kernel(const float* __restrict__ Q, int nq, const float* __restrict__ X, int dim,
                       const float* __restrict__ qnorm, float xmax, int metric,
@@ -774,20 +776,40 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
     WarpTopK<P> tk;
     tk.init(k, buf + warp * 64);
     const bool l2 = metric == EUCLIDEAN || metric == EUCLIDEAN_SQUARED;  // rank by L2^2
-    for (int base = 0; base < kp; base += 32) {
-        const int i = base + lane;
-        const uint64_t key = i < kp ? ak[i] : KEY_NONE;
-        uint64_t ek = KEY_NONE;
-        if (key != KEY_NONE) {
-            const uint32_t tag = key_tag(key);
-            const float* xv = X + (size_t)(tag - tag_base) * dim;
-            float d;
-            if (l2) d = l2sq_exact(qv, xv, dim);
-            else if (metric == DOT_PRODUCT) d = -dot_exact(qv, xv, dim);
-            else d = cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
-            ek = make_key(d, tag);
+    if (l2) {
+        // two rows per lane, interleaved: twice the loads in flight per round
+        const bool vec = (dim & 3) == 0;
+        for (int base = 0; base < kp; base += 64) {
+            const int i0 = base + lane, i1 = base + 32 + lane;
+            const uint64_t k0 = i0 < kp ? ak[i0] : KEY_NONE, k1 = i1 < kp ? ak[i1] : KEY_NONE;
+            const bool h0 = k0 != KEY_NONE, h1 = k1 != KEY_NONE;
+            // a missing entry repeats a present row (its result is discarded)
+            const uint32_t t0 = h0 ? key_tag(k0) : (h1 ? key_tag(k1) : (uint32_t)tag_base);
+            const uint32_t t1 = h1 ? key_tag(k1) : t0;
+            const float* rows[2] = {X + (size_t)(t0 - tag_base) * dim,
+                                    X + (size_t)(t1 - tag_base) * dim};
+            float d[2];
+            l2sq_rows<2, DIM>(qv, rows, dim, vec, d);
+            const uint64_t e0 = h0 ? make_key(d[0], t0) : KEY_NONE;
+            const uint64_t e1 = h1 ? make_key(d[1], t1) : KEY_NONE;
+            if (__any_sync(0xffffffffu, h0)) tk.merge32(e0);
+            if (__any_sync(0xffffffffu, h1)) tk.merge32(e1);
         }
-        if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
+    } else {
+        for (int base = 0; base < kp; base += 32) {
+            const int i = base + lane;
+            const uint64_t key = i < kp ? ak[i] : KEY_NONE;
+            uint64_t ek = KEY_NONE;
+            if (key != KEY_NONE) {
+                const uint32_t tag = key_tag(key);
+                const float* xv = X + (size_t)(tag - tag_base) * dim;
+                float d;
+                if (metric == DOT_PRODUCT) d = -dot_exact(qv, xv, dim);
+                else d = cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
+                ek = make_key(d, tag);
+            }
+            if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
+        }
     }
     const double qn = (double)qnorm[q];
     const double qlen = sqrt(qn);
@@ -823,9 +845,16 @@ void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, i
     if (nq == 0) return;
     unsigned grid = (unsigned)((nq + BRS_WARPS - 1) / BRS_WARPS);
 #define FDB_BRS(PP)                                                                           \
-    bf_rescore_kernel<PP><<<grid, BRS_WARPS * 32, 0, s>>>(                                    \
-        Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, w.cap, \
-        w.tau.p, out, flag_count, flag_list)
+    do {                                                                                     \
+        if (dim == 128)                                                                      \
+            bf_rescore_kernel<PP, 128><<<grid, BRS_WARPS * 32, 0, s>>>(                      \
+                Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, \
+                w.cap, w.tau.p, out, flag_count, flag_list);                                 \
+        else                                                                                 \
+            bf_rescore_kernel<PP, 0><<<grid, BRS_WARPS * 32, 0, s>>>(                        \
+                Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, \
+                w.cap, w.tau.p, out, flag_count, flag_list);                                 \
+    } while (0)
     if (k <= 32) FDB_BRS(1);
     else if (k <= 64) FDB_BRS(2);
     else if (k <= 128) FDB_BRS(4);
