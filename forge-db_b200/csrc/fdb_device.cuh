@@ -170,6 +170,43 @@ __device__ __forceinline__ float dot_exact(const float* a, const float* b, int l
     return t;
 }
 
+// dot_exact of one row against NC rows, the NC rows interleaved (as
+// l2sq_rows).  DIM > 0: a compile-time length (a multiple of 8, the rows
+// 16-byte aligned), every load in flight together; DIM == 0: one dot_exact
+// per row.
+template <int NC, int DIM>
+__device__ __forceinline__ void dot_rows(const float* __restrict__ qs,
+                                         const float* const (&c)[NC], int dim,
+                                         float (&out)[NC]) {
+    if constexpr (DIM == 0) {
+#pragma unroll
+        for (int r = 0; r < NC; ++r) out[r] = dot_exact(qs, c[r], dim);
+    } else {
+        static_assert(DIM % 8 == 0, "whole lane groups");
+        float acc[NC][8];
+#pragma unroll
+        for (int r = 0; r < NC; ++r)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[r][j] = 0.0f;
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+#pragma unroll
+        for (int i = 0; i < DIM; i += 8) {
+            const float4 qa = q4[i >> 2], qb = q4[(i >> 2) + 1];
+            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int r = 0; r < NC; ++r) {
+                const float4* c4 = reinterpret_cast<const float4*>(c[r]);
+                const float4 u = __ldg(c4 + (i >> 2)), w = __ldg(c4 + (i >> 2) + 1);
+                const float cv[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[r][j] = __fmaf_rn(qv[j], cv[j], acc[r][j]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NC; ++r) out[r] = lane_sum(acc[r]);
+    }
+}
+
 // manhattan_distance_avx2 (simd.rs:378-418)
 __device__ __forceinline__ float l1_exact(const float* a, const float* b, int len) {
     float acc[8];

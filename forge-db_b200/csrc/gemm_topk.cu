@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
     WarpTopK<P> tk;
     tk.init(k, buf + warp * 64);
     const bool l2 = metric == EUCLIDEAN || metric == EUCLIDEAN_SQUARED;  // rank by L2^2
-    if (l2) {
+    if (l2 || metric == DOT_PRODUCT) {
         // two rows per lane, interleaved: twice the loads in flight per round
         const bool vec = (dim & 3) == 0;
         for (int base = 0; base < kp; base += 64) {
@@ -789,7 +789,13 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
             const float* rows[2] = {X + (size_t)(t0 - tag_base) * dim,
                                     X + (size_t)(t1 - tag_base) * dim};
             float d[2];
-            l2sq_rows<2, DIM>(qv, rows, dim, vec, d);
+            if (l2) {
+                l2sq_rows<2, DIM>(qv, rows, dim, vec, d);
+            } else {
+                dot_rows<2, DIM>(qv, rows, dim, d);
+                d[0] = -d[0];
+                d[1] = -d[1];
+            }
             const uint64_t e0 = h0 ? make_key(d[0], t0) : KEY_NONE;
             const uint64_t e1 = h1 ? make_key(d[1], t1) : KEY_NONE;
             if (__any_sync(0xffffffffu, h0)) tk.merge32(e0);
@@ -803,9 +809,8 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
             if (key != KEY_NONE) {
                 const uint32_t tag = key_tag(key);
                 const float* xv = X + (size_t)(tag - tag_base) * dim;
-                float d;
-                if (metric == DOT_PRODUCT) d = -dot_exact(qv, xv, dim);
-                else d = cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
+                const float d =
+                    cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
                 ek = make_key(d, tag);
             }
             if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
