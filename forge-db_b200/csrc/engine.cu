@@ -969,7 +969,8 @@ void bf_search_dev(fdb_bf* h, const float* dQ, size_t nq, size_t k, uint64_t* d_
                            h->metric == COSINE ? h->rnorms.p : h->norms.p, h->metric, h->row0,
                            (int)kp, c.sm_count, h->xmax * h->xmax, h->gemm);
             tm.mark();
-            launch_bf_rescore(s, dQ, (int)nq, h->x.p, (int)h->dim, qn, h->xmax, h->metric,
+            launch_bf_rescore(s, dQ, (int)nq, h->x.p, (int)h->dim, qn, h->norms.p, h->xmax,
+                              h->metric,
                               h->row0, h->gemm, (int)kp, (int)k, h->s_keys.p, h->s_flags.p,
                               h->s_flags.p + 1);
             uint32_t hv[2] = {0, 0};

@@ -350,10 +350,11 @@ struct GemmScratch {
 void gemm_shortlist(cudaStream_t s, const __half* q16, int nq, const float* qnorm,
                     const __half* x16, size_t n, int kpad, const float* xnorm, int metric,
                     uint64_t tag_base, int kp, int sm_count, float colmax, GemmScratch& w);
+// xnorm: [rows] squared norms of X in the AVX2 order (dot_exact(x, x)).
 void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, int dim,
-                       const float* qnorm, float xmax, int metric, uint64_t tag_base,
-                       const GemmScratch& w, int kp, int k, uint64_t* out, uint32_t* flag_count,
-                       uint32_t* flag_list);
+                       const float* qnorm, const float* xnorm, float xmax, int metric,
+                       uint64_t tag_base, const GemmScratch& w, int kp, int k, uint64_t* out,
+                       uint32_t* flag_count, uint32_t* flag_list);
 
 }  // namespace fdb
 

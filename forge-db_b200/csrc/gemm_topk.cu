@@ -762,7 +762,8 @@ constexpr int BRS_WARPS = 8;
 template <int P, int DIM>
 __global__ void __launch_bounds__(BRS_WARPS * 32)
     bf_rescore_kernel(const float* __restrict__ Q, int nq, const float* __restrict__ X, int dim,
-                      const float* __restrict__ qnorm, float xmax, int metric,
+                      const float* __restrict__ qnorm, const float* __restrict__ xnorm,
+                      float xmax, int metric,
                       uint64_t tag_base, const uint64_t* __restrict__ approx, int kp, int k,
                       const unsigned* __restrict__ cand_cnt, int cap,
                       const float* __restrict__ tau, uint64_t* __restrict__ out,
@@ -776,8 +777,10 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
     WarpTopK<P> tk;
     tk.init(k, buf + warp * 64);
     const bool l2 = metric == EUCLIDEAN || metric == EUCLIDEAN_SQUARED;  // rank by L2^2
-    if (l2 || metric == DOT_PRODUCT) {
+    {
         // two rows per lane, interleaved: twice the loads in flight per round
+        // (cosine takes each row's squared norm from xnorm, computed in the
+        // same order as the dot product it would otherwise repeat)
         const bool vec = (dim & 3) == 0;
         for (int base = 0; base < kp; base += 64) {
             const int i0 = base + lane, i1 = base + 32 + lane;
@@ -793,27 +796,18 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
                 l2sq_rows<2, DIM>(qv, rows, dim, vec, d);
             } else {
                 dot_rows<2, DIM>(qv, rows, dim, d);
-                d[0] = -d[0];
-                d[1] = -d[1];
+                if (metric == DOT_PRODUCT) {
+                    d[0] = -d[0];
+                    d[1] = -d[1];
+                } else {
+                    d[0] = cosine_from(d[0], qnorm[q], xnorm[t0 - tag_base]);
+                    d[1] = cosine_from(d[1], qnorm[q], xnorm[t1 - tag_base]);
+                }
             }
             const uint64_t e0 = h0 ? make_key(d[0], t0) : KEY_NONE;
             const uint64_t e1 = h1 ? make_key(d[1], t1) : KEY_NONE;
             if (__any_sync(0xffffffffu, h0)) tk.merge32(e0);
             if (__any_sync(0xffffffffu, h1)) tk.merge32(e1);
-        }
-    } else {
-        for (int base = 0; base < kp; base += 32) {
-            const int i = base + lane;
-            const uint64_t key = i < kp ? ak[i] : KEY_NONE;
-            uint64_t ek = KEY_NONE;
-            if (key != KEY_NONE) {
-                const uint32_t tag = key_tag(key);
-                const float* xv = X + (size_t)(tag - tag_base) * dim;
-                const float d =
-                    cosine_from(dot_exact(qv, xv, dim), qnorm[q], dot_exact(xv, xv, dim));
-                ek = make_key(d, tag);
-            }
-            if (__any_sync(0xffffffffu, ek != KEY_NONE)) tk.merge32(ek);
         }
     }
     const double qn = (double)qnorm[q];
@@ -844,20 +838,22 @@ __global__ void __launch_bounds__(BRS_WARPS * 32)
 }
 
 void launch_bf_rescore(cudaStream_t s, const float* Q, int nq, const float* X, int dim,
-                       const float* qnorm, float xmax, int metric, uint64_t tag_base,
-                       const GemmScratch& w, int kp, int k, uint64_t* out, uint32_t* flag_count,
-                       uint32_t* flag_list) {
+                       const float* qnorm, const float* xnorm, float xmax, int metric,
+                       uint64_t tag_base, const GemmScratch& w, int kp, int k, uint64_t* out,
+                       uint32_t* flag_count, uint32_t* flag_list) {
     if (nq == 0) return;
     unsigned grid = (unsigned)((nq + BRS_WARPS - 1) / BRS_WARPS);
 #define FDB_BRS(PP)                                                                           \
     do {                                                                                     \
         if (dim == 128)                                                                      \
             bf_rescore_kernel<PP, 128><<<grid, BRS_WARPS * 32, 0, s>>>(                      \
-                Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, \
+                Q, nq, X, dim, qnorm, xnorm, xmax, metric, tag_base, w.approx.p, kp, k,          \
+                w.cand_cnt.p,                                                                 \
                 w.cap, w.tau.p, out, flag_count, flag_list);                                 \
         else                                                                                 \
             bf_rescore_kernel<PP, 0><<<grid, BRS_WARPS * 32, 0, s>>>(                        \
-                Q, nq, X, dim, qnorm, xmax, metric, tag_base, w.approx.p, kp, k, w.cand_cnt.p, \
+                Q, nq, X, dim, qnorm, xnorm, xmax, metric, tag_base, w.approx.p, kp, k,          \
+                w.cand_cnt.p,                                                                 \
                 w.cap, w.tau.p, out, flag_count, flag_list);                                 \
     } while (0)
     if (k <= 32) FDB_BRS(1);
